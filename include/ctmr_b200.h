@@ -1,0 +1,180 @@
+/*
+ * ctmr_b200 — C ABI of the B200 (sm_100a) convolution stack that replaces the
+ * reference's native path in mlx-generate-ctmr (v0.7.0):
+ *   implicit-GEMM Conv3d (3x3x3 pad 1 / 1x1x1, stride 1 / 2, nearest-2x and
+ *   trilinear-2x inputs) with the group-norm affine, SiLU, 2x average pool and
+ *   a two-tensor channel concat fused into its input preparation, and the bias
+ *   (per channel or per batch item) and residual add fused into its epilogue,
+ *   plus the GroupNorm statistics that feed it.
+ *
+ * Conventions
+ *   - Activations are channels-last (NDHWC): voxel rows of `channels` values,
+ *     `cstride` elements apart (a view into a wider row is allowed). The
+ *     reference's Python surface is NCDHW; torch's channels_last_3d storage of
+ *     an NCDHW tensor is exactly this layout.
+ *   - Weights use the Torch layout (O, C, k, k, k), fp32, and are packed once
+ *     with ctmr_pack_weight.
+ *   - Every call is asynchronous on `stream` (a cudaStream_t, NULL = legacy
+ *     default stream) and returns a status code; nothing throws across the ABI.
+ *   - No call allocates device memory: the caller passes workspace buffers
+ *     whose sizes the *_workspace_size functions return.
+ *   - All device-side waits are bounded; a kernel that gives up sets a bit in
+ *     the library's device error word (ctmr_get_device_error) instead of hanging.
+ */
+#ifndef CTMR_B200_H
+#define CTMR_B200_H
+
+#include <stddef.h>
+
+#if defined(__GNUC__)
+#define CTMR_API __attribute__((visibility("default")))
+#else
+#define CTMR_API
+#endif
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* Status codes. CTMR_ERR_INVALID corresponds to the reference's ValueError
+ * for shape/dtype mismatches (`_nax_conv.py:523-526, 537-541, 559-560`). */
+enum {
+  CTMR_OK = 0,
+  CTMR_ERR_INVALID = 1,
+  CTMR_ERR_UNSUPPORTED = 2,
+  CTMR_ERR_WORKSPACE = 3,
+  CTMR_ERR_CUDA = 4
+};
+
+enum { CTMR_DTYPE_F32 = 0, CTMR_DTYPE_BF16 = 1 };
+
+/* CTMR_PRECISION_FP32: fp32 operands carried as fp16 hi/lo pairs, three
+ *   tensor-core products per step, fp32 accumulation (~2^-22 relative product
+ *   error; needs |value| < 65504), the reference's "exact" mode
+ *   (`_nax_conv.py:27-35`).
+ * CTMR_PRECISION_BF16: bf16 operands, fp32 accumulation. */
+enum { CTMR_PRECISION_FP32 = 0, CTMR_PRECISION_BF16 = 1 };
+
+/* An NDHWC activation view. data == NULL means "absent". */
+typedef struct ctmr_tensor {
+  const void* data;
+  int dtype;            /* CTMR_DTYPE_* */
+  int channels;
+  long long cstride;    /* elements between consecutive voxel rows, >= channels */
+} ctmr_tensor;
+
+/* One convolution: y = conv(prepare(x ++ x2)) + bias (+ residual).
+ * Replaces `nax_conv3d(x, packed, bias, *, affine, silu, stride, upsample,
+ * trilinear, residual, mx)` (`_nax_conv.py:475-487`) together with the 1x1x1
+ * route of `fast_fp32.pointwise_conv_ncdhw` (`fast_fp32.py:121-130`) and the
+ * pooled conv1 of `fast_fp32.residual_block_ncdhw` (`fast_fp32.py:250-265`). */
+typedef struct ctmr_conv3d_desc {
+  int batch, depth, height, width; /* grid of x (and x2) */
+  ctmr_tensor x;
+  ctmr_tensor x2;                  /* optional second input, concatenated after x's channels */
+  int out_channels;
+  int kernel_size;                 /* 3 (padding 1) or 1 */
+  int stride;                      /* 1, or 2 with kernel_size 3 */
+  int upsample;                    /* convolve the nearest-2x upsampling of x (weights packed with upsample=1) */
+  int trilinear;                   /* convolve the half-pixel trilinear-2x upsampling of x */
+  int avgpool;                     /* convolve the 2x2x2 mean of silu?(affine?(x)) */
+  int precision;                   /* CTMR_PRECISION_* */
+  const void* weight;              /* ctmr_pack_weight output (bf16, or the fp16 hi plane) */
+  const void* weight_lo;           /* fp16 lo plane for CTMR_PRECISION_FP32 */
+  const float* affine;             /* (batch, C, 2) (scale, offset) pairs, or NULL */
+  int silu;                        /* apply SiLU after the affine */
+  const float* bias;               /* (out_channels) or (batch, out_channels), or NULL */
+  int bias_per_batch;
+  ctmr_tensor residual;            /* optional, on the output grid (half grid if residual_upsampled) */
+  int residual_upsampled;          /* residual is nearest-2x upsampled on the fly */
+  void* y;                         /* NDHWC output on the output grid */
+  int y_dtype;
+  long long y_cstride;
+  int y_coffset;                   /* first channel written in each output row */
+} ctmr_conv3d_desc;
+
+/* Packed-weight element count per plane for a Torch (O, C, k, k, k) weight:
+ * taps x round16(O) x round16(C), taps = k^3, or 64 with upsample.
+ * Replaces the shapes of `pack_weight` / `pack_upsample_weight` (`_nax_conv.py:391-445`). */
+CTMR_API size_t ctmr_packed_weight_elems(int out_channels, int in_channels, int kernel_size, int upsample);
+
+/* Pack an fp32 Torch-layout weight (device pointer). bf16 for CTMR_PRECISION_BF16
+ * (packed_lo unused), fp16 hi/lo planes for CTMR_PRECISION_FP32.
+ * Replaces `pack_weight` (`_nax_conv.py:391-404`) and, with upsample = 1,
+ * `pack_upsample_weight` (`_nax_conv.py:407-445`). */
+CTMR_API int ctmr_pack_weight(const float* weight, int out_channels, int in_channels, int kernel_size, int upsample,
+                     int precision, void* packed, void* packed_lo, void* stream);
+
+/* Workspace bytes ctmr_conv3d needs for this descriptor (the prepared operand). */
+CTMR_API size_t ctmr_conv3d_workspace_size(const ctmr_conv3d_desc* desc);
+
+/* Replaces `nax_conv3d` (`_nax_conv.py:475-684`). */
+CTMR_API int ctmr_conv3d(const ctmr_conv3d_desc* desc, void* workspace, size_t workspace_bytes, void* stream);
+
+/* Workspace bytes for ctmr_group_norm_affine. */
+CTMR_API size_t ctmr_group_norm_workspace_size(int batch, long long voxels, int groups);
+
+/* GroupNorm statistics of (x ++ x2) over each (batch item, group) ->
+ * affine[b][c] = (gamma[c] * rstd, beta[c] - mean * gamma[c] * rstd), fp32.
+ * Replaces `medmlx_core.group_norm.group_norm_affine` (called at `fast_fp32.py:183-189`;
+ * layout (B*C*2) consumed at `_nax_conv.py:174-176`). gamma/beta may be NULL (1/0). */
+CTMR_API int ctmr_group_norm_affine(ctmr_tensor x, ctmr_tensor x2, int batch, long long voxels, const float* gamma,
+                           const float* beta, int groups, float eps, float* affine, void* workspace,
+                           size_t workspace_bytes, void* stream);
+
+enum { CTMR_TRANSFORM_COPY = 0, CTMR_TRANSFORM_TRILINEAR = 1, CTMR_TRANSFORM_AVGPOOL = 2 };
+
+/* y = mode(silu?(affine?(x ++ x2))) materialised as fp32 or bf16 NDHWC, channels
+ * past the input zero-filled up to y_channels. Replaces the materialising ops of
+ * the operator surface: `fast_fp32.group_norm_ncdhw` (`fast_fp32.py:102-118`),
+ * `silu`, `avg_pool3d_ncdhw` and `upsample_trilinear_ncdhw` (`source_vae.py:95-111`). */
+typedef struct ctmr_transform_desc {
+  int batch, depth, height, width; /* grid of x */
+  ctmr_tensor x;
+  ctmr_tensor x2;
+  int mode;                        /* CTMR_TRANSFORM_* */
+  const float* affine;
+  int silu;
+  void* y;
+  int y_dtype;
+  int y_channels;
+  long long y_cstride;
+} ctmr_transform_desc;
+
+CTMR_API int ctmr_transform(const ctmr_transform_desc* desc, void* stream);
+
+/* (B, C, S) <-> (B, S, C) layout change (NCDHW <-> NDHWC), fp32/bf16 in and out. */
+CTMR_API int ctmr_ncdhw_to_ndhwc(const void* x, int x_dtype, void* y, int y_dtype, int batch, int channels,
+                        long long voxels, void* stream);
+CTMR_API int ctmr_ndhwc_to_ncdhw(const void* x, int x_dtype, void* y, int y_dtype, int batch, int channels,
+                        long long voxels, void* stream);
+
+/* Sliding-window blend (`decode.py:115-184`): acc += pred * w, wsum += w over one
+ * window at (z0, y0, x0) of the output grid, w = max(gz[z/scale] gy[y/scale] gx[x/scale], floor). */
+CTMR_API int ctmr_window_accumulate(ctmr_tensor pred, int batch, int wd, int wh, int ww, int z0, int y0, int x0,
+                           int od, int oh, int ow, const float* gz, const float* gy, const float* gx, int scale,
+                           float floor_value, float* acc, float* wsum, void* stream);
+
+/* out (NCDHW, B x C x cd x ch x cw) = acc / wsum over the crop at (cz0, cy0, cx0). */
+CTMR_API int ctmr_window_finalize(const float* acc, const float* wsum, float* out, int batch, int channels, int od, int oh,
+                         int ow, int cz0, int cy0, int cx0, int cd, int ch, int cw, void* stream);
+
+/* Guided Euler step of the rectified-flow sampler (`image.py:163-175`, `rflow.py:101-121`):
+ * v = vel[n:] + guidance * (vel[:n] - vel[n:]) when guided, else vel[:n]; out = z + v * dt. */
+CTMR_API int ctmr_rflow_step(const float* z, const float* vel, long long n, float guidance, int guided, float dt, float* out,
+                    void* stream);
+
+/* Device error word (bit set when a bounded wait gave up); optionally cleared.
+ * Synchronises the current device. */
+CTMR_API int ctmr_get_device_error(unsigned* bits, int clear);
+
+CTMR_API const char* ctmr_status_string(int status);
+
+/* Human-readable reason of the last failed call on this thread. */
+CTMR_API const char* ctmr_last_error(void);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* CTMR_B200_H */

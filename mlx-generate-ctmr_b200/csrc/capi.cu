@@ -1,0 +1,530 @@
+// The extern "C" boundary (include/ctmr_b200.h): argument validation, TMA
+// descriptor encoding, tile planning and kernel dispatch. No call allocates
+// device memory; every launch goes to the caller's stream.
+#include <cuda.h>
+#include <cudaTypedefs.h>
+#include <cuda_runtime.h>
+
+#include <algorithm>
+#include <cstdarg>
+#include <cstdint>
+#include <cstdio>
+#include <cstring>
+#include <mutex>
+
+#include "ctmr_b200.h"
+#include "conv3d_umma.cuh"
+#include "groupnorm.cuh"
+#include "misc.cuh"
+#include "pack.cuh"
+#include "prepare.cuh"
+
+namespace ctmr {
+int conv_stage_plan(int kc, int bn, bool exact, bool one_cta_per_sm, size_t* smem_bytes);
+cudaError_t launch_conv3d_umma(const ConvMaps& maps, const ConvGeom& g, int kc, bool exact, size_t smem,
+                               cudaStream_t stream);
+extern __device__ unsigned int g_device_error;
+}  // namespace ctmr
+
+namespace {
+
+thread_local char g_last_error[512] = "";
+
+int fail(int status, const char* fmt, ...) __attribute__((format(printf, 2, 3)));
+int fail(int status, const char* fmt, ...) {
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(g_last_error, sizeof(g_last_error), fmt, ap);
+  va_end(ap);
+  return status;
+}
+
+int cuda_fail(cudaError_t e, const char* what) {
+  return fail(CTMR_ERR_CUDA, "%s: %s", what, cudaGetErrorString(e));
+}
+
+inline long long round_up(long long v, long long a) { return (v + a - 1) / a * a; }
+inline int next_pow2(int v) {
+  int p = 1;
+  while (p < v) p <<= 1;
+  return p;
+}
+
+PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q{};
+    if (cudaGetDriverEntryPointByVersion("cuTensorMapEncodeTiled", &p, 12000, cudaEnableDefault, &q) !=
+            cudaSuccess ||
+        q != cudaDriverEntryPointSuccess)
+      p = nullptr;
+    return reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+  }();
+  return fn;
+}
+
+CUtensorMapSwizzle swizzle_for(int kc) {
+  return kc == 64 ? CU_TENSOR_MAP_SWIZZLE_128B : (kc == 32 ? CU_TENSOR_MAP_SWIZZLE_64B : CU_TENSOR_MAP_SWIZZLE_32B);
+}
+
+// 5-D activation view (C, W, H, D, B) with byte strides for W/H/D/B.
+int encode_act(CUtensorMap* map, const void* base, bool bf16, long long cpad, long long w, long long h, long long d,
+               long long b, long long sw, long long sh, long long sd, long long sb, int kc, int tw, int th, int td) {
+  auto enc = tensor_map_encoder();
+  if (enc == nullptr) return fail(CTMR_ERR_CUDA, "cuTensorMapEncodeTiled is unavailable");
+  cuuint64_t dims[5] = {static_cast<cuuint64_t>(cpad), static_cast<cuuint64_t>(w), static_cast<cuuint64_t>(h),
+                        static_cast<cuuint64_t>(d), static_cast<cuuint64_t>(b)};
+  cuuint64_t strides[4] = {static_cast<cuuint64_t>(sw), static_cast<cuuint64_t>(sh), static_cast<cuuint64_t>(sd),
+                           static_cast<cuuint64_t>(sb)};
+  cuuint32_t box[5] = {static_cast<cuuint32_t>(kc), static_cast<cuuint32_t>(tw), static_cast<cuuint32_t>(th),
+                       static_cast<cuuint32_t>(td), 1};
+  cuuint32_t estr[5] = {1, 1, 1, 1, 1};
+  CUresult r = enc(map, bf16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 5,
+                   const_cast<void*>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                   swizzle_for(kc), CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return fail(CTMR_ERR_INVALID, "activation tensor map rejected (CUresult %d)", int(r));
+  return CTMR_OK;
+}
+
+int encode_weight(CUtensorMap* map, const void* base, bool bf16, long long cpad, long long opad, long long taps,
+                  int kc, int bn) {
+  auto enc = tensor_map_encoder();
+  if (enc == nullptr) return fail(CTMR_ERR_CUDA, "cuTensorMapEncodeTiled is unavailable");
+  cuuint64_t dims[3] = {static_cast<cuuint64_t>(cpad), static_cast<cuuint64_t>(opad),
+                        static_cast<cuuint64_t>(taps)};
+  cuuint64_t strides[2] = {static_cast<cuuint64_t>(cpad * 2), static_cast<cuuint64_t>(cpad * 2 * opad)};
+  cuuint32_t box[3] = {static_cast<cuuint32_t>(kc), static_cast<cuuint32_t>(bn), 1};
+  cuuint32_t estr[3] = {1, 1, 1};
+  CUresult r = enc(map, bf16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 3,
+                   const_cast<void*>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                   swizzle_for(kc), CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return fail(CTMR_ERR_INVALID, "weight tensor map rejected (CUresult %d)", int(r));
+  return CTMR_OK;
+}
+
+bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+int check_view(const ctmr_tensor& t, const char* name, bool required) {
+  if (t.data == nullptr) {
+    if (required) return fail(CTMR_ERR_INVALID, "%s is missing", name);
+    return CTMR_OK;
+  }
+  if (t.dtype != CTMR_DTYPE_F32 && t.dtype != CTMR_DTYPE_BF16) return fail(CTMR_ERR_INVALID, "%s dtype", name);
+  if (t.channels <= 0 || t.cstride < t.channels) return fail(CTMR_ERR_INVALID, "%s channels/cstride", name);
+  return CTMR_OK;
+}
+
+ctmr::PrepSource as_source(const ctmr_tensor& t) {
+  ctmr::PrepSource s{};
+  if (t.data != nullptr) {
+    s.ptr = t.data;
+    s.bf16 = t.dtype == CTMR_DTYPE_BF16;
+    s.channels = t.channels;
+    s.cstride = t.cstride;
+  }
+  return s;
+}
+
+// Everything derived from a conv descriptor before any launch.
+struct ConvPlan {
+  int mode;
+  int cin, cpad, opad, kc, bn, taps, phases;
+  int in_d, in_h, in_w;     // grid the taps read (after trilinear / avgpool)
+  int row_d, row_h, row_w;  // GEMM rows
+  int out_d, out_h, out_w;
+  bool exact, prepare;
+  size_t prep_bytes;        // per plane
+};
+
+int plan_conv(const ctmr_conv3d_desc* d, ConvPlan* p) {
+  if (d == nullptr) return fail(CTMR_ERR_INVALID, "null descriptor");
+  if (d->batch <= 0 || d->depth <= 0 || d->height <= 0 || d->width <= 0)
+    return fail(CTMR_ERR_INVALID, "grid must be positive");
+  int st = check_view(d->x, "x", true);
+  if (st) return st;
+  if ((st = check_view(d->x2, "x2", false))) return st;
+  if ((st = check_view(d->residual, "residual", false))) return st;
+  if (d->precision != CTMR_PRECISION_FP32 && d->precision != CTMR_PRECISION_BF16)
+    return fail(CTMR_ERR_INVALID, "precision");
+  if (d->out_channels <= 0) return fail(CTMR_ERR_INVALID, "out_channels");
+  if (d->weight == nullptr || (d->precision == CTMR_PRECISION_FP32 && d->weight_lo == nullptr))
+    return fail(CTMR_ERR_INVALID, "packed weight missing");
+  if (d->y == nullptr || (d->y_dtype != CTMR_DTYPE_F32 && d->y_dtype != CTMR_DTYPE_BF16))
+    return fail(CTMR_ERR_INVALID, "output");
+  if (d->y_coffset < 0 || d->y_cstride < d->y_coffset + d->out_channels)
+    return fail(CTMR_ERR_INVALID, "output cstride %lld too small for offset %d + %d channels", d->y_cstride,
+                d->y_coffset, d->out_channels);
+  const int specials = (d->upsample != 0) + (d->trilinear != 0) + (d->avgpool != 0) + (d->stride == 2);
+  if (specials > 1) return fail(CTMR_ERR_UNSUPPORTED, "upsample, trilinear, avgpool and stride 2 are exclusive");
+  if (d->kernel_size == 1 && (d->upsample || d->stride != 1))
+    return fail(CTMR_ERR_UNSUPPORTED, "1x1x1 convolutions support stride 1 only");
+  if (d->kernel_size != 1 && d->kernel_size != 3) return fail(CTMR_ERR_UNSUPPORTED, "kernel_size must be 1 or 3");
+  if (d->stride != 1 && d->stride != 2) return fail(CTMR_ERR_UNSUPPORTED, "stride must be 1 or 2");
+  if (d->trilinear && (d->affine != nullptr || d->silu))
+    return fail(CTMR_ERR_UNSUPPORTED, "trilinear packing supports only a plain convolution");
+  if (d->avgpool && (d->depth % 2 || d->height % 2 || d->width % 2))
+    return fail(CTMR_ERR_INVALID, "average pooling needs even extents");
+  if (d->stride == 2 && (d->depth < 2 || d->height < 2 || d->width < 2))
+    return fail(CTMR_ERR_UNSUPPORTED, "stride-2 convolution needs extents >= 2");
+
+  p->exact = d->precision == CTMR_PRECISION_FP32;
+  p->cin = d->x.channels + (d->x2.data ? d->x2.channels : 0);
+  p->cpad = static_cast<int>(round_up(p->cin, 16));
+  p->opad = static_cast<int>(round_up(d->out_channels, 16));
+  p->kc = p->cpad % 64 == 0 ? 64 : (p->cpad % 32 == 0 ? 32 : 16);
+  p->bn = std::min(p->opad, 128);
+  p->in_d = d->depth, p->in_h = d->height, p->in_w = d->width;
+  if (d->trilinear) p->in_d *= 2, p->in_h *= 2, p->in_w *= 2;
+  if (d->avgpool) p->in_d /= 2, p->in_h /= 2, p->in_w /= 2;
+  p->phases = 1;
+  if (d->upsample) {
+    if (d->kernel_size != 3) return fail(CTMR_ERR_UNSUPPORTED, "upsample needs a 3x3x3 kernel");
+    p->mode = ctmr::kModeUp2;
+    p->taps = 8;
+    p->phases = 8;
+    p->row_d = p->in_d, p->row_h = p->in_h, p->row_w = p->in_w;
+    p->out_d = 2 * p->in_d, p->out_h = 2 * p->in_h, p->out_w = 2 * p->in_w;
+  } else if (d->kernel_size == 1) {
+    p->mode = ctmr::kModeConv1;
+    p->taps = 1;
+    p->row_d = p->out_d = p->in_d, p->row_h = p->out_h = p->in_h, p->row_w = p->out_w = p->in_w;
+  } else if (d->stride == 2) {
+    p->mode = ctmr::kModeStride2;
+    p->taps = 27;
+    p->row_d = p->out_d = (p->in_d - 1) / 2 + 1;
+    p->row_h = p->out_h = (p->in_h - 1) / 2 + 1;
+    p->row_w = p->out_w = (p->in_w - 1) / 2 + 1;
+  } else {
+    p->mode = ctmr::kModeConv3;
+    p->taps = 27;
+    p->row_d = p->out_d = p->in_d, p->row_h = p->out_h = p->in_h, p->row_w = p->out_w = p->in_w;
+  }
+  // The raw input can be the MMA operand directly only in bf16 mode, with no
+  // transform, 16-channel granularity and 16-byte aligned rows.
+  const bool direct = !p->exact && d->x2.data == nullptr && d->affine == nullptr && !d->silu && !d->trilinear &&
+                      !d->avgpool && d->x.dtype == CTMR_DTYPE_BF16 && d->x.channels % 16 == 0 &&
+                      d->x.cstride % 8 == 0 && aligned16(d->x.data);
+  p->prepare = !direct;
+  p->prep_bytes = p->prepare ? static_cast<size_t>(round_up(static_cast<long long>(d->batch) * p->in_d * p->in_h *
+                                                                p->in_w * p->cpad * 2,
+                                                            256))
+                             : 0;
+  if (d->residual.data != nullptr) {
+    if (d->residual.channels < d->out_channels)
+      return fail(CTMR_ERR_INVALID, "residual has %d channels, output %d", d->residual.channels, d->out_channels);
+  }
+  return CTMR_OK;
+}
+
+}  // namespace
+
+extern "C" {
+
+const char* ctmr_status_string(int status) {
+  switch (status) {
+    case CTMR_OK: return "ok";
+    case CTMR_ERR_INVALID: return "invalid argument";
+    case CTMR_ERR_UNSUPPORTED: return "unsupported configuration";
+    case CTMR_ERR_WORKSPACE: return "workspace too small";
+    case CTMR_ERR_CUDA: return "CUDA error";
+    default: return "unknown status";
+  }
+}
+
+const char* ctmr_last_error(void) { return g_last_error; }
+
+size_t ctmr_packed_weight_elems(int out_channels, int in_channels, int kernel_size, int upsample) {
+  if (out_channels <= 0 || in_channels <= 0 || (kernel_size != 1 && kernel_size != 3)) return 0;
+  const long long taps = upsample ? 64 : static_cast<long long>(kernel_size) * kernel_size * kernel_size;
+  return static_cast<size_t>(taps * round_up(out_channels, 16) * round_up(in_channels, 16));
+}
+
+int ctmr_pack_weight(const float* weight, int out_channels, int in_channels, int kernel_size, int upsample,
+                     int precision, void* packed, void* packed_lo, void* stream) {
+  if (weight == nullptr || packed == nullptr) return fail(CTMR_ERR_INVALID, "null weight pointer");
+  if (out_channels <= 0 || in_channels <= 0) return fail(CTMR_ERR_INVALID, "channel counts");
+  if (kernel_size != 1 && kernel_size != 3) return fail(CTMR_ERR_UNSUPPORTED, "kernel_size must be 1 or 3");
+  if (upsample && kernel_size != 3) return fail(CTMR_ERR_UNSUPPORTED, "upsample fold needs a 3x3x3 kernel");
+  const bool split = precision == CTMR_PRECISION_FP32;
+  if (split && packed_lo == nullptr) return fail(CTMR_ERR_INVALID, "lo plane missing");
+  cudaError_t e = ctmr::launch_pack_weight(weight, out_channels, in_channels, kernel_size, upsample,
+                                           static_cast<int>(round_up(out_channels, 16)),
+                                           static_cast<int>(round_up(in_channels, 16)), split, packed, packed_lo,
+                                           static_cast<cudaStream_t>(stream));
+  return e == cudaSuccess ? CTMR_OK : cuda_fail(e, "pack_weight launch");
+}
+
+size_t ctmr_conv3d_workspace_size(const ctmr_conv3d_desc* desc) {
+  ConvPlan p{};
+  if (plan_conv(desc, &p) != CTMR_OK) return 0;
+  return p.prep_bytes * (p.exact ? 2 : 1);
+}
+
+int ctmr_conv3d(const ctmr_conv3d_desc* d, void* workspace, size_t workspace_bytes, void* stream_ptr) {
+  ConvPlan p{};
+  int st = plan_conv(d, &p);
+  if (st != CTMR_OK) return st;
+  cudaStream_t stream = static_cast<cudaStream_t>(stream_ptr);
+  const size_t need = p.prep_bytes * (p.exact ? 2 : 1);
+  if (need > workspace_bytes || (need > 0 && workspace == nullptr))
+    return fail(CTMR_ERR_WORKSPACE, "conv3d needs %zu workspace bytes, got %zu", need, workspace_bytes);
+
+  // 1. Operand preparation (affine, SiLU, trilinear / avgpool, concat, cast or split).
+  const void* a_hi = d->x.data;
+  const void* a_lo = nullptr;
+  long long a_cstride = d->x.cstride;
+  if (p.prepare) {
+    ctmr::PrepParams pp{};
+    pp.src[0] = as_source(d->x);
+    pp.src[1] = as_source(d->x2);
+    pp.batch = d->batch;
+    pp.sd = d->depth, pp.sh = d->height, pp.sw = d->width;
+    pp.od = p.in_d, pp.oh = p.in_h, pp.ow = p.in_w;
+    pp.mode = d->trilinear ? ctmr::kPrepTrilinear : (d->avgpool ? ctmr::kPrepAvgPool : ctmr::kPrepCopy);
+    pp.affine = d->affine;
+    pp.silu = d->silu;
+    pp.cpad = p.cpad;
+    pp.out_cstride = p.cpad;
+    pp.out_kind = p.exact ? ctmr::kPrepOutSplitF16 : ctmr::kPrepOutBF16;
+    pp.out = workspace;
+    pp.out_lo = p.exact ? static_cast<uint8_t*>(workspace) + p.prep_bytes : nullptr;
+    cudaError_t e = ctmr::launch_prepare(pp, stream);
+    if (e != cudaSuccess) return cuda_fail(e, "prepare launch");
+    a_hi = pp.out;
+    a_lo = pp.out_lo;
+    a_cstride = p.cpad;
+  }
+
+  // 2. Tile plan over the GEMM-row grid: a 128-voxel box, w fastest.
+  ctmr::ConvGeom g{};
+  g.batch = d->batch;
+  g.row_d = p.row_d, g.row_h = p.row_h, g.row_w = p.row_w;
+  g.tile_w = std::min(next_pow2(p.row_w), 128);
+  g.tile_h = std::min(next_pow2(p.row_h), 128 / g.tile_w);
+  g.tile_d = 128 / (g.tile_w * g.tile_h);
+  g.tiles_w = (p.row_w + g.tile_w - 1) / g.tile_w;
+  g.tiles_h = (p.row_h + g.tile_h - 1) / g.tile_h;
+  g.tiles_d = (p.row_d + g.tile_d - 1) / g.tile_d;
+  g.phases = p.phases;
+  g.taps = p.taps;
+  g.kblocks = p.cpad / p.kc;
+  g.mode = p.mode;
+  g.bn = p.bn;
+  g.cout = d->out_channels;
+  // TMEM: one accumulator (bf16), or two alternating hi chunk buffers plus the lo accumulator (fp32).
+  const int acc_cols = p.bn * (p.exact ? 3 : 1);
+  g.tmem_cols = static_cast<uint32_t>(std::max(32, next_pow2(acc_cols)));
+  g.chunk_iters = std::max(1, 32 / (p.kc / 16));
+  size_t smem = 0;
+  g.stages = ctmr::conv_stage_plan(p.kc, p.bn, p.exact, g.tmem_cols > 256, &smem);
+  if (g.stages < 2) return fail(CTMR_ERR_UNSUPPORTED, "no pipeline fits shared memory");
+  g.bias = d->bias;
+  g.bias_bstride = d->bias_per_batch ? d->out_channels : 0;
+  g.res = d->residual.data;
+  g.res_bf16 = d->residual.dtype == CTMR_DTYPE_BF16;
+  g.res_cstride = d->residual.cstride;
+  g.res_up = d->residual_upsampled;
+  g.res_d = d->residual_upsampled ? p.out_d / 2 : p.out_d;
+  g.res_h = d->residual_upsampled ? p.out_h / 2 : p.out_h;
+  g.res_w = d->residual_upsampled ? p.out_w / 2 : p.out_w;
+  g.out = d->y;
+  g.out_bf16 = d->y_dtype == CTMR_DTYPE_BF16;
+  g.out_cstride = d->y_cstride;
+  g.out_coff = d->y_coffset;
+  g.out_d = p.out_d, g.out_h = p.out_h, g.out_w = p.out_w;
+  g.lo_scale = 1.0f / 2048.0f;
+
+  // 3. TMA descriptors.
+  ctmr::ConvMaps maps;
+  std::memset(&maps, 0, sizeof(maps));
+  const bool bf16 = !p.exact;
+  const long long eb = 2;  // element bytes (bf16 / fp16)
+  const long long rs = a_cstride * eb;
+  if (rs % 16 != 0) return fail(CTMR_ERR_INVALID, "operand row pitch must be a multiple of 16 bytes");
+  const long long W = p.in_w, H = p.in_h, D = p.in_d;
+  const void* planes[2] = {a_hi, a_lo};
+  for (int pl = 0; pl < (p.exact ? 2 : 1); ++pl) {
+    CUtensorMap* dst = pl == 0 ? maps.a : maps.a_lo;
+    if (p.mode == ctmr::kModeStride2) {
+      for (int par = 0; par < 8; ++par) {
+        const int pd = par >> 2, ph = (par >> 1) & 1, pw = par & 1;
+        const uint8_t* base = static_cast<const uint8_t*>(planes[pl]) + ((pd * H + ph) * W + pw) * rs;
+        st = encode_act(&dst[par], base, bf16, p.cpad, (W - pw + 1) / 2, (H - ph + 1) / 2, (D - pd + 1) / 2,
+                        d->batch, 2 * rs, 2 * W * rs, 2 * H * W * rs, D * H * W * rs, p.kc, g.tile_w, g.tile_h,
+                        g.tile_d);
+        if (st) return st;
+      }
+    } else {
+      st = encode_act(&dst[0], planes[pl], bf16, p.cpad, W, H, D, d->batch, rs, W * rs, H * W * rs, D * H * W * rs,
+                      p.kc, g.tile_w, g.tile_h, g.tile_d);
+      if (st) return st;
+    }
+  }
+  const long long wtaps = p.mode == ctmr::kModeUp2 ? 64 : p.taps;
+  st = encode_weight(&maps.b, d->weight, bf16, p.cpad, p.opad, wtaps, p.kc, p.bn);
+  if (st) return st;
+  if (p.exact) {
+    st = encode_weight(&maps.b_lo, d->weight_lo, bf16, p.cpad, p.opad, wtaps, p.kc, p.bn);
+    if (st) return st;
+  }
+
+  cudaError_t e = ctmr::launch_conv3d_umma(maps, g, p.kc, p.exact, smem, stream);
+  return e == cudaSuccess ? CTMR_OK : cuda_fail(e, "conv3d launch");
+}
+
+size_t ctmr_group_norm_workspace_size(int batch, long long voxels, int groups) {
+  if (batch <= 0 || voxels <= 0 || groups <= 0) return 0;
+  return static_cast<size_t>(batch) * ctmr::gn_chunks_for(batch, voxels) * groups * 3 * sizeof(float);
+}
+
+int ctmr_group_norm_affine(ctmr_tensor x, ctmr_tensor x2, int batch, long long voxels, const float* gamma,
+                           const float* beta, int groups, float eps, float* affine, void* workspace,
+                           size_t workspace_bytes, void* stream) {
+  int st = check_view(x, "x", true);
+  if (st) return st;
+  if ((st = check_view(x2, "x2", false))) return st;
+  const int ctot = x.channels + (x2.data ? x2.channels : 0);
+  if (batch <= 0 || voxels <= 0) return fail(CTMR_ERR_INVALID, "group_norm extents");
+  if (groups <= 0 || ctot % groups != 0) return fail(CTMR_ERR_INVALID, "group_norm channels must be divisible by num_groups");
+  if (ctot > 2048) return fail(CTMR_ERR_UNSUPPORTED, "group_norm supports at most 2048 channels");
+  if (affine == nullptr) return fail(CTMR_ERR_INVALID, "affine output missing");
+  const size_t need = ctmr_group_norm_workspace_size(batch, voxels, groups);
+  if (workspace == nullptr || workspace_bytes < need)
+    return fail(CTMR_ERR_WORKSPACE, "group_norm needs %zu workspace bytes, got %zu", need, workspace_bytes);
+  ctmr::GnParams p{};
+  p.src[0] = as_source(x);
+  p.src[1] = as_source(x2);
+  p.batch = batch;
+  p.voxels = voxels;
+  p.groups = groups;
+  p.eps = eps;
+  p.gamma = gamma;
+  p.beta = beta;
+  p.affine = affine;
+  p.partials = static_cast<float*>(workspace);
+  p.chunks = ctmr::gn_chunks_for(batch, voxels);
+  cudaError_t e = ctmr::launch_group_norm_affine(p, static_cast<cudaStream_t>(stream));
+  return e == cudaSuccess ? CTMR_OK : cuda_fail(e, "group_norm launch");
+}
+
+int ctmr_transform(const ctmr_transform_desc* d, void* stream) {
+  if (d == nullptr) return fail(CTMR_ERR_INVALID, "null descriptor");
+  int st = check_view(d->x, "x", true);
+  if (st) return st;
+  if ((st = check_view(d->x2, "x2", false))) return st;
+  if (d->batch <= 0 || d->depth <= 0 || d->height <= 0 || d->width <= 0)
+    return fail(CTMR_ERR_INVALID, "grid must be positive");
+  if (d->y == nullptr || (d->y_dtype != CTMR_DTYPE_F32 && d->y_dtype != CTMR_DTYPE_BF16))
+    return fail(CTMR_ERR_INVALID, "output");
+  const int ctot = d->x.channels + (d->x2.data ? d->x2.channels : 0);
+  if (d->y_channels < ctot || d->y_cstride < d->y_channels) return fail(CTMR_ERR_INVALID, "output channels");
+  if (d->mode == CTMR_TRANSFORM_TRILINEAR && (d->affine != nullptr || d->silu))
+    return fail(CTMR_ERR_UNSUPPORTED, "trilinear upsampling takes no affine/silu");
+  if (d->mode == CTMR_TRANSFORM_AVGPOOL && (d->depth % 2 || d->height % 2 || d->width % 2))
+    return fail(CTMR_ERR_INVALID, "average pooling needs even extents");
+  ctmr::PrepParams pp{};
+  pp.src[0] = as_source(d->x);
+  pp.src[1] = as_source(d->x2);
+  pp.batch = d->batch;
+  pp.sd = d->depth, pp.sh = d->height, pp.sw = d->width;
+  pp.od = d->depth, pp.oh = d->height, pp.ow = d->width;
+  if (d->mode == CTMR_TRANSFORM_TRILINEAR) {
+    pp.mode = ctmr::kPrepTrilinear;
+    pp.od *= 2, pp.oh *= 2, pp.ow *= 2;
+  } else if (d->mode == CTMR_TRANSFORM_AVGPOOL) {
+    pp.mode = ctmr::kPrepAvgPool;
+    pp.od /= 2, pp.oh /= 2, pp.ow /= 2;
+  } else if (d->mode == CTMR_TRANSFORM_COPY) {
+    pp.mode = ctmr::kPrepCopy;
+  } else {
+    return fail(CTMR_ERR_INVALID, "transform mode");
+  }
+  pp.affine = d->affine;
+  pp.silu = d->silu;
+  pp.cpad = d->y_channels;
+  pp.out_cstride = d->y_cstride;
+  pp.out_kind = d->y_dtype == CTMR_DTYPE_BF16 ? ctmr::kPrepOutBF16 : ctmr::kPrepOutF32;
+  pp.out = d->y;
+  cudaError_t e = ctmr::launch_prepare(pp, static_cast<cudaStream_t>(stream));
+  return e == cudaSuccess ? CTMR_OK : cuda_fail(e, "transform launch");
+}
+
+int ctmr_ncdhw_to_ndhwc(const void* x, int x_dtype, void* y, int y_dtype, int batch, int channels, long long voxels,
+                        void* stream) {
+  if (x == nullptr || y == nullptr || batch <= 0 || channels <= 0 || voxels <= 0 || voxels > 0x7FFFFFFF)
+    return fail(CTMR_ERR_INVALID, "layout arguments");
+  cudaError_t e = ctmr::launch_transpose_cs(x, x_dtype == CTMR_DTYPE_BF16, y, y_dtype == CTMR_DTYPE_BF16, batch,
+                                            channels, static_cast<int>(voxels), static_cast<cudaStream_t>(stream));
+  return e == cudaSuccess ? CTMR_OK : cuda_fail(e, "layout launch");
+}
+
+int ctmr_ndhwc_to_ncdhw(const void* x, int x_dtype, void* y, int y_dtype, int batch, int channels, long long voxels,
+                        void* stream) {
+  if (x == nullptr || y == nullptr || batch <= 0 || channels <= 0 || voxels <= 0 || voxels > 0x7FFFFFFF)
+    return fail(CTMR_ERR_INVALID, "layout arguments");
+  cudaError_t e = ctmr::launch_transpose_cs(x, x_dtype == CTMR_DTYPE_BF16, y, y_dtype == CTMR_DTYPE_BF16, batch,
+                                            static_cast<int>(voxels), channels, static_cast<cudaStream_t>(stream));
+  return e == cudaSuccess ? CTMR_OK : cuda_fail(e, "layout launch");
+}
+
+int ctmr_window_accumulate(ctmr_tensor pred, int batch, int wd, int wh, int ww, int z0, int y0, int x0, int od,
+                           int oh, int ow, const float* gz, const float* gy, const float* gx, int scale,
+                           float floor_value, float* acc, float* wsum, void* stream) {
+  int st = check_view(pred, "pred", true);
+  if (st) return st;
+  if (batch <= 0 || wd <= 0 || wh <= 0 || ww <= 0 || scale <= 0 || z0 < 0 || y0 < 0 || x0 < 0 || z0 + wd > od ||
+      y0 + wh > oh || x0 + ww > ow)
+    return fail(CTMR_ERR_INVALID, "window outside the output grid");
+  if (gz == nullptr || gy == nullptr || gx == nullptr || acc == nullptr || wsum == nullptr)
+    return fail(CTMR_ERR_INVALID, "window buffers");
+  ctmr::WindowParams p{};
+  p.pred = pred.data;
+  p.pred_bf16 = pred.dtype == CTMR_DTYPE_BF16;
+  p.pred_cstride = pred.cstride;
+  p.batch = batch;
+  p.channels = pred.channels;
+  p.wd = wd, p.wh = wh, p.ww = ww;
+  p.z0 = z0, p.y0 = y0, p.x0 = x0;
+  p.od = od, p.oh = oh, p.ow = ow;
+  p.gz = gz, p.gy = gy, p.gx = gx;
+  p.scale = scale;
+  p.floor_value = floor_value;
+  p.acc = acc;
+  p.wsum = wsum;
+  cudaError_t e = ctmr::launch_window_accumulate(p, static_cast<cudaStream_t>(stream));
+  return e == cudaSuccess ? CTMR_OK : cuda_fail(e, "window launch");
+}
+
+int ctmr_window_finalize(const float* acc, const float* wsum, float* out, int batch, int channels, int od, int oh,
+                         int ow, int cz0, int cy0, int cx0, int cd, int ch, int cw, void* stream) {
+  if (acc == nullptr || wsum == nullptr || out == nullptr || batch <= 0 || channels <= 0 || cz0 < 0 || cy0 < 0 ||
+      cx0 < 0 || cz0 + cd > od || cy0 + ch > oh || cx0 + cw > ow || cd <= 0 || ch <= 0 || cw <= 0)
+    return fail(CTMR_ERR_INVALID, "window finalize arguments");
+  cudaError_t e = ctmr::launch_window_finalize(acc, wsum, out, batch, channels, od, oh, ow, cz0, cy0, cx0, cd, ch, cw,
+                                               static_cast<cudaStream_t>(stream));
+  return e == cudaSuccess ? CTMR_OK : cuda_fail(e, "window finalize launch");
+}
+
+int ctmr_rflow_step(const float* z, const float* vel, long long n, float guidance, int guided, float dt, float* out,
+                    void* stream) {
+  if (z == nullptr || vel == nullptr || out == nullptr || n <= 0) return fail(CTMR_ERR_INVALID, "rflow arguments");
+  cudaError_t e = ctmr::launch_rflow_step(z, vel, n, guidance, guided, dt, out, static_cast<cudaStream_t>(stream));
+  return e == cudaSuccess ? CTMR_OK : cuda_fail(e, "rflow launch");
+}
+
+int ctmr_get_device_error(unsigned* bits, int clear) {
+  cudaError_t e = cudaDeviceSynchronize();
+  if (e != cudaSuccess) return cuda_fail(e, "synchronize");
+  unsigned v = 0;
+  e = cudaMemcpyFromSymbol(&v, ctmr::g_device_error, sizeof(v));
+  if (e != cudaSuccess) return cuda_fail(e, "read device error");
+  if (bits != nullptr) *bits = v;
+  if (clear && v != 0) {
+    const unsigned zero = 0;
+    e = cudaMemcpyToSymbol(ctmr::g_device_error, &zero, sizeof(zero));
+    if (e != cudaSuccess) return cuda_fail(e, "clear device error");
+  }
+  return CTMR_OK;
+}
+
+}  // extern "C"

@@ -1,0 +1,411 @@
+// Implicit-GEMM 3-D convolution on the sm_100a tensor cores (tcgen05 + TMEM),
+// fed by TMA tiled loads. Activations are channels-last (NDHWC).
+//
+// GEMM view (the reference computes the same contraction, `_nax_conv.py:200-317`):
+//   rows    M = output voxels, one 128-voxel box (tile_w x tile_h x tile_d) per CTA
+//   columns N = output channels, one N tile of `bn` per CTA
+//   depth   K = taps x padded input channels, walked tap-major in KC-channel blocks
+// For each (tap, channel block) one TMA load brings the input box shifted by the
+// tap offset; coordinates that fall outside the volume are zero-filled by the
+// TMA unit, which is exactly the convolution's zero padding, so no padded copy
+// and no im2col buffer exist. Weights are packed [tap][Cout_pad][Cin_pad]
+// (K-major) and loaded as a bn x KC box.
+//
+// Warp roles (192 threads): warp 0 lane 0 issues TMA loads, warp 1 owns TMEM
+// and lane 0 issues tcgen05.mma, warps 2-5 drain the accumulator: TMEM ->
+// registers -> +bias (per channel or per batch item) -> +residual -> store.
+//
+// Precision modes:
+//   bf16:     bf16 x bf16 products, fp32 accumulation, one rounding at the store.
+//   fp32 (EXACT): every fp32 operand v is carried as fp16 hi = half(v) and
+//             lo = half((v - hi) * 2^11); three MMAs per K step accumulate
+//             hi*hi into one TMEM accumulator and hi*lo + lo*hi into a second,
+//             which the epilogue folds in at 2^-11 before any addition. This is
+//             the split-precision scheme of Ootomo & Yokota (2022, "Recovering
+//             single precision accuracy from Tensor Cores while surpassing the
+//             FP32 theoretical peak performance"), the same operand split the
+//             reference uses (`_nax_conv.py:27-35`): ~2^-22 relative product error.
+#include "conv3d_umma.cuh"
+#include "ptx.cuh"
+
+#include <cuda_bf16.h>
+#include <cuda_fp16.h>
+
+namespace ctmr {
+
+__device__ unsigned int g_device_error = 0;
+
+namespace {
+
+constexpr int kThreads = 192;
+constexpr int kRows = 128;
+
+__host__ __device__ constexpr uint32_t round_up_u32(uint32_t v, uint32_t a) { return (v + a - 1) / a * a; }
+
+struct StageLayout {
+  uint32_t a_bytes, b_bytes, stage_bytes;
+  __host__ __device__ StageLayout(int kc, int bn, bool exact) {
+    a_bytes = round_up_u32(kRows * kc * 2, 1024);
+    b_bytes = round_up_u32(static_cast<uint32_t>(bn) * kc * 2, 1024);
+    stage_bytes = (a_bytes + b_bytes) * (exact ? 2u : 1u);
+  }
+};
+
+__device__ __forceinline__ float bf16_to_f32(uint16_t v) { return __uint_as_float(static_cast<uint32_t>(v) << 16); }
+
+__device__ __forceinline__ uint32_t pack_bf16x2(float a, float b) {
+  __nv_bfloat162 h = __floats2bfloat162_rn(a, b);
+  return *reinterpret_cast<uint32_t*>(&h);
+}
+
+// Add the residual and store 16 output columns [n, n+16) of one voxel row.
+__device__ __forceinline__ void store_row16(const ConvGeom& g, float (&v)[16], int n, long long out_off,
+                                            long long res_off) {
+  const int cnt = min(16, g.cout - n);
+  if (cnt <= 0) return;
+  if (g.res != nullptr) {
+    if (g.res_bf16) {
+      const uint16_t* r = static_cast<const uint16_t*>(g.res) + res_off;
+      if (cnt == 16 && (reinterpret_cast<uintptr_t>(r) & 15) == 0) {
+        const uint4 q0 = __ldg(reinterpret_cast<const uint4*>(r));
+        const uint4 q1 = __ldg(reinterpret_cast<const uint4*>(r) + 1);
+        const uint32_t w[8] = {q0.x, q0.y, q0.z, q0.w, q1.x, q1.y, q1.z, q1.w};
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+          v[2 * i] += bf16_to_f32(static_cast<uint16_t>(w[i] & 0xFFFFu));
+          v[2 * i + 1] += bf16_to_f32(static_cast<uint16_t>(w[i] >> 16));
+        }
+      } else {
+        for (int i = 0; i < cnt; ++i) v[i] += bf16_to_f32(r[i]);
+      }
+    } else {
+      const float* r = static_cast<const float*>(g.res) + res_off;
+      if (cnt == 16 && (reinterpret_cast<uintptr_t>(r) & 15) == 0) {
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+          const float4 q = __ldg(reinterpret_cast<const float4*>(r) + i);
+          v[4 * i] += q.x;
+          v[4 * i + 1] += q.y;
+          v[4 * i + 2] += q.z;
+          v[4 * i + 3] += q.w;
+        }
+      } else {
+        for (int i = 0; i < cnt; ++i) v[i] += __ldg(r + i);
+      }
+    }
+  }
+  if (g.out_bf16) {
+    uint16_t* o = static_cast<uint16_t*>(g.out) + out_off;
+    if (cnt == 16 && (reinterpret_cast<uintptr_t>(o) & 15) == 0) {
+      uint4 q0, q1;
+      q0.x = pack_bf16x2(v[0], v[1]);
+      q0.y = pack_bf16x2(v[2], v[3]);
+      q0.z = pack_bf16x2(v[4], v[5]);
+      q0.w = pack_bf16x2(v[6], v[7]);
+      q1.x = pack_bf16x2(v[8], v[9]);
+      q1.y = pack_bf16x2(v[10], v[11]);
+      q1.z = pack_bf16x2(v[12], v[13]);
+      q1.w = pack_bf16x2(v[14], v[15]);
+      reinterpret_cast<uint4*>(o)[0] = q0;
+      reinterpret_cast<uint4*>(o)[1] = q1;
+    } else {
+      for (int i = 0; i < cnt; ++i) {
+        __nv_bfloat16 h = __float2bfloat16_rn(v[i]);
+        o[i] = *reinterpret_cast<uint16_t*>(&h);
+      }
+    }
+  } else {
+    float* o = static_cast<float*>(g.out) + out_off;
+    if (cnt == 16 && (reinterpret_cast<uintptr_t>(o) & 15) == 0) {
+#pragma unroll
+      for (int i = 0; i < 4; ++i)
+        reinterpret_cast<float4*>(o)[i] = make_float4(v[4 * i], v[4 * i + 1], v[4 * i + 2], v[4 * i + 3]);
+    } else {
+      for (int i = 0; i < cnt; ++i) o[i] = v[i];
+    }
+  }
+}
+
+template <int KC, bool EXACT>
+__global__ void __launch_bounds__(kThreads, 1)
+    conv3d_umma_kernel(const __grid_constant__ ConvMaps maps, const __grid_constant__ ConvGeom g) {
+  constexpr uint32_t kRowBytes = KC * 2;
+  constexpr int kSteps = KC / 16;  // K=16 MMAs per channel block
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>(round_up_u32(smem_u32(smem_raw), 1024) - smem_u32(smem_raw) +
+                                             reinterpret_cast<uintptr_t>(smem_raw));
+  const StageLayout L(KC, g.bn, EXACT);
+  const int S = g.stages;
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + static_cast<size_t>(S) * L.stage_bytes);
+  uint64_t* empty = full + S;
+  uint64_t* acc_full = empty + S;
+  uint64_t* chunk_full = acc_full + 1;   // [2]: a promotion chunk of the hi accumulator is complete
+  uint64_t* chunk_empty = chunk_full + 2;  // [2]: the epilogue has drained that chunk buffer
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(chunk_empty + 2);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+
+  // Tile coordinates: w fastest, then h, d, batch item, parity phase.
+  int t = blockIdx.x;
+  const int tw_i = t % g.tiles_w; t /= g.tiles_w;
+  const int th_i = t % g.tiles_h; t /= g.tiles_h;
+  const int td_i = t % g.tiles_d; t /= g.tiles_d;
+  const int b = t % g.batch; t /= g.batch;
+  const int phase = t;
+  const int w0 = tw_i * g.tile_w, h0 = th_i * g.tile_h, d0 = td_i * g.tile_d;
+  const int n0 = blockIdx.y * g.bn;
+  const int n_iter = g.taps * g.kblocks;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < S; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    mbar_init(acc_full, 1);
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&chunk_full[i], 1);
+      mbar_init(&chunk_empty[i], 128);
+    }
+    *abort_flag = 0;
+    fence_barrier_init();
+  }
+  if (warp == 1) {
+    tmem_alloc(tmem_slot, g.tmem_cols);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+
+  if (warp == 0 && lane == 0) {
+    // ------------------------------------------------------------ TMA producer
+    const int nmaps = g.mode == kModeStride2 ? 8 : 1;
+    for (int i = 0; i < nmaps; ++i) {
+      tma_prefetch_desc(&maps.a[i]);
+      if (EXACT) tma_prefetch_desc(&maps.a_lo[i]);
+    }
+    tma_prefetch_desc(&maps.b);
+    if (EXACT) tma_prefetch_desc(&maps.b_lo);
+    const int pd = phase >> 2, ph = (phase >> 1) & 1, pw = phase & 1;
+    int issued = 0;
+    for (int it = 0; it < n_iter; ++it) {
+      const int s = it % S;
+      const uint32_t round = static_cast<uint32_t>(it / S);
+      if (it >= S && !mbar_wait_bounded(&empty[s], (round - 1) & 1u, kErrWaitEmpty)) {
+        *abort_flag = 1;
+        break;
+      }
+      if (*abort_flag) break;
+      const int tap = it / g.kblocks;
+      const int c = (it - tap * g.kblocks) * KC;
+      int map = 0, x = w0, y = h0, z = d0, btap = tap;
+      if (g.mode == kModeConv3) {
+        z += tap / 9 - 1;
+        y += (tap / 3) % 3 - 1;
+        x += tap % 3 - 1;
+      } else if (g.mode == kModeUp2) {
+        z += pd + (tap >> 2) - 1;
+        y += ph + ((tap >> 1) & 1) - 1;
+        x += pw + (tap & 1) - 1;
+        btap = phase * 8 + tap;
+      } else if (g.mode == kModeStride2) {
+        // Input index 2o + k - 1: k = 1 is even element o, k = 0 / 2 are odd elements o - 1 / o.
+        const int kd = tap / 9, kh = (tap / 3) % 3, kw = tap % 3;
+        map = (kd != 1) * 4 + (kh != 1) * 2 + (kw != 1);
+        z -= (kd == 0);
+        y -= (kh == 0);
+        x -= (kw == 0);
+      }
+      uint8_t* st = smem + static_cast<size_t>(s) * L.stage_bytes;
+      mbar_arrive_expect_tx(&full[s], (kRows + static_cast<uint32_t>(g.bn)) * kRowBytes * (EXACT ? 2u : 1u));
+      tma_load_5d(st, &maps.a[map], &full[s], c, x, y, z, b);
+      if (EXACT) tma_load_5d(st + L.a_bytes, &maps.a_lo[map], &full[s], c, x, y, z, b);
+      uint8_t* bs = st + L.a_bytes * (EXACT ? 2 : 1);
+      tma_load_3d(bs, &maps.b, &full[s], c, n0, btap);
+      if (EXACT) tma_load_3d(bs + L.b_bytes, &maps.b_lo, &full[s], c, n0, btap);
+      ++issued;
+    }
+    // Drain: the newest load of every stage must land before the CTA can exit.
+    for (int k = max(0, issued - S); k < issued; ++k) {
+      if (!mbar_wait_bounded(&full[k % S], static_cast<uint32_t>(k / S) & 1u, kErrWaitDrain)) break;
+    }
+  } else if (warp == 1 && lane == 0) {
+    // ------------------------------------------------------------ MMA issuer
+    // EXACT: the hi*hi products accumulate in chunks of `chunk_iters` iterations,
+    // alternating between two TMEM buffers; the epilogue warps add each finished
+    // chunk into fp32 registers with round-to-nearest adds while the next chunk
+    // accumulates. This bounds how long the tensor core's own fp32 accumulation
+    // runs, whose rounding error otherwise grows with K (27 * C_in products).
+    const uint32_t idesc = idesc_f16(!EXACT, kRows, static_cast<uint32_t>(g.bn));
+    const uint32_t bn = static_cast<uint32_t>(g.bn);
+    const uint32_t acc_lo = tmem + 2u * bn;
+    const int T = EXACT ? g.chunk_iters : n_iter;
+    for (int it = 0; it < n_iter; ++it) {
+      const int s = it % S;
+      const int chunk = it / T;
+      const int buf = chunk & 1;
+      const bool chunk_start = it - chunk * T == 0;
+      if (EXACT && chunk_start && chunk >= 2 &&
+          !mbar_wait_bounded(&chunk_empty[buf], static_cast<uint32_t>((chunk >> 1) - 1) & 1u, kErrWaitAcc)) {
+        *abort_flag = 1;
+        break;
+      }
+      if (!mbar_wait_bounded(&full[s], static_cast<uint32_t>(it / S) & 1u, kErrWaitFull)) {
+        *abort_flag = 1;
+        break;
+      }
+      if (*abort_flag) break;
+      tc_fence_after();
+      const uint32_t st = smem_u32(smem + static_cast<size_t>(s) * L.stage_bytes);
+      const uint32_t a_hi = st, a_lo = st + L.a_bytes;
+      const uint32_t b_hi = st + L.a_bytes * (EXACT ? 2 : 1), b_lo = b_hi + L.b_bytes;
+      const uint32_t acc_hi = tmem + static_cast<uint32_t>(buf) * bn;
+#pragma unroll
+      for (int k = 0; k < kSteps; ++k) {
+        const uint32_t koff = static_cast<uint32_t>(k) * 32u;  // 16 fp16/bf16 = 32 B along K
+        umma_f16(acc_hi, smem_desc_kmajor(a_hi + koff, kRowBytes), smem_desc_kmajor(b_hi + koff, kRowBytes),
+                 idesc, (chunk_start && k == 0) ? 0u : 1u);
+        if (EXACT) {
+          umma_f16(acc_lo, smem_desc_kmajor(a_hi + koff, kRowBytes), smem_desc_kmajor(b_lo + koff, kRowBytes),
+                   idesc, (it == 0 && k == 0) ? 0u : 1u);
+          umma_f16(acc_lo, smem_desc_kmajor(a_lo + koff, kRowBytes), smem_desc_kmajor(b_hi + koff, kRowBytes),
+                   idesc, 1u);
+        }
+      }
+      umma_commit(&empty[s]);
+      if (EXACT && (it - chunk * T == T - 1 || it == n_iter - 1)) umma_commit(&chunk_full[buf]);
+    }
+    // Signal the epilogue (also on abort, so it unwinds instead of waiting out its own limit).
+    umma_commit(acc_full);
+  } else if (warp >= 2) {
+    // ------------------------------------------------------------ epilogue
+    const int quarter = warp & 3;
+    const int row = quarter * 32 + lane;
+    const uint32_t lane_addr = tmem + (static_cast<uint32_t>(quarter * 32) << 16);
+    // EXACT: promote the hi chunks into fp32 registers as they complete.
+    float sum[EXACT ? 128 : 1];
+#pragma unroll
+    for (int i = 0; i < (EXACT ? 128 : 1); ++i) sum[i] = 0.f;
+    bool ok = true;
+    if (EXACT) {
+      const int T = g.chunk_iters;
+      const int nchunks = (g.taps * g.kblocks + T - 1) / T;
+      for (int chunk = 0; chunk < nchunks && ok; ++chunk) {
+        const int buf = chunk & 1;
+        ok = mbar_wait_bounded(&chunk_full[buf], static_cast<uint32_t>(chunk >> 1) & 1u, kErrWaitAcc);
+        tc_fence_after();
+#pragma unroll
+        for (int cb = 0; cb < 8; ++cb) {
+          if (cb * 16 < g.bn) {
+            float v[16];
+            tmem_ld16(lane_addr + static_cast<uint32_t>(buf * g.bn + cb * 16), v);
+#pragma unroll
+            for (int i = 0; i < 16; ++i) sum[(cb * 16 + i) & (EXACT ? 127 : 0)] += v[i];
+          }
+        }
+        tc_fence_before();
+        mbar_arrive(&chunk_empty[buf]);
+      }
+    }
+    ok = mbar_wait_bounded(acc_full, 0, kErrWaitAcc) && ok;
+    tc_fence_after();
+    const int ww = row % g.tile_w;
+    const int hh = (row / g.tile_w) % g.tile_h;
+    const int dd = row / (g.tile_w * g.tile_h);
+    const int rw = w0 + ww, rh = h0 + hh, rd = d0 + dd;
+    const bool valid = ok && rw < g.row_w && rh < g.row_h && rd < g.row_d;
+    int ow = rw, oh = rh, od = rd;
+    if (g.mode == kModeUp2) {
+      od = 2 * rd + (phase >> 2);
+      oh = 2 * rh + ((phase >> 1) & 1);
+      ow = 2 * rw + (phase & 1);
+    }
+    const long long vox = ((static_cast<long long>(b) * g.out_d + od) * g.out_h + oh) * g.out_w + ow;
+    const long long out_base = vox * g.out_cstride + g.out_coff;
+    long long res_base = 0;
+    if (g.res != nullptr) {
+      const int qd = g.res_up ? od >> 1 : od, qh = g.res_up ? oh >> 1 : oh, qw = g.res_up ? ow >> 1 : ow;
+      res_base = (((static_cast<long long>(b) * g.res_d + qd) * g.res_h + qh) * g.res_w + qw) * g.res_cstride;
+    }
+    const float* bias = g.bias != nullptr ? g.bias + static_cast<long long>(b) * g.bias_bstride : nullptr;
+#pragma unroll
+    for (int cb = 0; cb < 8; ++cb) {
+      const int c = cb * 16;
+      if (c < g.bn) {
+        float v[16];
+        if (EXACT) {
+          float l[16];
+          tmem_ld16(lane_addr + static_cast<uint32_t>(2 * g.bn + c), l);
+#pragma unroll
+          for (int i = 0; i < 16; ++i) v[i] = fmaf(l[i], g.lo_scale, sum[(c + i) & (EXACT ? 127 : 0)]);
+        } else {
+          tmem_ld16(lane_addr + static_cast<uint32_t>(c), v);
+        }
+        const int n = n0 + c;
+        if (valid && n < g.cout) {
+          if (bias != nullptr) {
+            const int cnt = min(16, g.cout - n);
+            for (int i = 0; i < cnt; ++i) v[i] += __ldg(bias + n + i);
+          }
+          store_row16(g, v, n, out_base + n, res_base + n);
+        }
+      }
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem, g.tmem_cols);
+  }
+}
+
+}  // namespace
+
+// ---------------------------------------------------------------- host side
+
+template <int KC, bool EXACT>
+static cudaError_t launch_typed(const ConvMaps& maps, const ConvGeom& g, dim3 grid, size_t smem,
+                                cudaStream_t stream) {
+  auto kern = conv3d_umma_kernel<KC, EXACT>;
+  cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
+  if (e != cudaSuccess) return e;
+  kern<<<grid, kThreads, smem, stream>>>(maps, g);
+  return cudaGetLastError();
+}
+
+// Chooses the pipeline depth for the smem budget: two CTAs per SM when at least
+// three stages fit in half the SM's shared memory, otherwise one deeper CTA.
+int conv_stage_plan(int kc, int bn, bool exact, bool one_cta_per_sm, size_t* smem_bytes) {
+  const StageLayout L(kc, bn, exact);
+  const size_t extra = 1024 /*align*/ + 256 /*barriers*/;
+  const size_t half_budget = 113 * 1024;
+  const size_t full_budget = 227 * 1024;
+  int stages = one_cta_per_sm ? 0 : static_cast<int>((half_budget - extra) / L.stage_bytes);
+  if (stages < 3) stages = static_cast<int>((full_budget - extra) / L.stage_bytes);
+  if (stages > 8) stages = 8;
+  if (stages < 2) return 0;
+  *smem_bytes = static_cast<size_t>(stages) * L.stage_bytes + extra;
+  return stages;
+}
+
+cudaError_t launch_conv3d_umma(const ConvMaps& maps, const ConvGeom& g, int kc, bool exact, size_t smem,
+                               cudaStream_t stream) {
+  const int n_tiles = (g.cout + g.bn - 1) / g.bn;
+  const long long m_tiles = static_cast<long long>(g.tiles_w) * g.tiles_h * g.tiles_d * g.batch * g.phases;
+  if (m_tiles <= 0 || m_tiles > 0x7FFFFFFFLL || n_tiles <= 0 || n_tiles > 65535) return cudaErrorInvalidValue;
+  const dim3 grid(static_cast<unsigned>(m_tiles), static_cast<unsigned>(n_tiles));
+  if (kc == 64) return exact ? launch_typed<64, true>(maps, g, grid, smem, stream)
+                             : launch_typed<64, false>(maps, g, grid, smem, stream);
+  if (kc == 32) return exact ? launch_typed<32, true>(maps, g, grid, smem, stream)
+                             : launch_typed<32, false>(maps, g, grid, smem, stream);
+  if (kc == 16) return exact ? launch_typed<16, true>(maps, g, grid, smem, stream)
+                             : launch_typed<16, false>(maps, g, grid, smem, stream);
+  return cudaErrorInvalidValue;
+}
+
+}  // namespace ctmr

@@ -1,0 +1,221 @@
+// GroupNorm statistics over NDHWC activations -> per-channel (scale, offset)
+// pairs, the operand of the conv prologue. Counterpart of the external
+// `medmlx_core.group_norm.group_norm_affine` the reference calls at
+// `fast_fp32.py:183-189` (layout (B*C*2), consumed at `_nax_conv.py:174-176`).
+//
+// Pass 1 (grid chunks x batch): each block reads a contiguous voxel range with
+// 16-byte loads (every voxel row is C contiguous channels). A thread owns one
+// 8-channel slice and a voxel lane; it accumulates sums of (x - pivot) and
+// (x - pivot)^2 around its first value, converts them to (count, mean, M2), and
+// the block merges lanes, then channels into groups, in a fixed order (Chan et
+// al.'s pairwise update), writing one (n, mean, M2) partial per group.
+// Pass 2 (grid batch): one thread per group merges the chunk partials in
+// order in double precision, then writes scale = gamma * rstd and
+// offset = beta - mean * scale for each channel. The fixed merge order makes
+// the result bitwise reproducible run to run.
+#include <cuda_runtime.h>
+#include <cstdint>
+
+#include "groupnorm.cuh"
+
+namespace ctmr {
+namespace {
+
+constexpr int kGnThreads = 256;
+
+__device__ __forceinline__ float gn_load(const PrepSource& s, long long vox, int c) {
+  const long long i = vox * s.cstride + c;
+  if (s.bf16) return __uint_as_float(static_cast<uint32_t>(__ldg(static_cast<const uint16_t*>(s.ptr) + i)) << 16);
+  return __ldg(static_cast<const float*>(s.ptr) + i);
+}
+
+__device__ __forceinline__ void gn_load8(const GnParams& p, long long vox, int c0, float (&v)[8], int& cnt) {
+  const int ctot = p.src[0].channels + p.src[1].channels;
+  cnt = min(8, ctot - c0);
+  const PrepSource& s0 = p.src[0];
+  if (cnt == 8 && c0 + 8 <= s0.channels && !s0.bf16) {
+    const float* ptr = static_cast<const float*>(s0.ptr) + vox * s0.cstride + c0;
+    if ((reinterpret_cast<uintptr_t>(ptr) & 15) == 0) {
+      const float4 a = __ldg(reinterpret_cast<const float4*>(ptr));
+      const float4 b = __ldg(reinterpret_cast<const float4*>(ptr) + 1);
+      v[0] = a.x; v[1] = a.y; v[2] = a.z; v[3] = a.w; v[4] = b.x; v[5] = b.y; v[6] = b.z; v[7] = b.w;
+      return;
+    }
+  }
+  if (cnt == 8 && c0 + 8 <= s0.channels && s0.bf16) {
+    const uint16_t* ptr = static_cast<const uint16_t*>(s0.ptr) + vox * s0.cstride + c0;
+    if ((reinterpret_cast<uintptr_t>(ptr) & 15) == 0) {
+      const uint4 q = __ldg(reinterpret_cast<const uint4*>(ptr));
+      const uint32_t w[4] = {q.x, q.y, q.z, q.w};
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        v[2 * i] = __uint_as_float(w[i] << 16);
+        v[2 * i + 1] = __uint_as_float(w[i] & 0xFFFF0000u);
+      }
+      return;
+    }
+  }
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+    const int c = c0 + i;
+    if (i >= cnt) v[i] = 0.f;
+    else if (c < s0.channels) v[i] = gn_load(s0, vox, c);
+    else v[i] = gn_load(p.src[1], vox, c - s0.channels);
+  }
+}
+
+struct Moments {
+  float n, mean, m2;
+};
+
+__device__ __forceinline__ Moments merge(Moments a, Moments b) {
+  if (b.n == 0.f) return a;
+  if (a.n == 0.f) return b;
+  const float n = a.n + b.n;
+  const float delta = b.mean - a.mean;
+  const float fb = b.n / n;
+  Moments r;
+  r.n = n;
+  r.mean = fmaf(delta, fb, a.mean);
+  r.m2 = a.m2 + b.m2 + delta * delta * a.n * fb;
+  return r;
+}
+
+__global__ void __launch_bounds__(kGnThreads) gn_partial_kernel(const GnParams p) {
+  __shared__ float s_mean[kGnThreads][8];
+  __shared__ float s_m2[kGnThreads][8];
+  __shared__ float s_n[kGnThreads];
+  extern __shared__ float s_chan[];  // [ctot][3]
+  const int ctot = p.src[0].channels + p.src[1].channels;
+  const int nslices = (ctot + 7) / 8;
+  const int lanes = kGnThreads / nslices;
+  const int tid = threadIdx.x;
+  const int slice = tid % nslices;
+  const int lane = tid / nslices;
+  const int b = blockIdx.y;
+  const long long per = (p.voxels + p.chunks - 1) / p.chunks;
+  const long long v_begin = min(p.voxels, per * blockIdx.x);
+  const long long v_end = min(p.voxels, v_begin + per);
+  const long long base = static_cast<long long>(b) * p.voxels;
+
+  float pivot[8], s[8], q[8];
+  float n = 0.f;
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+    pivot[i] = 0.f;
+    s[i] = 0.f;
+    q[i] = 0.f;
+  }
+  if (lane < lanes) {
+    long long v = v_begin + lane;
+    if (v < v_end) {
+      float x[8];
+      int cnt;
+      gn_load8(p, base + v, slice * 8, x, cnt);
+#pragma unroll
+      for (int i = 0; i < 8; ++i) pivot[i] = x[i];
+      n = 1.f;
+      v += lanes;
+    }
+    for (; v < v_end; v += lanes) {
+      float x[8];
+      int cnt;
+      gn_load8(p, base + v, slice * 8, x, cnt);
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        const float d = x[i] - pivot[i];
+        s[i] += d;
+        q[i] = fmaf(d, d, q[i]);
+      }
+      n += 1.f;
+    }
+  }
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+    const float mean_d = n > 0.f ? s[i] / n : 0.f;
+    s_mean[tid][i] = pivot[i] + mean_d;
+    s_m2[tid][i] = fmaxf(0.f, q[i] - s[i] * mean_d);
+  }
+  s_n[tid] = (lane < lanes) ? n : 0.f;
+  __syncthreads();
+
+  // Lanes -> channels (fixed lane order).
+  for (int c = tid; c < ctot; c += kGnThreads) {
+    const int sl = c / 8, i = c % 8;
+    Moments m{0.f, 0.f, 0.f};
+    for (int l = 0; l < lanes; ++l) {
+      const int t = l * nslices + sl;
+      m = merge(m, Moments{s_n[t], s_mean[t][i], s_m2[t][i]});
+    }
+    s_chan[3 * c] = m.n;
+    s_chan[3 * c + 1] = m.mean;
+    s_chan[3 * c + 2] = m.m2;
+  }
+  __syncthreads();
+  // Channels -> groups (fixed channel order).
+  const int cpg = ctot / p.groups;
+  for (int g = tid; g < p.groups; g += kGnThreads) {
+    Moments m{0.f, 0.f, 0.f};
+    for (int c = g * cpg; c < (g + 1) * cpg; ++c) m = merge(m, Moments{s_chan[3 * c], s_chan[3 * c + 1], s_chan[3 * c + 2]});
+    float* out = p.partials + ((static_cast<long long>(b) * p.chunks + blockIdx.x) * p.groups + g) * 3;
+    out[0] = m.n;
+    out[1] = m.mean;
+    out[2] = m.m2;
+  }
+}
+
+__global__ void gn_finalize_kernel(const GnParams p) {
+  const int b = blockIdx.x;
+  const int ctot = p.src[0].channels + p.src[1].channels;
+  const int cpg = ctot / p.groups;
+  for (int g = threadIdx.x; g < p.groups; g += blockDim.x) {
+    double n = 0.0, mean = 0.0, m2 = 0.0;
+    for (int k = 0; k < p.chunks; ++k) {
+      const float* q = p.partials + ((static_cast<long long>(b) * p.chunks + k) * p.groups + g) * 3;
+      const double nb = q[0];
+      if (nb == 0.0) continue;
+      const double tot = n + nb;
+      const double delta = static_cast<double>(q[1]) - mean;
+      mean += delta * nb / tot;
+      m2 += static_cast<double>(q[2]) + delta * delta * n * nb / tot;
+      n = tot;
+    }
+    const double var = n > 0.0 ? m2 / n : 0.0;
+    const double rstd = 1.0 / sqrt(var + static_cast<double>(p.eps));
+    for (int c = g * cpg; c < (g + 1) * cpg; ++c) {
+      const double gam = p.gamma != nullptr ? static_cast<double>(p.gamma[c]) : 1.0;
+      const double bet = p.beta != nullptr ? static_cast<double>(p.beta[c]) : 0.0;
+      const double scale = gam * rstd;
+      float* a = p.affine + (static_cast<long long>(b) * ctot + c) * 2;
+      a[0] = static_cast<float>(scale);
+      a[1] = static_cast<float>(bet - mean * scale);
+    }
+  }
+}
+
+}  // namespace
+
+int gn_chunks_for(int batch, long long voxels) {
+  long long chunks = (4LL * 148 + batch - 1) / batch;
+  const long long max_chunks = (voxels + 255) / 256;
+  if (chunks > max_chunks) chunks = max_chunks;
+  if (chunks < 1) chunks = 1;
+  return static_cast<int>(chunks);
+}
+
+cudaError_t launch_group_norm_affine(const GnParams& p, cudaStream_t stream) {
+  const int ctot = p.src[0].channels + p.src[1].channels;
+  const size_t chan_smem = static_cast<size_t>(ctot) * 3 * sizeof(float);
+  if (chan_smem > 48 * 1024) {
+    cudaError_t e = cudaFuncSetAttribute(gn_partial_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         static_cast<int>(chan_smem));
+    if (e != cudaSuccess) return e;
+  }
+  gn_partial_kernel<<<dim3(p.chunks, p.batch), kGnThreads, chan_smem, stream>>>(p);
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return e;
+  gn_finalize_kernel<<<p.batch, 128, 0, stream>>>(p);
+  return cudaGetLastError();
+}
+
+}  // namespace ctmr

@@ -1,0 +1,83 @@
+// Weight packing for the implicit-GEMM convolution: Torch (O, C, k, k, k) fp32
+// -> K-major taps [T][O_pad][C_pad] in bf16, or in fp16 hi/lo planes for the
+// split-fp32 mode. Counterpart of `pack_weight` / `pack_upsample_weight`
+// (`_nax_conv.py:391-445`), with the tap-major rows transposed to the K-major
+// operand layout the tensor cores read.
+//
+// For a nearest-2x-upsampled input (T = 64 = 8 parities x 8 taps) the three
+// taps of each axis fold into two per output parity p: output 2m + p reads
+// upsampled 2m + p - 1 + k = source m - 1, m, m (p = 0) or m, m, m + 1 (p = 1),
+// so tap t of parity p (source offset p + t - 1) sums the kernel taps
+// {0} / {1, 2} for p = 0 and {0, 1} / {2} for p = 1. The folded sums are
+// formed in fp32 before rounding or splitting, as in the reference.
+#include <cuda_bf16.h>
+#include <cuda_fp16.h>
+#include <cstdint>
+
+#include "pack.cuh"
+
+namespace ctmr {
+namespace {
+
+__device__ __forceinline__ void fold_range(int p, int t, int& k0, int& k1) {
+  // Kernel taps [k0, k1] merged into folded tap t of parity p.
+  if (p == 0) {
+    k0 = t == 0 ? 0 : 1;
+    k1 = t == 0 ? 0 : 2;
+  } else {
+    k0 = t == 0 ? 0 : 2;
+    k1 = t == 0 ? 1 : 2;
+  }
+}
+
+__global__ void pack_weight_kernel(const float* __restrict__ w, int O, int C, int k, int upsample, int opad,
+                                   int cpad, int split, void* __restrict__ out, void* __restrict__ out_lo) {
+  const int taps = upsample ? 64 : k * k * k;
+  const long long total = static_cast<long long>(taps) * opad * cpad;
+  for (long long i = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x; i < total;
+       i += static_cast<long long>(gridDim.x) * blockDim.x) {
+    const int c = static_cast<int>(i % cpad);
+    const int o = static_cast<int>((i / cpad) % opad);
+    const int tap = static_cast<int>(i / (static_cast<long long>(cpad) * opad));
+    float v = 0.f;
+    if (o < O && c < C) {
+      const float* src = w + (static_cast<long long>(o) * C + c) * k * k * k;
+      if (!upsample) {
+        v = src[tap];
+      } else {
+        const int phase = tap >> 3, t = tap & 7;
+        int d0, d1, h0, h1, w0, w1;
+        fold_range(phase >> 2, t >> 2, d0, d1);
+        fold_range((phase >> 1) & 1, (t >> 1) & 1, h0, h1);
+        fold_range(phase & 1, t & 1, w0, w1);
+        for (int kd = d0; kd <= d1; ++kd)
+          for (int kh = h0; kh <= h1; ++kh)
+            for (int kw = w0; kw <= w1; ++kw) v += src[(kd * 3 + kh) * 3 + kw];
+      }
+    }
+    if (split) {
+      const __half hi = __float2half_rn(v);
+      const __half lo = __float2half_rn((v - __half2float(hi)) * 2048.f);
+      static_cast<__half*>(out)[i] = hi;
+      static_cast<__half*>(out_lo)[i] = lo;
+    } else {
+      static_cast<__nv_bfloat16*>(out)[i] = __float2bfloat16_rn(v);
+    }
+  }
+}
+
+}  // namespace
+
+cudaError_t launch_pack_weight(const float* w, int O, int C, int k, int upsample, int opad, int cpad, int split,
+                               void* out, void* out_lo, cudaStream_t stream) {
+  const int taps = upsample ? 64 : k * k * k;
+  const long long total = static_cast<long long>(taps) * opad * cpad;
+  long long blocks = (total + 255) / 256;
+  if (blocks > 148LL * 32) blocks = 148LL * 32;
+  if (blocks < 1) blocks = 1;
+  pack_weight_kernel<<<static_cast<unsigned>(blocks), 256, 0, stream>>>(w, O, C, k, upsample, opad, cpad, split,
+                                                                        out, out_lo);
+  return cudaGetLastError();
+}
+
+}  // namespace ctmr

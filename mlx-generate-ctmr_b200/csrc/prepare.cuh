@@ -1,0 +1,35 @@
+// Parameters of the conv-input preparation pass (see prepare.cu).
+#pragma once
+
+#include <cuda_runtime.h>
+
+namespace ctmr {
+
+enum PrepMode : int { kPrepCopy = 0, kPrepTrilinear = 1, kPrepAvgPool = 2 };
+enum PrepOut : int { kPrepOutBF16 = 0, kPrepOutSplitF16 = 1, kPrepOutF32 = 2 };
+
+struct PrepSource {
+  const void* ptr;       // NDHWC rows, `cstride` elements apart
+  int bf16;              // 1: bf16 elements, 0: fp32
+  int channels;          // channels taken from this source (0: unused)
+  long long cstride;
+};
+
+struct PrepParams {
+  PrepSource src[2];     // virtual channel concat src[0] ++ src[1]
+  int batch;
+  int sd, sh, sw;        // source grid
+  int od, oh, ow;        // output grid
+  int mode;
+  const float* affine;   // [batch][channels][2] (scale, offset) or null
+  int silu;
+  int cpad;              // output channels (zero padded past the sources)
+  long long out_cstride; // elements between output voxel rows (>= cpad)
+  int out_kind;
+  void* out;             // bf16 / fp16 hi / fp32 plane
+  void* out_lo;          // fp16 lo plane for kPrepOutSplitF16
+};
+
+cudaError_t launch_prepare(const PrepParams& p, cudaStream_t stream);
+
+}  // namespace ctmr

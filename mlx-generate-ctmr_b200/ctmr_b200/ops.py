@@ -1,0 +1,347 @@
+"""Torch-tensor entry points over the C ABI.
+
+Activations are torch tensors with the reference's logical NCDHW shape stored
+channels-last (``torch.channels_last_3d``), i.e. physically NDHWC rows; a
+channel slice of such a tensor is also accepted (its rows keep the parent's
+stride). Every function launches on the current torch CUDA stream and
+allocates its outputs and workspaces through torch's caching allocator, so the
+calls can be captured in CUDA graphs.
+"""
+
+from __future__ import annotations
+
+import ctypes
+from dataclasses import dataclass
+
+import torch
+
+from . import _lib
+from ._lib import LIB, check
+
+F32 = torch.float32
+BF16 = torch.bfloat16
+PRECISIONS = ("fp32", "bf16")
+
+
+def _stream() -> int:
+    return torch.cuda.current_stream().cuda_stream
+
+
+def _dtype_code(dtype: torch.dtype) -> int:
+    if dtype == F32:
+        return _lib.DTYPE_F32
+    if dtype == BF16:
+        return _lib.DTYPE_BF16
+    raise ValueError(f"ctmr_b200 activations must be float32 or bfloat16, got {dtype}")
+
+
+def _precision_code(precision: str) -> int:
+    if precision == "fp32":
+        return _lib.PRECISION_FP32
+    if precision == "bf16":
+        return _lib.PRECISION_BF16
+    raise ValueError(f"precision must be one of {PRECISIONS}; got {precision!r}")
+
+
+def rows_stride(x: torch.Tensor) -> int:
+    """Elements between voxel rows of an NDHWC-stored NCDHW tensor; raises if not so stored."""
+    if x.dim() != 5:
+        raise ValueError(f"expected an NCDHW tensor, got shape {tuple(x.shape)}")
+    b, c, d, h, w = (int(n) for n in x.shape)
+    if w > 1:
+        cs = x.stride(4)
+    elif h > 1:
+        cs = x.stride(3)
+    elif d > 1:
+        cs = x.stride(2)
+    elif b > 1:
+        cs = x.stride(0)
+    else:
+        cs = c
+    ok = cs >= c and (c == 1 or x.stride(1) == 1)
+    ok = ok and (w == 1 or x.stride(4) == cs) and (h == 1 or x.stride(3) == w * cs)
+    ok = ok and (d == 1 or x.stride(2) == h * w * cs) and (b == 1 or x.stride(0) == d * h * w * cs)
+    if not ok:
+        raise ValueError(
+            f"tensor of shape {tuple(x.shape)} and strides {x.stride()} is not channels-last (NDHWC rows)"
+        )
+    return int(cs)
+
+
+def view(x: torch.Tensor | None) -> _lib.Tensor:
+    """``ctmr_tensor`` for an NDHWC-stored tensor (or an absent one)."""
+    if x is None:
+        return _lib.Tensor(None, 0, 0, 0)
+    if not x.is_cuda:
+        raise ValueError("ctmr_b200 tensors must live on a CUDA device")
+    return _lib.Tensor(x.data_ptr(), _dtype_code(x.dtype), int(x.shape[1]), rows_stride(x))
+
+
+def empty_ndhwc(b: int, c: int, d: int, h: int, w: int, dtype: torch.dtype, device) -> torch.Tensor:
+    """Uninitialised NCDHW tensor with channels-last storage."""
+    return torch.empty((b, c, d, h, w), dtype=dtype, device=device, memory_format=torch.channels_last_3d)
+
+
+def to_ndhwc(x: torch.Tensor, dtype: torch.dtype | None = None) -> torch.Tensor:
+    """Channels-last copy of an NCDHW tensor (via the library's transpose kernel when contiguous NCDHW)."""
+    dtype = dtype or x.dtype
+    try:
+        rows_stride(x)
+        return x if x.dtype == dtype else transform(x, out_dtype=dtype)
+    except ValueError:
+        pass
+    x = x.contiguous()
+    b, c, d, h, w = x.shape
+    out = empty_ndhwc(b, c, d, h, w, dtype, x.device)
+    check(
+        LIB.ctmr_ncdhw_to_ndhwc(
+            x.data_ptr(), _dtype_code(x.dtype), out.data_ptr(), _dtype_code(dtype), b, c, d * h * w, _stream()
+        ),
+        "ncdhw_to_ndhwc",
+    )
+    return out
+
+
+def to_ncdhw(x: torch.Tensor, dtype: torch.dtype = F32) -> torch.Tensor:
+    """Contiguous NCDHW copy of a channels-last tensor (library transpose kernel)."""
+    cs = rows_stride(x)
+    b, c, d, h, w = x.shape
+    if cs != c:
+        x = transform(x, out_dtype=x.dtype)
+    out = torch.empty((b, c, d, h, w), dtype=dtype, device=x.device)
+    check(
+        LIB.ctmr_ndhwc_to_ncdhw(
+            x.data_ptr(), _dtype_code(x.dtype), out.data_ptr(), _dtype_code(dtype), b, c, d * h * w, _stream()
+        ),
+        "ndhwc_to_ncdhw",
+    )
+    return out
+
+
+@dataclass(frozen=True)
+class PackedWeight:
+    """Convolution weight packed for the tensor cores (``ctmr_pack_weight``)."""
+
+    hi: torch.Tensor
+    lo: torch.Tensor | None
+    out_channels: int
+    in_channels: int
+    kernel_size: int
+    upsample: bool
+    precision: str
+
+
+def pack_weight(weight: torch.Tensor, precision: str, *, upsample: bool = False) -> PackedWeight:
+    """Pack a Torch ``(O, C, k, k, k)`` weight; the nearest-2x fold with ``upsample``.
+
+    Counterpart of ``pack_weight`` / ``pack_upsample_weight`` (``_nax_conv.py:391-445``).
+    """
+    if weight.dim() != 5 or weight.shape[2] != weight.shape[3] or weight.shape[3] != weight.shape[4]:
+        raise ValueError(f"conv weight must be (O, C, k, k, k); got {tuple(weight.shape)}")
+    o, c, k = int(weight.shape[0]), int(weight.shape[1]), int(weight.shape[2])
+    code = _precision_code(precision)
+    w = weight.detach().to(dtype=F32).contiguous()
+    n = int(LIB.ctmr_packed_weight_elems(o, c, k, int(upsample)))
+    if n == 0:
+        raise ValueError(f"unsupported conv weight shape {tuple(weight.shape)}")
+    if precision == "fp32":
+        hi = torch.empty(n, dtype=torch.float16, device=w.device)
+        lo = torch.empty(n, dtype=torch.float16, device=w.device)
+    else:
+        hi = torch.empty(n, dtype=BF16, device=w.device)
+        lo = None
+    check(
+        LIB.ctmr_pack_weight(
+            w.data_ptr(), o, c, k, int(upsample), code, hi.data_ptr(), lo.data_ptr() if lo is not None else None,
+            _stream(),
+        ),
+        "pack_weight",
+    )
+    return PackedWeight(hi, lo, o, c, k, upsample, precision)
+
+
+def conv3d(
+    x: torch.Tensor,
+    packed: PackedWeight,
+    bias: torch.Tensor | None = None,
+    *,
+    x2: torch.Tensor | None = None,
+    affine: torch.Tensor | None = None,
+    silu: bool = False,
+    stride: int = 1,
+    trilinear: bool = False,
+    avgpool: bool = False,
+    residual: torch.Tensor | None = None,
+    residual_upsampled: bool = False,
+    out: torch.Tensor | None = None,
+    out_dtype: torch.dtype | None = None,
+) -> torch.Tensor:
+    """``conv(prepare(x ++ x2)) + bias (+ residual)`` in one call (``ctmr_conv3d``).
+
+    Mirrors ``nax_conv3d`` (``_nax_conv.py:475-487``): ``bias`` is ``(O,)`` or per
+    batch item ``(B, O)``; ``affine`` is the ``(B, C, 2)`` group-norm scale/offset;
+    ``silu`` follows it; ``packed.upsample`` convolves the nearest-2x upsampling,
+    ``trilinear`` the half-pixel trilinear-2x upsampling and ``avgpool`` the 2x2x2
+    mean of the prepared input; the residual (on the output grid, or the half grid
+    when ``residual_upsampled``) is added before the single rounding.
+    """
+    b, cx, d, h, w = (int(n) for n in x.shape)
+    cin = cx + (int(x2.shape[1]) if x2 is not None else 0)
+    if x2 is not None and tuple(x2.shape[2:]) != (d, h, w):
+        raise ValueError(f"concat inputs differ in grid: {tuple(x.shape)} vs {tuple(x2.shape)}")
+    if cin != packed.in_channels:
+        raise ValueError(f"packed weight has {packed.in_channels} input channels, input has {cin}")
+    k = packed.kernel_size
+    if packed.upsample:
+        od, oh, ow = 2 * d, 2 * h, 2 * w
+    elif trilinear:
+        od, oh, ow = 2 * d, 2 * h, 2 * w
+    elif avgpool:
+        od, oh, ow = d // 2, h // 2, w // 2
+    elif stride == 2:
+        od, oh, ow = (d - 1) // 2 + 1, (h - 1) // 2 + 1, (w - 1) // 2 + 1
+    else:
+        od, oh, ow = d, h, w
+    o = packed.out_channels
+    if bias is not None:
+        bias = bias.to(dtype=F32).contiguous()
+        if not (bias.shape == (o,) or bias.shape == (b, o)):
+            raise ValueError(f"bias shape {tuple(bias.shape)} must be ({o},) or ({b}, {o})")
+    if affine is not None:
+        affine = affine.to(dtype=F32).contiguous()
+        if affine.numel() != b * cin * 2:
+            raise ValueError(f"affine must hold (B, C, 2) = ({b}, {cin}, 2) values")
+    if residual is not None:
+        expect = (b, o, od // 2, oh // 2, ow // 2) if residual_upsampled else (b, o, od, oh, ow)
+        if tuple(residual.shape) != expect:
+            raise ValueError(f"residual shape {tuple(residual.shape)} != output {expect}")
+    if out is None:
+        dtype = out_dtype or (F32 if packed.precision == "fp32" else BF16)
+        out = empty_ndhwc(b, o, od, oh, ow, dtype, x.device)
+    elif tuple(out.shape) != (b, o, od, oh, ow):
+        raise ValueError(f"out shape {tuple(out.shape)} != {(b, o, od, oh, ow)}")
+    ycs = rows_stride(out)
+    desc = _lib.Conv3dDesc()
+    desc.batch, desc.depth, desc.height, desc.width = b, d, h, w
+    desc.x = view(x)
+    desc.x2 = view(x2)
+    desc.out_channels = o
+    desc.kernel_size = k
+    desc.stride = stride
+    desc.upsample = int(packed.upsample)
+    desc.trilinear = int(trilinear)
+    desc.avgpool = int(avgpool)
+    desc.precision = _precision_code(packed.precision)
+    desc.weight = packed.hi.data_ptr()
+    desc.weight_lo = packed.lo.data_ptr() if packed.lo is not None else None
+    desc.affine = affine.data_ptr() if affine is not None else None
+    desc.silu = int(silu)
+    desc.bias = bias.data_ptr() if bias is not None else None
+    desc.bias_per_batch = int(bias is not None and bias.dim() == 2)
+    desc.residual = view(residual)
+    desc.residual_upsampled = int(residual_upsampled)
+    desc.y = out.data_ptr()  # a channel slice's pointer already includes its first channel
+    desc.y_dtype = _dtype_code(out.dtype)
+    desc.y_cstride = ycs
+    desc.y_coffset = 0
+    ws_bytes = int(LIB.ctmr_conv3d_workspace_size(ctypes.byref(desc)))
+    if ws_bytes == 0:
+        # Either no preparation is needed or the descriptor is invalid; ctmr_conv3d reports which.
+        ws = None
+    else:
+        ws = torch.empty(ws_bytes, dtype=torch.uint8, device=x.device)
+    check(
+        LIB.ctmr_conv3d(ctypes.byref(desc), ws.data_ptr() if ws is not None else None, ws_bytes, _stream()),
+        "conv3d",
+    )
+    return out
+
+
+def group_norm_affine(
+    x: torch.Tensor,
+    weight: torch.Tensor | None,
+    bias: torch.Tensor | None,
+    *,
+    groups: int,
+    eps: float,
+    x2: torch.Tensor | None = None,
+) -> torch.Tensor:
+    """GroupNorm statistics of ``x ++ x2`` as ``(B, C, 2)`` (scale, offset) pairs (``ctmr_group_norm_affine``)."""
+    b, c, d, h, w = (int(n) for n in x.shape)
+    ctot = c + (int(x2.shape[1]) if x2 is not None else 0)
+    voxels = d * h * w
+    if ctot % groups:
+        raise ValueError("group_norm channels must be divisible by num_groups")
+    gamma = weight.to(dtype=F32).contiguous() if weight is not None else None
+    beta = bias.to(dtype=F32).contiguous() if bias is not None else None
+    affine = torch.empty((b, ctot, 2), dtype=F32, device=x.device)
+    ws_bytes = int(LIB.ctmr_group_norm_workspace_size(b, voxels, groups))
+    ws = torch.empty(max(ws_bytes, 4), dtype=torch.uint8, device=x.device)
+    check(
+        LIB.ctmr_group_norm_affine(
+            view(x), view(x2), b, voxels,
+            gamma.data_ptr() if gamma is not None else None,
+            beta.data_ptr() if beta is not None else None,
+            groups, float(eps), affine.data_ptr(), ws.data_ptr(), ws_bytes, _stream(),
+        ),
+        "group_norm_affine",
+    )
+    return affine
+
+
+def transform(
+    x: torch.Tensor,
+    *,
+    x2: torch.Tensor | None = None,
+    mode: int = _lib.TRANSFORM_COPY,
+    affine: torch.Tensor | None = None,
+    silu: bool = False,
+    out_dtype: torch.dtype | None = None,
+    out_channels: int | None = None,
+    out: torch.Tensor | None = None,
+) -> torch.Tensor:
+    """Materialise ``mode(silu?(affine?(x ++ x2)))`` channels-last (``ctmr_transform``)."""
+    b, c, d, h, w = (int(n) for n in x.shape)
+    ctot = c + (int(x2.shape[1]) if x2 is not None else 0)
+    if mode == _lib.TRANSFORM_TRILINEAR:
+        od, oh, ow = 2 * d, 2 * h, 2 * w
+    elif mode == _lib.TRANSFORM_AVGPOOL:
+        od, oh, ow = d // 2, h // 2, w // 2
+    else:
+        od, oh, ow = d, h, w
+    cout = out_channels or ctot
+    if out is None:
+        out = empty_ndhwc(b, cout, od, oh, ow, out_dtype or x.dtype, x.device)
+    if affine is not None:
+        affine = affine.to(dtype=F32).contiguous()
+    desc = _lib.TransformDesc()
+    desc.batch, desc.depth, desc.height, desc.width = b, d, h, w
+    desc.x = view(x)
+    desc.x2 = view(x2)
+    desc.mode = mode
+    desc.affine = affine.data_ptr() if affine is not None else None
+    desc.silu = int(silu)
+    desc.y = out.data_ptr()
+    desc.y_dtype = _dtype_code(out.dtype)
+    desc.y_channels = int(out.shape[1])
+    desc.y_cstride = rows_stride(out)
+    check(LIB.ctmr_transform(ctypes.byref(desc), _stream()), "transform")
+    return out
+
+
+def rflow_step(z: torch.Tensor, velocity: torch.Tensor, *, guidance: float | None, dt: float,
+               out: torch.Tensor | None = None) -> torch.Tensor:
+    """Guided Euler update ``z + dt * (u + s (c - u))`` (``ctmr_rflow_step``) on contiguous fp32 tensors."""
+    if z.dtype != F32 or velocity.dtype != F32 or not z.is_contiguous() or not velocity.is_contiguous():
+        raise ValueError("rflow_step takes contiguous float32 tensors")
+    n = z.numel()
+    guided = guidance is not None
+    if velocity.numel() != (2 * n if guided else n):
+        raise ValueError("velocity must hold the [cond, uncond] batch when guided")
+    out = out if out is not None else torch.empty_like(z)
+    check(
+        LIB.ctmr_rflow_step(z.data_ptr(), velocity.data_ptr(), n, float(guidance or 0.0), int(guided), float(dt),
+                            out.data_ptr(), _stream()),
+        "rflow_step",
+    )
+    return out

@@ -1,0 +1,135 @@
+"""Implicit-GEMM conv3d on the GPU against the float64 oracle.
+
+Mirrors the reference's kernel tests (``tests/test_fast_fp32.py:59-150``): the
+same five shapes (one per tiling branch there), seeds, weight scaling and the
+reference's bar for the fp32 mode, ``atol = 2e-6 * max|ref|`` elementwise
+(``tests/test_fast_fp32.py:18, 51-56``).
+
+The bf16 mode rounds both operands to bf16 (relative rounding error RMS about
+2^-9 each), which alone puts a single convolution's rel-L2 near 2e-3; a lone
+conv is therefore held to 4e-3, while whole blocks (where the fp32 residual
+dominates) are held to the stated 2e-3 in the block tests.
+"""
+
+from __future__ import annotations
+
+import numpy as np
+import pytest
+import torch
+
+from oracle import ops_ref
+
+pytestmark = pytest.mark.gpu
+
+RELATIVE = 2e-6
+BF16_CONV_REL_L2 = 4e-3
+
+SHAPES = [
+    ((2, 64, 8, 16, 16), 64, 1),
+    ((2, 512, 4, 8, 8), 512, 1),
+    ((2, 256, 8, 16, 16), 128, 1),
+    ((1, 4, 8, 8, 8), 4, 1),
+    ((1, 32, 8, 12, 16), 64, 2),
+]
+
+
+def _close_fp32(actual: torch.Tensor, expected: torch.Tensor) -> None:
+    host = actual.detach().double().cpu()
+    assert host.shape == expected.shape
+    assert torch.isfinite(host).all()
+    atol = RELATIVE * expected.abs().max().item()
+    err = (host - expected).abs().max().item()
+    assert err <= atol, f"max abs err {err:.3e} > {atol:.3e}"
+
+
+def _inputs(shape, out_channels, seed=3):
+    rng = np.random.default_rng(seed)
+    x = rng.standard_normal(shape).astype(np.float32)
+    w = (rng.standard_normal((out_channels, shape[1], 3, 3, 3)) / np.sqrt(27 * shape[1])).astype(np.float32)
+    b = rng.standard_normal(out_channels).astype(np.float32)
+    return torch.from_numpy(x), torch.from_numpy(w), torch.from_numpy(b)
+
+
+@pytest.mark.parametrize(("shape", "out_channels", "stride"), SHAPES)
+def test_conv_fp32_matches_float64(cuda, shape, out_channels, stride):
+    from ctmr_b200 import ops
+
+    x, w, b = _inputs(shape, out_channels)
+    packed = ops.pack_weight(w.to(cuda), "fp32")
+    y = ops.conv3d(ops.to_ndhwc(x.to(cuda)), packed, b.to(cuda), stride=stride)
+    torch.cuda.synchronize()
+    expected = ops_ref.conv3d_ref(x.double(), w.double(), b.double(), stride=stride)
+    _close_fp32(y, expected)
+
+
+@pytest.mark.parametrize(("shape", "out_channels", "stride"), SHAPES)
+def test_conv_bf16_matches_float64(cuda, shape, out_channels, stride):
+    from ctmr_b200 import ops
+
+    x, w, b = _inputs(shape, out_channels)
+    packed = ops.pack_weight(w.to(cuda), "bf16")
+    y = ops.conv3d(ops.to_ndhwc(x.to(cuda)), packed, b.to(cuda), stride=stride, out_dtype=torch.float32)
+    torch.cuda.synchronize()
+    expected = ops_ref.conv3d_ref(x.double(), w.double(), b.double(), stride=stride)
+    err = ops_ref.rel_l2(y.cpu(), expected)
+    assert err <= BF16_CONV_REL_L2, f"rel-L2 {err:.3e}"
+
+
+@pytest.mark.parametrize("upsample", [False, True])
+def test_fused_norm_conv_matches_float64(cuda, upsample):
+    """``tests/test_fast_fp32.py:91-127``: GN + SiLU (+ nearest 2x) + conv + per-batch bias + residual."""
+    from ctmr_b200 import ops
+
+    rng = np.random.default_rng(5)
+    batch, channels, out_channels, groups = 2, 64, 32, 8
+    x = (3 * rng.standard_normal((batch, channels, 4, 8, 8)) + 1).astype(np.float32)
+    w = (rng.standard_normal((out_channels, channels, 3, 3, 3)) / np.sqrt(27 * channels)).astype(np.float32)
+    batch_bias = rng.standard_normal((batch, out_channels)).astype(np.float32)
+    norm_w = (1 + 0.1 * rng.standard_normal(channels)).astype(np.float32)
+    norm_b = (0.1 * rng.standard_normal(channels)).astype(np.float32)
+    scale = 2 if upsample else 1
+    residual = rng.standard_normal((batch, out_channels, 4 * scale, 8 * scale, 8 * scale)).astype(np.float32)
+    xt, wt = torch.from_numpy(x), torch.from_numpy(w)
+    xg = ops.to_ndhwc(xt.to(cuda))
+    affine = ops.group_norm_affine(xg, torch.from_numpy(norm_w).to(cuda), torch.from_numpy(norm_b).to(cuda),
+                                   groups=groups, eps=1e-6)
+    packed = ops.pack_weight(wt.to(cuda), "fp32", upsample=upsample)
+    y = ops.conv3d(xg, packed, torch.from_numpy(batch_bias).to(cuda), affine=affine, silu=True,
+                   residual=ops.to_ndhwc(torch.from_numpy(residual).to(cuda)))
+    torch.cuda.synchronize()
+    prepared = ops_ref.group_norm_silu_ref(xt.double(), torch.from_numpy(norm_w).double(),
+                                           torch.from_numpy(norm_b).double(), groups)
+    if upsample:
+        prepared = ops_ref.upsample_nearest_ref(prepared)
+    expected = ops_ref.conv3d_ref(prepared, wt.double())
+    expected = expected + torch.from_numpy(batch_bias).double()[:, :, None, None, None] + torch.from_numpy(residual).double()
+    _close_fp32(y, expected)
+
+
+def test_trilinear_conv_matches_materialized_upsampling(cuda):
+    """``tests/test_fast_fp32.py:130-150``: fused trilinear conv equals materialised trilinear + conv bitwise."""
+    from ctmr_b200 import ops, _lib
+
+    rng = np.random.default_rng(7)
+    x = torch.from_numpy(rng.standard_normal((2, 24, 3, 5, 6)).astype(np.float32))
+    w = torch.from_numpy((rng.standard_normal((32, 24, 3, 3, 3)) / np.sqrt(27 * 24)).astype(np.float32))
+    b = torch.from_numpy(rng.standard_normal(32).astype(np.float32))
+    xg = ops.to_ndhwc(x.to(cuda))
+    packed = ops.pack_weight(w.to(cuda), "fp32")
+    fused = ops.conv3d(xg, packed, b.to(cuda), trilinear=True)
+    up = ops.transform(xg, mode=_lib.TRANSFORM_TRILINEAR)
+    materialized = ops.conv3d(up, packed, b.to(cuda))
+    torch.cuda.synchronize()
+    assert tuple(fused.shape) == (2, 32, 6, 10, 12)
+    assert torch.equal(fused.cpu(), materialized.cpu())
+    # and the upsampling itself matches the oracle's half-pixel trilinear
+    ref_up = ops_ref.upsample_trilinear_ref(x.double())
+    assert (up.cpu().double() - ref_up).abs().max().item() < 1e-5
+    expected = ops_ref.conv3d_ref(ref_up, w.double(), b.double())
+    _close_fp32(fused, expected)
+
+
+def test_no_device_wait_timed_out(cuda):
+    from ctmr_b200 import _lib
+
+    assert _lib.device_error(clear=True) == 0
