@@ -1,0 +1,342 @@
+"""Benchmark: 256x256x128 MR-Brain volumes/min on B200 (BASELINE.json ``metric``).
+
+One step = one MR-Brain volume: 30 guided rectified-flow steps of the production
+UNet (CFG batch 2, latent 1x4x64x64x32) and the production VAE decode to
+256x256x128 as four overlapping depth windows (ROI (24,64,32), overlap 0.25,
+Gaussian blend) - BASELINE configs 3 and 2 together. Weights are random-init of
+the named architectures (no checkpoints exist offline), inputs synthetic.
+
+  python bench.py [--gpus N --steps K --warmup W] [--precision bf16|fp32] [--impl reference]
+
+N = 1: one GPU per volume. N >= 2 (torchrun, one process per GPU): ranks pair
+up; each pair makes one volume per step with the CFG branches split across the
+pair (one velocity all_gather per step) and the decode windows split (one
+all_reduce of the blend); per-pair work is fixed, so scaling is "weak".
+``--impl reference`` times the reference's arithmetic on the host CPU (the
+torch-CPU restatement in ``oracle/``; the reference itself needs MLX/Metal).
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import math
+import os
+import statistics
+import subprocess
+import sys
+import tempfile
+import time
+from pathlib import Path
+
+ROOT = Path(__file__).resolve().parent
+for _p in (ROOT, ROOT / "mlx-generate-ctmr_b200"):
+    if str(_p) not in sys.path:
+        sys.path.insert(0, str(_p))
+
+import numpy as np  # noqa: E402
+import torch  # noqa: E402
+
+METRIC = "256x256x128 MR-Brain volumes/min (30 rflow steps CFG batch 2 + VAE decode)"
+UNIT = "volumes/min"
+LATENT = (1, 4, 64, 64, 32)
+OUTPUT = (256, 256, 128)
+SPACING = (0.94, 0.94, 1.36)
+MODALITY = 9
+GUIDANCE = 2.0
+STEPS_RFLOW = 30
+DECODE_ROI = (24, 64, 32)
+DECODE_OVERLAP = 0.25
+FALLBACK_PEAKS = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}
+
+
+def _args():
+    p = argparse.ArgumentParser(description=__doc__.splitlines()[0])
+    p.add_argument("--gpus", type=int, default=1)
+    p.add_argument("--steps", type=int, default=2)
+    p.add_argument("--warmup", type=int, default=3)
+    p.add_argument("--impl", choices=("ours", "reference"), default="ours")
+    p.add_argument("--precision", choices=("bf16", "fp32"), default="bf16")
+    p.add_argument("--no-graph", action="store_true")
+    p.add_argument("--no-cpu-baseline", action="store_true")
+    return p.parse_args()
+
+
+def _peaks() -> tuple[dict, str]:
+    path = ROOT / "MEASURED_PEAKS.json"
+    if path.exists():
+        return json.loads(path.read_text()), "measured"
+    return FALLBACK_PEAKS, "fallback"
+
+
+# ---------------------------------------------------------------- clocks
+class ClockSampler:
+    """nvidia-smi clocks / throttle reasons sampled every 200 ms during the timed region."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index: int) -> None:
+        self.file = tempfile.NamedTemporaryFile("w+", suffix=".csv", delete=False)
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits", "-lms", "200",
+                 "-i", str(gpu_index)], stdout=self.file, stderr=subprocess.DEVNULL)
+        except OSError:
+            self.proc = None
+
+    def stop(self) -> dict:
+        if self.proc is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except subprocess.TimeoutExpired:
+            self.proc.kill()
+        self.file.flush()
+        rows = [r.split(",") for r in Path(self.file.name).read_text().strip().splitlines() if r.strip()]
+        os.unlink(self.file.name)
+        sm = [float(r[1]) for r in rows if len(r) >= 9 and r[1].strip().replace(".", "").isdigit()]
+        mx = [float(r[2]) for r in rows if len(r) >= 9 and r[2].strip().replace(".", "").isdigit()]
+        names = ("hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap")
+        reasons = sorted({n for r in rows if len(r) >= 9 for n, v in zip(names, r[5:9]) if v.strip() == "Active"})
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": max(mx) if mx else None,
+                "reasons": reasons, "samples": len(rows)}
+
+
+# ---------------------------------------------------------------- CPU baseline (oracle)
+def cpu_baseline(reps: int = 1) -> dict:
+    """The reference's arithmetic restated in torch on the host CPU (``oracle/``), a bounded sample.
+
+    Sample: one guided UNet step (CFG batch 2, 64x64x32) and the VAE decoder on one
+    (8, 64, 32) latent slab; per-volume time = 30 x UNet step + decode scaled by the
+    4-window decode's FLOPs over the slab's.
+    """
+    from ctmr_b200 import pipeline as P
+    from ctmr_b200 import weights as W
+    from oracle import networks_ref as N
+
+    threads = len(os.sched_getaffinity(0))
+    torch.set_num_threads(threads)
+    unet_w = W.random_weights(W.unet_shapes(P.PRODUCTION_UNET), seed=0, device="cpu")
+    vae_w = W.random_weights(W.vae_decoder_shapes(P.PRODUCTION_VAE), seed=1, device="cpu")
+    gen = torch.Generator().manual_seed(0)
+    z = torch.randn(LATENT, generator=gen)
+    spacing = N.image_spacing_tensor(SPACING)
+    slab = torch.randn((1, 4, 8, 64, 32), generator=gen)
+    with torch.inference_mode():
+        t0 = time.perf_counter()
+        for _ in range(reps):
+            N.guided_velocity(z, 1000.0, torch.tensor([MODALITY]), spacing, unet_w, P.PRODUCTION_UNET, GUIDANCE)
+        unet_s = (time.perf_counter() - t0) / reps
+        t0 = time.perf_counter()
+        N.decode_vae(slab, vae_w, P.PRODUCTION_VAE)
+        slab_s = time.perf_counter() - t0
+    windows = len(P.plan_windows(LATENT[2:], DECODE_ROI, DECODE_OVERLAP).starts)
+    decode_s = slab_s * windows * math.prod(DECODE_ROI) / (8 * 64 * 32)
+    per_volume = STEPS_RFLOW * unet_s + decode_s
+    cpu = "unknown"
+    try:
+        cpu = next(line.split(":", 1)[1].strip() for line in Path("/proc/cpuinfo").read_text().splitlines()
+                   if line.startswith("model name"))
+    except (OSError, StopIteration):
+        pass
+    return {"value": 60.0 / per_volume, "unit": UNIT, "cores": threads, "kind": "port",
+            "sample": (f"torch-CPU fp32 oracle: 1 guided UNet step (CFG batch 2, 64x64x32) x30 = {30 * unet_s:.1f} s "
+                       f"+ VAE decoder on a (8,64,32) latent slab scaled to {windows} windows of {DECODE_ROI} "
+                       f"= {decode_s:.1f} s per volume; {cpu}")}
+
+
+def run_reference(args, rank: int) -> None:
+    """``--impl reference``: the oracle port on all host cores; each step is one bounded sample."""
+    if rank != 0:
+        return
+    for _ in range(args.warmup):
+        cpu_baseline()
+    samples = [cpu_baseline() for _ in range(args.steps)]
+    value = statistics.median(s["value"] for s in samples)
+    base = dict(samples[-1], value=value)
+    line = {"impl": "reference", "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": args.gpus,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": 60000.0 / value, "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+            "config": {"workload": "MR-Brain 256x256x128: 30 rflow steps (CFG batch 2) + 4-window VAE decode",
+                       "model": "MAISI rflow UNet + VAE decoder (random init)", "parallelism": "host CPU"},
+            "cpu_baseline": base,
+            "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    print(json.dumps(line), flush=True)
+
+
+# ---------------------------------------------------------------- GPU arm
+def main() -> None:
+    args = _args()
+    from ctmr_b200 import distributed as D
+
+    rank, world, local = D.init_from_env() if int(os.environ.get("WORLD_SIZE", "1")) > 1 else (0, 1, 0)
+    if args.impl == "reference":
+        run_reference(args, rank)
+        if world > 1:
+            torch.distributed.destroy_process_group()
+        return
+    if world > 1 and world % 2:
+        raise SystemExit("N > 1 must be even (ranks pair up per volume)")
+    dev = torch.device("cuda", local)
+    torch.cuda.set_device(dev)
+
+    from ctmr_b200 import fast_b200 as A
+    from ctmr_b200 import ops
+    from ctmr_b200 import pipeline as P
+    from ctmr_b200 import weights as W
+
+    unet_w = W.random_weights(W.unet_shapes(P.PRODUCTION_UNET), seed=0, device=dev)
+    vae_w = W.random_weights(W.vae_decoder_shapes(P.PRODUCTION_VAE), seed=1, device=dev)
+    spacing = P.image_spacing_tensor(SPACING, dev)
+    timesteps, _ = P.set_timesteps_rflow(num_inference_steps=STEPS_RFLOW, input_img_size_numel=math.prod(LATENT[2:]))
+    pairs = D.Pairs(rank, world) if world > 1 else None
+    seed_volume = rank // 2 if world > 1 else 0
+    latent_host = torch.randn(LATENT, generator=torch.Generator().manual_seed(seed_volume)).pin_memory()
+    ctx = A.arithmetic_precision(args.precision)
+    ctx.__enter__()
+    if pairs is None:
+        sampler = P.GuidedUNetStep(unet_w, P.PRODUCTION_UNET, LATENT, class_label=MODALITY, spacing=spacing,
+                                   guidance_scale=GUIDANCE, device=dev, use_cuda_graph=not args.no_graph)
+    else:
+        sampler = D.CfgSplitStep(unet_w, P.PRODUCTION_UNET, LATENT, class_label=MODALITY, spacing=spacing,
+                                 guidance_scale=GUIDANCE, device=dev, pairs=pairs, use_cuda_graph=not args.no_graph)
+    sampler.prepare()
+
+    def decode(latent: torch.Tensor) -> torch.Tensor:
+        if pairs is None:
+            return P.sliding_window_decode_ncdhw(latent, vae_w, constructor=P.PRODUCTION_VAE, roi=DECODE_ROI,
+                                                 overlap=DECODE_OVERLAP, scale_factor=1.0)
+        return D.pair_window_decode(latent, vae_w, constructor=P.PRODUCTION_VAE, roi=DECODE_ROI,
+                                    overlap=DECODE_OVERLAP, scale_factor=1.0, pairs=pairs)
+
+    latent_dev = latent_host.to(dev).contiguous(memory_format=torch.channels_last_3d)
+
+    def volume() -> torch.Tensor:
+        final = sampler.sample(latent_dev, timesteps)
+        return decode(final)
+
+    def barrier() -> None:
+        if world > 1:
+            torch.distributed.barrier(device_ids=[local])
+        torch.cuda.synchronize(dev)
+
+    for _ in range(args.warmup):
+        out = volume()
+    barrier()
+    # ------------------------------------------------ timed region (device-resident inputs)
+    clocks = ClockSampler(local) if local == 0 else None
+    launches0 = ops.LAUNCHES[0]
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    barrier()
+    start.record()
+    for _ in range(args.steps):
+        out = volume()
+    end.record()
+    barrier()
+    clock_info = clocks.stop() if clocks is not None else None
+    ms = start.elapsed_time(end) / args.steps
+    launches = (ops.LAUNCHES[0] - launches0) / args.steps
+    if world > 1:
+        t = torch.tensor([ms], device=dev)
+        torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
+        ms = float(t.item())
+    volumes_per_step = max(1, world // 2)
+    value = volumes_per_step * 60000.0 / ms
+    assert torch.isfinite(out).all(), "non-finite decoded volume"
+
+    # ------------------------------------------------ end to end through the public API, host buffers
+    h2d = latent_host.numel() * latent_host.element_size()
+    d2h = math.prod(OUTPUT) * 2  # int16 image
+    barrier()
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        if pairs is None:
+            res = P.sample_image_ncdhw(OUTPUT, SPACING, unet_weights=unet_w, vae_weights=vae_w,
+                                       configuration="mr-brain", modality=MODALITY, guidance_scale=GUIDANCE,
+                                       latent=latent_host.to(dev, non_blocking=True), roi=DECODE_ROI,
+                                       overlap=DECODE_OVERLAP, device=dev, sampler=sampler)
+            image = res.image
+        else:
+            final = sampler.sample(latent_host.to(dev, non_blocking=True).contiguous(
+                memory_format=torch.channels_last_3d), timesteps)
+            dec = decode(final)
+            image = P.output_intensities(dec.cpu().numpy(), configuration="mr-brain") if pairs.member == 0 else None
+    barrier()
+    e2e_s = (time.perf_counter() - t0) / args.steps
+    if world > 1:
+        t = torch.tensor([e2e_s], device=dev)
+        torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
+        e2e_s = float(t.item())
+    if image is not None:
+        assert image.dtype == np.int16 and image.shape == (1, 1, *OUTPUT)
+
+    # ------------------------------------------------ conv roofline: GEMM launches timed with events
+    prof: list = []
+    ops.PROFILE = prof
+    if pairs is None:
+        eager = P.GuidedUNetStep(unet_w, P.PRODUCTION_UNET, LATENT, class_label=MODALITY, spacing=spacing,
+                                 guidance_scale=GUIDANCE, device=dev, use_cuda_graph=False)
+        eager.z.copy_(latent_dev)
+        eager.t.fill_(float(timesteps[0]))
+        eager.dt.fill_(P.euler_dt(timesteps[0], timesteps[1]))
+        n0 = len(prof)
+        eager._step()
+        unet_part = prof[n0:]
+        n1 = len(prof)
+        decode(latent_dev)
+        vae_part = prof[n1:]
+    else:
+        unet_part, vae_part = [], []
+    ops.PROFILE = None
+    torch.cuda.synchronize(dev)
+    peaks, peak_kind = _peaks()
+    roofline = None
+    if unet_part:
+        conv_ms = STEPS_RFLOW * sum(s.elapsed_time(e) for s, e, _ in unet_part) + sum(
+            s.elapsed_time(e) for s, e, _ in vae_part)
+        conv_flop = STEPS_RFLOW * sum(f for _, _, f in unet_part) + sum(f for _, _, f in vae_part)
+        n_launch = STEPS_RFLOW * len(unet_part) + len(vae_part)
+        achieved = conv_flop / (conv_ms * 1e-3) / 1e12
+        peak = float(peaks.get("bf16_tflops_sustained", FALLBACK_PEAKS["bf16_tflops_sustained"]))
+        roofline = {"bound": "tensor", "achieved": round(achieved, 1), "peak": peak, "unit": "TFLOP/s",
+                    "frac": round(achieved / peak, 4), "traffic": None,
+                    "kernel": "conv3d_umma_kernel (implicit-GEMM conv3d, all launches of one volume)",
+                    "launches_per_volume": n_launch, "algorithmic_tflop_per_volume": round(conv_flop / 1e12, 2),
+                    "conv_ms_per_volume": round(conv_ms, 2), "peak_source": f"{peak_kind} bf16_tflops_sustained",
+                    "share_of_step": round(conv_ms / ms, 3)}
+
+    if rank == 0:
+        base = None
+        if world == 1 and not args.no_cpu_baseline:
+            base = cpu_baseline()
+        line = {
+            "metric": METRIC, "value": round(value, 3), "unit": UNIT, "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": round(ms, 2), "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": args.precision, "data": "synthetic (random-init weights, N(0,1) latent)",
+            "config": {"workload": "MR-Brain 256x256x128: 30 rflow steps (CFG batch 2, latent 1x4x64x64x32) + "
+                                   "VAE decode as 4 depth windows ROI (24,64,32) overlap 0.25",
+                       "model": "MAISI rflow UNet [64,128,256,512] + VAE decoder [64,128,256] (random init)",
+                       "global_batch": volumes_per_step, "seq_len": None,
+                       "parallelism": "single GPU" if world == 1 else f"{world // 2} pairs x (CFG split + window split)",
+                       "l2": "working set far above L2 (VAE activations 2.1 GB per tensor)",
+                       "precision": args.precision, "cuda_graph": not args.no_graph},
+            "e2e": {"value": round(volumes_per_step * 60.0 / e2e_s, 3), "unit": UNIT, "h2d_bytes_per_step": h2d,
+                    "d2h_bytes_per_step": d2h},
+            "gpu_launches": int(launches),
+            "clocks": clock_info,
+            "roofline": roofline,
+            "cpu_baseline": base,
+        }
+        print(json.dumps(line), flush=True)
+    sampler.release()
+    ctx.__exit__(None, None, None)
+    if world > 1:
+        torch.distributed.barrier(device_ids=[local])
+        torch.distributed.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

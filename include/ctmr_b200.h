@@ -108,8 +108,17 @@ CTMR_API int ctmr_pack_weight(const float* weight, int out_channels, int in_chan
 /* Workspace bytes ctmr_conv3d needs for this descriptor (the prepared operand). */
 CTMR_API size_t ctmr_conv3d_workspace_size(const ctmr_conv3d_desc* desc);
 
-/* Replaces `nax_conv3d` (`_nax_conv.py:475-684`). */
+/* Replaces `nax_conv3d` (`_nax_conv.py:475-684`): operand preparation (when
+ * needed) followed by the implicit-GEMM kernel. */
 CTMR_API int ctmr_conv3d(const ctmr_conv3d_desc* desc, void* workspace, size_t workspace_bytes, void* stream);
+
+/* The two launches of ctmr_conv3d separately, as the reference's pack and
+ * GEMM kernels are (`_nax_conv.py:583-646`): stages = CTMR_CONV_PREPARE,
+ * CTMR_CONV_GEMM or both. The GEMM stage reads the operand a previous
+ * PREPARE stage left in the same workspace. */
+enum { CTMR_CONV_PREPARE = 1, CTMR_CONV_GEMM = 2 };
+CTMR_API int ctmr_conv3d_stages(const ctmr_conv3d_desc* desc, void* workspace, size_t workspace_bytes, int stages,
+                                void* stream);
 
 /* Workspace bytes for ctmr_group_norm_affine. */
 CTMR_API size_t ctmr_group_norm_workspace_size(int batch, long long voxels, int groups);
@@ -160,9 +169,11 @@ CTMR_API int ctmr_window_finalize(const float* acc, const float* wsum, float* ou
                          int ow, int cz0, int cy0, int cx0, int cd, int ch, int cw, void* stream);
 
 /* Guided Euler step of the rectified-flow sampler (`image.py:163-175`, `rflow.py:101-121`):
- * v = vel[n:] + guidance * (vel[:n] - vel[n:]) when guided, else vel[:n]; out = z + v * dt. */
-CTMR_API int ctmr_rflow_step(const float* z, const float* vel, long long n, float guidance, int guided, float dt, float* out,
-                    void* stream);
+ * v = vel[n:] + guidance * (vel[:n] - vel[n:]) when guided, else vel[:n]; out = z + v * dt.
+ * When dt_device is not NULL the step reads dt from that device scalar instead
+ * (so one captured CUDA graph serves every step). out may alias z. */
+CTMR_API int ctmr_rflow_step(const float* z, const float* vel, long long n, float guidance, int guided, float dt,
+                             const float* dt_device, float* out, void* stream);
 
 /* Device error word (bit set when a bounded wait gave up); optionally cleared.
  * Synchronises the current device. */

@@ -261,6 +261,13 @@ size_t ctmr_conv3d_workspace_size(const ctmr_conv3d_desc* desc) {
 }
 
 int ctmr_conv3d(const ctmr_conv3d_desc* d, void* workspace, size_t workspace_bytes, void* stream_ptr) {
+  return ctmr_conv3d_stages(d, workspace, workspace_bytes, CTMR_CONV_PREPARE | CTMR_CONV_GEMM, stream_ptr);
+}
+
+int ctmr_conv3d_stages(const ctmr_conv3d_desc* d, void* workspace, size_t workspace_bytes, int stages,
+                       void* stream_ptr) {
+  if ((stages & ~(CTMR_CONV_PREPARE | CTMR_CONV_GEMM)) != 0 || stages == 0)
+    return fail(CTMR_ERR_INVALID, "stages must combine CTMR_CONV_PREPARE and CTMR_CONV_GEMM");
   ConvPlan p{};
   int st = plan_conv(d, &p);
   if (st != CTMR_OK) return st;
@@ -274,6 +281,11 @@ int ctmr_conv3d(const ctmr_conv3d_desc* d, void* workspace, size_t workspace_byt
   const void* a_lo = nullptr;
   long long a_cstride = d->x.cstride;
   if (p.prepare) {
+    a_hi = workspace;
+    a_lo = p.exact ? static_cast<uint8_t*>(workspace) + p.prep_bytes : nullptr;
+    a_cstride = p.cpad;
+  }
+  if (p.prepare && (stages & CTMR_CONV_PREPARE)) {
     ctmr::PrepParams pp{};
     pp.src[0] = as_source(d->x);
     pp.src[1] = as_source(d->x2);
@@ -290,10 +302,8 @@ int ctmr_conv3d(const ctmr_conv3d_desc* d, void* workspace, size_t workspace_byt
     pp.out_lo = p.exact ? static_cast<uint8_t*>(workspace) + p.prep_bytes : nullptr;
     cudaError_t e = ctmr::launch_prepare(pp, stream);
     if (e != cudaSuccess) return cuda_fail(e, "prepare launch");
-    a_hi = pp.out;
-    a_lo = pp.out_lo;
-    a_cstride = p.cpad;
   }
+  if (!(stages & CTMR_CONV_GEMM)) return CTMR_OK;
 
   // 2. Tile plan over the GEMM-row grid: a 128-voxel box, w fastest.
   ctmr::ConvGeom g{};
@@ -505,10 +515,11 @@ int ctmr_window_finalize(const float* acc, const float* wsum, float* out, int ba
   return e == cudaSuccess ? CTMR_OK : cuda_fail(e, "window finalize launch");
 }
 
-int ctmr_rflow_step(const float* z, const float* vel, long long n, float guidance, int guided, float dt, float* out,
-                    void* stream) {
+int ctmr_rflow_step(const float* z, const float* vel, long long n, float guidance, int guided, float dt,
+                    const float* dt_device, float* out, void* stream) {
   if (z == nullptr || vel == nullptr || out == nullptr || n <= 0) return fail(CTMR_ERR_INVALID, "rflow arguments");
-  cudaError_t e = ctmr::launch_rflow_step(z, vel, n, guidance, guided, dt, out, static_cast<cudaStream_t>(stream));
+  cudaError_t e = ctmr::launch_rflow_step(z, vel, n, guidance, guided, dt, dt_device, out,
+                                          static_cast<cudaStream_t>(stream));
   return e == cudaSuccess ? CTMR_OK : cuda_fail(e, "rflow launch");
 }
 

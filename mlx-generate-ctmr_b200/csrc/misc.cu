@@ -86,8 +86,9 @@ __global__ void window_finalize_kernel(const float* __restrict__ acc, const floa
 }
 
 // z_next = z + dt * v, v = u + s * (c - u) with c = vel[:n], u = vel[n:] (or v = vel when s < 0).
-__global__ void rflow_step_kernel(const float* __restrict__ z, const float* __restrict__ vel, long long n,
-                                  float guidance, int guided, float dt, float* __restrict__ out) {
+__global__ void rflow_step_kernel(const float* z, const float* __restrict__ vel, long long n, float guidance,
+                                  int guided, float dt, const float* __restrict__ dt_device, float* out) {
+  if (dt_device != nullptr) dt = *dt_device;
   for (long long i = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x; i < n;
        i += static_cast<long long>(gridDim.x) * blockDim.x) {
     float v = vel[i];
@@ -132,8 +133,8 @@ cudaError_t launch_window_finalize(const float* acc, const float* wsum, float* o
 }
 
 cudaError_t launch_rflow_step(const float* z, const float* vel, long long n, float guidance, int guided, float dt,
-                              float* out, cudaStream_t stream) {
-  rflow_step_kernel<<<grid_for(n, 256), 256, 0, stream>>>(z, vel, n, guidance, guided, dt, out);
+                              const float* dt_device, float* out, cudaStream_t stream) {
+  rflow_step_kernel<<<grid_for(n, 256), 256, 0, stream>>>(z, vel, n, guidance, guided, dt, dt_device, out);
   return cudaGetLastError();
 }
 

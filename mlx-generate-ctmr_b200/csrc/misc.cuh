@@ -29,6 +29,6 @@ cudaError_t launch_window_finalize(const float* acc, const float* wsum, float* o
                                    int oh, int ow, int cz0, int cy0, int cx0, int cd, int ch, int cw,
                                    cudaStream_t stream);
 cudaError_t launch_rflow_step(const float* z, const float* vel, long long n, float guidance, int guided, float dt,
-                              float* out, cudaStream_t stream);
+                              const float* dt_device, float* out, cudaStream_t stream);
 
 }  // namespace ctmr

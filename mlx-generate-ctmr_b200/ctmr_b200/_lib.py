@@ -25,6 +25,8 @@ PRECISION_BF16 = 1
 TRANSFORM_COPY = 0
 TRANSFORM_TRILINEAR = 1
 TRANSFORM_AVGPOOL = 2
+CONV_PREPARE = 1
+CONV_GEMM = 2
 
 # Every symbol the header declares; tests check the library exports all of them.
 EXPORTED_SYMBOLS = (
@@ -32,6 +34,7 @@ EXPORTED_SYMBOLS = (
     "ctmr_pack_weight",
     "ctmr_conv3d_workspace_size",
     "ctmr_conv3d",
+    "ctmr_conv3d_stages",
     "ctmr_group_norm_workspace_size",
     "ctmr_group_norm_affine",
     "ctmr_transform",
@@ -122,6 +125,7 @@ def _load() -> ctypes.CDLL:
         "ctmr_pack_weight": (i, [vp, i, i, i, i, i, vp, vp, vp]),
         "ctmr_conv3d_workspace_size": (sz, [ctypes.POINTER(Conv3dDesc)]),
         "ctmr_conv3d": (i, [ctypes.POINTER(Conv3dDesc), vp, sz, vp]),
+        "ctmr_conv3d_stages": (i, [ctypes.POINTER(Conv3dDesc), vp, sz, i, vp]),
         "ctmr_group_norm_workspace_size": (sz, [i, ll, i]),
         "ctmr_group_norm_affine": (i, [Tensor, Tensor, i, ll, vp, vp, i, f, vp, vp, sz, vp]),
         "ctmr_transform": (i, [ctypes.POINTER(TransformDesc), vp]),
@@ -129,7 +133,7 @@ def _load() -> ctypes.CDLL:
         "ctmr_ndhwc_to_ncdhw": (i, [vp, i, vp, i, i, i, ll, vp]),
         "ctmr_window_accumulate": (i, [Tensor, i, i, i, i, i, i, i, i, i, i, vp, vp, vp, i, f, vp, vp, vp]),
         "ctmr_window_finalize": (i, [vp, vp, vp, i, i, i, i, i, i, i, i, i, i, i, vp]),
-        "ctmr_rflow_step": (i, [vp, vp, ll, f, i, f, vp, vp]),
+        "ctmr_rflow_step": (i, [vp, vp, ll, f, i, f, vp, vp, vp]),
         "ctmr_get_device_error": (i, [ctypes.POINTER(ctypes.c_uint), i]),
         "ctmr_status_string": (ctypes.c_char_p, [i]),
         "ctmr_last_error": (ctypes.c_char_p, []),

@@ -1,0 +1,340 @@
+"""Drop-in arithmetic module: the operator surface of the reference's ``fast_fp32``
+(``fast_fp32.py:1-406``; protocols ``_types.py:216-286``) on torch CUDA tensors,
+executed by ``libctmr_b200`` (sm_100a).
+
+Tensors keep the reference's logical NCDHW shape and are stored channels-last
+(``torch.channels_last_3d``, i.e. NDHWC rows), so no pack pass is needed: the
+convolution's TMA loads read the activations in place and zero-fill padding.
+
+Precision (request-scoped, like the reference's ``arithmetic_mode``):
+  ``"fp32"`` (default) — convolutions in the split-fp16 "exact" mode (fp32
+      accumulation, ~2^-22 relative product error), the reference's default
+      arithmetic.
+  ``"bf16"`` — bf16 tensor-core operands with fp32 accumulation and fp32
+      epilogue additions.
+Activations between layers are stored in fp32 in both modes: the conv-input
+preparation pass (which applies the group norm and SiLU anyway) writes the
+bf16 or split-fp16 operand, so a bf16 operand costs no extra pass, and the
+residual stream never accumulates bf16 storage rounding.
+
+The fused entry points (``residual_block_ncdhw``, ``vae_resblock_ncdhw``,
+``norm_conv3d_ncdhw``, ``trilinear_conv3d_ncdhw``) follow ``fast_fp32`` exactly in
+where normalisation, SiLU, the time embedding, the skip and the upsampling
+happen. There is no CPU or alternative backend: every convolution, group norm
+and elementwise transform runs in the CUDA library, and the small dense ops the
+reference also leaves to its framework (embedding MLPs, Q/K/V projections,
+attention) run in torch's CUDA kernels.
+"""
+
+from __future__ import annotations
+
+import contextlib
+import math
+import weakref
+from collections.abc import Generator, Iterable, Mapping
+from contextvars import ContextVar
+from dataclasses import dataclass
+
+import torch
+import torch.nn.functional as F
+
+from . import _lib, ops
+
+_precision: ContextVar[str] = ContextVar("ctmr_b200_precision", default="fp32")
+
+
+@contextlib.contextmanager
+def arithmetic_precision(precision: str) -> Generator[None]:
+    """Select ``"fp32"`` or ``"bf16"`` for calls made inside the block (restored on exit)."""
+    if precision not in ops.PRECISIONS:
+        raise ValueError(f"precision must be one of {ops.PRECISIONS}; got {precision!r}")
+    token = _precision.set(precision)
+    try:
+        yield
+    finally:
+        _precision.reset(token)
+
+
+def active_precision() -> str:
+    return _precision.get()
+
+
+def activation_dtype() -> torch.dtype:
+    """Storage dtype of activations between layers (fp32 in both precisions)."""
+    return torch.float32
+
+
+@dataclass(frozen=True)
+class ChannelConcat:
+    """``concat(first, second)`` along channels, never materialised.
+
+    The UNet up path concatenates the running hidden state with a stored skip
+    before every ResBlock (``unet.py:444``); the group-norm statistics, the
+    input preparation and the 1x1x1 skip projection read both tensors directly.
+    """
+
+    first: torch.Tensor
+    second: torch.Tensor
+
+    @property
+    def shape(self) -> tuple[int, ...]:
+        b, c1, d, h, w = self.first.shape
+        return (int(b), int(c1) + int(self.second.shape[1]), int(d), int(h), int(w))
+
+    def materialize(self) -> torch.Tensor:
+        return ops.transform(self.first, x2=self.second, out_dtype=self.first.dtype)
+
+
+def concat_channels_ncdhw(first: torch.Tensor, second: torch.Tensor, mx=None) -> ChannelConcat:
+    """Lazy channel concat (``medmlx_core.ops.concat_channels_ncdhw``'s role)."""
+    if tuple(first.shape[2:]) != tuple(second.shape[2:]) or first.shape[0] != second.shape[0]:
+        raise ValueError(f"cannot concat {tuple(first.shape)} and {tuple(second.shape)}")
+    return ChannelConcat(ops.to_ndhwc(first, activation_dtype()), ops.to_ndhwc(second, activation_dtype()))
+
+
+def _split(x) -> tuple[torch.Tensor, torch.Tensor | None]:
+    if isinstance(x, ChannelConcat):
+        return x.first, x.second
+    return ops.to_ndhwc(x, activation_dtype()), None
+
+
+# ---------------------------------------------------------------- packed weights
+# Keyed by (id(weight), upsample, precision); the weak reference both validates
+# that the id still names the same tensor and evicts on collection
+# (``fast_fp32.py:70-90``).
+_packed: dict[tuple[int, bool, str], tuple[weakref.ref, ops.PackedWeight]] = {}
+
+
+def _pack(weight: torch.Tensor, *, upsample: bool = False) -> ops.PackedWeight:
+    precision = _precision.get()
+    key = (id(weight), upsample, precision)
+    hit = _packed.get(key)
+    if hit is not None and hit[0]() is weight:
+        return hit[1]
+    packed = ops.pack_weight(weight, precision, upsample=upsample)
+    _packed[key] = (weakref.ref(weight, lambda _: _packed.pop(key, None)), packed)
+    return packed
+
+
+def drop_packed_weights(weights: Iterable[torch.Tensor]) -> None:
+    """Forget the packed copies of ``weights``; a later use packs them again."""
+    ids = {id(w) for w in weights}
+    for key in [k for k in _packed if k[0] in ids]:
+        del _packed[key]
+
+
+# ---------------------------------------------------------------- elementwise surface
+def silu(array, mx=None) -> torch.Tensor:
+    """SiLU ``y / (1 + exp(-y))`` on activations, or torch's on small dense tensors."""
+    if isinstance(array, torch.Tensor) and array.dim() != 5:
+        return F.silu(array)
+    x, x2 = _split(array)
+    return ops.transform(x, x2=x2, silu=True, out_dtype=activation_dtype())
+
+
+def linear(array: torch.Tensor, weight: torch.Tensor, bias: torch.Tensor | None, mx=None) -> torch.Tensor:
+    """Dense projection of small tensors (embeddings, attention tokens) in fp32 or the activation dtype."""
+    dtype = array.dtype if array.dtype in (torch.float32, torch.bfloat16) else torch.float32
+    return F.linear(array.to(dtype), weight.to(dtype), None if bias is None else bias.to(dtype))
+
+
+def group_norm_ncdhw(array, weight, bias, *, num_groups: int, eps: float, mx=None, apply_silu: bool = False):
+    """Group norm with fp32 statistics and an optional fused SiLU (``fast_fp32.py:102-118``)."""
+    x, x2 = _split(array)
+    affine = ops.group_norm_affine(x, weight, bias, groups=num_groups, eps=eps, x2=x2)
+    return ops.transform(x, x2=x2, affine=affine, silu=apply_silu, out_dtype=activation_dtype())
+
+
+def avg_pool3d_ncdhw(array, *, mx=None) -> torch.Tensor:
+    x, x2 = _split(array)
+    return ops.transform(x, x2=x2, mode=_lib.TRANSFORM_AVGPOOL, out_dtype=activation_dtype())
+
+
+def upsample_nearest_ncdhw(array, *, mx=None) -> torch.Tensor:
+    x, _ = _split(array)
+    return x.repeat_interleave(2, 2).repeat_interleave(2, 3).repeat_interleave(2, 4).contiguous(
+        memory_format=torch.channels_last_3d)
+
+
+def upsample_trilinear_ncdhw(array, *, mx=None, scale: int = 2) -> torch.Tensor:
+    """Half-pixel trilinear 2x (``source_vae.py:95-111``)."""
+    if scale != 2:
+        raise ValueError("NV-Generate VAE trilinear upsampling requires scale=2")
+    x, x2 = _split(array)
+    return ops.transform(x, x2=x2, mode=_lib.TRANSFORM_TRILINEAR, out_dtype=activation_dtype())
+
+
+def sinusoidal_timestep_embedding(timesteps: torch.Tensor, embedding_dim: int, *, mx=None,
+                                  max_period: int = 10000) -> torch.Tensor:
+    """``[cos, sin]`` timestep features (``embed.py:15-42``), fp32."""
+    if timesteps.dim() != 1:
+        raise ValueError("Timesteps should be a 1d-array")
+    half = embedding_dim // 2
+    exponent = -math.log(max_period) * torch.arange(half, dtype=torch.float32, device=timesteps.device)
+    freqs = torch.exp(exponent / half)
+    args = timesteps.to(torch.float32).reshape(-1, 1) * freqs.reshape(1, -1)
+    emb = torch.cat([torch.cos(args), torch.sin(args)], dim=-1)
+    if embedding_dim % 2 == 1:
+        emb = F.pad(emb, (0, 1))
+    return emb
+
+
+# ---------------------------------------------------------------- convolutions
+def _bias(weight: torch.Tensor, bias: torch.Tensor | None) -> torch.Tensor:
+    return torch.zeros(int(weight.shape[0]), dtype=torch.float32, device=weight.device) if bias is None else bias
+
+
+def pointwise_conv_ncdhw(array, weight: torch.Tensor, bias: torch.Tensor | None, *, mx=None) -> torch.Tensor:
+    """1x1x1 convolution as an implicit GEMM with one tap (``fast_fp32.py:121-130``)."""
+    x, x2 = _split(array)
+    return ops.conv3d(x, _pack(weight), bias, x2=x2, out_dtype=activation_dtype())
+
+
+def conv3d_ncdhw(array, weight: torch.Tensor, bias: torch.Tensor | None, *, padding: int, mx=None,
+                 stride: int = 1) -> torch.Tensor:
+    """NCDHW convolution with a Torch ``(O, C, K, K, K)`` weight (``fast_fp32.py:133-154``)."""
+    k = int(weight.shape[2])
+    if k == 1 and padding == 0 and stride == 1:
+        return pointwise_conv_ncdhw(array, weight, bias)
+    if k != 3 or padding != 1 or stride not in (1, 2):
+        raise ValueError(f"unsupported convolution: kernel {k}, padding {padding}, stride {stride}")
+    x, x2 = _split(array)
+    return ops.conv3d(x, _pack(weight), bias, x2=x2, stride=stride, out_dtype=activation_dtype())
+
+
+def norm_conv3d_ncdhw(array, weight: torch.Tensor, bias: torch.Tensor, *, norm, num_groups: int, eps: float,
+                      apply_silu: bool, mx=None, upsample: bool = False, residual=None,
+                      residual_upsampled: bool = False, avgpool: bool = False) -> torch.Tensor:
+    """``conv(upsample?(silu?(norm?(x)))) + bias (+ residual)`` for padding-1 3x3x3 kernels (``fast_fp32.py:162-211``).
+
+    ``bias`` is ``(O,)`` or per batch item ``(B, O)``. ``residual_upsampled`` reads
+    the residual on the half-resolution grid (nearest 2x), ``avgpool`` convolves
+    the 2x2x2 mean of the prepared input; both are this module's fusions of the
+    surrounding ops in ``fast_fp32.residual_block_ncdhw``.
+    """
+    x, x2 = _split(array)
+    affine = None
+    if norm is not None:
+        affine = ops.group_norm_affine(x, norm[0], norm[1], groups=num_groups, eps=eps, x2=x2)
+    res = None
+    if residual is not None:
+        res = residual if isinstance(residual, torch.Tensor) else residual.materialize()
+        res = ops.to_ndhwc(res)
+    return ops.conv3d(x, _pack(weight, upsample=upsample), bias, x2=x2, affine=affine, silu=apply_silu,
+                      avgpool=avgpool, residual=res, residual_upsampled=residual_upsampled,
+                      out_dtype=activation_dtype())
+
+
+def trilinear_conv3d_ncdhw(array, weight: torch.Tensor, bias: torch.Tensor, *, mx=None) -> torch.Tensor:
+    """Padding-1 3x3x3 conv of the half-pixel trilinear 2x upsampling, computed while preparing the operand."""
+    x, x2 = _split(array)
+    if x2 is not None:
+        x = ChannelConcat(x, x2).materialize()
+    return ops.conv3d(x, _pack(weight), bias, trilinear=True, out_dtype=activation_dtype())
+
+
+def residual_block_ncdhw(x, emb: torch.Tensor, weights: Mapping[str, torch.Tensor], *, num_groups: int, eps: float,
+                         mx=None, up: bool = False, down: bool = False) -> torch.Tensor:
+    """Fused UNet ResBlock (``fast_fp32.py:214-291``).
+
+    The time-embedding projection joins conv1's bias per batch item; the skip
+    (after its optional 1x1x1 projection, on the small grid) joins conv2's
+    accumulator. ``down``: conv1 reads the 2x2x2 mean of ``silu(norm1(x))``
+    (pooling after the activation, as the reference). ``up``: conv1 reads the
+    nearest-2x upsampling through the folded weights, and the skip stays on the
+    small grid and is upsampled by index in conv2's epilogue.
+    """
+    xa, xb = _split(x)
+    temb = linear(F.silu(emb.to(torch.float32)), weights["time_emb_proj.weight"], weights["time_emb_proj.bias"])
+    bias1 = weights["conv1.conv.bias"].to(torch.float32).reshape(1, -1) + temb
+    norm1 = (weights["norm1.weight"], weights["norm1.bias"])
+    cin = int(xa.shape[1]) + (int(xb.shape[1]) if xb is not None else 0)
+    project = cin != int(weights["conv1.conv.weight"].shape[0])
+    dtype = activation_dtype()
+    affine1 = ops.group_norm_affine(xa, *norm1, groups=num_groups, eps=eps, x2=xb)
+    if down:
+        if project:
+            skip = ops.conv3d(xa, _pack(weights["skip_connection.conv.weight"]), weights["skip_connection.conv.bias"],
+                              x2=xb, avgpool=True, out_dtype=dtype)
+        else:
+            skip = ops.transform(xa, x2=xb, mode=_lib.TRANSFORM_AVGPOOL, out_dtype=dtype)
+        hidden = ops.conv3d(xa, _pack(weights["conv1.conv.weight"]), bias1, x2=xb, affine=affine1, silu=True,
+                            avgpool=True, out_dtype=dtype)
+    else:
+        if project:
+            skip = ops.conv3d(xa, _pack(weights["skip_connection.conv.weight"]), weights["skip_connection.conv.bias"],
+                              x2=xb, out_dtype=dtype)
+        else:
+            skip = xa if xb is None else ChannelConcat(xa, xb).materialize()
+        hidden = ops.conv3d(xa, _pack(weights["conv1.conv.weight"], upsample=up), bias1, x2=xb, affine=affine1,
+                            silu=True, out_dtype=dtype)
+    affine2 = ops.group_norm_affine(hidden, weights["norm2.weight"], weights["norm2.bias"], groups=num_groups, eps=eps)
+    return ops.conv3d(hidden, _pack(weights["conv2.conv.weight"]), weights["conv2.conv.bias"], affine=affine2,
+                      silu=True, residual=skip, residual_upsampled=up, out_dtype=dtype)
+
+
+def vae_resblock_ncdhw(state: list, conv1, conv2, norm1, norm2, shortcut, *, num_groups: int, eps: float,
+                       mx=None) -> torch.Tensor:
+    """Fused ``MaisiResBlock`` (``fast_fp32.py:294-336``); consumes ``state`` so the input can be freed early."""
+    array = state.pop()
+    x, x2 = _split(array)
+    del array
+    dtype = activation_dtype()
+    affine1 = ops.group_norm_affine(x, norm1[0], norm1[1], groups=num_groups, eps=eps, x2=x2)
+    hidden = ops.conv3d(x, _pack(conv1[0]), conv1[1], x2=x2, affine=affine1, silu=True, out_dtype=dtype)
+    if shortcut is None:
+        skip = x if x2 is None else ChannelConcat(x, x2).materialize()
+    else:
+        skip = ops.conv3d(x, _pack(shortcut[0]), shortcut[1], x2=x2, out_dtype=dtype)
+    del x, x2
+    affine2 = ops.group_norm_affine(hidden, norm2[0], norm2[1], groups=num_groups, eps=eps)
+    out = ops.conv3d(hidden, _pack(conv2[0]), conv2[1], affine=affine2, silu=True, residual=skip, out_dtype=dtype)
+    return out
+
+
+# ---------------------------------------------------------------- attention
+def attention(query: torch.Tensor, key: torch.Tensor, value: torch.Tensor, *, scale: float, mx=None) -> torch.Tensor:
+    """``softmax(Q K^T * scale) V`` on ``(B, H, L, D)`` heads."""
+    return F.scaled_dot_product_attention(query, key, value, scale=scale)
+
+
+def attention_projection(array: torch.Tensor, weight: torch.Tensor, bias: torch.Tensor, mx=None) -> torch.Tensor:
+    return linear(array, weight, bias)
+
+
+def self_attention_tokens(tokens: torch.Tensor, weights: Mapping[str, torch.Tensor], *, heads: int, scale: float,
+                          include_fc: bool, mx=None, prefix: str = "attn", qkv_bias: bool = True) -> torch.Tensor:
+    """Q/K/V projections, multi-head self-attention and optional ``out_proj`` on ``(B, L, C)`` (``fast_fp32.py:352-396``)."""
+    q, k, v = (
+        linear(tokens, weights[f"{prefix}.to_{n}.weight"], weights[f"{prefix}.to_{n}.bias"] if qkv_bias else None)
+        for n in ("q", "k", "v")
+    )
+    b, length, c = q.shape
+
+    def split(a):
+        return a.reshape(b, length, heads, c // heads).transpose(1, 2)
+
+    att = F.scaled_dot_product_attention(split(q), split(k), split(v), scale=scale)
+    merged = att.transpose(1, 2).reshape(b, length, c)
+    if include_fc:
+        merged = linear(merged, weights[f"{prefix}.out_proj.weight"], weights[f"{prefix}.out_proj.bias"])
+    return merged
+
+
+def spatial_attention_ncdhw(x: torch.Tensor, weights: Mapping[str, torch.Tensor], *, num_groups: int, eps: float,
+                            num_head_channels: int, include_fc: bool, mx=None) -> torch.Tensor:
+    """Residual self-attention over all voxels (``attention.py:92-160`` fast path).
+
+    With channels-last storage the tokens ``(B, D*H*W, C)`` are a view of the
+    normalised tensor, and the merged result viewed back is again channels-last.
+    """
+    x = ops.to_ndhwc(x, activation_dtype())
+    b, c, d, h, w = (int(n) for n in x.shape)
+    if c % num_head_channels:
+        raise ValueError("num_channels must be divisible by num_head_channels")
+    heads, scale = c // num_head_channels, float(num_head_channels) ** -0.5
+    normed = group_norm_ncdhw(x, weights["norm.weight"], weights["norm.bias"], num_groups=num_groups, eps=eps)
+    tokens = normed.permute(0, 2, 3, 4, 1).reshape(b, d * h * w, c)
+    merged = self_attention_tokens(tokens, weights, heads=heads, scale=scale, include_fc=include_fc)
+    out = merged.to(x.dtype).reshape(b, d, h, w, c).permute(0, 4, 1, 2, 3)
+    return x + out

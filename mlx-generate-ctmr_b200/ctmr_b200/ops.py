@@ -22,6 +22,16 @@ F32 = torch.float32
 BF16 = torch.bfloat16
 PRECISIONS = ("fp32", "bf16")
 
+# Instrumentation: LAUNCHES counts the library's kernel launches issued from
+# Python; when PROFILE is a list, conv3d records (start, end, flops) CUDA events
+# around each implicit-GEMM launch on the current stream.
+LAUNCHES = [0]
+PROFILE: list | None = None
+
+
+def _count(n: int) -> None:
+    LAUNCHES[0] += n
+
 
 def _stream() -> int:
     return torch.cuda.current_stream().cuda_stream
@@ -93,6 +103,7 @@ def to_ndhwc(x: torch.Tensor, dtype: torch.dtype | None = None) -> torch.Tensor:
     x = x.contiguous()
     b, c, d, h, w = x.shape
     out = empty_ndhwc(b, c, d, h, w, dtype, x.device)
+    _count(1)
     check(
         LIB.ctmr_ncdhw_to_ndhwc(
             x.data_ptr(), _dtype_code(x.dtype), out.data_ptr(), _dtype_code(dtype), b, c, d * h * w, _stream()
@@ -109,6 +120,7 @@ def to_ncdhw(x: torch.Tensor, dtype: torch.dtype = F32) -> torch.Tensor:
     if cs != c:
         x = transform(x, out_dtype=x.dtype)
     out = torch.empty((b, c, d, h, w), dtype=dtype, device=x.device)
+    _count(1)
     check(
         LIB.ctmr_ndhwc_to_ncdhw(
             x.data_ptr(), _dtype_code(x.dtype), out.data_ptr(), _dtype_code(dtype), b, c, d * h * w, _stream()
@@ -150,6 +162,7 @@ def pack_weight(weight: torch.Tensor, precision: str, *, upsample: bool = False)
     else:
         hi = torch.empty(n, dtype=BF16, device=w.device)
         lo = None
+    _count(1)
     check(
         LIB.ctmr_pack_weight(
             w.data_ptr(), o, c, k, int(upsample), code, hi.data_ptr(), lo.data_ptr() if lo is not None else None,
@@ -245,15 +258,21 @@ def conv3d(
     desc.y_cstride = ycs
     desc.y_coffset = 0
     ws_bytes = int(LIB.ctmr_conv3d_workspace_size(ctypes.byref(desc)))
-    if ws_bytes == 0:
-        # Either no preparation is needed or the descriptor is invalid; ctmr_conv3d reports which.
-        ws = None
+    ws = torch.empty(ws_bytes, dtype=torch.uint8, device=x.device) if ws_bytes else None
+    ws_ptr = ws.data_ptr() if ws is not None else None
+    _count(2 if ws_bytes else 1)
+    if PROFILE is None:
+        check(LIB.ctmr_conv3d(ctypes.byref(desc), ws_ptr, ws_bytes, _stream()), "conv3d")
     else:
-        ws = torch.empty(ws_bytes, dtype=torch.uint8, device=x.device)
-    check(
-        LIB.ctmr_conv3d(ctypes.byref(desc), ws.data_ptr() if ws is not None else None, ws_bytes, _stream()),
-        "conv3d",
-    )
+        if ws_bytes:
+            check(LIB.ctmr_conv3d_stages(ctypes.byref(desc), ws_ptr, ws_bytes, _lib.CONV_PREPARE, _stream()),
+                  "conv3d prepare")
+        start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        start.record()
+        check(LIB.ctmr_conv3d_stages(ctypes.byref(desc), ws_ptr, ws_bytes, _lib.CONV_GEMM, _stream()), "conv3d gemm")
+        end.record()
+        taps = 8 if packed.upsample else k ** 3
+        PROFILE.append((start, end, 2.0 * b * od * oh * ow * o * cin * taps))
     return out
 
 
@@ -275,6 +294,7 @@ def group_norm_affine(
     gamma = weight.to(dtype=F32).contiguous() if weight is not None else None
     beta = bias.to(dtype=F32).contiguous() if bias is not None else None
     affine = torch.empty((b, ctot, 2), dtype=F32, device=x.device)
+    _count(2)
     ws_bytes = int(LIB.ctmr_group_norm_workspace_size(b, voxels, groups))
     ws = torch.empty(max(ws_bytes, 4), dtype=torch.uint8, device=x.device)
     check(
@@ -325,23 +345,72 @@ def transform(
     desc.y_dtype = _dtype_code(out.dtype)
     desc.y_channels = int(out.shape[1])
     desc.y_cstride = rows_stride(out)
+    _count(1)
     check(LIB.ctmr_transform(ctypes.byref(desc), _stream()), "transform")
     return out
 
 
-def rflow_step(z: torch.Tensor, velocity: torch.Tensor, *, guidance: float | None, dt: float,
+def rflow_step(z: torch.Tensor, velocity: torch.Tensor, *, guidance: float | None, dt: float | torch.Tensor,
                out: torch.Tensor | None = None) -> torch.Tensor:
-    """Guided Euler update ``z + dt * (u + s (c - u))`` (``ctmr_rflow_step``) on contiguous fp32 tensors."""
-    if z.dtype != F32 or velocity.dtype != F32 or not z.is_contiguous() or not velocity.is_contiguous():
-        raise ValueError("rflow_step takes contiguous float32 tensors")
+    """Guided Euler update ``z + dt * (u + s (c - u))`` (``ctmr_rflow_step``).
+
+    ``z`` and ``velocity`` are fp32 and share one memory layout (``velocity`` holds
+    the [cond, uncond] batch when guided); ``dt`` may be a device scalar tensor,
+    read at execution time; ``out`` may be ``z``.
+    """
+    if z.dtype != F32 or velocity.dtype != F32:
+        raise ValueError("rflow_step takes float32 tensors")
+    if z.stride() != velocity[: z.shape[0]].stride() or not (z.is_contiguous() or z.is_contiguous(
+            memory_format=torch.channels_last_3d)):
+        raise ValueError("z and velocity must be dense with the same memory layout")
     n = z.numel()
     guided = guidance is not None
     if velocity.numel() != (2 * n if guided else n):
         raise ValueError("velocity must hold the [cond, uncond] batch when guided")
     out = out if out is not None else torch.empty_like(z)
+    dt_dev = dt.data_ptr() if isinstance(dt, torch.Tensor) else None
+    _count(1)
     check(
-        LIB.ctmr_rflow_step(z.data_ptr(), velocity.data_ptr(), n, float(guidance or 0.0), int(guided), float(dt),
-                            out.data_ptr(), _stream()),
+        LIB.ctmr_rflow_step(z.data_ptr(), velocity.data_ptr(), n, float(guidance or 0.0), int(guided),
+                            0.0 if dt_dev is not None else float(dt), dt_dev, out.data_ptr(), _stream()),
         "rflow_step",
+    )
+    return out
+
+
+def window_accumulate(pred: torch.Tensor, acc: torch.Tensor, wsum: torch.Tensor, *, origin: tuple[int, int, int],
+                      tables: list[torch.Tensor], scale: int, floor: float) -> None:
+    """Add one decoded window, Gaussian-weighted, into the blend (``ctmr_window_accumulate``).
+
+    ``pred`` is the channels-last window ``(B, C, wd, wh, ww)``; ``acc`` is the
+    fp32 NDHWC accumulator ``(B, OD, OH, OW, C)`` and ``wsum`` the fp32 weight
+    sum ``(OD, OH, OW)``; ``tables`` are the per-axis 1-D Gaussians over the
+    latent ROI, resized by ``scale`` with nearest indexing.
+    """
+    b, c, wd, wh, ww = (int(n) for n in pred.shape)
+    od, oh, ow = (int(n) for n in acc.shape[1:4])
+    if acc.dtype != F32 or wsum.dtype != F32 or not acc.is_contiguous() or not wsum.is_contiguous():
+        raise ValueError("window accumulators must be contiguous float32")
+    gz, gy, gx = (t.to(F32).contiguous() for t in tables)
+    _count(1)
+    check(
+        LIB.ctmr_window_accumulate(view(pred), b, wd, wh, ww, int(origin[0]), int(origin[1]), int(origin[2]), od, oh,
+                                   ow, gz.data_ptr(), gy.data_ptr(), gx.data_ptr(), int(scale), float(floor),
+                                   acc.data_ptr(), wsum.data_ptr(), _stream()),
+        "window_accumulate",
+    )
+
+
+def window_finalize(acc: torch.Tensor, wsum: torch.Tensor, *, origin: tuple[int, int, int],
+                    extent: tuple[int, int, int]) -> torch.Tensor:
+    """``acc / wsum`` over the crop at ``origin`` as a contiguous NCDHW fp32 tensor (``ctmr_window_finalize``)."""
+    b, od, oh, ow, c = (int(n) for n in acc.shape)
+    out = torch.empty((b, c, *(int(e) for e in extent)), dtype=F32, device=acc.device)
+    _count(1)
+    check(
+        LIB.ctmr_window_finalize(acc.data_ptr(), wsum.data_ptr(), out.data_ptr(), b, c, od, oh, ow, int(origin[0]),
+                                 int(origin[1]), int(origin[2]), int(extent[0]), int(extent[1]), int(extent[2]),
+                                 _stream()),
+        "window_finalize",
     )
     return out

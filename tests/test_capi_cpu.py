@@ -1,0 +1,89 @@
+"""The C-ABI library loads on a CPU host, exports every declared symbol, and validates arguments
+(status codes, no CUDA call) exactly as the header documents."""
+
+from __future__ import annotations
+
+import ctypes
+import re
+from pathlib import Path
+
+import pytest
+
+from ctmr_b200 import _lib
+
+HEADER = Path(__file__).resolve().parents[1] / "include" / "ctmr_b200.h"
+
+
+def test_header_symbols_are_exported():
+    declared = set(re.findall(r"CTMR_API\s+[\w\s\*]+?\b(ctmr_\w+)\s*\(", HEADER.read_text()))
+    assert declared == set(_lib.EXPORTED_SYMBOLS)
+    for name in declared:
+        assert hasattr(_lib.LIB, name), name
+
+
+def test_packed_weight_elems():
+    assert _lib.LIB.ctmr_packed_weight_elems(64, 64, 3, 0) == 27 * 64 * 64
+    assert _lib.LIB.ctmr_packed_weight_elems(4, 4, 3, 0) == 27 * 16 * 16
+    assert _lib.LIB.ctmr_packed_weight_elems(32, 24, 3, 1) == 64 * 32 * 32
+    assert _lib.LIB.ctmr_packed_weight_elems(1, 64, 1, 0) == 16 * 64
+    assert _lib.LIB.ctmr_packed_weight_elems(4, 4, 5, 0) == 0
+
+
+def _desc(**kw) -> _lib.Conv3dDesc:
+    d = _lib.Conv3dDesc()
+    d.batch, d.depth, d.height, d.width = 1, 4, 4, 4
+    d.x = _lib.Tensor(0x10000, _lib.DTYPE_F32, 32, 32)
+    d.out_channels, d.kernel_size, d.stride = 32, 3, 1
+    d.precision = _lib.PRECISION_FP32
+    d.weight, d.weight_lo = 0x20000, 0x30000
+    d.y, d.y_dtype, d.y_cstride = 0x40000, _lib.DTYPE_F32, 32
+    for k, v in kw.items():
+        setattr(d, k, v)
+    return d
+
+
+def _status(desc) -> int:
+    return _lib.LIB.ctmr_conv3d(ctypes.byref(desc), None, 0, None)
+
+
+def test_workspace_size_reports_prepared_operand():
+    # fp32 split mode: hi + lo fp16 planes of B * D * H * W * round16(C) elements.
+    assert _lib.LIB.ctmr_conv3d_workspace_size(ctypes.byref(_desc())) == 2 * 64 * 32 * 2
+    # trilinear input doubles every axis before the conv
+    assert _lib.LIB.ctmr_conv3d_workspace_size(ctypes.byref(_desc(trilinear=1))) == 2 * 512 * 32 * 2
+
+
+@pytest.mark.parametrize(("overrides", "status"), [
+    ({"batch": 0}, _lib.CTMR_ERR_INVALID),
+    ({"kernel_size": 5}, _lib.CTMR_ERR_UNSUPPORTED),
+    ({"stride": 3}, _lib.CTMR_ERR_UNSUPPORTED),
+    ({"upsample": 1, "trilinear": 1}, _lib.CTMR_ERR_UNSUPPORTED),
+    ({"avgpool": 1, "depth": 3}, _lib.CTMR_ERR_INVALID),
+    ({"y_cstride": 16}, _lib.CTMR_ERR_INVALID),
+    ({"weight_lo": None}, _lib.CTMR_ERR_INVALID),
+    ({"precision": 7}, _lib.CTMR_ERR_INVALID),
+    ({"trilinear": 1, "silu": 1}, _lib.CTMR_ERR_UNSUPPORTED),
+    ({"stride": 2, "width": 1}, _lib.CTMR_ERR_UNSUPPORTED),
+])
+def test_conv_argument_validation(overrides, status):
+    assert _status(_desc(**overrides)) == status
+    assert _lib.LIB.ctmr_last_error()
+
+
+def test_conv_workspace_too_small():
+    assert _status(_desc()) == _lib.CTMR_ERR_WORKSPACE
+
+
+def test_check_maps_status_to_exceptions():
+    with pytest.raises(ValueError):
+        _lib.check(_lib.CTMR_ERR_INVALID, "x")
+    with pytest.raises(_lib.CtmrError):
+        _lib.check(_lib.CTMR_ERR_CUDA, "x")
+    _lib.check(_lib.CTMR_OK, "x")
+
+
+def test_group_norm_validation():
+    t = _lib.Tensor(0x10000, _lib.DTYPE_F32, 30, 30)
+    none = _lib.Tensor(None, 0, 0, 0)
+    st = _lib.LIB.ctmr_group_norm_affine(t, none, 1, 64, None, None, 32, 1e-6, 0x2000, 0x3000, 1 << 20, None)
+    assert st == _lib.CTMR_ERR_INVALID  # 30 channels are not divisible by 32 groups

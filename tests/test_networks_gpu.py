@@ -1,0 +1,229 @@
+"""B200 networks and pipeline against the reference's golden vectors and the CPU oracle.
+
+Golden tolerances are the reference's own (``maisi_mlx_feasibility.py:10-29``):
+residual 1e-5/1e-6, attention/VAE/UNet 1e-4/1e-5 (rtol/atol). The bf16 mode is
+held to rel-L2 <= 2e-3 per block and <= 1e-2 on a decoded volume against the
+fp32 oracle.
+"""
+
+from __future__ import annotations
+
+import numpy as np
+import pytest
+import torch
+
+from golden_io import load, t, weights
+from oracle import networks_ref as N
+from oracle import ops_ref
+
+pytestmark = pytest.mark.gpu
+
+RESIDUAL = dict(rtol=1e-5, atol=1e-6)
+NET = dict(rtol=1e-4, atol=1e-5)
+
+
+def _on(d, dev):
+    return {k: v.to(dev) for k, v in d.items()}
+
+
+def _close(actual: torch.Tensor, expected: np.ndarray, tol: dict) -> None:
+    np.testing.assert_allclose(actual.detach().float().cpu().numpy(), expected, **tol)
+
+
+def _mr_intensity_parity(actual: np.ndarray, reference_decoded: np.ndarray) -> None:
+    """Each int16 voxel is attainable within the decoder budget (``tests/numerical.py:11-27``)."""
+    reference = reference_decoded.astype(np.float64)
+    error = 1e-5 + 1e-4 * np.abs(reference)
+    lower = (np.maximum(reference - error, 0).astype(np.float32) * np.float32(1000)).astype(np.int32)
+    upper = (np.maximum(reference + error, 0).astype(np.float32) * np.float32(1000)).astype(np.int32)
+    assert actual.dtype == np.int16 and actual.shape == reference_decoded.shape
+    assert np.all(actual >= lower) and np.all(actual <= upper)
+
+
+def test_residual_block_golden(cuda):
+    from ctmr_b200 import networks
+
+    a, meta = load("maisi_residual")
+    c = meta["constructor"]
+    y = networks.residual_block_ncdhw(t(a["x"]).to(cuda), t(a["emb"]).to(cuda), _on(weights(meta), cuda),
+                                      num_groups=c["norm_num_groups"], eps=c["norm_eps"])
+    _close(y, a["y"], RESIDUAL)
+
+
+def test_attention_golden(cuda):
+    from ctmr_b200 import fast_b200
+
+    a, meta = load("maisi_attention")
+    c = meta["constructor"]
+    y = fast_b200.spatial_attention_ncdhw(t(a["x"]).to(cuda), _on(weights(meta), cuda), num_groups=c["norm_num_groups"],
+                                          eps=c["norm_eps"], num_head_channels=c["num_head_channels"],
+                                          include_fc=c["include_fc"])
+    _close(y, a["y"], NET)
+
+
+def test_vae_decoder_golden(cuda):
+    from ctmr_b200 import networks
+
+    a, meta = load("maisi_vae")
+    post, dec = networks.decode_vae_ncdhw(t(a["z"]).to(cuda), _on(weights(meta), cuda), constructor=meta["constructor"])
+    _close(post, a["post_quant"], NET)
+    _close(dec, a["decoded"], NET)
+
+
+def test_vae_tiled_decode_golden(cuda):
+    """Sliding-window decode, roi (2,2,2), overlap 0.5, scale 1.25 (``tests/fixture_cases.py:80-88``)."""
+    from ctmr_b200 import pipeline
+
+    a, meta = load("vae")
+    w = _on(weights(meta), cuda)
+    z = t(a["input.z"]).to(cuda)
+    tiled = pipeline.sliding_window_decode_ncdhw(z, w, constructor=meta["constructor"], roi=(2, 2, 2), overlap=0.5,
+                                                 scale_factor=1.25)
+    _close(tiled, a["output.tiled"], NET)
+    direct = pipeline.sliding_window_decode_ncdhw(z, w, constructor=meta["constructor"], roi=(8, 8, 8), overlap=0.5)
+    _close(direct, a["output.decoded"], NET)
+
+
+def test_diffusion_unet_golden(cuda):
+    from ctmr_b200 import networks
+
+    a, meta = load("maisi_diffusion")
+    t_emb, y = networks.denoise_unet_ncdhw(t(a["x"]).to(cuda), t(a["timesteps"]).to(cuda),
+                                           torch.from_numpy(a["class_labels"]).to(cuda), t(a["spacing"]).to(cuda),
+                                           _on(weights(meta), cuda), constructor=meta["constructor"])
+    _close(t_emb, a["t_emb"], NET)
+    _close(y, a["y"], NET)
+
+
+def test_unet_case_golden(cuda):
+    from ctmr_b200 import networks
+
+    a, meta = load("unet")
+    _, y = networks.denoise_unet_ncdhw(t(a["input.x"]).to(cuda), t(a["input.timesteps"]).to(cuda),
+                                       torch.from_numpy(a["input.class_labels"]).to(cuda),
+                                       t(a["input.spacing"]).to(cuda), _on(weights(meta), cuda),
+                                       constructor=meta["constructor"])
+    _close(y, a["output.velocity"], NET)
+
+
+@pytest.mark.parametrize("name", ["mr_brain", "mr"])
+def test_mr_pipeline_golden(cuda, name):
+    """``tests/test_mr.py:183-247``: CFG velocity batch, 30 guided steps (CUDA graph), decode, int16 image."""
+    from ctmr_b200 import networks, pipeline
+
+    a, meta = load(name)
+    ctor = meta["constructor"]
+    unet_w, vae_w = _on(weights(meta, "weight.unet."), cuda), _on(weights(meta, "weight.vae."), cuda)
+    modality = int(meta["modality"])
+    x = t(a["input.latent"]).to(cuda)
+    spacing = pipeline.image_spacing_tensor(a["input.spacing_mm"].tolist(), cuda)
+    _, v = networks.denoise_unet_ncdhw(torch.cat([x, x]), torch.tensor([1000.0, 1000.0], device=cuda),
+                                       torch.tensor([modality, 0], device=cuda), spacing.repeat(2, 1), unet_w,
+                                       constructor=ctor["unet"])
+    _close(v, a["output.velocity_batch"], NET)
+    pipeline.CONFIGURATIONS.setdefault(meta["configuration"], {})
+    result = pipeline.sample_image_ncdhw((32, 32, 32), a["input.spacing_mm"].tolist(), unet_weights=unet_w,
+                                         vae_weights=vae_w, unet_constructor=ctor["unet"],
+                                         vae_constructor=ctor["vae"], scale_factor=1.25,
+                                         configuration=meta["configuration"], modality=modality,
+                                         guidance_scale=float(meta["guidance_scale"]), latent=x, device=cuda)
+    _close(result.latent, a["output.latent"], NET)
+    _close(result.decoded, a["output.decoded"], NET)
+    _mr_intensity_parity(result.image, a["output.decoded"])
+
+
+def _kaiming(o, c, k, gen):
+    bound = 1 / (c * k ** 3) ** 0.5
+    return (torch.rand((o, c, k, k, k), generator=gen) * 2 - 1) * bound, (torch.rand(o, generator=gen) * 2 - 1) * bound
+
+
+@pytest.mark.parametrize("precision", ["fp32", "bf16"])
+def test_config1_vae_resblock(cuda, precision):
+    """VAE ResBlock 1x64x32^3, GN(32, 1e-6), two 3x3x3 convs + residual."""
+    from ctmr_b200 import fast_b200
+
+    gen = torch.Generator().manual_seed(0)
+    x = torch.randn((1, 64, 32, 32, 32), generator=gen)
+    w1, b1 = _kaiming(64, 64, 3, gen)
+    w2, b2 = _kaiming(64, 64, 3, gen)
+    g, beta = torch.ones(64), torch.zeros(64)
+    ref = N.vae_resblock(x.double(), {"p.norm1.weight": g.double(), "p.norm1.bias": beta.double(),
+                                      "p.conv1.conv.weight": w1.double(), "p.conv1.conv.bias": b1.double(),
+                                      "p.norm2.weight": g.double(), "p.norm2.bias": beta.double(),
+                                      "p.conv2.conv.weight": w2.double(), "p.conv2.conv.bias": b2.double()},
+                         "p", 32, 1e-6)
+    with fast_b200.arithmetic_precision(precision):
+        state = [x.to(cuda)]
+        y = fast_b200.vae_resblock_ncdhw(state, (w1.to(cuda), b1.to(cuda)), (w2.to(cuda), b2.to(cuda)),
+                                         (g.to(cuda), beta.to(cuda)), (g.to(cuda), beta.to(cuda)), None,
+                                         num_groups=32, eps=1e-6)
+    err = ops_ref.rel_l2(y.float().cpu(), ref)
+    assert err <= (1e-5 if precision == "fp32" else 2e-3), f"{precision} rel-L2 {err:.3e}"
+
+
+def test_bf16_tiny_goldens(cuda):
+    """bf16 mode on the MR-Brain golden networks (2-8 channel layers, GN of 1-4 channels per group).
+
+    With so few products per output the bf16 operand rounding does not average
+    out, so these narrow networks are held to rel-L2 <= 2e-2; the stated
+    production budget is checked on the production decoder below.
+    """
+    from ctmr_b200 import fast_b200, networks, pipeline
+
+    a, meta = load("mr_brain")
+    ctor = meta["constructor"]
+    unet_w, vae_w = _on(weights(meta, "weight.unet."), cuda), _on(weights(meta, "weight.vae."), cuda)
+    x = t(a["input.latent"]).to(cuda)
+    spacing = pipeline.image_spacing_tensor(a["input.spacing_mm"].tolist(), cuda)
+    with fast_b200.arithmetic_precision("bf16"):
+        _, v = networks.denoise_unet_ncdhw(torch.cat([x, x]), torch.tensor([1000.0, 1000.0], device=cuda),
+                                           torch.tensor([int(meta["modality"]), 0], device=cuda),
+                                           spacing.repeat(2, 1), unet_w, constructor=ctor["unet"])
+        dec = pipeline.sliding_window_decode_ncdhw(t(a["output.latent"]).to(cuda), vae_w, constructor=ctor["vae"],
+                                                   roi=(80, 80, 80), overlap=0.4, scale_factor=1.25)
+    assert ops_ref.rel_l2(v.float().cpu(), torch.from_numpy(a["output.velocity_batch"])) <= 2e-2
+    assert ops_ref.rel_l2(dec.float().cpu(), torch.from_numpy(a["output.decoded"])) <= 2e-2
+
+
+@pytest.mark.parametrize(("precision", "budget"), [("bf16", 1e-2), ("fp32", 1e-5)])
+def test_production_vae_decode_budget(cuda, precision, budget):
+    """Production VAE decoder (random init) on a (1,4,8,16,8) latent vs the fp32 CPU oracle:
+    decoded volume rel-L2 <= 1e-2 in bf16 mode (the stated budget), <= 1e-5 in fp32 mode."""
+    from ctmr_b200 import fast_b200, networks
+    from ctmr_b200 import pipeline as P
+    from ctmr_b200 import weights as W
+
+    w = W.random_weights(W.vae_decoder_shapes(P.PRODUCTION_VAE), seed=1, device="cpu")
+    z = torch.randn((1, 4, 8, 16, 8), generator=torch.Generator().manual_seed(2))
+    with torch.inference_mode():
+        _, ref = N.decode_vae(z, w, P.PRODUCTION_VAE)
+    with fast_b200.arithmetic_precision(precision):
+        _, dec = networks.decode_vae_ncdhw(z.to(cuda), _on(w, cuda), constructor=P.PRODUCTION_VAE)
+    err = ops_ref.rel_l2(dec.float().cpu(), ref)
+    assert err <= budget, f"{precision} decoded rel-L2 {err:.3e}"
+
+
+@pytest.mark.parametrize(("precision", "budget"), [("bf16", 1e-2), ("fp32", 1e-5)])
+def test_production_unet_velocity(cuda, precision, budget):
+    """Production rflow UNet (random init), CFG batch 2 on a 32x32x16 latent, vs the fp32 CPU oracle."""
+    from ctmr_b200 import fast_b200, networks
+    from ctmr_b200 import pipeline as P
+    from ctmr_b200 import weights as W
+
+    w = W.random_weights(W.unet_shapes(P.PRODUCTION_UNET), seed=0, device="cpu")
+    z = torch.randn((1, 4, 32, 32, 16), generator=torch.Generator().manual_seed(3))
+    spacing = N.image_spacing_tensor((0.94, 0.94, 1.36))
+    x, tt, cls, sp = torch.cat([z, z]), torch.tensor([900.0, 900.0]), torch.tensor([9, 0]), spacing.repeat(2, 1)
+    with torch.inference_mode():
+        _, ref = N.denoise_unet(x, tt, cls, sp, w, P.PRODUCTION_UNET)
+    with fast_b200.arithmetic_precision(precision):
+        _, v = networks.denoise_unet_ncdhw(x.to(cuda), tt.to(cuda), cls.to(cuda), sp.to(cuda), _on(w, cuda),
+                                           constructor=P.PRODUCTION_UNET)
+    err = ops_ref.rel_l2(v.float().cpu(), ref)
+    assert err <= budget, f"{precision} velocity rel-L2 {err:.3e}"
+
+
+def test_no_device_wait_timed_out(cuda):
+    from ctmr_b200 import _lib
+
+    assert _lib.device_error(clear=True) == 0
