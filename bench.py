@@ -56,7 +56,7 @@ def _args():
     p.add_argument("--steps", type=int, default=2)
     p.add_argument("--warmup", type=int, default=3)
     p.add_argument("--impl", choices=("ours", "reference"), default="ours")
-    p.add_argument("--precision", choices=("bf16", "fp32"), default="bf16")
+    p.add_argument("--precision", choices=("fp16", "bf16", "fp32"), default="fp16")
     p.add_argument("--no-graph", action="store_true")
     p.add_argument("--no-cpu-baseline", action="store_true")
     return p.parse_args()

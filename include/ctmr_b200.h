@@ -52,8 +52,10 @@ enum { CTMR_DTYPE_F32 = 0, CTMR_DTYPE_BF16 = 1 };
  *   tensor-core products per step, fp32 accumulation (~2^-22 relative product
  *   error; needs |value| < 65504), the reference's "exact" mode
  *   (`_nax_conv.py:27-35`).
- * CTMR_PRECISION_BF16: bf16 operands, fp32 accumulation. */
-enum { CTMR_PRECISION_FP32 = 0, CTMR_PRECISION_BF16 = 1 };
+ * CTMR_PRECISION_BF16: bf16 operands, fp32 accumulation.
+ * CTMR_PRECISION_FP16: fp16 operands (needs |value| < 65504), fp32 accumulation;
+ *   the same tensor-core rate as bf16 with 3 more mantissa bits. */
+enum { CTMR_PRECISION_FP32 = 0, CTMR_PRECISION_BF16 = 1, CTMR_PRECISION_FP16 = 2 };
 
 /* An NDHWC activation view. data == NULL means "absent". */
 typedef struct ctmr_tensor {
@@ -79,7 +81,7 @@ typedef struct ctmr_conv3d_desc {
   int trilinear;                   /* convolve the half-pixel trilinear-2x upsampling of x */
   int avgpool;                     /* convolve the 2x2x2 mean of silu?(affine?(x)) */
   int precision;                   /* CTMR_PRECISION_* */
-  const void* weight;              /* ctmr_pack_weight output (bf16, or the fp16 hi plane) */
+  const void* weight;              /* ctmr_pack_weight output (bf16 / fp16, or the fp16 hi plane) */
   const void* weight_lo;           /* fp16 lo plane for CTMR_PRECISION_FP32 */
   const float* affine;             /* (batch, C, 2) (scale, offset) pairs, or NULL */
   int silu;                        /* apply SiLU after the affine */
@@ -98,8 +100,8 @@ typedef struct ctmr_conv3d_desc {
  * Replaces the shapes of `pack_weight` / `pack_upsample_weight` (`_nax_conv.py:391-445`). */
 CTMR_API size_t ctmr_packed_weight_elems(int out_channels, int in_channels, int kernel_size, int upsample);
 
-/* Pack an fp32 Torch-layout weight (device pointer). bf16 for CTMR_PRECISION_BF16
- * (packed_lo unused), fp16 hi/lo planes for CTMR_PRECISION_FP32.
+/* Pack an fp32 Torch-layout weight (device pointer). bf16 for CTMR_PRECISION_BF16,
+ * fp16 for CTMR_PRECISION_FP16 (packed_lo unused), fp16 hi/lo planes for CTMR_PRECISION_FP32.
  * Replaces `pack_weight` (`_nax_conv.py:391-404`) and, with upsample = 1,
  * `pack_upsample_weight` (`_nax_conv.py:407-445`). */
 CTMR_API int ctmr_pack_weight(const float* weight, int out_channels, int in_channels, int kernel_size, int upsample,

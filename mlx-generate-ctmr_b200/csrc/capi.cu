@@ -132,7 +132,7 @@ struct ConvPlan {
   int in_d, in_h, in_w;     // grid the taps read (after trilinear / avgpool)
   int row_d, row_h, row_w;  // GEMM rows
   int out_d, out_h, out_w;
-  bool exact, prepare;
+  bool exact, prepare, bf16;
   size_t prep_bytes;        // per plane
 };
 
@@ -144,7 +144,8 @@ int plan_conv(const ctmr_conv3d_desc* d, ConvPlan* p) {
   if (st) return st;
   if ((st = check_view(d->x2, "x2", false))) return st;
   if ((st = check_view(d->residual, "residual", false))) return st;
-  if (d->precision != CTMR_PRECISION_FP32 && d->precision != CTMR_PRECISION_BF16)
+  if (d->precision != CTMR_PRECISION_FP32 && d->precision != CTMR_PRECISION_BF16 &&
+      d->precision != CTMR_PRECISION_FP16)
     return fail(CTMR_ERR_INVALID, "precision");
   if (d->out_channels <= 0) return fail(CTMR_ERR_INVALID, "out_channels");
   if (d->weight == nullptr || (d->precision == CTMR_PRECISION_FP32 && d->weight_lo == nullptr))
@@ -168,6 +169,7 @@ int plan_conv(const ctmr_conv3d_desc* d, ConvPlan* p) {
     return fail(CTMR_ERR_UNSUPPORTED, "stride-2 convolution needs extents >= 2");
 
   p->exact = d->precision == CTMR_PRECISION_FP32;
+  p->bf16 = d->precision == CTMR_PRECISION_BF16;
   p->cin = d->x.channels + (d->x2.data ? d->x2.channels : 0);
   p->cpad = static_cast<int>(round_up(p->cin, 16));
   p->opad = static_cast<int>(round_up(d->out_channels, 16));
@@ -201,7 +203,7 @@ int plan_conv(const ctmr_conv3d_desc* d, ConvPlan* p) {
   }
   // The raw input can be the MMA operand directly only in bf16 mode, with no
   // transform, 16-channel granularity and 16-byte aligned rows.
-  const bool direct = !p->exact && d->x2.data == nullptr && d->affine == nullptr && !d->silu && !d->trilinear &&
+  const bool direct = p->bf16 && d->x2.data == nullptr && d->affine == nullptr && !d->silu && !d->trilinear &&
                       !d->avgpool && d->x.dtype == CTMR_DTYPE_BF16 && d->x.channels % 16 == 0 &&
                       d->x.cstride % 8 == 0 && aligned16(d->x.data);
   p->prepare = !direct;
@@ -245,11 +247,14 @@ int ctmr_pack_weight(const float* weight, int out_channels, int in_channels, int
   if (out_channels <= 0 || in_channels <= 0) return fail(CTMR_ERR_INVALID, "channel counts");
   if (kernel_size != 1 && kernel_size != 3) return fail(CTMR_ERR_UNSUPPORTED, "kernel_size must be 1 or 3");
   if (upsample && kernel_size != 3) return fail(CTMR_ERR_UNSUPPORTED, "upsample fold needs a 3x3x3 kernel");
+  if (precision != CTMR_PRECISION_FP32 && precision != CTMR_PRECISION_BF16 && precision != CTMR_PRECISION_FP16)
+    return fail(CTMR_ERR_INVALID, "precision");
   const bool split = precision == CTMR_PRECISION_FP32;
   if (split && packed_lo == nullptr) return fail(CTMR_ERR_INVALID, "lo plane missing");
+  const int kind = split ? ctmr::kPackSplitF16 : (precision == CTMR_PRECISION_BF16 ? ctmr::kPackBF16 : ctmr::kPackF16);
   cudaError_t e = ctmr::launch_pack_weight(weight, out_channels, in_channels, kernel_size, upsample,
                                            static_cast<int>(round_up(out_channels, 16)),
-                                           static_cast<int>(round_up(in_channels, 16)), split, packed, packed_lo,
+                                           static_cast<int>(round_up(in_channels, 16)), kind, packed, packed_lo,
                                            static_cast<cudaStream_t>(stream));
   return e == cudaSuccess ? CTMR_OK : cuda_fail(e, "pack_weight launch");
 }
@@ -297,7 +302,7 @@ int ctmr_conv3d_stages(const ctmr_conv3d_desc* d, void* workspace, size_t worksp
     pp.silu = d->silu;
     pp.cpad = p.cpad;
     pp.out_cstride = p.cpad;
-    pp.out_kind = p.exact ? ctmr::kPrepOutSplitF16 : ctmr::kPrepOutBF16;
+    pp.out_kind = p.exact ? ctmr::kPrepOutSplitF16 : (p.bf16 ? ctmr::kPrepOutBF16 : ctmr::kPrepOutF16);
     pp.out = workspace;
     pp.out_lo = p.exact ? static_cast<uint8_t*>(workspace) + p.prep_bytes : nullptr;
     cudaError_t e = ctmr::launch_prepare(pp, stream);
@@ -343,11 +348,12 @@ int ctmr_conv3d_stages(const ctmr_conv3d_desc* d, void* workspace, size_t worksp
   g.out_coff = d->y_coffset;
   g.out_d = p.out_d, g.out_h = p.out_h, g.out_w = p.out_w;
   g.lo_scale = 1.0f / 2048.0f;
+  g.operand_bf16 = p.bf16 ? 1 : 0;
 
   // 3. TMA descriptors.
   ctmr::ConvMaps maps;
   std::memset(&maps, 0, sizeof(maps));
-  const bool bf16 = !p.exact;
+  const bool bf16 = p.bf16;
   const long long eb = 2;  // element bytes (bf16 / fp16)
   const long long rs = a_cstride * eb;
   if (rs % 16 != 0) return fail(CTMR_ERR_INVALID, "operand row pitch must be a multiple of 16 bytes");

@@ -16,7 +16,7 @@
 // registers -> +bias (per channel or per batch item) -> +residual -> store.
 //
 // Precision modes:
-//   bf16:     bf16 x bf16 products, fp32 accumulation, one rounding at the store.
+//   bf16/fp16: bf16 x bf16 or fp16 x fp16 products, fp32 accumulation, one rounding at the store.
 //   fp32 (EXACT): every fp32 operand v is carried as fp16 hi = half(v) and
 //             lo = half((v - hi) * 2^11); three MMAs per K step accumulate
 //             hi*hi into one TMEM accumulator and hi*lo + lo*hi into a second,
@@ -239,7 +239,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     // chunk into fp32 registers with round-to-nearest adds while the next chunk
     // accumulates. This bounds how long the tensor core's own fp32 accumulation
     // runs, whose rounding error otherwise grows with K (27 * C_in products).
-    const uint32_t idesc = idesc_f16(!EXACT, kRows, static_cast<uint32_t>(g.bn));
+    const uint32_t idesc = idesc_f16(!EXACT && g.operand_bf16 != 0, kRows, static_cast<uint32_t>(g.bn));
     const uint32_t bn = static_cast<uint32_t>(g.bn);
     const uint32_t acc_lo = tmem + 2u * bn;
     const int T = EXACT ? g.chunk_iters : n_iter;

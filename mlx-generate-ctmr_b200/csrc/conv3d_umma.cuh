@@ -37,6 +37,7 @@ struct ConvGeom {
   int stages;
   uint32_t tmem_cols;
   int chunk_iters;              // EXACT: K iterations per promoted accumulator chunk
+  int operand_bf16;             // single-plane modes: 1 bf16 operands, 0 fp16 operands
   // epilogue
   const float* bias;            // may be null
   int bias_bstride;             // 0 (per channel) or cout (per batch item)

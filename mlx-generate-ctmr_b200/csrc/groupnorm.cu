@@ -9,10 +9,10 @@
 // (x - pivot)^2 around its first value, converts them to (count, mean, M2), and
 // the block merges lanes, then channels into groups, in a fixed order (Chan et
 // al.'s pairwise update), writing one (n, mean, M2) partial per group.
-// Pass 2 (grid batch): one thread per group merges the chunk partials in
-// order in double precision, then writes scale = gamma * rstd and
-// offset = beta - mean * scale for each channel. The fixed merge order makes
-// the result bitwise reproducible run to run.
+// Pass 2 (grid batch): one warp per group merges the chunk partials (lanes in
+// order, then a fixed shuffle tree) in double precision, then writes
+// scale = gamma * rstd and offset = beta - mean * scale for each channel. The
+// fixed merge order makes the result bitwise reproducible run to run.
 #include <cuda_runtime.h>
 #include <cstdint>
 
@@ -164,31 +164,53 @@ __global__ void __launch_bounds__(kGnThreads) gn_partial_kernel(const GnParams p
   }
 }
 
+struct MomentsD {
+  double n, mean, m2;
+};
+
+__device__ __forceinline__ MomentsD merge_d(MomentsD a, MomentsD b) {
+  if (b.n == 0.0) return a;
+  if (a.n == 0.0) return b;
+  const double n = a.n + b.n;
+  const double delta = b.mean - a.mean;
+  const double fb = b.n / n;
+  return MomentsD{n, a.mean + delta * fb, a.m2 + b.m2 + delta * delta * a.n * fb};
+}
+
+// One warp per group: lanes merge strided chunk subsets in order, then a fixed
+// shuffle tree joins the lanes (double precision, deterministic).
 __global__ void gn_finalize_kernel(const GnParams p) {
   const int b = blockIdx.x;
   const int ctot = p.src[0].channels + p.src[1].channels;
   const int cpg = ctot / p.groups;
-  for (int g = threadIdx.x; g < p.groups; g += blockDim.x) {
-    double n = 0.0, mean = 0.0, m2 = 0.0;
-    for (int k = 0; k < p.chunks; ++k) {
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int nwarps = blockDim.x >> 5;
+  for (int g = warp; g < p.groups; g += nwarps) {
+    MomentsD m{0.0, 0.0, 0.0};
+    for (int k = lane; k < p.chunks; k += 32) {
       const float* q = p.partials + ((static_cast<long long>(b) * p.chunks + k) * p.groups + g) * 3;
-      const double nb = q[0];
-      if (nb == 0.0) continue;
-      const double tot = n + nb;
-      const double delta = static_cast<double>(q[1]) - mean;
-      mean += delta * nb / tot;
-      m2 += static_cast<double>(q[2]) + delta * delta * n * nb / tot;
-      n = tot;
+      m = merge_d(m, MomentsD{q[0], q[1], q[2]});
     }
-    const double var = n > 0.0 ? m2 / n : 0.0;
+#pragma unroll
+    for (int off = 1; off < 32; off <<= 1) {
+      MomentsD o;
+      o.n = __shfl_down_sync(0xffffffffu, m.n, off);
+      o.mean = __shfl_down_sync(0xffffffffu, m.mean, off);
+      o.m2 = __shfl_down_sync(0xffffffffu, m.m2, off);
+      if ((lane & (2 * off - 1)) == 0) m = merge_d(m, o);
+    }
+    m.n = __shfl_sync(0xffffffffu, m.n, 0);
+    m.mean = __shfl_sync(0xffffffffu, m.mean, 0);
+    m.m2 = __shfl_sync(0xffffffffu, m.m2, 0);
+    const double var = m.n > 0.0 ? m.m2 / m.n : 0.0;
     const double rstd = 1.0 / sqrt(var + static_cast<double>(p.eps));
-    for (int c = g * cpg; c < (g + 1) * cpg; ++c) {
+    for (int c = g * cpg + lane; c < (g + 1) * cpg; c += 32) {
       const double gam = p.gamma != nullptr ? static_cast<double>(p.gamma[c]) : 1.0;
       const double bet = p.beta != nullptr ? static_cast<double>(p.beta[c]) : 0.0;
       const double scale = gam * rstd;
       float* a = p.affine + (static_cast<long long>(b) * ctot + c) * 2;
       a[0] = static_cast<float>(scale);
-      a[1] = static_cast<float>(bet - mean * scale);
+      a[1] = static_cast<float>(bet - m.mean * scale);
     }
   }
 }
@@ -196,8 +218,8 @@ __global__ void gn_finalize_kernel(const GnParams p) {
 }  // namespace
 
 int gn_chunks_for(int batch, long long voxels) {
-  long long chunks = (4LL * 148 + batch - 1) / batch;
-  const long long max_chunks = (voxels + 255) / 256;
+  long long chunks = (2LL * 148 + batch - 1) / batch;
+  const long long max_chunks = (voxels + 511) / 512;
   if (chunks > max_chunks) chunks = max_chunks;
   if (chunks < 1) chunks = 1;
   return static_cast<int>(chunks);
@@ -214,7 +236,7 @@ cudaError_t launch_group_norm_affine(const GnParams& p, cudaStream_t stream) {
   gn_partial_kernel<<<dim3(p.chunks, p.batch), kGnThreads, chan_smem, stream>>>(p);
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return e;
-  gn_finalize_kernel<<<p.batch, 128, 0, stream>>>(p);
+  gn_finalize_kernel<<<p.batch, 512, 0, stream>>>(p);
   return cudaGetLastError();
 }
 

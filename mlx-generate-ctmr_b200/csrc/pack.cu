@@ -1,6 +1,6 @@
 // Weight packing for the implicit-GEMM convolution: Torch (O, C, k, k, k) fp32
-// -> K-major taps [T][O_pad][C_pad] in bf16, or in fp16 hi/lo planes for the
-// split-fp32 mode. Counterpart of `pack_weight` / `pack_upsample_weight`
+// -> K-major taps [T][O_pad][C_pad] in bf16 or fp16, or in fp16 hi/lo planes
+// for the split-fp32 mode. Counterpart of `pack_weight` / `pack_upsample_weight`
 // (`_nax_conv.py:391-445`), with the tap-major rows transposed to the K-major
 // operand layout the tensor cores read.
 //
@@ -31,7 +31,7 @@ __device__ __forceinline__ void fold_range(int p, int t, int& k0, int& k1) {
 }
 
 __global__ void pack_weight_kernel(const float* __restrict__ w, int O, int C, int k, int upsample, int opad,
-                                   int cpad, int split, void* __restrict__ out, void* __restrict__ out_lo) {
+                                   int cpad, int kind, void* __restrict__ out, void* __restrict__ out_lo) {
   const int taps = upsample ? 64 : k * k * k;
   const long long total = static_cast<long long>(taps) * opad * cpad;
   for (long long i = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x; i < total;
@@ -55,11 +55,13 @@ __global__ void pack_weight_kernel(const float* __restrict__ w, int O, int C, in
             for (int kw = w0; kw <= w1; ++kw) v += src[(kd * 3 + kh) * 3 + kw];
       }
     }
-    if (split) {
+    if (kind == kPackSplitF16) {
       const __half hi = __float2half_rn(v);
       const __half lo = __float2half_rn((v - __half2float(hi)) * 2048.f);
       static_cast<__half*>(out)[i] = hi;
       static_cast<__half*>(out_lo)[i] = lo;
+    } else if (kind == kPackF16) {
+      static_cast<__half*>(out)[i] = __float2half_rn(v);
     } else {
       static_cast<__nv_bfloat16*>(out)[i] = __float2bfloat16_rn(v);
     }
@@ -68,14 +70,14 @@ __global__ void pack_weight_kernel(const float* __restrict__ w, int O, int C, in
 
 }  // namespace
 
-cudaError_t launch_pack_weight(const float* w, int O, int C, int k, int upsample, int opad, int cpad, int split,
+cudaError_t launch_pack_weight(const float* w, int O, int C, int k, int upsample, int opad, int cpad, int kind,
                                void* out, void* out_lo, cudaStream_t stream) {
   const int taps = upsample ? 64 : k * k * k;
   const long long total = static_cast<long long>(taps) * opad * cpad;
   long long blocks = (total + 255) / 256;
   if (blocks > 148LL * 32) blocks = 148LL * 32;
   if (blocks < 1) blocks = 1;
-  pack_weight_kernel<<<static_cast<unsigned>(blocks), 256, 0, stream>>>(w, O, C, k, upsample, opad, cpad, split,
+  pack_weight_kernel<<<static_cast<unsigned>(blocks), 256, 0, stream>>>(w, O, C, k, upsample, opad, cpad, kind,
                                                                         out, out_lo);
   return cudaGetLastError();
 }

@@ -5,7 +5,9 @@
 
 namespace ctmr {
 
-cudaError_t launch_pack_weight(const float* w, int O, int C, int k, int upsample, int opad, int cpad, int split,
+enum PackKind : int { kPackBF16 = 0, kPackSplitF16 = 1, kPackF16 = 2 };
+
+cudaError_t launch_pack_weight(const float* w, int O, int C, int k, int upsample, int opad, int cpad, int kind,
                                void* out, void* out_lo, cudaStream_t stream);
 
 }  // namespace ctmr

@@ -223,6 +223,20 @@ __global__ void prepare_kernel(const PrepParams p) {
       }
       *reinterpret_cast<uint4*>(static_cast<uint16_t*>(p.out) + oidx) = make_uint4(hw[0], hw[1], hw[2], hw[3]);
       *reinterpret_cast<uint4*>(static_cast<uint16_t*>(p.out_lo) + oidx) = make_uint4(lw[0], lw[1], lw[2], lw[3]);
+    } else if (p.out_kind == kPrepOutF16) {
+      uint16_t* o = static_cast<uint16_t*>(p.out) + oidx;
+      const int n = min(8, p.cpad - c0);
+      uint32_t hw[4];
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        hw[i] = static_cast<uint32_t>(__half_as_ushort(__float2half_rn(out[2 * i]))) |
+                (static_cast<uint32_t>(__half_as_ushort(__float2half_rn(out[2 * i + 1]))) << 16);
+      }
+      if (n == 8 && (reinterpret_cast<uintptr_t>(o) & 15) == 0) {
+        *reinterpret_cast<uint4*>(o) = make_uint4(hw[0], hw[1], hw[2], hw[3]);
+      } else {
+        for (int i = 0; i < n; ++i) o[i] = static_cast<uint16_t>(hw[i / 2] >> (16 * (i % 2)));
+      }
     } else if (p.out_kind == kPrepOutF32) {
       float* o = static_cast<float*>(p.out) + oidx;
       const int n = min(8, p.cpad - c0);

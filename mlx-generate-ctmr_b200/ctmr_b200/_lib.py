@@ -22,6 +22,7 @@ DTYPE_F32 = 0
 DTYPE_BF16 = 1
 PRECISION_FP32 = 0
 PRECISION_BF16 = 1
+PRECISION_FP16 = 2
 TRANSFORM_COPY = 0
 TRANSFORM_TRILINEAR = 1
 TRANSFORM_AVGPOOL = 2

@@ -52,6 +52,18 @@ class Pairs:
         self.leader = rank - self.member
 
 
+def gather_pair(local: torch.Tensor, out: torch.Tensor, group) -> torch.Tensor:
+    """``out = [member 0's local, member 1's local]`` (flat), the pair's [cond, uncond] velocity."""
+    n = local.numel()
+    dist.all_gather([out[:n], out[n:]], local.reshape(-1), group=group)
+    return out
+
+
+def window_partition(n_windows: int, member: int, members: int = 2) -> list[int]:
+    """Windows a pair member decodes: round-robin, so every window is decoded exactly once."""
+    return [i for i in range(n_windows) if i % members == member]
+
+
 class CfgSplitStep:
     """One guided step with the two CFG branches on the two members of a pair.
 
@@ -113,8 +125,7 @@ class CfgSplitStep:
                 ops.LAUNCHES[0] += self.launches_per_step
             else:
                 self._unet()
-            flat = self.v_local.permute(0, 2, 3, 4, 1).reshape(-1)
-            dist.all_gather_into_tensor(self.v_pair, flat, group=self.pairs.group)
+            gather_pair(self.v_local.permute(0, 2, 3, 4, 1), self.v_pair, self.pairs.group)
             ops.rflow_step(self.z, self.v_pair_view, guidance=self.guidance, dt=self.dt, out=self.z)
         return self.z.clone()
 

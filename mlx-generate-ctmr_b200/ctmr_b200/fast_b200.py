@@ -10,8 +10,11 @@ Precision (request-scoped, like the reference's ``arithmetic_mode``):
   ``"fp32"`` (default) — convolutions in the split-fp16 "exact" mode (fp32
       accumulation, ~2^-22 relative product error), the reference's default
       arithmetic.
-  ``"bf16"`` — bf16 tensor-core operands with fp32 accumulation and fp32
-      epilogue additions.
+  ``"bf16"`` / ``"fp16"`` — bf16 or fp16 tensor-core operands with fp32
+      accumulation and fp32 epilogue additions (same tensor-core rate; fp16
+      carries 3 more mantissa bits and needs |value| < 65504, like the split
+      mode's hi plane). The small dense ops (attention, Q/K/V projections) run
+      in the same 16-bit type with fp32 accumulation.
 Activations between layers are stored in fp32 in both modes: the conv-input
 preparation pass (which applies the group norm and SiLU anyway) writes the
 bf16 or split-fp16 operand, so a bf16 operand costs no extra pass, and the
@@ -105,8 +108,31 @@ def _split(x) -> tuple[torch.Tensor, torch.Tensor | None]:
 _packed: dict[tuple[int, bool, str], tuple[weakref.ref, ops.PackedWeight]] = {}
 
 
-def _pack(weight: torch.Tensor, *, upsample: bool = False) -> ops.PackedWeight:
+NARROW_CHANNELS = 16
+
+
+def conv_precision(weight: torch.Tensor) -> str:
+    """Operand precision of one convolution under the active mode.
+
+    In the 16-bit modes the narrow input and output convolutions (at most 16
+    channels on either side: the latent-facing conv_in / post_quant_conv and the
+    4- or 1-channel output convs) keep the split-fp32 operands. Those layers are
+    memory-bound, so the extra operand plane costs no measurable time, and the
+    output conv otherwise dominates the decoded volume's error budget.
+    """
     precision = _precision.get()
+    if precision != "fp32" and min(int(weight.shape[0]), int(weight.shape[1])) <= NARROW_CHANNELS:
+        return "fp32"
+    return precision
+
+
+def dense_dtype() -> torch.dtype:
+    """Operand type of the dense (non-conv) tensor-core ops: fp32, or the 16-bit mode's type."""
+    return {"fp32": torch.float32, "bf16": torch.bfloat16, "fp16": torch.float16}[_precision.get()]
+
+
+def _pack(weight: torch.Tensor, *, upsample: bool = False) -> ops.PackedWeight:
+    precision = conv_precision(weight)
     key = (id(weight), upsample, precision)
     hit = _packed.get(key)
     if hit is not None and hit[0]() is weight:
@@ -305,8 +331,11 @@ def attention_projection(array: torch.Tensor, weight: torch.Tensor, bias: torch.
 def self_attention_tokens(tokens: torch.Tensor, weights: Mapping[str, torch.Tensor], *, heads: int, scale: float,
                           include_fc: bool, mx=None, prefix: str = "attn", qkv_bias: bool = True) -> torch.Tensor:
     """Q/K/V projections, multi-head self-attention and optional ``out_proj`` on ``(B, L, C)`` (``fast_fp32.py:352-396``)."""
+    dt = dense_dtype()
+    tokens = tokens.to(dt)
     q, k, v = (
-        linear(tokens, weights[f"{prefix}.to_{n}.weight"], weights[f"{prefix}.to_{n}.bias"] if qkv_bias else None)
+        F.linear(tokens, weights[f"{prefix}.to_{n}.weight"].to(dt),
+                 weights[f"{prefix}.to_{n}.bias"].to(dt) if qkv_bias else None)
         for n in ("q", "k", "v")
     )
     b, length, c = q.shape
@@ -317,7 +346,7 @@ def self_attention_tokens(tokens: torch.Tensor, weights: Mapping[str, torch.Tens
     att = F.scaled_dot_product_attention(split(q), split(k), split(v), scale=scale)
     merged = att.transpose(1, 2).reshape(b, length, c)
     if include_fc:
-        merged = linear(merged, weights[f"{prefix}.out_proj.weight"], weights[f"{prefix}.out_proj.bias"])
+        merged = F.linear(merged, weights[f"{prefix}.out_proj.weight"].to(dt), weights[f"{prefix}.out_proj.bias"].to(dt))
     return merged
 
 
@@ -336,5 +365,5 @@ def spatial_attention_ncdhw(x: torch.Tensor, weights: Mapping[str, torch.Tensor]
     normed = group_norm_ncdhw(x, weights["norm.weight"], weights["norm.bias"], num_groups=num_groups, eps=eps)
     tokens = normed.permute(0, 2, 3, 4, 1).reshape(b, d * h * w, c)
     merged = self_attention_tokens(tokens, weights, heads=heads, scale=scale, include_fc=include_fc)
-    out = merged.to(x.dtype).reshape(b, d, h, w, c).permute(0, 4, 1, 2, 3)
-    return x + out
+    out = merged.reshape(b, d, h, w, c).permute(0, 4, 1, 2, 3)
+    return x + out.to(x.dtype)

@@ -20,7 +20,7 @@ from ._lib import LIB, check
 
 F32 = torch.float32
 BF16 = torch.bfloat16
-PRECISIONS = ("fp32", "bf16")
+PRECISIONS = ("fp32", "bf16", "fp16")
 
 # Instrumentation: LAUNCHES counts the library's kernel launches issued from
 # Python; when PROFILE is a list, conv3d records (start, end, flops) CUDA events
@@ -50,6 +50,8 @@ def _precision_code(precision: str) -> int:
         return _lib.PRECISION_FP32
     if precision == "bf16":
         return _lib.PRECISION_BF16
+    if precision == "fp16":
+        return _lib.PRECISION_FP16
     raise ValueError(f"precision must be one of {PRECISIONS}; got {precision!r}")
 
 
@@ -160,7 +162,7 @@ def pack_weight(weight: torch.Tensor, precision: str, *, upsample: bool = False)
         hi = torch.empty(n, dtype=torch.float16, device=w.device)
         lo = torch.empty(n, dtype=torch.float16, device=w.device)
     else:
-        hi = torch.empty(n, dtype=BF16, device=w.device)
+        hi = torch.empty(n, dtype=BF16 if precision == "bf16" else torch.float16, device=w.device)
         lo = None
     _count(1)
     check(
