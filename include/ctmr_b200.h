@@ -122,6 +122,25 @@ enum { CTMR_CONV_PREPARE = 1, CTMR_CONV_GEMM = 2 };
 CTMR_API int ctmr_conv3d_stages(const ctmr_conv3d_desc* desc, void* workspace, size_t workspace_bytes, int stages,
                                 void* stream);
 
+/* The convolution of ctmr_conv3d for callers that cannot allocate device
+ * memory. (No counterpart in the reference: its MLX runtime allocates every
+ * buffer itself.) Plugins living inside another framework's memory pool and
+ * real-time or safety-constrained callers whose allocations are all made up
+ * front cannot call cudaMalloc for the workspace ctmr_conv3d needs; this
+ * variant takes that scratch from one static device
+ * array of CTMR_CONV3D_NOALLOC_SCRATCH_BYTES that every GPU loading the
+ * library holds until exit, and allocates nothing.
+ *   - Inputs and outputs are passed exactly as for ctmr_conv3d.
+ *   - Convolutions whose prepared operand (ctmr_conv3d_workspace_size) exceeds
+ *     the scratch are rejected with CTMR_ERR_WORKSPACE, nothing launched.
+ *   - The first call on a device looks up the array's address on that device
+ *     (cudaGetSymbolAddress); make it before any stream capture.
+ *   - All calls share the array and it keeps the last call's contents; nothing
+ *     in it needs to start at zero. Calls whose kernels overlap on the GPU
+ *     (unordered streams) race on it and must not be issued. */
+#define CTMR_CONV3D_NOALLOC_SCRATCH_BYTES (32u << 20)
+CTMR_API int ctmr_conv3d_noalloc(const ctmr_conv3d_desc* desc, void* stream);
+
 /* Workspace bytes for ctmr_group_norm_affine. */
 CTMR_API size_t ctmr_group_norm_workspace_size(int batch, long long voxels, int groups);
 

@@ -220,6 +220,11 @@ int plan_conv(const ctmr_conv3d_desc* d, ConvPlan* p) {
 
 }  // namespace
 
+namespace ctmr {
+// Records `message` as this thread's ctmr_last_error() and returns `status`.
+int set_last_error(int status, const char* message) { return fail(status, "%s", message); }
+}  // namespace ctmr
+
 extern "C" {
 
 const char* ctmr_status_string(int status) {

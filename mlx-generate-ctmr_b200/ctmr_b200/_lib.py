@@ -36,6 +36,7 @@ EXPORTED_SYMBOLS = (
     "ctmr_conv3d_workspace_size",
     "ctmr_conv3d",
     "ctmr_conv3d_stages",
+    "ctmr_conv3d_noalloc",
     "ctmr_group_norm_workspace_size",
     "ctmr_group_norm_affine",
     "ctmr_transform",
@@ -127,6 +128,7 @@ def _load() -> ctypes.CDLL:
         "ctmr_conv3d_workspace_size": (sz, [ctypes.POINTER(Conv3dDesc)]),
         "ctmr_conv3d": (i, [ctypes.POINTER(Conv3dDesc), vp, sz, vp]),
         "ctmr_conv3d_stages": (i, [ctypes.POINTER(Conv3dDesc), vp, sz, i, vp]),
+        "ctmr_conv3d_noalloc": (i, [ctypes.POINTER(Conv3dDesc), vp]),
         "ctmr_group_norm_workspace_size": (sz, [i, ll, i]),
         "ctmr_group_norm_affine": (i, [Tensor, Tensor, i, ll, vp, vp, i, f, vp, vp, sz, vp]),
         "ctmr_transform": (i, [ctypes.POINTER(TransformDesc), vp]),
