@@ -59,6 +59,12 @@ def _args():
     p.add_argument("--precision", choices=("fp16", "bf16", "fp32"), default="fp16")
     p.add_argument("--no-graph", action="store_true")
     p.add_argument("--no-cpu-baseline", action="store_true")
+    p.add_argument("--case", choices=("volume", "sweep", "conv", "unet-step", "vae-window"), default="volume",
+                   help="volume: the benchmark; sweep: BASELINE config 5 conv sweep (TFLOP/s per shape); "
+                        "conv / unet-step / vae-window: one kernel shape, one UNet step or one decode window "
+                        "(bounded workloads for profiler captures)")
+    p.add_argument("--shape", default="2,64,64,64,32,64", help="conv case: B,C,D,H,W,O")
+    p.add_argument("--iters", type=int, default=3)
     return p.parse_args()
 
 
@@ -167,9 +173,79 @@ def run_reference(args, rank: int) -> None:
     print(json.dumps(line), flush=True)
 
 
+# ---------------------------------------------------------------- kernel-level cases
+SWEEP_SHAPES = [(b, c, n, n, n, o) for n in (16, 32, 64) for c, o in ((32, 32), (64, 64), (128, 128), (256, 256))
+                for b in (1, 2)] + [(2, 512, 8, 8, 4, 512), (2, 512, 16, 16, 8, 512), (1, 128, 128, 128, 64, 128),
+                                    (1, 64, 128, 128, 64, 64)]
+
+
+def _time_conv(shape, precision: str, iters: int, dev) -> tuple[float, float]:
+    from ctmr_b200 import ops
+
+    b, c, d, h, w, o = shape
+    gen = torch.Generator(device=dev).manual_seed(0)
+    x = torch.randn((b, c, d, h, w), device=dev, generator=gen).contiguous(memory_format=torch.channels_last_3d)
+    wt = torch.randn((o, c, 3, 3, 3), device=dev, generator=gen) / (27 * c) ** 0.5
+    bias = torch.randn(o, device=dev, generator=gen)
+    packed = ops.pack_weight(wt, precision)
+    for _ in range(2):
+        ops.conv3d(x, packed, bias)
+    prof: list = []
+    ops.PROFILE = prof
+    for _ in range(iters):
+        ops.conv3d(x, packed, bias)
+    ops.PROFILE = None
+    torch.cuda.synchronize(dev)
+    ms = statistics.median(s_.elapsed_time(e_) for s_, e_, _ in prof)
+    return ms, prof[0][2] / (ms * 1e-3) / 1e12
+
+
+def run_case(args) -> None:
+    from ctmr_b200 import fast_b200 as A
+    from ctmr_b200 import pipeline as P
+    from ctmr_b200 import weights as W
+
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    with A.arithmetic_precision(args.precision):
+        if args.case in ("sweep", "conv"):
+            shapes = SWEEP_SHAPES if args.case == "sweep" else [tuple(int(v) for v in args.shape.split(","))]
+            peaks, kind = _peaks()
+            peak = float(peaks.get("bf16_tflops", FALLBACK_PEAKS["bf16_tflops"]))
+            for shape in shapes:
+                ms, tflops = _time_conv(shape, args.precision, args.iters, dev)
+                print(json.dumps({"case": "conv3d 3x3x3", "shape_bcdhwo": shape, "precision": args.precision,
+                                  "gemm_ms": round(ms, 4), "tflops": round(tflops, 1),
+                                  "frac_of_peak": round(tflops / peak, 3), "peak": f"{kind} bf16_tflops {peak}"}),
+                      flush=True)
+            return
+        if args.case == "unet-step":
+            w = W.random_weights(W.unet_shapes(P.PRODUCTION_UNET), seed=0, device=dev)
+            step = P.GuidedUNetStep(w, P.PRODUCTION_UNET, LATENT, class_label=MODALITY,
+                                    spacing=P.image_spacing_tensor(SPACING, dev), guidance_scale=GUIDANCE,
+                                    device=dev, use_cuda_graph=False)
+            step.z.copy_(torch.randn(LATENT, device=dev))
+            step.t.fill_(900.0)
+            step.dt.fill_(0.01)
+            for _ in range(args.iters):
+                step._step()
+        else:
+            w = W.random_weights(W.vae_decoder_shapes(P.PRODUCTION_VAE), seed=1, device=dev)
+            from ctmr_b200 import networks
+
+            z = torch.randn((1, 4, *DECODE_ROI), device=dev)
+            for _ in range(args.iters):
+                networks.decode_vae_ncdhw(z, w, constructor=P.PRODUCTION_VAE)
+        torch.cuda.synchronize(dev)
+        print(json.dumps({"case": args.case, "precision": args.precision, "iters": args.iters, "ok": True}))
+
+
 # ---------------------------------------------------------------- GPU arm
 def main() -> None:
     args = _args()
+    if args.case != "volume":
+        run_case(args)
+        return
     from ctmr_b200 import distributed as D
 
     rank, world, local = D.init_from_env() if int(os.environ.get("WORLD_SIZE", "1")) > 1 else (0, 1, 0)

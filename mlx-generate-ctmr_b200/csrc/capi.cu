@@ -395,7 +395,7 @@ int ctmr_conv3d_stages(const ctmr_conv3d_desc* d, void* workspace, size_t worksp
 
 size_t ctmr_group_norm_workspace_size(int batch, long long voxels, int groups) {
   if (batch <= 0 || voxels <= 0 || groups <= 0) return 0;
-  return static_cast<size_t>(batch) * ctmr::gn_chunks_for(batch, voxels) * groups * 3 * sizeof(float);
+  return static_cast<size_t>(batch) * ctmr::gn_max_chunks(batch) * groups * 3 * sizeof(float);
 }
 
 int ctmr_group_norm_affine(ctmr_tensor x, ctmr_tensor x2, int batch, long long voxels, const float* gamma,
@@ -423,7 +423,7 @@ int ctmr_group_norm_affine(ctmr_tensor x, ctmr_tensor x2, int batch, long long v
   p.beta = beta;
   p.affine = affine;
   p.partials = static_cast<float*>(workspace);
-  p.chunks = ctmr::gn_chunks_for(batch, voxels);
+  p.chunks = ctmr::gn_chunks_for(batch, voxels, ctot);
   cudaError_t e = ctmr::launch_group_norm_affine(p, static_cast<cudaStream_t>(stream));
   return e == cudaSuccess ? CTMR_OK : cuda_fail(e, "group_norm launch");
 }

@@ -217,10 +217,13 @@ __global__ void gn_finalize_kernel(const GnParams p) {
 
 }  // namespace
 
-int gn_chunks_for(int batch, long long voxels) {
-  long long chunks = (2LL * 148 + batch - 1) / batch;
-  const long long max_chunks = (voxels + 511) / 512;
-  if (chunks > max_chunks) chunks = max_chunks;
+int gn_max_chunks(int batch) { return (2 * 296 + batch - 1) / batch; }
+
+// About 128 KB of input per block, at least 16 voxels, at most ~600 blocks in all.
+int gn_chunks_for(int batch, long long voxels, int channels) {
+  long long chunks = (voxels * channels * 4 + (128 << 10) - 1) / (128 << 10);
+  if (chunks > gn_max_chunks(batch)) chunks = gn_max_chunks(batch);
+  if (chunks > (voxels + 15) / 16) chunks = (voxels + 15) / 16;
   if (chunks < 1) chunks = 1;
   return static_cast<int>(chunks);
 }

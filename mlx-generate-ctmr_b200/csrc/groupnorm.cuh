@@ -20,7 +20,8 @@ struct GnParams {
   int chunks;
 };
 
-int gn_chunks_for(int batch, long long voxels);
+int gn_max_chunks(int batch);
+int gn_chunks_for(int batch, long long voxels, int channels);
 cudaError_t launch_group_norm_affine(const GnParams& p, cudaStream_t stream);
 
 }  // namespace ctmr

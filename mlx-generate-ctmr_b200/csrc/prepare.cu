@@ -91,31 +91,95 @@ __device__ __forceinline__ float lerp_ref(float lo, float hi, float a) {
   return __fmaf_rn(1.f - a, lo, __fmul_rn(a, hi));
 }
 
-__global__ void prepare_kernel(const PrepParams p) {
-  const int chunks = (p.cpad + 7) >> 3;
-  const long long total = static_cast<long long>(p.batch) * p.od * p.oh * p.ow * chunks;
+// SiLU y / (1 + e^-y). FAST (16-bit outputs, rounded afterwards anyway) uses
+// the hardware exponential and reciprocal; the fp32 modes use expf and an IEEE
+// division.
+template <bool FAST>
+__device__ __forceinline__ float silu_f(float t) {
+  if (FAST) return __fdividef(t, 1.f + __expf(-t));
+  return t / (1.f + expf(-t));
+}
+
+__device__ __forceinline__ void store8(const PrepParams& p, long long oidx, int c0, const float (&out)[8]) {
+  if (p.out_kind == kPrepOutBF16) {
+    uint16_t* o = static_cast<uint16_t*>(p.out) + oidx;
+    const int n = min(8, p.cpad - c0);
+    uint32_t w[4];
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      __nv_bfloat162 h = __floats2bfloat162_rn(out[2 * i], out[2 * i + 1]);
+      w[i] = *reinterpret_cast<uint32_t*>(&h);
+    }
+    if (n == 8 && (reinterpret_cast<uintptr_t>(o) & 15) == 0) {
+      *reinterpret_cast<uint4*>(o) = make_uint4(w[0], w[1], w[2], w[3]);
+    } else {
+      for (int i = 0; i < n; ++i) o[i] = static_cast<uint16_t>(w[i / 2] >> (16 * (i % 2)));
+    }
+  } else if (p.out_kind == kPrepOutF16) {
+    uint16_t* o = static_cast<uint16_t*>(p.out) + oidx;
+    const int n = min(8, p.cpad - c0);
+    uint32_t hw[4];
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      hw[i] = static_cast<uint32_t>(__half_as_ushort(__float2half_rn(out[2 * i]))) |
+              (static_cast<uint32_t>(__half_as_ushort(__float2half_rn(out[2 * i + 1]))) << 16);
+    }
+    if (n == 8 && (reinterpret_cast<uintptr_t>(o) & 15) == 0) {
+      *reinterpret_cast<uint4*>(o) = make_uint4(hw[0], hw[1], hw[2], hw[3]);
+    } else {
+      for (int i = 0; i < n; ++i) o[i] = static_cast<uint16_t>(hw[i / 2] >> (16 * (i % 2)));
+    }
+  } else if (p.out_kind == kPrepOutSplitF16) {
+    uint32_t hw[4], lw[4];
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const __half h0 = __float2half_rn(out[2 * i]);
+      const __half h1 = __float2half_rn(out[2 * i + 1]);
+      const __half l0 = __float2half_rn((out[2 * i] - __half2float(h0)) * 2048.f);
+      const __half l1 = __float2half_rn((out[2 * i + 1] - __half2float(h1)) * 2048.f);
+      hw[i] = static_cast<uint32_t>(__half_as_ushort(h0)) | (static_cast<uint32_t>(__half_as_ushort(h1)) << 16);
+      lw[i] = static_cast<uint32_t>(__half_as_ushort(l0)) | (static_cast<uint32_t>(__half_as_ushort(l1)) << 16);
+    }
+    *reinterpret_cast<uint4*>(static_cast<uint16_t*>(p.out) + oidx) = make_uint4(hw[0], hw[1], hw[2], hw[3]);
+    *reinterpret_cast<uint4*>(static_cast<uint16_t*>(p.out_lo) + oidx) = make_uint4(lw[0], lw[1], lw[2], lw[3]);
+  } else {
+    float* o = static_cast<float*>(p.out) + oidx;
+    const int n = min(8, p.cpad - c0);
+    if (n == 8 && (reinterpret_cast<uintptr_t>(o) & 15) == 0) {
+      reinterpret_cast<float4*>(o)[0] = make_float4(out[0], out[1], out[2], out[3]);
+      reinterpret_cast<float4*>(o)[1] = make_float4(out[4], out[5], out[6], out[7]);
+    } else {
+      for (int i = 0; i < n; ++i) o[i] = out[i];
+    }
+  }
+}
+
+// One item = one output voxel x 8 channels. All index arithmetic is 32-bit
+// (voxel counts per batch item fit comfortably; the host checks), and the copy
+// mode needs no spatial decomposition because output voxel v is input voxel v.
+template <int MODE, bool FAST>
+__global__ void __launch_bounds__(256) prepare_kernel(const PrepParams p, const unsigned chunks_log2,
+                                                      const unsigned vox_out) {
+  const unsigned chunks = 1u << chunks_log2;
+  const unsigned items_per_batch = vox_out << chunks_log2;
+  const unsigned total = items_per_batch * static_cast<unsigned>(p.batch);
   const int ctot = p.src[0].channels + p.src[1].channels;
-  for (long long gid = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x; gid < total;
-       gid += static_cast<long long>(gridDim.x) * blockDim.x) {
-    const int chunk = static_cast<int>(gid % chunks);
-    long long v = gid / chunks;
-    const int x = static_cast<int>(v % p.ow); v /= p.ow;
-    const int y = static_cast<int>(v % p.oh); v /= p.oh;
-    const int z = static_cast<int>(v % p.od);
-    const int b = static_cast<int>(v / p.od);
-    const int c0 = chunk * 8;
+  const unsigned vox_in = static_cast<unsigned>(p.sd) * p.sh * p.sw;
+  for (unsigned item = blockIdx.x * blockDim.x + threadIdx.x; item < total; item += gridDim.x * blockDim.x) {
+    const unsigned b = item / items_per_batch;
+    const unsigned rem = item - b * items_per_batch;
+    const unsigned v = rem >> chunks_log2;
+    const int c0 = static_cast<int>(rem & (chunks - 1)) * 8;
+    if (c0 >= p.cpad) continue;  // chunk slots past the row when the chunk count is not a power of two
     float out[8];
 #pragma unroll
     for (int i = 0; i < 8; ++i) out[i] = 0.f;
     if (c0 < ctot) {
-      // The chunk reads one source with vector loads when it lies inside it;
-      // chunks that straddle the concat boundary or the channel end go per channel.
       const int cnt = min(8, ctot - c0);
-      const bool in0 = c0 + cnt <= p.src[0].channels;
       const bool in1 = c0 >= p.src[0].channels;
+      const bool single = (c0 + cnt <= p.src[0].channels) || in1;
       const PrepSource& s = p.src[in1 ? 1 : 0];
       const int cs = in1 ? c0 - p.src[0].channels : c0;
-      const bool single = in0 || in1;
       float sc[8], of[8];
 #pragma unroll
       for (int i = 0; i < 8; ++i) {
@@ -123,142 +187,125 @@ __global__ void prepare_kernel(const PrepParams p) {
         of[i] = 0.f;
       }
       if (p.affine != nullptr) {
-        for (int i = 0; i < cnt; ++i) {
-          const long long a = (static_cast<long long>(b) * ctot + c0 + i) * 2;
-          sc[i] = __ldg(p.affine + a);
-          of[i] = __ldg(p.affine + a + 1);
+        const float* a = p.affine + (static_cast<long long>(b) * ctot + c0) * 2;
+        if (cnt == 8 && (reinterpret_cast<uintptr_t>(a) & 15) == 0) {
+#pragma unroll
+          for (int i = 0; i < 4; ++i) {
+            const float4 q = __ldg(reinterpret_cast<const float4*>(a) + i);
+            sc[2 * i] = q.x;
+            of[2 * i] = q.y;
+            sc[2 * i + 1] = q.z;
+            of[2 * i + 1] = q.w;
+          }
+        } else {
+          for (int i = 0; i < cnt; ++i) {
+            sc[i] = __ldg(a + 2 * i);
+            of[i] = __ldg(a + 2 * i + 1);
+          }
         }
       }
-      const long long bvox = static_cast<long long>(b) * p.sd * p.sh * p.sw;
-      if (p.mode == kPrepTrilinear) {
-        int z0, z1, y0, y1, x0, x1;
-        float az, ay, ax;
-        tri_axis(z, p.sd, z0, z1, az);
-        tri_axis(y, p.sh, y0, y1, ay);
-        tri_axis(x, p.sw, x0, x1, ax);
-        float r[2][2][2][8];
-        const int zs[2] = {z0, z1}, ys[2] = {y0, y1}, xs[2] = {x0, x1};
-#pragma unroll
-        for (int i = 0; i < 2; ++i)
-#pragma unroll
-          for (int j = 0; j < 2; ++j)
-#pragma unroll
-            for (int k = 0; k < 2; ++k)
-              load8_cat(p, single, s, bvox + (static_cast<long long>(zs[i]) * p.sh + ys[j]) * p.sw + xs[k], c0, cs, cnt, r[i][j][k]);
-#pragma unroll
-        for (int c = 0; c < 8; ++c) {
-          const float r00 = lerp_ref(r[0][0][0][c], r[0][0][1][c], ax);
-          const float r01 = lerp_ref(r[0][1][0][c], r[0][1][1][c], ax);
-          const float r10 = lerp_ref(r[1][0][0][c], r[1][0][1][c], ax);
-          const float r11 = lerp_ref(r[1][1][0][c], r[1][1][1][c], ax);
-          const float p0 = lerp_ref(r00, r01, ay);
-          const float p1 = lerp_ref(r10, r11, ay);
-          out[c] = lerp_ref(p0, p1, az);
-        }
-      } else if (p.mode == kPrepAvgPool) {
-        float acc[8];
-#pragma unroll
-        for (int c = 0; c < 8; ++c) acc[c] = 0.f;
-#pragma unroll
-        for (int dz = 0; dz < 2; ++dz)
-#pragma unroll
-          for (int dy = 0; dy < 2; ++dy)
-#pragma unroll
-            for (int dx = 0; dx < 2; ++dx) {
-              float r[8];
-              load8_cat(p, single, s, bvox + (static_cast<long long>(2 * z + dz) * p.sh + 2 * y + dy) * p.sw + 2 * x + dx,
-                        c0, cs, cnt, r);
-#pragma unroll
-              for (int c = 0; c < 8; ++c) {
-                float t = fmaf(r[c], sc[c], of[c]);
-                if (p.silu) t = t / (1.f + expf(-t));
-                acc[c] += t;
-              }
-            }
-#pragma unroll
-        for (int c = 0; c < 8; ++c) out[c] = acc[c] * 0.125f;
-      } else {
+      const long long bvox = static_cast<long long>(b) * vox_in;
+      if (MODE == kPrepCopy) {
         float r[8];
-        load8_cat(p, single, s, bvox + (static_cast<long long>(z) * p.sh + y) * p.sw + x, c0, cs, cnt, r);
+        load8_cat(p, single, s, bvox + v, c0, cs, cnt, r);
 #pragma unroll
         for (int c = 0; c < 8; ++c) {
           float t = fmaf(r[c], sc[c], of[c]);
-          if (p.silu) t = t / (1.f + expf(-t));
+          if (p.silu) t = silu_f<FAST>(t);
           out[c] = t;
+        }
+      } else {
+        const unsigned x = v % static_cast<unsigned>(p.ow);
+        const unsigned yz = v / static_cast<unsigned>(p.ow);
+        const unsigned y = yz % static_cast<unsigned>(p.oh);
+        const unsigned z = yz / static_cast<unsigned>(p.oh);
+        if (MODE == kPrepTrilinear) {
+          int z0, z1, y0, y1, x0, x1;
+          float az, ay, ax;
+          tri_axis(static_cast<int>(z), p.sd, z0, z1, az);
+          tri_axis(static_cast<int>(y), p.sh, y0, y1, ay);
+          tri_axis(static_cast<int>(x), p.sw, x0, x1, ax);
+          float r[2][2][2][8];
+          const int zs[2] = {z0, z1}, ys[2] = {y0, y1}, xs[2] = {x0, x1};
+#pragma unroll
+          for (int i = 0; i < 2; ++i)
+#pragma unroll
+            for (int j = 0; j < 2; ++j)
+#pragma unroll
+              for (int k = 0; k < 2; ++k)
+                load8_cat(p, single, s, bvox + (static_cast<long long>(zs[i]) * p.sh + ys[j]) * p.sw + xs[k], c0, cs,
+                          cnt, r[i][j][k]);
+#pragma unroll
+          for (int c = 0; c < 8; ++c) {
+            const float r00 = lerp_ref(r[0][0][0][c], r[0][0][1][c], ax);
+            const float r01 = lerp_ref(r[0][1][0][c], r[0][1][1][c], ax);
+            const float r10 = lerp_ref(r[1][0][0][c], r[1][0][1][c], ax);
+            const float r11 = lerp_ref(r[1][1][0][c], r[1][1][1][c], ax);
+            const float p0 = lerp_ref(r00, r01, ay);
+            const float p1 = lerp_ref(r10, r11, ay);
+            out[c] = lerp_ref(p0, p1, az);
+          }
+        } else {  // kPrepAvgPool
+          float acc[8];
+#pragma unroll
+          for (int c = 0; c < 8; ++c) acc[c] = 0.f;
+#pragma unroll
+          for (int dz = 0; dz < 2; ++dz)
+#pragma unroll
+            for (int dy = 0; dy < 2; ++dy)
+#pragma unroll
+              for (int dx = 0; dx < 2; ++dx) {
+                float r[8];
+                load8_cat(p, single, s,
+                          bvox + (static_cast<long long>(2 * z + dz) * p.sh + 2 * y + dy) * p.sw + 2 * x + dx, c0, cs,
+                          cnt, r);
+#pragma unroll
+                for (int c = 0; c < 8; ++c) {
+                  float t = fmaf(r[c], sc[c], of[c]);
+                  if (p.silu) t = silu_f<FAST>(t);
+                  acc[c] += t;
+                }
+              }
+#pragma unroll
+          for (int c = 0; c < 8; ++c) out[c] = acc[c] * 0.125f;
         }
       }
 #pragma unroll
       for (int c = 0; c < 8; ++c)
         if (c >= cnt) out[c] = 0.f;
     }
-    const long long orow = ((static_cast<long long>(b) * p.od + z) * p.oh + y) * p.ow + x;
-    const long long oidx = orow * p.out_cstride + c0;
-    if (p.out_kind == kPrepOutBF16) {
-      uint16_t* o = static_cast<uint16_t*>(p.out) + oidx;
-      const int n = min(8, p.cpad - c0);
-      if (n == 8 && (reinterpret_cast<uintptr_t>(o) & 15) == 0) {
-        uint32_t w[4];
-#pragma unroll
-        for (int i = 0; i < 4; ++i) {
-          __nv_bfloat162 h = __floats2bfloat162_rn(out[2 * i], out[2 * i + 1]);
-          w[i] = *reinterpret_cast<uint32_t*>(&h);
-        }
-        *reinterpret_cast<uint4*>(o) = make_uint4(w[0], w[1], w[2], w[3]);
-      } else {
-        for (int i = 0; i < n; ++i) {
-          __nv_bfloat16 h = __float2bfloat16_rn(out[i]);
-          o[i] = *reinterpret_cast<uint16_t*>(&h);
-        }
-      }
-    } else if (p.out_kind == kPrepOutSplitF16) {
-      uint32_t hw[4], lw[4];
-#pragma unroll
-      for (int i = 0; i < 4; ++i) {
-        const __half h0 = __float2half_rn(out[2 * i]);
-        const __half h1 = __float2half_rn(out[2 * i + 1]);
-        const __half l0 = __float2half_rn((out[2 * i] - __half2float(h0)) * 2048.f);
-        const __half l1 = __float2half_rn((out[2 * i + 1] - __half2float(h1)) * 2048.f);
-        hw[i] = static_cast<uint32_t>(__half_as_ushort(h0)) | (static_cast<uint32_t>(__half_as_ushort(h1)) << 16);
-        lw[i] = static_cast<uint32_t>(__half_as_ushort(l0)) | (static_cast<uint32_t>(__half_as_ushort(l1)) << 16);
-      }
-      *reinterpret_cast<uint4*>(static_cast<uint16_t*>(p.out) + oidx) = make_uint4(hw[0], hw[1], hw[2], hw[3]);
-      *reinterpret_cast<uint4*>(static_cast<uint16_t*>(p.out_lo) + oidx) = make_uint4(lw[0], lw[1], lw[2], lw[3]);
-    } else if (p.out_kind == kPrepOutF16) {
-      uint16_t* o = static_cast<uint16_t*>(p.out) + oidx;
-      const int n = min(8, p.cpad - c0);
-      uint32_t hw[4];
-#pragma unroll
-      for (int i = 0; i < 4; ++i) {
-        hw[i] = static_cast<uint32_t>(__half_as_ushort(__float2half_rn(out[2 * i]))) |
-                (static_cast<uint32_t>(__half_as_ushort(__float2half_rn(out[2 * i + 1]))) << 16);
-      }
-      if (n == 8 && (reinterpret_cast<uintptr_t>(o) & 15) == 0) {
-        *reinterpret_cast<uint4*>(o) = make_uint4(hw[0], hw[1], hw[2], hw[3]);
-      } else {
-        for (int i = 0; i < n; ++i) o[i] = static_cast<uint16_t>(hw[i / 2] >> (16 * (i % 2)));
-      }
-    } else if (p.out_kind == kPrepOutF32) {
-      float* o = static_cast<float*>(p.out) + oidx;
-      const int n = min(8, p.cpad - c0);
-      if (n == 8 && (reinterpret_cast<uintptr_t>(o) & 15) == 0) {
-        reinterpret_cast<float4*>(o)[0] = make_float4(out[0], out[1], out[2], out[3]);
-        reinterpret_cast<float4*>(o)[1] = make_float4(out[4], out[5], out[6], out[7]);
-      } else {
-        for (int i = 0; i < n; ++i) o[i] = out[i];
-      }
-    }
+    store8(p, (static_cast<long long>(b) * vox_out + v) * p.out_cstride + c0, c0, out);
   }
 }
 
 }  // namespace
 
 cudaError_t launch_prepare(const PrepParams& p, cudaStream_t stream) {
-  const long long total = static_cast<long long>(p.batch) * p.od * p.oh * p.ow * ((p.cpad + 7) >> 3);
+  const int chunks = (p.cpad + 7) >> 3;
+  unsigned log2 = 0;
+  while ((1 << log2) < chunks) ++log2;
+  const long long vox_out = static_cast<long long>(p.od) * p.oh * p.ow;
+  const long long total = static_cast<long long>(p.batch) * (vox_out << log2);
   if (total <= 0) return cudaSuccess;
+  if (total >= (1LL << 31) || static_cast<long long>(p.sd) * p.sh * p.sw >= (1LL << 31))
+    return cudaErrorInvalidValue;  // the 32-bit item space of prepare_kernel
   const int threads = 256;
   long long blocks = (total + threads - 1) / threads;
-  if (blocks > 148LL * 64) blocks = 148LL * 64;
-  prepare_kernel<<<static_cast<unsigned>(blocks), threads, 0, stream>>>(p);
+  if (blocks > 148LL * 16) blocks = 148LL * 16;
+  const bool fast = p.out_kind == kPrepOutBF16 || p.out_kind == kPrepOutF16;
+  const dim3 grid(static_cast<unsigned>(blocks));
+  const unsigned vo = static_cast<unsigned>(vox_out);
+#define CTMR_PREP(MODE)                                                         \
+  if (fast) prepare_kernel<MODE, true><<<grid, threads, 0, stream>>>(p, log2, vo); \
+  else prepare_kernel<MODE, false><<<grid, threads, 0, stream>>>(p, log2, vo);
+  if (p.mode == kPrepTrilinear) {
+    CTMR_PREP(kPrepTrilinear)
+  } else if (p.mode == kPrepAvgPool) {
+    CTMR_PREP(kPrepAvgPool)
+  } else {
+    CTMR_PREP(kPrepCopy)
+  }
+#undef CTMR_PREP
   return cudaGetLastError();
 }
 
