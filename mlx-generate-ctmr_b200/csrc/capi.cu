@@ -9,6 +9,7 @@
 #include <cstdarg>
 #include <cstdint>
 #include <cstdio>
+#include <cstdlib>
 #include <cstring>
 #include <mutex>
 
@@ -23,6 +24,9 @@ namespace ctmr {
 int conv_stage_plan(int kc, int bn, bool exact, bool one_cta_per_sm, size_t* smem_bytes);
 cudaError_t launch_conv3d_umma(const ConvMaps& maps, const ConvGeom& g, int kc, bool exact, size_t smem,
                                cudaStream_t stream);
+int conv_v2_stage_plan(int kc, int mt, int tw, int bn, size_t* smem_bytes);
+cudaError_t launch_conv3d_umma_v2(const ConvMaps& maps, const ConvGeom& g, int kc, int mt, int tw, int sms,
+                                  size_t smem, cudaStream_t stream);
 extern __device__ unsigned int g_device_error;
 }  // namespace ctmr
 
@@ -102,7 +106,34 @@ int encode_weight(CUtensorMap* map, const void* base, bool bf16, long long cpad,
   return CTMR_OK;
 }
 
+int encode_weight3(CUtensorMap* map, const void* base, bool bf16, long long cpad, long long opad, long long taps,
+                   int kc, int bn, int box_taps) {
+  auto enc = tensor_map_encoder();
+  if (enc == nullptr) return fail(CTMR_ERR_CUDA, "cuTensorMapEncodeTiled is unavailable");
+  cuuint64_t dims[3] = {static_cast<cuuint64_t>(cpad), static_cast<cuuint64_t>(opad),
+                        static_cast<cuuint64_t>(taps)};
+  cuuint64_t strides[2] = {static_cast<cuuint64_t>(cpad * 2), static_cast<cuuint64_t>(cpad * 2 * opad)};
+  cuuint32_t box[3] = {static_cast<cuuint32_t>(kc), static_cast<cuuint32_t>(bn), static_cast<cuuint32_t>(box_taps)};
+  cuuint32_t estr[3] = {1, 1, 1};
+  CUresult r = enc(map, bf16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 3,
+                   const_cast<void*>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                   swizzle_for(kc), CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return fail(CTMR_ERR_INVALID, "weight tensor map rejected (CUresult %d)", int(r));
+  return CTMR_OK;
+}
+
 bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+int sm_count() {
+  int dev = 0, n = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess)
+    return 148;
+  return n > 0 ? n : 148;
+}
+
+// Set when the driver rejects the H-before-W tensor view of the persistent kernel; every
+// later convolution then takes the per-tap kernel.
+bool g_v2_unavailable = false;
 
 int check_view(const ctmr_tensor& t, const char* name, bool required) {
   if (t.data == nullptr) {
@@ -134,6 +165,10 @@ struct ConvPlan {
   int out_d, out_h, out_w;
   bool exact, prepare, bf16;
   size_t prep_bytes;        // per plane
+  // per-tap kernel tiling and its split-K
+  int tile_w, tile_h, tile_d, tiles_w, tiles_h, tiles_d, n_tiles, ksplit;
+  size_t part_bytes;
+  size_t workspace() const { return prep_bytes * (exact ? 2 : 1) + part_bytes; }
 };
 
 int plan_conv(const ctmr_conv3d_desc* d, ConvPlan* p) {
@@ -215,6 +250,29 @@ int plan_conv(const ctmr_conv3d_desc* d, ConvPlan* p) {
     if (d->residual.channels < d->out_channels)
       return fail(CTMR_ERR_INVALID, "residual has %d channels, output %d", d->residual.channels, d->out_channels);
   }
+  // Per-tap kernel: a 128-voxel box over the GEMM rows, w fastest.
+  p->tile_w = std::min(next_pow2(p->row_w), 128);
+  p->tile_h = std::min(next_pow2(p->row_h), 128 / p->tile_w);
+  p->tile_d = 128 / (p->tile_w * p->tile_h);
+  p->tiles_w = (p->row_w + p->tile_w - 1) / p->tile_w;
+  p->tiles_h = (p->row_h + p->tile_h - 1) / p->tile_h;
+  p->tiles_d = (p->row_d + p->tile_d - 1) / p->tile_d;
+  p->n_tiles = (p->opad + p->bn - 1) / p->bn;
+  // Split K over the grid's z when the tiles alone cannot fill the GPU (the deep,
+  // small grids): about 2 CTAs per SM, at least 4 K iterations per split.
+  const long long ctas = static_cast<long long>(p->tiles_w) * p->tiles_h * p->tiles_d * d->batch * p->phases *
+                         p->n_tiles;
+  const int n_iter = p->taps * (p->cpad / p->kc);
+  p->ksplit = 1;
+  if (p->mode != ctmr::kModeUp2 && ctas < 120) {
+    long long want = (2 * 148 + ctas - 1) / ctas;
+    want = std::min<long long>(want, n_iter / 4);
+    if (want >= 2) p->ksplit = static_cast<int>(want);
+  }
+  p->part_bytes = p->ksplit > 1 ? static_cast<size_t>(p->ksplit) * d->batch * p->row_d * p->row_h * p->row_w *
+                                      p->n_tiles * p->bn * sizeof(float)
+                                : 0;
+  p->part_bytes = static_cast<size_t>(round_up(static_cast<long long>(p->part_bytes), 256));
   return CTMR_OK;
 }
 
@@ -267,7 +325,7 @@ int ctmr_pack_weight(const float* weight, int out_channels, int in_channels, int
 size_t ctmr_conv3d_workspace_size(const ctmr_conv3d_desc* desc) {
   ConvPlan p{};
   if (plan_conv(desc, &p) != CTMR_OK) return 0;
-  return p.prep_bytes * (p.exact ? 2 : 1);
+  return p.workspace();
 }
 
 int ctmr_conv3d(const ctmr_conv3d_desc* d, void* workspace, size_t workspace_bytes, void* stream_ptr) {
@@ -282,7 +340,7 @@ int ctmr_conv3d_stages(const ctmr_conv3d_desc* d, void* workspace, size_t worksp
   int st = plan_conv(d, &p);
   if (st != CTMR_OK) return st;
   cudaStream_t stream = static_cast<cudaStream_t>(stream_ptr);
-  const size_t need = p.prep_bytes * (p.exact ? 2 : 1);
+  const size_t need = p.workspace();
   if (need > workspace_bytes || (need > 0 && workspace == nullptr))
     return fail(CTMR_ERR_WORKSPACE, "conv3d needs %zu workspace bytes, got %zu", need, workspace_bytes);
 
@@ -315,16 +373,92 @@ int ctmr_conv3d_stages(const ctmr_conv3d_desc* d, void* workspace, size_t worksp
   }
   if (!(stages & CTMR_CONV_GEMM)) return CTMR_OK;
 
-  // 2. Tile plan over the GEMM-row grid: a 128-voxel box, w fastest.
+  // 2a. The persistent atom-shifted kernel for 16-bit stride-1 3x3x3 (and nearest-2x) convolutions.
+  if (!p.exact && !g_v2_unavailable && (p.mode == ctmr::kModeConv3 || p.mode == ctmr::kModeUp2) &&
+      p.row_w >= 16 && p.row_h >= 8 && getenv("CTMR_DISABLE_V2") == nullptr) {
+    const int tw = p.mode == ctmr::kModeConv3 ? 3 : 2;
+    const int mt = p.row_d >= 2 ? 2 : 1;
+    const int bn = std::min(p.opad, 128);
+    // Largest channel block whose pipeline is at least 3 stages deep (else 2).
+    int kc = 0;
+    size_t smem2 = 0;
+    int stages2 = 0;
+    for (int min_stages : {3, 2}) {
+      for (int cand : {64, 32, 16}) {
+        size_t sm_b = 0;
+        const int st = p.cpad % cand ? 0 : ctmr::conv_v2_stage_plan(cand, mt, tw, bn, &sm_b);
+        if (st >= min_stages) {
+          kc = cand, smem2 = sm_b, stages2 = st;
+          break;
+        }
+      }
+      if (kc) break;
+    }
+    if (kc != 0) {
+      ctmr::ConvGeom g{};
+      g.batch = d->batch;
+      g.row_d = p.row_d, g.row_h = p.row_h, g.row_w = p.row_w;
+      g.tile_w = 16, g.tile_h = 8, g.tile_d = mt;
+      g.tiles_w = (p.row_w + 15) / 16;
+      g.tiles_h = (p.row_h + 7) / 8;
+      g.tiles_d = (p.row_d + mt - 1) / mt;
+      g.phases = p.phases;
+      g.taps = p.taps;
+      g.kblocks = p.cpad / kc;
+      g.mode = p.mode;
+      g.bn = bn;
+      g.cout = d->out_channels;
+      g.stages = stages2;
+      g.tmem_cols = static_cast<uint32_t>(std::max(32, next_pow2(2 * mt * bn)));
+      g.operand_bf16 = p.bf16 ? 1 : 0;
+      g.ksplit = 1;
+      g.n_tiles = (p.opad + bn - 1) / bn;
+      const long long total = static_cast<long long>(g.n_tiles) * g.tiles_w * g.tiles_h * g.tiles_d * d->batch *
+                              p.phases;
+      if (total > 0 && total < (1LL << 31)) {
+        g.total_tiles = static_cast<int>(total);
+        g.bias = d->bias;
+        g.bias_bstride = d->bias_per_batch ? d->out_channels : 0;
+        g.res = d->residual.data;
+        g.res_bf16 = d->residual.dtype == CTMR_DTYPE_BF16;
+        g.res_cstride = d->residual.cstride;
+        g.res_up = d->residual_upsampled;
+        g.res_d = d->residual_upsampled ? p.out_d / 2 : p.out_d;
+        g.res_h = d->residual_upsampled ? p.out_h / 2 : p.out_h;
+        g.res_w = d->residual_upsampled ? p.out_w / 2 : p.out_w;
+        g.out = d->y;
+        g.out_bf16 = d->y_dtype == CTMR_DTYPE_BF16;
+        g.out_cstride = d->y_cstride;
+        g.out_coff = d->y_coffset;
+        g.out_d = p.out_d, g.out_h = p.out_h, g.out_w = p.out_w;
+        ctmr::ConvMaps maps;
+        std::memset(&maps, 0, sizeof(maps));
+        const long long rs = a_cstride * 2;
+        const long long W = p.in_w, H = p.in_h, D = p.in_d;
+        // H before W: an 8-row swizzle atom holds 8 consecutive h of one w.
+        if (rs % 16 == 0 &&
+            encode_act(&maps.a[0], a_hi, p.bf16, p.cpad, H, W, D, d->batch, W * rs, rs, H * W * rs, D * H * W * rs,
+                       kc, 8, 16 + tw - 1, mt) == CTMR_OK &&
+            encode_weight3(&maps.b, d->weight, p.bf16, p.cpad, p.opad, p.mode == ctmr::kModeUp2 ? 64 : 27, kc, bn,
+                           tw) == CTMR_OK) {
+          cudaError_t e = ctmr::launch_conv3d_umma_v2(maps, g, kc, mt, tw, sm_count(), smem2, stream);
+          return e == cudaSuccess ? CTMR_OK : cuda_fail(e, "conv3d v2 launch");
+        }
+        g_v2_unavailable = true;  // fall through to the per-tap kernel
+      }
+    }
+  }
+
+  // 2. Tile plan over the GEMM-row grid: a 128-voxel box, w fastest (planned in plan_conv).
   ctmr::ConvGeom g{};
   g.batch = d->batch;
   g.row_d = p.row_d, g.row_h = p.row_h, g.row_w = p.row_w;
-  g.tile_w = std::min(next_pow2(p.row_w), 128);
-  g.tile_h = std::min(next_pow2(p.row_h), 128 / g.tile_w);
-  g.tile_d = 128 / (g.tile_w * g.tile_h);
-  g.tiles_w = (p.row_w + g.tile_w - 1) / g.tile_w;
-  g.tiles_h = (p.row_h + g.tile_h - 1) / g.tile_h;
-  g.tiles_d = (p.row_d + g.tile_d - 1) / g.tile_d;
+  g.tile_w = p.tile_w, g.tile_h = p.tile_h, g.tile_d = p.tile_d;
+  g.tiles_w = p.tiles_w, g.tiles_h = p.tiles_h, g.tiles_d = p.tiles_d;
+  g.ksplit = p.ksplit;
+  g.partial = p.ksplit > 1 ? reinterpret_cast<float*>(static_cast<uint8_t*>(workspace) + p.prep_bytes * (p.exact ? 2 : 1))
+                           : nullptr;
+  g.part_cstride = p.n_tiles * p.bn;
   g.phases = p.phases;
   g.taps = p.taps;
   g.kblocks = p.cpad / p.kc;

@@ -26,6 +26,7 @@
 //             FP32 theoretical peak performance"), the same operand split the
 //             reference uses (`_nax_conv.py:27-35`): ~2^-22 relative product error.
 #include "conv3d_umma.cuh"
+#include "epilogue.cuh"
 #include "ptx.cuh"
 
 #include <cuda_bf16.h>
@@ -50,81 +51,6 @@ struct StageLayout {
     stage_bytes = (a_bytes + b_bytes) * (exact ? 2u : 1u);
   }
 };
-
-__device__ __forceinline__ float bf16_to_f32(uint16_t v) { return __uint_as_float(static_cast<uint32_t>(v) << 16); }
-
-__device__ __forceinline__ uint32_t pack_bf16x2(float a, float b) {
-  __nv_bfloat162 h = __floats2bfloat162_rn(a, b);
-  return *reinterpret_cast<uint32_t*>(&h);
-}
-
-// Add the residual and store 16 output columns [n, n+16) of one voxel row.
-__device__ __forceinline__ void store_row16(const ConvGeom& g, float (&v)[16], int n, long long out_off,
-                                            long long res_off) {
-  const int cnt = min(16, g.cout - n);
-  if (cnt <= 0) return;
-  if (g.res != nullptr) {
-    if (g.res_bf16) {
-      const uint16_t* r = static_cast<const uint16_t*>(g.res) + res_off;
-      if (cnt == 16 && (reinterpret_cast<uintptr_t>(r) & 15) == 0) {
-        const uint4 q0 = __ldg(reinterpret_cast<const uint4*>(r));
-        const uint4 q1 = __ldg(reinterpret_cast<const uint4*>(r) + 1);
-        const uint32_t w[8] = {q0.x, q0.y, q0.z, q0.w, q1.x, q1.y, q1.z, q1.w};
-#pragma unroll
-        for (int i = 0; i < 8; ++i) {
-          v[2 * i] += bf16_to_f32(static_cast<uint16_t>(w[i] & 0xFFFFu));
-          v[2 * i + 1] += bf16_to_f32(static_cast<uint16_t>(w[i] >> 16));
-        }
-      } else {
-        for (int i = 0; i < cnt; ++i) v[i] += bf16_to_f32(r[i]);
-      }
-    } else {
-      const float* r = static_cast<const float*>(g.res) + res_off;
-      if (cnt == 16 && (reinterpret_cast<uintptr_t>(r) & 15) == 0) {
-#pragma unroll
-        for (int i = 0; i < 4; ++i) {
-          const float4 q = __ldg(reinterpret_cast<const float4*>(r) + i);
-          v[4 * i] += q.x;
-          v[4 * i + 1] += q.y;
-          v[4 * i + 2] += q.z;
-          v[4 * i + 3] += q.w;
-        }
-      } else {
-        for (int i = 0; i < cnt; ++i) v[i] += __ldg(r + i);
-      }
-    }
-  }
-  if (g.out_bf16) {
-    uint16_t* o = static_cast<uint16_t*>(g.out) + out_off;
-    if (cnt == 16 && (reinterpret_cast<uintptr_t>(o) & 15) == 0) {
-      uint4 q0, q1;
-      q0.x = pack_bf16x2(v[0], v[1]);
-      q0.y = pack_bf16x2(v[2], v[3]);
-      q0.z = pack_bf16x2(v[4], v[5]);
-      q0.w = pack_bf16x2(v[6], v[7]);
-      q1.x = pack_bf16x2(v[8], v[9]);
-      q1.y = pack_bf16x2(v[10], v[11]);
-      q1.z = pack_bf16x2(v[12], v[13]);
-      q1.w = pack_bf16x2(v[14], v[15]);
-      reinterpret_cast<uint4*>(o)[0] = q0;
-      reinterpret_cast<uint4*>(o)[1] = q1;
-    } else {
-      for (int i = 0; i < cnt; ++i) {
-        __nv_bfloat16 h = __float2bfloat16_rn(v[i]);
-        o[i] = *reinterpret_cast<uint16_t*>(&h);
-      }
-    }
-  } else {
-    float* o = static_cast<float*>(g.out) + out_off;
-    if (cnt == 16 && (reinterpret_cast<uintptr_t>(o) & 15) == 0) {
-#pragma unroll
-      for (int i = 0; i < 4; ++i)
-        reinterpret_cast<float4*>(o)[i] = make_float4(v[4 * i], v[4 * i + 1], v[4 * i + 2], v[4 * i + 3]);
-    } else {
-      for (int i = 0; i < cnt; ++i) o[i] = v[i];
-    }
-  }
-}
 
 template <int KC, bool EXACT>
 __global__ void __launch_bounds__(kThreads, 1)
@@ -156,7 +82,10 @@ __global__ void __launch_bounds__(kThreads, 1)
   const int phase = t;
   const int w0 = tw_i * g.tile_w, h0 = th_i * g.tile_h, d0 = td_i * g.tile_d;
   const int n0 = blockIdx.y * g.bn;
-  const int n_iter = g.taps * g.kblocks;
+  // Split-K: this CTA accumulates K iterations [it_begin, it_begin + n_iter) of the tap-major walk.
+  const int n_iter_all = g.taps * g.kblocks;
+  const int it_begin = static_cast<int>(static_cast<long long>(n_iter_all) * blockIdx.z / g.ksplit);
+  const int n_iter = static_cast<int>(static_cast<long long>(n_iter_all) * (blockIdx.z + 1) / g.ksplit) - it_begin;
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < S; ++s) {
@@ -199,8 +128,8 @@ __global__ void __launch_bounds__(kThreads, 1)
         break;
       }
       if (*abort_flag) break;
-      const int tap = it / g.kblocks;
-      const int c = (it - tap * g.kblocks) * KC;
+      const int tap = (it_begin + it) / g.kblocks;
+      const int c = (it_begin + it - tap * g.kblocks) * KC;
       int map = 0, x = w0, y = h0, z = d0, btap = tap;
       if (g.mode == kModeConv3) {
         z += tap / 9 - 1;
@@ -292,7 +221,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     bool ok = true;
     if (EXACT) {
       const int T = g.chunk_iters;
-      const int nchunks = (g.taps * g.kblocks + T - 1) / T;
+      const int nchunks = (n_iter + T - 1) / T;
       for (int chunk = 0; chunk < nchunks && ok; ++chunk) {
         const int buf = chunk & 1;
         ok = mbar_wait_bounded(&chunk_full[buf], static_cast<uint32_t>(chunk >> 1) & 1u, kErrWaitAcc);
@@ -345,7 +274,14 @@ __global__ void __launch_bounds__(kThreads, 1)
           tmem_ld16(lane_addr + static_cast<uint32_t>(c), v);
         }
         const int n = n0 + c;
-        if (valid && n < g.cout) {
+        if (valid && g.ksplit > 1) {
+          // Raw fp32 partial sum; bias and residual are added by the reduction.
+          float* dst = g.partial + ((((static_cast<long long>(blockIdx.z) * g.batch + b) * g.row_d + rd) * g.row_h + rh) *
+                                        g.row_w + rw) * g.part_cstride + n;
+#pragma unroll
+          for (int i = 0; i < 4; ++i)
+            reinterpret_cast<float4*>(dst)[i] = make_float4(v[4 * i], v[4 * i + 1], v[4 * i + 2], v[4 * i + 3]);
+        } else if (valid && n < g.cout) {
           if (bias != nullptr) {
             const int cnt = min(16, g.cout - n);
             for (int i = 0; i < cnt; ++i) v[i] += __ldg(bias + n + i);
@@ -361,6 +297,50 @@ __global__ void __launch_bounds__(kThreads, 1)
   if (warp == 1) {
     tc_fence_after();
     tmem_dealloc(tmem, g.tmem_cols);
+  }
+}
+
+// Split-K reduction (the role of the reference's `_REDUCE`, `_nax_conv.py:320-331`):
+// sums the fp32 partial planes in split order, adds bias and the residual, and
+// rounds once to the output type. One thread per (row voxel, 4 channels).
+__global__ void splitk_reduce_kernel(const ConvGeom g) {
+  const int q4 = (g.cout + 3) / 4;
+  const long long rows = static_cast<long long>(g.batch) * g.row_d * g.row_h * g.row_w;
+  const long long total = rows * q4;
+  const long long plane = rows * g.part_cstride;
+  for (long long i = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x; i < total;
+       i += static_cast<long long>(gridDim.x) * blockDim.x) {
+    const int n = static_cast<int>(i % q4) * 4;
+    const long long r = i / q4;
+    long long t = r;
+    const int rw = static_cast<int>(t % g.row_w); t /= g.row_w;
+    const int rh = static_cast<int>(t % g.row_h); t /= g.row_h;
+    const int rd = static_cast<int>(t % g.row_d);
+    const int b = static_cast<int>(t / g.row_d);
+    float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+    const float* src = g.partial + r * g.part_cstride + n;
+    for (int z = 0; z < g.ksplit; ++z) {
+      const float4 q = __ldg(reinterpret_cast<const float4*>(src + z * plane));
+      acc.x += q.x;
+      acc.y += q.y;
+      acc.z += q.z;
+      acc.w += q.w;
+    }
+    float v[16] = {acc.x, acc.y, acc.z, acc.w};
+    const int cnt = min(4, g.cout - n);
+    if (g.bias != nullptr) {
+      const float* bias = g.bias + static_cast<long long>(b) * g.bias_bstride;
+      for (int k = 0; k < cnt; ++k) v[k] += __ldg(bias + n + k);
+    }
+    const long long vox = ((static_cast<long long>(b) * g.out_d + rd) * g.out_h + rh) * g.out_w + rw;
+    long long res_base = 0;
+    if (g.res != nullptr) {
+      const int qd = g.res_up ? rd >> 1 : rd, qh = g.res_up ? rh >> 1 : rh, qw = g.res_up ? rw >> 1 : rw;
+      res_base = (((static_cast<long long>(b) * g.res_d + qd) * g.res_h + qh) * g.res_w + qw) * g.res_cstride;
+    }
+    ConvGeom g4 = g;
+    g4.cout = n + cnt;  // store_row16 writes min(16, cout - n) columns
+    store_row16(g4, v, n, vox * g.out_cstride + g.out_coff + n, res_base + n);
   }
 }
 
@@ -398,14 +378,22 @@ cudaError_t launch_conv3d_umma(const ConvMaps& maps, const ConvGeom& g, int kc, 
   const int n_tiles = (g.cout + g.bn - 1) / g.bn;
   const long long m_tiles = static_cast<long long>(g.tiles_w) * g.tiles_h * g.tiles_d * g.batch * g.phases;
   if (m_tiles <= 0 || m_tiles > 0x7FFFFFFFLL || n_tiles <= 0 || n_tiles > 65535) return cudaErrorInvalidValue;
-  const dim3 grid(static_cast<unsigned>(m_tiles), static_cast<unsigned>(n_tiles));
-  if (kc == 64) return exact ? launch_typed<64, true>(maps, g, grid, smem, stream)
-                             : launch_typed<64, false>(maps, g, grid, smem, stream);
-  if (kc == 32) return exact ? launch_typed<32, true>(maps, g, grid, smem, stream)
-                             : launch_typed<32, false>(maps, g, grid, smem, stream);
-  if (kc == 16) return exact ? launch_typed<16, true>(maps, g, grid, smem, stream)
-                             : launch_typed<16, false>(maps, g, grid, smem, stream);
-  return cudaErrorInvalidValue;
+  if (g.ksplit < 1 || g.ksplit > 65535 || (g.ksplit > 1 && (g.partial == nullptr || g.mode == kModeUp2)))
+    return cudaErrorInvalidValue;
+  const dim3 grid(static_cast<unsigned>(m_tiles), static_cast<unsigned>(n_tiles), static_cast<unsigned>(g.ksplit));
+  cudaError_t e = cudaErrorInvalidValue;
+  if (kc == 64) e = exact ? launch_typed<64, true>(maps, g, grid, smem, stream)
+                          : launch_typed<64, false>(maps, g, grid, smem, stream);
+  else if (kc == 32) e = exact ? launch_typed<32, true>(maps, g, grid, smem, stream)
+                               : launch_typed<32, false>(maps, g, grid, smem, stream);
+  else if (kc == 16) e = exact ? launch_typed<16, true>(maps, g, grid, smem, stream)
+                               : launch_typed<16, false>(maps, g, grid, smem, stream);
+  if (e != cudaSuccess || g.ksplit == 1) return e;
+  const long long total = static_cast<long long>(g.batch) * g.row_d * g.row_h * g.row_w * ((g.cout + 3) / 4);
+  long long blocks = (total + 255) / 256;
+  if (blocks > 148LL * 16) blocks = 148LL * 16;
+  splitk_reduce_kernel<<<static_cast<unsigned>(blocks), 256, 0, stream>>>(g);
+  return cudaGetLastError();
 }
 
 }  // namespace ctmr

@@ -38,6 +38,11 @@ struct ConvGeom {
   uint32_t tmem_cols;
   int chunk_iters;              // EXACT: K iterations per promoted accumulator chunk
   int operand_bf16;             // single-plane modes: 1 bf16 operands, 0 fp16 operands
+  int n_tiles;                  // persistent kernel: N tiles per M tile
+  int total_tiles;              // persistent kernel: all (M tile, N tile) pairs
+  int ksplit;                   // per-tap kernel: K iterations split over grid.z (fp32 partial planes)
+  float* partial;               // [ksplit][batch][row_d][row_h][row_w][part_cstride] when ksplit > 1
+  int part_cstride;
   // epilogue
   const float* bias;            // may be null
   int bias_bstride;             // 0 (per channel) or cout (per batch item)

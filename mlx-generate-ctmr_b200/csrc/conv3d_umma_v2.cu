@@ -1,0 +1,290 @@
+// Persistent implicit-GEMM conv3d for the 16-bit operand modes that reuses
+// each input box across the taps along w.
+//
+// The M tile is 8 (h) x 16 (w) output voxels of one depth, ordered so that each
+// 8-row core group of the K-major swizzled operand (one swizzle atom: 8 rows x
+// KC channels) is one w position holding 8 consecutive h. A tap shift along w
+// is then a whole-atom shift of the operand start address, so one TMA box of
+// (16 + TW - 1) atoms — the input rows for all TW taps along w — feeds TW MMAs
+// through descriptor offsets. The TMA view of the activations puts H before W
+// (dims C, H, W, D, B) so the box lands in exactly this atom order, and
+// out-of-range coordinates are zero-filled (the convolution's padding).
+//
+// Each CTA owns MT M tiles at consecutive depths that share every weight box,
+// and walks its tiles persistently: the accumulator (MT x bn fp32 columns) is
+// double-buffered in TMEM so the epilogue warps drain tile i while the MMA
+// issuer accumulates tile i + 1.
+//
+// Modes: kModeConv3 (TW = 3; stages over (kd, kh)) and kModeUp2 (TW = 2; stages
+// over the (td, th) of each nearest-2x parity, whose taps are the folded
+// weights of pack_weight(upsample=1)).
+#include <cuda_bf16.h>
+#include <cuda_fp16.h>
+
+#include "conv3d_umma.cuh"
+#include "epilogue.cuh"
+#include "ptx.cuh"
+
+namespace ctmr {
+namespace {
+
+constexpr int kThreadsV2 = 192;
+
+__host__ __device__ constexpr uint32_t ru(uint32_t v, uint32_t a) { return (v + a - 1) / a * a; }
+
+struct V2Layout {
+  uint32_t atom_bytes, a_m_bytes, a_bytes, b_tap_bytes, b_bytes, stage_bytes;
+  __host__ __device__ V2Layout(int kc, int mt, int tw, int bn) {
+    atom_bytes = 8u * static_cast<uint32_t>(kc) * 2u;
+    a_m_bytes = static_cast<uint32_t>(16 + tw - 1) * atom_bytes;
+    a_bytes = ru(static_cast<uint32_t>(mt) * a_m_bytes, 1024);
+    b_tap_bytes = static_cast<uint32_t>(bn) * kc * 2u;
+    b_bytes = ru(static_cast<uint32_t>(tw) * b_tap_bytes, 1024);
+    stage_bytes = a_bytes + b_bytes;
+  }
+};
+
+template <int KC, int MT, int TW>
+__global__ void __launch_bounds__(kThreadsV2, 1)
+    conv3d_umma_v2_kernel(const __grid_constant__ ConvMaps maps, const __grid_constant__ ConvGeom g) {
+  constexpr uint32_t kRowBytes = KC * 2;
+  constexpr int kSteps = KC / 16;
+  constexpr int KDH = TW == 3 ? 9 : 4;  // (kd, kh) or (td, th) pairs per tile
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>(ru(smem_u32(smem_raw), 1024) - smem_u32(smem_raw) +
+                                             reinterpret_cast<uintptr_t>(smem_raw));
+  const V2Layout L(KC, MT, TW, g.bn);
+  const int S = g.stages;
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + static_cast<size_t>(S) * L.stage_bytes);
+  uint64_t* empty = full + S;
+  uint64_t* tmem_full = empty + S;      // [2]
+  uint64_t* tmem_empty = tmem_full + 2;  // [2]
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(tmem_empty + 2);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const int stages_per_tile = KDH * g.kblocks;
+  const uint32_t bn = static_cast<uint32_t>(g.bn);
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < S; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&tmem_full[i], 1);
+      mbar_init(&tmem_empty[i], 128);
+    }
+    *abort_flag = 0;
+    fence_barrier_init();
+  }
+  if (warp == 1) {
+    tmem_alloc(tmem_slot, g.tmem_cols);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+
+  // Tile t -> (n tile fastest, then w, h, d, batch item, parity phase).
+  auto decode = [&](int t, int& n0, int& w0, int& h0, int& d0, int& b, int& phase) {
+    const int nt = t % g.n_tiles; t /= g.n_tiles;
+    const int tw_i = t % g.tiles_w; t /= g.tiles_w;
+    const int th_i = t % g.tiles_h; t /= g.tiles_h;
+    const int td_i = t % g.tiles_d; t /= g.tiles_d;
+    b = t % g.batch;
+    phase = t / g.batch;
+    n0 = nt * g.bn;
+    w0 = tw_i * 16;
+    h0 = th_i * 8;
+    d0 = td_i * MT;
+  };
+
+  if (warp == 0 && lane == 0) {
+    // ------------------------------------------------------------ TMA producer
+    tma_prefetch_desc(&maps.a[0]);
+    tma_prefetch_desc(&maps.b);
+    int it = 0;
+    int issued = 0;
+    for (int t = blockIdx.x; t < g.total_tiles && !*abort_flag; t += gridDim.x) {
+      int n0, w0, h0, d0, b, phase;
+      decode(t, n0, w0, h0, d0, b, phase);
+      const int pd = phase >> 2, ph = (phase >> 1) & 1, pw = phase & 1;
+      for (int st = 0; st < stages_per_tile; ++st, ++it) {
+        const int s = it % S;
+        const uint32_t round = static_cast<uint32_t>(it / S);
+        if (it >= S && !mbar_wait_bounded(&empty[s], (round - 1) & 1u, kErrWaitEmpty)) {
+          *abort_flag = 1;
+          break;
+        }
+        const int kdh = st / g.kblocks;
+        const int c = (st - kdh * g.kblocks) * KC;
+        int y, x, z, btap;
+        if (TW == 3) {
+          const int kd = kdh / 3, kh = kdh % 3;
+          z = d0 + kd - 1;
+          y = h0 + kh - 1;
+          x = w0 - 1;
+          btap = kd * 9 + kh * 3;
+        } else {
+          const int td = kdh >> 1, th = kdh & 1;
+          z = d0 + pd + td - 1;
+          y = h0 + ph + th - 1;
+          x = w0 + pw - 1;
+          btap = phase * 8 + td * 4 + th * 2;
+        }
+        uint8_t* st_base = smem + static_cast<size_t>(s) * L.stage_bytes;
+        mbar_arrive_expect_tx(&full[s], static_cast<uint32_t>(MT) * L.a_m_bytes + static_cast<uint32_t>(TW) *
+                                                                                    L.b_tap_bytes);
+        tma_load_5d(st_base, &maps.a[0], &full[s], c, y, x, z, b);
+        tma_load_3d(st_base + L.a_bytes, &maps.b, &full[s], c, n0, btap);
+        ++issued;
+      }
+    }
+    for (int k = max(0, issued - S); k < issued; ++k) {
+      if (!mbar_wait_bounded(&full[k % S], static_cast<uint32_t>(k / S) & 1u, kErrWaitDrain)) break;
+    }
+  } else if (warp == 1 && lane == 0) {
+    // ------------------------------------------------------------ MMA issuer
+    const uint32_t idesc = idesc_f16(g.operand_bf16 != 0, 128, bn);
+    int it = 0;
+    int lt = 0;
+    for (int t = blockIdx.x; t < g.total_tiles && !*abort_flag; t += gridDim.x, ++lt) {
+      const int buf = lt & 1;
+      if (lt >= 2 &&
+          !mbar_wait_bounded(&tmem_empty[buf], static_cast<uint32_t>((lt >> 1) - 1) & 1u, kErrWaitAcc)) {
+        *abort_flag = 1;
+        break;
+      }
+      tc_fence_after();
+      const uint32_t acc0 = tmem + static_cast<uint32_t>(buf * MT) * bn;
+      for (int st = 0; st < stages_per_tile; ++st, ++it) {
+        const int s = it % S;
+        if (!mbar_wait_bounded(&full[s], static_cast<uint32_t>(it / S) & 1u, kErrWaitFull)) {
+          *abort_flag = 1;
+          break;
+        }
+        tc_fence_after();
+        const uint32_t a_base = smem_u32(smem + static_cast<size_t>(s) * L.stage_bytes);
+        const uint32_t b_base = a_base + L.a_bytes;
+#pragma unroll
+        for (int m = 0; m < MT; ++m) {
+#pragma unroll
+          for (int kw = 0; kw < TW; ++kw) {
+#pragma unroll
+            for (int k = 0; k < kSteps; ++k) {
+              const uint32_t a_addr = a_base + static_cast<uint32_t>(m) * L.a_m_bytes +
+                                      static_cast<uint32_t>(kw) * L.atom_bytes + static_cast<uint32_t>(k) * 32u;
+              const uint32_t b_addr = b_base + static_cast<uint32_t>(kw) * L.b_tap_bytes + static_cast<uint32_t>(k) * 32u;
+              umma_f16(acc0 + static_cast<uint32_t>(m) * bn, smem_desc_kmajor(a_addr, kRowBytes),
+                       smem_desc_kmajor(b_addr, kRowBytes), idesc, (st == 0 && kw == 0 && k == 0) ? 0u : 1u);
+            }
+          }
+        }
+        umma_commit(&empty[s]);
+      }
+      umma_commit(&tmem_full[buf]);
+    }
+  } else if (warp >= 2) {
+    // ------------------------------------------------------------ epilogue
+    const int quarter = warp & 3;
+    const int row = quarter * 32 + lane;
+    const int aw = row >> 3, ih = row & 7;  // atom (w offset), row in atom (h offset)
+    const uint32_t lane_addr = tmem + (static_cast<uint32_t>(quarter * 32) << 16);
+    int lt = 0;
+    for (int t = blockIdx.x; t < g.total_tiles && !*abort_flag; t += gridDim.x, ++lt) {
+      const int buf = lt & 1;
+      if (!mbar_wait_bounded(&tmem_full[buf], static_cast<uint32_t>(lt >> 1) & 1u, kErrWaitAcc)) {
+        *abort_flag = 1;
+        break;
+      }
+      tc_fence_after();
+      int n0, w0, h0, d0, b, phase;
+      decode(t, n0, w0, h0, d0, b, phase);
+      const float* bias = g.bias != nullptr ? g.bias + static_cast<long long>(b) * g.bias_bstride : nullptr;
+#pragma unroll 1
+      for (int m = 0; m < MT; ++m) {
+        const int rd = d0 + m, rh = h0 + ih, rw = w0 + aw;
+        const bool valid = rw < g.row_w && rh < g.row_h && rd < g.row_d;
+        int od = rd, oh = rh, ow = rw;
+        if (TW == 2) {
+          od = 2 * rd + (phase >> 2);
+          oh = 2 * rh + ((phase >> 1) & 1);
+          ow = 2 * rw + (phase & 1);
+        }
+        const long long vox = ((static_cast<long long>(b) * g.out_d + od) * g.out_h + oh) * g.out_w + ow;
+        const long long out_base = vox * g.out_cstride + g.out_coff;
+        long long res_base = 0;
+        if (g.res != nullptr) {
+          const int qd = g.res_up ? od >> 1 : od, qh = g.res_up ? oh >> 1 : oh, qw = g.res_up ? ow >> 1 : ow;
+          res_base =
+              (((static_cast<long long>(b) * g.res_d + qd) * g.res_h + qh) * g.res_w + qw) * g.res_cstride;
+        }
+        const uint32_t acc = lane_addr + static_cast<uint32_t>(buf * MT + m) * bn;
+#pragma unroll 1
+        for (int c = 0; c < g.bn; c += 16) {
+          float v[16];
+          tmem_ld16(acc + static_cast<uint32_t>(c), v);
+          const int n = n0 + c;
+          if (valid && n < g.cout) {
+            if (bias != nullptr) {
+              const int cnt = min(16, g.cout - n);
+              for (int i = 0; i < cnt; ++i) v[i] += __ldg(bias + n + i);
+            }
+            store_row16(g, v, n, out_base + n, res_base + n);
+          }
+        }
+      }
+      tc_fence_before();
+      mbar_arrive(&tmem_empty[buf]);
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem, g.tmem_cols);
+  }
+}
+
+template <int KC, int MT, int TW>
+cudaError_t launch_v2_typed(const ConvMaps& maps, const ConvGeom& g, int grid, size_t smem, cudaStream_t stream) {
+  auto kern = conv3d_umma_v2_kernel<KC, MT, TW>;
+  cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
+  if (e != cudaSuccess) return e;
+  kern<<<grid, kThreadsV2, smem, stream>>>(maps, g);
+  return cudaGetLastError();
+}
+
+}  // namespace
+
+// Shared-memory plan of the v2 kernel: the deepest pipeline (<= 6 stages) that
+// fits one CTA per SM; 0 when fewer than 2 stages fit.
+int conv_v2_stage_plan(int kc, int mt, int tw, int bn, size_t* smem_bytes) {
+  const V2Layout L(kc, mt, tw, bn);
+  const size_t extra = 1024 + 256;
+  int stages = static_cast<int>((227 * 1024 - extra) / L.stage_bytes);
+  if (stages > 6) stages = 6;
+  if (stages < 2) return 0;
+  *smem_bytes = static_cast<size_t>(stages) * L.stage_bytes + extra;
+  return stages;
+}
+
+cudaError_t launch_conv3d_umma_v2(const ConvMaps& maps, const ConvGeom& g, int kc, int mt, int tw, int sms,
+                                  size_t smem, cudaStream_t stream) {
+  if (g.total_tiles <= 0) return cudaErrorInvalidValue;
+  const int grid = g.total_tiles < sms ? g.total_tiles : sms;
+#define CTMR_V2(KC_, MT_, TW_) \
+  if (kc == KC_ && mt == MT_ && tw == TW_) return launch_v2_typed<KC_, MT_, TW_>(maps, g, grid, smem, stream);
+  CTMR_V2(64, 2, 3) CTMR_V2(32, 2, 3) CTMR_V2(16, 2, 3)
+  CTMR_V2(64, 1, 3) CTMR_V2(32, 1, 3) CTMR_V2(16, 1, 3)
+  CTMR_V2(64, 2, 2) CTMR_V2(32, 2, 2) CTMR_V2(16, 2, 2)
+  CTMR_V2(64, 1, 2) CTMR_V2(32, 1, 2) CTMR_V2(16, 1, 2)
+#undef CTMR_V2
+  return cudaErrorInvalidValue;
+}
+
+}  // namespace ctmr

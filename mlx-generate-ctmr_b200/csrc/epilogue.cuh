@@ -1,0 +1,87 @@
+// Epilogue helpers shared by the implicit-GEMM kernels: residual add and the
+// store of 16 output columns of one voxel row (vectorised when aligned).
+#pragma once
+
+#include <cuda_bf16.h>
+#include <cstdint>
+
+#include "conv3d_umma.cuh"
+
+namespace ctmr {
+
+__device__ __forceinline__ float bf16_to_f32(uint16_t v) { return __uint_as_float(static_cast<uint32_t>(v) << 16); }
+
+__device__ __forceinline__ uint32_t pack_bf16x2(float a, float b) {
+  __nv_bfloat162 h = __floats2bfloat162_rn(a, b);
+  return *reinterpret_cast<uint32_t*>(&h);
+}
+
+// Add the residual and store 16 output columns [n, n+16) of one voxel row.
+__device__ __forceinline__ void store_row16(const ConvGeom& g, float (&v)[16], int n, long long out_off,
+                                            long long res_off) {
+  const int cnt = min(16, g.cout - n);
+  if (cnt <= 0) return;
+  if (g.res != nullptr) {
+    if (g.res_bf16) {
+      const uint16_t* r = static_cast<const uint16_t*>(g.res) + res_off;
+      if (cnt == 16 && (reinterpret_cast<uintptr_t>(r) & 15) == 0) {
+        const uint4 q0 = __ldg(reinterpret_cast<const uint4*>(r));
+        const uint4 q1 = __ldg(reinterpret_cast<const uint4*>(r) + 1);
+        const uint32_t w[8] = {q0.x, q0.y, q0.z, q0.w, q1.x, q1.y, q1.z, q1.w};
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+          v[2 * i] += bf16_to_f32(static_cast<uint16_t>(w[i] & 0xFFFFu));
+          v[2 * i + 1] += bf16_to_f32(static_cast<uint16_t>(w[i] >> 16));
+        }
+      } else {
+        for (int i = 0; i < cnt; ++i) v[i] += bf16_to_f32(r[i]);
+      }
+    } else {
+      const float* r = static_cast<const float*>(g.res) + res_off;
+      if (cnt == 16 && (reinterpret_cast<uintptr_t>(r) & 15) == 0) {
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+          const float4 q = __ldg(reinterpret_cast<const float4*>(r) + i);
+          v[4 * i] += q.x;
+          v[4 * i + 1] += q.y;
+          v[4 * i + 2] += q.z;
+          v[4 * i + 3] += q.w;
+        }
+      } else {
+        for (int i = 0; i < cnt; ++i) v[i] += __ldg(r + i);
+      }
+    }
+  }
+  if (g.out_bf16) {
+    uint16_t* o = static_cast<uint16_t*>(g.out) + out_off;
+    if (cnt == 16 && (reinterpret_cast<uintptr_t>(o) & 15) == 0) {
+      uint4 q0, q1;
+      q0.x = pack_bf16x2(v[0], v[1]);
+      q0.y = pack_bf16x2(v[2], v[3]);
+      q0.z = pack_bf16x2(v[4], v[5]);
+      q0.w = pack_bf16x2(v[6], v[7]);
+      q1.x = pack_bf16x2(v[8], v[9]);
+      q1.y = pack_bf16x2(v[10], v[11]);
+      q1.z = pack_bf16x2(v[12], v[13]);
+      q1.w = pack_bf16x2(v[14], v[15]);
+      reinterpret_cast<uint4*>(o)[0] = q0;
+      reinterpret_cast<uint4*>(o)[1] = q1;
+    } else {
+      for (int i = 0; i < cnt; ++i) {
+        __nv_bfloat16 h = __float2bfloat16_rn(v[i]);
+        o[i] = *reinterpret_cast<uint16_t*>(&h);
+      }
+    }
+  } else {
+    float* o = static_cast<float*>(g.out) + out_off;
+    if (cnt == 16 && (reinterpret_cast<uintptr_t>(o) & 15) == 0) {
+#pragma unroll
+      for (int i = 0; i < 4; ++i)
+        reinterpret_cast<float4*>(o)[i] = make_float4(v[4 * i], v[4 * i + 1], v[4 * i + 2], v[4 * i + 3]);
+    } else {
+      for (int i = 0; i < cnt; ++i) o[i] = v[i];
+    }
+  }
+}
+
+}  // namespace ctmr

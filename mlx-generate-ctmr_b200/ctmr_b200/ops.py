@@ -231,7 +231,7 @@ def conv3d(
         if tuple(residual.shape) != expect:
             raise ValueError(f"residual shape {tuple(residual.shape)} != output {expect}")
     if out is None:
-        dtype = out_dtype or (F32 if packed.precision == "fp32" else BF16)
+        dtype = out_dtype or F32
         out = empty_ndhwc(b, o, od, oh, ow, dtype, x.device)
     elif tuple(out.shape) != (b, o, od, oh, ow):
         raise ValueError(f"out shape {tuple(out.shape)} != {(b, o, od, oh, ow)}")

@@ -47,10 +47,15 @@ def _status(desc) -> int:
 
 
 def test_workspace_size_reports_prepared_operand():
-    # fp32 split mode: hi + lo fp16 planes of B * D * H * W * round16(C) elements.
-    assert _lib.LIB.ctmr_conv3d_workspace_size(ctypes.byref(_desc())) == 2 * 64 * 32 * 2
+    # fp32 split mode on a grid large enough to fill the GPU: hi + lo fp16 planes of
+    # B * D * H * W * round16(C) elements, nothing else.
+    big = _desc(depth=64, height=64, width=64)
+    assert _lib.LIB.ctmr_conv3d_workspace_size(ctypes.byref(big)) == 2 * 64 ** 3 * 32 * 2
     # trilinear input doubles every axis before the conv
-    assert _lib.LIB.ctmr_conv3d_workspace_size(ctypes.byref(_desc(trilinear=1))) == 2 * 512 * 32 * 2
+    assert _lib.LIB.ctmr_conv3d_workspace_size(ctypes.byref(_desc(depth=32, height=32, width=32, trilinear=1))) == (
+        2 * 64 ** 3 * 32 * 2)
+    # a tiny grid splits K across CTAs: the fp32 partial planes come on top of the operand
+    assert _lib.LIB.ctmr_conv3d_workspace_size(ctypes.byref(_desc())) > 2 * 64 * 32 * 2
 
 
 @pytest.mark.parametrize(("overrides", "status"), [

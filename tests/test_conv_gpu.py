@@ -136,3 +136,57 @@ def test_no_device_wait_timed_out(cuda):
     from ctmr_b200 import _lib
 
     assert _lib.device_error(clear=True) == 0
+
+
+V2_SHAPES = [
+    ((2, 64, 3, 12, 24), 64, False),   # partial w, h and depth-pair tiles
+    ((1, 32, 5, 16, 32), 48, False),   # 32-channel blocks, N = 48
+    ((1, 128, 4, 8, 16), 256, False),  # two N tiles
+    ((2, 64, 3, 8, 16), 32, True),     # nearest-2x fold (two taps along w per parity)
+    ((1, 16, 2, 8, 16), 16, False),    # 16-channel blocks
+]
+
+
+@pytest.mark.parametrize("precision", ["fp16", "bf16"])
+@pytest.mark.parametrize(("shape", "out_channels", "upsample"), V2_SHAPES)
+def test_persistent_kernel_shapes(cuda, shape, out_channels, upsample, precision):
+    """16-bit stride-1 convs on grids with W >= 16 and H >= 8 run the persistent
+    atom-shifted kernel; bias per batch item and a residual exercise its epilogue."""
+    from ctmr_b200 import ops
+
+    rng = np.random.default_rng(13)
+    x = torch.from_numpy(rng.standard_normal(shape).astype(np.float32))
+    w = torch.from_numpy((rng.standard_normal((out_channels, shape[1], 3, 3, 3)) / np.sqrt(27 * shape[1]))
+                         .astype(np.float32))
+    bias = torch.from_numpy(rng.standard_normal((shape[0], out_channels)).astype(np.float32))
+    scale = 2 if upsample else 1
+    out_sp = tuple(scale * n for n in shape[2:])
+    res = torch.from_numpy(rng.standard_normal((shape[0], out_channels, *out_sp)).astype(np.float32))
+    packed = ops.pack_weight(w.to(cuda), precision, upsample=upsample)
+    y = ops.conv3d(ops.to_ndhwc(x.to(cuda)), packed, bias.to(cuda), residual=ops.to_ndhwc(res.to(cuda)))
+    torch.cuda.synchronize()
+    xin = ops_ref.upsample_nearest_ref(x.double()) if upsample else x.double()
+    expected = ops_ref.conv3d_ref(xin, w.double(), bias.double()) + res.double()
+    err = ops_ref.rel_l2(y.cpu(), expected)
+    assert err <= (FP16_CONV_REL_L2 if precision == "fp16" else BF16_CONV_REL_L2), f"{precision} rel-L2 {err:.3e}"
+
+
+@pytest.mark.parametrize("precision", ["fp32", "fp16"])
+def test_splitk_reduction_epilogue(cuda, precision):
+    """A deep, small grid (2 x 256 x 4^3) splits K across CTAs; the reduction adds the
+    per-batch bias and the residual before the single rounding."""
+    from ctmr_b200 import ops
+
+    rng = np.random.default_rng(17)
+    x = torch.from_numpy(rng.standard_normal((2, 256, 4, 4, 4)).astype(np.float32))
+    w = torch.from_numpy((rng.standard_normal((256, 256, 3, 3, 3)) / np.sqrt(27 * 256)).astype(np.float32))
+    bias = torch.from_numpy(rng.standard_normal((2, 256)).astype(np.float32))
+    res = torch.from_numpy(rng.standard_normal((2, 256, 4, 4, 4)).astype(np.float32))
+    y = ops.conv3d(ops.to_ndhwc(x.to(cuda)), ops.pack_weight(w.to(cuda), precision), bias.to(cuda),
+                   residual=ops.to_ndhwc(res.to(cuda)))
+    torch.cuda.synchronize()
+    expected = ops_ref.conv3d_ref(x.double(), w.double(), bias.double()) + res.double()
+    if precision == "fp32":
+        _close_fp32(y, expected)
+    else:
+        assert ops_ref.rel_l2(y.cpu(), expected) <= FP16_CONV_REL_L2
