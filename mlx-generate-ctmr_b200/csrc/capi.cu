@@ -16,6 +16,7 @@
 #include "ctmr_b200.h"
 #include "conv3d_umma.cuh"
 #include "groupnorm.cuh"
+#include "conv3d_narrow.cuh"
 #include "misc.cuh"
 #include "pack.cuh"
 #include "prepare.cuh"
@@ -163,7 +164,7 @@ struct ConvPlan {
   int in_d, in_h, in_w;     // grid the taps read (after trilinear / avgpool)
   int row_d, row_h, row_w;  // GEMM rows
   int out_d, out_h, out_w;
-  bool exact, prepare, bf16;
+  bool exact, prepare, bf16, narrow;
   size_t prep_bytes;        // per plane
   // per-tap kernel tiling and its split-K
   int tile_w, tile_h, tile_d, tiles_w, tiles_h, tiles_d, n_tiles, ksplit;
@@ -241,7 +242,13 @@ int plan_conv(const ctmr_conv3d_desc* d, ConvPlan* p) {
   const bool direct = p->bf16 && d->x2.data == nullptr && d->affine == nullptr && !d->silu && !d->trilinear &&
                       !d->avgpool && d->x.dtype == CTMR_DTYPE_BF16 && d->x.channels % 16 == 0 &&
                       d->x.cstride % 8 == 0 && aligned16(d->x.data);
-  p->prepare = !direct;
+  // Narrow outputs (<= 4 channels, e.g. the UNet / VAE output convolutions) with split-fp32
+  // weights and an fp32 input run the direct fp32 kernel, which normalises while staging.
+  p->narrow = p->exact && p->mode == ctmr::kModeConv3 && !d->trilinear && !d->avgpool && d->out_channels <= 4 &&
+              d->x2.data == nullptr &&
+              d->x.dtype == CTMR_DTYPE_F32 && (d->residual.data == nullptr || d->residual.dtype == CTMR_DTYPE_F32) &&
+              d->y_dtype == CTMR_DTYPE_F32 && getenv("CTMR_DISABLE_NARROW") == nullptr;
+  p->prepare = !direct && !p->narrow;
   p->prep_bytes = p->prepare ? static_cast<size_t>(round_up(static_cast<long long>(d->batch) * p->in_d * p->in_h *
                                                                 p->in_w * p->cpad * 2,
                                                             256))
@@ -273,6 +280,7 @@ int plan_conv(const ctmr_conv3d_desc* d, ConvPlan* p) {
                                       p->n_tiles * p->bn * sizeof(float)
                                 : 0;
   p->part_bytes = static_cast<size_t>(round_up(static_cast<long long>(p->part_bytes), 256));
+  if (p->narrow) p->part_bytes = 0;
   return CTMR_OK;
 }
 
@@ -343,6 +351,29 @@ int ctmr_conv3d_stages(const ctmr_conv3d_desc* d, void* workspace, size_t worksp
   const size_t need = p.workspace();
   if (need > workspace_bytes || (need > 0 && workspace == nullptr))
     return fail(CTMR_ERR_WORKSPACE, "conv3d needs %zu workspace bytes, got %zu", need, workspace_bytes);
+
+  if (p.narrow) {
+    if (!(stages & CTMR_CONV_GEMM)) return CTMR_OK;
+    ctmr::NarrowParams np{};
+    np.x = d->x.data;
+    np.x_cstride = d->x.cstride;
+    np.batch = d->batch, np.d = d->depth, np.h = d->height, np.w = d->width;
+    np.cin = p.cin, np.cout = d->out_channels;
+    np.affine = d->affine;
+    np.silu = d->silu;
+    np.w_hi = static_cast<const __half*>(d->weight);
+    np.w_lo = static_cast<const __half*>(d->weight_lo);
+    np.opad = p.opad, np.cpad = p.cpad;
+    np.bias = d->bias;
+    np.bias_bstride = d->bias_per_batch ? d->out_channels : 0;
+    np.res = static_cast<const float*>(d->residual.data);
+    np.res_cstride = d->residual.cstride;
+    np.res_up = d->residual_upsampled;
+    np.y = static_cast<float*>(d->y) + d->y_coffset;
+    np.y_cstride = d->y_cstride;
+    cudaError_t e = ctmr::launch_narrow_conv(np, stream);
+    return e == cudaSuccess ? CTMR_OK : cuda_fail(e, "narrow conv launch");
+  }
 
   // 1. Operand preparation (affine, SiLU, trilinear / avgpool, concat, cast or split).
   const void* a_hi = d->x.data;

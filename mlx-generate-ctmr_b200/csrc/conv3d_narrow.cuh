@@ -1,0 +1,29 @@
+// Parameters of the narrow-output direct convolution (see conv3d_narrow.cu).
+#pragma once
+
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+
+namespace ctmr {
+
+struct NarrowParams {
+  const void* x;            // fp32 NDHWC input, x_cstride elements per voxel row
+  long long x_cstride;
+  int batch, d, h, w, cin, cout;
+  const float* affine;      // (B, C, 2) scale/offset or null
+  int silu;
+  const __half* w_hi;       // split-fp32 packed weights [27][opad][cpad]
+  const __half* w_lo;
+  int opad, cpad;
+  const float* bias;        // (cout) or (B, cout) or null
+  int bias_bstride;
+  const float* res;         // fp32 residual NDHWC or null
+  long long res_cstride;
+  int res_up;               // residual on the half-resolution grid (nearest 2x upsampled by index)
+  float* y;                 // fp32 NDHWC output
+  long long y_cstride;
+};
+
+cudaError_t launch_narrow_conv(const NarrowParams& p, cudaStream_t stream);
+
+}  // namespace ctmr

@@ -190,3 +190,64 @@ def test_splitk_reduction_epilogue(cuda, precision):
         _close_fp32(y, expected)
     else:
         assert ops_ref.rel_l2(y.cpu(), expected) <= FP16_CONV_REL_L2
+
+
+@pytest.mark.parametrize(("shape", "out_channels", "silu"), [
+    ((2, 64, 5, 12, 40), 4, True),   # UNet out.2 shape class, partial blocks on every axis
+    ((1, 64, 8, 16, 16), 1, False),  # VAE decoder output conv
+    ((1, 24, 3, 9, 7), 3, True),     # channels not a multiple of the 8-channel staging slice
+])
+def test_narrow_output_conv(cuda, shape, out_channels, silu):
+    """<= 4 output channels run the direct fp32 kernel (GN affine + SiLU applied while staging);
+    held to the reference's fp32 bar."""
+    from ctmr_b200 import ops
+
+    rng = np.random.default_rng(19)
+    b, c = shape[:2]
+    x = torch.from_numpy((2 * rng.standard_normal(shape) + 0.5).astype(np.float32))
+    w = torch.from_numpy((rng.standard_normal((out_channels, c, 3, 3, 3)) / np.sqrt(27 * c)).astype(np.float32))
+    bias = torch.from_numpy(rng.standard_normal((b, out_channels)).astype(np.float32))
+    res = torch.from_numpy(rng.standard_normal((b, out_channels, *shape[2:])).astype(np.float32))
+    norm_w = torch.from_numpy((1 + 0.1 * rng.standard_normal(c)).astype(np.float32))
+    norm_b = torch.from_numpy((0.1 * rng.standard_normal(c)).astype(np.float32))
+    groups = 8
+    xg = ops.to_ndhwc(x.to(cuda))
+    affine = ops.group_norm_affine(xg, norm_w.to(cuda), norm_b.to(cuda), groups=groups, eps=1e-6)
+    y = ops.conv3d(xg, ops.pack_weight(w.to(cuda), "fp32"), bias.to(cuda), affine=affine, silu=silu,
+                   residual=ops.to_ndhwc(res.to(cuda)))
+    torch.cuda.synchronize()
+    prepared = ops_ref.group_norm_ref(x.double(), norm_w.double(), norm_b.double(), groups, 1e-6)
+    if silu:
+        prepared = ops_ref.silu_ref(prepared)
+    expected = ops_ref.conv3d_ref(prepared, w.double(), bias.double()) + res.double()
+    _close_fp32(y, expected)
+
+
+@pytest.mark.parametrize("mode", ["trilinear", "avgpool"])
+def test_narrow_output_with_resampled_input(cuda, mode):
+    """A <= 4-channel conv of a trilinear-upsampled or pooled input still prepares the operand."""
+    from ctmr_b200 import ops
+
+    rng = np.random.default_rng(23)
+    x = torch.from_numpy(rng.standard_normal((1, 8, 4, 6, 8)).astype(np.float32))
+    w = torch.from_numpy((rng.standard_normal((4, 8, 3, 3, 3)) / np.sqrt(27 * 8)).astype(np.float32))
+    xg = ops.to_ndhwc(x.to(cuda))
+    y = ops.conv3d(xg, ops.pack_weight(w.to(cuda), "fp32"), None, **{mode: True})
+    torch.cuda.synchronize()
+    xin = ops_ref.upsample_trilinear_ref(x.double()) if mode == "trilinear" else ops_ref.avg_pool_ref(x.double())
+    _close_fp32(y, ops_ref.conv3d_ref(xin, w.double()))
+
+
+def test_narrow_output_with_half_grid_residual(cuda):
+    """The UNet up-block conv2 adds its skip from the half-resolution grid (nearest 2x by index)."""
+    from ctmr_b200 import ops
+
+    rng = np.random.default_rng(29)
+    x = torch.from_numpy(rng.standard_normal((2, 8, 4, 6, 8)).astype(np.float32))
+    w = torch.from_numpy((rng.standard_normal((4, 8, 3, 3, 3)) / np.sqrt(27 * 8)).astype(np.float32))
+    res = torch.from_numpy(rng.standard_normal((2, 4, 2, 3, 4)).astype(np.float32))
+    y = ops.conv3d(ops.to_ndhwc(x.to(cuda)), ops.pack_weight(w.to(cuda), "fp32"), None,
+                   residual=ops.to_ndhwc(res.to(cuda)), residual_upsampled=True)
+    torch.cuda.synchronize()
+    expected = ops_ref.conv3d_ref(x.double(), w.double()) + ops_ref.upsample_nearest_ref(res.double())
+    _close_fp32(y, expected)
