@@ -126,6 +126,22 @@ def conv_precision(weight: torch.Tensor) -> str:
     return precision
 
 
+_dense: dict[tuple[int, torch.dtype], tuple[weakref.ref, torch.Tensor]] = {}
+
+
+def _dense_weight(weight: torch.Tensor, dtype: torch.dtype) -> torch.Tensor:
+    """``weight`` in ``dtype``, cast once and cached like the packed conv weights."""
+    if weight.dtype == dtype:
+        return weight
+    key = (id(weight), dtype)
+    hit = _dense.get(key)
+    if hit is not None and hit[0]() is weight:
+        return hit[1]
+    cast = weight.detach().to(dtype)
+    _dense[key] = (weakref.ref(weight, lambda _: _dense.pop(key, None)), cast)
+    return cast
+
+
 def dense_dtype() -> torch.dtype:
     """Operand type of the dense (non-conv) tensor-core ops: fp32, or the 16-bit mode's type."""
     return {"fp32": torch.float32, "bf16": torch.bfloat16, "fp16": torch.float16}[_precision.get()]
@@ -147,6 +163,8 @@ def drop_packed_weights(weights: Iterable[torch.Tensor]) -> None:
     ids = {id(w) for w in weights}
     for key in [k for k in _packed if k[0] in ids]:
         del _packed[key]
+    for key in [k for k in _dense if k[0] in ids]:
+        del _dense[key]
 
 
 # ---------------------------------------------------------------- elementwise surface
@@ -334,8 +352,8 @@ def self_attention_tokens(tokens: torch.Tensor, weights: Mapping[str, torch.Tens
     dt = dense_dtype()
     tokens = tokens.to(dt)
     q, k, v = (
-        F.linear(tokens, weights[f"{prefix}.to_{n}.weight"].to(dt),
-                 weights[f"{prefix}.to_{n}.bias"].to(dt) if qkv_bias else None)
+        F.linear(tokens, _dense_weight(weights[f"{prefix}.to_{n}.weight"], dt),
+                 _dense_weight(weights[f"{prefix}.to_{n}.bias"], dt) if qkv_bias else None)
         for n in ("q", "k", "v")
     )
     b, length, c = q.shape
@@ -346,7 +364,8 @@ def self_attention_tokens(tokens: torch.Tensor, weights: Mapping[str, torch.Tens
     att = F.scaled_dot_product_attention(split(q), split(k), split(v), scale=scale)
     merged = att.transpose(1, 2).reshape(b, length, c)
     if include_fc:
-        merged = F.linear(merged, weights[f"{prefix}.out_proj.weight"].to(dt), weights[f"{prefix}.out_proj.bias"].to(dt))
+        merged = F.linear(merged, _dense_weight(weights[f"{prefix}.out_proj.weight"], dt),
+                          _dense_weight(weights[f"{prefix}.out_proj.bias"], dt))
     return merged
 
 

@@ -371,7 +371,7 @@ def run(*, model: str = "mlx-generate-ctmr-mr-brain", output_dir=None, modality:
         raise ValueError(f"unknown model {model!r}; supported: {sorted(MODELS)}")
     configuration = MODELS[model]
     if configuration == "ct":
-        raise ValueError("mlx-generate-ctmr-ct generates from a label mask: use sample_ct_from_mask_ncdhw")
+        raise ValueError("mlx-generate-ctmr-ct generates from a label mask: use sample_ct_from_mask_ncdhw")  # noqa
     config = CONFIGURATIONS[configuration]
     mod = config["modality"] if modality is None else int(modality)
     if mod not in config["modalities"]:
@@ -406,3 +406,144 @@ def run(*, model: str = "mlx-generate-ctmr-mr-brain", output_dir=None, modality:
         "peak_memory_bytes": int(torch.cuda.max_memory_allocated(device)),
     }
     return {"outputs": outputs, "artifacts": {}, "details": details}
+
+
+# ---------------------------------------------------------------- CT from a label mask (from_mask.py)
+VALID_LABELS = frozenset(range(133)) | {200}
+
+
+def require_label(label) -> np.ndarray:
+    """``from_mask._require_label`` (``from_mask.py:356-376``): integer NCDHW, ids 0..132 + body 200."""
+    host = np.asarray(label.cpu() if isinstance(label, torch.Tensor) else label)
+    if host.ndim != 5 or int(host.shape[1]) != 1:
+        raise ValueError(f"label must be NCDHW with 1 channel; got {host.shape}")
+    if not np.issubdtype(host.dtype, np.integer):
+        raise ValueError(f"label must be integer; got {host.dtype}")
+    unique = {int(v) for v in np.unique(host)}
+    unknown = sorted(v for v in unique if v not in VALID_LABELS)
+    if unknown:
+        raise ValueError("MAISI mask contains labels outside 0..132 plus body label 200: "
+                         + ", ".join(str(v) for v in unknown[:10]))
+    if 200 not in unique:
+        raise ValueError("MAISI mask is missing body-envelope label 200; add it before generation")
+    if any(int(s) % Z_SCALE for s in host.shape[2:]):
+        raise ValueError(f"label spatial {tuple(host.shape[2:])} must be multiples of {Z_SCALE}")
+    return host
+
+
+def binarize_labels_ncdhw(label: torch.Tensor, bits: int = 8) -> torch.Tensor:
+    """Bit k of each label id as channel k, fp32, channels-last (``condition.py:20-43``)."""
+    if bits != 8:
+        raise ValueError("from-mask dest packs 8 bits")
+    ids = label.to(torch.int32)
+    planes = ((ids >> torch.arange(bits, device=ids.device, dtype=torch.int32).reshape(1, bits, 1, 1, 1)) & 1)
+    return planes.to(torch.float32).contiguous(memory_format=torch.channels_last_3d)
+
+
+def spacing_tensor_ncdhw(spacing_mm: Sequence[float], device) -> torch.Tensor:
+    """``spacing_mm * 100`` as ``(1, 3)`` fp32, no FP16 rounding (``condition.py:46-64``)."""
+    values = [float(a) * 100.0 for a in spacing_mm]
+    if len(values) != 3 or any(not math.isfinite(v) or v <= 0 for v in values):
+        raise ValueError(f"spacing_mm * 100 must be three finite values > 0; got {values}")
+    return torch.tensor([values], dtype=torch.float32, device=device)
+
+
+def to_hu_ncdhw(image: torch.Tensor, label: torch.Tensor) -> torch.Tensor:
+    """``clip(x, 0, 1) * 2000 - 1000`` HU with background (label 0) at -1000 (``decode.py:248-259``)."""
+    hu = image.clamp(0.0, 1.0) * 2000.0 - 1000.0
+    return torch.where(label.to(hu.device) == 0, torch.full_like(hu, -1000.0), hu)
+
+
+class ControlNetUNetStep:
+    """One ControlNet-conditioned UNet velocity + Euler update (``from_mask.py:298-338``), graph-captured.
+
+    The label's conditioning embedding is computed once (``controlnet.py:167-194``)
+    and reused by every step, as the reference does.
+    """
+
+    def __init__(self, unet_weights, controlnet_weights, unet_constructor, controlnet_constructor, latent_shape, *,
+                 conditioning_embedding: torch.Tensor, class_label: int, spacing: torch.Tensor, device,
+                 use_cuda_graph: bool = True) -> None:
+        self.uw, self.cw = unet_weights, controlnet_weights
+        self.uc, self.cc = unet_constructor, controlnet_constructor
+        batch = int(latent_shape[0])
+        self.z = torch.zeros(tuple(latent_shape), dtype=torch.float32, device=device).contiguous(
+            memory_format=torch.channels_last_3d)
+        self.t = torch.zeros((batch,), dtype=torch.float32, device=device)
+        self.dt = torch.zeros((), dtype=torch.float32, device=device)
+        self.classes = torch.full((batch,), int(class_label), dtype=torch.int64, device=device)
+        self.spacing = spacing.to(device=device, dtype=torch.float32).expand(batch, 3).contiguous()
+        self.embedding = conditioning_embedding
+        self.use_cuda_graph = use_cuda_graph
+        self.graph: torch.cuda.CUDAGraph | None = None
+        self.launches_per_step = 0
+
+    def velocity(self) -> torch.Tensor:
+        down, mid = networks.controlnet_residuals_ncdhw(self.z, self.t, self.classes, None, self.cw,
+                                                        constructor=self.cc,
+                                                        conditioning_embedding=self.embedding)
+        _, v = networks.denoise_unet_ncdhw(self.z, self.t, self.classes, self.spacing, self.uw, constructor=self.uc,
+                                           down_block_additional_residuals=down, mid_block_additional_residual=mid)
+        return v
+
+    def _step(self) -> None:
+        v = self.velocity().to(torch.float32).contiguous(memory_format=torch.channels_last_3d)
+        ops.rflow_step(self.z, v, guidance=None, dt=self.dt, out=self.z)
+
+    prepare = GuidedUNetStep.prepare
+    sample = GuidedUNetStep.sample
+    release = GuidedUNetStep.release
+
+
+@dataclass
+class FromMaskResult:
+    latent: torch.Tensor
+    decoded: torch.Tensor
+    hu: torch.Tensor
+    stage_timings_s: dict[str, float] = field(default_factory=dict)
+
+
+def sample_ct_from_mask_ncdhw(label, spacing_mm: Sequence[float], *, unet_weights, controlnet_weights, vae_weights,
+                              unet_constructor=PRODUCTION_UNET, controlnet_constructor=PRODUCTION_CONTROLNET,
+                              vae_constructor=PRODUCTION_VAE, scale_factor: float = 1.0, seed: int | None = None,
+                              latent: torch.Tensor | None = None, num_inference_steps: int = 30,
+                              guidance_scale: float = 0.0, roi=CT_ROI, overlap=CT_OVERLAP, device=None,
+                              use_cuda_graph: bool = True) -> FromMaskResult:
+    """CT volume from a MAISI label map (``from_mask.sample_ct_from_mask_ncdhw``, ``from_mask.py:121-295``)."""
+    if float(guidance_scale) != 0.0:
+        raise ValueError("the CT path uses ControlNet conditioning, not guidance")
+    if not math.isfinite(float(scale_factor)) or float(scale_factor) == 0.0:
+        raise ValueError("scale_factor must be a finite non-zero caller value")
+    device = torch.device(device or "cuda")
+    host = require_label(label)
+    label_dev = torch.from_numpy(host).to(device)
+    shape = (int(host.shape[0]), 4, *(int(s) // Z_SCALE for s in host.shape[2:]))
+    if latent is None:
+        if seed is None:
+            raise ValueError("seed is required when latent is omitted")
+        latent = init_latent_ncdhw(shape, seed=int(seed), device=device)
+    elif tuple(latent.shape) != shape:
+        raise ValueError(f"latent shape {tuple(latent.shape)} != {shape}")
+    started = time.perf_counter()
+    cond = binarize_labels_ncdhw(label_dev)
+    embedding = networks.encode_controlnet_condition_ncdhw(cond, controlnet_weights,
+                                                            constructor=controlnet_constructor)
+    del cond
+    timesteps, _ = set_timesteps_rflow(num_inference_steps=num_inference_steps,
+                                       input_img_size_numel=math.prod(shape[2:]))
+    step = ControlNetUNetStep(unet_weights, controlnet_weights, unet_constructor, controlnet_constructor, shape,
+                              conditioning_embedding=embedding, class_label=CONFIGURATIONS["ct"]["modality"],
+                              spacing=spacing_tensor_ncdhw(spacing_mm, device), device=device,
+                              use_cuda_graph=use_cuda_graph)
+    final = step.sample(latent.to(device=device, dtype=torch.float32).contiguous(
+        memory_format=torch.channels_last_3d), timesteps)
+    step.release()
+    torch.cuda.synchronize(device)
+    rflow_s = time.perf_counter() - started
+    started = time.perf_counter()
+    decoded = sliding_window_decode_ncdhw(final, vae_weights, constructor=vae_constructor, roi=roi, overlap=overlap,
+                                          scale_factor=scale_factor)
+    hu = to_hu_ncdhw(decoded, label_dev)
+    torch.cuda.synchronize(device)
+    return FromMaskResult(final, decoded, hu, {"rflow_controlnet_unet": rflow_s,
+                                               "vae_decode": time.perf_counter() - started})

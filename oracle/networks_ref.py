@@ -401,3 +401,35 @@ def binarize_labels(label: torch.Tensor, bits: int = 8) -> torch.Tensor:
     ids = label.to(torch.int32)[:, 0]
     planes = [((ids >> k) & 1).to(torch.float32) for k in range(bits)]
     return torch.stack(planes, dim=1)
+
+
+def spacing_tensor(spacing_mm: Sequence[float]) -> torch.Tensor:
+    """CT-path spacing: ``spacing_mm * 100`` as (1, 3) fp32, no FP16 rounding (``condition.py:46-64``)."""
+    return torch.tensor([[float(a) * 100.0 for a in spacing_mm]], dtype=torch.float32)
+
+
+def to_hu(decoded: torch.Tensor, label: torch.Tensor) -> torch.Tensor:
+    """``decode.to_hu_ncdhw`` (``decode.py:248-259``)."""
+    hu = decoded.clamp(0.0, 1.0) * 2000.0 - 1000.0
+    return torch.where(label == 0, torch.tensor(-1000.0, dtype=hu.dtype), hu)
+
+
+def sample_ct_from_mask(label, spacing_mm, unet_w: Weights, unet_ctor: Mapping, cn_w: Weights, cn_ctor: Mapping,
+                        vae_w: Weights, vae_ctor: Mapping, latent, num_inference_steps: int, scale_factor: float,
+                        roi, overlap, modality: int = 1):
+    """``from_mask.sample_ct_from_mask_ncdhw`` (``from_mask.py:121-295``): ControlNet-conditioned rflow,
+    sliding-window decode, HU mapping. Returns ``(latent, decoded, hu)``."""
+    cond = binarize_labels(label)
+    embedding = controlnet_cond_embed(cond, cn_w, cn_ctor)
+    spacing = spacing_tensor(spacing_mm).repeat(latent.shape[0], 1)
+    classes = torch.full((latent.shape[0],), int(modality), dtype=torch.int64)
+    timesteps, _ = set_timesteps_rflow(num_inference_steps, int(np.prod(latent.shape[2:])))
+
+    def velocity(z, t):
+        tt = torch.full((z.shape[0],), float(t), dtype=torch.float32)
+        down, mid = controlnet_residuals(z, tt, classes, cond, cn_w, cn_ctor, conditioning_embedding=embedding)
+        return denoise_unet(z, tt, classes, spacing, unet_w, unet_ctor, down_residuals=down, mid_residual=mid)[1]
+
+    final = sample_rflow(latent, velocity, timesteps)
+    decoded = sliding_window_decode(final, vae_w, vae_ctor, roi, overlap, scale_factor=scale_factor)
+    return final, decoded, to_hu(decoded, label)
