@@ -1,9 +1,9 @@
-"""Benchmark: 256x256x128 MR-Brain volumes/min on B200 (BASELINE.json ``metric``).
+"""Benchmark: 256x256x128 MR-Brain volumes/min on B200 (the headline metric).
 
 One step = one MR-Brain volume: 30 guided rectified-flow steps of the production
 UNet (CFG batch 2, latent 1x4x64x64x32) and the production VAE decode to
 256x256x128 as four overlapping depth windows (ROI (24,64,32), overlap 0.25,
-Gaussian blend) - BASELINE configs 3 and 2 together. Weights are random-init of
+Gaussian blend): the MR-Brain generation and the VAE decode stages together. Weights are random-init of
 the named architectures (no checkpoints exist offline), inputs synthetic.
 
   python bench.py [--gpus N --steps K --warmup W] [--precision bf16|fp32] [--impl reference]
@@ -59,10 +59,12 @@ def _args():
     p.add_argument("--precision", choices=("fp16", "bf16", "fp32"), default="fp16")
     p.add_argument("--no-graph", action="store_true")
     p.add_argument("--no-cpu-baseline", action="store_true")
-    p.add_argument("--case", choices=("volume", "sweep", "conv", "unet-step", "vae-window"), default="volume",
-                   help="volume: the benchmark; sweep: BASELINE config 5 conv sweep (TFLOP/s per shape); "
+    p.add_argument("--case", choices=("volume", "sweep", "conv", "unet-step", "vae-window", "breakdown"),
+                   default="volume",
+                   help="volume: the benchmark; sweep: the reference's conv-kernel sweep (TFLOP/s per shape); "
                         "conv / unet-step / vae-window: one kernel shape, one UNet step or one decode window "
-                        "(bounded workloads for profiler captures)")
+                        "(bounded workloads for profiler captures); breakdown: per-stage device times of one "
+                        "UNet step and one decode window")
     p.add_argument("--shape", default="2,64,64,64,32,64", help="conv case: B,C,D,H,W,O")
     p.add_argument("--iters", type=int, default=3)
     return p.parse_args()
@@ -196,8 +198,60 @@ def _time_conv(shape, precision: str, iters: int, dev) -> tuple[float, float]:
         ops.conv3d(x, packed, bias)
     ops.PROFILE = None
     torch.cuda.synchronize(dev)
-    ms = statistics.median(s_.elapsed_time(e_) for s_, e_, _ in prof)
-    return ms, prof[0][2] / (ms * 1e-3) / 1e12
+    gemm = [r for r in prof if r["kind"] == "gemm"]
+    ms = statistics.median(r["start"].elapsed_time(r["end"]) for r in gemm)
+    return ms, gemm[0]["flops"] / (ms * 1e-3) / 1e12
+
+
+def _total_ms(records) -> float:
+    return sum(r["start"].elapsed_time(r["end"]) for r in records)
+
+
+def _breakdown(part: str, records, total_ms: float) -> None:
+    """Per-stage and per-shape device times of one eager pass (CUDA events around each launch group)."""
+    by_kind: dict[str, float] = {}
+    rows: dict[tuple[str, str], list[float]] = {}
+    for r in records:
+        t = r["start"].elapsed_time(r["end"])
+        by_kind[r["kind"]] = by_kind.get(r["kind"], 0.0) + t
+        acc = rows.setdefault((r["kind"], r["what"]), [0, 0.0, 0.0])
+        acc[0] += 1
+        acc[1] += t
+        acc[2] += r["flops"]
+    other = total_ms - sum(by_kind.values())
+    print(json.dumps({"part": part, "total_ms": round(total_ms, 3),
+                      "by_kind_ms": {k: round(v, 3) for k, v in sorted(by_kind.items())},
+                      "other_ms": round(other, 3)}), flush=True)
+    for (kind, what), (n, t, fl) in sorted(rows.items(), key=lambda kv: -kv[1][1]):
+        line = {"part": part, "kind": kind, "what": what, "n": n, "ms": round(t, 4),
+                "share": round(t / total_ms, 4)}
+        if fl:
+            line["tflops"] = round(fl / (t * 1e-3) / 1e12, 1)
+        print(json.dumps(line), flush=True)
+
+
+def _profile_pass(part: str, fn, dev) -> None:
+    from ctmr_b200 import ops
+
+    torch.cuda.synchronize(dev)
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    plain = []
+    for _ in range(3):
+        start.record()
+        fn()
+        end.record()
+        torch.cuda.synchronize(dev)
+        plain.append(start.elapsed_time(end))
+    prof: list = []
+    ops.PROFILE = prof
+    start.record()
+    fn()
+    end.record()
+    ops.PROFILE = None
+    torch.cuda.synchronize(dev)
+    total = start.elapsed_time(end)
+    print(json.dumps({"part": part, "plain_ms": [round(v, 3) for v in plain], "profiled_ms": round(total, 3)}))
+    _breakdown(part, prof, total)
 
 
 def run_case(args) -> None:
@@ -219,7 +273,7 @@ def run_case(args) -> None:
                                   "frac_of_peak": round(tflops / peak, 3), "peak": f"{kind} bf16_tflops {peak}"}),
                       flush=True)
             return
-        if args.case == "unet-step":
+        if args.case in ("unet-step", "breakdown"):
             w = W.random_weights(W.unet_shapes(P.PRODUCTION_UNET), seed=0, device=dev)
             step = P.GuidedUNetStep(w, P.PRODUCTION_UNET, LATENT, class_label=MODALITY,
                                     spacing=P.image_spacing_tensor(SPACING, dev), guidance_scale=GUIDANCE,
@@ -229,13 +283,18 @@ def run_case(args) -> None:
             step.dt.fill_(0.01)
             for _ in range(args.iters):
                 step._step()
-        else:
+            if args.case == "breakdown":
+                _profile_pass("unet-step", step._step, dev)
+        if args.case in ("vae-window", "breakdown"):
             w = W.random_weights(W.vae_decoder_shapes(P.PRODUCTION_VAE), seed=1, device=dev)
             from ctmr_b200 import networks
 
             z = torch.randn((1, 4, *DECODE_ROI), device=dev)
             for _ in range(args.iters):
                 networks.decode_vae_ncdhw(z, w, constructor=P.PRODUCTION_VAE)
+            if args.case == "breakdown":
+                _profile_pass("vae-window", lambda: networks.decode_vae_ncdhw(z, w, constructor=P.PRODUCTION_VAE),
+                              dev)
         torch.cuda.synchronize(dev)
         print(json.dumps({"case": args.case, "precision": args.precision, "iters": args.iters, "ok": True}))
 
@@ -371,10 +430,11 @@ def main() -> None:
     peaks, peak_kind = _peaks()
     roofline = None
     if unet_part:
-        conv_ms = STEPS_RFLOW * sum(s.elapsed_time(e) for s, e, _ in unet_part) + sum(
-            s.elapsed_time(e) for s, e, _ in vae_part)
-        conv_flop = STEPS_RFLOW * sum(f for _, _, f in unet_part) + sum(f for _, _, f in vae_part)
-        n_launch = STEPS_RFLOW * len(unet_part) + len(vae_part)
+        unet_gemm = [r for r in unet_part if r["kind"] == "gemm"]
+        vae_gemm = [r for r in vae_part if r["kind"] == "gemm"]
+        conv_ms = STEPS_RFLOW * _total_ms(unet_gemm) + _total_ms(vae_gemm)
+        conv_flop = STEPS_RFLOW * sum(r["flops"] for r in unet_gemm) + sum(r["flops"] for r in vae_gemm)
+        n_launch = STEPS_RFLOW * len(unet_gemm) + len(vae_gemm)
         achieved = conv_flop / (conv_ms * 1e-3) / 1e12
         peak = float(peaks.get("bf16_tflops_sustained", FALLBACK_PEAKS["bf16_tflops_sustained"]))
         roofline = {"bound": "tensor", "achieved": round(achieved, 1), "peak": peak, "unit": "TFLOP/s",

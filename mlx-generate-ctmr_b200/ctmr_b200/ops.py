@@ -23,14 +23,31 @@ BF16 = torch.bfloat16
 PRECISIONS = ("fp32", "bf16", "fp16")
 
 # Instrumentation: LAUNCHES counts the library's kernel launches issued from
-# Python; when PROFILE is a list, conv3d records (start, end, flops) CUDA events
-# around each implicit-GEMM launch on the current stream.
+# Python; when PROFILE is a list, conv3d and group_norm_affine append one record
+# per stage ({"kind": "prepare" | "gemm" | "gn", "start", "end", "flops", "what"},
+# CUDA events on the current stream) around their launches.
 LAUNCHES = [0]
 PROFILE: list | None = None
 
 
 def _count(n: int) -> None:
     LAUNCHES[0] += n
+
+
+class _profiled:
+    """Append a PROFILE record bracketing the enclosed launches with CUDA events."""
+
+    def __init__(self, kind: str, flops: float, what: str) -> None:
+        self.rec = {"kind": kind, "flops": flops, "what": what,
+                    "start": torch.cuda.Event(enable_timing=True), "end": torch.cuda.Event(enable_timing=True)}
+
+    def __enter__(self):
+        self.rec["start"].record()
+        return self
+
+    def __exit__(self, *exc) -> None:
+        self.rec["end"].record()
+        PROFILE.append(self.rec)
 
 
 def _stream() -> int:
@@ -266,15 +283,16 @@ def conv3d(
     if PROFILE is None:
         check(LIB.ctmr_conv3d(ctypes.byref(desc), ws_ptr, ws_bytes, _stream()), "conv3d")
     else:
-        if ws_bytes:
-            check(LIB.ctmr_conv3d_stages(ctypes.byref(desc), ws_ptr, ws_bytes, _lib.CONV_PREPARE, _stream()),
-                  "conv3d prepare")
-        start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        start.record()
-        check(LIB.ctmr_conv3d_stages(ctypes.byref(desc), ws_ptr, ws_bytes, _lib.CONV_GEMM, _stream()), "conv3d gemm")
-        end.record()
         taps = 8 if packed.upsample else k ** 3
-        PROFILE.append((start, end, 2.0 * b * od * oh * ow * o * cin * taps))
+        what = (f"{b}x{cin}->{o} out {od}x{oh}x{ow} k{k} s{stride} up{int(packed.upsample)} tri{int(trilinear)} "
+                f"pool{int(avgpool)} norm{int(affine is not None)} res{int(residual is not None)} {packed.precision}")
+        if ws_bytes:
+            with _profiled("prepare", 0.0, what):
+                check(LIB.ctmr_conv3d_stages(ctypes.byref(desc), ws_ptr, ws_bytes, _lib.CONV_PREPARE, _stream()),
+                      "conv3d prepare")
+        with _profiled("gemm", 2.0 * b * od * oh * ow * o * cin * taps, what):
+            check(LIB.ctmr_conv3d_stages(ctypes.byref(desc), ws_ptr, ws_bytes, _lib.CONV_GEMM, _stream()),
+                  "conv3d gemm")
     return out
 
 
@@ -299,15 +317,22 @@ def group_norm_affine(
     _count(2)
     ws_bytes = int(LIB.ctmr_group_norm_workspace_size(b, voxels, groups))
     ws = torch.empty(max(ws_bytes, 4), dtype=torch.uint8, device=x.device)
-    check(
-        LIB.ctmr_group_norm_affine(
-            view(x), view(x2), b, voxels,
-            gamma.data_ptr() if gamma is not None else None,
-            beta.data_ptr() if beta is not None else None,
-            groups, float(eps), affine.data_ptr(), ws.data_ptr(), ws_bytes, _stream(),
-        ),
-        "group_norm_affine",
-    )
+    def launch() -> None:
+        check(
+            LIB.ctmr_group_norm_affine(
+                view(x), view(x2), b, voxels,
+                gamma.data_ptr() if gamma is not None else None,
+                beta.data_ptr() if beta is not None else None,
+                groups, float(eps), affine.data_ptr(), ws.data_ptr(), ws_bytes, _stream(),
+            ),
+            "group_norm_affine",
+        )
+
+    if PROFILE is None:
+        launch()
+    else:
+        with _profiled("gn", 0.0, f"{b}x{ctot} {d}x{h}x{w} g{groups}"):
+            launch()
     return affine
 
 

@@ -139,7 +139,7 @@ def _kaiming(o, c, k, gen):
 
 @pytest.mark.parametrize("precision", ["fp32", "bf16", "fp16"])
 def test_config1_vae_resblock(cuda, precision):
-    """VAE ResBlock 1x64x32^3, GN(32, 1e-6), two 3x3x3 convs + residual."""
+    """Smallest benchmark configuration: VAE ResBlock 1x64x32^3, GN(32, 1e-6), two 3x3x3 convs + residual."""
     from ctmr_b200 import fast_b200
 
     gen = torch.Generator().manual_seed(0)
