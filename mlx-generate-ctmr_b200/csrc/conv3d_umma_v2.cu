@@ -193,48 +193,95 @@ __global__ void __launch_bounds__(kThreadsV2, 1)
     const int row = quarter * 32 + lane;
     const int aw = row >> 3, ih = row & 7;  // atom (w offset), row in atom (h offset)
     const uint32_t lane_addr = tmem + (static_cast<uint32_t>(quarter * 32) << 16);
+    // Each tile is drained in blocks of (M tile m, 64 columns); the residual of
+    // block k + 1 is loaded while block k is finished, and block 0's before the
+    // accumulator wait, so the residual reads overlap instead of serialising.
+    const int halves = (g.bn + 63) >> 6;
+    const int nblk = MT * halves;
+    int n0 = 0, w0 = 0, h0 = 0, d0 = 0, b = 0, phase = 0;
+    auto row_of = [&](int m, bool& valid, long long& out_base, long long& res_base) {
+      const int rd = d0 + m, rh = h0 + ih, rw = w0 + aw;
+      valid = rw < g.row_w && rh < g.row_h && rd < g.row_d;
+      int od = rd, oh = rh, ow = rw;
+      if (TW == 2) {
+        od = 2 * rd + (phase >> 2);
+        oh = 2 * rh + ((phase >> 1) & 1);
+        ow = 2 * rw + (phase & 1);
+      }
+      const long long vox = ((static_cast<long long>(b) * g.out_d + od) * g.out_h + oh) * g.out_w + ow;
+      out_base = vox * g.out_cstride + g.out_coff;
+      res_base = 0;
+      if (g.res != nullptr) {
+        const int qd = g.res_up ? od >> 1 : od, qh = g.res_up ? oh >> 1 : oh, qw = g.res_up ? ow >> 1 : ow;
+        res_base = (((static_cast<long long>(b) * g.res_d + qd) * g.res_h + qh) * g.res_w + qw) * g.res_cstride;
+      }
+    };
+    auto issue = [&](int k, uint32_t(&w)[64]) {
+      if (g.res == nullptr) return;
+      const int m = k / halves, c0 = (k - m * halves) * 64;
+      bool valid;
+      long long out_base, res_base;
+      row_of(m, valid, out_base, res_base);
+      if (valid) res_issue64(g, n0 + c0, res_base + n0 + c0, w);
+    };
     int lt = 0;
+    auto finish = [&](int k, const uint32_t(&w)[64]) {
+      const int m = k / halves, c0 = (k - m * halves) * 64;
+      bool valid;
+      long long out_base, res_base;
+      row_of(m, valid, out_base, res_base);
+      const float* bias = g.bias != nullptr ? g.bias + static_cast<long long>(b) * g.bias_bstride : nullptr;
+      const uint32_t acc = lane_addr + static_cast<uint32_t>((lt & 1) * MT + m) * bn;
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const int c = c0 + 16 * j;
+        if (c >= g.bn) break;
+        float v[16];
+        tmem_ld16(acc + static_cast<uint32_t>(c), v);  // warp-collective: every lane loads
+        const int n = n0 + c;
+        if (valid && n < g.cout) {
+          const int cnt = min(16, g.cout - n);
+          if (bias != nullptr) {
+            if (cnt == 16 && (reinterpret_cast<uintptr_t>(bias + n) & 15) == 0) {
+#pragma unroll
+              for (int i = 0; i < 4; ++i) {
+                const float4 q = __ldg(reinterpret_cast<const float4*>(bias + n) + i);
+                v[4 * i] += q.x;
+                v[4 * i + 1] += q.y;
+                v[4 * i + 2] += q.z;
+                v[4 * i + 3] += q.w;
+              }
+            } else {
+#pragma unroll
+              for (int i = 0; i < 16; ++i)
+                if (i < cnt) v[i] += __ldg(bias + n + i);
+            }
+          }
+          if (g.res != nullptr) {
+#pragma unroll
+            for (int i = 0; i < 16; ++i) v[i] += res_word(g, w, 16 * j + i);
+          }
+          store16(g, v, n, out_base + n);
+        }
+      }
+    };
     for (int t = blockIdx.x; t < g.total_tiles && !*abort_flag; t += gridDim.x, ++lt) {
       const int buf = lt & 1;
+      decode(t, n0, w0, h0, d0, b, phase);
+      uint32_t ra[64], rb[64];
+      issue(0, ra);
       if (!mbar_wait_bounded(&tmem_full[buf], static_cast<uint32_t>(lt >> 1) & 1u, kErrWaitAcc)) {
         *abort_flag = 1;
         break;
       }
       tc_fence_after();
-      int n0, w0, h0, d0, b, phase;
-      decode(t, n0, w0, h0, d0, b, phase);
-      const float* bias = g.bias != nullptr ? g.bias + static_cast<long long>(b) * g.bias_bstride : nullptr;
 #pragma unroll 1
-      for (int m = 0; m < MT; ++m) {
-        const int rd = d0 + m, rh = h0 + ih, rw = w0 + aw;
-        const bool valid = rw < g.row_w && rh < g.row_h && rd < g.row_d;
-        int od = rd, oh = rh, ow = rw;
-        if (TW == 2) {
-          od = 2 * rd + (phase >> 2);
-          oh = 2 * rh + ((phase >> 1) & 1);
-          ow = 2 * rw + (phase & 1);
-        }
-        const long long vox = ((static_cast<long long>(b) * g.out_d + od) * g.out_h + oh) * g.out_w + ow;
-        const long long out_base = vox * g.out_cstride + g.out_coff;
-        long long res_base = 0;
-        if (g.res != nullptr) {
-          const int qd = g.res_up ? od >> 1 : od, qh = g.res_up ? oh >> 1 : oh, qw = g.res_up ? ow >> 1 : ow;
-          res_base =
-              (((static_cast<long long>(b) * g.res_d + qd) * g.res_h + qh) * g.res_w + qw) * g.res_cstride;
-        }
-        const uint32_t acc = lane_addr + static_cast<uint32_t>(buf * MT + m) * bn;
-#pragma unroll 1
-        for (int c = 0; c < g.bn; c += 16) {
-          float v[16];
-          tmem_ld16(acc + static_cast<uint32_t>(c), v);
-          const int n = n0 + c;
-          if (valid && n < g.cout) {
-            if (bias != nullptr) {
-              const int cnt = min(16, g.cout - n);
-              for (int i = 0; i < cnt; ++i) v[i] += __ldg(bias + n + i);
-            }
-            store_row16(g, v, n, out_base + n, res_base + n);
-          }
+      for (int k = 0; k < nblk; k += 2) {
+        if (k + 1 < nblk) issue(k + 1, rb);
+        finish(k, ra);
+        if (k + 1 < nblk) {
+          if (k + 2 < nblk) issue(k + 2, ra);
+          finish(k + 1, rb);
         }
       }
       tc_fence_before();

@@ -84,4 +84,93 @@ __device__ __forceinline__ void store_row16(const ConvGeom& g, float (&v)[16], i
   }
 }
 
+// Store 16 finished output columns [n, n+16) of one voxel row.
+__device__ __forceinline__ void store16(const ConvGeom& g, const float (&v)[16], int n, long long out_off) {
+  const int cnt = min(16, g.cout - n);
+  if (g.out_bf16) {
+    uint16_t* o = static_cast<uint16_t*>(g.out) + out_off;
+    if (cnt == 16 && (reinterpret_cast<uintptr_t>(o) & 15) == 0) {
+      uint4 q0, q1;
+      q0.x = pack_bf16x2(v[0], v[1]);
+      q0.y = pack_bf16x2(v[2], v[3]);
+      q0.z = pack_bf16x2(v[4], v[5]);
+      q0.w = pack_bf16x2(v[6], v[7]);
+      q1.x = pack_bf16x2(v[8], v[9]);
+      q1.y = pack_bf16x2(v[10], v[11]);
+      q1.z = pack_bf16x2(v[12], v[13]);
+      q1.w = pack_bf16x2(v[14], v[15]);
+      reinterpret_cast<uint4*>(o)[0] = q0;
+      reinterpret_cast<uint4*>(o)[1] = q1;
+    } else {
+#pragma unroll
+      for (int i = 0; i < 16; ++i) {
+        if (i < cnt) {
+          __nv_bfloat16 h = __float2bfloat16_rn(v[i]);
+          o[i] = *reinterpret_cast<uint16_t*>(&h);
+        }
+      }
+    }
+  } else {
+    float* o = static_cast<float*>(g.out) + out_off;
+    if (cnt == 16 && (reinterpret_cast<uintptr_t>(o) & 15) == 0) {
+#pragma unroll
+      for (int i = 0; i < 4; ++i)
+        reinterpret_cast<float4*>(o)[i] = make_float4(v[4 * i], v[4 * i + 1], v[4 * i + 2], v[4 * i + 3]);
+    } else {
+#pragma unroll
+      for (int i = 0; i < 16; ++i)
+        if (i < cnt) o[i] = v[i];
+    }
+  }
+}
+
+// Issue the residual loads for output columns [n, n + 64) of one voxel row into
+// raw 32-bit words (fp32: one column per word; bf16: two columns per word), so
+// that their latency overlaps the accumulator wait and the previous block.
+__device__ __forceinline__ void res_issue64(const ConvGeom& g, int n, long long res_off, uint32_t (&w)[64]) {
+  const int cnt = min(64, g.cout - n);
+  if (cnt <= 0) return;
+  if (g.res_bf16) {
+    const uint16_t* r = static_cast<const uint16_t*>(g.res) + res_off;
+    if (cnt == 64 && (reinterpret_cast<uintptr_t>(r) & 15) == 0) {
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        const uint4 q = __ldg(reinterpret_cast<const uint4*>(r) + i);
+        w[4 * i] = q.x;
+        w[4 * i + 1] = q.y;
+        w[4 * i + 2] = q.z;
+        w[4 * i + 3] = q.w;
+      }
+    } else {
+#pragma unroll
+      for (int i = 0; i < 32; ++i) {
+        const uint32_t lo = 2 * i < cnt ? r[2 * i] : 0u;
+        const uint32_t hi = 2 * i + 1 < cnt ? r[2 * i + 1] : 0u;
+        w[i] = lo | (hi << 16);
+      }
+    }
+  } else {
+    const float* r = static_cast<const float*>(g.res) + res_off;
+    if (cnt == 64 && (reinterpret_cast<uintptr_t>(r) & 15) == 0) {
+#pragma unroll
+      for (int i = 0; i < 16; ++i) {
+        const uint4 q = __ldg(reinterpret_cast<const uint4*>(r) + i);
+        w[4 * i] = q.x;
+        w[4 * i + 1] = q.y;
+        w[4 * i + 2] = q.z;
+        w[4 * i + 3] = q.w;
+      }
+    } else {
+#pragma unroll
+      for (int i = 0; i < 64; ++i) w[i] = i < cnt ? __float_as_uint(__ldg(r + i)) : 0u;
+    }
+  }
+}
+
+// Residual column j (0..63) of a block loaded by res_issue64.
+__device__ __forceinline__ float res_word(const ConvGeom& g, const uint32_t (&w)[64], int j) {
+  if (g.res_bf16) return __uint_as_float((j & 1) ? (w[j >> 1] & 0xFFFF0000u) : (w[j >> 1] << 16));
+  return __uint_as_float(w[j]);
+}
+
 }  // namespace ctmr

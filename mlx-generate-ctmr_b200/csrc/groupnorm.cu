@@ -9,8 +9,9 @@
 // (x - pivot)^2 around its first value, converts them to (count, mean, M2), and
 // the block merges lanes, then channels into groups, in a fixed order (Chan et
 // al.'s pairwise update), writing one (n, mean, M2) partial per group.
-// Pass 2 (grid batch): one warp per group merges the chunk partials (lanes in
-// order, then a fixed shuffle tree) in double precision, then writes
+// Pass 2 (grid groups x batch): one block per group merges the chunk partials
+// (each thread its strided chunks in order, a fixed shuffle tree per warp, then
+// the warps in order) in double precision, then writes
 // scale = gamma * rstd and offset = beta - mean * scale for each channel. The
 // fixed merge order makes the result bitwise reproducible run to run.
 #include <cuda_runtime.h>
@@ -177,41 +178,70 @@ __device__ __forceinline__ MomentsD merge_d(MomentsD a, MomentsD b) {
   return MomentsD{n, a.mean + delta * fb, a.m2 + b.m2 + delta * delta * a.n * fb};
 }
 
-// One warp per group: lanes merge strided chunk subsets in order, then a fixed
-// shuffle tree joins the lanes (double precision, deterministic).
-__global__ void gn_finalize_kernel(const GnParams p) {
-  const int b = blockIdx.x;
+__device__ __forceinline__ MomentsD shfl_down_moments(const MomentsD& m, int off) {
+  return MomentsD{__shfl_down_sync(0xffffffffu, m.n, off), __shfl_down_sync(0xffffffffu, m.mean, off),
+                  __shfl_down_sync(0xffffffffu, m.m2, off)};
+}
+
+// One block per (group, batch item): thread i merges chunks i, i + 128, ... in
+// order (all of its loads issued before the merges), then a fixed shuffle tree
+// joins the lanes of each warp and thread 0 joins the four warps in order (double
+// precision, deterministic).
+constexpr int kFinThreads = 128;
+constexpr int kFinPerThread = 5;  // ceil(gn_max_chunks(1) / kFinThreads)
+
+__global__ void __launch_bounds__(kFinThreads) gn_finalize_kernel(const GnParams p) {
+  __shared__ double s_m[kFinThreads / 32][3];
+  __shared__ double s_stat[2];
+  const int g = blockIdx.x, b = blockIdx.y;
   const int ctot = p.src[0].channels + p.src[1].channels;
   const int cpg = ctot / p.groups;
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int nwarps = blockDim.x >> 5;
-  for (int g = warp; g < p.groups; g += nwarps) {
-    MomentsD m{0.0, 0.0, 0.0};
-    for (int k = lane; k < p.chunks; k += 32) {
-      const float* q = p.partials + ((static_cast<long long>(b) * p.chunks + k) * p.groups + g) * 3;
-      m = merge_d(m, MomentsD{q[0], q[1], q[2]});
-    }
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  float q[kFinPerThread][3];
 #pragma unroll
-    for (int off = 1; off < 32; off <<= 1) {
-      MomentsD o;
-      o.n = __shfl_down_sync(0xffffffffu, m.n, off);
-      o.mean = __shfl_down_sync(0xffffffffu, m.mean, off);
-      o.m2 = __shfl_down_sync(0xffffffffu, m.m2, off);
-      if ((lane & (2 * off - 1)) == 0) m = merge_d(m, o);
+  for (int j = 0; j < kFinPerThread; ++j) {
+    const int k = tid + j * kFinThreads;
+    if (k < p.chunks) {
+      const float* src = p.partials + ((static_cast<long long>(b) * p.chunks + k) * p.groups + g) * 3;
+      q[j][0] = src[0];
+      q[j][1] = src[1];
+      q[j][2] = src[2];
+    } else {
+      q[j][0] = 0.f;
+      q[j][1] = 0.f;
+      q[j][2] = 0.f;
     }
-    m.n = __shfl_sync(0xffffffffu, m.n, 0);
-    m.mean = __shfl_sync(0xffffffffu, m.mean, 0);
-    m.m2 = __shfl_sync(0xffffffffu, m.m2, 0);
-    const double var = m.n > 0.0 ? m.m2 / m.n : 0.0;
-    const double rstd = 1.0 / sqrt(var + static_cast<double>(p.eps));
-    for (int c = g * cpg + lane; c < (g + 1) * cpg; c += 32) {
-      const double gam = p.gamma != nullptr ? static_cast<double>(p.gamma[c]) : 1.0;
-      const double bet = p.beta != nullptr ? static_cast<double>(p.beta[c]) : 0.0;
-      const double scale = gam * rstd;
-      float* a = p.affine + (static_cast<long long>(b) * ctot + c) * 2;
-      a[0] = static_cast<float>(scale);
-      a[1] = static_cast<float>(bet - m.mean * scale);
-    }
+  }
+  MomentsD m{0.0, 0.0, 0.0};
+#pragma unroll
+  for (int j = 0; j < kFinPerThread; ++j) m = merge_d(m, MomentsD{q[j][0], q[j][1], q[j][2]});
+#pragma unroll
+  for (int off = 1; off < 32; off <<= 1) {
+    const MomentsD o = shfl_down_moments(m, off);
+    if ((lane & (2 * off - 1)) == 0) m = merge_d(m, o);
+  }
+  if (lane == 0) {
+    s_m[warp][0] = m.n;
+    s_m[warp][1] = m.mean;
+    s_m[warp][2] = m.m2;
+  }
+  __syncthreads();
+  if (tid == 0) {
+    MomentsD t{0.0, 0.0, 0.0};
+    for (int w = 0; w < kFinThreads / 32; ++w) t = merge_d(t, MomentsD{s_m[w][0], s_m[w][1], s_m[w][2]});
+    const double var = t.n > 0.0 ? t.m2 / t.n : 0.0;
+    s_stat[0] = t.mean;
+    s_stat[1] = 1.0 / sqrt(var + static_cast<double>(p.eps));
+  }
+  __syncthreads();
+  const double mean = s_stat[0], rstd = s_stat[1];
+  for (int c = g * cpg + tid; c < (g + 1) * cpg; c += kFinThreads) {
+    const double gam = p.gamma != nullptr ? static_cast<double>(p.gamma[c]) : 1.0;
+    const double bet = p.beta != nullptr ? static_cast<double>(p.beta[c]) : 0.0;
+    const double scale = gam * rstd;
+    float* a = p.affine + (static_cast<long long>(b) * ctot + c) * 2;
+    a[0] = static_cast<float>(scale);
+    a[1] = static_cast<float>(bet - mean * scale);
   }
 }
 
@@ -239,7 +269,8 @@ cudaError_t launch_group_norm_affine(const GnParams& p, cudaStream_t stream) {
   gn_partial_kernel<<<dim3(p.chunks, p.batch), kGnThreads, chan_smem, stream>>>(p);
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return e;
-  gn_finalize_kernel<<<p.batch, 512, 0, stream>>>(p);
+  if (p.chunks > kFinThreads * kFinPerThread) return cudaErrorInvalidValue;
+  gn_finalize_kernel<<<dim3(p.groups, p.batch), kFinThreads, 0, stream>>>(p);
   return cudaGetLastError();
 }
 
