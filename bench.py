@@ -67,6 +67,8 @@ def _args():
                         "UNet step and one decode window")
     p.add_argument("--shape", default="2,64,64,64,32,64", help="conv case: B,C,D,H,W,O")
     p.add_argument("--iters", type=int, default=3)
+    p.add_argument("--input", choices=("plain", "norm", "tri"), default="plain",
+                   help="conv case: input as is, group-norm affine + SiLU, or trilinear 2x of a half grid")
     return p.parse_args()
 
 
@@ -181,26 +183,40 @@ SWEEP_SHAPES = [(b, c, n, n, n, o) for n in (16, 32, 64) for c, o in ((32, 32), 
                                     (1, 64, 128, 128, 64, 64)]
 
 
-def _time_conv(shape, precision: str, iters: int, dev) -> tuple[float, float]:
+def _time_conv(shape, precision: str, iters: int, dev, input_kind: str = "plain") -> tuple[float, float, float]:
+    """Median GEMM ms, its TFLOP/s and the median prepare ms of one conv3d shape (output grid D, H, W).
+
+    ``input_kind``: plain (the input as is), norm (group-norm affine + SiLU applied
+    by the prepare pass) or tri (trilinear 2x upsampling of a half-grid input).
+    """
     from ctmr_b200 import ops
 
     b, c, d, h, w, o = shape
     gen = torch.Generator(device=dev).manual_seed(0)
-    x = torch.randn((b, c, d, h, w), device=dev, generator=gen).contiguous(memory_format=torch.channels_last_3d)
+    sp = (d // 2, h // 2, w // 2) if input_kind == "tri" else (d, h, w)
+    x = torch.randn((b, c, *sp), device=dev, generator=gen).contiguous(memory_format=torch.channels_last_3d)
     wt = torch.randn((o, c, 3, 3, 3), device=dev, generator=gen) / (27 * c) ** 0.5
     bias = torch.randn(o, device=dev, generator=gen)
     packed = ops.pack_weight(wt, precision)
+    kw = {}
+    if input_kind == "norm":
+        affine = torch.stack([torch.rand((b, c), device=dev, generator=gen) + 0.5,
+                              torch.randn((b, c), device=dev, generator=gen)], dim=-1).contiguous()
+        kw = {"affine": affine, "silu": True}
+    elif input_kind == "tri":
+        kw = {"trilinear": True}
     for _ in range(2):
-        ops.conv3d(x, packed, bias)
+        ops.conv3d(x, packed, bias, **kw)
     prof: list = []
     ops.PROFILE = prof
     for _ in range(iters):
-        ops.conv3d(x, packed, bias)
+        ops.conv3d(x, packed, bias, **kw)
     ops.PROFILE = None
     torch.cuda.synchronize(dev)
     gemm = [r for r in prof if r["kind"] == "gemm"]
+    prep = [r["start"].elapsed_time(r["end"]) for r in prof if r["kind"] == "prepare"]
     ms = statistics.median(r["start"].elapsed_time(r["end"]) for r in gemm)
-    return ms, gemm[0]["flops"] / (ms * 1e-3) / 1e12
+    return ms, gemm[0]["flops"] / (ms * 1e-3) / 1e12, statistics.median(prep) if prep else 0.0
 
 
 def _total_ms(records) -> float:
@@ -267,8 +283,9 @@ def run_case(args) -> None:
             peaks, kind = _peaks()
             peak = float(peaks.get("bf16_tflops", FALLBACK_PEAKS["bf16_tflops"]))
             for shape in shapes:
-                ms, tflops = _time_conv(shape, args.precision, args.iters, dev)
+                ms, tflops, prep_ms = _time_conv(shape, args.precision, args.iters, dev, args.input)
                 print(json.dumps({"case": "conv3d 3x3x3", "shape_bcdhwo": shape, "precision": args.precision,
+                                  "input": args.input, "prepare_ms": round(prep_ms, 4),
                                   "gemm_ms": round(ms, 4), "tflops": round(tflops, 1),
                                   "frac_of_peak": round(tflops / peak, 3), "peak": f"{kind} bf16_tflops {peak}"}),
                       flush=True)

@@ -247,7 +247,8 @@ int plan_conv(const ctmr_conv3d_desc* d, ConvPlan* p) {
   p->narrow = p->exact && p->mode == ctmr::kModeConv3 && !d->trilinear && !d->avgpool && d->out_channels <= 4 &&
               d->x2.data == nullptr &&
               d->x.dtype == CTMR_DTYPE_F32 && (d->residual.data == nullptr || d->residual.dtype == CTMR_DTYPE_F32) &&
-              d->y_dtype == CTMR_DTYPE_F32 && getenv("CTMR_DISABLE_NARROW") == nullptr;
+              d->y_dtype == CTMR_DTYPE_F32 && ctmr::narrow_conv_supported(p->cin, d->out_channels) &&
+              getenv("CTMR_DISABLE_NARROW") == nullptr;
   p->prepare = !direct && !p->narrow;
   p->prep_bytes = p->prepare ? static_cast<size_t>(round_up(static_cast<long long>(d->batch) * p->in_d * p->in_h *
                                                                 p->in_w * p->cpad * 2,
@@ -357,6 +358,7 @@ int ctmr_conv3d_stages(const ctmr_conv3d_desc* d, void* workspace, size_t worksp
     ctmr::NarrowParams np{};
     np.x = d->x.data;
     np.x_cstride = d->x.cstride;
+    np.vec4 = (d->x.cstride % 4 == 0) && (reinterpret_cast<uintptr_t>(d->x.data) % 16 == 0);
     np.batch = d->batch, np.d = d->depth, np.h = d->height, np.w = d->width;
     np.cin = p.cin, np.cout = d->out_channels;
     np.affine = d->affine;

@@ -9,6 +9,7 @@ namespace ctmr {
 struct NarrowParams {
   const void* x;            // fp32 NDHWC input, x_cstride elements per voxel row
   long long x_cstride;
+  int vec4;                 // x and x_cstride allow 16-byte loads of four channels
   int batch, d, h, w, cin, cout;
   const float* affine;      // (B, C, 2) scale/offset or null
   int silu;
@@ -24,6 +25,8 @@ struct NarrowParams {
   long long y_cstride;
 };
 
+// Whether the direct kernel takes this channel count (its weights stay in shared memory).
+bool narrow_conv_supported(int cin, int cout);
 cudaError_t launch_narrow_conv(const NarrowParams& p, cudaStream_t stream);
 
 }  // namespace ctmr

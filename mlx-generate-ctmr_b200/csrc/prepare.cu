@@ -278,6 +278,275 @@ __global__ void __launch_bounds__(256) prepare_kernel(const PrepParams p, const 
   }
 }
 
+// ---------------------------------------------------------------- vectorised fast paths
+// Division by a runtime divisor d as a multiply-high and shift (Granlund and
+// Montgomery's round-up method): q = (umulhi(m, n) + n) >> l with l = ceil(log2 d)
+// and m = floor(2^32 (2^l - d) / d) + 1, exact for every 32-bit n.
+struct FastDiv {
+  uint32_t d, m, l;
+};
+
+FastDiv make_fastdiv(uint32_t d) {
+  uint32_t l = 0;
+  while ((1ull << l) < d) ++l;
+  const uint64_t m = ((1ull << 32) * ((1ull << l) - d)) / d + 1;
+  return FastDiv{d, static_cast<uint32_t>(m), l};
+}
+
+__device__ __forceinline__ uint32_t fdiv(const FastDiv& f, uint32_t n) {
+  return static_cast<uint32_t>((static_cast<uint64_t>(__umulhi(f.m, n)) + n) >> f.l);
+}
+
+template <int OUTK, int N>
+__device__ __forceinline__ void store_vec(const PrepParams& p, long long oidx, const float (&v)[N]) {
+  static_assert(N == 4 || N == 8, "4 or 8 channels");
+  if (OUTK == kPrepOutF32) {
+    float4* o = reinterpret_cast<float4*>(static_cast<float*>(p.out) + oidx);
+#pragma unroll
+    for (int i = 0; i < N / 4; ++i) o[i] = make_float4(v[4 * i], v[4 * i + 1], v[4 * i + 2], v[4 * i + 3]);
+  } else {
+    uint32_t hw[N / 2], lw[N / 2];
+#pragma unroll
+    for (int i = 0; i < N / 2; ++i) {
+      if (OUTK == kPrepOutBF16) {
+        __nv_bfloat162 h = __floats2bfloat162_rn(v[2 * i], v[2 * i + 1]);
+        hw[i] = *reinterpret_cast<uint32_t*>(&h);
+      } else {
+        const __half h0 = __float2half_rn(v[2 * i]);
+        const __half h1 = __float2half_rn(v[2 * i + 1]);
+        hw[i] = static_cast<uint32_t>(__half_as_ushort(h0)) | (static_cast<uint32_t>(__half_as_ushort(h1)) << 16);
+        if (OUTK == kPrepOutSplitF16) {
+          const __half l0 = __float2half_rn((v[2 * i] - __half2float(h0)) * 2048.f);
+          const __half l1 = __float2half_rn((v[2 * i + 1] - __half2float(h1)) * 2048.f);
+          lw[i] = static_cast<uint32_t>(__half_as_ushort(l0)) | (static_cast<uint32_t>(__half_as_ushort(l1)) << 16);
+        }
+      }
+    }
+    uint16_t* o = static_cast<uint16_t*>(p.out) + oidx;
+    if constexpr (N == 8) {
+      *reinterpret_cast<uint4*>(o) = make_uint4(hw[0], hw[1], hw[2], hw[3]);
+      if (OUTK == kPrepOutSplitF16)
+        *reinterpret_cast<uint4*>(static_cast<uint16_t*>(p.out_lo) + oidx) = make_uint4(lw[0], lw[1], lw[2], lw[3]);
+    } else {
+      *reinterpret_cast<uint2*>(o) = make_uint2(hw[0], hw[1]);
+      if (OUTK == kPrepOutSplitF16)
+        *reinterpret_cast<uint2*>(static_cast<uint16_t*>(p.out_lo) + oidx) = make_uint2(lw[0], lw[1]);
+    }
+  }
+}
+
+// N consecutive fp32 channels [c0, c0 + N) of the virtual concat at one voxel
+// (the concat boundary and the channel count are multiples of N; past the
+// channels the value is 0).
+template <int N>
+__device__ __forceinline__ void load_vec(const PrepParams& p, int ctot, long long vox, int c0, float (&v)[N]) {
+  if (c0 >= ctot) {
+#pragma unroll
+    for (int i = 0; i < N; ++i) v[i] = 0.f;
+    return;
+  }
+  const bool in1 = c0 >= p.src[0].channels;
+  const PrepSource& s = p.src[in1 ? 1 : 0];
+  const float4* q = reinterpret_cast<const float4*>(static_cast<const float*>(s.ptr) + vox * s.cstride +
+                                                    (in1 ? c0 - p.src[0].channels : c0));
+#pragma unroll
+  for (int i = 0; i < N / 4; ++i) {
+    const float4 a = __ldg(q + i);
+    v[4 * i] = a.x;
+    v[4 * i + 1] = a.y;
+    v[4 * i + 2] = a.z;
+    v[4 * i + 3] = a.w;
+  }
+}
+
+// Copy mode, 8 channels per item, two items in flight per thread; batch item
+// on grid y. Preconditions (checked by the launcher): fp32 sources, channel
+// counts, strides and cpad multiples of 8, 16-byte aligned rows.
+template <int OUTK, bool FAST>
+__global__ void __launch_bounds__(256) prepare_copy_kernel(const PrepParams p, const FastDiv qdiv,
+                                                           const unsigned vox) {
+  const int b = blockIdx.y;
+  const int ctot = p.src[0].channels + p.src[1].channels;
+  const unsigned items = vox * qdiv.d;
+  const long long bvox = static_cast<long long>(b) * vox;
+  const unsigned step = gridDim.x * blockDim.x;
+  for (unsigned base = blockIdx.x * blockDim.x + threadIdx.x; base < items; base += 2 * step) {
+    float r[2][8];
+    int c0[2];
+    unsigned v[2];
+#pragma unroll
+    for (int k = 0; k < 2; ++k) {
+      const unsigned item = base + k * step;
+      v[k] = fdiv(qdiv, item);
+      c0[k] = static_cast<int>(item - v[k] * qdiv.d) * 8;
+      if (item < items) load_vec<8>(p, ctot, bvox + v[k], c0[k], r[k]);
+    }
+#pragma unroll
+    for (int k = 0; k < 2; ++k) {
+      if (base + k * step >= items) break;
+      if (c0[k] < ctot) {
+        if (p.affine != nullptr) {
+          const float4* a = reinterpret_cast<const float4*>(p.affine + (static_cast<long long>(b) * ctot + c0[k]) * 2);
+#pragma unroll
+          for (int i = 0; i < 4; ++i) {
+            const float4 q = __ldg(a + i);
+            r[k][2 * i] = fmaf(r[k][2 * i], q.x, q.y);
+            r[k][2 * i + 1] = fmaf(r[k][2 * i + 1], q.z, q.w);
+          }
+        }
+        if (p.silu) {
+#pragma unroll
+          for (int i = 0; i < 8; ++i) r[k][i] = silu_f<FAST>(r[k][i]);
+        }
+      }
+      store_vec<OUTK, 8>(p, (bvox + v[k]) * p.out_cstride + c0[k], r[k]);
+    }
+  }
+}
+
+// Trilinear 2x (half-pixel, clamped; no transform), 4 channels per item and a
+// 2 (h) x 2 (w) output block per thread at one output depth: the block reads a
+// 2 x 3 x 3 source neighbourhood (4.5 loads per output instead of 8). Each
+// output uses exactly the source pair and weight of tri_axis and the same lerp
+// order (w, then h, then d) as the general path, so results are bitwise equal.
+template <int OUTK>
+__global__ void __launch_bounds__(128) prepare_tri_kernel(const PrepParams p, const FastDiv qdiv, const FastDiv xdiv,
+                                                          const FastDiv ydiv, const unsigned items) {
+  const int b = blockIdx.y;
+  const int ctot = p.src[0].channels + p.src[1].channels;
+  const long long bsrc = static_cast<long long>(b) * p.sd * p.sh * p.sw;
+  const long long bout = static_cast<long long>(b) * p.od * p.oh * p.ow;
+  for (unsigned item = blockIdx.x * blockDim.x + threadIdx.x; item < items; item += gridDim.x * blockDim.x) {
+    const unsigned r1 = fdiv(qdiv, item);
+    const int c0 = static_cast<int>(item - r1 * qdiv.d) * 4;
+    const unsigned r2 = fdiv(xdiv, r1);
+    const int xi = static_cast<int>(r1 - r2 * xdiv.d);  // source w index = output w pair
+    const unsigned z = fdiv(ydiv, r2);
+    const int yj = static_cast<int>(r2 - z * ydiv.d);   // source h index = output h pair
+    int z0, z1;
+    float az;
+    tri_axis(static_cast<int>(z), p.sd, z0, z1, az);
+    const int xs[3] = {max(xi - 1, 0), xi, min(xi + 1, p.sw - 1)};
+    const int ys[3] = {max(yj - 1, 0), yj, min(yj + 1, p.sh - 1)};
+    // Output pair element e (0: 2i, 1: 2i + 1) uses slots (lo, hi) and weight a:
+    // e = 0: (0, 1, 0.75) for i >= 1, (1, 2, 0) for i = 0; e = 1: (1, 2, 0.25).
+    int xo[2], yo[2];
+    float ax[2], ay[2];
+    {
+      int i0, i1;
+      tri_axis(2 * xi, p.sw, i0, i1, ax[0]);
+      tri_axis(2 * xi + 1, p.sw, i0, i1, ax[1]);
+      tri_axis(2 * yj, p.sh, i0, i1, ay[0]);
+      tri_axis(2 * yj + 1, p.sh, i0, i1, ay[1]);
+      xo[0] = xi >= 1 ? 0 : 1;
+      xo[1] = 1;
+      yo[0] = yj >= 1 ? 0 : 1;
+      yo[1] = 1;
+    }
+    float o[2][2][4];  // [h pair][w pair][channel]
+    float zr[2][2][2][4];  // [z][h pair][w pair] after the w and h lerps
+#pragma unroll
+    for (int zi = 0; zi < 2; ++zi) {
+      const int zz = zi == 0 ? z0 : z1;
+      float s[3][3][4];
+#pragma unroll
+      for (int a = 0; a < 3; ++a)
+#pragma unroll
+        for (int c = 0; c < 3; ++c)
+          load_vec<4>(p, ctot, bsrc + (static_cast<long long>(zz) * p.sh + ys[a]) * p.sw + xs[c], c0, s[a][c]);
+      // w lerps for every source row, both output w elements.
+      float wl[3][2][4];
+#pragma unroll
+      for (int a = 0; a < 3; ++a)
+#pragma unroll
+        for (int e = 0; e < 2; ++e)
+#pragma unroll
+          for (int ch = 0; ch < 4; ++ch) {
+            const float lo = xo[e] == 0 ? s[a][0][ch] : s[a][1][ch];
+            const float hi = xo[e] == 0 ? s[a][1][ch] : s[a][2][ch];
+            wl[a][e][ch] = lerp_ref(lo, hi, ax[e]);
+          }
+#pragma unroll
+      for (int f = 0; f < 2; ++f)
+#pragma unroll
+        for (int e = 0; e < 2; ++e)
+#pragma unroll
+          for (int ch = 0; ch < 4; ++ch) {
+            const float lo = yo[f] == 0 ? wl[0][e][ch] : wl[1][e][ch];
+            const float hi = yo[f] == 0 ? wl[1][e][ch] : wl[2][e][ch];
+            zr[zi][f][e][ch] = lerp_ref(lo, hi, ay[f]);
+          }
+    }
+#pragma unroll
+    for (int f = 0; f < 2; ++f)
+#pragma unroll
+      for (int e = 0; e < 2; ++e)
+#pragma unroll
+        for (int ch = 0; ch < 4; ++ch) o[f][e][ch] = lerp_ref(zr[0][f][e][ch], zr[1][f][e][ch], az);
+#pragma unroll
+    for (int f = 0; f < 2; ++f)
+#pragma unroll
+      for (int e = 0; e < 2; ++e) {
+        const long long ov = bout + (static_cast<long long>(z) * p.oh + 2 * yj + f) * p.ow + 2 * xi + e;
+        store_vec<OUTK, 4>(p, ov * p.out_cstride + c0, o[f][e]);
+      }
+  }
+}
+
+bool aligned16(const void* q) { return (reinterpret_cast<uintptr_t>(q) & 15) == 0; }
+
+// Whether the vectorised paths apply: fp32 sources whose channel counts,
+// strides and row starts allow `vec`-channel loads, and an output whose rows
+// take vec-channel stores.
+bool vec_ok(const PrepParams& p, int vec) {
+  for (int i = 0; i < 2; ++i) {
+    const PrepSource& s = p.src[i];
+    if (s.channels == 0) continue;
+    if (s.bf16 || s.channels % vec || s.cstride % 4 || !aligned16(s.ptr)) return false;
+  }
+  const int obytes = p.out_kind == kPrepOutF32 ? 4 : 2;
+  if (p.cpad % vec || (p.out_cstride * obytes) % 16 || !aligned16(p.out)) return false;
+  if (p.out_kind == kPrepOutSplitF16 && !aligned16(p.out_lo)) return false;
+  if (p.affine != nullptr && !aligned16(p.affine)) return false;
+  return true;
+}
+
+cudaError_t launch_copy_fast(const PrepParams& p, cudaStream_t stream) {
+  const unsigned vox = static_cast<unsigned>(static_cast<long long>(p.od) * p.oh * p.ow);
+  const FastDiv q = make_fastdiv(static_cast<uint32_t>(p.cpad / 8));
+  const long long items = static_cast<long long>(vox) * q.d;
+  long long blocks = (items + 511) / 512;
+  const long long cap = 148LL * 8 / p.batch + 1;
+  if (blocks > cap) blocks = cap;
+  const dim3 grid(static_cast<unsigned>(blocks), static_cast<unsigned>(p.batch));
+  switch (p.out_kind) {
+    case kPrepOutBF16: prepare_copy_kernel<kPrepOutBF16, true><<<grid, 256, 0, stream>>>(p, q, vox); break;
+    case kPrepOutF16: prepare_copy_kernel<kPrepOutF16, true><<<grid, 256, 0, stream>>>(p, q, vox); break;
+    case kPrepOutSplitF16: prepare_copy_kernel<kPrepOutSplitF16, false><<<grid, 256, 0, stream>>>(p, q, vox); break;
+    default: prepare_copy_kernel<kPrepOutF32, false><<<grid, 256, 0, stream>>>(p, q, vox); break;
+  }
+  return cudaGetLastError();
+}
+
+cudaError_t launch_tri_fast(const PrepParams& p, cudaStream_t stream) {
+  const FastDiv q = make_fastdiv(static_cast<uint32_t>(p.cpad / 4));
+  const FastDiv xd = make_fastdiv(static_cast<uint32_t>(p.sw));
+  const FastDiv yd = make_fastdiv(static_cast<uint32_t>(p.sh));
+  const long long items = static_cast<long long>(p.od) * p.sh * p.sw * q.d;
+  long long blocks = (items + 127) / 128;
+  const long long cap = 148LL * 16 / p.batch + 1;
+  if (blocks > cap) blocks = cap;
+  const dim3 grid(static_cast<unsigned>(blocks), static_cast<unsigned>(p.batch));
+  const unsigned n = static_cast<unsigned>(items);
+  switch (p.out_kind) {
+    case kPrepOutBF16: prepare_tri_kernel<kPrepOutBF16><<<grid, 128, 0, stream>>>(p, q, xd, yd, n); break;
+    case kPrepOutF16: prepare_tri_kernel<kPrepOutF16><<<grid, 128, 0, stream>>>(p, q, xd, yd, n); break;
+    case kPrepOutSplitF16: prepare_tri_kernel<kPrepOutSplitF16><<<grid, 128, 0, stream>>>(p, q, xd, yd, n); break;
+    default: prepare_tri_kernel<kPrepOutF32><<<grid, 128, 0, stream>>>(p, q, xd, yd, n); break;
+  }
+  return cudaGetLastError();
+}
+
 }  // namespace
 
 cudaError_t launch_prepare(const PrepParams& p, cudaStream_t stream) {
@@ -289,6 +558,11 @@ cudaError_t launch_prepare(const PrepParams& p, cudaStream_t stream) {
   if (total <= 0) return cudaSuccess;
   if (total >= (1LL << 31) || static_cast<long long>(p.sd) * p.sh * p.sw >= (1LL << 31))
     return cudaErrorInvalidValue;  // the 32-bit item space of prepare_kernel
+  if (p.mode == kPrepCopy && p.od == p.sd && p.oh == p.sh && p.ow == p.sw && vec_ok(p, 8))
+    return launch_copy_fast(p, stream);
+  if (p.mode == kPrepTrilinear && p.affine == nullptr && !p.silu && p.od == 2 * p.sd && p.oh == 2 * p.sh &&
+      p.ow == 2 * p.sw && vec_ok(p, 4))
+    return launch_tri_fast(p, stream);
   const int threads = 256;
   long long blocks = (total + threads - 1) / threads;
   if (blocks > 148LL * 16) blocks = 148LL * 16;

@@ -195,7 +195,10 @@ def test_splitk_reduction_epilogue(cuda, precision):
 @pytest.mark.parametrize(("shape", "out_channels", "silu"), [
     ((2, 64, 5, 12, 40), 4, True),   # UNet out.2 shape class, partial blocks on every axis
     ((1, 64, 8, 16, 16), 1, False),  # VAE decoder output conv
-    ((1, 24, 3, 9, 7), 3, True),     # channels not a multiple of the 8-channel staging slice
+    ((1, 24, 3, 9, 7), 3, True),     # fewer channels than one 32-channel staging slice
+    ((1, 64, 21, 34, 70), 1, True),  # several h / w columns and depth chunks, one output channel
+    ((1, 30, 6, 17, 33), 2, True),   # channels not a multiple of 4 (scalar staging), two outputs
+    ((2, 72, 7, 16, 32), 1, False),  # two staging slices plus a partial one
 ])
 def test_narrow_output_conv(cuda, shape, out_channels, silu):
     """<= 4 output channels run the direct fp32 kernel (GN affine + SiLU applied while staging);
@@ -210,7 +213,7 @@ def test_narrow_output_conv(cuda, shape, out_channels, silu):
     res = torch.from_numpy(rng.standard_normal((b, out_channels, *shape[2:])).astype(np.float32))
     norm_w = torch.from_numpy((1 + 0.1 * rng.standard_normal(c)).astype(np.float32))
     norm_b = torch.from_numpy((0.1 * rng.standard_normal(c)).astype(np.float32))
-    groups = 8
+    groups = 8 if c % 8 == 0 else 2
     xg = ops.to_ndhwc(x.to(cuda))
     affine = ops.group_norm_affine(xg, norm_w.to(cuda), norm_b.to(cuda), groups=groups, eps=1e-6)
     y = ops.conv3d(xg, ops.pack_weight(w.to(cuda), "fp32"), bias.to(cuda), affine=affine, silu=silu,
