@@ -406,10 +406,11 @@ int ctmr_conv3d_stages(const ctmr_conv3d_desc* d, void* workspace, size_t worksp
   }
   if (!(stages & CTMR_CONV_GEMM)) return CTMR_OK;
 
-  // 2a. The persistent atom-shifted kernel for 16-bit stride-1 3x3x3 (and nearest-2x) convolutions.
-  if (!p.exact && !g_v2_unavailable && (p.mode == ctmr::kModeConv3 || p.mode == ctmr::kModeUp2) &&
-      p.row_w >= 16 && p.row_h >= 8 && getenv("CTMR_DISABLE_V2") == nullptr) {
-    const int tw = p.mode == ctmr::kModeConv3 ? 3 : 2;
+  // 2a. The persistent atom-shifted kernel for 16-bit stride-1 3x3x3, nearest-2x and 1x1x1 convolutions.
+  if (!p.exact && !g_v2_unavailable &&
+      (p.mode == ctmr::kModeConv3 || p.mode == ctmr::kModeUp2 || p.mode == ctmr::kModeConv1) && p.row_w >= 16 &&
+      p.row_h >= 8 && getenv("CTMR_DISABLE_V2") == nullptr) {
+    const int tw = p.mode == ctmr::kModeConv3 ? 3 : (p.mode == ctmr::kModeUp2 ? 2 : 1);
     const int mt = p.row_d >= 2 ? 2 : 1;
     const int bn = std::min(p.opad, 128);
     // Largest channel block whose pipeline is at least 3 stages deep (else 2).
@@ -472,7 +473,8 @@ int ctmr_conv3d_stages(const ctmr_conv3d_desc* d, void* workspace, size_t worksp
         if (rs % 16 == 0 &&
             encode_act(&maps.a[0], a_hi, p.bf16, p.cpad, H, W, D, d->batch, W * rs, rs, H * W * rs, D * H * W * rs,
                        kc, 8, 16 + tw - 1, mt) == CTMR_OK &&
-            encode_weight3(&maps.b, d->weight, p.bf16, p.cpad, p.opad, p.mode == ctmr::kModeUp2 ? 64 : 27, kc, bn,
+            encode_weight3(&maps.b, d->weight, p.bf16, p.cpad, p.opad,
+                           p.mode == ctmr::kModeUp2 ? 64 : (p.mode == ctmr::kModeConv1 ? 1 : 27), kc, bn,
                            tw) == CTMR_OK) {
           cudaError_t e = ctmr::launch_conv3d_umma_v2(maps, g, kc, mt, tw, sm_count(), smem2, stream);
           return e == cudaSuccess ? CTMR_OK : cuda_fail(e, "conv3d v2 launch");

@@ -15,9 +15,11 @@
 // double-buffered in TMEM so the epilogue warps drain tile i while the MMA
 // issuer accumulates tile i + 1.
 //
-// Modes: kModeConv3 (TW = 3; stages over (kd, kh)) and kModeUp2 (TW = 2; stages
+// Modes: kModeConv3 (TW = 3; stages over (kd, kh)), kModeUp2 (TW = 2; stages
 // over the (td, th) of each nearest-2x parity, whose taps are the folded
-// weights of pack_weight(upsample=1)).
+// weights of pack_weight(upsample=1)) and kModeConv1 (TW = 1: the 1x1x1
+// convolution, one box per channel block; the kernel is then a persistent
+// streaming GEMM).
 #include <cuda_bf16.h>
 #include <cuda_fp16.h>
 
@@ -49,7 +51,7 @@ __global__ void __launch_bounds__(kThreadsV2, 1)
     conv3d_umma_v2_kernel(const __grid_constant__ ConvMaps maps, const __grid_constant__ ConvGeom g) {
   constexpr uint32_t kRowBytes = KC * 2;
   constexpr int kSteps = KC / 16;
-  constexpr int KDH = TW == 3 ? 9 : 4;  // (kd, kh) or (td, th) pairs per tile
+  constexpr int KDH = TW == 3 ? 9 : (TW == 2 ? 4 : 1);  // (kd, kh) or (td, th) pairs per tile (1x1: one)
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>(ru(smem_u32(smem_raw), 1024) - smem_u32(smem_raw) +
                                              reinterpret_cast<uintptr_t>(smem_raw));
@@ -128,6 +130,11 @@ __global__ void __launch_bounds__(kThreadsV2, 1)
           y = h0 + kh - 1;
           x = w0 - 1;
           btap = kd * 9 + kh * 3;
+        } else if (TW == 1) {
+          z = d0;
+          y = h0;
+          x = w0;
+          btap = 0;
         } else {
           const int td = kdh >> 1, th = kdh & 1;
           z = d0 + pd + td - 1;
@@ -330,6 +337,8 @@ cudaError_t launch_conv3d_umma_v2(const ConvMaps& maps, const ConvGeom& g, int k
   CTMR_V2(64, 1, 3) CTMR_V2(32, 1, 3) CTMR_V2(16, 1, 3)
   CTMR_V2(64, 2, 2) CTMR_V2(32, 2, 2) CTMR_V2(16, 2, 2)
   CTMR_V2(64, 1, 2) CTMR_V2(32, 1, 2) CTMR_V2(16, 1, 2)
+  CTMR_V2(64, 2, 1) CTMR_V2(32, 2, 1) CTMR_V2(16, 2, 1)
+  CTMR_V2(64, 1, 1) CTMR_V2(32, 1, 1) CTMR_V2(16, 1, 1)
 #undef CTMR_V2
   return cudaErrorInvalidValue;
 }

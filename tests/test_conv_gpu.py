@@ -171,6 +171,34 @@ def test_persistent_kernel_shapes(cuda, shape, out_channels, upsample, precision
     assert err <= (FP16_CONV_REL_L2 if precision == "fp16" else BF16_CONV_REL_L2), f"{precision} rel-L2 {err:.3e}"
 
 
+@pytest.mark.parametrize("precision", ["fp16", "bf16"])
+@pytest.mark.parametrize(("shape", "x2_channels", "out_channels"), [
+    ((2, 64, 3, 12, 24), 128, 64),   # skip 1x1 over cat(hidden, skip): partial tiles, two sources
+    ((1, 128, 4, 16, 32), 0, 64),    # VAE shortcut class
+    ((1, 32, 2, 8, 16), 0, 256),     # two N tiles
+])
+def test_persistent_pointwise_conv(cuda, shape, x2_channels, out_channels, precision):
+    """16-bit 1x1x1 convs on grids with W >= 16 and H >= 8 run the persistent kernel (one box per
+    channel block); a virtual concat input, per-batch bias and a residual exercise its paths."""
+    from ctmr_b200 import ops
+
+    rng = np.random.default_rng(31)
+    b, c = shape[:2]
+    x = torch.from_numpy(rng.standard_normal(shape).astype(np.float32))
+    x2 = torch.from_numpy(rng.standard_normal((b, x2_channels, *shape[2:])).astype(np.float32)) if x2_channels else None
+    cin = c + x2_channels
+    w = torch.from_numpy((rng.standard_normal((out_channels, cin, 1, 1, 1)) / np.sqrt(cin)).astype(np.float32))
+    bias = torch.from_numpy(rng.standard_normal((b, out_channels)).astype(np.float32))
+    res = torch.from_numpy(rng.standard_normal((b, out_channels, *shape[2:])).astype(np.float32))
+    y = ops.conv3d(ops.to_ndhwc(x.to(cuda)), ops.pack_weight(w.to(cuda), precision), bias.to(cuda),
+                   x2=ops.to_ndhwc(x2.to(cuda)) if x2 is not None else None, residual=ops.to_ndhwc(res.to(cuda)))
+    torch.cuda.synchronize()
+    xin = torch.cat([x, x2], dim=1) if x2 is not None else x
+    expected = ops_ref.conv3d_ref(xin.double(), w.double(), bias.double(), padding=0) + res.double()
+    err = ops_ref.rel_l2(y.cpu(), expected)
+    assert err <= (FP16_CONV_REL_L2 if precision == "fp16" else BF16_CONV_REL_L2), f"{precision} rel-L2 {err:.3e}"
+
+
 @pytest.mark.parametrize("precision", ["fp32", "fp16"])
 def test_splitk_reduction_epilogue(cuda, precision):
     """A deep, small grid (2 x 256 x 4^3) splits K across CTAs; the reduction adds the
