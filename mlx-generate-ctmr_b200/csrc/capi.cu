@@ -17,6 +17,7 @@
 #include "conv3d_umma.cuh"
 #include "groupnorm.cuh"
 #include "conv3d_narrow.cuh"
+#include "conv3d_tiny.cuh"
 #include "misc.cuh"
 #include "pack.cuh"
 #include "prepare.cuh"
@@ -165,11 +166,15 @@ struct ConvPlan {
   int row_d, row_h, row_w;  // GEMM rows
   int out_d, out_h, out_w;
   bool exact, prepare, bf16, narrow;
+  bool tiny;                // fp32 conv of <= 4 input channels: direct FMA kernel
+  bool im2col;              // tiny-input 3x3x3 conv run as a 1x1x1 conv of its im2col rows
+  int cin_raw, cpad_src;    // im2col: input channels and the packed weights' channel padding
   size_t prep_bytes;        // per plane
+  size_t wrep_bytes;        // im2col: repacked weights, per plane
   // per-tap kernel tiling and its split-K
   int tile_w, tile_h, tile_d, tiles_w, tiles_h, tiles_d, n_tiles, ksplit;
   size_t part_bytes;
-  size_t workspace() const { return prep_bytes * (exact ? 2 : 1) + part_bytes; }
+  size_t workspace() const { return (prep_bytes + wrep_bytes) * (exact ? 2 : 1) + part_bytes; }
 };
 
 int plan_conv(const ctmr_conv3d_desc* d, ConvPlan* p) {
@@ -249,7 +254,26 @@ int plan_conv(const ctmr_conv3d_desc* d, ConvPlan* p) {
               d->x.dtype == CTMR_DTYPE_F32 && (d->residual.data == nullptr || d->residual.dtype == CTMR_DTYPE_F32) &&
               d->y_dtype == CTMR_DTYPE_F32 && ctmr::narrow_conv_supported(p->cin, d->out_channels) &&
               getenv("CTMR_DISABLE_NARROW") == nullptr;
-  p->prepare = !direct && !p->narrow;
+  // Inputs of at most 4 channels (the UNet / ControlNet / VAE conv_in on the 4-channel latent):
+  // im2col rows of 27 * C columns instead of 27 taps of 16 mostly-zero channels.
+  // In the fp32 mode they run a direct FMA kernel (108 products per output need no tensor cores).
+  p->tiny = !p->narrow && p->exact && p->mode == ctmr::kModeConv3 && p->cin <= 4 && !d->trilinear && !d->avgpool &&
+            d->x2.data == nullptr && d->x.dtype == CTMR_DTYPE_F32 &&
+            (d->residual.data == nullptr || (d->residual.dtype == CTMR_DTYPE_F32 && !d->residual_upsampled)) &&
+            d->y_dtype == CTMR_DTYPE_F32 && getenv("CTMR_DISABLE_TINY") == nullptr;
+  p->im2col = !p->narrow && !p->tiny && p->mode == ctmr::kModeConv3 && p->cin <= 4 && !d->trilinear &&
+              !d->avgpool && d->x2.data == nullptr && getenv("CTMR_DISABLE_IM2COL") == nullptr;
+  p->cin_raw = p->cin;
+  p->cpad_src = p->cpad;
+  p->wrep_bytes = 0;
+  if (p->im2col) {
+    p->mode = ctmr::kModeConv1;
+    p->taps = 1;
+    p->cpad = static_cast<int>(round_up(27 * p->cin, 16));
+    p->kc = p->cpad % 64 == 0 ? 64 : (p->cpad % 32 == 0 ? 32 : 16);
+    p->wrep_bytes = static_cast<size_t>(round_up(static_cast<long long>(p->opad) * p->cpad * 2, 256));
+  }
+  p->prepare = (!direct || p->im2col) && !p->narrow && !p->tiny;
   p->prep_bytes = p->prepare ? static_cast<size_t>(round_up(static_cast<long long>(d->batch) * p->in_d * p->in_h *
                                                                 p->in_w * p->cpad * 2,
                                                             256))
@@ -281,7 +305,7 @@ int plan_conv(const ctmr_conv3d_desc* d, ConvPlan* p) {
                                       p->n_tiles * p->bn * sizeof(float)
                                 : 0;
   p->part_bytes = static_cast<size_t>(round_up(static_cast<long long>(p->part_bytes), 256));
-  if (p->narrow) p->part_bytes = 0;
+  if (p->narrow || p->tiny) p->part_bytes = 0;
   return CTMR_OK;
 }
 
@@ -376,6 +400,28 @@ int ctmr_conv3d_stages(const ctmr_conv3d_desc* d, void* workspace, size_t worksp
     cudaError_t e = ctmr::launch_narrow_conv(np, stream);
     return e == cudaSuccess ? CTMR_OK : cuda_fail(e, "narrow conv launch");
   }
+  if (p.tiny) {
+    if (!(stages & CTMR_CONV_GEMM)) return CTMR_OK;
+    ctmr::TinyParams tp{};
+    tp.x = d->x.data;
+    tp.x_cstride = d->x.cstride;
+    tp.vec4 = (d->x.cstride % 4 == 0) && (reinterpret_cast<uintptr_t>(d->x.data) % 16 == 0);
+    tp.batch = d->batch, tp.d = d->depth, tp.h = d->height, tp.w = d->width;
+    tp.cin = p.cin, tp.cout = d->out_channels;
+    tp.affine = d->affine;
+    tp.silu = d->silu;
+    tp.w_hi = static_cast<const __half*>(d->weight);
+    tp.w_lo = static_cast<const __half*>(d->weight_lo);
+    tp.opad = p.opad, tp.cpad = p.cpad;
+    tp.bias = d->bias;
+    tp.bias_bstride = d->bias_per_batch ? d->out_channels : 0;
+    tp.res = static_cast<const float*>(d->residual.data);
+    tp.res_cstride = d->residual.cstride;
+    tp.y = static_cast<float*>(d->y) + d->y_coffset;
+    tp.y_cstride = d->y_cstride;
+    cudaError_t e = ctmr::launch_tiny_conv(tp, stream);
+    return e == cudaSuccess ? CTMR_OK : cuda_fail(e, "tiny-input conv launch");
+  }
 
   // 1. Operand preparation (affine, SiLU, trilinear / avgpool, concat, cast or split).
   const void* a_hi = d->x.data;
@@ -386,7 +432,32 @@ int ctmr_conv3d_stages(const ctmr_conv3d_desc* d, void* workspace, size_t worksp
     a_lo = p.exact ? static_cast<uint8_t*>(workspace) + p.prep_bytes : nullptr;
     a_cstride = p.cpad;
   }
-  if (p.prepare && (stages & CTMR_CONV_PREPARE)) {
+  // im2col: repacked weights after the prepared planes.
+  const void* w_hi = d->weight;
+  const void* w_lo = d->weight_lo;
+  if (p.im2col) {
+    uint8_t* wr = static_cast<uint8_t*>(workspace) + p.prep_bytes * (p.exact ? 2 : 1);
+    w_hi = wr;
+    w_lo = p.exact ? wr + p.wrep_bytes : nullptr;
+  }
+  if (p.im2col && (stages & CTMR_CONV_PREPARE)) {
+    ctmr::PrepParams pp{};
+    pp.src[0] = as_source(d->x);
+    pp.batch = d->batch;
+    pp.sd = pp.od = d->depth, pp.sh = pp.oh = d->height, pp.sw = pp.ow = d->width;
+    pp.affine = d->affine;
+    pp.silu = d->silu;
+    pp.cpad = p.cpad;
+    pp.out_cstride = p.cpad;
+    pp.out_kind = p.exact ? ctmr::kPrepOutSplitF16 : (p.bf16 ? ctmr::kPrepOutBF16 : ctmr::kPrepOutF16);
+    pp.out = workspace;
+    pp.out_lo = p.exact ? static_cast<uint8_t*>(workspace) + p.prep_bytes : nullptr;
+    cudaError_t e = ctmr::launch_im2col(pp, p.cin_raw, p.cpad, stream);
+    if (e != cudaSuccess) return cuda_fail(e, "im2col launch");
+    e = ctmr::launch_repack_im2col(d->weight, p.exact ? d->weight_lo : nullptr, p.opad, p.cpad_src, p.cin_raw,
+                                   p.cpad, const_cast<void*>(w_hi), const_cast<void*>(w_lo), stream);
+    if (e != cudaSuccess) return cuda_fail(e, "im2col weight repack launch");
+  } else if (p.prepare && (stages & CTMR_CONV_PREPARE)) {
     ctmr::PrepParams pp{};
     pp.src[0] = as_source(d->x);
     pp.src[1] = as_source(d->x2);
@@ -473,7 +544,7 @@ int ctmr_conv3d_stages(const ctmr_conv3d_desc* d, void* workspace, size_t worksp
         if (rs % 16 == 0 &&
             encode_act(&maps.a[0], a_hi, p.bf16, p.cpad, H, W, D, d->batch, W * rs, rs, H * W * rs, D * H * W * rs,
                        kc, 8, 16 + tw - 1, mt) == CTMR_OK &&
-            encode_weight3(&maps.b, d->weight, p.bf16, p.cpad, p.opad,
+            encode_weight3(&maps.b, w_hi, p.bf16, p.cpad, p.opad,
                            p.mode == ctmr::kModeUp2 ? 64 : (p.mode == ctmr::kModeConv1 ? 1 : 27), kc, bn,
                            tw) == CTMR_OK) {
           cudaError_t e = ctmr::launch_conv3d_umma_v2(maps, g, kc, mt, tw, sm_count(), smem2, stream);
@@ -491,7 +562,8 @@ int ctmr_conv3d_stages(const ctmr_conv3d_desc* d, void* workspace, size_t worksp
   g.tile_w = p.tile_w, g.tile_h = p.tile_h, g.tile_d = p.tile_d;
   g.tiles_w = p.tiles_w, g.tiles_h = p.tiles_h, g.tiles_d = p.tiles_d;
   g.ksplit = p.ksplit;
-  g.partial = p.ksplit > 1 ? reinterpret_cast<float*>(static_cast<uint8_t*>(workspace) + p.prep_bytes * (p.exact ? 2 : 1))
+  g.partial = p.ksplit > 1 ? reinterpret_cast<float*>(static_cast<uint8_t*>(workspace) +
+                                                      (p.prep_bytes + p.wrep_bytes) * (p.exact ? 2 : 1))
                            : nullptr;
   g.part_cstride = p.n_tiles * p.bn;
   g.phases = p.phases;
@@ -551,10 +623,10 @@ int ctmr_conv3d_stages(const ctmr_conv3d_desc* d, void* workspace, size_t worksp
     }
   }
   const long long wtaps = p.mode == ctmr::kModeUp2 ? 64 : p.taps;
-  st = encode_weight(&maps.b, d->weight, bf16, p.cpad, p.opad, wtaps, p.kc, p.bn);
+  st = encode_weight(&maps.b, w_hi, bf16, p.cpad, p.opad, wtaps, p.kc, p.bn);
   if (st) return st;
   if (p.exact) {
-    st = encode_weight(&maps.b_lo, d->weight_lo, bf16, p.cpad, p.opad, wtaps, p.kc, p.bn);
+    st = encode_weight(&maps.b_lo, w_lo, bf16, p.cpad, p.opad, wtaps, p.kc, p.bn);
     if (st) return st;
   }
 

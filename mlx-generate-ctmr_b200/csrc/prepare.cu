@@ -547,6 +547,70 @@ cudaError_t launch_tri_fast(const PrepParams& p, cudaStream_t stream) {
   return cudaGetLastError();
 }
 
+// ---------------------------------------------------------------- im2col for tiny inputs
+// A 3x3x3 stride-1 convolution of a C <= 4 channel input as a 1x1x1 convolution
+// of its im2col expansion: row v holds transform(x[v + tap])[c] at column
+// tap * C + c (tap = kd * 9 + kh * 3 + kw, zero outside the volume and past
+// 27 * C up to kdense), so the GEMM's K is 27 * C rounded up to 16 instead of
+// 27 taps x 16 padded channels.
+template <int OUTK>
+__global__ void __launch_bounds__(256) im2col_kernel(const PrepParams p, const int cin, const int kdense) {
+  const int b = blockIdx.y;
+  const unsigned vox = static_cast<unsigned>(p.od) * p.oh * p.ow;
+  const int chunks = kdense / 8;
+  const unsigned items = vox * static_cast<unsigned>(chunks);
+  const PrepSource& s = p.src[0];
+  for (unsigned item = blockIdx.x * blockDim.x + threadIdx.x; item < items; item += gridDim.x * blockDim.x) {
+    const unsigned v = item / static_cast<unsigned>(chunks);
+    const int k0 = static_cast<int>(item - v * static_cast<unsigned>(chunks)) * 8;
+    const int x = static_cast<int>(v % static_cast<unsigned>(p.ow));
+    const unsigned yz = v / static_cast<unsigned>(p.ow);
+    const int y = static_cast<int>(yz % static_cast<unsigned>(p.oh));
+    const int z = static_cast<int>(yz / static_cast<unsigned>(p.oh));
+    float out[8];
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      const int k = k0 + i;
+      const int tap = k / cin, c = k - tap * cin;
+      float t = 0.f;
+      if (tap < 27) {
+        const int gz = z + tap / 9 - 1, gy = y + (tap / 3) % 3 - 1, gx = x + tap % 3 - 1;
+        if (gz >= 0 && gz < p.od && gy >= 0 && gy < p.oh && gx >= 0 && gx < p.ow) {
+          const long long src = ((static_cast<long long>(b) * p.od + gz) * p.oh + gy) * p.ow + gx;
+          t = load_ch(s.ptr, s.bf16, src * s.cstride + c);
+          if (p.affine != nullptr) {
+            const float* a = p.affine + (static_cast<long long>(b) * cin + c) * 2;
+            t = fmaf(t, __ldg(a), __ldg(a + 1));
+          }
+          if (p.silu) t = silu_f<false>(t);
+        }
+      }
+      out[i] = t;
+    }
+    store_vec<OUTK, 8>(p, (static_cast<long long>(b) * vox + v) * p.out_cstride + k0, out);
+  }
+}
+
+// Packed weights [27][opad][cpad_src] (hi and, for the split kind, lo) ->
+// [opad][kdense] with column tap * cin + c, zero past 27 * cin.
+__global__ void repack_im2col_kernel(const uint16_t* __restrict__ hi, const uint16_t* __restrict__ lo, int opad,
+                                     int cpad_src, int cin, int kdense, uint16_t* __restrict__ out_hi,
+                                     uint16_t* __restrict__ out_lo) {
+  const int n = opad * kdense;
+  for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < n; i += gridDim.x * blockDim.x) {
+    const int o = i / kdense, k = i - o * kdense;
+    const int tap = k / cin, c = k - tap * cin;
+    uint16_t h = 0, l = 0;
+    if (tap < 27) {
+      const long long src = (static_cast<long long>(tap) * opad + o) * cpad_src + c;
+      h = hi[src];
+      if (lo != nullptr) l = lo[src];
+    }
+    out_hi[i] = h;
+    if (out_lo != nullptr) out_lo[i] = l;
+  }
+}
+
 }  // namespace
 
 cudaError_t launch_prepare(const PrepParams& p, cudaStream_t stream) {
@@ -580,6 +644,36 @@ cudaError_t launch_prepare(const PrepParams& p, cudaStream_t stream) {
     CTMR_PREP(kPrepCopy)
   }
 #undef CTMR_PREP
+  return cudaGetLastError();
+}
+
+}  // namespace ctmr
+
+namespace ctmr {
+
+cudaError_t launch_im2col(const PrepParams& p, int cin, int kdense, cudaStream_t stream) {
+  if (cin < 1 || cin > 4 || kdense % 8 || kdense < 27 * cin || p.out_cstride % 8) return cudaErrorInvalidValue;
+  const long long items = static_cast<long long>(p.od) * p.oh * p.ow * (kdense / 8);
+  if (items >= (1LL << 31)) return cudaErrorInvalidValue;
+  long long blocks = (items + 255) / 256;
+  const long long cap = 148LL * 8 / p.batch + 1;
+  if (blocks > cap) blocks = cap;
+  const dim3 grid(static_cast<unsigned>(blocks), static_cast<unsigned>(p.batch));
+  switch (p.out_kind) {
+    case kPrepOutBF16: im2col_kernel<kPrepOutBF16><<<grid, 256, 0, stream>>>(p, cin, kdense); break;
+    case kPrepOutF16: im2col_kernel<kPrepOutF16><<<grid, 256, 0, stream>>>(p, cin, kdense); break;
+    case kPrepOutSplitF16: im2col_kernel<kPrepOutSplitF16><<<grid, 256, 0, stream>>>(p, cin, kdense); break;
+    default: return cudaErrorInvalidValue;
+  }
+  return cudaGetLastError();
+}
+
+cudaError_t launch_repack_im2col(const void* hi, const void* lo, int opad, int cpad_src, int cin, int kdense,
+                                 void* out_hi, void* out_lo, cudaStream_t stream) {
+  const int n = opad * kdense;
+  repack_im2col_kernel<<<(n + 255) / 256, 256, 0, stream>>>(
+      static_cast<const uint16_t*>(hi), static_cast<const uint16_t*>(lo), opad, cpad_src, cin, kdense,
+      static_cast<uint16_t*>(out_hi), static_cast<uint16_t*>(out_lo));
   return cudaGetLastError();
 }
 

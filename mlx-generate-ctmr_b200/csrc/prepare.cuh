@@ -32,4 +32,11 @@ struct PrepParams {
 
 cudaError_t launch_prepare(const PrepParams& p, cudaStream_t stream);
 
+// im2col expansion of a stride-1 3x3x3 convolution input with cin <= 4 channels
+// (src[0] only; od/oh/ow is the grid) into kdense-column rows, and the matching
+// repack of [27][opad][cpad_src] packed weights into [opad][kdense].
+cudaError_t launch_im2col(const PrepParams& p, int cin, int kdense, cudaStream_t stream);
+cudaError_t launch_repack_im2col(const void* hi, const void* lo, int opad, int cpad_src, int cin, int kdense,
+                                 void* out_hi, void* out_lo, cudaStream_t stream);
+
 }  // namespace ctmr

@@ -200,6 +200,42 @@ def test_persistent_pointwise_conv(cuda, shape, x2_channels, out_channels, preci
 
 
 @pytest.mark.parametrize("precision", ["fp32", "fp16"])
+@pytest.mark.parametrize(("shape", "out_channels", "norm"), [
+    ((2, 4, 8, 16, 12), 64, False),   # the UNet / ControlNet conv_in class
+    ((1, 4, 5, 7, 9), 256, False),    # the VAE decoder conv_in class, two N tiles, odd extents
+    ((1, 3, 4, 6, 8), 32, True),      # 3 channels with group-norm affine + SiLU
+    ((1, 1, 3, 5, 4), 16, False),     # one channel
+])
+def test_tiny_input_im2col(cuda, shape, out_channels, norm, precision):
+    """3x3x3 convs of <= 4 input channels: the fp32 mode runs the direct FMA kernel, the 16-bit
+    modes a 1x1x1 GEMM over im2col rows of 27 * C columns."""
+    from ctmr_b200 import ops
+
+    rng = np.random.default_rng(37)
+    b, c = shape[:2]
+    x = torch.from_numpy(rng.standard_normal(shape).astype(np.float32))
+    w = torch.from_numpy((rng.standard_normal((out_channels, c, 3, 3, 3)) / np.sqrt(27 * c)).astype(np.float32))
+    bias = torch.from_numpy(rng.standard_normal(out_channels).astype(np.float32))
+    res = torch.from_numpy(rng.standard_normal((b, out_channels, *shape[2:])).astype(np.float32))
+    kw = {}
+    xin = x.double()
+    if norm:
+        affine = torch.from_numpy(np.stack([1 + 0.2 * rng.standard_normal((b, c)), 0.3 * rng.standard_normal((b, c))],
+                                           axis=-1).astype(np.float32))
+        kw = {"affine": affine.to(cuda), "silu": True}
+        a = affine.double()
+        xin = ops_ref.silu_ref(xin * a[..., 0][..., None, None, None] + a[..., 1][..., None, None, None])
+    y = ops.conv3d(ops.to_ndhwc(x.to(cuda)), ops.pack_weight(w.to(cuda), precision), bias.to(cuda),
+                   residual=ops.to_ndhwc(res.to(cuda)), **kw)
+    torch.cuda.synchronize()
+    expected = ops_ref.conv3d_ref(xin, w.double(), bias.double()) + res.double()
+    if precision == "fp32":
+        _close_fp32(y, expected)
+    else:
+        assert ops_ref.rel_l2(y.cpu(), expected) <= FP16_CONV_REL_L2
+
+
+@pytest.mark.parametrize("precision", ["fp32", "fp16"])
 def test_splitk_reduction_epilogue(cuda, precision):
     """A deep, small grid (2 x 256 x 4^3) splits K across CTAs; the reduction adds the
     per-batch bias and the residual before the single rounding."""
