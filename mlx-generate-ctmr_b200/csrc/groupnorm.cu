@@ -118,6 +118,23 @@ __global__ void __launch_bounds__(kGnThreads) gn_partial_kernel(const GnParams p
       n = 1.f;
       v += lanes;
     }
+    // Four voxels per step, all loads issued before any accumulation.
+    for (; v + 3 * lanes < v_end; v += 4 * lanes) {
+      float x[4][8];
+      int cnt;
+#pragma unroll
+      for (int k = 0; k < 4; ++k) gn_load8(p, base + v + k * lanes, slice * 8, x[k], cnt);
+#pragma unroll
+      for (int k = 0; k < 4; ++k) {
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+          const float d = x[k][i] - pivot[i];
+          s[i] += d;
+          q[i] = fmaf(d, d, q[i]);
+        }
+      }
+      n += 4.f;
+    }
     for (; v < v_end; v += lanes) {
       float x[8];
       int cnt;
@@ -249,9 +266,10 @@ __global__ void __launch_bounds__(kFinThreads) gn_finalize_kernel(const GnParams
 
 int gn_max_chunks(int batch) { return (2 * 296 + batch - 1) / batch; }
 
-// About 128 KB of input per block, at least 16 voxels, at most ~600 blocks in all.
+// About 32 KB of input per block (small tensors still spread over many SMs), at
+// least 16 voxels, at most ~600 blocks in all.
 int gn_chunks_for(int batch, long long voxels, int channels) {
-  long long chunks = (voxels * channels * 4 + (128 << 10) - 1) / (128 << 10);
+  long long chunks = (voxels * channels * 4 + (32 << 10) - 1) / (32 << 10);
   if (chunks > gn_max_chunks(batch)) chunks = gn_max_chunks(batch);
   if (chunks > (voxels + 15) / 16) chunks = (voxels + 15) / 16;
   if (chunks < 1) chunks = 1;
