@@ -302,6 +302,21 @@ def run_case(args) -> None:
                 step._step()
             if args.case == "breakdown":
                 _profile_pass("unet-step", step._step, dev)
+                graphed = P.GuidedUNetStep(w, P.PRODUCTION_UNET, LATENT, class_label=MODALITY,
+                                           spacing=P.image_spacing_tensor(SPACING, dev), guidance_scale=GUIDANCE,
+                                           device=dev, use_cuda_graph=True)
+                graphed.prepare()
+                start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                for _ in range(3):
+                    graphed.graph.replay()
+                start.record()
+                for _ in range(10):
+                    graphed.graph.replay()
+                end.record()
+                torch.cuda.synchronize(dev)
+                print(json.dumps({"part": "unet-step", "graph_replay_ms": round(start.elapsed_time(end) / 10, 3),
+                                  "launches_per_step": graphed.launches_per_step}), flush=True)
+                graphed.release()
         if args.case in ("vae-window", "breakdown"):
             w = W.random_weights(W.vae_decoder_shapes(P.PRODUCTION_VAE), seed=1, device=dev)
             from ctmr_b200 import networks
