@@ -296,8 +296,15 @@ int plan_conv(const ctmr_conv3d_desc* d, ConvPlan* p) {
                          p->n_tiles;
   const int n_iter = p->taps * (p->cpad / p->kc);
   p->ksplit = 1;
-  if (p->mode != ctmr::kModeUp2 && ctas < 120) {
-    long long want = (2 * 148 + ctas - 1) / ctas;
+  // Resident CTAs per SM of the per-tap kernel (its shared-memory plan; a TMEM
+  // footprint above 256 columns forces one), so that the split grid is one wave.
+  size_t smem_probe = 0;
+  const int tcols = std::max(32, next_pow2(p->bn * (p->exact ? 3 : 1)));
+  const int stages_probe = ctmr::conv_stage_plan(p->kc, p->bn, p->exact, tcols > 256, &smem_probe);
+  const int per_sm = (stages_probe >= 2 && smem_probe + 1024 <= 114 * 1024) ? 2 : 1;
+  const long long wave = 148LL * per_sm;
+  if (p->mode != ctmr::kModeUp2 && ctas < 148) {
+    long long want = wave / ctas;  // whole splits per wave: no second, nearly empty wave
     want = std::min<long long>(want, n_iter / 4);
     if (want >= 2) p->ksplit = static_cast<int>(want);
   }
