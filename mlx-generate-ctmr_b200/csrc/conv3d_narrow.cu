@@ -28,6 +28,7 @@
 #include <cstdint>
 
 #include "conv3d_narrow.cuh"
+#include "launch.cuh"
 
 namespace ctmr {
 namespace {
@@ -68,6 +69,8 @@ __device__ __forceinline__ float2 ffma2(float2 a, float2 b, float2 c) {
 
 template <int CO>
 __global__ void __launch_bounds__(kThreads) narrow_conv_kernel(const NarrowParams p, const int chunk_d) {
+  griddep_wait();  // the preceding kernel's writes are visible from here on
+  griddep_launch_dependents();
   extern __shared__ __align__(16) float smem[];
   float* s_in = smem;                                        // [kCS][kHH][kRow]
   float* s_red = s_in + kCS * kPlane;                        // [4][kSpatial] (CO == 1)
@@ -302,7 +305,7 @@ cudaError_t launch_typed(const NarrowParams& p, cudaStream_t stream) {
   const int chunks = (p.d + chunk_d - 1) / chunk_d;
   const int tiles = ((p.w + kTW - 1) / kTW) * ((p.h + kTH - 1) / kTH) * chunks;
   const dim3 grid(static_cast<unsigned>(tiles), static_cast<unsigned>(p.batch));
-  kern<<<grid, kThreads, smem, stream>>>(p, chunk_d);
+  launch_kernel(kern, grid, kThreads, smem, stream, p, chunk_d);
   return cudaGetLastError();
 }
 

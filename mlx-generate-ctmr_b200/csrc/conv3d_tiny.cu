@@ -18,6 +18,7 @@
 #include <cstdint>
 
 #include "conv3d_tiny.cuh"
+#include "launch.cuh"
 
 namespace ctmr {
 namespace {
@@ -28,6 +29,8 @@ constexpr int kVPT = 4;                // voxels per thread
 constexpr int kTile = 32 * kVPT;       // voxels per block tile
 
 __global__ void __launch_bounds__(kThreads) tiny_conv_kernel(const TinyParams p) {
+  griddep_wait();  // the preceding kernel's writes are visible from here on
+  griddep_launch_dependents();
   extern __shared__ __align__(16) float smem[];
   float* s_w = smem;                                                    // [tap][c][o]
   float (*s_out)[kOG + 4] = reinterpret_cast<float (*)[kOG + 4]>(smem + 27 * 4 * kOG);  // [kTile] epilogue rows
@@ -203,7 +206,7 @@ cudaError_t launch_tiny_conv(const TinyParams& p, cudaStream_t stream) {
   cudaError_t e = cudaFuncSetAttribute(tiny_conv_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                        static_cast<int>(smem));
   if (e != cudaSuccess) return e;
-  tiny_conv_kernel<<<grid, kThreads, smem, stream>>>(p);
+  launch_kernel(tiny_conv_kernel, grid, kThreads, smem, stream, p);
   return cudaGetLastError();
 }
 

@@ -28,6 +28,7 @@
 #include "conv3d_umma.cuh"
 #include "epilogue.cuh"
 #include "ptx.cuh"
+#include "launch.cuh"
 
 #include <cuda_bf16.h>
 #include <cuda_fp16.h>
@@ -108,6 +109,11 @@ __global__ void __launch_bounds__(kThreads, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
+  // Barrier and TMEM set-up above overlaps the preceding kernel's tail; global
+  // memory (TMA loads, epilogue stores) only from here on. Dependents are
+  // released once every CTA holds its TMEM.
+  griddep_wait();
+  griddep_launch_dependents();
 
   if (warp == 0 && lane == 0) {
     // ------------------------------------------------------------ TMA producer
@@ -304,6 +310,8 @@ __global__ void __launch_bounds__(kThreads, 1)
 // sums the fp32 partial planes in split order, adds bias and the residual, and
 // rounds once to the output type. One thread per (row voxel, 4 channels).
 __global__ void splitk_reduce_kernel(const ConvGeom g) {
+  griddep_wait();  // the preceding kernel's writes are visible from here on
+  griddep_launch_dependents();
   const int q4 = (g.cout + 3) / 4;
   const long long rows = static_cast<long long>(g.batch) * g.row_d * g.row_h * g.row_w;
   const long long total = rows * q4;
@@ -354,7 +362,7 @@ static cudaError_t launch_typed(const ConvMaps& maps, const ConvGeom& g, dim3 gr
   auto kern = conv3d_umma_kernel<KC, EXACT>;
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
   if (e != cudaSuccess) return e;
-  kern<<<grid, kThreads, smem, stream>>>(maps, g);
+  launch_kernel(kern, grid, kThreads, smem, stream, maps, g);
   return cudaGetLastError();
 }
 
@@ -392,7 +400,7 @@ cudaError_t launch_conv3d_umma(const ConvMaps& maps, const ConvGeom& g, int kc, 
   const long long total = static_cast<long long>(g.batch) * g.row_d * g.row_h * g.row_w * ((g.cout + 3) / 4);
   long long blocks = (total + 255) / 256;
   if (blocks > 148LL * 16) blocks = 148LL * 16;
-  splitk_reduce_kernel<<<static_cast<unsigned>(blocks), 256, 0, stream>>>(g);
+  launch_kernel(splitk_reduce_kernel, static_cast<unsigned>(blocks), 256, 0, stream, g);
   return cudaGetLastError();
 }
 

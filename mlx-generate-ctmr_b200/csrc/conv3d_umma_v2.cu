@@ -26,6 +26,7 @@
 #include "conv3d_umma.cuh"
 #include "epilogue.cuh"
 #include "ptx.cuh"
+#include "launch.cuh"
 
 namespace ctmr {
 namespace {
@@ -89,6 +90,11 @@ __global__ void __launch_bounds__(kThreadsV2, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
+  // Barrier and TMEM set-up above overlaps the preceding kernel's tail; global
+  // memory (TMA loads, epilogue stores) only from here on. Dependents are
+  // released once every CTA holds its TMEM.
+  griddep_wait();
+  griddep_launch_dependents();
 
   // Tile t -> (n tile fastest, then w, h, d, batch item, parity phase).
   auto decode = [&](int t, int& n0, int& w0, int& h0, int& d0, int& b, int& phase) {
@@ -309,7 +315,7 @@ cudaError_t launch_v2_typed(const ConvMaps& maps, const ConvGeom& g, int grid, s
   auto kern = conv3d_umma_v2_kernel<KC, MT, TW>;
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
   if (e != cudaSuccess) return e;
-  kern<<<grid, kThreadsV2, smem, stream>>>(maps, g);
+  launch_kernel(kern, grid, kThreadsV2, smem, stream, maps, g);
   return cudaGetLastError();
 }
 

@@ -18,6 +18,7 @@
 #include <cstdint>
 
 #include "groupnorm.cuh"
+#include "launch.cuh"
 
 namespace ctmr {
 namespace {
@@ -83,6 +84,8 @@ __device__ __forceinline__ Moments merge(Moments a, Moments b) {
 }
 
 __global__ void __launch_bounds__(kGnThreads) gn_partial_kernel(const GnParams p) {
+  griddep_wait();  // the preceding kernel's writes are visible from here on
+  griddep_launch_dependents();
   __shared__ float s_mean[kGnThreads][8];
   __shared__ float s_m2[kGnThreads][8];
   __shared__ float s_n[kGnThreads];
@@ -208,6 +211,8 @@ constexpr int kFinThreads = 128;
 constexpr int kFinPerThread = 5;  // ceil(gn_max_chunks(1) / kFinThreads)
 
 __global__ void __launch_bounds__(kFinThreads) gn_finalize_kernel(const GnParams p) {
+  griddep_wait();  // the preceding kernel's writes are visible from here on
+  griddep_launch_dependents();
   __shared__ double s_m[kFinThreads / 32][3];
   __shared__ double s_stat[2];
   const int g = blockIdx.x, b = blockIdx.y;
@@ -284,11 +289,11 @@ cudaError_t launch_group_norm_affine(const GnParams& p, cudaStream_t stream) {
                                          static_cast<int>(chan_smem));
     if (e != cudaSuccess) return e;
   }
-  gn_partial_kernel<<<dim3(p.chunks, p.batch), kGnThreads, chan_smem, stream>>>(p);
+  launch_kernel(gn_partial_kernel, dim3(p.chunks, p.batch), dim3(kGnThreads), chan_smem, stream, p);
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return e;
   if (p.chunks > kFinThreads * kFinPerThread) return cudaErrorInvalidValue;
-  gn_finalize_kernel<<<dim3(p.groups, p.batch), kFinThreads, 0, stream>>>(p);
+  launch_kernel(gn_finalize_kernel, dim3(p.groups, p.batch), dim3(kFinThreads), 0, stream, p);
   return cudaGetLastError();
 }
 

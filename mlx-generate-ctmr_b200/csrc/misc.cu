@@ -7,6 +7,7 @@
 #include <cstdint>
 
 #include "misc.cuh"
+#include "launch.cuh"
 
 namespace ctmr {
 namespace {
@@ -27,6 +28,8 @@ __device__ __forceinline__ void st_any(void* p, int bf16, long long i, float v) 
 // (B, C, S) <-> (B, S, C) through a 32x33 shared tile; one batch item per grid.z.
 __global__ void transpose_cs_kernel(const void* __restrict__ in, int in_bf16, void* __restrict__ out, int out_bf16,
                                     int rows, int cols) {
+  griddep_wait();  // the preceding kernel's writes are visible from here on
+  griddep_launch_dependents();
   __shared__ float tile[32][33];
   const long long boff = static_cast<long long>(blockIdx.z) * rows * cols;
   const int r0 = blockIdx.y * 32, c0 = blockIdx.x * 32;
@@ -45,6 +48,8 @@ __global__ void transpose_cs_kernel(const void* __restrict__ in, int in_bf16, vo
 // w = max(gz[z/scale] * gy[y/scale] * gx[x/scale], floor), the nearest-resized
 // Gaussian importance map of `decode.py:88-112` / `:164`.
 __global__ void window_accumulate_kernel(const WindowParams p) {
+  griddep_wait();  // the preceding kernel's writes are visible from here on
+  griddep_launch_dependents();
   const long long per_b = static_cast<long long>(p.wd) * p.wh * p.ww;
   const long long total = per_b * p.batch * p.channels;
   for (long long i = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x; i < total;
@@ -69,6 +74,8 @@ __global__ void window_accumulate_kernel(const WindowParams p) {
 __global__ void window_finalize_kernel(const float* __restrict__ acc, const float* __restrict__ wsum,
                                        float* __restrict__ out, int batch, int channels, int od, int oh, int ow,
                                        int cz0, int cy0, int cx0, int cd, int ch, int cw) {
+  griddep_wait();  // the preceding kernel's writes are visible from here on
+  griddep_launch_dependents();
   // out is NCDHW (B, C, cd, ch, cw): the cropped blend, acc / wsum.
   const long long total = static_cast<long long>(batch) * channels * cd * ch * cw;
   for (long long i = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x; i < total;
@@ -88,6 +95,8 @@ __global__ void window_finalize_kernel(const float* __restrict__ acc, const floa
 // z_next = z + dt * v, v = u + s * (c - u) with c = vel[:n], u = vel[n:] (or v = vel when s < 0).
 __global__ void rflow_step_kernel(const float* z, const float* __restrict__ vel, long long n, float guidance,
                                   int guided, float dt, const float* __restrict__ dt_device, float* out) {
+  griddep_wait();  // the preceding kernel's writes are visible from here on
+  griddep_launch_dependents();
   if (dt_device != nullptr) dt = *dt_device;
   for (long long i = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x; i < n;
        i += static_cast<long long>(gridDim.x) * blockDim.x) {
@@ -113,13 +122,13 @@ cudaError_t launch_transpose_cs(const void* in, int in_bf16, void* out, int out_
                                 cudaStream_t stream) {
   if (batch <= 0 || rows <= 0 || cols <= 0) return cudaSuccess;
   const dim3 grid((cols + 31) / 32, (rows + 31) / 32, batch);
-  transpose_cs_kernel<<<grid, dim3(32, 8), 0, stream>>>(in, in_bf16, out, out_bf16, rows, cols);
+  launch_kernel(transpose_cs_kernel, grid, dim3(32, 8), 0, stream, in, in_bf16, out, out_bf16, rows, cols);
   return cudaGetLastError();
 }
 
 cudaError_t launch_window_accumulate(const WindowParams& p, cudaStream_t stream) {
   const long long total = static_cast<long long>(p.wd) * p.wh * p.ww * p.batch * p.channels;
-  window_accumulate_kernel<<<grid_for(total, 256), 256, 0, stream>>>(p);
+  launch_kernel(window_accumulate_kernel, grid_for(total, 256), dim3(256), 0, stream, p);
   return cudaGetLastError();
 }
 
@@ -127,14 +136,14 @@ cudaError_t launch_window_finalize(const float* acc, const float* wsum, float* o
                                    int oh, int ow, int cz0, int cy0, int cx0, int cd, int ch, int cw,
                                    cudaStream_t stream) {
   const long long total = static_cast<long long>(batch) * channels * cd * ch * cw;
-  window_finalize_kernel<<<grid_for(total, 256), 256, 0, stream>>>(acc, wsum, out, batch, channels, od, oh, ow, cz0,
+  launch_kernel(window_finalize_kernel, grid_for(total, 256), dim3(256), 0, stream, acc, wsum, out, batch, channels, od, oh, ow, cz0,
                                                                     cy0, cx0, cd, ch, cw);
   return cudaGetLastError();
 }
 
 cudaError_t launch_rflow_step(const float* z, const float* vel, long long n, float guidance, int guided, float dt,
                               const float* dt_device, float* out, cudaStream_t stream) {
-  rflow_step_kernel<<<grid_for(n, 256), 256, 0, stream>>>(z, vel, n, guidance, guided, dt, dt_device, out);
+  launch_kernel(rflow_step_kernel, grid_for(n, 256), dim3(256), 0, stream, z, vel, n, guidance, guided, dt, dt_device, out);
   return cudaGetLastError();
 }
 

@@ -15,6 +15,7 @@
 #include <cstdint>
 
 #include "pack.cuh"
+#include "launch.cuh"
 
 namespace ctmr {
 namespace {
@@ -32,6 +33,8 @@ __device__ __forceinline__ void fold_range(int p, int t, int& k0, int& k1) {
 
 __global__ void pack_weight_kernel(const float* __restrict__ w, int O, int C, int k, int upsample, int opad,
                                    int cpad, int kind, void* __restrict__ out, void* __restrict__ out_lo) {
+  griddep_wait();  // the preceding kernel's writes are visible from here on
+  griddep_launch_dependents();
   const int taps = upsample ? 64 : k * k * k;
   const long long total = static_cast<long long>(taps) * opad * cpad;
   for (long long i = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x; i < total;
@@ -77,7 +80,7 @@ cudaError_t launch_pack_weight(const float* w, int O, int C, int k, int upsample
   long long blocks = (total + 255) / 256;
   if (blocks > 148LL * 32) blocks = 148LL * 32;
   if (blocks < 1) blocks = 1;
-  pack_weight_kernel<<<static_cast<unsigned>(blocks), 256, 0, stream>>>(w, O, C, k, upsample, opad, cpad, kind,
+  launch_kernel(pack_weight_kernel, static_cast<unsigned>(blocks), 256, 0, stream, w, O, C, k, upsample, opad, cpad, kind,
                                                                         out, out_lo);
   return cudaGetLastError();
 }

@@ -17,6 +17,7 @@
 #include <cstdint>
 
 #include "prepare.cuh"
+#include "launch.cuh"
 
 namespace ctmr {
 namespace {
@@ -160,6 +161,8 @@ __device__ __forceinline__ void store8(const PrepParams& p, long long oidx, int 
 template <int MODE, bool FAST>
 __global__ void __launch_bounds__(256) prepare_kernel(const PrepParams p, const unsigned chunks_log2,
                                                       const unsigned vox_out) {
+  griddep_wait();  // the preceding kernel's writes are visible from here on
+  griddep_launch_dependents();
   const unsigned chunks = 1u << chunks_log2;
   const unsigned items_per_batch = vox_out << chunks_log2;
   const unsigned total = items_per_batch * static_cast<unsigned>(p.batch);
@@ -365,6 +368,8 @@ __device__ __forceinline__ void load_vec(const PrepParams& p, int ctot, long lon
 template <int OUTK, bool FAST>
 __global__ void __launch_bounds__(256) prepare_copy_kernel(const PrepParams p, const FastDiv qdiv,
                                                            const unsigned vox) {
+  griddep_wait();  // the preceding kernel's writes are visible from here on
+  griddep_launch_dependents();
   const int b = blockIdx.y;
   const int ctot = p.src[0].channels + p.src[1].channels;
   const unsigned items = vox * qdiv.d;
@@ -412,6 +417,8 @@ __global__ void __launch_bounds__(256) prepare_copy_kernel(const PrepParams p, c
 template <int OUTK>
 __global__ void __launch_bounds__(128) prepare_tri_kernel(const PrepParams p, const FastDiv qdiv, const FastDiv xdiv,
                                                           const FastDiv ydiv, const unsigned items) {
+  griddep_wait();  // the preceding kernel's writes are visible from here on
+  griddep_launch_dependents();
   const int b = blockIdx.y;
   const int ctot = p.src[0].channels + p.src[1].channels;
   const long long bsrc = static_cast<long long>(b) * p.sd * p.sh * p.sw;
@@ -520,10 +527,10 @@ cudaError_t launch_copy_fast(const PrepParams& p, cudaStream_t stream) {
   if (blocks > cap) blocks = cap;
   const dim3 grid(static_cast<unsigned>(blocks), static_cast<unsigned>(p.batch));
   switch (p.out_kind) {
-    case kPrepOutBF16: prepare_copy_kernel<kPrepOutBF16, true><<<grid, 256, 0, stream>>>(p, q, vox); break;
-    case kPrepOutF16: prepare_copy_kernel<kPrepOutF16, true><<<grid, 256, 0, stream>>>(p, q, vox); break;
-    case kPrepOutSplitF16: prepare_copy_kernel<kPrepOutSplitF16, false><<<grid, 256, 0, stream>>>(p, q, vox); break;
-    default: prepare_copy_kernel<kPrepOutF32, false><<<grid, 256, 0, stream>>>(p, q, vox); break;
+    case kPrepOutBF16: launch_kernel(prepare_copy_kernel<kPrepOutBF16, true>, grid, 256, 0, stream, p, q, vox); break;
+    case kPrepOutF16: launch_kernel(prepare_copy_kernel<kPrepOutF16, true>, grid, 256, 0, stream, p, q, vox); break;
+    case kPrepOutSplitF16: launch_kernel(prepare_copy_kernel<kPrepOutSplitF16, false>, grid, 256, 0, stream, p, q, vox); break;
+    default: launch_kernel(prepare_copy_kernel<kPrepOutF32, false>, grid, 256, 0, stream, p, q, vox); break;
   }
   return cudaGetLastError();
 }
@@ -539,10 +546,10 @@ cudaError_t launch_tri_fast(const PrepParams& p, cudaStream_t stream) {
   const dim3 grid(static_cast<unsigned>(blocks), static_cast<unsigned>(p.batch));
   const unsigned n = static_cast<unsigned>(items);
   switch (p.out_kind) {
-    case kPrepOutBF16: prepare_tri_kernel<kPrepOutBF16><<<grid, 128, 0, stream>>>(p, q, xd, yd, n); break;
-    case kPrepOutF16: prepare_tri_kernel<kPrepOutF16><<<grid, 128, 0, stream>>>(p, q, xd, yd, n); break;
-    case kPrepOutSplitF16: prepare_tri_kernel<kPrepOutSplitF16><<<grid, 128, 0, stream>>>(p, q, xd, yd, n); break;
-    default: prepare_tri_kernel<kPrepOutF32><<<grid, 128, 0, stream>>>(p, q, xd, yd, n); break;
+    case kPrepOutBF16: launch_kernel(prepare_tri_kernel<kPrepOutBF16>, grid, 128, 0, stream, p, q, xd, yd, n); break;
+    case kPrepOutF16: launch_kernel(prepare_tri_kernel<kPrepOutF16>, grid, 128, 0, stream, p, q, xd, yd, n); break;
+    case kPrepOutSplitF16: launch_kernel(prepare_tri_kernel<kPrepOutSplitF16>, grid, 128, 0, stream, p, q, xd, yd, n); break;
+    default: launch_kernel(prepare_tri_kernel<kPrepOutF32>, grid, 128, 0, stream, p, q, xd, yd, n); break;
   }
   return cudaGetLastError();
 }
@@ -555,6 +562,8 @@ cudaError_t launch_tri_fast(const PrepParams& p, cudaStream_t stream) {
 // 27 taps x 16 padded channels.
 template <int OUTK>
 __global__ void __launch_bounds__(256) im2col_kernel(const PrepParams p, const int cin, const int kdense) {
+  griddep_wait();  // the preceding kernel's writes are visible from here on
+  griddep_launch_dependents();
   const int b = blockIdx.y;
   const unsigned vox = static_cast<unsigned>(p.od) * p.oh * p.ow;
   const int chunks = kdense / 8;
@@ -596,6 +605,8 @@ __global__ void __launch_bounds__(256) im2col_kernel(const PrepParams p, const i
 __global__ void repack_im2col_kernel(const uint16_t* __restrict__ hi, const uint16_t* __restrict__ lo, int opad,
                                      int cpad_src, int cin, int kdense, uint16_t* __restrict__ out_hi,
                                      uint16_t* __restrict__ out_lo) {
+  griddep_wait();  // the preceding kernel's writes are visible from here on
+  griddep_launch_dependents();
   const int n = opad * kdense;
   for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < n; i += gridDim.x * blockDim.x) {
     const int o = i / kdense, k = i - o * kdense;
@@ -634,8 +645,8 @@ cudaError_t launch_prepare(const PrepParams& p, cudaStream_t stream) {
   const dim3 grid(static_cast<unsigned>(blocks));
   const unsigned vo = static_cast<unsigned>(vox_out);
 #define CTMR_PREP(MODE)                                                         \
-  if (fast) prepare_kernel<MODE, true><<<grid, threads, 0, stream>>>(p, log2, vo); \
-  else prepare_kernel<MODE, false><<<grid, threads, 0, stream>>>(p, log2, vo);
+  if (fast) launch_kernel(prepare_kernel<MODE, true>, grid, threads, 0, stream, p, log2, vo); \
+  else launch_kernel(prepare_kernel<MODE, false>, grid, threads, 0, stream, p, log2, vo);
   if (p.mode == kPrepTrilinear) {
     CTMR_PREP(kPrepTrilinear)
   } else if (p.mode == kPrepAvgPool) {
@@ -660,9 +671,9 @@ cudaError_t launch_im2col(const PrepParams& p, int cin, int kdense, cudaStream_t
   if (blocks > cap) blocks = cap;
   const dim3 grid(static_cast<unsigned>(blocks), static_cast<unsigned>(p.batch));
   switch (p.out_kind) {
-    case kPrepOutBF16: im2col_kernel<kPrepOutBF16><<<grid, 256, 0, stream>>>(p, cin, kdense); break;
-    case kPrepOutF16: im2col_kernel<kPrepOutF16><<<grid, 256, 0, stream>>>(p, cin, kdense); break;
-    case kPrepOutSplitF16: im2col_kernel<kPrepOutSplitF16><<<grid, 256, 0, stream>>>(p, cin, kdense); break;
+    case kPrepOutBF16: launch_kernel(im2col_kernel<kPrepOutBF16>, grid, 256, 0, stream, p, cin, kdense); break;
+    case kPrepOutF16: launch_kernel(im2col_kernel<kPrepOutF16>, grid, 256, 0, stream, p, cin, kdense); break;
+    case kPrepOutSplitF16: launch_kernel(im2col_kernel<kPrepOutSplitF16>, grid, 256, 0, stream, p, cin, kdense); break;
     default: return cudaErrorInvalidValue;
   }
   return cudaGetLastError();
@@ -671,7 +682,7 @@ cudaError_t launch_im2col(const PrepParams& p, int cin, int kdense, cudaStream_t
 cudaError_t launch_repack_im2col(const void* hi, const void* lo, int opad, int cpad_src, int cin, int kdense,
                                  void* out_hi, void* out_lo, cudaStream_t stream) {
   const int n = opad * kdense;
-  repack_im2col_kernel<<<(n + 255) / 256, 256, 0, stream>>>(
+  launch_kernel(repack_im2col_kernel, (n + 255) / 256, 256, 0, stream, 
       static_cast<const uint16_t*>(hi), static_cast<const uint16_t*>(lo), opad, cpad_src, cin, kdense,
       static_cast<uint16_t*>(out_hi), static_cast<uint16_t*>(out_lo));
   return cudaGetLastError();
