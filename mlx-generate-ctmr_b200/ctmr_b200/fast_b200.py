@@ -277,8 +277,46 @@ def trilinear_conv3d_ncdhw(array, weight: torch.Tensor, bias: torch.Tensor, *, m
     return ops.conv3d(x, _pack(weight), bias, trilinear=True, out_dtype=activation_dtype())
 
 
+_TIME_TABLES: dict[tuple, tuple[torch.Tensor, torch.Tensor, torch.Tensor, list[tuple[int, int, int]]]] = {}
+
+
+class TimeBiasTable:
+    """Every residual block's ``conv1`` bias + time-embedding projection for one network pass.
+
+    The reference projects ``silu(emb)`` once per block (``residual.py:75``, one
+    small GEMV each); here all blocks' ``time_emb_proj`` weights are stacked
+    (once per weight set) and projected with one GEMM, and each block takes its
+    column slice. ``bias_for(block_weights)`` finds the slice by the block's
+    projection tensor. The stacked copy assumes the weights are not modified in
+    place, as the packed convolution weights do.
+    """
+
+    def __init__(self, emb: torch.Tensor, weights: Mapping[str, torch.Tensor]) -> None:
+        names = sorted(k[: -len("time_emb_proj.weight")] for k in weights if k.endswith("time_emb_proj.weight"))
+        key = tuple(weights[n + "time_emb_proj.weight"].data_ptr() for n in names)
+        if key not in _TIME_TABLES:
+            ws = [weights[n + "time_emb_proj.weight"].to(torch.float32) for n in names]
+            bs = [weights[n + "time_emb_proj.bias"].to(torch.float32) for n in names]
+            cs = [weights[n + "conv1.conv.bias"].to(torch.float32) for n in names]
+            spans, start = [], 0
+            for n, w in zip(names, ws, strict=True):
+                spans.append((weights[n + "time_emb_proj.weight"].data_ptr(), start, start + int(w.shape[0])))
+                start += int(w.shape[0])
+            _TIME_TABLES[key] = (torch.cat(ws).contiguous(), torch.cat(bs).contiguous(),
+                                 torch.cat(cs).reshape(1, -1).contiguous(), spans)
+        w_all, b_all, c_all, spans = _TIME_TABLES[key]
+        self.emb = emb
+        bias = c_all + F.linear(F.silu(emb.to(torch.float32)), w_all, b_all)
+        self._by_ptr = {ptr: bias[:, a:b] for ptr, a, b in spans}
+
+    def bias_for(self, weights: Mapping[str, torch.Tensor]) -> torch.Tensor | None:
+        w = weights.get("time_emb_proj.weight")
+        return None if w is None else self._by_ptr.get(w.data_ptr())
+
+
 def residual_block_ncdhw(x, emb: torch.Tensor, weights: Mapping[str, torch.Tensor], *, num_groups: int, eps: float,
-                         mx=None, up: bool = False, down: bool = False) -> torch.Tensor:
+                         mx=None, up: bool = False, down: bool = False,
+                         time_bias: torch.Tensor | None = None) -> torch.Tensor:
     """Fused UNet ResBlock (``fast_fp32.py:214-291``).
 
     The time-embedding projection joins conv1's bias per batch item; the skip
@@ -286,11 +324,15 @@ def residual_block_ncdhw(x, emb: torch.Tensor, weights: Mapping[str, torch.Tenso
     accumulator. ``down``: conv1 reads the 2x2x2 mean of ``silu(norm1(x))``
     (pooling after the activation, as the reference). ``up``: conv1 reads the
     nearest-2x upsampling through the folded weights, and the skip stays on the
-    small grid and is upsampled by index in conv2's epilogue.
+    small grid and is upsampled by index in conv2's epilogue. ``time_bias``: the
+    block's ``conv1`` bias + projected embedding when already computed.
     """
     xa, xb = _split(x)
-    temb = linear(F.silu(emb.to(torch.float32)), weights["time_emb_proj.weight"], weights["time_emb_proj.bias"])
-    bias1 = weights["conv1.conv.bias"].to(torch.float32).reshape(1, -1) + temb
+    if time_bias is not None:  # precomputed by a TimeBiasTable
+        bias1 = time_bias
+    else:
+        temb = linear(F.silu(emb.to(torch.float32)), weights["time_emb_proj.weight"], weights["time_emb_proj.bias"])
+        bias1 = weights["conv1.conv.bias"].to(torch.float32).reshape(1, -1) + temb
     norm1 = (weights["norm1.weight"], weights["norm1.bias"])
     cin = int(xa.shape[1]) + (int(xb.shape[1]) if xb is not None else 0)
     project = cin != int(weights["conv1.conv.weight"].shape[0])

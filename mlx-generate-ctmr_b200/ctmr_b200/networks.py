@@ -56,7 +56,14 @@ def _require_ncdhw(x, name: str) -> None:
 
 def residual_block_ncdhw(x, emb: torch.Tensor, weights: Weights, *, num_groups: int, eps: float, up: bool = False,
                          down: bool = False) -> torch.Tensor:
-    """``residual.residual_block_ncdhw`` validation (``residual.py:55-78``) then the fused block."""
+    """``residual.residual_block_ncdhw`` validation (``residual.py:55-78``) then the fused block.
+
+    ``emb`` may be a ``TimeBiasTable`` holding every block's projected embedding.
+    """
+    time_bias = None
+    if isinstance(emb, A.TimeBiasTable):
+        time_bias = emb.bias_for(weights)
+        emb = emb.emb
     _require_ncdhw(x, "residual input")
     if emb.dim() != 2:
         raise ValueError(f"residual emb must be [N, temb]; got ndim={emb.dim()}")
@@ -69,7 +76,8 @@ def residual_block_ncdhw(x, emb: torch.Tensor, weights: Weights, *, num_groups: 
         skip_missing = [k for k in _SKIP_KEYS if k not in weights]
         if skip_missing:
             raise ValueError("residual skip weights missing: " + ", ".join(skip_missing))
-    return A.residual_block_ncdhw(x, emb, weights, num_groups=num_groups, eps=eps, up=up, down=down)
+    return A.residual_block_ncdhw(x, emb, weights, num_groups=num_groups, eps=eps, up=up, down=down,
+                                  time_bias=time_bias)
 
 
 def _silu_mlp(x: torch.Tensor, weights: Weights, prefix: str) -> torch.Tensor:
@@ -191,6 +199,7 @@ def denoise_unet_ncdhw(x, timesteps, class_labels, spacing, weights: Weights, *,
     t_emb, emb = condition_embedding(timesteps, class_labels, spacing, weights, constructor)
     hidden = A.conv3d_ncdhw(ops.to_ndhwc(x), required_weight(weights, "conv_in.conv.weight"),
                             required_weight(weights, "conv_in.conv.bias"), padding=1)
+    emb = A.TimeBiasTable(emb, weights)  # every block's projected embedding in one GEMM
     hidden, skips = apply_down_blocks(hidden, emb, weights, constructor, down_block_additional_residuals)
     hidden = apply_mid_block(hidden, emb, weights, constructor)
     if mid_block_additional_residual is not None:
@@ -268,6 +277,7 @@ def controlnet_residuals_ncdhw(x, timesteps, class_labels, cond, weights: Weight
     hidden = ops.conv3d(ops.to_ndhwc(x, A.activation_dtype()), A._pack(required_weight(weights, "conv_in.conv.weight")),
                         required_weight(weights, "conv_in.conv.bias"), residual=ops.to_ndhwc(embed),
                         out_dtype=A.activation_dtype())
+    emb = A.TimeBiasTable(emb, weights)
     hidden, skips = apply_down_blocks(hidden, emb, weights, constructor)
     hidden = apply_mid_block(hidden, emb, weights, constructor)
     down = [_zero_conv(s, weights, f"controlnet_down_blocks.{i}") for i, s in enumerate(skips)]
