@@ -142,6 +142,20 @@ def _dense_weight(weight: torch.Tensor, dtype: torch.dtype) -> torch.Tensor:
     return cast
 
 
+_stacked: dict[tuple, tuple] = {}
+
+
+def _stacked_dense(tensors: tuple[torch.Tensor, ...], dtype: torch.dtype) -> torch.Tensor:
+    """``cat(tensors)`` in ``dtype`` (the Q/K/V projections as one), cached while the sources live."""
+    key = (tuple(id(t) for t in tensors), dtype)
+    hit = _stacked.get(key)
+    if hit is not None and all(r() is t for r, t in zip(hit[0], tensors, strict=True)):
+        return hit[1]
+    out = torch.cat([t.detach().to(dtype) for t in tensors]).contiguous()
+    _stacked[key] = (tuple(weakref.ref(t, lambda _: _stacked.pop(key, None)) for t in tensors), out)
+    return out
+
+
 def dense_dtype() -> torch.dtype:
     """Operand type of the dense (non-conv) tensor-core ops: fp32, or the 16-bit mode's type."""
     return {"fp32": torch.float32, "bf16": torch.bfloat16, "fp16": torch.float16}[_precision.get()]
@@ -393,11 +407,11 @@ def self_attention_tokens(tokens: torch.Tensor, weights: Mapping[str, torch.Tens
     """Q/K/V projections, multi-head self-attention and optional ``out_proj`` on ``(B, L, C)`` (``fast_fp32.py:352-396``)."""
     dt = dense_dtype()
     tokens = tokens.to(dt)
-    q, k, v = (
-        F.linear(tokens, _dense_weight(weights[f"{prefix}.to_{n}.weight"], dt),
-                 _dense_weight(weights[f"{prefix}.to_{n}.bias"], dt) if qkv_bias else None)
-        for n in ("q", "k", "v")
-    )
+    # One projection GEMM with the Q, K and V weights stacked (same products as three).
+    names = ("q", "k", "v")
+    w_qkv = _stacked_dense(tuple(weights[f"{prefix}.to_{n}.weight"] for n in names), dt)
+    b_qkv = _stacked_dense(tuple(weights[f"{prefix}.to_{n}.bias"] for n in names), dt) if qkv_bias else None
+    q, k, v = F.linear(tokens, w_qkv, b_qkv).chunk(3, dim=-1)
     b, length, c = q.shape
 
     def split(a):
@@ -427,4 +441,4 @@ def spatial_attention_ncdhw(x: torch.Tensor, weights: Mapping[str, torch.Tensor]
     tokens = normed.permute(0, 2, 3, 4, 1).reshape(b, d * h * w, c)
     merged = self_attention_tokens(tokens, weights, heads=heads, scale=scale, include_fc=include_fc)
     out = merged.reshape(b, d, h, w, c).permute(0, 4, 1, 2, 3)
-    return x + out.to(x.dtype)
+    return torch.add(x, out)  # promotes a 16-bit projection to x's dtype in the same kernel
