@@ -93,6 +93,12 @@ typedef struct ctmr_conv3d_desc {
   int y_dtype;
   long long y_cstride;
   int y_coffset;                   /* first channel written in each output row */
+  /* Optional GroupNorm statistics of the output, for ctmr_group_norm_affine_from_stats:
+   * float[batch][stats_slots][out_channels][3] moments (count, mean, M2) per
+   * (batch item, slot, channel). stats_slots must be ctmr_conv3d_stats_slots(desc)
+   * (> 0). Null: none. */
+  float* stats;
+  int stats_slots;
 } ctmr_conv3d_desc;
 
 /* Packed-weight element count per plane for a Torch (O, C, k, k, k) weight:
@@ -151,6 +157,23 @@ CTMR_API size_t ctmr_group_norm_workspace_size(int batch, long long voxels, int 
 CTMR_API int ctmr_group_norm_affine(ctmr_tensor x, ctmr_tensor x2, int batch, long long voxels, const float* gamma,
                            const float* beta, int groups, float eps, float* affine, void* workspace,
                            size_t workspace_bytes, void* stream);
+
+/* Statistics slots a convolution writes when desc->stats is set (its persistent
+ * kernel's CTA count bound), or 0 when this convolution does not produce them (it
+ * does not run the persistent kernel, has fewer than 128 output channels, or
+ * batch x out_channels > 512). Has no
+ * reference counterpart: the reference recomputes the statistics from the tensor. */
+CTMR_API int ctmr_conv3d_stats_slots(const ctmr_conv3d_desc* desc);
+
+/* The affine of ctmr_group_norm_affine from convolution output statistics instead
+ * of a pass over the tensor: stats_a (channels_a) ++ stats_b (channels_b, may be
+ * NULL with channels_b 0) in the ctmr_conv3d_desc.stats layout, each with `slots`
+ * slots. Same result definition as `group_norm_affine` (`fast_fp32.py:183-189`);
+ * the moments are merged in double precision in a fixed order. */
+CTMR_API int ctmr_group_norm_affine_from_stats(const float* stats_a, int channels_a, const float* stats_b,
+                                               int channels_b, int slots, int batch, const float* gamma,
+                                               const float* beta, int groups, float eps, float* affine,
+                                               void* stream);
 
 enum { CTMR_TRANSFORM_COPY = 0, CTMR_TRANSFORM_TRILINEAR = 1, CTMR_TRANSFORM_AVGPOOL = 2 };
 

@@ -26,7 +26,7 @@ namespace ctmr {
 int conv_stage_plan(int kc, int bn, bool exact, bool one_cta_per_sm, size_t* smem_bytes);
 cudaError_t launch_conv3d_umma(const ConvMaps& maps, const ConvGeom& g, int kc, bool exact, size_t smem,
                                cudaStream_t stream);
-int conv_v2_stage_plan(int kc, int mt, int tw, int bn, size_t* smem_bytes);
+int conv_v2_stage_plan(int kc, int mt, int tw, int bn, size_t* smem_bytes, size_t stats_bytes);
 cudaError_t launch_conv3d_umma_v2(const ConvMaps& maps, const ConvGeom& g, int kc, int mt, int tw, int sms,
                                   size_t smem, cudaStream_t stream);
 extern __device__ unsigned int g_device_error;
@@ -136,6 +136,7 @@ int sm_count() {
 // Set when the driver rejects the H-before-W tensor view of the persistent kernel; every
 // later convolution then takes the per-tap kernel.
 bool g_v2_unavailable = false;
+constexpr long long kStatsMaxEntries = 512;  // batch x output channels with output statistics
 
 int check_view(const ctmr_tensor& t, const char* name, bool required) {
   if (t.data == nullptr) {
@@ -316,6 +317,43 @@ int plan_conv(const ctmr_conv3d_desc* d, ConvPlan* p) {
   return CTMR_OK;
 }
 
+
+// The persistent kernel's plan for a convolution, or false when it does not apply.
+struct V2Plan {
+  int kc, mt, tw, bn, stages;
+  size_t smem, stats_bytes;
+};
+
+bool plan_v2(const ConvPlan& p, const ctmr_conv3d_desc* d, bool with_stats, V2Plan* v) {
+  if (p.exact || g_v2_unavailable ||
+      !(p.mode == ctmr::kModeConv3 || p.mode == ctmr::kModeUp2 || p.mode == ctmr::kModeConv1) || p.row_w < 16 ||
+      p.row_h < 8 || getenv("CTMR_DISABLE_V2") != nullptr)
+    return false;
+  v->tw = p.mode == ctmr::kModeConv3 ? 3 : (p.mode == ctmr::kModeUp2 ? 2 : 1);
+  v->mt = p.row_d >= 2 ? 2 : 1;
+  v->bn = std::min(p.opad, 128);
+  v->stats_bytes = 0;
+  if (with_stats) {
+    // Below 128 output channels the MMA work per tile is too short to hide the
+    // statistics reduction in the epilogue; a separate pass is cheaper there.
+    if (d->out_channels < 128) return false;
+    // One (count, mean, M2) accumulator per epilogue warp for every (batch item, channel).
+    if (static_cast<long long>(d->batch) * d->out_channels > kStatsMaxEntries) return false;
+    v->stats_bytes = static_cast<size_t>(4) * d->batch * d->out_channels * 3 * sizeof(float);
+  }
+  // Largest channel block whose pipeline is at least 3 stages deep (else 2).
+  for (int min_stages : {3, 2}) {
+    for (int cand : {64, 32, 16}) {
+      size_t sm_b = 0;
+      const int st = p.cpad % cand ? 0 : ctmr::conv_v2_stage_plan(cand, v->mt, v->tw, v->bn, &sm_b, v->stats_bytes);
+      if (st >= min_stages) {
+        v->kc = cand, v->smem = sm_b, v->stages = st;
+        return true;
+      }
+    }
+  }
+  return false;
+}
 }  // namespace
 
 namespace ctmr {
@@ -383,6 +421,8 @@ int ctmr_conv3d_stages(const ctmr_conv3d_desc* d, void* workspace, size_t worksp
   const size_t need = p.workspace();
   if (need > workspace_bytes || (need > 0 && workspace == nullptr))
     return fail(CTMR_ERR_WORKSPACE, "conv3d needs %zu workspace bytes, got %zu", need, workspace_bytes);
+  if (d->stats != nullptr && (p.narrow || p.tiny))
+    return fail(CTMR_ERR_UNSUPPORTED, "output statistics need the persistent kernel (ctmr_conv3d_stats_slots)");
 
   if (p.narrow) {
     if (!(stages & CTMR_CONV_GEMM)) return CTMR_OK;
@@ -485,27 +525,13 @@ int ctmr_conv3d_stages(const ctmr_conv3d_desc* d, void* workspace, size_t worksp
   if (!(stages & CTMR_CONV_GEMM)) return CTMR_OK;
 
   // 2a. The persistent atom-shifted kernel for 16-bit stride-1 3x3x3, nearest-2x and 1x1x1 convolutions.
-  if (!p.exact && !g_v2_unavailable &&
-      (p.mode == ctmr::kModeConv3 || p.mode == ctmr::kModeUp2 || p.mode == ctmr::kModeConv1) && p.row_w >= 16 &&
-      p.row_h >= 8 && getenv("CTMR_DISABLE_V2") == nullptr) {
-    const int tw = p.mode == ctmr::kModeConv3 ? 3 : (p.mode == ctmr::kModeUp2 ? 2 : 1);
-    const int mt = p.row_d >= 2 ? 2 : 1;
-    const int bn = std::min(p.opad, 128);
-    // Largest channel block whose pipeline is at least 3 stages deep (else 2).
-    int kc = 0;
-    size_t smem2 = 0;
-    int stages2 = 0;
-    for (int min_stages : {3, 2}) {
-      for (int cand : {64, 32, 16}) {
-        size_t sm_b = 0;
-        const int st = p.cpad % cand ? 0 : ctmr::conv_v2_stage_plan(cand, mt, tw, bn, &sm_b);
-        if (st >= min_stages) {
-          kc = cand, smem2 = sm_b, stages2 = st;
-          break;
-        }
-      }
-      if (kc) break;
-    }
+  const bool with_stats = d->stats != nullptr;
+  V2Plan v2{};
+  if (with_stats && (d->stats_slots < sm_count() || !plan_v2(p, d, true, &v2)))
+    return fail(CTMR_ERR_UNSUPPORTED, "output statistics need the persistent kernel (ctmr_conv3d_stats_slots)");
+  if (plan_v2(p, d, with_stats, &v2)) {
+    const int tw = v2.tw, mt = v2.mt, bn = v2.bn, kc = v2.kc, stages2 = v2.stages;
+    const size_t smem2 = v2.smem;
     if (kc != 0) {
       ctmr::ConvGeom g{};
       g.batch = d->batch;
@@ -543,6 +569,8 @@ int ctmr_conv3d_stages(const ctmr_conv3d_desc* d, void* workspace, size_t worksp
         g.out_cstride = d->y_cstride;
         g.out_coff = d->y_coffset;
         g.out_d = p.out_d, g.out_h = p.out_h, g.out_w = p.out_w;
+        g.stats = static_cast<float*>(d->stats);
+        g.stats_slots = d->stats_slots;
         ctmr::ConvMaps maps;
         std::memset(&maps, 0, sizeof(maps));
         const long long rs = a_cstride * 2;
@@ -558,6 +586,7 @@ int ctmr_conv3d_stages(const ctmr_conv3d_desc* d, void* workspace, size_t worksp
           return e == cudaSuccess ? CTMR_OK : cuda_fail(e, "conv3d v2 launch");
         }
         g_v2_unavailable = true;  // fall through to the per-tap kernel
+        if (with_stats) return fail(CTMR_ERR_UNSUPPORTED, "persistent kernel unavailable for output statistics");
       }
     }
   }
@@ -674,6 +703,39 @@ int ctmr_group_norm_affine(ctmr_tensor x, ctmr_tensor x2, int batch, long long v
   p.chunks = ctmr::gn_chunks_for(batch, voxels, ctot);
   cudaError_t e = ctmr::launch_group_norm_affine(p, static_cast<cudaStream_t>(stream));
   return e == cudaSuccess ? CTMR_OK : cuda_fail(e, "group_norm launch");
+}
+
+int ctmr_conv3d_stats_slots(const ctmr_conv3d_desc* d) {
+  ConvPlan p{};
+  if (d == nullptr || plan_conv(d, &p) != CTMR_OK) return 0;
+  V2Plan v2{};
+  if (p.narrow || p.tiny || !plan_v2(p, d, true, &v2)) return 0;
+  return sm_count();
+}
+
+int ctmr_group_norm_affine_from_stats(const float* stats_a, int channels_a, const float* stats_b, int channels_b,
+                                      int slots, int batch, const float* gamma, const float* beta, int groups,
+                                      float eps, float* affine, void* stream) {
+  if (stats_a == nullptr || channels_a <= 0 || (channels_b > 0 && stats_b == nullptr) || channels_b < 0)
+    return fail(CTMR_ERR_INVALID, "group_norm statistics missing");
+  if (slots <= 0 || batch <= 0) return fail(CTMR_ERR_INVALID, "group_norm statistics extents");
+  const int ctot = channels_a + channels_b;
+  if (groups <= 0 || ctot % groups != 0) return fail(CTMR_ERR_INVALID, "group_norm channels must be divisible by num_groups");
+  if (affine == nullptr) return fail(CTMR_ERR_INVALID, "affine output missing");
+  ctmr::GnStatsParams p{};
+  p.stats[0] = stats_a;
+  p.stats[1] = channels_b > 0 ? stats_b : nullptr;
+  p.channels[0] = channels_a;
+  p.channels[1] = channels_b;
+  p.slots = slots;
+  p.batch = batch;
+  p.groups = groups;
+  p.eps = eps;
+  p.gamma = gamma;
+  p.beta = beta;
+  p.affine = affine;
+  cudaError_t e = ctmr::launch_group_norm_from_stats(p, static_cast<cudaStream_t>(stream));
+  return e == cudaSuccess ? CTMR_OK : cuda_fail(e, "group_norm from statistics launch");
 }
 
 int ctmr_transform(const ctmr_transform_desc* d, void* stream) {

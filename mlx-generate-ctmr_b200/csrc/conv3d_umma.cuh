@@ -57,6 +57,10 @@ struct ConvGeom {
   int out_coff;
   int out_d, out_h, out_w;
   float lo_scale;               // 2^-11: weight of the hi*lo + lo*hi accumulator
+  // GroupNorm statistics of the output (persistent kernel): per (batch item, CTA
+  // slot, channel) moments (count, mean, M2) as float[batch][stats_slots][cout][3].
+  float* stats;                 // null: not requested
+  int stats_slots;              // slots in the buffer (>= the grid; the rest are zeroed)
 };
 
 }  // namespace ctmr

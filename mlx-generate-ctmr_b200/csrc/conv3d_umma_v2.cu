@@ -47,7 +47,7 @@ struct V2Layout {
   }
 };
 
-template <int KC, int MT, int TW>
+template <int KC, int MT, int TW, bool STATS>
 __global__ void __launch_bounds__(kThreadsV2, 1)
     conv3d_umma_v2_kernel(const __grid_constant__ ConvMaps maps, const __grid_constant__ ConvGeom g) {
   constexpr uint32_t kRowBytes = KC * 2;
@@ -64,6 +64,8 @@ __global__ void __launch_bounds__(kThreadsV2, 1)
   uint64_t* tmem_empty = tmem_full + 2;  // [2]
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(tmem_empty + 2);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+  // Output statistics: one accumulator per epilogue warp, [4][batch][cout][3].
+  float* s_stats = reinterpret_cast<float*>(smem + static_cast<size_t>(S) * L.stage_bytes + 256);
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
@@ -276,8 +278,16 @@ __global__ void __launch_bounds__(kThreadsV2, 1)
           }
           store16(g, v, n, out_base + n);
         }
+        if (STATS && n < g.cout)
+          warp_stats16(v, valid, min(16, g.cout - n),
+                       s_stats + ((static_cast<size_t>(warp - 2) * g.batch + b) * g.cout + n) * 3);
       }
     };
+    if (STATS) {
+      float* mine = s_stats + static_cast<size_t>(warp - 2) * g.batch * g.cout * 3;
+      for (int e = lane; e < g.batch * g.cout * 3; e += 32) mine[e] = 0.f;
+      __syncwarp();
+    }
     for (int t = blockIdx.x; t < g.total_tiles && !*abort_flag; t += gridDim.x, ++lt) {
       const int buf = lt & 1;
       decode(t, n0, w0, h0, d0, b, phase);
@@ -300,6 +310,36 @@ __global__ void __launch_bounds__(kThreadsV2, 1)
       tc_fence_before();
       mbar_arrive(&tmem_empty[buf]);
     }
+    if (STATS) {
+      // Every epilogue warp reaches this point (finished or aborted): merge the
+      // four warps' moments in order and write this CTA's slot.
+      asm volatile("bar.sync 1, 128;" ::: "memory");
+      const int et = threadIdx.x - 64;
+      const int bc = g.batch * g.cout;
+      for (int e = et; e < bc; e += 128) {
+        float m[3] = {0.f, 0.f, 0.f};
+#pragma unroll
+        for (int wq = 0; wq < 4; ++wq) {
+          const float* a = s_stats + (static_cast<size_t>(wq) * bc + e) * 3;
+          chan_merge(m, a[0], a[1], a[2]);
+        }
+        const int bb = e / g.cout, c = e - bb * g.cout;
+        float* dst = g.stats + ((static_cast<size_t>(bb) * g.stats_slots + blockIdx.x) * g.cout + c) * 3;
+        dst[0] = m[0];
+        dst[1] = m[1];
+        dst[2] = m[2];
+      }
+      if (blockIdx.x == 0) {  // slots past the grid hold nothing
+        const int extra = g.stats_slots - static_cast<int>(gridDim.x);
+        for (int e = et; e < g.batch * extra * g.cout; e += 128) {
+          const int bb = e / (extra * g.cout), r = e - bb * extra * g.cout;
+          float* dst = g.stats + (static_cast<size_t>(bb) * g.stats_slots * g.cout + gridDim.x * g.cout + r) * 3;
+          dst[0] = 0.f;
+          dst[1] = 0.f;
+          dst[2] = 0.f;
+        }
+      }
+    }
   }
 
   tc_fence_before();
@@ -312,20 +352,20 @@ __global__ void __launch_bounds__(kThreadsV2, 1)
 
 template <int KC, int MT, int TW>
 cudaError_t launch_v2_typed(const ConvMaps& maps, const ConvGeom& g, int grid, size_t smem, cudaStream_t stream) {
-  auto kern = conv3d_umma_v2_kernel<KC, MT, TW>;
+  // The statistics epilogue is a separate instantiation so the plain kernel keeps its registers.
+  auto kern = g.stats != nullptr ? conv3d_umma_v2_kernel<KC, MT, TW, true> : conv3d_umma_v2_kernel<KC, MT, TW, false>;
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
   if (e != cudaSuccess) return e;
-  launch_kernel(kern, grid, kThreadsV2, smem, stream, maps, g);
-  return cudaGetLastError();
+  return launch_kernel(kern, grid, kThreadsV2, smem, stream, maps, g);
 }
 
 }  // namespace
 
 // Shared-memory plan of the v2 kernel: the deepest pipeline (<= 6 stages) that
 // fits one CTA per SM; 0 when fewer than 2 stages fit.
-int conv_v2_stage_plan(int kc, int mt, int tw, int bn, size_t* smem_bytes) {
+int conv_v2_stage_plan(int kc, int mt, int tw, int bn, size_t* smem_bytes, size_t stats_bytes) {
   const V2Layout L(kc, mt, tw, bn);
-  const size_t extra = 1024 + 256;
+  const size_t extra = 1024 + 256 + stats_bytes;
   int stages = static_cast<int>((227 * 1024 - extra) / L.stage_bytes);
   if (stages > 6) stages = 6;
   if (stages < 2) return 0;

@@ -173,4 +173,68 @@ __device__ __forceinline__ float res_word(const ConvGeom& g, const uint32_t (&w)
   return __uint_as_float(w[j]);
 }
 
+// ---------------------------------------------------------------- output statistics
+// Chan et al.'s pairwise update of (count, mean, M2) moments.
+__device__ __forceinline__ void chan_merge(float* m, float nb, float meanb, float m2b) {
+  if (nb == 0.f) return;
+  const float na = m[0];
+  if (na == 0.f) {
+    m[0] = nb;
+    m[1] = meanb;
+    m[2] = m2b;
+    return;
+  }
+  const float n = na + nb;
+  const float delta = meanb - m[1];
+  const float fb = nb / n;
+  m[1] = fmaf(delta, fb, m[1]);
+  m[2] = m[2] + m2b + delta * delta * na * fb;
+  m[0] = n;
+}
+
+// Reduce-scatter of 16 per-lane columns over the warp (16 shuffles, fixed
+// order): lane l ends up with the warp total of column stat_col(l).
+__device__ __forceinline__ int stat_col(int lane) {
+  return ((lane >> 4) & 1) * 8 + ((lane >> 3) & 1) * 4 + ((lane >> 2) & 1) * 2 + ((lane >> 1) & 1);
+}
+__device__ __forceinline__ int stat_src(int col) {
+  return (((col >> 3) & 1) << 4) | (((col >> 2) & 1) << 3) | (((col >> 1) & 1) << 2) | ((col & 1) << 1);
+}
+__device__ __forceinline__ float reduce_scatter16(const float (&x)[16], int lane) {
+  float a[8], b[4], c[2];
+  const bool h4 = lane & 16, h3 = lane & 8, h2 = lane & 4, h1 = lane & 2;
+#pragma unroll
+  for (int i = 0; i < 8; ++i) a[i] = (h4 ? x[i + 8] : x[i]) + __shfl_xor_sync(0xffffffffu, h4 ? x[i] : x[i + 8], 16);
+#pragma unroll
+  for (int i = 0; i < 4; ++i) b[i] = (h3 ? a[i + 4] : a[i]) + __shfl_xor_sync(0xffffffffu, h3 ? a[i] : a[i + 4], 8);
+#pragma unroll
+  for (int i = 0; i < 2; ++i) c[i] = (h2 ? b[i + 2] : b[i]) + __shfl_xor_sync(0xffffffffu, h2 ? b[i] : b[i + 2], 4);
+  const float d = (h1 ? c[1] : c[0]) + __shfl_xor_sync(0xffffffffu, h1 ? c[0] : c[1], 2);
+  return d + __shfl_xor_sync(0xffffffffu, d, 1);
+}
+
+// Moments of 16 output columns over this warp's valid rows (two passes: means,
+// then squared deviations), merged into the warp-private accumulator `acc`
+// (column i at acc + 3 * i) for the first `cnt` columns. Warp-collective.
+__device__ __forceinline__ void warp_stats16(const float (&v)[16], bool valid, int cnt, float* acc) {
+  const int lane = threadIdx.x & 31;
+  const unsigned vm = __ballot_sync(0xffffffffu, valid);
+  if (vm == 0u) return;
+  const float nw = static_cast<float>(__popc(vm));
+  float x[16];
+#pragma unroll
+  for (int i = 0; i < 16; ++i) x[i] = valid ? v[i] : 0.f;
+  const float mean = reduce_scatter16(x, lane) / nw;
+#pragma unroll
+  for (int i = 0; i < 16; ++i) {
+    const float mi = __shfl_sync(0xffffffffu, mean, stat_src(i));
+    const float d = valid ? v[i] - mi : 0.f;
+    x[i] = d * d;
+  }
+  const float m2 = reduce_scatter16(x, lane);
+  const int col = stat_col(lane);
+  if ((lane & 1) == 0 && col < cnt) chan_merge(acc + 3 * col, nw, mean, m2);
+  __syncwarp();
+}
+
 }  // namespace ctmr

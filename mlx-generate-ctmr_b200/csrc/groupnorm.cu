@@ -267,6 +267,60 @@ __global__ void __launch_bounds__(kFinThreads) gn_finalize_kernel(const GnParams
   }
 }
 
+// From convolution output statistics: one block per (group, batch item); thread
+// i merges the (slot, channel) entries i, i + 128, ... of the group in order
+// (slot-major within each source, then the second source), then the fixed
+// shuffle tree and the warps in order, in double precision.
+__global__ void __launch_bounds__(kFinThreads) gn_from_stats_kernel(const GnStatsParams p) {
+  griddep_wait();
+  griddep_launch_dependents();
+  __shared__ double s_m[kFinThreads / 32][3];
+  __shared__ double s_stat[2];
+  const int g = blockIdx.x, b = blockIdx.y;
+  const int ctot = p.channels[0] + p.channels[1];
+  const int cpg = ctot / p.groups;
+  const int c_begin = g * cpg;
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int entries = p.slots * cpg;
+  MomentsD m{0.0, 0.0, 0.0};
+  for (int e = tid; e < entries; e += kFinThreads) {
+    const int slot = e / cpg, cl = e - slot * cpg;
+    const int c = c_begin + cl;
+    const int src = c < p.channels[0] ? 0 : 1;
+    const int cs = src == 0 ? c : c - p.channels[0];
+    const float* q = p.stats[src] + ((static_cast<long long>(b) * p.slots + slot) * p.channels[src] + cs) * 3;
+    m = merge_d(m, MomentsD{q[0], q[1], q[2]});
+  }
+#pragma unroll
+  for (int off = 1; off < 32; off <<= 1) {
+    const MomentsD o = shfl_down_moments(m, off);
+    if ((lane & (2 * off - 1)) == 0) m = merge_d(m, o);
+  }
+  if (lane == 0) {
+    s_m[warp][0] = m.n;
+    s_m[warp][1] = m.mean;
+    s_m[warp][2] = m.m2;
+  }
+  __syncthreads();
+  if (tid == 0) {
+    MomentsD t{0.0, 0.0, 0.0};
+    for (int w = 0; w < kFinThreads / 32; ++w) t = merge_d(t, MomentsD{s_m[w][0], s_m[w][1], s_m[w][2]});
+    const double var = t.n > 0.0 ? t.m2 / t.n : 0.0;
+    s_stat[0] = t.mean;
+    s_stat[1] = 1.0 / sqrt(var + static_cast<double>(p.eps));
+  }
+  __syncthreads();
+  const double mean = s_stat[0], rstd = s_stat[1];
+  for (int c = c_begin + tid; c < c_begin + cpg; c += kFinThreads) {
+    const double gam = p.gamma != nullptr ? static_cast<double>(p.gamma[c]) : 1.0;
+    const double bet = p.beta != nullptr ? static_cast<double>(p.beta[c]) : 0.0;
+    const double scale = gam * rstd;
+    float* a = p.affine + (static_cast<long long>(b) * ctot + c) * 2;
+    a[0] = static_cast<float>(scale);
+    a[1] = static_cast<float>(bet - mean * scale);
+  }
+}
+
 }  // namespace
 
 int gn_max_chunks(int batch) { return (2 * 296 + batch - 1) / batch; }
@@ -295,6 +349,14 @@ cudaError_t launch_group_norm_affine(const GnParams& p, cudaStream_t stream) {
   if (p.chunks > kFinThreads * kFinPerThread) return cudaErrorInvalidValue;
   launch_kernel(gn_finalize_kernel, dim3(p.groups, p.batch), dim3(kFinThreads), 0, stream, p);
   return cudaGetLastError();
+}
+
+}  // namespace ctmr
+
+namespace ctmr {
+
+cudaError_t launch_group_norm_from_stats(const GnStatsParams& p, cudaStream_t stream) {
+  return launch_kernel(gn_from_stats_kernel, dim3(p.groups, p.batch), dim3(kFinThreads), 0, stream, p);
 }
 
 }  // namespace ctmr

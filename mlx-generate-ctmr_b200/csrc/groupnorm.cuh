@@ -20,7 +20,20 @@ struct GnParams {
   int chunks;
 };
 
+// Affine from convolution output statistics: moments float[batch][slots][channels][3]
+// of up to two sources (the virtual concat a ++ b).
+struct GnStatsParams {
+  const float* stats[2];
+  int channels[2];
+  int slots, batch, groups;
+  float eps;
+  const float* gamma;
+  const float* beta;
+  float* affine;          // out: [batch][C][2]
+};
+
 int gn_max_chunks(int batch);
+cudaError_t launch_group_norm_from_stats(const GnStatsParams& p, cudaStream_t stream);
 int gn_chunks_for(int batch, long long voxels, int channels);
 cudaError_t launch_group_norm_affine(const GnParams& p, cudaStream_t stream);
 

@@ -39,6 +39,8 @@ EXPORTED_SYMBOLS = (
     "ctmr_conv3d_noalloc",
     "ctmr_group_norm_workspace_size",
     "ctmr_group_norm_affine",
+    "ctmr_conv3d_stats_slots",
+    "ctmr_group_norm_affine_from_stats",
     "ctmr_transform",
     "ctmr_ncdhw_to_ndhwc",
     "ctmr_ndhwc_to_ncdhw",
@@ -91,6 +93,8 @@ class Conv3dDesc(ctypes.Structure):
         ("y_dtype", ctypes.c_int),
         ("y_cstride", ctypes.c_longlong),
         ("y_coffset", ctypes.c_int),
+        ("stats", ctypes.c_void_p),
+        ("stats_slots", ctypes.c_int),
     ]
 
 
@@ -131,6 +135,8 @@ def _load() -> ctypes.CDLL:
         "ctmr_conv3d_noalloc": (i, [ctypes.POINTER(Conv3dDesc), vp]),
         "ctmr_group_norm_workspace_size": (sz, [i, ll, i]),
         "ctmr_group_norm_affine": (i, [Tensor, Tensor, i, ll, vp, vp, i, f, vp, vp, sz, vp]),
+        "ctmr_conv3d_stats_slots": (i, [ctypes.POINTER(Conv3dDesc)]),
+        "ctmr_group_norm_affine_from_stats": (i, [vp, i, vp, i, i, i, vp, vp, i, f, vp, vp]),
         "ctmr_transform": (i, [ctypes.POINTER(TransformDesc), vp]),
         "ctmr_ncdhw_to_ndhwc": (i, [vp, i, vp, i, i, i, ll, vp]),
         "ctmr_ndhwc_to_ncdhw": (i, [vp, i, vp, i, i, i, ll, vp]),

@@ -33,6 +33,7 @@ from __future__ import annotations
 
 import contextlib
 import math
+import os
 import weakref
 from collections.abc import Generator, Iterable, Mapping
 from contextvars import ContextVar
@@ -141,6 +142,12 @@ def _dense_weight(weight: torch.Tensor, dtype: torch.dtype) -> torch.Tensor:
     _dense[key] = (weakref.ref(weight, lambda _: _dense.pop(key, None)), cast)
     return cast
 
+
+# Whether GroupNorm-feeding convolutions reduce their output statistics in the
+# epilogue (ops.conv3d(stats=True)) instead of the GroupNorm pass reading the
+# tensor. Off by default: measured on the MAISI networks, the epilogue reduction
+# costs the 64- to 128-channel convolutions more than the pass it saves.
+OUTPUT_STATS = os.environ.get("CTMR_OUTPUT_STATS", "0") == "1"
 
 _stacked: dict[tuple, tuple] = {}
 
@@ -257,7 +264,7 @@ def conv3d_ncdhw(array, weight: torch.Tensor, bias: torch.Tensor | None, *, padd
     if k != 3 or padding != 1 or stride not in (1, 2):
         raise ValueError(f"unsupported convolution: kernel {k}, padding {padding}, stride {stride}")
     x, x2 = _split(array)
-    return ops.conv3d(x, _pack(weight), bias, x2=x2, stride=stride, out_dtype=activation_dtype())
+    return ops.conv3d(x, _pack(weight), bias, x2=x2, stride=stride, out_dtype=activation_dtype(), stats=OUTPUT_STATS)
 
 
 def norm_conv3d_ncdhw(array, weight: torch.Tensor, bias: torch.Tensor, *, norm, num_groups: int, eps: float,
@@ -280,7 +287,7 @@ def norm_conv3d_ncdhw(array, weight: torch.Tensor, bias: torch.Tensor, *, norm, 
         res = ops.to_ndhwc(res)
     return ops.conv3d(x, _pack(weight, upsample=upsample), bias, x2=x2, affine=affine, silu=apply_silu,
                       avgpool=avgpool, residual=res, residual_upsampled=residual_upsampled,
-                      out_dtype=activation_dtype())
+                      out_dtype=activation_dtype(), stats=OUTPUT_STATS)
 
 
 def trilinear_conv3d_ncdhw(array, weight: torch.Tensor, bias: torch.Tensor, *, mx=None) -> torch.Tensor:
@@ -288,7 +295,7 @@ def trilinear_conv3d_ncdhw(array, weight: torch.Tensor, bias: torch.Tensor, *, m
     x, x2 = _split(array)
     if x2 is not None:
         x = ChannelConcat(x, x2).materialize()
-    return ops.conv3d(x, _pack(weight), bias, trilinear=True, out_dtype=activation_dtype())
+    return ops.conv3d(x, _pack(weight), bias, trilinear=True, out_dtype=activation_dtype(), stats=OUTPUT_STATS)
 
 
 _TIME_TABLES: dict[tuple, tuple[torch.Tensor, torch.Tensor, torch.Tensor, list[tuple[int, int, int]]]] = {}
@@ -359,7 +366,7 @@ def residual_block_ncdhw(x, emb: torch.Tensor, weights: Mapping[str, torch.Tenso
         else:
             skip = ops.transform(xa, x2=xb, mode=_lib.TRANSFORM_AVGPOOL, out_dtype=dtype)
         hidden = ops.conv3d(xa, _pack(weights["conv1.conv.weight"]), bias1, x2=xb, affine=affine1, silu=True,
-                            avgpool=True, out_dtype=dtype)
+                            avgpool=True, out_dtype=dtype, stats=OUTPUT_STATS)
     else:
         if project:
             skip = ops.conv3d(xa, _pack(weights["skip_connection.conv.weight"]), weights["skip_connection.conv.bias"],
@@ -367,10 +374,10 @@ def residual_block_ncdhw(x, emb: torch.Tensor, weights: Mapping[str, torch.Tenso
         else:
             skip = xa if xb is None else ChannelConcat(xa, xb).materialize()
         hidden = ops.conv3d(xa, _pack(weights["conv1.conv.weight"], upsample=up), bias1, x2=xb, affine=affine1,
-                            silu=True, out_dtype=dtype)
+                            silu=True, out_dtype=dtype, stats=OUTPUT_STATS)
     affine2 = ops.group_norm_affine(hidden, weights["norm2.weight"], weights["norm2.bias"], groups=num_groups, eps=eps)
     return ops.conv3d(hidden, _pack(weights["conv2.conv.weight"]), weights["conv2.conv.bias"], affine=affine2,
-                      silu=True, residual=skip, residual_upsampled=up, out_dtype=dtype)
+                      silu=True, residual=skip, residual_upsampled=up, out_dtype=dtype, stats=OUTPUT_STATS)
 
 
 def vae_resblock_ncdhw(state: list, conv1, conv2, norm1, norm2, shortcut, *, num_groups: int, eps: float,
@@ -381,14 +388,15 @@ def vae_resblock_ncdhw(state: list, conv1, conv2, norm1, norm2, shortcut, *, num
     del array
     dtype = activation_dtype()
     affine1 = ops.group_norm_affine(x, norm1[0], norm1[1], groups=num_groups, eps=eps, x2=x2)
-    hidden = ops.conv3d(x, _pack(conv1[0]), conv1[1], x2=x2, affine=affine1, silu=True, out_dtype=dtype)
+    hidden = ops.conv3d(x, _pack(conv1[0]), conv1[1], x2=x2, affine=affine1, silu=True, out_dtype=dtype, stats=OUTPUT_STATS)
     if shortcut is None:
         skip = x if x2 is None else ChannelConcat(x, x2).materialize()
     else:
         skip = ops.conv3d(x, _pack(shortcut[0]), shortcut[1], x2=x2, out_dtype=dtype)
     del x, x2
     affine2 = ops.group_norm_affine(hidden, norm2[0], norm2[1], groups=num_groups, eps=eps)
-    out = ops.conv3d(hidden, _pack(conv2[0]), conv2[1], affine=affine2, silu=True, residual=skip, out_dtype=dtype)
+    out = ops.conv3d(hidden, _pack(conv2[0]), conv2[1], affine=affine2, silu=True, residual=skip, out_dtype=dtype,
+                     stats=OUTPUT_STATS)
     return out
 
 

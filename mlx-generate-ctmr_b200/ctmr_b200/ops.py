@@ -207,6 +207,7 @@ def conv3d(
     residual_upsampled: bool = False,
     out: torch.Tensor | None = None,
     out_dtype: torch.dtype | None = None,
+    stats: bool = False,
 ) -> torch.Tensor:
     """``conv(prepare(x ++ x2)) + bias (+ residual)`` in one call (``ctmr_conv3d``).
 
@@ -276,6 +277,13 @@ def conv3d(
     desc.y_dtype = _dtype_code(out.dtype)
     desc.y_cstride = ycs
     desc.y_coffset = 0
+    stats_buf = None
+    if stats:  # GroupNorm moments of the output from the conv epilogue, when its kernel can produce them
+        slots = int(LIB.ctmr_conv3d_stats_slots(ctypes.byref(desc)))
+        if slots > 0:
+            stats_buf = torch.empty((b, slots, o, 3), dtype=F32, device=x.device)
+            desc.stats = stats_buf.data_ptr()
+            desc.stats_slots = slots
     ws_bytes = int(LIB.ctmr_conv3d_workspace_size(ctypes.byref(desc)))
     ws = torch.empty(ws_bytes, dtype=torch.uint8, device=x.device) if ws_bytes else None
     ws_ptr = ws.data_ptr() if ws is not None else None
@@ -293,7 +301,23 @@ def conv3d(
         with _profiled("gemm", 2.0 * b * od * oh * ow * o * cin * taps, what):
             check(LIB.ctmr_conv3d_stages(ctypes.byref(desc), ws_ptr, ws_bytes, _lib.CONV_GEMM, _stream()),
                   "conv3d gemm")
+    if stats_buf is not None:
+        out._ctmr_stats = OutputStats(stats_buf, int(desc.stats_slots), o)
     return out
+
+
+class OutputStats:
+    """Per-(batch item, slot, channel) moments a convolution wrote for its output tensor."""
+
+    __slots__ = ("buffer", "slots", "channels")
+
+    def __init__(self, buffer: torch.Tensor, slots: int, channels: int) -> None:
+        self.buffer, self.slots, self.channels = buffer, slots, channels
+
+
+def output_stats(t: torch.Tensor | None) -> OutputStats | None:
+    """The statistics attached to ``t`` by the convolution that produced it, if any."""
+    return getattr(t, "_ctmr_stats", None) if t is not None else None
 
 
 def group_norm_affine(
@@ -314,6 +338,25 @@ def group_norm_affine(
     gamma = weight.to(dtype=F32).contiguous() if weight is not None else None
     beta = bias.to(dtype=F32).contiguous() if bias is not None else None
     affine = torch.empty((b, ctot, 2), dtype=F32, device=x.device)
+    sa, sb = output_stats(x), output_stats(x2)
+    if (sa is not None and sa.channels == c and (x2 is None or (sb is not None and sb.slots == sa.slots and
+                                                                sb.channels == ctot - c))):
+        # The producing convolutions already reduced the moments: merge them only.
+        _count(1)
+
+        def from_stats() -> None:
+            check(LIB.ctmr_group_norm_affine_from_stats(
+                sa.buffer.data_ptr(), c, sb.buffer.data_ptr() if sb is not None else None, ctot - c if sb else 0,
+                sa.slots, b, gamma.data_ptr() if gamma is not None else None,
+                beta.data_ptr() if beta is not None else None, groups, float(eps), affine.data_ptr(), _stream()),
+                "group_norm_affine_from_stats")
+
+        if PROFILE is None:
+            from_stats()
+        else:
+            with _profiled("gn", 0.0, f"{b}x{ctot} {d}x{h}x{w} g{groups} from-stats"):
+                from_stats()
+        return affine
     _count(2)
     ws_bytes = int(LIB.ctmr_group_norm_workspace_size(b, voxels, groups))
     ws = torch.empty(max(ws_bytes, 4), dtype=torch.uint8, device=x.device)

@@ -318,3 +318,53 @@ def test_narrow_output_with_half_grid_residual(cuda):
     torch.cuda.synchronize()
     expected = ops_ref.conv3d_ref(x.double(), w.double()) + ops_ref.upsample_nearest_ref(res.double())
     _close_fp32(y, expected)
+
+
+@pytest.mark.parametrize("precision", ["fp16", "bf16"])
+@pytest.mark.parametrize(("shape", "out_channels", "upsample", "k"), [
+    ((2, 64, 3, 12, 24), 128, False, 3),  # partial tiles, batch 2
+    ((1, 32, 2, 8, 16), 192, False, 3),   # 192 channels: N tiles of 128 + 64
+    ((2, 64, 3, 8, 16), 128, True, 3),    # nearest-2x fold: every parity writes its voxels
+    ((1, 128, 4, 16, 32), 256, False, 1), # 1x1x1, two N tiles
+])
+def test_output_statistics_match_a_pass(cuda, shape, out_channels, upsample, k, precision):
+    """GroupNorm moments reduced in the persistent kernel's epilogue give the affine of a separate
+    statistics pass over the stored output (and over a virtual concat of two such outputs)."""
+    from ctmr_b200 import ops
+
+    rng = np.random.default_rng(41)
+    b, c = shape[:2]
+    x = ops.to_ndhwc(torch.from_numpy(rng.standard_normal(shape).astype(np.float32)).to(cuda))
+    w = torch.from_numpy((rng.standard_normal((out_channels, c, k, k, k)) / np.sqrt(c * k ** 3)).astype(np.float32))
+    bias = torch.from_numpy(rng.standard_normal((b, out_channels)).astype(np.float32) + 3.0).to(cuda)
+    packed = ops.pack_weight(w.to(cuda), precision, upsample=upsample)
+    y = ops.conv3d(x, packed, bias, stats=True)
+    assert ops.output_stats(y) is not None, "the persistent kernel should produce statistics here"
+    gamma = torch.from_numpy(rng.standard_normal(out_channels).astype(np.float32)).to(cuda)
+    beta = torch.from_numpy(rng.standard_normal(out_channels).astype(np.float32)).to(cuda)
+    fused = ops.group_norm_affine(y, gamma, beta, groups=16, eps=1e-6)
+    plain = ops.group_norm_affine(y.clone(), gamma, beta, groups=16, eps=1e-6)  # no statistics attached
+    torch.cuda.synchronize()
+    torch.testing.assert_close(fused, plain, rtol=2e-5, atol=1e-6)
+    # Concat of two outputs (the UNet up path's cat(hidden, skip)), groups spanning the boundary.
+    y2 = ops.conv3d(x, packed, bias * 0.5, stats=True)
+    g2 = 2 * out_channels // 8 if (2 * out_channels) % 8 == 0 else 2
+    cat_gamma = torch.cat([gamma, gamma])
+    fused = ops.group_norm_affine(y, cat_gamma, None, groups=g2, eps=1e-6, x2=y2)
+    plain = ops.group_norm_affine(y.clone(), cat_gamma, None, groups=g2, eps=1e-6, x2=y2.clone())
+    torch.cuda.synchronize()
+    torch.testing.assert_close(fused, plain, rtol=2e-5, atol=1e-6)
+
+
+def test_output_statistics_refused_where_unsupported(cuda):
+    """A conv that does not run the persistent kernel reports no slots and attaches nothing."""
+    from ctmr_b200 import ops
+
+    x = ops.to_ndhwc(torch.randn((1, 64, 4, 8, 8), device=cuda))
+    w = torch.randn((4, 64, 3, 3, 3), device=cuda) / 40
+    y = ops.conv3d(x, ops.pack_weight(w, "fp32"), None, stats=True)  # narrow fp32 kernel
+    assert ops.output_stats(y) is None
+    w = torch.randn((64, 64, 3, 3, 3), device=cuda) / 40
+    y = ops.conv3d(ops.to_ndhwc(torch.randn((1, 64, 4, 8, 16), device=cuda)), ops.pack_weight(w, "fp16"), None,
+                   stats=True)  # under 128 output channels: a separate pass is cheaper
+    assert ops.output_stats(y) is None
