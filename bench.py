@@ -184,7 +184,9 @@ SWEEP_SHAPES = [(b, c, n, n, n, o) for n in (16, 32, 64) for c, o in ((32, 32), 
 
 
 def _time_conv(shape, precision: str, iters: int, dev, input_kind: str = "plain") -> tuple[float, float, float]:
-    """Median GEMM ms, its TFLOP/s and the median prepare ms of one conv3d shape (output grid D, H, W).
+    """Device ms of one GEMM launch, its TFLOP/s, and the prepare stage's ms, for one conv3d shape
+    (output grid D, H, W): each stage is captured in its own CUDA graph and replayed ``iters`` times
+    back to back, so no host gap enters the CUDA-event time (inputs below L2 size stay resident).
 
     ``input_kind``: plain (the input as is), norm (group-norm affine + SiLU applied
     by the prepare pass) or tri (trilinear 2x upsampling of a half-grid input).
@@ -209,14 +211,52 @@ def _time_conv(shape, precision: str, iters: int, dev, input_kind: str = "plain"
         ops.conv3d(x, packed, bias, **kw)
     prof: list = []
     ops.PROFILE = prof
-    for _ in range(iters):
-        ops.conv3d(x, packed, bias, **kw)
+    ops.conv3d(x, packed, bias, **kw)
     ops.PROFILE = None
     torch.cuda.synchronize(dev)
     gemm = [r for r in prof if r["kind"] == "gemm"]
-    prep = [r["start"].elapsed_time(r["end"]) for r in prof if r["kind"] == "prepare"]
-    ms = statistics.median(r["start"].elapsed_time(r["end"]) for r in gemm)
-    return ms, gemm[0]["flops"] / (ms * 1e-3) / 1e12, statistics.median(prep) if prep else 0.0
+    flops = gemm[0]["flops"]
+    # Device time of each stage without host gaps: one CUDA graph per stage, replayed back to back.
+    from ctmr_b200 import _lib
+
+    need = _conv_workspace_bytes(x, packed, bias, kw)
+    ws = torch.empty(max(need, 1), dtype=torch.uint8, device=dev)
+    out = ops.conv3d(x, packed, bias, **kw, workspace=ws, stages=_lib.CONV_PREPARE | _lib.CONV_GEMM)
+    times = {}
+    for name, stage in (("prepare", _lib.CONV_PREPARE), ("gemm", _lib.CONV_GEMM)):
+        if stage == _lib.CONV_PREPARE and need == 0:
+            times[name] = 0.0
+            continue
+        side = torch.cuda.Stream(dev)
+        side.wait_stream(torch.cuda.current_stream(dev))
+        with torch.cuda.stream(side):
+            ops.conv3d(x, packed, bias, **kw, out=out, workspace=ws, stages=stage)
+        torch.cuda.current_stream(dev).wait_stream(side)
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph):
+            ops.conv3d(x, packed, bias, **kw, out=out, workspace=ws, stages=stage)
+        for _ in range(3):
+            graph.replay()
+        start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        start.record()
+        for _ in range(iters):
+            graph.replay()
+        end.record()
+        torch.cuda.synchronize(dev)
+        times[name] = start.elapsed_time(end) / iters
+    ms = times["gemm"]
+    return ms, flops / (ms * 1e-3) / 1e12, times["prepare"]
+
+
+def _conv_workspace_bytes(x, packed, bias, kw) -> int:
+    """Workspace bytes ops.conv3d needs for this call (by asking with an empty workspace)."""
+    from ctmr_b200 import ops
+
+    try:
+        ops.conv3d(x, packed, bias, **kw, workspace=torch.empty(0, dtype=torch.uint8, device=x.device), stages=2)
+    except ops.WorkspaceTooSmall as e:
+        return e.needed
+    return 0
 
 
 def _total_ms(records) -> float:

@@ -208,6 +208,8 @@ def conv3d(
     out: torch.Tensor | None = None,
     out_dtype: torch.dtype | None = None,
     stats: bool = False,
+    workspace: torch.Tensor | None = None,
+    stages: int | None = None,
 ) -> torch.Tensor:
     """``conv(prepare(x ++ x2)) + bias (+ residual)`` in one call (``ctmr_conv3d``).
 
@@ -285,8 +287,17 @@ def conv3d(
             desc.stats = stats_buf.data_ptr()
             desc.stats_slots = slots
     ws_bytes = int(LIB.ctmr_conv3d_workspace_size(ctypes.byref(desc)))
-    ws = torch.empty(ws_bytes, dtype=torch.uint8, device=x.device) if ws_bytes else None
+    if workspace is not None:  # caller-held workspace (e.g. to time the GEMM stage alone)
+        if workspace.numel() < ws_bytes:
+            raise WorkspaceTooSmall(ws_bytes, workspace.numel())
+        ws = workspace
+    else:
+        ws = torch.empty(ws_bytes, dtype=torch.uint8, device=x.device) if ws_bytes else None
     ws_ptr = ws.data_ptr() if ws is not None else None
+    if stages is not None:  # one or both stages (_lib.CONV_PREPARE | _lib.CONV_GEMM)
+        _count(1)
+        check(LIB.ctmr_conv3d_stages(ctypes.byref(desc), ws_ptr, ws_bytes, int(stages), _stream()), "conv3d stages")
+        return out
     _count(2 if ws_bytes else 1)
     if PROFILE is None:
         check(LIB.ctmr_conv3d(ctypes.byref(desc), ws_ptr, ws_bytes, _stream()), "conv3d")
@@ -304,6 +315,14 @@ def conv3d(
     if stats_buf is not None:
         out._ctmr_stats = OutputStats(stats_buf, int(desc.stats_slots), o)
     return out
+
+
+class WorkspaceTooSmall(ValueError):
+    """A caller-held conv3d workspace is smaller than the call needs (``needed`` bytes)."""
+
+    def __init__(self, needed: int, given: int) -> None:
+        super().__init__(f"conv3d workspace holds {given} bytes, needs {needed}")
+        self.needed = needed
 
 
 class OutputStats:
