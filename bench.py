@@ -178,6 +178,11 @@ def run_reference(args, rank: int) -> None:
 
 
 # ---------------------------------------------------------------- kernel-level cases
+# The bench roofline's launch: the VAE decoder's full-resolution 64 -> 64 conv (B, C, D, H, W, O),
+# and the DRAM bytes per output voxel ncu measured for that kernel (248.5 MB over 786,432 voxels).
+DOMINANT_CONV = (1, 64, 96, 256, 128, 64)
+DOMINANT_TRAFFIC_PER_VOXEL = (101.009664e6 + 147.503104e6) / 786432
+
 SWEEP_SHAPES = [(b, c, n, n, n, o) for n in (16, 32, 64) for c, o in ((32, 32), (64, 64), (128, 128), (256, 256))
                 for b in (1, 2)] + [(2, 512, 8, 8, 4, 512), (2, 512, 16, 16, 8, 512), (1, 128, 128, 128, 64, 128),
                                     (1, 64, 128, 128, 64, 64)]
@@ -507,14 +512,32 @@ def main() -> None:
         conv_ms = STEPS_RFLOW * _total_ms(unet_gemm) + _total_ms(vae_gemm)
         conv_flop = STEPS_RFLOW * sum(r["flops"] for r in unet_gemm) + sum(r["flops"] for r in vae_gemm)
         n_launch = STEPS_RFLOW * len(unet_gemm) + len(vae_gemm)
-        achieved = conv_flop / (conv_ms * 1e-3) / 1e12
-        peak = float(peaks.get("bf16_tflops_sustained", FALLBACK_PEAKS["bf16_tflops_sustained"]))
-        roofline = {"bound": "tensor", "achieved": round(achieved, 1), "peak": peak, "unit": "TFLOP/s",
-                    "frac": round(achieved / peak, 4), "traffic": None,
-                    "kernel": "conv3d_umma_kernel (implicit-GEMM conv3d, all launches of one volume)",
-                    "launches_per_volume": n_launch, "algorithmic_tflop_per_volume": round(conv_flop / 1e12, 2),
-                    "conv_ms_per_volume": round(conv_ms, 2), "peak_source": f"{peak_kind} bf16_tflops_sustained",
-                    "share_of_step": round(conv_ms / ms, 3)}
+        agg = conv_flop / (conv_ms * 1e-3) / 1e12
+        sustained = float(peaks.get("bf16_tflops_sustained", FALLBACK_PEAKS["bf16_tflops_sustained"]))
+        burst = float(peaks.get("bf16_tflops", FALLBACK_PEAKS["bf16_tflops"]))
+        # The largest launch class: the decoder's full-resolution 64 -> 64 conv (GN + SiLU input),
+        # one launch timed by CUDA-graph replay on the device (no host gaps), against the burst peak.
+        dom_ms, dom_tflops, dom_prep_ms = _time_conv(DOMINANT_CONV, args.precision, 5, dev, "norm")
+        b_, c_, d_, h_, w_, o_ = DOMINANT_CONV
+        vox = b_ * d_ * h_ * w_
+        roofline = {"bound": "tensor", "achieved": round(dom_tflops, 1), "peak": burst, "unit": "TFLOP/s",
+                    "frac": round(dom_tflops / burst, 4),
+                    "traffic": round(DOMINANT_TRAFFIC_PER_VOXEL * vox),
+                    "kernel": "conv3d_umma_v2_kernel<64,2,3>: VAE decoder full-resolution 64->64 conv "
+                              f"{b_}x{c_}x{d_}x{h_}x{w_} (GN affine + SiLU input), the largest launch class",
+                    "launch_ms": round(dom_ms, 4), "prepare_ms": round(dom_prep_ms, 4),
+                    "algorithmic_bytes": vox * (c_ * 2 + o_ * 4),
+                    "traffic_source": "ncu dram__bytes_read+write of the same kernel on 1x64x48x128x128 "
+                                      "(profiles/conv3d_umma_v2_fp16_64to64_48x128x128.md), scaled by voxels",
+                    "peak_source": f"{peak_kind} bf16_tflops (burst: one launch timed alone)",
+                    "all_conv_launches": {"achieved": round(agg, 1), "peak": sustained,
+                                          "frac": round(agg / sustained, 4),
+                                          "peak_source": f"{peak_kind} bf16_tflops_sustained",
+                                          "launches_per_volume": n_launch,
+                                          "algorithmic_tflop_per_volume": round(conv_flop / 1e12, 2),
+                                          "conv_ms_per_volume": round(conv_ms, 2),
+                                          "share_of_step": round(conv_ms / ms, 3),
+                                          "timing": "CUDA events around each GEMM stage in an eager pass"}}
 
     if rank == 0:
         base = None
