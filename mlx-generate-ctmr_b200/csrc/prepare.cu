@@ -600,6 +600,55 @@ __global__ void __launch_bounds__(256) im2col_kernel(const PrepParams p, const i
   }
 }
 
+// Four input channels (the 4-channel latent): one item = one voxel x two taps,
+// i.e. the 8 consecutive columns [8p, 8p + 8) written as one 16-byte store, from
+// two 16-byte neighbour loads (tap 27 is the zero padding up to 112 columns).
+template <int OUTK>
+__global__ void __launch_bounds__(256) im2col4_kernel(const PrepParams p, const FastDiv pdiv, const FastDiv wdiv,
+                                                      const FastDiv hdiv, const unsigned items) {
+  griddep_wait();  // the preceding kernel's writes are visible from here on
+  griddep_launch_dependents();
+  const int b = blockIdx.y;
+  const unsigned vox = static_cast<unsigned>(p.od) * p.oh * p.ow;
+  const PrepSource& s = p.src[0];
+  for (unsigned item = blockIdx.x * blockDim.x + threadIdx.x; item < items; item += gridDim.x * blockDim.x) {
+    const unsigned v = fdiv(pdiv, item);
+    const int pair = static_cast<int>(item - v * pdiv.d);
+    const unsigned yz = fdiv(wdiv, v);
+    const int x = static_cast<int>(v - yz * wdiv.d);
+    const unsigned z = fdiv(hdiv, yz);
+    const int y = static_cast<int>(yz - z * hdiv.d);
+    float out[8];
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {
+      const int tap = 2 * pair + h;
+      float4 q = make_float4(0.f, 0.f, 0.f, 0.f);
+      if (tap < 27) {
+        const int gz = static_cast<int>(z) + tap / 9 - 1, gy = y + (tap / 3) % 3 - 1, gx = x + tap % 3 - 1;
+        if (gz >= 0 && gz < p.od && gy >= 0 && gy < p.oh && gx >= 0 && gx < p.ow) {
+          const long long src = ((static_cast<long long>(b) * p.od + gz) * p.oh + gy) * p.ow + gx;
+          q = __ldg(reinterpret_cast<const float4*>(static_cast<const float*>(s.ptr) + src * s.cstride));
+          float t[4] = {q.x, q.y, q.z, q.w};
+#pragma unroll
+          for (int c = 0; c < 4; ++c) {
+            if (p.affine != nullptr) {
+              const float* a = p.affine + (static_cast<long long>(b) * 4 + c) * 2;
+              t[c] = fmaf(t[c], __ldg(a), __ldg(a + 1));
+            }
+            if (p.silu) t[c] = silu_f<false>(t[c]);
+          }
+          q = make_float4(t[0], t[1], t[2], t[3]);
+        }
+      }
+      out[4 * h] = q.x;
+      out[4 * h + 1] = q.y;
+      out[4 * h + 2] = q.z;
+      out[4 * h + 3] = q.w;
+    }
+    store_vec<OUTK, 8>(p, (static_cast<long long>(b) * vox + v) * p.out_cstride + 8 * pair, out);
+  }
+}
+
 // Packed weights [27][opad][cpad_src] (hi and, for the split kind, lo) ->
 // [opad][kdense] with column tap * cin + c, zero past 27 * cin.
 __global__ void repack_im2col_kernel(const uint16_t* __restrict__ hi, const uint16_t* __restrict__ lo, int opad,
@@ -664,6 +713,25 @@ namespace ctmr {
 
 cudaError_t launch_im2col(const PrepParams& p, int cin, int kdense, cudaStream_t stream) {
   if (cin < 1 || cin > 4 || kdense % 8 || kdense < 27 * cin || p.out_cstride % 8) return cudaErrorInvalidValue;
+  const PrepSource& s0 = p.src[0];
+  if (cin == 4 && kdense == 112 && !s0.bf16 && s0.cstride % 4 == 0 &&
+      (reinterpret_cast<uintptr_t>(s0.ptr) & 15) == 0 && p.out_kind != kPrepOutF32) {
+    const FastDiv pd = make_fastdiv(14), wd = make_fastdiv(static_cast<uint32_t>(p.ow)),
+                  hd = make_fastdiv(static_cast<uint32_t>(p.oh));
+    const long long items = static_cast<long long>(p.od) * p.oh * p.ow * 14;
+    if (items >= (1LL << 31)) return cudaErrorInvalidValue;
+    long long blocks = (items + 255) / 256;
+    const long long cap = 148LL * 8 / p.batch + 1;
+    if (blocks > cap) blocks = cap;
+    const dim3 grid(static_cast<unsigned>(blocks), static_cast<unsigned>(p.batch));
+    const unsigned n = static_cast<unsigned>(items);
+    switch (p.out_kind) {
+      case kPrepOutBF16: launch_kernel(im2col4_kernel<kPrepOutBF16>, grid, 256, 0, stream, p, pd, wd, hd, n); break;
+      case kPrepOutF16: launch_kernel(im2col4_kernel<kPrepOutF16>, grid, 256, 0, stream, p, pd, wd, hd, n); break;
+      default: launch_kernel(im2col4_kernel<kPrepOutSplitF16>, grid, 256, 0, stream, p, pd, wd, hd, n); break;
+    }
+    return cudaGetLastError();
+  }
   const long long items = static_cast<long long>(p.od) * p.oh * p.ow * (kdense / 8);
   if (items >= (1LL << 31)) return cudaErrorInvalidValue;
   long long blocks = (items + 255) / 256;

@@ -115,14 +115,15 @@ NARROW_CHANNELS = 16
 def conv_precision(weight: torch.Tensor) -> str:
     """Operand precision of one convolution under the active mode.
 
-    In the 16-bit modes the narrow input and output convolutions (at most 16
+    In the bf16 mode the narrow input and output convolutions (at most 16
     channels on either side: the latent-facing conv_in / post_quant_conv and the
-    4- or 1-channel output convs) keep the split-fp32 operands. Those layers are
-    memory-bound, so the extra operand plane costs no measurable time, and the
-    output conv otherwise dominates the decoded volume's error budget.
+    4- or 1-channel output convs) keep the split-fp32 operands: with bf16's 8-bit
+    significand the output conv otherwise dominates the decoded volume's error
+    budget. fp16's 11-bit significand keeps them within it, so the fp16 mode runs
+    them on the tensor cores like every other layer.
     """
     precision = _precision.get()
-    if precision != "fp32" and min(int(weight.shape[0]), int(weight.shape[1])) <= NARROW_CHANNELS:
+    if precision == "bf16" and min(int(weight.shape[0]), int(weight.shape[1])) <= NARROW_CHANNELS:
         return "fp32"
     return precision
 
@@ -168,8 +169,17 @@ def dense_dtype() -> torch.dtype:
     return {"fp32": torch.float32, "bf16": torch.bfloat16, "fp16": torch.float16}[_precision.get()]
 
 
-def _pack(weight: torch.Tensor, *, upsample: bool = False) -> ops.PackedWeight:
+# At or above this many output voxels a <= 4-output-channel conv runs faster on the
+# direct fp32 kernel than as an N = 16 tensor-core GEMM (measured: the VAE decoder's
+# 64 -> 1 conv on 96 x 256 x 128 voxels, 0.71 ms vs 1.24 ms with its operand pass;
+# the UNet's 64 -> 4 on 2 x 64 x 64 x 32 voxels prefers the GEMM, 0.11 vs 0.22 ms).
+NARROW_DIRECT_VOXELS = 1 << 21
+
+
+def _pack(weight: torch.Tensor, *, upsample: bool = False, out_voxels: int = 0) -> ops.PackedWeight:
     precision = conv_precision(weight)
+    if precision == "fp16" and int(weight.shape[0]) <= 4 and out_voxels >= NARROW_DIRECT_VOXELS:
+        precision = "fp32"
     key = (id(weight), upsample, precision)
     hit = _packed.get(key)
     if hit is not None and hit[0]() is weight:
@@ -285,7 +295,11 @@ def norm_conv3d_ncdhw(array, weight: torch.Tensor, bias: torch.Tensor, *, norm, 
     if residual is not None:
         res = residual if isinstance(residual, torch.Tensor) else residual.materialize()
         res = ops.to_ndhwc(res)
-    return ops.conv3d(x, _pack(weight, upsample=upsample), bias, x2=x2, affine=affine, silu=apply_silu,
+    b, _, d, h, w = (int(n) for n in x.shape)
+    scale = 8 if upsample else 1
+    voxels = b * d * h * w * scale // (8 if avgpool else 1)
+    return ops.conv3d(x, _pack(weight, upsample=upsample, out_voxels=voxels), bias, x2=x2, affine=affine,
+                      silu=apply_silu,
                       avgpool=avgpool, residual=res, residual_upsampled=residual_upsampled,
                       out_dtype=activation_dtype(), stats=OUTPUT_STATS)
 

@@ -112,6 +112,25 @@ def output_intensities(decoded: np.ndarray, *, configuration: str = "ct") -> np.
     return scaled.astype(np.int16)
 
 
+def output_intensities_device(decoded: torch.Tensor, *, configuration: str = "ct") -> torch.Tensor:
+    """``output_intensities`` on the device, returning int16 on the same device.
+
+    The same float32 operations in the same order (a multiply, then the offset for
+    CT, then the clip; no fused multiply-add) and the same float -> int16 cast
+    (toward zero through int32, wrapping out-of-range values as numpy's astype
+    does), so the result is bitwise the host function's; only the int16 volume
+    crosses to the host.
+    """
+    if not bool(torch.isfinite(decoded).all()):
+        raise ValueError("decoded image must be finite")
+    data = decoded.to(torch.float32)
+    if configuration == "ct":
+        scaled = torch.clamp(torch.sub(torch.mul(data, 2000.0), 1000.0), -1000.0, 1000.0)
+    else:
+        scaled = torch.clamp(torch.mul(data, 1000.0), min=0.0)
+    return scaled.to(torch.int32).to(torch.int16)
+
+
 def init_latent_ncdhw(shape: Sequence[int], *, seed: int, device) -> torch.Tensor:
     """Seeded N(0, 1) fp32 latent. (The reference seeds MLX's generator, whose stream cannot be reproduced here.)"""
     gen = torch.Generator(device=device).manual_seed(int(seed))
@@ -347,7 +366,7 @@ def sample_image_ncdhw(output_size: Sequence[int], spacing_mm: Sequence[float], 
                                           scale_factor=scale_factor)
     image = None
     if to_host:
-        image = output_intensities(decoded.cpu().numpy(), configuration=configuration)
+        image = output_intensities_device(decoded, configuration=configuration).contiguous().cpu().numpy()
     torch.cuda.synchronize(device)
     return ImageResult(final, decoded, image, np.diag((*map(float, spacing_mm), 1.0)),
                        {"rflow_unet": rflow_s, "vae_decode": time.perf_counter() - started})

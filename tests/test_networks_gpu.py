@@ -233,3 +233,18 @@ def test_no_device_wait_timed_out(cuda):
     from ctmr_b200 import _lib
 
     assert _lib.device_error(clear=True) == 0
+
+
+@pytest.mark.parametrize("configuration", ["ct", "mr-brain"])
+def test_output_intensities_on_device_match_host(cuda, configuration):
+    """The device int16 conversion is bitwise the host one (``image.py:68-87``), incl. clipping and
+    the out-of-range wrap of the cast."""
+    from ctmr_b200 import pipeline as P
+
+    rng = np.random.default_rng(43)
+    decoded = (rng.standard_normal((1, 1, 9, 10, 11)) * 3).astype(np.float32)
+    decoded.flat[:5] = [40.0, -40.0, 0.49999997, 1.0000001, 32.7675]  # beyond int16 after x1000, halves, edges
+    dev = P.output_intensities_device(torch.from_numpy(decoded).to(cuda), configuration=configuration).cpu().numpy()
+    host = P.output_intensities(decoded, configuration=configuration)
+    assert dev.dtype == np.int16 and dev.shape == host.shape
+    np.testing.assert_array_equal(dev, host)
