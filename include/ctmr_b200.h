@@ -99,6 +99,16 @@ typedef struct ctmr_conv3d_desc {
    * (> 0). Null: none. */
   float* stats;
   int stats_slots;
+  /* Optional GroupNorm of the input computed inside the call (instead of passing
+   * `affine`): gamma/beta per input channel (NULL: 1/0), gn_groups > 0 groups over
+   * x ++ x2, gn_eps. The statistics are those of ctmr_group_norm_affine, reduced by
+   * the call before its operand pass (with CTMR_GN_FUSED=1 in the environment, small
+   * tensors use one kernel that reduces them and writes the operand). `affine` must
+   * be NULL. */
+  const float* gn_gamma;
+  const float* gn_beta;
+  int gn_groups;
+  float gn_eps;
 } ctmr_conv3d_desc;
 
 /* Packed-weight element count per plane for a Torch (O, C, k, k, k) weight:
@@ -157,6 +167,10 @@ CTMR_API size_t ctmr_group_norm_workspace_size(int batch, long long voxels, int 
 CTMR_API int ctmr_group_norm_affine(ctmr_tensor x, ctmr_tensor x2, int batch, long long voxels, const float* gamma,
                            const float* beta, int groups, float eps, float* affine, void* workspace,
                            size_t workspace_bytes, void* stream);
+
+/* Kernel launches one ctmr_conv3d call with this descriptor issues (instrumentation;
+ * no reference counterpart), or 0 for an invalid descriptor. */
+CTMR_API int ctmr_conv3d_launch_count(const ctmr_conv3d_desc* desc);
 
 /* Statistics slots a convolution writes when desc->stats is set (its persistent
  * kernel's CTA count bound), or 0 when this convolution does not produce them (it

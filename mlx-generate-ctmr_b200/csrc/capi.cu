@@ -172,10 +172,15 @@ struct ConvPlan {
   int cin_raw, cpad_src;    // im2col: input channels and the packed weights' channel padding
   size_t prep_bytes;        // per plane
   size_t wrep_bytes;        // im2col: repacked weights, per plane
+  bool gn_in;               // the call computes the input's GroupNorm itself
+  bool gn_small;            // ... in the fused small-tensor operand kernel
+  size_t gn_bytes;          // workspace for the affine [+ statistics partials] otherwise
+  int gn_chunks;
   // per-tap kernel tiling and its split-K
   int tile_w, tile_h, tile_d, tiles_w, tiles_h, tiles_d, n_tiles, ksplit;
   size_t part_bytes;
-  size_t workspace() const { return (prep_bytes + wrep_bytes) * (exact ? 2 : 1) + part_bytes; }
+  size_t workspace() const { return (prep_bytes + wrep_bytes) * (exact ? 2 : 1) + part_bytes + gn_bytes; }
+  size_t gn_offset() const { return (prep_bytes + wrep_bytes) * (exact ? 2 : 1) + part_bytes; }
 };
 
 int plan_conv(const ctmr_conv3d_desc* d, ConvPlan* p) {
@@ -203,13 +208,15 @@ int plan_conv(const ctmr_conv3d_desc* d, ConvPlan* p) {
     return fail(CTMR_ERR_UNSUPPORTED, "1x1x1 convolutions support stride 1 only");
   if (d->kernel_size != 1 && d->kernel_size != 3) return fail(CTMR_ERR_UNSUPPORTED, "kernel_size must be 1 or 3");
   if (d->stride != 1 && d->stride != 2) return fail(CTMR_ERR_UNSUPPORTED, "stride must be 1 or 2");
-  if (d->trilinear && (d->affine != nullptr || d->silu))
+  if (d->trilinear && (d->affine != nullptr || d->silu || d->gn_groups > 0))
     return fail(CTMR_ERR_UNSUPPORTED, "trilinear packing supports only a plain convolution");
   if (d->avgpool && (d->depth % 2 || d->height % 2 || d->width % 2))
     return fail(CTMR_ERR_INVALID, "average pooling needs even extents");
   if (d->stride == 2 && (d->depth < 2 || d->height < 2 || d->width < 2))
     return fail(CTMR_ERR_UNSUPPORTED, "stride-2 convolution needs extents >= 2");
 
+  if (d->gn_groups < 0 || (d->gn_groups > 0 && d->affine != nullptr))
+    return fail(CTMR_ERR_INVALID, "pass either an input affine or gn_groups, not both");
   p->exact = d->precision == CTMR_PRECISION_FP32;
   p->bf16 = d->precision == CTMR_PRECISION_BF16;
   p->cin = d->x.channels + (d->x2.data ? d->x2.channels : 0);
@@ -245,7 +252,8 @@ int plan_conv(const ctmr_conv3d_desc* d, ConvPlan* p) {
   }
   // The raw input can be the MMA operand directly only in bf16 mode, with no
   // transform, 16-channel granularity and 16-byte aligned rows.
-  const bool direct = p->bf16 && d->x2.data == nullptr && d->affine == nullptr && !d->silu && !d->trilinear &&
+  const bool direct = p->bf16 && d->x2.data == nullptr && d->affine == nullptr && d->gn_groups == 0 && !d->silu &&
+                      !d->trilinear &&
                       !d->avgpool && d->x.dtype == CTMR_DTYPE_BF16 && d->x.channels % 16 == 0 &&
                       d->x.cstride % 8 == 0 && aligned16(d->x.data);
   // Narrow outputs (<= 4 channels, e.g. the UNet / VAE output convolutions) with split-fp32
@@ -314,6 +322,24 @@ int plan_conv(const ctmr_conv3d_desc* d, ConvPlan* p) {
                                 : 0;
   p->part_bytes = static_cast<size_t>(round_up(static_cast<long long>(p->part_bytes), 256));
   if (p->narrow || p->tiny) p->part_bytes = 0;
+  // GroupNorm of the input inside the call.
+  p->gn_in = d->gn_groups > 0;
+  p->gn_small = false;
+  p->gn_bytes = 0;
+  p->gn_chunks = 0;
+  if (p->gn_in) {
+    const long long voxels = static_cast<long long>(d->depth) * d->height * d->width;
+    if (p->cin % d->gn_groups != 0) return fail(CTMR_ERR_INVALID, "gn_groups must divide the input channels");
+    if (p->cin > 2048) return fail(CTMR_ERR_UNSUPPORTED, "group_norm supports at most 2048 channels");
+    p->gn_small = p->prepare && !p->im2col && !d->trilinear && !d->avgpool &&
+                  ctmr::gn_prepare_small_fits(voxels, p->cin, d->gn_groups) &&
+                  getenv("CTMR_GN_FUSED") != nullptr;  // opt-in: slower in the MAISI UNet step (6.39 vs 6.26 ms)
+    if (!p->gn_small) {
+      p->gn_chunks = ctmr::gn_chunks_for(d->batch, voxels, p->cin);
+      p->gn_bytes = static_cast<size_t>(round_up(static_cast<long long>(d->batch) * p->cin * 2 * 4, 256)) +
+                    static_cast<size_t>(d->batch) * ctmr::gn_max_chunks(d->batch) * d->gn_groups * 3 * sizeof(float);
+    }
+  }
   return CTMR_OK;
 }
 
@@ -423,6 +449,29 @@ int ctmr_conv3d_stages(const ctmr_conv3d_desc* d, void* workspace, size_t worksp
     return fail(CTMR_ERR_WORKSPACE, "conv3d needs %zu workspace bytes, got %zu", need, workspace_bytes);
   if (d->stats != nullptr && (p.narrow || p.tiny))
     return fail(CTMR_ERR_UNSUPPORTED, "output statistics need the persistent kernel (ctmr_conv3d_stats_slots)");
+  // GroupNorm of the input inside the call: the statistics pass writes the affine
+  // into the workspace (the fused small-tensor operand kernel needs none).
+  const float* affine = d->affine;
+  if (p.gn_in && !p.gn_small) {
+    float* gn_affine = reinterpret_cast<float*>(static_cast<uint8_t*>(workspace) + p.gn_offset());
+    affine = gn_affine;
+    if (stages & CTMR_CONV_PREPARE) {
+      ctmr::GnParams gp{};
+      gp.src[0] = as_source(d->x);
+      gp.src[1] = as_source(d->x2);
+      gp.batch = d->batch;
+      gp.voxels = static_cast<long long>(d->depth) * d->height * d->width;
+      gp.groups = d->gn_groups;
+      gp.eps = d->gn_eps;
+      gp.gamma = d->gn_gamma;
+      gp.beta = d->gn_beta;
+      gp.affine = gn_affine;
+      gp.partials = gn_affine + round_up(static_cast<long long>(d->batch) * p.cin * 2, 64);
+      gp.chunks = p.gn_chunks;
+      cudaError_t e = ctmr::launch_group_norm_affine(gp, stream);
+      if (e != cudaSuccess) return cuda_fail(e, "group_norm launch");
+    }
+  }
 
   if (p.narrow) {
     if (!(stages & CTMR_CONV_GEMM)) return CTMR_OK;
@@ -432,7 +481,7 @@ int ctmr_conv3d_stages(const ctmr_conv3d_desc* d, void* workspace, size_t worksp
     np.vec4 = (d->x.cstride % 4 == 0) && (reinterpret_cast<uintptr_t>(d->x.data) % 16 == 0);
     np.batch = d->batch, np.d = d->depth, np.h = d->height, np.w = d->width;
     np.cin = p.cin, np.cout = d->out_channels;
-    np.affine = d->affine;
+    np.affine = affine;
     np.silu = d->silu;
     np.w_hi = static_cast<const __half*>(d->weight);
     np.w_lo = static_cast<const __half*>(d->weight_lo);
@@ -455,7 +504,7 @@ int ctmr_conv3d_stages(const ctmr_conv3d_desc* d, void* workspace, size_t worksp
     tp.vec4 = (d->x.cstride % 4 == 0) && (reinterpret_cast<uintptr_t>(d->x.data) % 16 == 0);
     tp.batch = d->batch, tp.d = d->depth, tp.h = d->height, tp.w = d->width;
     tp.cin = p.cin, tp.cout = d->out_channels;
-    tp.affine = d->affine;
+    tp.affine = affine;
     tp.silu = d->silu;
     tp.w_hi = static_cast<const __half*>(d->weight);
     tp.w_lo = static_cast<const __half*>(d->weight_lo);
@@ -492,7 +541,7 @@ int ctmr_conv3d_stages(const ctmr_conv3d_desc* d, void* workspace, size_t worksp
     pp.src[0] = as_source(d->x);
     pp.batch = d->batch;
     pp.sd = pp.od = d->depth, pp.sh = pp.oh = d->height, pp.sw = pp.ow = d->width;
-    pp.affine = d->affine;
+    pp.affine = affine;
     pp.silu = d->silu;
     pp.cpad = p.cpad;
     pp.out_cstride = p.cpad;
@@ -512,14 +561,16 @@ int ctmr_conv3d_stages(const ctmr_conv3d_desc* d, void* workspace, size_t worksp
     pp.sd = d->depth, pp.sh = d->height, pp.sw = d->width;
     pp.od = p.in_d, pp.oh = p.in_h, pp.ow = p.in_w;
     pp.mode = d->trilinear ? ctmr::kPrepTrilinear : (d->avgpool ? ctmr::kPrepAvgPool : ctmr::kPrepCopy);
-    pp.affine = d->affine;
+    pp.affine = affine;
     pp.silu = d->silu;
     pp.cpad = p.cpad;
     pp.out_cstride = p.cpad;
     pp.out_kind = p.exact ? ctmr::kPrepOutSplitF16 : (p.bf16 ? ctmr::kPrepOutBF16 : ctmr::kPrepOutF16);
     pp.out = workspace;
     pp.out_lo = p.exact ? static_cast<uint8_t*>(workspace) + p.prep_bytes : nullptr;
-    cudaError_t e = ctmr::launch_prepare(pp, stream);
+    cudaError_t e = p.gn_small ? ctmr::launch_gn_prepare_small(pp, d->gn_gamma, d->gn_beta, d->gn_groups, d->gn_eps,
+                                                              stream)
+                               : ctmr::launch_prepare(pp, stream);
     if (e != cudaSuccess) return cuda_fail(e, "prepare launch");
   }
   if (!(stages & CTMR_CONV_GEMM)) return CTMR_OK;
@@ -711,6 +762,17 @@ int ctmr_conv3d_stats_slots(const ctmr_conv3d_desc* d) {
   V2Plan v2{};
   if (p.narrow || p.tiny || !plan_v2(p, d, true, &v2)) return 0;
   return sm_count();
+}
+
+int ctmr_conv3d_launch_count(const ctmr_conv3d_desc* d) {
+  ConvPlan p{};
+  if (d == nullptr || plan_conv(d, &p) != CTMR_OK) return 0;
+  int n = (p.gn_in && !p.gn_small) ? 2 : 0;
+  if (p.narrow || p.tiny) return n + 1;
+  if (p.prepare) n += p.im2col ? 2 : 1;
+  V2Plan v2{};
+  if (plan_v2(p, d, d->stats != nullptr, &v2)) return n + 1;
+  return n + 1 + (p.ksplit > 1 ? 1 : 0);
 }
 
 int ctmr_group_norm_affine_from_stats(const float* stats_a, int channels_a, const float* stats_b, int channels_b,

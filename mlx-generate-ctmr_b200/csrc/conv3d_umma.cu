@@ -290,7 +290,9 @@ __global__ void __launch_bounds__(kThreads, 1)
         } else if (valid && n < g.cout) {
           if (bias != nullptr) {
             const int cnt = min(16, g.cout - n);
-            for (int i = 0; i < cnt; ++i) v[i] += __ldg(bias + n + i);
+#pragma unroll
+            for (int i = 0; i < 16; ++i)
+              if (i < cnt) v[i] += __ldg(bias + n + i);
           }
           store_row16(g, v, n, out_base + n, res_base + n);
         }
@@ -338,7 +340,9 @@ __global__ void splitk_reduce_kernel(const ConvGeom g) {
     const int cnt = min(4, g.cout - n);
     if (g.bias != nullptr) {
       const float* bias = g.bias + static_cast<long long>(b) * g.bias_bstride;
-      for (int k = 0; k < cnt; ++k) v[k] += __ldg(bias + n + k);
+#pragma unroll
+      for (int k = 0; k < 4; ++k)
+        if (k < cnt) v[k] += __ldg(bias + n + k);
     }
     const long long vox = ((static_cast<long long>(b) * g.out_d + rd) * g.out_h + rh) * g.out_w + rw;
     long long res_base = 0;

@@ -34,7 +34,9 @@ __device__ __forceinline__ void store_row16(const ConvGeom& g, float (&v)[16], i
           v[2 * i + 1] += bf16_to_f32(static_cast<uint16_t>(w[i] >> 16));
         }
       } else {
-        for (int i = 0; i < cnt; ++i) v[i] += bf16_to_f32(r[i]);
+#pragma unroll
+        for (int i = 0; i < 16; ++i)
+          if (i < cnt) v[i] += bf16_to_f32(r[i]);
       }
     } else {
       const float* r = static_cast<const float*>(g.res) + res_off;
@@ -48,7 +50,9 @@ __device__ __forceinline__ void store_row16(const ConvGeom& g, float (&v)[16], i
           v[4 * i + 3] += q.w;
         }
       } else {
-        for (int i = 0; i < cnt; ++i) v[i] += __ldg(r + i);
+#pragma unroll
+        for (int i = 0; i < 16; ++i)
+          if (i < cnt) v[i] += __ldg(r + i);
       }
     }
   }
@@ -67,9 +71,12 @@ __device__ __forceinline__ void store_row16(const ConvGeom& g, float (&v)[16], i
       reinterpret_cast<uint4*>(o)[0] = q0;
       reinterpret_cast<uint4*>(o)[1] = q1;
     } else {
-      for (int i = 0; i < cnt; ++i) {
-        __nv_bfloat16 h = __float2bfloat16_rn(v[i]);
-        o[i] = *reinterpret_cast<uint16_t*>(&h);
+#pragma unroll
+      for (int i = 0; i < 16; ++i) {
+        if (i < cnt) {
+          __nv_bfloat16 h = __float2bfloat16_rn(v[i]);
+          o[i] = *reinterpret_cast<uint16_t*>(&h);
+        }
       }
     }
   } else {
@@ -79,7 +86,9 @@ __device__ __forceinline__ void store_row16(const ConvGeom& g, float (&v)[16], i
       for (int i = 0; i < 4; ++i)
         reinterpret_cast<float4*>(o)[i] = make_float4(v[4 * i], v[4 * i + 1], v[4 * i + 2], v[4 * i + 3]);
     } else {
-      for (int i = 0; i < cnt; ++i) o[i] = v[i];
+#pragma unroll
+      for (int i = 0; i < 16; ++i)
+        if (i < cnt) o[i] = v[i];
     }
   }
 }

@@ -286,9 +286,11 @@ __global__ void __launch_bounds__(kFinThreads) gn_from_stats_kernel(const GnStat
   for (int e = tid; e < entries; e += kFinThreads) {
     const int slot = e / cpg, cl = e - slot * cpg;
     const int c = c_begin + cl;
-    const int src = c < p.channels[0] ? 0 : 1;
-    const int cs = src == 0 ? c : c - p.channels[0];
-    const float* q = p.stats[src] + ((static_cast<long long>(b) * p.slots + slot) * p.channels[src] + cs) * 3;
+    const bool second = c >= p.channels[0];
+    const int cs = second ? c - p.channels[0] : c;
+    const float* base = second ? p.stats[1] : p.stats[0];
+    const int nch = second ? p.channels[1] : p.channels[0];
+    const float* q = base + ((static_cast<long long>(b) * p.slots + slot) * nch + cs) * 3;
     m = merge_d(m, MomentsD{q[0], q[1], q[2]});
   }
 #pragma unroll

@@ -181,7 +181,8 @@ __global__ void __launch_bounds__(256) prepare_kernel(const PrepParams p, const 
       const int cnt = min(8, ctot - c0);
       const bool in1 = c0 >= p.src[0].channels;
       const bool single = (c0 + cnt <= p.src[0].channels) || in1;
-      const PrepSource& s = p.src[in1 ? 1 : 0];
+      const PrepSource s{in1 ? p.src[1].ptr : p.src[0].ptr, in1 ? p.src[1].bf16 : p.src[0].bf16,
+                         in1 ? p.src[1].channels : p.src[0].channels, in1 ? p.src[1].cstride : p.src[0].cstride};
       const int cs = in1 ? c0 - p.src[0].channels : c0;
       float sc[8], of[8];
 #pragma unroll
@@ -349,8 +350,10 @@ __device__ __forceinline__ void load_vec(const PrepParams& p, int ctot, long lon
     return;
   }
   const bool in1 = c0 >= p.src[0].channels;
-  const PrepSource& s = p.src[in1 ? 1 : 0];
-  const float4* q = reinterpret_cast<const float4*>(static_cast<const float*>(s.ptr) + vox * s.cstride +
+  // Field selects (not a runtime index into the parameter array, which would copy it to local memory).
+  const void* ptr = in1 ? p.src[1].ptr : p.src[0].ptr;
+  const long long cstride = in1 ? p.src[1].cstride : p.src[0].cstride;
+  const float4* q = reinterpret_cast<const float4*>(static_cast<const float*>(ptr) + vox * cstride +
                                                     (in1 ? c0 - p.src[0].channels : c0));
 #pragma unroll
   for (int i = 0; i < N / 4; ++i) {
@@ -600,6 +603,128 @@ __global__ void __launch_bounds__(256) im2col_kernel(const PrepParams p, const i
   }
 }
 
+// ---------------------------------------------------------------- small-tensor GroupNorm + operand
+// One kernel for a copy-mode operand with its GroupNorm computed in place, for
+// tensors small enough that one block per (group, batch item) reads its group
+// twice from L2: pass 1 reduces (count, mean, M2) (pivot-shifted per thread,
+// Chan merges in double in a fixed order), pass 2 applies the affine (computed as
+// ctmr_group_norm_affine does) and the optional SiLU and writes the operand. The
+// block of the last group also writes the zero channels [ctot, cpad).
+struct MomD {
+  double n, mean, m2;
+};
+
+__device__ __forceinline__ MomD mom_merge(MomD a, MomD b) {
+  if (b.n == 0.0) return a;
+  if (a.n == 0.0) return b;
+  const double n = a.n + b.n, delta = b.mean - a.mean, fb = b.n / n;
+  return MomD{n, a.mean + delta * fb, a.m2 + b.m2 + delta * delta * a.n * fb};
+}
+
+constexpr int kGnPrepThreads = 256;
+
+template <int OUTK, bool FAST>
+__global__ void __launch_bounds__(kGnPrepThreads) gn_prepare_small_kernel(const PrepParams p, const float* gamma,
+                                                                          const float* beta, const float eps,
+                                                                          const FastDiv cdiv) {
+  griddep_wait();  // the preceding kernel's writes are visible from here on
+  griddep_launch_dependents();
+  __shared__ double s_m[kGnPrepThreads / 32][3];
+  __shared__ float s_scale[64], s_offset[64];
+  const int g = blockIdx.x, b = blockIdx.y;
+  const int groups = gridDim.x;
+  const int c0s = p.src[0].channels;
+  const int ctot = c0s + p.src[1].channels;
+  const int cpg = static_cast<int>(cdiv.d);
+  const int cbase = g * cpg;
+  const unsigned vox = static_cast<unsigned>(p.od) * p.oh * p.ow;
+  const unsigned elems = vox * static_cast<unsigned>(cpg);
+  const long long bvox = static_cast<long long>(b) * vox;
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  auto load = [&](unsigned e, int& c) -> float {
+    const unsigned v = fdiv(cdiv, e);
+    c = cbase + static_cast<int>(e - v * cdiv.d);
+    const bool second = c >= c0s;
+    const void* ptr = second ? p.src[1].ptr : p.src[0].ptr;
+    const int bf = second ? p.src[1].bf16 : p.src[0].bf16;
+    const long long cs = second ? p.src[1].cstride : p.src[0].cstride;
+    return load_ch(ptr, bf, (bvox + v) * cs + (second ? c - c0s : c));
+  };
+  // Pass 1: moments of the group.
+  // Eight elements' loads in flight per thread (the loops are latency-bound).
+  float pivot = 0.f, sd = 0.f, sq = 0.f, n = 0.f;
+  if (tid < elems) {
+    int c;
+    pivot = load(tid, c);
+  }
+#pragma unroll 8
+  for (unsigned e = tid; e < elems; e += kGnPrepThreads) {
+    int c;
+    const float x = load(e, c);
+    const float d = x - pivot;
+    sd += d;
+    sq = fmaf(d, d, sq);
+    n += 1.f;
+  }
+  MomD m{0.0, 0.0, 0.0};
+  if (n > 0.f) {
+    const double md = static_cast<double>(sd) / n;
+    m = MomD{n, pivot + md, fmax(0.0, static_cast<double>(sq) - static_cast<double>(sd) * md)};
+  }
+#pragma unroll
+  for (int off = 1; off < 32; off <<= 1) {
+    const MomD o{__shfl_down_sync(0xffffffffu, m.n, off), __shfl_down_sync(0xffffffffu, m.mean, off),
+                 __shfl_down_sync(0xffffffffu, m.m2, off)};
+    if ((lane & (2 * off - 1)) == 0) m = mom_merge(m, o);
+  }
+  if (lane == 0) {
+    s_m[warp][0] = m.n;
+    s_m[warp][1] = m.mean;
+    s_m[warp][2] = m.m2;
+  }
+  __syncthreads();
+  if (tid < cpg) {
+    MomD t{0.0, 0.0, 0.0};
+    for (int w = 0; w < kGnPrepThreads / 32; ++w) t = mom_merge(t, MomD{s_m[w][0], s_m[w][1], s_m[w][2]});
+    const double var = t.n > 0.0 ? t.m2 / t.n : 0.0;
+    const double rstd = 1.0 / sqrt(var + static_cast<double>(eps));
+    const int c = cbase + tid;
+    const double gam = gamma != nullptr ? static_cast<double>(gamma[c]) : 1.0;
+    const double bet = beta != nullptr ? static_cast<double>(beta[c]) : 0.0;
+    const double scale = gam * rstd;
+    s_scale[tid] = static_cast<float>(scale);
+    s_offset[tid] = static_cast<float>(bet - t.mean * scale);
+  }
+  __syncthreads();
+  // Pass 2: the operand.
+#pragma unroll 8
+  for (unsigned e = tid; e < elems; e += kGnPrepThreads) {
+    int c;
+    const float x = load(e, c);
+    float t = fmaf(x, s_scale[c - cbase], s_offset[c - cbase]);
+    if (p.silu) t = silu_f<FAST>(t);
+    const unsigned v = fdiv(cdiv, e);
+    const long long o = (bvox + v) * p.out_cstride + c;
+    if (OUTK == kPrepOutBF16) {
+      __nv_bfloat16 h = __float2bfloat16_rn(t);
+      static_cast<uint16_t*>(p.out)[o] = *reinterpret_cast<uint16_t*>(&h);
+    } else {
+      const __half h = __float2half_rn(t);
+      static_cast<__half*>(p.out)[o] = h;
+      if (OUTK == kPrepOutSplitF16) static_cast<__half*>(p.out_lo)[o] = __float2half_rn((t - __half2float(h)) * 2048.f);
+    }
+  }
+  if (g == groups - 1 && p.cpad > ctot) {
+    const int pad = p.cpad - ctot;
+    for (unsigned e = tid; e < vox * static_cast<unsigned>(pad); e += kGnPrepThreads) {
+      const unsigned v = e / static_cast<unsigned>(pad);
+      const long long o = (bvox + v) * p.out_cstride + ctot + static_cast<int>(e - v * pad);
+      static_cast<uint16_t*>(p.out)[o] = 0;
+      if (OUTK == kPrepOutSplitF16) static_cast<uint16_t*>(p.out_lo)[o] = 0;
+    }
+  }
+}
+
 // Four input channels (the 4-channel latent): one item = one voxel x two taps,
 // i.e. the 8 consecutive columns [8p, 8p + 8) written as one 16-byte store, from
 // two 16-byte neighbour loads (tap 27 is the zero padding up to 112 columns).
@@ -754,6 +879,39 @@ cudaError_t launch_repack_im2col(const void* hi, const void* lo, int opad, int c
       static_cast<const uint16_t*>(hi), static_cast<const uint16_t*>(lo), opad, cpad_src, cin, kdense,
       static_cast<uint16_t*>(out_hi), static_cast<uint16_t*>(out_lo));
   return cudaGetLastError();
+}
+
+}  // namespace ctmr
+
+namespace ctmr {
+
+bool gn_prepare_small_fits(long long voxels, int channels, int groups) {
+  if (groups <= 0 || channels % groups != 0 || channels / groups > 64) return false;
+  return voxels * (channels / groups) <= kGnPrepSmallElems;
+}
+
+cudaError_t launch_gn_prepare_small(const PrepParams& p, const float* gamma, const float* beta, int groups, float eps,
+                                    cudaStream_t stream) {
+  const int ctot = p.src[0].channels + p.src[1].channels;
+  const long long vox = static_cast<long long>(p.od) * p.oh * p.ow;
+  if (p.mode != kPrepCopy || p.od != p.sd || p.oh != p.sh || p.ow != p.sw || p.affine != nullptr ||
+      !gn_prepare_small_fits(vox, ctot, groups))
+    return cudaErrorInvalidValue;
+  const FastDiv cd = make_fastdiv(static_cast<uint32_t>(ctot / groups));
+  const dim3 grid(static_cast<unsigned>(groups), static_cast<unsigned>(p.batch));
+  switch (p.out_kind) {
+    case kPrepOutBF16:
+      return launch_kernel(gn_prepare_small_kernel<kPrepOutBF16, true>, grid, dim3(kGnPrepThreads), 0, stream, p,
+                           gamma, beta, eps, cd);
+    case kPrepOutF16:
+      return launch_kernel(gn_prepare_small_kernel<kPrepOutF16, true>, grid, dim3(kGnPrepThreads), 0, stream, p,
+                           gamma, beta, eps, cd);
+    case kPrepOutSplitF16:
+      return launch_kernel(gn_prepare_small_kernel<kPrepOutSplitF16, false>, grid, dim3(kGnPrepThreads), 0, stream,
+                           p, gamma, beta, eps, cd);
+    default:
+      return cudaErrorInvalidValue;
+  }
 }
 
 }  // namespace ctmr

@@ -32,6 +32,17 @@ struct PrepParams {
 
 cudaError_t launch_prepare(const PrepParams& p, cudaStream_t stream);
 
+// Copy-mode operand with its GroupNorm computed in the same kernel (one block per
+// (group, batch item)); only for tensors whose groups are small, see
+// gn_prepare_small_fits (voxels x channels-per-group <= kGnPrepSmallElems). With
+// one block per group it has less parallelism than the separate statistics and
+// operand passes, which measured faster on the MAISI UNet; the conv uses it only
+// when CTMR_GN_FUSED is set.
+constexpr long long kGnPrepSmallElems = 32768;
+bool gn_prepare_small_fits(long long voxels, int channels, int groups);
+cudaError_t launch_gn_prepare_small(const PrepParams& p, const float* gamma, const float* beta, int groups, float eps,
+                                    cudaStream_t stream);
+
 // im2col expansion of a stride-1 3x3x3 convolution input with cin <= 4 channels
 // (src[0] only; od/oh/ow is the grid) into kdense-column rows, and the matching
 // repack of [27][opad][cpad_src] packed weights into [opad][kdense].

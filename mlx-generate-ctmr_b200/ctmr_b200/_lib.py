@@ -40,6 +40,7 @@ EXPORTED_SYMBOLS = (
     "ctmr_group_norm_workspace_size",
     "ctmr_group_norm_affine",
     "ctmr_conv3d_stats_slots",
+    "ctmr_conv3d_launch_count",
     "ctmr_group_norm_affine_from_stats",
     "ctmr_transform",
     "ctmr_ncdhw_to_ndhwc",
@@ -95,6 +96,10 @@ class Conv3dDesc(ctypes.Structure):
         ("y_coffset", ctypes.c_int),
         ("stats", ctypes.c_void_p),
         ("stats_slots", ctypes.c_int),
+        ("gn_gamma", ctypes.c_void_p),
+        ("gn_beta", ctypes.c_void_p),
+        ("gn_groups", ctypes.c_int),
+        ("gn_eps", ctypes.c_float),
     ]
 
 
@@ -136,6 +141,7 @@ def _load() -> ctypes.CDLL:
         "ctmr_group_norm_workspace_size": (sz, [i, ll, i]),
         "ctmr_group_norm_affine": (i, [Tensor, Tensor, i, ll, vp, vp, i, f, vp, vp, sz, vp]),
         "ctmr_conv3d_stats_slots": (i, [ctypes.POINTER(Conv3dDesc)]),
+        "ctmr_conv3d_launch_count": (i, [ctypes.POINTER(Conv3dDesc)]),
         "ctmr_group_norm_affine_from_stats": (i, [vp, i, vp, i, i, i, vp, vp, i, f, vp, vp]),
         "ctmr_transform": (i, [ctypes.POINTER(TransformDesc), vp]),
         "ctmr_ncdhw_to_ndhwc": (i, [vp, i, vp, i, i, i, ll, vp]),

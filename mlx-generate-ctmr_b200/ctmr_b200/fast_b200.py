@@ -255,6 +255,18 @@ def sinusoidal_timestep_embedding(timesteps: torch.Tensor, embedding_dim: int, *
 
 
 # ---------------------------------------------------------------- convolutions
+def _norm_args(x, x2, weight, bias, *, groups: int, eps: float) -> dict:
+    """Keyword arguments that GroupNorm ``x ++ x2`` for the conv consuming it.
+
+    From the producing convolutions' epilogue statistics when they are attached
+    (the opt-in path), else inside the conv call itself (``norm=``): one fused
+    kernel for small tensors, the statistics pass + operand pass for large ones.
+    """
+    if ops.output_stats(x) is not None and (x2 is None or ops.output_stats(x2) is not None):
+        return {"affine": ops.group_norm_affine(x, weight, bias, groups=groups, eps=eps, x2=x2)}
+    return {"norm": (weight, bias, groups, eps)}
+
+
 def _bias(weight: torch.Tensor, bias: torch.Tensor | None) -> torch.Tensor:
     return torch.zeros(int(weight.shape[0]), dtype=torch.float32, device=weight.device) if bias is None else bias
 
@@ -288,9 +300,9 @@ def norm_conv3d_ncdhw(array, weight: torch.Tensor, bias: torch.Tensor, *, norm, 
     surrounding ops in ``fast_fp32.residual_block_ncdhw``.
     """
     x, x2 = _split(array)
-    affine = None
+    nargs = {}
     if norm is not None:
-        affine = ops.group_norm_affine(x, norm[0], norm[1], groups=num_groups, eps=eps, x2=x2)
+        nargs = _norm_args(x, x2, norm[0], norm[1], groups=num_groups, eps=eps)
     res = None
     if residual is not None:
         res = residual if isinstance(residual, torch.Tensor) else residual.materialize()
@@ -298,7 +310,7 @@ def norm_conv3d_ncdhw(array, weight: torch.Tensor, bias: torch.Tensor, *, norm, 
     b, _, d, h, w = (int(n) for n in x.shape)
     scale = 8 if upsample else 1
     voxels = b * d * h * w * scale // (8 if avgpool else 1)
-    return ops.conv3d(x, _pack(weight, upsample=upsample, out_voxels=voxels), bias, x2=x2, affine=affine,
+    return ops.conv3d(x, _pack(weight, upsample=upsample, out_voxels=voxels), bias, x2=x2, **nargs,
                       silu=apply_silu,
                       avgpool=avgpool, residual=res, residual_upsampled=residual_upsampled,
                       out_dtype=activation_dtype(), stats=OUTPUT_STATS)
@@ -372,14 +384,14 @@ def residual_block_ncdhw(x, emb: torch.Tensor, weights: Mapping[str, torch.Tenso
     cin = int(xa.shape[1]) + (int(xb.shape[1]) if xb is not None else 0)
     project = cin != int(weights["conv1.conv.weight"].shape[0])
     dtype = activation_dtype()
-    affine1 = ops.group_norm_affine(xa, *norm1, groups=num_groups, eps=eps, x2=xb)
+    n1 = _norm_args(xa, xb, *norm1, groups=num_groups, eps=eps)
     if down:
         if project:
             skip = ops.conv3d(xa, _pack(weights["skip_connection.conv.weight"]), weights["skip_connection.conv.bias"],
                               x2=xb, avgpool=True, out_dtype=dtype)
         else:
             skip = ops.transform(xa, x2=xb, mode=_lib.TRANSFORM_AVGPOOL, out_dtype=dtype)
-        hidden = ops.conv3d(xa, _pack(weights["conv1.conv.weight"]), bias1, x2=xb, affine=affine1, silu=True,
+        hidden = ops.conv3d(xa, _pack(weights["conv1.conv.weight"]), bias1, x2=xb, **n1, silu=True,
                             avgpool=True, out_dtype=dtype, stats=OUTPUT_STATS)
     else:
         if project:
@@ -387,10 +399,10 @@ def residual_block_ncdhw(x, emb: torch.Tensor, weights: Mapping[str, torch.Tenso
                               x2=xb, out_dtype=dtype)
         else:
             skip = xa if xb is None else ChannelConcat(xa, xb).materialize()
-        hidden = ops.conv3d(xa, _pack(weights["conv1.conv.weight"], upsample=up), bias1, x2=xb, affine=affine1,
+        hidden = ops.conv3d(xa, _pack(weights["conv1.conv.weight"], upsample=up), bias1, x2=xb, **n1,
                             silu=True, out_dtype=dtype, stats=OUTPUT_STATS)
-    affine2 = ops.group_norm_affine(hidden, weights["norm2.weight"], weights["norm2.bias"], groups=num_groups, eps=eps)
-    return ops.conv3d(hidden, _pack(weights["conv2.conv.weight"]), weights["conv2.conv.bias"], affine=affine2,
+    n2 = _norm_args(hidden, None, weights["norm2.weight"], weights["norm2.bias"], groups=num_groups, eps=eps)
+    return ops.conv3d(hidden, _pack(weights["conv2.conv.weight"]), weights["conv2.conv.bias"], **n2,
                       silu=True, residual=skip, residual_upsampled=up, out_dtype=dtype, stats=OUTPUT_STATS)
 
 
@@ -401,15 +413,15 @@ def vae_resblock_ncdhw(state: list, conv1, conv2, norm1, norm2, shortcut, *, num
     x, x2 = _split(array)
     del array
     dtype = activation_dtype()
-    affine1 = ops.group_norm_affine(x, norm1[0], norm1[1], groups=num_groups, eps=eps, x2=x2)
-    hidden = ops.conv3d(x, _pack(conv1[0]), conv1[1], x2=x2, affine=affine1, silu=True, out_dtype=dtype, stats=OUTPUT_STATS)
+    n1 = _norm_args(x, x2, norm1[0], norm1[1], groups=num_groups, eps=eps)
+    hidden = ops.conv3d(x, _pack(conv1[0]), conv1[1], x2=x2, **n1, silu=True, out_dtype=dtype, stats=OUTPUT_STATS)
     if shortcut is None:
         skip = x if x2 is None else ChannelConcat(x, x2).materialize()
     else:
         skip = ops.conv3d(x, _pack(shortcut[0]), shortcut[1], x2=x2, out_dtype=dtype)
     del x, x2
-    affine2 = ops.group_norm_affine(hidden, norm2[0], norm2[1], groups=num_groups, eps=eps)
-    out = ops.conv3d(hidden, _pack(conv2[0]), conv2[1], affine=affine2, silu=True, residual=skip, out_dtype=dtype,
+    n2 = _norm_args(hidden, None, norm2[0], norm2[1], groups=num_groups, eps=eps)
+    out = ops.conv3d(hidden, _pack(conv2[0]), conv2[1], **n2, silu=True, residual=skip, out_dtype=dtype,
                      stats=OUTPUT_STATS)
     return out
 

@@ -210,6 +210,7 @@ def conv3d(
     stats: bool = False,
     workspace: torch.Tensor | None = None,
     stages: int | None = None,
+    norm: tuple | None = None,
 ) -> torch.Tensor:
     """``conv(prepare(x ++ x2)) + bias (+ residual)`` in one call (``ctmr_conv3d``).
 
@@ -279,6 +280,16 @@ def conv3d(
     desc.y_dtype = _dtype_code(out.dtype)
     desc.y_cstride = ycs
     desc.y_coffset = 0
+    keep = []
+    if norm is not None:  # (gamma, beta, groups, eps): the input's GroupNorm computed inside the call
+        gamma, beta, groups, eps = norm
+        gamma = gamma.to(dtype=F32).contiguous() if gamma is not None else None
+        beta = beta.to(dtype=F32).contiguous() if beta is not None else None
+        keep = [gamma, beta]
+        desc.gn_gamma = gamma.data_ptr() if gamma is not None else None
+        desc.gn_beta = beta.data_ptr() if beta is not None else None
+        desc.gn_groups = int(groups)
+        desc.gn_eps = float(eps)
     stats_buf = None
     if stats:  # GroupNorm moments of the output from the conv epilogue, when its kernel can produce them
         slots = int(LIB.ctmr_conv3d_stats_slots(ctypes.byref(desc)))
@@ -295,16 +306,17 @@ def conv3d(
         ws = torch.empty(ws_bytes, dtype=torch.uint8, device=x.device) if ws_bytes else None
     ws_ptr = ws.data_ptr() if ws is not None else None
     if stages is not None:  # one or both stages (_lib.CONV_PREPARE | _lib.CONV_GEMM)
-        _count(1)
+        _count(int(LIB.ctmr_conv3d_launch_count(ctypes.byref(desc))))
         check(LIB.ctmr_conv3d_stages(ctypes.byref(desc), ws_ptr, ws_bytes, int(stages), _stream()), "conv3d stages")
         return out
-    _count(2 if ws_bytes else 1)
+    _count(int(LIB.ctmr_conv3d_launch_count(ctypes.byref(desc))))
     if PROFILE is None:
         check(LIB.ctmr_conv3d(ctypes.byref(desc), ws_ptr, ws_bytes, _stream()), "conv3d")
     else:
         taps = 8 if packed.upsample else k ** 3
         what = (f"{b}x{cin}->{o} out {od}x{oh}x{ow} k{k} s{stride} up{int(packed.upsample)} tri{int(trilinear)} "
-                f"pool{int(avgpool)} norm{int(affine is not None)} res{int(residual is not None)} {packed.precision}")
+                f"pool{int(avgpool)} norm{int(affine is not None or norm is not None)} res{int(residual is not None)} "
+                f"{packed.precision}")
         if ws_bytes:
             with _profiled("prepare", 0.0, what):
                 check(LIB.ctmr_conv3d_stages(ctypes.byref(desc), ws_ptr, ws_bytes, _lib.CONV_PREPARE, _stream()),
@@ -314,6 +326,7 @@ def conv3d(
                   "conv3d gemm")
     if stats_buf is not None:
         out._ctmr_stats = OutputStats(stats_buf, int(desc.stats_slots), o)
+    del keep
     return out
 
 

@@ -368,3 +368,44 @@ def test_output_statistics_refused_where_unsupported(cuda):
     y = ops.conv3d(ops.to_ndhwc(torch.randn((1, 64, 4, 8, 16), device=cuda)), ops.pack_weight(w, "fp16"), None,
                    stats=True)  # under 128 output channels: a separate pass is cheaper
     assert ops.output_stats(y) is None
+
+
+@pytest.mark.parametrize(("shape", "x2_channels", "out_channels", "precision", "groups"), [
+    ((2, 512, 4, 8, 8), 0, 512, "fp16", 32),      # deep level (fused small-tensor kernel if enabled)
+    ((2, 256, 4, 8, 8), 256, 256, "fp16", 32),    # concat input
+    ((1, 64, 16, 32, 64), 0, 64, "fp16", 32),     # large: statistics pass + operand pass
+    ((1, 64, 16, 32, 64), 32, 64, "bf16", 32),    # large with concat
+    ((2, 24, 3, 5, 7), 0, 32, "fp32", 8),         # split-fp32 operand, padded channels 24..31 zeroed
+    ((1, 64, 5, 12, 40), 0, 4, "fp32", 32),       # narrow fp32 kernel takes the affine from the workspace
+])
+@pytest.mark.parametrize("fused", [False, True])
+def test_groupnorm_inside_the_conv_call(cuda, shape, x2_channels, out_channels, precision, groups, fused,
+                                        monkeypatch):
+    """``conv3d(norm=...)`` (statistics computed inside the call, also through the opt-in fused
+    small-tensor kernel) equals ``conv3d(affine=...)`` with the affine of ``ctmr_group_norm_affine``."""
+    from ctmr_b200 import ops
+
+    if fused:
+        monkeypatch.setenv("CTMR_GN_FUSED", "1")
+    else:
+        monkeypatch.delenv("CTMR_GN_FUSED", raising=False)
+
+    rng = np.random.default_rng(47)
+    b, c = shape[:2]
+    x = ops.to_ndhwc(torch.from_numpy((rng.standard_normal(shape) * 2 + 0.7).astype(np.float32)).to(cuda))
+    x2 = None
+    if x2_channels:
+        x2 = ops.to_ndhwc(torch.from_numpy(rng.standard_normal((b, x2_channels, *shape[2:])).astype(np.float32))
+                          .to(cuda))
+    cin = c + x2_channels
+    w = torch.from_numpy((rng.standard_normal((out_channels, cin, 3, 3, 3)) / np.sqrt(27 * cin)).astype(np.float32))
+    gamma = torch.from_numpy((1 + 0.2 * rng.standard_normal(cin)).astype(np.float32)).to(cuda)
+    beta = torch.from_numpy((0.3 * rng.standard_normal(cin)).astype(np.float32)).to(cuda)
+    bias = torch.from_numpy(rng.standard_normal(out_channels).astype(np.float32)).to(cuda)
+    packed = ops.pack_weight(w.to(cuda), precision)
+    affine = ops.group_norm_affine(x, gamma, beta, groups=groups, eps=1e-6, x2=x2)
+    ref = ops.conv3d(x, packed, bias, x2=x2, affine=affine, silu=True)
+    got = ops.conv3d(x, packed, bias, x2=x2, norm=(gamma, beta, groups, 1e-6), silu=True)
+    torch.cuda.synchronize()
+    err = ops_ref.rel_l2(got.cpu(), ref.cpu().double())
+    assert err <= (1e-6 if precision == "fp32" else 1e-3), f"{precision} rel-L2 {err:.3e}"
