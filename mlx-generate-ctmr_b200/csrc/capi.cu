@@ -29,6 +29,10 @@ cudaError_t launch_conv3d_umma(const ConvMaps& maps, const ConvGeom& g, int kc, 
 int conv_v2_stage_plan(int kc, int mt, int tw, int bn, size_t* smem_bytes, size_t stats_bytes);
 cudaError_t launch_conv3d_umma_v2(const ConvMaps& maps, const ConvGeom& g, int kc, int mt, int tw, int sms,
                                   size_t smem, cudaStream_t stream);
+int conv_khcat_stage_plan(int kc, int bn, int mt, size_t* smem_bytes);
+int conv_khcat_rows();
+cudaError_t launch_conv3d_khcat(const ConvMaps& maps, const ConvGeom& g, int kc, int mt, int sms, size_t smem,
+                                cudaStream_t stream);
 extern __device__ unsigned int g_device_error;
 }  // namespace ctmr
 
@@ -118,6 +122,24 @@ int encode_weight3(CUtensorMap* map, const void* base, bool bf16, long long cpad
   cuuint32_t box[3] = {static_cast<cuuint32_t>(kc), static_cast<cuuint32_t>(bn), static_cast<cuuint32_t>(box_taps)};
   cuuint32_t estr[3] = {1, 1, 1};
   CUresult r = enc(map, bf16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 3,
+                   const_cast<void*>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                   swizzle_for(kc), CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return fail(CTMR_ERR_INVALID, "weight tensor map rejected (CUresult %d)", int(r));
+  return CTMR_OK;
+}
+
+// 5-D view (c, o, kw, kh, kd) of 3x3x3 packed weights [kd][kh][kw][O][C]: a box of
+// (kc, opad, 1, 3, 1) holds the three kh taps of one (kd, kw) as 3 x opad rows.
+int encode_weight_kh(CUtensorMap* map, const void* base, bool bf16, long long cpad, long long opad, int kc) {
+  auto enc = tensor_map_encoder();
+  if (enc == nullptr) return fail(CTMR_ERR_CUDA, "cuTensorMapEncodeTiled is unavailable");
+  const long long tap = cpad * 2 * opad;
+  cuuint64_t dims[5] = {static_cast<cuuint64_t>(cpad), static_cast<cuuint64_t>(opad), 3, 3, 3};
+  cuuint64_t strides[4] = {static_cast<cuuint64_t>(cpad * 2), static_cast<cuuint64_t>(tap),
+                           static_cast<cuuint64_t>(3 * tap), static_cast<cuuint64_t>(9 * tap)};
+  cuuint32_t box[5] = {static_cast<cuuint32_t>(kc), static_cast<cuuint32_t>(opad), 1, 3, 1};
+  cuuint32_t estr[5] = {1, 1, 1, 1, 1};
+  CUresult r = enc(map, bf16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 5,
                    const_cast<void*>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
                    swizzle_for(kc), CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   if (r != CUDA_SUCCESS) return fail(CTMR_ERR_INVALID, "weight tensor map rejected (CUresult %d)", int(r));
@@ -350,6 +372,37 @@ struct V2Plan {
   size_t smem, stats_bytes;
 };
 
+bool g_khcat_unavailable = false;  // a tensor map for the kh-concatenated kernel was refused once
+
+struct KhPlan {
+  int kc, mt, stages;
+  size_t smem;
+};
+
+// The kh-concatenated kernel: 16-bit stride-1 3x3x3 convolutions with at most 64
+// output channels (three taps side by side fill an N = 3 x C_out MMA).
+bool plan_khcat(const ConvPlan& p, const ctmr_conv3d_desc* d, KhPlan* k) {
+  if (p.exact || p.mode != ctmr::kModeConv3 || p.opad > 64 || d->stats != nullptr || g_khcat_unavailable ||
+      p.row_w < 8 || p.row_h < 8 || getenv("CTMR_DISABLE_KHCAT") != nullptr)
+    return false;
+  // Two depth tiles share each weight box (measured faster than one depth with two accumulator
+  // buffers); CTMR_KHCAT_MT=1 selects the latter.
+  const char* mt_env = getenv("CTMR_KHCAT_MT");
+  k->mt = mt_env != nullptr && mt_env[0] == '1' ? 1 : 2;
+  if (p.row_d < 2) k->mt = 1;
+  for (int min_stages : {3, 2}) {
+    for (int cand : {64, 32, 16}) {
+      size_t sm_b = 0;
+      const int st = p.cpad % cand ? 0 : ctmr::conv_khcat_stage_plan(cand, p.opad, k->mt, &sm_b);
+      if (st >= min_stages) {
+        k->kc = cand, k->smem = sm_b, k->stages = st;
+        return true;
+      }
+    }
+  }
+  return false;
+}
+
 bool plan_v2(const ConvPlan& p, const ctmr_conv3d_desc* d, bool with_stats, V2Plan* v) {
   if (p.exact || g_v2_unavailable ||
       !(p.mode == ctmr::kModeConv3 || p.mode == ctmr::kModeUp2 || p.mode == ctmr::kModeConv1) || p.row_w < 16 ||
@@ -580,6 +633,59 @@ int ctmr_conv3d_stages(const ctmr_conv3d_desc* d, void* workspace, size_t worksp
   V2Plan v2{};
   if (with_stats && (d->stats_slots < sm_count() || !plan_v2(p, d, true, &v2)))
     return fail(CTMR_ERR_UNSUPPORTED, "output statistics need the persistent kernel (ctmr_conv3d_stats_slots)");
+  KhPlan kh{};
+  if (plan_khcat(p, d, &kh)) {
+    const int rows = ctmr::conv_khcat_rows(), md = kh.mt;
+    ctmr::ConvGeom g{};
+    g.batch = d->batch;
+    g.row_d = p.row_d, g.row_h = p.row_h, g.row_w = p.row_w;
+    g.tile_w = 8, g.tile_h = rows, g.tile_d = md;
+    g.tiles_w = (p.row_w + 7) / 8;
+    g.tiles_h = (p.row_h + rows - 1) / rows;
+    g.tiles_d = (p.row_d + md - 1) / md;
+    g.phases = 1;
+    g.taps = 27;
+    g.kblocks = p.cpad / kh.kc;
+    g.mode = p.mode;
+    g.bn = p.opad;
+    g.cout = d->out_channels;
+    g.stages = kh.stages;
+    g.tmem_cols = 512;
+    g.operand_bf16 = p.bf16 ? 1 : 0;
+    g.ksplit = 1;
+    g.n_tiles = 1;
+    const long long total = static_cast<long long>(g.tiles_w) * g.tiles_h * g.tiles_d * d->batch;
+    if (total > 0 && total < (1LL << 31)) {
+      g.total_tiles = static_cast<int>(total);
+      g.bias = d->bias;
+      g.bias_bstride = d->bias_per_batch ? d->out_channels : 0;
+      g.res = d->residual.data;
+      g.res_bf16 = d->residual.dtype == CTMR_DTYPE_BF16;
+      g.res_cstride = d->residual.cstride;
+      g.res_up = d->residual_upsampled;
+      g.res_d = d->residual_upsampled ? p.out_d / 2 : p.out_d;
+      g.res_h = d->residual_upsampled ? p.out_h / 2 : p.out_h;
+      g.res_w = d->residual_upsampled ? p.out_w / 2 : p.out_w;
+      g.out = d->y;
+      g.out_bf16 = d->y_dtype == CTMR_DTYPE_BF16;
+      g.out_cstride = d->y_cstride;
+      g.out_coff = d->y_coffset;
+      g.out_d = p.out_d, g.out_h = p.out_h, g.out_w = p.out_w;
+      ctmr::ConvMaps maps;
+      std::memset(&maps, 0, sizeof(maps));
+      const long long rs = a_cstride * 2;
+      const long long W = p.in_w, H = p.in_h, D = p.in_d;
+      // W before H: an 8-row swizzle atom holds 8 consecutive w of one h.
+      if (rs % 16 == 0 &&
+          encode_act(&maps.a[0], a_hi, p.bf16, p.cpad, W, H, D, d->batch, rs, W * rs, H * W * rs, D * H * W * rs,
+                     kh.kc, 8, 16, md) == CTMR_OK &&
+          encode_weight_kh(&maps.b, w_hi, p.bf16, p.cpad, p.opad, kh.kc) == CTMR_OK) {
+        cudaError_t e = ctmr::launch_conv3d_khcat(maps, g, kh.kc, kh.mt, sm_count(), kh.smem, stream);
+        return e == cudaSuccess ? CTMR_OK : cuda_fail(e, "conv3d kh-concatenated launch");
+      }
+      g_khcat_unavailable = true;  // fall through to the other kernels
+    }
+  }
   if (plan_v2(p, d, with_stats, &v2)) {
     const int tw = v2.tw, mt = v2.mt, bn = v2.bn, kc = v2.kc, stages2 = v2.stages;
     const size_t smem2 = v2.smem;
@@ -771,7 +877,8 @@ int ctmr_conv3d_launch_count(const ctmr_conv3d_desc* d) {
   if (p.narrow || p.tiny) return n + 1;
   if (p.prepare) n += p.im2col ? 2 : 1;
   V2Plan v2{};
-  if (plan_v2(p, d, d->stats != nullptr, &v2)) return n + 1;
+  KhPlan kh{};
+  if (plan_khcat(p, d, &kh) || plan_v2(p, d, d->stats != nullptr, &v2)) return n + 1;
   return n + 1 + (p.ksplit > 1 ? 1 : 0);
 }
 

@@ -150,8 +150,9 @@ V2_SHAPES = [
 @pytest.mark.parametrize("precision", ["fp16", "bf16"])
 @pytest.mark.parametrize(("shape", "out_channels", "upsample"), V2_SHAPES)
 def test_persistent_kernel_shapes(cuda, shape, out_channels, upsample, precision):
-    """16-bit stride-1 convs on grids with W >= 16 and H >= 8 run the persistent
-    atom-shifted kernel; bias per batch item and a residual exercise its epilogue."""
+    """16-bit stride-1 convs on grids with W >= 16 and H >= 8 run a persistent kernel (the
+    kh-concatenated one for <= 64 output channels, else the atom-shifted one); bias per batch
+    item and a residual exercise its epilogue."""
     from ctmr_b200 import ops
 
     rng = np.random.default_rng(13)
@@ -169,6 +170,56 @@ def test_persistent_kernel_shapes(cuda, shape, out_channels, upsample, precision
     expected = ops_ref.conv3d_ref(xin, w.double(), bias.double()) + res.double()
     err = ops_ref.rel_l2(y.cpu(), expected)
     assert err <= (FP16_CONV_REL_L2 if precision == "fp16" else BF16_CONV_REL_L2), f"{precision} rel-L2 {err:.3e}"
+
+
+KHCAT_SHAPES = [
+    ((2, 64, 3, 30, 20), 64),    # partial h (14 + 14 + 2 rows), w (8 + 8 + 4) and depth-pair tiles
+    ((1, 128, 4, 16, 16), 48),   # two channel blocks, N = 3 x 48
+    ((1, 32, 2, 8, 8), 16),      # 32-channel blocks, N = 3 x 16, smallest grid
+    ((2, 192, 2, 14, 24), 64),   # three channel blocks, H = one tile
+]
+
+
+@pytest.mark.parametrize("depths", ["1", "2"])
+@pytest.mark.parametrize("precision", ["fp16", "bf16"])
+@pytest.mark.parametrize(("shape", "out_channels"), KHCAT_SHAPES)
+def test_kh_concatenated_kernel(cuda, shape, out_channels, precision, depths, monkeypatch):
+    """16-bit stride-1 3x3x3 convs with <= 64 output channels run the kh-concatenated kernel (the
+    three taps along h side by side in one N = 3 x C_out MMA, row-shifted sums in the epilogue):
+    per-batch bias, a residual and a bf16 output written into a channel slice exercise it, against
+    the float64 oracle and against the atom-shifted kernel (CTMR_DISABLE_KHCAT) on the same inputs."""
+    from ctmr_b200 import ops
+
+    rng = np.random.default_rng(57)
+    b, c = shape[:2]
+    x = torch.from_numpy(rng.standard_normal(shape).astype(np.float32))
+    w = torch.from_numpy((rng.standard_normal((out_channels, c, 3, 3, 3)) / np.sqrt(27 * c)).astype(np.float32))
+    bias = torch.from_numpy(rng.standard_normal((b, out_channels)).astype(np.float32))
+    res = torch.from_numpy(rng.standard_normal((b, out_channels, *shape[2:])).astype(np.float32))
+    xc, bc, rc = ops.to_ndhwc(x.to(cuda)), bias.to(cuda), ops.to_ndhwc(res.to(cuda))
+    packed = ops.pack_weight(w.to(cuda), precision)
+    monkeypatch.delenv("CTMR_DISABLE_KHCAT", raising=False)
+    monkeypatch.setenv("CTMR_KHCAT_MT", depths)  # depth tiles per weight box (1: two accumulator buffers)
+    y = ops.conv3d(xc, packed, bc, residual=rc)
+    plain = ops.conv3d(xc, packed, bc)
+    wide = ops.empty_ndhwc(b, out_channels + 32, *shape[2:], torch.bfloat16, xc.device).zero_()
+    ops.conv3d(xc, packed, bc, out=wide[:, 16:16 + out_channels])
+    monkeypatch.setenv("CTMR_DISABLE_KHCAT", "1")
+    y_v2 = ops.conv3d(xc, packed, bc, residual=rc)
+    monkeypatch.delenv("CTMR_DISABLE_KHCAT")
+    torch.cuda.synchronize()
+    expected = ops_ref.conv3d_ref(x.double(), w.double(), bias.double()) + res.double()
+    err = ops_ref.rel_l2(y.cpu(), expected)
+    assert err <= (FP16_CONV_REL_L2 if precision == "fp16" else BF16_CONV_REL_L2), f"{precision} rel-L2 {err:.3e}"
+    # Same rounded operands, fp32 sums in another order: the two kernels agree to fp32 rounding,
+    # and do not agree bitwise (which would mean the route switch changed nothing).
+    diff = ops_ref.rel_l2(y.cpu(), y_v2.cpu().double())
+    assert diff <= 1e-5, f"kh-concatenated vs atom-shifted rel-L2 {diff:.3e}"
+    assert not torch.equal(y, y_v2)
+    # bf16 output into a channel slice: the fp32 result rounded once; the other channels untouched.
+    torch.testing.assert_close(wide[:, 16:16 + out_channels].float(), plain.to(torch.bfloat16).float(),
+                               rtol=0, atol=0)
+    assert not wide[:, :16].any() and not wide[:, 16 + out_channels:].any()
 
 
 @pytest.mark.parametrize("precision", ["fp16", "bf16"])
