@@ -328,10 +328,22 @@ __global__ void __launch_bounds__(kFinThreads) gn_from_stats_kernel(const GnStat
 int gn_max_chunks(int batch) { return (2 * 296 + batch - 1) / batch; }
 
 // About 32 KB of input per block (small tensors still spread over many SMs), at
-// least 16 voxels, at most ~600 blocks in all.
+// least 16 voxels, at most one resident wave of blocks over all batch items (a
+// second, partial wave measured slower than fewer, longer blocks).
 int gn_chunks_for(int batch, long long voxels, int channels) {
+  static const int wave = [] {
+    int dev = 0, sms = 0, per_sm = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess ||
+        cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || sms < 1)
+      sms = 148;
+    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, gn_partial_kernel, kGnThreads, 1024) != cudaSuccess ||
+        per_sm < 1)
+      per_sm = 1;
+    return sms * per_sm;
+  }();
   long long chunks = (voxels * channels * 4 + (32 << 10) - 1) / (32 << 10);
   if (chunks > gn_max_chunks(batch)) chunks = gn_max_chunks(batch);
+  if (chunks > wave / batch) chunks = wave / batch;
   if (chunks > (voxels + 15) / 16) chunks = (voxels + 15) / 16;
   if (chunks < 1) chunks = 1;
   return static_cast<int>(chunks);

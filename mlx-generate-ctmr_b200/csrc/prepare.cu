@@ -521,12 +521,26 @@ bool vec_ok(const PrepParams& p, int vec) {
   return true;
 }
 
+// Blocks of `kern` resident on the whole GPU at once (SMs x blocks per SM).
+template <typename K>
+long long resident_blocks(K kern, int threads, size_t smem) {
+  int dev = 0, sms = 0, per_sm = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess ||
+      cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || sms < 1)
+    sms = 148;
+  if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, threads, smem) != cudaSuccess || per_sm < 1)
+    per_sm = 1;
+  return static_cast<long long>(sms) * per_sm;
+}
+
 cudaError_t launch_copy_fast(const PrepParams& p, cudaStream_t stream) {
   const unsigned vox = static_cast<unsigned>(static_cast<long long>(p.od) * p.oh * p.ow);
   const FastDiv q = make_fastdiv(static_cast<uint32_t>(p.cpad / 8));
   const long long items = static_cast<long long>(vox) * q.d;
   long long blocks = (items + 511) / 512;
-  const long long cap = 148LL * 8 / p.batch + 1;
+  // One resident wave over all batch items (a second, partial wave would idle most SMs).
+  static const long long resident = resident_blocks(prepare_copy_kernel<kPrepOutF16, true>, 256, 0);
+  const long long cap = resident / p.batch > 0 ? resident / p.batch : 1;
   if (blocks > cap) blocks = cap;
   const dim3 grid(static_cast<unsigned>(blocks), static_cast<unsigned>(p.batch));
   switch (p.out_kind) {
@@ -544,7 +558,8 @@ cudaError_t launch_tri_fast(const PrepParams& p, cudaStream_t stream) {
   const FastDiv yd = make_fastdiv(static_cast<uint32_t>(p.sh));
   const long long items = static_cast<long long>(p.od) * p.sh * p.sw * q.d;
   long long blocks = (items + 127) / 128;
-  const long long cap = 148LL * 16 / p.batch + 1;
+  static const long long resident = resident_blocks(prepare_tri_kernel<kPrepOutF16>, 128, 0);
+  const long long cap = resident / p.batch > 0 ? resident / p.batch : 1;
   if (blocks > cap) blocks = cap;
   const dim3 grid(static_cast<unsigned>(blocks), static_cast<unsigned>(p.batch));
   const unsigned n = static_cast<unsigned>(items);
@@ -846,7 +861,8 @@ cudaError_t launch_im2col(const PrepParams& p, int cin, int kdense, cudaStream_t
     const long long items = static_cast<long long>(p.od) * p.oh * p.ow * 14;
     if (items >= (1LL << 31)) return cudaErrorInvalidValue;
     long long blocks = (items + 255) / 256;
-    const long long cap = 148LL * 8 / p.batch + 1;
+    static const long long resident = resident_blocks(im2col4_kernel<kPrepOutF16>, 256, 0);
+    const long long cap = resident / p.batch > 0 ? resident / p.batch : 1;
     if (blocks > cap) blocks = cap;
     const dim3 grid(static_cast<unsigned>(blocks), static_cast<unsigned>(p.batch));
     const unsigned n = static_cast<unsigned>(items);
