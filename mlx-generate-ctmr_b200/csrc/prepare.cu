@@ -367,9 +367,10 @@ __device__ __forceinline__ void load_vec(const PrepParams& p, int ctot, long lon
 
 // Copy mode, 8 channels per item, two items in flight per thread; batch item
 // on grid y. Preconditions (checked by the launcher): fp32 sources, channel
-// counts, strides and cpad multiples of 8, 16-byte aligned rows.
+// counts, strides and cpad multiples of 8, 16-byte aligned rows. At most 48
+// registers, so five blocks share an SM (more loads in flight; no spills).
 template <int OUTK, bool FAST>
-__global__ void __launch_bounds__(256) prepare_copy_kernel(const PrepParams p, const FastDiv qdiv,
+__global__ void __launch_bounds__(256, 5) prepare_copy_kernel(const PrepParams p, const FastDiv qdiv,
                                                            const unsigned vox) {
   griddep_wait();  // the preceding kernel's writes are visible from here on
   griddep_launch_dependents();
