@@ -179,9 +179,9 @@ def run_reference(args, rank: int) -> None:
 
 # ---------------------------------------------------------------- kernel-level cases
 # The bench roofline's launch: the VAE decoder's full-resolution 64 -> 64 conv (B, C, D, H, W, O),
-# and the DRAM bytes per output voxel ncu measured for that kernel (248.5 MB over 786,432 voxels).
+# and the DRAM bytes per output voxel ncu measured for that kernel (248.9 MB over 786,432 voxels).
 DOMINANT_CONV = (1, 64, 96, 256, 128, 64)
-DOMINANT_TRAFFIC_PER_VOXEL = (101.009664e6 + 147.503104e6) / 786432
+DOMINANT_TRAFFIC_PER_VOXEL = (101.027584e6 + 147.916032e6) / 786432
 
 SWEEP_SHAPES = [(b, c, n, n, n, o) for n in (16, 32, 64) for c, o in ((32, 32), (64, 64), (128, 128), (256, 256))
                 for b in (1, 2)] + [(2, 512, 8, 8, 4, 512), (2, 512, 16, 16, 8, 512), (1, 128, 128, 128, 64, 128),
@@ -524,12 +524,12 @@ def main() -> None:
         roofline = {"bound": "tensor", "achieved": round(dom_tflops, 1), "peak": burst, "unit": "TFLOP/s",
                     "frac": round(dom_tflops / burst, 4),
                     "traffic": round(DOMINANT_TRAFFIC_PER_VOXEL * vox),
-                    "kernel": "conv3d_umma_v2_kernel<64,2,3>: VAE decoder full-resolution 64->64 conv "
+                    "kernel": "conv3d_khcat_kernel<64,2>: VAE decoder full-resolution 64->64 conv "
                               f"{b_}x{c_}x{d_}x{h_}x{w_} (GN affine + SiLU input), the largest launch class",
                     "launch_ms": round(dom_ms, 4), "prepare_ms": round(dom_prep_ms, 4),
                     "algorithmic_bytes": vox * (c_ * 2 + o_ * 4),
                     "traffic_source": "ncu dram__bytes_read+write of the same kernel on 1x64x48x128x128 "
-                                      "(profiles/conv3d_umma_v2_fp16_64to64_48x128x128.md), scaled by voxels",
+                                      "(profiles/conv3d_khcat_fp16_64to64_48x128x128.md), scaled by voxels",
                     "peak_source": f"{peak_kind} bf16_tflops (burst: one launch timed alone)",
                     "all_conv_launches": {"achieved": round(agg, 1), "peak": sustained,
                                           "frac": round(agg / sustained, 4),
