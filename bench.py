@@ -8,10 +8,13 @@ the named architectures (no checkpoints exist offline), inputs synthetic.
 
   python bench.py [--gpus N --steps K --warmup W] [--precision bf16|fp32] [--impl reference]
 
-N = 1: one GPU per volume. N >= 2 (torchrun, one process per GPU): ranks pair
-up; each pair makes one volume per step with the CFG branches split across the
-pair (one velocity all_gather per step) and the decode windows split (one
-all_reduce of the blend); per-pair work is fixed, so scaling is "weak".
+N = 1: one GPU per volume. N >= 2 (torchrun, one process per GPU), `--mode
+replicas` (default): every rank makes its own volumes (seed = rank), no
+collective on the data path; `--mode split`: ranks pair up and each pair makes
+one volume per step with the CFG branches split across the pair (one velocity
+all_gather per step) and the decode windows split (one all_reduce of the blend).
+Per-GPU work is fixed either way, so scaling is "weak". In replicas mode with an
+even N the split mode is timed too and reported beside the headline ("split").
 ``--impl reference`` times the reference's arithmetic on the host CPU (the
 torch-CPU restatement in ``oracle/``; the reference itself needs MLX/Metal).
 """
@@ -57,6 +60,8 @@ def _args():
     p.add_argument("--warmup", type=int, default=3)
     p.add_argument("--impl", choices=("ours", "reference"), default="ours")
     p.add_argument("--precision", choices=("fp16", "bf16", "fp32"), default="fp16")
+    p.add_argument("--mode", choices=("replicas", "split"), default="replicas",
+                   help="N > 1: independent volumes per GPU, or pairs splitting CFG branches and decode windows")
     p.add_argument("--no-graph", action="store_true")
     p.add_argument("--no-cpu-baseline", action="store_true")
     p.add_argument("--case", choices=("volume", "sweep", "conv", "unet-step", "vae-window", "breakdown"),
@@ -390,8 +395,8 @@ def main() -> None:
         if world > 1:
             torch.distributed.destroy_process_group()
         return
-    if world > 1 and world % 2:
-        raise SystemExit("N > 1 must be even (ranks pair up per volume)")
+    if world > 1 and world % 2 and args.mode == "split":
+        raise SystemExit("--mode split needs an even N (ranks pair up per volume)")
     dev = torch.device("cuda", local)
     torch.cuda.set_device(dev)
 
@@ -404,8 +409,8 @@ def main() -> None:
     vae_w = W.random_weights(W.vae_decoder_shapes(P.PRODUCTION_VAE), seed=1, device=dev)
     spacing = P.image_spacing_tensor(SPACING, dev)
     timesteps, _ = P.set_timesteps_rflow(num_inference_steps=STEPS_RFLOW, input_img_size_numel=math.prod(LATENT[2:]))
-    pairs = D.Pairs(rank, world) if world > 1 else None
-    seed_volume = rank // 2 if world > 1 else 0
+    pairs = D.Pairs(rank, world) if world > 1 and args.mode == "split" else None
+    seed_volume = rank // 2 if pairs is not None else rank
     latent_host = torch.randn(LATENT, generator=torch.Generator().manual_seed(seed_volume)).pin_memory()
     ctx = A.arithmetic_precision(args.precision)
     ctx.__enter__()
@@ -455,7 +460,7 @@ def main() -> None:
         t = torch.tensor([ms], device=dev)
         torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
         ms = float(t.item())
-    volumes_per_step = max(1, world // 2)
+    volumes_per_step = world // 2 if pairs is not None else world
     value = volumes_per_step * 60000.0 / ms
     assert torch.isfinite(out).all(), "non-finite decoded volume"
 
@@ -540,6 +545,40 @@ def main() -> None:
                                           "share_of_step": round(conv_ms / ms, 3),
                                           "timing": "CUDA events around each GEMM stage in an eager pass"}}
 
+    # ------------------------------------------------ the north-star partition beside the replicas
+    split = None
+    if pairs is None and world > 1 and world % 2 == 0:
+        split_pairs = D.Pairs(rank, world)
+        split_sampler = D.CfgSplitStep(unet_w, P.PRODUCTION_UNET, LATENT, class_label=MODALITY, spacing=spacing,
+                                       guidance_scale=GUIDANCE, device=dev, pairs=split_pairs,
+                                       use_cuda_graph=not args.no_graph)
+        split_sampler.prepare()
+        split_latent = torch.randn(LATENT, generator=torch.Generator().manual_seed(rank // 2)).to(dev).contiguous(
+            memory_format=torch.channels_last_3d)
+
+        def split_volume() -> torch.Tensor:
+            final = split_sampler.sample(split_latent, timesteps)
+            return D.pair_window_decode(final, vae_w, constructor=P.PRODUCTION_VAE, roi=DECODE_ROI,
+                                        overlap=DECODE_OVERLAP, scale_factor=1.0, pairs=split_pairs)
+
+        for _ in range(args.warmup):
+            split_volume()
+        barrier()
+        s0, s1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        s0.record()
+        for _ in range(args.steps):
+            split_out = split_volume()
+        s1.record()
+        barrier()
+        split_ms = torch.tensor([s0.elapsed_time(s1) / args.steps], device=dev)
+        torch.distributed.all_reduce(split_ms, op=torch.distributed.ReduceOp.MAX)
+        assert torch.isfinite(split_out).all(), "non-finite decoded volume (split mode)"
+        split = {"value": round((world // 2) * 60000.0 / float(split_ms.item()), 3), "unit": UNIT,
+                 "ms_per_step": round(float(split_ms.item()), 2), "volumes_per_step": world // 2,
+                 "parallelism": f"{world // 2} pairs x (CFG branches split, one velocity all_gather per rflow "
+                                "step; decode windows split, one all_reduce of the blend)"}
+        split_sampler.release()
+
     if rank == 0:
         base = None
         if world == 1 and not args.no_cpu_baseline:
@@ -552,7 +591,9 @@ def main() -> None:
                                    "VAE decode as 4 depth windows ROI (24,64,32) overlap 0.25",
                        "model": "MAISI rflow UNet [64,128,256,512] + VAE decoder [64,128,256] (random init)",
                        "global_batch": volumes_per_step, "seq_len": None,
-                       "parallelism": "single GPU" if world == 1 else f"{world // 2} pairs x (CFG split + window split)",
+                       "parallelism": ("single GPU" if world == 1 else
+                                       f"{world // 2} pairs x (CFG split + window split)" if pairs is not None else
+                                       f"{world} replicas (one volume per GPU per step, no data-path collective)"),
                        "l2": "working set far above L2 (VAE activations 2.1 GB per tensor)",
                        "precision": args.precision, "cuda_graph": not args.no_graph},
             "e2e": {"value": round(volumes_per_step * 60.0 / e2e_s, 3), "unit": UNIT, "h2d_bytes_per_step": h2d,
@@ -562,6 +603,8 @@ def main() -> None:
             "roofline": roofline,
             "cpu_baseline": base,
         }
+        if split is not None:
+            line["split"] = split
         print(json.dumps(line), flush=True)
     sampler.release()
     ctx.__exit__(None, None, None)
