@@ -46,7 +46,7 @@ enum {
   CTMR_ERR_CUDA = 4
 };
 
-enum { CTMR_DTYPE_F32 = 0, CTMR_DTYPE_BF16 = 1 };
+enum { CTMR_DTYPE_F32 = 0, CTMR_DTYPE_BF16 = 1, CTMR_DTYPE_F16 = 2 /* ctmr_transform outputs only */ };
 
 /* CTMR_PRECISION_FP32: fp32 operands carried as fp16 hi/lo pairs, three
  *   tensor-core products per step, fp32 accumulation (~2^-22 relative product
@@ -109,6 +109,10 @@ typedef struct ctmr_conv3d_desc {
   const float* gn_beta;
   int gn_groups;
   float gn_eps;
+  /* Elements between consecutive batch items' rows of a per-batch bias (0: out_channels,
+   * i.e. a dense (batch, out_channels) array; otherwise >= out_channels, e.g. a column
+   * slice of a wider (batch, N) table). */
+  long long bias_row_stride;
 } ctmr_conv3d_desc;
 
 /* Packed-weight element count per plane for a Torch (O, C, k, k, k) weight:

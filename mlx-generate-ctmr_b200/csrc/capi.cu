@@ -217,6 +217,8 @@ int plan_conv(const ctmr_conv3d_desc* d, ConvPlan* p) {
       d->precision != CTMR_PRECISION_FP16)
     return fail(CTMR_ERR_INVALID, "precision");
   if (d->out_channels <= 0) return fail(CTMR_ERR_INVALID, "out_channels");
+  if (d->bias_row_stride != 0 && (d->bias_row_stride < d->out_channels || d->bias_row_stride > (1LL << 30)))
+    return fail(CTMR_ERR_INVALID, "bias_row_stride %lld must be 0 or in [out_channels, 2^30]", d->bias_row_stride);
   if (d->weight == nullptr || (d->precision == CTMR_PRECISION_FP32 && d->weight_lo == nullptr))
     return fail(CTMR_ERR_INVALID, "packed weight missing");
   if (d->y == nullptr || (d->y_dtype != CTMR_DTYPE_F32 && d->y_dtype != CTMR_DTYPE_BF16))
@@ -371,6 +373,12 @@ struct V2Plan {
   int kc, mt, tw, bn, stages;
   size_t smem, stats_bytes;
 };
+
+// Elements between the per-batch bias rows (0 for a per-channel bias).
+int bias_row_stride(const ctmr_conv3d_desc* d) {
+  if (!d->bias_per_batch) return 0;
+  return static_cast<int>(d->bias_row_stride > 0 ? d->bias_row_stride : d->out_channels);
+}
 
 bool g_khcat_unavailable = false;  // a tensor map for the kh-concatenated kernel was refused once
 
@@ -543,7 +551,7 @@ int ctmr_conv3d_stages(const ctmr_conv3d_desc* d, void* workspace, size_t worksp
     np.w_lo = static_cast<const __half*>(d->weight_lo);
     np.opad = p.opad, np.cpad = p.cpad;
     np.bias = d->bias;
-    np.bias_bstride = d->bias_per_batch ? d->out_channels : 0;
+    np.bias_bstride = bias_row_stride(d);
     np.res = static_cast<const float*>(d->residual.data);
     np.res_cstride = d->residual.cstride;
     np.res_up = d->residual_upsampled;
@@ -566,7 +574,7 @@ int ctmr_conv3d_stages(const ctmr_conv3d_desc* d, void* workspace, size_t worksp
     tp.w_lo = static_cast<const __half*>(d->weight_lo);
     tp.opad = p.opad, tp.cpad = p.cpad;
     tp.bias = d->bias;
-    tp.bias_bstride = d->bias_per_batch ? d->out_channels : 0;
+    tp.bias_bstride = bias_row_stride(d);
     tp.res = static_cast<const float*>(d->residual.data);
     tp.res_cstride = d->residual.cstride;
     tp.y = static_cast<float*>(d->y) + d->y_coffset;
@@ -661,7 +669,7 @@ int ctmr_conv3d_stages(const ctmr_conv3d_desc* d, void* workspace, size_t worksp
     if (total > 0 && total < (1LL << 31)) {
       g.total_tiles = static_cast<int>(total);
       g.bias = d->bias;
-      g.bias_bstride = d->bias_per_batch ? d->out_channels : 0;
+      g.bias_bstride = bias_row_stride(d);
       g.res = d->residual.data;
       g.res_bf16 = d->residual.dtype == CTMR_DTYPE_BF16;
       g.res_cstride = d->residual.cstride;
@@ -716,7 +724,7 @@ int ctmr_conv3d_stages(const ctmr_conv3d_desc* d, void* workspace, size_t worksp
       if (total > 0 && total < (1LL << 31)) {
         g.total_tiles = static_cast<int>(total);
         g.bias = d->bias;
-        g.bias_bstride = d->bias_per_batch ? d->out_channels : 0;
+        g.bias_bstride = bias_row_stride(d);
         g.res = d->residual.data;
         g.res_bf16 = d->residual.dtype == CTMR_DTYPE_BF16;
         g.res_cstride = d->residual.cstride;
@@ -776,7 +784,7 @@ int ctmr_conv3d_stages(const ctmr_conv3d_desc* d, void* workspace, size_t worksp
   g.stages = ctmr::conv_stage_plan(p.kc, p.bn, p.exact, g.tmem_cols > 256, &smem);
   if (g.stages < 2) return fail(CTMR_ERR_UNSUPPORTED, "no pipeline fits shared memory");
   g.bias = d->bias;
-  g.bias_bstride = d->bias_per_batch ? d->out_channels : 0;
+  g.bias_bstride = bias_row_stride(d);
   g.res = d->residual.data;
   g.res_bf16 = d->residual.dtype == CTMR_DTYPE_BF16;
   g.res_cstride = d->residual.cstride;
@@ -917,7 +925,8 @@ int ctmr_transform(const ctmr_transform_desc* d, void* stream) {
   if ((st = check_view(d->x2, "x2", false))) return st;
   if (d->batch <= 0 || d->depth <= 0 || d->height <= 0 || d->width <= 0)
     return fail(CTMR_ERR_INVALID, "grid must be positive");
-  if (d->y == nullptr || (d->y_dtype != CTMR_DTYPE_F32 && d->y_dtype != CTMR_DTYPE_BF16))
+  if (d->y == nullptr ||
+      (d->y_dtype != CTMR_DTYPE_F32 && d->y_dtype != CTMR_DTYPE_BF16 && d->y_dtype != CTMR_DTYPE_F16))
     return fail(CTMR_ERR_INVALID, "output");
   const int ctot = d->x.channels + (d->x2.data ? d->x2.channels : 0);
   if (d->y_channels < ctot || d->y_cstride < d->y_channels) return fail(CTMR_ERR_INVALID, "output channels");
@@ -946,7 +955,8 @@ int ctmr_transform(const ctmr_transform_desc* d, void* stream) {
   pp.silu = d->silu;
   pp.cpad = d->y_channels;
   pp.out_cstride = d->y_cstride;
-  pp.out_kind = d->y_dtype == CTMR_DTYPE_BF16 ? ctmr::kPrepOutBF16 : ctmr::kPrepOutF32;
+  pp.out_kind = d->y_dtype == CTMR_DTYPE_BF16 ? ctmr::kPrepOutBF16
+                : (d->y_dtype == CTMR_DTYPE_F16 ? ctmr::kPrepOutF16 : ctmr::kPrepOutF32);
   pp.out = d->y;
   cudaError_t e = ctmr::launch_prepare(pp, static_cast<cudaStream_t>(stream));
   return e == cudaSuccess ? CTMR_OK : cuda_fail(e, "transform launch");

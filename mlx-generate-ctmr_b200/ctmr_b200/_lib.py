@@ -20,6 +20,7 @@ CTMR_ERR_CUDA = 4
 
 DTYPE_F32 = 0
 DTYPE_BF16 = 1
+DTYPE_F16 = 2  # ctmr_transform outputs only
 PRECISION_FP32 = 0
 PRECISION_BF16 = 1
 PRECISION_FP16 = 2
@@ -100,6 +101,7 @@ class Conv3dDesc(ctypes.Structure):
         ("gn_beta", ctypes.c_void_p),
         ("gn_groups", ctypes.c_int),
         ("gn_eps", ctypes.c_float),
+        ("bias_row_stride", ctypes.c_longlong),
     ]
 
 

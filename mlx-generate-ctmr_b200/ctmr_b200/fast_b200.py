@@ -213,11 +213,15 @@ def linear(array: torch.Tensor, weight: torch.Tensor, bias: torch.Tensor | None,
     return F.linear(array.to(dtype), weight.to(dtype), None if bias is None else bias.to(dtype))
 
 
-def group_norm_ncdhw(array, weight, bias, *, num_groups: int, eps: float, mx=None, apply_silu: bool = False):
-    """Group norm with fp32 statistics and an optional fused SiLU (``fast_fp32.py:102-118``)."""
+def group_norm_ncdhw(array, weight, bias, *, num_groups: int, eps: float, mx=None, apply_silu: bool = False,
+                     out_dtype: torch.dtype | None = None):
+    """Group norm with fp32 statistics and an optional fused SiLU (``fast_fp32.py:102-118``).
+
+    ``out_dtype`` (default: the activation dtype) may also be fp16, for a result that
+    only feeds 16-bit dense operands (the attention tokens)."""
     x, x2 = _split(array)
     affine = ops.group_norm_affine(x, weight, bias, groups=num_groups, eps=eps, x2=x2)
-    return ops.transform(x, x2=x2, affine=affine, silu=apply_silu, out_dtype=activation_dtype())
+    return ops.transform(x, x2=x2, affine=affine, silu=apply_silu, out_dtype=out_dtype or activation_dtype())
 
 
 def avg_pool3d_ncdhw(array, *, mx=None) -> torch.Tensor:
@@ -471,7 +475,9 @@ def spatial_attention_ncdhw(x: torch.Tensor, weights: Mapping[str, torch.Tensor]
     if c % num_head_channels:
         raise ValueError("num_channels must be divisible by num_head_channels")
     heads, scale = c // num_head_channels, float(num_head_channels) ** -0.5
-    normed = group_norm_ncdhw(x, weights["norm.weight"], weights["norm.bias"], num_groups=num_groups, eps=eps)
+    # The normalised tokens feed only the Q/K/V projection: written directly in its operand dtype.
+    normed = group_norm_ncdhw(x, weights["norm.weight"], weights["norm.bias"], num_groups=num_groups, eps=eps,
+                              out_dtype=dense_dtype())
     tokens = normed.permute(0, 2, 3, 4, 1).reshape(b, d * h * w, c)
     merged = self_attention_tokens(tokens, weights, heads=heads, scale=scale, include_fc=include_fc)
     out = merged.reshape(b, d, h, w, c).permute(0, 4, 1, 2, 3)

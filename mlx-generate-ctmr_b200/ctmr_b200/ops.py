@@ -54,11 +54,13 @@ def _stream() -> int:
     return torch.cuda.current_stream().cuda_stream
 
 
-def _dtype_code(dtype: torch.dtype) -> int:
+def _dtype_code(dtype: torch.dtype, *, allow_f16: bool = False) -> int:
     if dtype == F32:
         return _lib.DTYPE_F32
     if dtype == BF16:
         return _lib.DTYPE_BF16
+    if allow_f16 and dtype == torch.float16:
+        return _lib.DTYPE_F16
     raise ValueError(f"ctmr_b200 activations must be float32 or bfloat16, got {dtype}")
 
 
@@ -239,10 +241,14 @@ def conv3d(
     else:
         od, oh, ow = d, h, w
     o = packed.out_channels
+    bias_rows = 0
     if bias is not None:
-        bias = bias.to(dtype=F32).contiguous()
         if not (bias.shape == (o,) or bias.shape == (b, o)):
             raise ValueError(f"bias shape {tuple(bias.shape)} must be ({o},) or ({b}, {o})")
+        if bias.dim() == 2 and bias.dtype == F32 and bias.stride(1) == 1 and bias.stride(0) >= o:
+            bias_rows = int(bias.stride(0))  # a column slice of a wider table: read in place
+        else:
+            bias = bias.to(dtype=F32).contiguous()
     if affine is not None:
         affine = affine.to(dtype=F32).contiguous()
         if affine.numel() != b * cin * 2:
@@ -274,6 +280,7 @@ def conv3d(
     desc.silu = int(silu)
     desc.bias = bias.data_ptr() if bias is not None else None
     desc.bias_per_batch = int(bias is not None and bias.dim() == 2)
+    desc.bias_row_stride = bias_rows
     desc.residual = view(residual)
     desc.residual_upsampled = int(residual_upsampled)
     desc.y = out.data_ptr()  # a channel slice's pointer already includes its first channel
@@ -444,7 +451,7 @@ def transform(
     desc.affine = affine.data_ptr() if affine is not None else None
     desc.silu = int(silu)
     desc.y = out.data_ptr()
-    desc.y_dtype = _dtype_code(out.dtype)
+    desc.y_dtype = _dtype_code(out.dtype, allow_f16=True)  # fp16 is a transform-only output (dense operands)
     desc.y_channels = int(out.shape[1])
     desc.y_cstride = rows_stride(out)
     _count(1)

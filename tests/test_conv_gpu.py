@@ -460,3 +460,40 @@ def test_groupnorm_inside_the_conv_call(cuda, shape, x2_channels, out_channels, 
     torch.cuda.synchronize()
     err = ops_ref.rel_l2(got.cpu(), ref.cpu().double())
     assert err <= (1e-6 if precision == "fp32" else 1e-3), f"{precision} rel-L2 {err:.3e}"
+
+
+@pytest.mark.parametrize("shape", [(2, 64, 3, 16, 16), (2, 32, 2, 8, 16)])
+def test_bias_rows_read_in_place(cuda, shape):
+    """A per-batch bias that is a column slice of a wider table (bias_row_stride) gives the same
+    output, bitwise, as the same bias made contiguous."""
+    from ctmr_b200 import ops
+
+    rng = np.random.default_rng(61)
+    b, c = shape[:2]
+    o = 48
+    x = ops.to_ndhwc(torch.from_numpy(rng.standard_normal(shape).astype(np.float32)).to(cuda))
+    w = torch.from_numpy((rng.standard_normal((o, c, 3, 3, 3)) / np.sqrt(27 * c)).astype(np.float32)).to(cuda)
+    table = torch.from_numpy(rng.standard_normal((b, 200)).astype(np.float32)).to(cuda)
+    sliced = table[:, 37:37 + o]
+    assert not sliced.is_contiguous()
+    packed = ops.pack_weight(w, "fp16")
+    y_slice = ops.conv3d(x, packed, sliced)
+    y_dense = ops.conv3d(x, packed, sliced.contiguous())
+    torch.cuda.synchronize()
+    assert torch.equal(y_slice, y_dense)
+
+
+def test_transform_fp16_output(cuda):
+    """GroupNorm transform written in fp16 equals the fp32 transform rounded once (attention tokens)."""
+    from ctmr_b200 import ops
+
+    rng = np.random.default_rng(67)
+    x = ops.to_ndhwc(torch.from_numpy(rng.standard_normal((2, 64, 4, 8, 8)).astype(np.float32)).to(cuda))
+    gamma = torch.from_numpy(rng.standard_normal(64).astype(np.float32)).to(cuda)
+    beta = torch.from_numpy(rng.standard_normal(64).astype(np.float32)).to(cuda)
+    affine = ops.group_norm_affine(x, gamma, beta, groups=32, eps=1e-6)
+    y32 = ops.transform(x, affine=affine, out_dtype=torch.float32)
+    y16 = ops.transform(x, affine=affine, out_dtype=torch.float16)
+    torch.cuda.synchronize()
+    assert y16.dtype == torch.float16
+    assert torch.equal(y16, y32.to(torch.float16))
