@@ -127,6 +127,14 @@ CTMR_API size_t ctmr_packed_weight_elems(int out_channels, int in_channels, int 
 CTMR_API int ctmr_pack_weight(const float* weight, int out_channels, int in_channels, int kernel_size, int upsample,
                      int precision, void* packed, void* packed_lo, void* stream);
 
+/* ctmr_pack_weight for a weight stored channels-last, (O, k, k, k, C) (device pointer): the
+ * layout of released safetensors checkpoints, which the reference transposes to Torch
+ * layout on load (`weights.py:152-156`, LAYOUT_CONV3D_W); packed here without that copy.
+ * Same packed result, bit for bit. */
+CTMR_API int ctmr_pack_weight_channels_last(const float* weight, int out_channels, int in_channels,
+                     int kernel_size, int upsample, int precision, void* packed, void* packed_lo,
+                     void* stream);
+
 /* Workspace bytes ctmr_conv3d needs for this descriptor (the prepared operand). */
 CTMR_API size_t ctmr_conv3d_workspace_size(const ctmr_conv3d_desc* desc);
 

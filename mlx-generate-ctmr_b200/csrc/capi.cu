@@ -472,8 +472,9 @@ size_t ctmr_packed_weight_elems(int out_channels, int in_channels, int kernel_si
   return static_cast<size_t>(taps * round_up(out_channels, 16) * round_up(in_channels, 16));
 }
 
-int ctmr_pack_weight(const float* weight, int out_channels, int in_channels, int kernel_size, int upsample,
-                     int precision, void* packed, void* packed_lo, void* stream) {
+namespace {
+int pack_weight_any(const float* weight, int out_channels, int in_channels, int kernel_size, int upsample,
+                    int precision, void* packed, void* packed_lo, void* stream, int channels_last) {
   if (weight == nullptr || packed == nullptr) return fail(CTMR_ERR_INVALID, "null weight pointer");
   if (out_channels <= 0 || in_channels <= 0) return fail(CTMR_ERR_INVALID, "channel counts");
   if (kernel_size != 1 && kernel_size != 3) return fail(CTMR_ERR_UNSUPPORTED, "kernel_size must be 1 or 3");
@@ -486,8 +487,21 @@ int ctmr_pack_weight(const float* weight, int out_channels, int in_channels, int
   cudaError_t e = ctmr::launch_pack_weight(weight, out_channels, in_channels, kernel_size, upsample,
                                            static_cast<int>(round_up(out_channels, 16)),
                                            static_cast<int>(round_up(in_channels, 16)), kind, packed, packed_lo,
-                                           static_cast<cudaStream_t>(stream));
+                                           static_cast<cudaStream_t>(stream), channels_last);
   return e == cudaSuccess ? CTMR_OK : cuda_fail(e, "pack_weight launch");
+}
+}  // namespace
+
+int ctmr_pack_weight(const float* weight, int out_channels, int in_channels, int kernel_size, int upsample,
+                     int precision, void* packed, void* packed_lo, void* stream) {
+  return pack_weight_any(weight, out_channels, in_channels, kernel_size, upsample, precision, packed, packed_lo,
+                         stream, 0);
+}
+
+int ctmr_pack_weight_channels_last(const float* weight, int out_channels, int in_channels, int kernel_size,
+                                   int upsample, int precision, void* packed, void* packed_lo, void* stream) {
+  return pack_weight_any(weight, out_channels, in_channels, kernel_size, upsample, precision, packed, packed_lo,
+                         stream, 1);
 }
 
 size_t ctmr_conv3d_workspace_size(const ctmr_conv3d_desc* desc) {

@@ -1,6 +1,7 @@
-// Weight packing for the implicit-GEMM convolution: Torch (O, C, k, k, k) fp32
-// -> K-major taps [T][O_pad][C_pad] in bf16 or fp16, or in fp16 hi/lo planes
-// for the split-fp32 mode. Counterpart of `pack_weight` / `pack_upsample_weight`
+// Weight packing for the implicit-GEMM convolution: Torch (O, C, k, k, k) fp32,
+// or the channels-last (O, k, k, k, C) of released checkpoints, -> K-major taps
+// [T][O_pad][C_pad] in bf16 or fp16, or in fp16 hi/lo planes for the split-fp32
+// mode. Counterpart of `pack_weight` / `pack_upsample_weight`
 // (`_nax_conv.py:391-445`), with the tap-major rows transposed to the K-major
 // operand layout the tensor cores read.
 //
@@ -32,7 +33,8 @@ __device__ __forceinline__ void fold_range(int p, int t, int& k0, int& k1) {
 }
 
 __global__ void pack_weight_kernel(const float* __restrict__ w, int O, int C, int k, int upsample, int opad,
-                                   int cpad, int kind, void* __restrict__ out, void* __restrict__ out_lo) {
+                                   int cpad, int kind, void* __restrict__ out, void* __restrict__ out_lo,
+                                   int channels_last) {
   griddep_wait();  // the preceding kernel's writes are visible from here on
   griddep_launch_dependents();
   const int taps = upsample ? 64 : k * k * k;
@@ -44,9 +46,12 @@ __global__ void pack_weight_kernel(const float* __restrict__ w, int O, int C, in
     const int tap = static_cast<int>(i / (static_cast<long long>(cpad) * opad));
     float v = 0.f;
     if (o < O && c < C) {
-      const float* src = w + (static_cast<long long>(o) * C + c) * k * k * k;
+      // Kernel tap q of (o, c): Torch src[q], channels-last src[q * C].
+      const long long k3 = static_cast<long long>(k) * k * k;
+      const float* src = channels_last ? w + static_cast<long long>(o) * k3 * C + c : w + (static_cast<long long>(o) * C + c) * k3;
+      const long long step = channels_last ? C : 1;
       if (!upsample) {
-        v = src[tap];
+        v = src[tap * step];
       } else {
         const int phase = tap >> 3, t = tap & 7;
         int d0, d1, h0, h1, w0, w1;
@@ -55,7 +60,7 @@ __global__ void pack_weight_kernel(const float* __restrict__ w, int O, int C, in
         fold_range(phase & 1, t & 1, w0, w1);
         for (int kd = d0; kd <= d1; ++kd)
           for (int kh = h0; kh <= h1; ++kh)
-            for (int kw = w0; kw <= w1; ++kw) v += src[(kd * 3 + kh) * 3 + kw];
+            for (int kw = w0; kw <= w1; ++kw) v += src[((kd * 3 + kh) * 3 + kw) * step];
       }
     }
     if (kind == kPackSplitF16) {
@@ -74,14 +79,14 @@ __global__ void pack_weight_kernel(const float* __restrict__ w, int O, int C, in
 }  // namespace
 
 cudaError_t launch_pack_weight(const float* w, int O, int C, int k, int upsample, int opad, int cpad, int kind,
-                               void* out, void* out_lo, cudaStream_t stream) {
+                               void* out, void* out_lo, cudaStream_t stream, int channels_last) {
   const int taps = upsample ? 64 : k * k * k;
   const long long total = static_cast<long long>(taps) * opad * cpad;
   long long blocks = (total + 255) / 256;
   if (blocks > 148LL * 32) blocks = 148LL * 32;
   if (blocks < 1) blocks = 1;
   launch_kernel(pack_weight_kernel, static_cast<unsigned>(blocks), 256, 0, stream, w, O, C, k, upsample, opad, cpad, kind,
-                                                                        out, out_lo);
+                out, out_lo, channels_last);
   return cudaGetLastError();
 }
 

@@ -7,7 +7,9 @@ namespace ctmr {
 
 enum PackKind : int { kPackBF16 = 0, kPackSplitF16 = 1, kPackF16 = 2 };
 
+// `channels_last`: the source is (O, k, k, k, C) (the channels-last layout of
+// released checkpoints) instead of Torch's (O, C, k, k, k).
 cudaError_t launch_pack_weight(const float* w, int O, int C, int k, int upsample, int opad, int cpad, int kind,
-                               void* out, void* out_lo, cudaStream_t stream);
+                               void* out, void* out_lo, cudaStream_t stream, int channels_last = 0);
 
 }  // namespace ctmr

@@ -168,12 +168,20 @@ def pack_weight(weight: torch.Tensor, precision: str, *, upsample: bool = False)
     """Pack a Torch ``(O, C, k, k, k)`` weight; the nearest-2x fold with ``upsample``.
 
     Counterpart of ``pack_weight`` / ``pack_upsample_weight`` (``_nax_conv.py:391-445``).
+    A weight whose storage is channels-last ``(O, k, k, k, C)`` — the Torch-layout view
+    ``weights.load_network_file`` returns for a released checkpoint — is packed from
+    that storage directly (``ctmr_pack_weight_channels_last``), without a transposed copy.
     """
     if weight.dim() != 5 or weight.shape[2] != weight.shape[3] or weight.shape[3] != weight.shape[4]:
         raise ValueError(f"conv weight must be (O, C, k, k, k); got {tuple(weight.shape)}")
     o, c, k = int(weight.shape[0]), int(weight.shape[1]), int(weight.shape[2])
     code = _precision_code(precision)
-    w = weight.detach().to(dtype=F32).contiguous()
+    w = weight.detach()
+    channels_last = (w.dtype == F32 and c > 1 and k > 1 and
+                     w.is_contiguous(memory_format=torch.channels_last_3d))
+    if not channels_last:
+        w = w.to(dtype=F32).contiguous()
+    entry = LIB.ctmr_pack_weight_channels_last if channels_last else LIB.ctmr_pack_weight
     n = int(LIB.ctmr_packed_weight_elems(o, c, k, int(upsample)))
     if n == 0:
         raise ValueError(f"unsupported conv weight shape {tuple(weight.shape)}")
@@ -185,7 +193,7 @@ def pack_weight(weight: torch.Tensor, precision: str, *, upsample: bool = False)
         lo = None
     _count(1)
     check(
-        LIB.ctmr_pack_weight(
+        entry(
             w.data_ptr(), o, c, k, int(upsample), code, hi.data_ptr(), lo.data_ptr() if lo is not None else None,
             _stream(),
         ),

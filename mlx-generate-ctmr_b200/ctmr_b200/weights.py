@@ -198,3 +198,89 @@ def _is_gn(name: str, shapes: Shapes) -> bool:
     stem = name.rsplit(".", 1)[0]
     w = shapes.get(f"{stem}.weight")
     return w is not None and len(w) == 1
+
+
+# ---------------------------------------------------------------- released checkpoints
+def disk_shape(torch_shape: tuple[int, ...]) -> tuple[int, ...]:
+    """Stored shape of a parameter: convolution weights channels-last ``(O, k, k, k, I)``
+    (the reference's ``LAYOUT_CONV3D_W``, ``maisi_mlx_weights.py:123-133``), everything else
+    as in Torch."""
+    if len(torch_shape) == 5:
+        o, i, kd, kh, kw = torch_shape
+        return (o, kd, kh, kw, i)
+    return tuple(torch_shape)
+
+
+def load_network_file(path, network: str, shapes: Shapes, *, device=None
+                      ) -> tuple[dict[str, torch.Tensor], float | None]:
+    """Load one network from a native ``.safetensors`` checkpoint (``weights.py:102-166``).
+
+    ``shapes`` is the network's Torch-layout inventory (``unet_shapes``,
+    ``controlnet_shapes``, ``vae_decoder_shapes``). A file named
+    ``model.safetensors`` holds every network under ``<network>.``-prefixed keys;
+    any other file holds one network unprefixed. Every tensor must be listed,
+    finite float32 in its stored layout; the UNet file carries the latent
+    ``scale_factor``, the others must not. Returns ``(weights, scale_factor)``:
+    convolution weights are Torch-layout views ``(O, I, k, k, k)`` of the
+    channels-last storage (no transposed copy; ``ops.pack_weight`` packs such a
+    view from its storage), on ``device`` when given. Raises ``ValueError`` as the
+    reference raises ``InvalidInputError``.
+    """
+    from pathlib import Path
+
+    from safetensors import safe_open
+
+    path = Path(path)
+    if path.suffix != ".safetensors":
+        raise ValueError(f"{path.name} must be a safetensors file")
+    prefix = network + "." if path.name == "model.safetensors" else ""
+    weights: dict[str, torch.Tensor] = {}
+    scale_factor = None
+    with safe_open(str(path), framework="pt") as f:
+        selected = {k.removeprefix(prefix): k for k in f.keys() if k.startswith(prefix)}
+        for name in selected:
+            if name != "scale_factor" and name not in shapes:
+                raise ValueError(f"{path.name} has unexpected tensor {name}")
+        missing = [name for name in shapes if name not in selected]
+        if missing:
+            raise ValueError(f"{path.name} is missing {missing[0]}")
+        if network == "unet":
+            if "scale_factor" not in selected:
+                raise ValueError(f"{path.name} is missing scale_factor")
+            scale = f.get_tensor(selected["scale_factor"])
+            if scale.numel() != 1 or not torch.isfinite(scale).all() or float(scale.reshape(())) <= 0.0:
+                raise ValueError(f"{path.name} scale_factor must be one finite positive value")
+            scale_factor = float(scale.reshape(()))
+        elif "scale_factor" in selected:
+            raise ValueError(f"{path.name} must not contain scale_factor")
+        for name, stored in selected.items():
+            if name == "scale_factor":
+                continue
+            t = f.get_tensor(stored)
+            expected = disk_shape(shapes[name])
+            if tuple(t.shape) != expected or t.dtype != torch.float32 or not torch.isfinite(t).all():
+                raise ValueError(f"{path.name} tensor {name} must be finite float32 with shape {expected}; "
+                                 f"got {t.dtype} {tuple(t.shape)}")
+            if device is not None:
+                t = t.to(device)
+            weights[name] = t.permute(0, 4, 1, 2, 3) if t.dim() == 5 else t
+    return weights, scale_factor
+
+
+def save_network_file(path, network: str, weights: Mapping[str, torch.Tensor], *,
+                      scale_factor: float | None = None) -> None:
+    """Write Torch-layout ``weights`` as a native checkpoint (the inverse of
+    ``load_network_file``): convolution weights channels-last, float32."""
+    from pathlib import Path
+
+    from safetensors.torch import save_file
+
+    path = Path(path)
+    prefix = network + "." if path.name == "model.safetensors" else ""
+    out = {}
+    for name, t in weights.items():
+        t = t.detach().to("cpu", torch.float32)
+        out[prefix + name] = (t.permute(0, 2, 3, 4, 1) if t.dim() == 5 else t).contiguous()
+    if scale_factor is not None:
+        out[prefix + "scale_factor"] = torch.tensor(float(scale_factor), dtype=torch.float32)
+    save_file(out, str(path))

@@ -497,3 +497,41 @@ def test_transform_fp16_output(cuda):
     torch.cuda.synchronize()
     assert y16.dtype == torch.float16
     assert torch.equal(y16, y32.to(torch.float16))
+
+
+@pytest.mark.parametrize("precision", ["fp32", "bf16", "fp16"])
+@pytest.mark.parametrize(("o", "c", "k", "upsample"), [(48, 64, 3, False), (32, 16, 3, True), (20, 24, 3, False)])
+def test_channels_last_weight_packs_identically(cuda, o, c, k, upsample, precision):
+    """A weight stored channels-last (O, k, k, k, C) — a released checkpoint's layout, seen through
+    a Torch-layout view — packs to the same bits as the Torch-layout weight."""
+    from ctmr_b200 import ops
+
+    g = torch.Generator().manual_seed(71)
+    w = torch.randn(o, c, k, k, k, generator=g)
+    view = w.permute(0, 2, 3, 4, 1).contiguous().permute(0, 4, 1, 2, 3).to(cuda)
+    assert view.is_contiguous(memory_format=torch.channels_last_3d) and not view.is_contiguous()
+    a = ops.pack_weight(w.to(cuda), precision, upsample=upsample)
+    b = ops.pack_weight(view, precision, upsample=upsample)
+    torch.cuda.synchronize()
+    assert torch.equal(a.hi, b.hi)
+    assert (a.lo is None and b.lo is None) or torch.equal(a.lo, b.lo)
+
+
+def test_decoder_from_a_native_checkpoint(cuda, tmp_path):
+    """The production VAE decoder run on weights loaded from a native checkpoint (channels-last
+    conv weights, packed from that storage) gives the same volume, bitwise, as on the weights it
+    was written from."""
+    from ctmr_b200 import fast_b200, networks, pipeline as P, weights as W
+
+    shapes = W.vae_decoder_shapes(P.PRODUCTION_VAE)
+    w = W.random_weights(shapes, seed=9, device="cpu")
+    W.save_network_file(tmp_path / "vae.safetensors", "vae", w)
+    loaded, scale = W.load_network_file(tmp_path / "vae.safetensors", "vae", shapes, device=cuda)
+    assert scale is None
+    w_dev = {k: t.to(cuda) for k, t in w.items()}
+    latent = torch.randn(1, 4, 8, 8, 8, generator=torch.Generator().manual_seed(3)).to(cuda)
+    with fast_b200.arithmetic_precision("fp16"):
+        a = networks.decode_vae_ncdhw(latent, w_dev, constructor=P.PRODUCTION_VAE)
+        b = networks.decode_vae_ncdhw(latent, loaded, constructor=P.PRODUCTION_VAE)
+    torch.cuda.synchronize()
+    assert all(torch.equal(x, y) for x, y in zip(a, b, strict=True))
