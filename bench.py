@@ -64,7 +64,7 @@ def _args():
                    help="N > 1: independent volumes per GPU, or pairs splitting CFG branches and decode windows")
     p.add_argument("--no-graph", action="store_true")
     p.add_argument("--no-cpu-baseline", action="store_true")
-    p.add_argument("--case", choices=("volume", "sweep", "conv", "unet-step", "vae-window", "breakdown"),
+    p.add_argument("--case", choices=("volume", "sweep", "conv", "gn", "unet-step", "vae-window", "breakdown"),
                    default="volume",
                    help="volume: the benchmark; sweep: the reference's conv-kernel sweep (TFLOP/s per shape); "
                         "conv / unet-step / vae-window: one kernel shape, one UNet step or one decode window "
@@ -320,6 +320,52 @@ def _profile_pass(part: str, fn, dev) -> None:
     _breakdown(part, prof, total)
 
 
+def _time_groupnorm(shape: tuple[int, ...], iters: int, dev: torch.device) -> None:
+    """The memory-bound passes around each conv on one (B, C, D, H, W) fp32 tensor, each captured
+    as a CUDA graph and replayed ``iters`` times between events: the GroupNorm statistics
+    (``ctmr_group_norm_affine``: one read) and the normalise + SiLU + fp16 cast the conv's operand
+    pass performs (``ctmr_transform``: one read, one half-size write). GB/s of algorithmic bytes
+    against the measured HBM copy bandwidth; inputs above L2 (126 MB) come from HBM."""
+    from ctmr_b200 import ops
+
+    b, c, d, h, w = shape
+    gen = torch.Generator(device=dev).manual_seed(0)
+    x = ops.to_ndhwc(torch.randn((b, c, d, h, w), device=dev, generator=gen))
+    gamma = torch.rand(c, device=dev, generator=gen) + 0.5
+    beta = torch.randn(c, device=dev, generator=gen)
+    affine = ops.group_norm_affine(x, gamma, beta, groups=32, eps=1e-6)
+    out = ops.empty_ndhwc(b, c, d, h, w, torch.float16, dev)
+    elems = b * c * d * h * w
+    peaks, kind = _peaks()
+    hbm = float(peaks.get("hbm_gbs", FALLBACK_PEAKS.get("hbm_gbs", 6650.0)))
+    passes = {"gn_statistics": (lambda: ops.group_norm_affine(x, gamma, beta, groups=32, eps=1e-6),
+                                elems * 4),
+              "normalise_silu_fp16": (lambda: ops.transform(x, affine=affine, silu=True, out=out), elems * 6)}
+    for name, (fn, nbytes) in passes.items():
+        for _ in range(3):
+            fn()
+        torch.cuda.synchronize(dev)
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g):
+            for _ in range(iters):
+                fn()
+        g.replay()
+        torch.cuda.synchronize(dev)
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        g.replay()
+        e1.record()
+        torch.cuda.synchronize(dev)
+        ms = e0.elapsed_time(e1) / iters
+        gbs = nbytes / (ms * 1e-3) / 1e9
+        print(json.dumps({"case": name, "shape_bcdhw": list(shape), "ms": round(ms, 4),
+                          "algorithmic_bytes": nbytes, "gbs": round(gbs, 1), "frac_of_hbm": round(gbs / hbm, 3),
+                          "peak": f"{kind} hbm_gbs {hbm}",
+                          "l2": "input above L2" if elems * 4 > 126e6 else "input fits L2 (stays resident)"}),
+              flush=True)
+        del g
+
+
 def run_case(args) -> None:
     from ctmr_b200 import fast_b200 as A
     from ctmr_b200 import pipeline as P
@@ -339,6 +385,9 @@ def run_case(args) -> None:
                                   "gemm_ms": round(ms, 4), "tflops": round(tflops, 1),
                                   "frac_of_peak": round(tflops / peak, 3), "peak": f"{kind} bf16_tflops {peak}"}),
                       flush=True)
+            return
+        if args.case == "gn":
+            _time_groupnorm(tuple(int(v) for v in args.shape.split(","))[:5], args.iters, dev)
             return
         if args.case in ("unet-step", "breakdown"):
             w = W.random_weights(W.unet_shapes(P.PRODUCTION_UNET), seed=0, device=dev)

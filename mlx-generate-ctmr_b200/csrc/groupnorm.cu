@@ -6,9 +6,11 @@
 // Pass 1 (grid chunks x batch): each block reads a contiguous voxel range with
 // 16-byte loads (every voxel row is C contiguous channels). A thread owns one
 // 8-channel slice and a voxel lane; it accumulates sums of (x - pivot) and
-// (x - pivot)^2 around its first value, converts them to (count, mean, M2), and
-// the block merges lanes, then channels into groups, in a fixed order (Chan et
-// al.'s pairwise update), writing one (n, mean, M2) partial per group.
+// (x - pivot)^2 around one pivot per channel shared by the block (the chunk's
+// first voxel), so lanes combine by plain addition: a shuffle-xor tree inside
+// each warp, then the warps in order through shared memory. Channels then merge
+// into groups in a fixed order (Chan et al.'s pairwise update), one (n, mean,
+// M2) partial per group.
 // Pass 2 (grid groups x batch): one block per group merges the chunk partials
 // (each thread its strided chunks in order, a fixed shuffle tree per warp, then
 // the warps in order) in double precision, then writes
@@ -86,10 +88,10 @@ __device__ __forceinline__ Moments merge(Moments a, Moments b) {
 __global__ void __launch_bounds__(kGnThreads) gn_partial_kernel(const GnParams p) {
   griddep_wait();  // the preceding kernel's writes are visible from here on
   griddep_launch_dependents();
-  __shared__ float s_mean[kGnThreads][8];
-  __shared__ float s_m2[kGnThreads][8];
+  __shared__ float s_sum[kGnThreads][8];   // per thread, then per warp: sums of (x - pivot)
+  __shared__ float s_sq[kGnThreads][8];    // ... of (x - pivot)^2
   __shared__ float s_n[kGnThreads];
-  extern __shared__ float s_chan[];  // [ctot][3]
+  extern __shared__ float s_chan[];        // [ctot][3]: (count, mean, M2) per channel
   const int ctot = p.src[0].channels + p.src[1].channels;
   const int nslices = (ctot + 7) / 8;
   const int lanes = kGnThreads / nslices;
@@ -102,6 +104,9 @@ __global__ void __launch_bounds__(kGnThreads) gn_partial_kernel(const GnParams p
   const long long v_end = min(p.voxels, v_begin + per);
   const long long base = static_cast<long long>(b) * p.voxels;
 
+  // One pivot per channel for the whole block (the chunk's first voxel), so that the
+  // shifted sums of all lanes add without rescaling: n, S = sum(x - p), Q = sum((x - p)^2)
+  // give mean = p + S / n and M2 = Q - S^2 / n.
   float pivot[8], s[8], q[8];
   float n = 0.f;
 #pragma unroll
@@ -110,17 +115,12 @@ __global__ void __launch_bounds__(kGnThreads) gn_partial_kernel(const GnParams p
     s[i] = 0.f;
     q[i] = 0.f;
   }
+  if (v_begin < v_end) {
+    int cnt;
+    gn_load8(p, base + v_begin, slice * 8, pivot, cnt);
+  }
   if (lane < lanes) {
     long long v = v_begin + lane;
-    if (v < v_end) {
-      float x[8];
-      int cnt;
-      gn_load8(p, base + v, slice * 8, x, cnt);
-#pragma unroll
-      for (int i = 0; i < 8; ++i) pivot[i] = x[i];
-      n = 1.f;
-      v += lanes;
-    }
     // Four voxels per step, all loads issued before any accumulation.
     for (; v + 3 * lanes < v_end; v += 4 * lanes) {
       float x[4][8];
@@ -151,29 +151,66 @@ __global__ void __launch_bounds__(kGnThreads) gn_partial_kernel(const GnParams p
       n += 1.f;
     }
   }
+  // Lanes -> channels. With a power-of-two slice count below 32 the lanes of one
+  // slice sit nslices apart in a warp: a shuffle-xor tree sums them, then the
+  // warps add in order through shared memory. Otherwise every thread's sums go
+  // through shared memory and add in lane order. Fixed order either way.
+  const bool shfl = (nslices & (nslices - 1)) == 0 && nslices < 32;
+  if (shfl) {
+    for (int off = nslices; off < 32; off <<= 1) {
 #pragma unroll
-  for (int i = 0; i < 8; ++i) {
-    const float mean_d = n > 0.f ? s[i] / n : 0.f;
-    s_mean[tid][i] = pivot[i] + mean_d;
-    s_m2[tid][i] = fmaxf(0.f, q[i] - s[i] * mean_d);
+      for (int i = 0; i < 8; ++i) {
+        s[i] += __shfl_xor_sync(0xffffffffu, s[i], off);
+        q[i] += __shfl_xor_sync(0xffffffffu, q[i], off);
+      }
+      n += __shfl_xor_sync(0xffffffffu, n, off);
+    }
+    const int wl = tid & 31;
+    if (wl < nslices) {
+      const int row = (tid >> 5) * nslices + wl;  // [warp][slice]
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        s_sum[row][i] = s[i];
+        s_sq[row][i] = q[i];
+      }
+      s_n[row] = n;
+    }
+  } else {
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      s_sum[tid][i] = s[i];
+      s_sq[tid][i] = q[i];
+    }
+    s_n[tid] = lane < lanes ? n : 0.f;
   }
-  s_n[tid] = (lane < lanes) ? n : 0.f;
   __syncthreads();
-
-  // Lanes -> channels (fixed lane order).
+  const int rows = shfl ? kGnThreads / 32 : lanes;  // partial sums per slice
   for (int c = tid; c < ctot; c += kGnThreads) {
     const int sl = c / 8, i = c % 8;
-    Moments m{0.f, 0.f, 0.f};
-    for (int l = 0; l < lanes; ++l) {
-      const int t = l * nslices + sl;
-      m = merge(m, Moments{s_n[t], s_mean[t][i], s_m2[t][i]});
+    float nn = 0.f, ss = 0.f, qq = 0.f;
+    for (int r = 0; r < rows; ++r) {
+      const int t = r * nslices + sl;
+      nn += s_n[t];
+      ss += s_sum[t][i];
+      qq += s_sq[t][i];
     }
-    s_chan[3 * c] = m.n;
-    s_chan[3 * c + 1] = m.mean;
-    s_chan[3 * c + 2] = m.m2;
+    // The pivot of channel c (every thread of its slice loaded the same value).
+    float pv = 0.f;
+    if (v_begin < v_end) {
+      float x[8];
+      int cnt;
+      gn_load8(p, base + v_begin, sl * 8, x, cnt);
+#pragma unroll
+      for (int k = 0; k < 8; ++k)
+        if (k == i) pv = x[k];
+    }
+    const float mean_d = nn > 0.f ? ss / nn : 0.f;
+    s_chan[3 * c] = nn;
+    s_chan[3 * c + 1] = pv + mean_d;
+    s_chan[3 * c + 2] = fmaxf(0.f, qq - ss * mean_d);
   }
   __syncthreads();
-  // Channels -> groups (fixed channel order).
+  // Channels -> groups (fixed channel order, Chan et al.'s pairwise update).
   const int cpg = ctot / p.groups;
   for (int g = tid; g < p.groups; g += kGnThreads) {
     Moments m{0.f, 0.f, 0.f};
