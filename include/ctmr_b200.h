@@ -135,6 +135,16 @@ CTMR_API int ctmr_pack_weight_channels_last(const float* weight, int out_channel
                      int kernel_size, int upsample, int precision, void* packed, void* packed_lo,
                      void* stream);
 
+/* Multi-head self-attention with head size 32, out = softmax(Q K^T * scale) V per head, on
+ * the tensor cores in one flash-attention pass. `qkv` is the fused projection (batch, tokens,
+ * 3 * heads * 32) of 16-bit values (dtype CTMR_DTYPE_BF16, or CTMR_DTYPE_F16 for fp16),
+ * contiguous, head h at columns h*32 (q), C + h*32 (k), 2C + h*32 (v); `out` is
+ * (batch, tokens, heads * 32) of the same type. tokens must be a multiple of 128.
+ * Replaces `_flash_attention.flash_attention` (`_flash_attention.py:320-360`) as called by
+ * `fast_fp32.self_attention_tokens` (`fast_fp32.py:352-396`). */
+CTMR_API int ctmr_attention_d32(const void* qkv, int dtype, int batch, int tokens, int heads, float scale, void* out,
+                       void* stream);
+
 /* Workspace bytes ctmr_conv3d needs for this descriptor (the prepared operand). */
 CTMR_API size_t ctmr_conv3d_workspace_size(const ctmr_conv3d_desc* desc);
 

@@ -17,6 +17,7 @@
 #include "conv3d_umma.cuh"
 #include "groupnorm.cuh"
 #include "conv3d_narrow.cuh"
+#include "attention.cuh"
 #include "conv3d_tiny.cuh"
 #include "misc.cuh"
 #include "pack.cuh"
@@ -491,6 +492,31 @@ int pack_weight_any(const float* weight, int out_channels, int in_channels, int 
   return e == cudaSuccess ? CTMR_OK : cuda_fail(e, "pack_weight launch");
 }
 }  // namespace
+
+int ctmr_attention_d32(const void* qkv, int dtype, int batch, int tokens, int heads, float scale, void* out,
+                       void* stream) {
+  if (qkv == nullptr || out == nullptr) return fail(CTMR_ERR_INVALID, "null attention pointer");
+  if (dtype != CTMR_DTYPE_BF16 && dtype != CTMR_DTYPE_F16) return fail(CTMR_ERR_INVALID, "attention dtype");
+  if (batch <= 0 || heads <= 0 || tokens <= 0) return fail(CTMR_ERR_INVALID, "attention extents");
+  if (tokens % 128 != 0) return fail(CTMR_ERR_UNSUPPORTED, "attention tokens must be a multiple of 128");
+  if (!aligned16(qkv) || !aligned16(out)) return fail(CTMR_ERR_INVALID, "attention pointers must be 16-byte aligned");
+  auto enc = tensor_map_encoder();
+  if (enc == nullptr) return fail(CTMR_ERR_CUDA, "cuTensorMapEncodeTiled is unavailable");
+  const long long c3 = 3LL * heads * 32;
+  CUtensorMap map;
+  cuuint64_t dims[3] = {static_cast<cuuint64_t>(c3), static_cast<cuuint64_t>(tokens), static_cast<cuuint64_t>(batch)};
+  cuuint64_t strides[2] = {static_cast<cuuint64_t>(c3 * 2), static_cast<cuuint64_t>(c3 * 2 * tokens)};
+  cuuint32_t box[3] = {32, 128, 1};
+  cuuint32_t estr[3] = {1, 1, 1};
+  CUresult r = enc(&map, dtype == CTMR_DTYPE_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16,
+                   3, const_cast<void*>(qkv), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                   CU_TENSOR_MAP_SWIZZLE_64B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return fail(CTMR_ERR_INVALID, "attention tensor map rejected (CUresult %d)", int(r));
+  ctmr::AttnParams p{};
+  p.batch = batch, p.tokens = tokens, p.heads = heads, p.scale = scale, p.out = out;
+  cudaError_t e = ctmr::launch_attention_d32(map, p, dtype == CTMR_DTYPE_BF16, static_cast<cudaStream_t>(stream));
+  return e == cudaSuccess ? CTMR_OK : cuda_fail(e, "attention launch");
+}
 
 int ctmr_pack_weight(const float* weight, int out_channels, int in_channels, int kernel_size, int upsample,
                      int precision, void* packed, void* packed_lo, void* stream) {

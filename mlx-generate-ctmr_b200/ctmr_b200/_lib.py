@@ -35,6 +35,7 @@ EXPORTED_SYMBOLS = (
     "ctmr_packed_weight_elems",
     "ctmr_pack_weight",
     "ctmr_pack_weight_channels_last",
+    "ctmr_attention_d32",
     "ctmr_conv3d_workspace_size",
     "ctmr_conv3d",
     "ctmr_conv3d_stages",
@@ -138,6 +139,7 @@ def _load() -> ctypes.CDLL:
         "ctmr_packed_weight_elems": (sz, [i, i, i, i]),
         "ctmr_pack_weight": (i, [vp, i, i, i, i, i, vp, vp, vp]),
         "ctmr_pack_weight_channels_last": (i, [vp, i, i, i, i, i, vp, vp, vp]),
+        "ctmr_attention_d32": (i, [vp, i, i, i, i, ctypes.c_float, vp, vp]),
         "ctmr_conv3d_workspace_size": (sz, [ctypes.POINTER(Conv3dDesc)]),
         "ctmr_conv3d": (i, [ctypes.POINTER(Conv3dDesc), vp, sz, vp]),
         "ctmr_conv3d_stages": (i, [ctypes.POINTER(Conv3dDesc), vp, sz, i, vp]),

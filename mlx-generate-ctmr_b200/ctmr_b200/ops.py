@@ -426,6 +426,25 @@ def group_norm_affine(
     return affine
 
 
+def attention_d32(qkv: torch.Tensor, heads: int, scale: float) -> torch.Tensor:
+    """``softmax(Q K^T * scale) V`` per head for head size 32 (``ctmr_attention_d32``).
+
+    ``qkv`` is the fused projection ``(B, L, 3 * heads * 32)`` in fp16 or bf16 with
+    ``L`` a multiple of 128; returns ``(B, L, heads * 32)`` in the same type. The
+    counterpart of the reference's ``flash_attention`` (``_flash_attention.py:320-360``).
+    """
+    if qkv.dim() != 3 or qkv.dtype not in (torch.float16, BF16) or not qkv.is_contiguous():
+        raise ValueError("qkv must be a contiguous (B, L, 3C) fp16/bf16 tensor")
+    b, length, c3 = (int(n) for n in qkv.shape)
+    if c3 != 3 * heads * 32 or length % 128:
+        raise ValueError(f"qkv {tuple(qkv.shape)} does not hold {heads} heads of 32 over a multiple of 128 tokens")
+    out = torch.empty((b, length, heads * 32), dtype=qkv.dtype, device=qkv.device)
+    _count(1)
+    check(LIB.ctmr_attention_d32(qkv.data_ptr(), _lib.DTYPE_BF16 if qkv.dtype == BF16 else _lib.DTYPE_F16, b, length,
+                                 heads, float(scale), out.data_ptr(), _stream()), "attention")
+    return out
+
+
 def transform(
     x: torch.Tensor,
     *,

@@ -535,3 +535,29 @@ def test_decoder_from_a_native_checkpoint(cuda, tmp_path):
         b = networks.decode_vae_ncdhw(latent, loaded, constructor=P.PRODUCTION_VAE)
     torch.cuda.synchronize()
     assert all(torch.equal(x, y) for x, y in zip(a, b, strict=True))
+
+
+@pytest.mark.parametrize("dtype", [torch.float16, torch.bfloat16])
+@pytest.mark.parametrize(("b", "length", "heads"), [(2, 2048, 8), (2, 256, 16), (1, 128, 1), (1, 384, 2)])
+def test_attention_d32_matches_sdpa(cuda, b, length, heads, dtype):
+    """The tensor-core head-size-32 attention against fp32 SDPA on the same 16-bit Q/K/V (the
+    MAISI UNet's level-2 and level-3 token counts and smaller ones): P is rounded to the operand
+    type once per key tile, so the bar is 2e-3 rel-L2 for fp16 and 1e-2 for bf16."""
+    from ctmr_b200 import ops
+
+    g = torch.Generator().manual_seed(73)
+    c = heads * 32
+    qkv = (torch.randn(b, length, 3 * c, generator=g) * 1.5).to(cuda, dtype)
+    scale = 32 ** -0.5
+    out = ops.attention_d32(qkv, heads, scale)
+    q, k, v = qkv.float().chunk(3, dim=-1)
+
+    def split(a):
+        return a.reshape(b, length, heads, 32).transpose(1, 2)
+
+    ref = torch.nn.functional.scaled_dot_product_attention(split(q), split(k), split(v), scale=scale)
+    ref = ref.transpose(1, 2).reshape(b, length, c)
+    torch.cuda.synchronize()
+    assert out.shape == ref.shape and out.dtype == dtype
+    err = ((out.float() - ref).norm() / ref.norm()).item()
+    assert err <= (2e-3 if dtype == torch.float16 else 1e-2), f"rel-L2 {err:.3e}"
