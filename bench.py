@@ -529,7 +529,7 @@ def main() -> None:
             final = sampler.sample(latent_host.to(dev, non_blocking=True).contiguous(
                 memory_format=torch.channels_last_3d), timesteps)
             dec = decode(final)
-            image = (P.output_intensities_device(dec, configuration="mr-brain").contiguous().cpu().numpy()
+            image = (P.to_host_array(P.output_intensities_device(dec, configuration="mr-brain"))
                      if pairs.member == 0 else None)
     barrier()
     e2e_s = (time.perf_counter() - t0) / args.steps

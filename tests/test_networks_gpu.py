@@ -248,3 +248,15 @@ def test_output_intensities_on_device_match_host(cuda, configuration):
     host = P.output_intensities(decoded, configuration=configuration)
     assert dev.dtype == np.int16 and dev.shape == host.shape
     np.testing.assert_array_equal(dev, host)
+
+
+def test_pinned_host_readback_is_stable(cuda):
+    """``to_host_array`` returns the device tensor's values, and an array already handed out is not
+    overwritten by later readbacks (each holds its own pinned block until dropped)."""
+    from ctmr_b200 import pipeline as P
+
+    a_dev = torch.arange(4096, dtype=torch.int16, device=cuda).reshape(1, 1, 16, 16, 16)
+    a = P.to_host_array(a_dev)
+    b = P.to_host_array(a_dev * 2)
+    assert a.dtype == np.int16 and a.shape == (1, 1, 16, 16, 16)
+    assert np.array_equal(a, a_dev.cpu().numpy()) and np.array_equal(b, (a_dev * 2).cpu().numpy())
