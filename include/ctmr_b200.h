@@ -46,7 +46,16 @@ enum {
   CTMR_ERR_CUDA = 4
 };
 
-enum { CTMR_DTYPE_F32 = 0, CTMR_DTYPE_BF16 = 1, CTMR_DTYPE_F16 = 2 /* ctmr_transform outputs only */ };
+enum {
+  CTMR_DTYPE_F32 = 0,
+  CTMR_DTYPE_BF16 = 1,
+  CTMR_DTYPE_F16 = 2,    /* ctmr_transform outputs only */
+  /* Conv input `x` only: one int16 label id per voxel (cstride elements apart), read as 8
+   * channels, channel k = bit k of the id (0.0 or 1.0): the ControlNet condition of
+   * `condition.binarize_labels_ncdhw` (`condition.py:20-43`) formed in the operand pass.
+   * channels must be 8; no x2, resampling or in-call GroupNorm. */
+  CTMR_DTYPE_LABEL8 = 3
+};
 
 /* CTMR_PRECISION_FP32: fp32 operands carried as fp16 hi/lo pairs, three
  *   tensor-core products per step, fp32 accumulation (~2^-22 relative product

@@ -161,9 +161,14 @@ int sm_count() {
 bool g_v2_unavailable = false;
 constexpr long long kStatsMaxEntries = 512;  // batch x output channels with output statistics
 
-int check_view(const ctmr_tensor& t, const char* name, bool required) {
+int check_view(const ctmr_tensor& t, const char* name, bool required, bool labels_ok = false) {
   if (t.data == nullptr) {
     if (required) return fail(CTMR_ERR_INVALID, "%s is missing", name);
+    return CTMR_OK;
+  }
+  if (t.dtype == CTMR_DTYPE_LABEL8) {
+    if (!labels_ok) return fail(CTMR_ERR_INVALID, "%s cannot be a label volume", name);
+    if (t.channels != 8 || t.cstride < 1) return fail(CTMR_ERR_INVALID, "%s label volume must be 8 channels", name);
     return CTMR_OK;
   }
   if (t.dtype != CTMR_DTYPE_F32 && t.dtype != CTMR_DTYPE_BF16) return fail(CTMR_ERR_INVALID, "%s dtype", name);
@@ -175,7 +180,7 @@ ctmr::PrepSource as_source(const ctmr_tensor& t) {
   ctmr::PrepSource s{};
   if (t.data != nullptr) {
     s.ptr = t.data;
-    s.bf16 = t.dtype == CTMR_DTYPE_BF16;
+    s.bf16 = t.dtype == CTMR_DTYPE_BF16 ? 1 : (t.dtype == CTMR_DTYPE_LABEL8 ? 2 : 0);
     s.channels = t.channels;
     s.cstride = t.cstride;
   }
@@ -210,10 +215,13 @@ int plan_conv(const ctmr_conv3d_desc* d, ConvPlan* p) {
   if (d == nullptr) return fail(CTMR_ERR_INVALID, "null descriptor");
   if (d->batch <= 0 || d->depth <= 0 || d->height <= 0 || d->width <= 0)
     return fail(CTMR_ERR_INVALID, "grid must be positive");
-  int st = check_view(d->x, "x", true);
+  int st = check_view(d->x, "x", true, true);
   if (st) return st;
   if ((st = check_view(d->x2, "x2", false))) return st;
   if ((st = check_view(d->residual, "residual", false))) return st;
+  if (d->x.dtype == CTMR_DTYPE_LABEL8 &&
+      (d->x2.data != nullptr || d->trilinear || d->avgpool || d->upsample || d->stride != 1 || d->gn_groups > 0))
+    return fail(CTMR_ERR_UNSUPPORTED, "a label volume input takes no x2, resampling, stride or in-call GroupNorm");
   if (d->precision != CTMR_PRECISION_FP32 && d->precision != CTMR_PRECISION_BF16 &&
       d->precision != CTMR_PRECISION_FP16)
     return fail(CTMR_ERR_INVALID, "precision");

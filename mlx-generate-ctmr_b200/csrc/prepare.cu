@@ -27,8 +27,15 @@ __device__ __forceinline__ float load_ch(const void* base, int bf16, long long i
   return __ldg(static_cast<const float*>(base) + idx);
 }
 
-// 8 consecutive channels of one source voxel (vectorised when aligned).
+// 8 consecutive channels of one source voxel (vectorised when aligned). A label
+// source holds one int16 id per voxel; its channel k is bit k of the id.
 __device__ __forceinline__ void load8(const PrepSource& s, long long vox, int c, int cnt, float (&v)[8]) {
+  if (s.bf16 == 2) {
+    const int id = __ldg(static_cast<const int16_t*>(s.ptr) + vox * s.cstride);
+#pragma unroll
+    for (int i = 0; i < 8; ++i) v[i] = i < cnt ? static_cast<float>((id >> (c + i)) & 1) : 0.f;
+    return;
+  }
   const long long idx = vox * s.cstride + c;
   if (cnt == 8) {
     if (s.bf16) {

@@ -10,7 +10,7 @@ enum PrepOut : int { kPrepOutBF16 = 0, kPrepOutSplitF16 = 1, kPrepOutF32 = 2, kP
 
 struct PrepSource {
   const void* ptr;       // NDHWC rows, `cstride` elements apart
-  int bf16;              // 1: bf16 elements, 0: fp32
+  int bf16;              // 1: bf16 elements, 0: fp32, 2: int16 label ids read as 8 bit-plane channels
   int channels;          // channels taken from this source (0: unused)
   long long cstride;
 };

@@ -21,6 +21,7 @@ CTMR_ERR_CUDA = 4
 DTYPE_F32 = 0
 DTYPE_BF16 = 1
 DTYPE_F16 = 2  # ctmr_transform outputs only
+DTYPE_LABEL8 = 3  # conv input only: int16 label ids read as 8 bit-plane channels
 PRECISION_FP32 = 0
 PRECISION_BF16 = 1
 PRECISION_FP16 = 2

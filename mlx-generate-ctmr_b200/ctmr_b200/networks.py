@@ -216,8 +216,12 @@ def denoise_unet_ncdhw(x, timesteps, class_labels, spacing, weights: Weights, *,
 def _cond_embed(cond, weights: Weights, channels: Sequence[int]) -> torch.Tensor:
     """``controlnet._cond_embed`` (``controlnet.py:197-255``): each SiLU after a conv runs in the next conv's prologue."""
     p = "controlnet_cond_embedding"
-    h = A.conv3d_ncdhw(ops.to_ndhwc(cond), required_weight(weights, f"{p}.conv_in.conv.weight"),
-                       required_weight(weights, f"{p}.conv_in.conv.bias"), padding=1)
+    w_in, b_in = required_weight(weights, f"{p}.conv_in.conv.weight"), required_weight(weights, f"{p}.conv_in.conv.bias")
+    if isinstance(cond, ops.LabelBits):
+        # The bit planes are formed in conv_in's operand pass from the int16 labels.
+        h = ops.conv3d(cond, A._pack(w_in), b_in, out_dtype=A.activation_dtype())
+    else:
+        h = A.conv3d_ncdhw(ops.to_ndhwc(cond), w_in, b_in, padding=1)
     block = 0
     dtype = A.activation_dtype()
     for _ in range(len(channels) - 1):

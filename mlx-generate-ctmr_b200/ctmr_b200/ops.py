@@ -99,10 +99,32 @@ def rows_stride(x: torch.Tensor) -> int:
     return int(cs)
 
 
-def view(x: torch.Tensor | None) -> _lib.Tensor:
-    """``ctmr_tensor`` for an NDHWC-stored tensor (or an absent one)."""
+class LabelBits:
+    """An int16 label volume ``(N, 1, D, H, W)`` that ``conv3d`` reads as its 8 bit-plane
+    channels (channel k = bit k of the id, 0.0 or 1.0), formed in the conv's operand pass
+    (``CTMR_DTYPE_LABEL8``) instead of as a materialised fp32 condition: the ControlNet
+    condition of ``condition.binarize_labels_ncdhw`` (``condition.py:20-43``)."""
+
+    def __init__(self, label: torch.Tensor) -> None:
+        if label.dim() != 5 or int(label.shape[1]) != 1 or not label.is_cuda:
+            raise ValueError(f"label must be a CUDA (N, 1, D, H, W) tensor; got {tuple(label.shape)}")
+        if label.dtype not in (torch.int16, torch.int32, torch.int64, torch.uint8):
+            raise ValueError(f"label must be integer; got {label.dtype}")
+        self.label = label.to(torch.int16).contiguous()
+        self.shape = torch.Size((int(label.shape[0]), 8, *(int(s) for s in label.shape[2:])))
+        self.device = label.device
+        self.dtype = torch.int16
+
+    def dim(self) -> int:
+        return 5
+
+
+def view(x) -> _lib.Tensor:
+    """``ctmr_tensor`` for an NDHWC-stored tensor, a ``LabelBits`` volume, or an absent one."""
     if x is None:
         return _lib.Tensor(None, 0, 0, 0)
+    if isinstance(x, LabelBits):
+        return _lib.Tensor(x.label.data_ptr(), _lib.DTYPE_LABEL8, 8, 1)
     if not x.is_cuda:
         raise ValueError("ctmr_b200 tensors must live on a CUDA device")
     return _lib.Tensor(x.data_ptr(), _dtype_code(x.dtype), int(x.shape[1]), rows_stride(x))

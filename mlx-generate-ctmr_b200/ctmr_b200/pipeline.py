@@ -558,10 +558,9 @@ def sample_ct_from_mask_ncdhw(label, spacing_mm: Sequence[float], *, unet_weight
     elif tuple(latent.shape) != shape:
         raise ValueError(f"latent shape {tuple(latent.shape)} != {shape}")
     started = time.perf_counter()
-    cond = binarize_labels_ncdhw(label_dev)
-    embedding = networks.encode_controlnet_condition_ncdhw(cond, controlnet_weights,
+    # The 8 bit planes of the labels are formed inside the first embedding conv's operand pass.
+    embedding = networks.encode_controlnet_condition_ncdhw(ops.LabelBits(label_dev), controlnet_weights,
                                                             constructor=controlnet_constructor)
-    del cond
     timesteps, _ = set_timesteps_rflow(num_inference_steps=num_inference_steps,
                                        input_img_size_numel=math.prod(shape[2:]))
     step = ControlNetUNetStep(unet_weights, controlnet_weights, unet_constructor, controlnet_constructor, shape,

@@ -92,3 +92,27 @@ def test_ct_from_mask_sampler(cuda, precision, budget):
     assert torch.equal(hu, N.to_hu(res.decoded.float().cpu(), lab_t))
     if precision == "fp32":
         assert float((hu - ref_hu).abs().max()) <= 2000.0 * 1e-4 * max(1.0, float(ref_dec.abs().max()))
+
+
+@pytest.mark.parametrize("precision", ["fp32", "fp16", "bf16"])
+def test_condition_bit_planes_formed_in_the_conv(cuda, precision):
+    """The ControlNet condition embedding read straight from the int16 labels (the 8 bit planes
+    formed in conv_in's operand pass, ``ops.LabelBits``) equals, bitwise, the embedding of the
+    materialised fp32 bit-plane condition; a label input refuses resampling and a second source."""
+    from ctmr_b200 import fast_b200, networks, ops
+    from ctmr_b200 import pipeline as P
+    from ctmr_b200 import weights as W
+
+    ctor = P.PRODUCTION_CONTROLNET
+    wd = _on(W.random_weights(W.controlnet_shapes(ctor), seed=5, device="cpu"), cuda)
+    lab = torch.from_numpy(_label((64, 64, 32), seed=3)).to(cuda)
+    with fast_b200.arithmetic_precision(precision):
+        fused = networks.encode_controlnet_condition_ncdhw(ops.LabelBits(lab), wd, constructor=ctor)
+        plain = networks.encode_controlnet_condition_ncdhw(P.binarize_labels_ncdhw(lab), wd, constructor=ctor)
+        torch.cuda.synchronize()
+        assert torch.equal(fused, plain)
+        packed = fast_b200._pack(wd["controlnet_cond_embedding.conv_in.conv.weight"])
+        with pytest.raises(ValueError):
+            ops.conv3d(ops.LabelBits(lab), packed, None, stride=2)
+        with pytest.raises(ValueError):
+            ops.conv3d(ops.LabelBits(lab), packed, None, trilinear=True)
