@@ -734,10 +734,12 @@ int ctmr_conv3d_stages(const ctmr_conv3d_desc* d, void* workspace, size_t worksp
       std::memset(&maps, 0, sizeof(maps));
       const long long rs = a_cstride * 2;
       const long long W = p.in_w, H = p.in_h, D = p.in_d;
-      // W before H: an 8-row swizzle atom holds 8 consecutive w of one h.
+      // H before W: the 16 h of one w are consecutive tile rows, so the kernel's shift by one h
+      // is a shift by one TMEM lane and one by one w (the kw taps) 16 rows. Boxes of 10 w hold
+      // the windows of all three kw taps.
       if (rs % 16 == 0 &&
-          encode_act(&maps.a[0], a_hi, p.bf16, p.cpad, W, H, D, d->batch, rs, W * rs, H * W * rs, D * H * W * rs,
-                     kh.kc, 8, 16, md) == CTMR_OK &&
+          encode_act(&maps.a[0], a_hi, p.bf16, p.cpad, H, W, D, d->batch, W * rs, rs, H * W * rs, D * H * W * rs,
+                     kh.kc, 16, 10, md) == CTMR_OK &&
           encode_weight_kh(&maps.b, w_hi, p.bf16, p.cpad, p.opad, kh.kc) == CTMR_OK) {
         cudaError_t e = ctmr::launch_conv3d_khcat(maps, g, kh.kc, kh.mt, sm_count(), kh.smem, stream);
         return e == cudaSuccess ? CTMR_OK : cuda_fail(e, "conv3d kh-concatenated launch");

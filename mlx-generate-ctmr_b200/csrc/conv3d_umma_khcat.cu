@@ -9,17 +9,21 @@
 //
 //   y[h] = P0[h - 1] + P1[h] + P2[h + 1],   Pk[r] = sum_{kd, kw, c} x[r] w[kd, kh = k, kw, c]
 //
-// The M tile is 16 h x 8 w voxels of one depth with each 8-row swizzle atom
-// holding 8 consecutive w of one h, so a shift by one h is a shift by one atom
-// (8 TMEM lanes). A tile covers input rows h0 - 1 .. h0 + 14 and produces the
-// 14 output rows h0 .. h0 + 13 (the first and last atom only feed neighbours).
-// Stages walk (kd, kw) x channel blocks: one TMA box of the activations at the
-// (kd, kw) offset and one box of the three kh taps' weights, shared by MT = 2
-// depth tiles. The accumulator (2 x 3 x C_out fp32 columns) has one TMEM buffer;
-// the eight epilogue warps (two per TMEM lane quarter, one per column half)
-// read it out, combine the shifts (lane shuffles inside a warp, shared memory
-// across quarters), release the accumulator, then add bias and residual and
-// store while the next tile's MMAs run.
+// The M tile is 16 h x 8 w voxels of one depth with h fastest (the TMA view is
+// (C, H, W, D, B)): row r = 16 w + h, so the 16 h of one w sit in one half of a
+// warp's 32 TMEM lanes and a shift by one h is a shift by one lane. A tile covers
+// input rows h0 - 1 .. h0 + 14 and produces the 14 output rows h0 .. h0 + 13
+// (rows h = 0 and 15 only feed their neighbours).
+// Per (kd, channel block) one TMA box of the activations, 16 h x 10 w x MT depths,
+// serves the three kw taps: the window of tap kw starts 16 rows (whole 8-row
+// swizzle atoms) further on. Each (kd, kw, channel block) has its own box of the
+// three kh taps' weights, shared by the MT = 2 depth tiles; activation and weight
+// boxes stream through two rings (2 or 4 and up to 12 slots). The accumulator
+// (2 x 3 x C_out fp32 columns) has one TMEM buffer; the eight epilogue warps (two
+// per TMEM lane quarter, one per column half) read it out, combine the shifts
+// with 16-wide lane shuffles and release it, then add bias and residual and
+// store while the next tile's MMAs run (with 64 output channels through an
+// 8-lane transpose, so that each warp store writes whole 128-byte lines).
 #include <cuda_bf16.h>
 #include <cuda_fp16.h>
 
@@ -33,21 +37,25 @@ namespace {
 
 constexpr int kKhThreads = 320;  // warp 0 TMA, warp 1 MMA + TMEM, warps 2..9 epilogue
 constexpr int kKhRows = 14;      // output rows along h per tile
-// Quarter-edge exchange: per (column half, buffer, TMEM quarter) the P0 rows of lanes 24..31 and
-// the P2 rows of lanes 0..7, 16 columns each at a 20-float lane pitch (conflict-free float4s).
-constexpr uint32_t kKhLanePitch = 20;
-constexpr uint32_t kKhEdgeQuarter = 2u * 8u * kKhLanePitch;                // floats: [P0|P2][lane][col]
-constexpr uint32_t kKhEdgeFloats = 2u * 2u * 4u * kKhEdgeQuarter;           // [half][buf][quarter]
+constexpr int kKhBoxW = 10;      // w per activation box: 8 output columns and the kw halo
+constexpr int kKhMaxBSlots = 12;  // weight ring slots at most
 
 __host__ __device__ constexpr uint32_t ru_kh(uint32_t v, uint32_t a) { return (v + a - 1) / a * a; }
 
+// Shared-memory ring slots: activations (MT depth slabs of 16 h x 10 w rows of kc channels) and
+// weights (3 x C_out rows of kc channels). All sizes are multiples of 1024 bytes, the 128-byte
+// swizzle period, so every MMA operand window starts on a swizzle-atom boundary.
+// Small activation boxes (<= 24 KB: 32 or 16 channels per block) serve only a few short MMA
+// stages each, so their ring is deeper (4 slots) to keep enough loads in flight.
 struct KhLayout {
-  uint32_t a_m_bytes, a_bytes, b_bytes, stage_bytes;
+  uint32_t a_m_bytes, a_bytes, kw_bytes, b_bytes;
+  int a_slots;
   __host__ __device__ KhLayout(int kc, int bn, int mt) {
-    a_m_bytes = 128u * static_cast<uint32_t>(kc) * 2u;
+    kw_bytes = 16u * static_cast<uint32_t>(kc) * 2u;
+    a_m_bytes = static_cast<uint32_t>(kKhBoxW) * kw_bytes;
     a_bytes = static_cast<uint32_t>(mt) * a_m_bytes;
     b_bytes = ru_kh(3u * static_cast<uint32_t>(bn) * static_cast<uint32_t>(kc) * 2u, 1024);
-    stage_bytes = a_bytes + b_bytes;
+    a_slots = a_bytes <= 24u * 1024u ? 4 : 2;
   }
 };
 
@@ -84,21 +92,85 @@ __device__ __forceinline__ bool barrier_all(int id, int threads, bool v) {
   return r != 0;
 }
 
-__device__ __forceinline__ void sts128(uint32_t addr, uint32_t a, uint32_t b, uint32_t c, uint32_t d) {
-  asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(addr), "r"(a), "r"(b), "r"(c), "r"(d) : "memory");
+// Transposes N x N float4s across each group of N lanes (gi = lane % N, N = 4 or 8): afterwards
+// q[k] holds what lane k of the group had in q[gi]. log2(N) butterfly stages, each swapping the
+// off-diagonal halves with the partner lane (gi ^ s).
+template <int N>
+__device__ __forceinline__ void transpose_f4(float4 (&q)[N], int gi) {
+#pragma unroll
+  for (int s = N / 2; s >= 1; s >>= 1) {
+    const bool upper = (gi & s) != 0;
+#pragma unroll
+    for (int k = 0; k < N; ++k) {
+      if (k & s) continue;
+      const float4 send = upper ? q[k] : q[k | s];
+      float4 recv;
+      recv.x = __shfl_xor_sync(0xffffffffu, send.x, s);
+      recv.y = __shfl_xor_sync(0xffffffffu, send.y, s);
+      recv.z = __shfl_xor_sync(0xffffffffu, send.z, s);
+      recv.w = __shfl_xor_sync(0xffffffffu, send.w, s);
+      if (upper) q[k] = recv;
+      else q[k | s] = recv;
+    }
+  }
 }
 
-__device__ __forceinline__ float4 lds128(uint32_t addr) {
-  float4 v;
-  asm volatile("ld.shared.v4.f32 {%0, %1, %2, %3}, [%4];"
-               : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w)
-               : "r"(addr)
-               : "memory");
-  return v;
+// Reads the residual of 4 consecutive output channels n .. n + 3 (fp32 or bf16) as fp32;
+// channels at or beyond C_out read as zero.
+__device__ __forceinline__ float4 kh_load4(const ConvGeom& g, long long res_off, int n) {
+  const int cnt = min(4, g.cout - n);
+  float x[4] = {0.f, 0.f, 0.f, 0.f};
+  if (g.res_bf16) {
+    const uint16_t* r = static_cast<const uint16_t*>(g.res) + res_off;
+    if (cnt == 4 && (reinterpret_cast<uintptr_t>(r) & 7) == 0) {
+      const uint2 q = __ldg(reinterpret_cast<const uint2*>(r));
+      x[0] = bf16_to_f32(static_cast<uint16_t>(q.x & 0xFFFFu));
+      x[1] = bf16_to_f32(static_cast<uint16_t>(q.x >> 16));
+      x[2] = bf16_to_f32(static_cast<uint16_t>(q.y & 0xFFFFu));
+      x[3] = bf16_to_f32(static_cast<uint16_t>(q.y >> 16));
+    } else {
+#pragma unroll
+      for (int e = 0; e < 4; ++e)
+        if (e < cnt) x[e] = bf16_to_f32(r[e]);
+    }
+  } else {
+    const float* r = static_cast<const float*>(g.res) + res_off;
+    if (cnt == 4 && (reinterpret_cast<uintptr_t>(r) & 15) == 0) return __ldg(reinterpret_cast<const float4*>(r));
+#pragma unroll
+    for (int e = 0; e < 4; ++e)
+      if (e < cnt) x[e] = __ldg(r + e);
+  }
+  return make_float4(x[0], x[1], x[2], x[3]);
 }
 
-__device__ __forceinline__ void named_barrier(int id, int threads) {
-  asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(threads) : "memory");
+// Stores 4 consecutive output channels n .. n + 3 in the output type; channels at or beyond
+// C_out are skipped.
+__device__ __forceinline__ void kh_store4(const ConvGeom& g, float4 v, int n, long long out_off) {
+  const int cnt = min(4, g.cout - n);
+  const float x[4] = {v.x, v.y, v.z, v.w};
+  if (g.out_bf16) {
+    uint16_t* o = static_cast<uint16_t*>(g.out) + out_off;
+    if (cnt == 4 && (reinterpret_cast<uintptr_t>(o) & 7) == 0) {
+      *reinterpret_cast<uint2*>(o) = make_uint2(pack_bf16x2(x[0], x[1]), pack_bf16x2(x[2], x[3]));
+    } else {
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        if (e < cnt) {
+          __nv_bfloat16 h = __float2bfloat16_rn(x[e]);
+          o[e] = *reinterpret_cast<uint16_t*>(&h);
+        }
+      }
+    }
+  } else {
+    float* o = static_cast<float*>(g.out) + out_off;
+    if (cnt == 4 && (reinterpret_cast<uintptr_t>(o) & 15) == 0) {
+      *reinterpret_cast<float4*>(o) = v;
+    } else {
+#pragma unroll
+      for (int e = 0; e < 4; ++e)
+        if (e < cnt) o[e] = x[e];
+    }
+  }
 }
 
 // Accumulator buffers in the 512 TMEM columns: two (the epilogue of tile i overlaps the MMAs of
@@ -114,9 +186,12 @@ __global__ void __launch_bounds__(kKhThreads, 1)
   uint8_t* smem = reinterpret_cast<uint8_t*>(ru_kh(smem_u32(smem_raw), 1024) - smem_u32(smem_raw) +
                                              reinterpret_cast<uintptr_t>(smem_raw));
   const KhLayout L(KC, g.bn, MT);
-  const int S = g.stages;
-  uint8_t* edges = smem + static_cast<size_t>(S) * L.stage_bytes;
-  uint64_t* full = reinterpret_cast<uint64_t*>(edges + kKhEdgeFloats * sizeof(float));
+  const int S = g.stages;  // weight ring slots
+  const int SA = L.a_slots;  // activation ring slots
+  uint8_t* b_ring = smem + static_cast<size_t>(SA) * L.a_bytes;
+  uint64_t* a_full = reinterpret_cast<uint64_t*>(b_ring + static_cast<size_t>(S) * L.b_bytes);
+  uint64_t* a_empty = a_full + SA;
+  uint64_t* full = a_empty + SA;  // weight ring
   uint64_t* empty = full + S;
   uint64_t* tmem_full = empty + S;      // [2]: accumulator buffer complete
   uint64_t* tmem_empty = tmem_full + 2;  // [2]: buffer (two buffers) or depth (one buffer) read out
@@ -125,12 +200,16 @@ __global__ void __launch_bounds__(kKhThreads, 1)
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
-  const int stages_per_tile = 9 * g.kblocks;
+  const int groups_per_tile = 3 * g.kblocks;  // (kd, channel block) pairs, three kw taps each
   const int bn = g.bn;
   const uint32_t n3 = 3u * static_cast<uint32_t>(bn);
   const int nbuf = kh_buffers(MT, bn);
 
   if (threadIdx.x == 0) {
+    for (int s = 0; s < SA; ++s) {
+      mbar_init(&a_full[s], 1);
+      mbar_init(&a_empty[s], 1);
+    }
     for (int s = 0; s < S; ++s) {
       mbar_init(&full[s], 1);
       mbar_init(&empty[s], 1);
@@ -168,95 +247,119 @@ __global__ void __launch_bounds__(kKhThreads, 1)
     // ------------------------------------------------------------ TMA producer
     tma_prefetch_desc(&maps.a[0]);
     tma_prefetch_desc(&maps.b);
-    int it = 0;
-    int issued = 0;
-    const uint32_t stage_tx = L.a_bytes + n3 * KC * 2u;
-    for (int t = blockIdx.x; t < g.total_tiles && !*abort_flag; t += gridDim.x) {
+    int ia = 0;  // activation boxes issued
+    int ib = 0;  // weight boxes issued
+    const uint32_t b_tx = n3 * KC * 2u;
+    bool stop = false;
+    for (int t = blockIdx.x; t < g.total_tiles && !stop && !*abort_flag; t += gridDim.x) {
       int w0, h0, d0, b;
       decode(t, w0, h0, d0, b);
-      for (int st = 0; st < stages_per_tile; ++st, ++it) {
-        const int s = it % S;
-        const uint32_t round = static_cast<uint32_t>(it / S);
-        if (it >= S && !mbar_wait_bounded(&empty[s], (round - 1) & 1u, kErrWaitEmpty)) {
-          *abort_flag = 1;
+      for (int gi = 0; gi < groups_per_tile && !stop; ++gi) {
+        const int kd = gi / g.kblocks;
+        const int c = (gi - kd * g.kblocks) * KC;
+        const int sa = ia % SA;
+        if (ia >= SA &&
+            !mbar_wait_bounded(&a_empty[sa], static_cast<uint32_t>(ia / SA - 1) & 1u, kErrWaitEmpty)) {
+          stop = true;
           break;
         }
-        const int kdw = st / g.kblocks;
-        const int c = (st - kdw * g.kblocks) * KC;
-        const int kd = kdw / 3, kw = kdw - 3 * (kdw / 3);
-        uint8_t* st_base = smem + static_cast<size_t>(s) * L.stage_bytes;
-        mbar_arrive_expect_tx(&full[s], stage_tx);
-        // Activations (C, W, H, D, B): 8 w at the kw offset, 16 h from h0 - 1, MT depths at the kd offset.
-        tma_load_5d(st_base, &maps.a[0], &full[s], c, w0 + kw - 1, h0 - 1, d0 + kd - 1, b);
-        // Weights (c, o, kw, kh, kd): the three kh taps of (kd, kw) as N = 3 x C_out rows.
-        tma_load_5d(st_base + L.a_bytes, &maps.b, &full[s], c, 0, kw, 0, kd);
-        ++issued;
+        mbar_arrive_expect_tx(&a_full[sa], L.a_bytes);
+        // Activations (C, H, W, D, B): 16 h from h0 - 1, 10 w from w0 - 1 (the windows of all
+        // three kw taps), MT depths at the kd offset.
+        tma_load_5d(smem + static_cast<size_t>(sa) * L.a_bytes, &maps.a[0], &a_full[sa], c, h0 - 1, w0 - 1,
+                    d0 + kd - 1, b);
+        ++ia;
+        for (int kw = 0; kw < 3; ++kw) {
+          const int s = ib % S;
+          if (ib >= S && !mbar_wait_bounded(&empty[s], static_cast<uint32_t>(ib / S - 1) & 1u, kErrWaitEmpty)) {
+            stop = true;
+            break;
+          }
+          mbar_arrive_expect_tx(&full[s], b_tx);
+          // Weights (c, o, kw, kh, kd): the three kh taps of (kd, kw) as N = 3 x C_out rows.
+          tma_load_5d(b_ring + static_cast<size_t>(s) * L.b_bytes, &maps.b, &full[s], c, 0, kw, 0, kd);
+          ++ib;
+        }
       }
     }
-    for (int k = max(0, issued - S); k < issued; ++k) {
+    if (stop) *abort_flag = 1;
+    // Every box in flight lands before the CTA exits.
+    for (int k = max(0, ia - SA); k < ia; ++k) {
+      if (!mbar_wait_bounded(&a_full[k % SA], static_cast<uint32_t>(k / SA) & 1u, kErrWaitDrain)) break;
+    }
+    for (int k = max(0, ib - S); k < ib; ++k) {
       if (!mbar_wait_bounded(&full[k % S], static_cast<uint32_t>(k / S) & 1u, kErrWaitDrain)) break;
     }
   } else if (warp == 1 && lane == 0) {
     // ------------------------------------------------------------ MMA issuer
     const uint32_t idesc = idesc_f16(g.operand_bf16 != 0, 128, n3);
-    int it = 0;
+    int ia = 0;
+    int ib = 0;
     int lt = 0;
-    for (int t = blockIdx.x; t < g.total_tiles && !*abort_flag; t += gridDim.x, ++lt) {
+    bool stop = false;
+    for (int t = blockIdx.x; t < g.total_tiles && !stop && !*abort_flag; t += gridDim.x, ++lt) {
       const int buf = nbuf == 2 ? (lt & 1) : 0;
       const uint32_t acc0 = tmem + static_cast<uint32_t>(buf * MT) * n3;
-      for (int st = 0; st < stages_per_tile; ++st, ++it) {
-        const int s = it % S;
-        if (!mbar_wait_bounded(&full[s], static_cast<uint32_t>(it / S) & 1u, kErrWaitFull)) {
-          *abort_flag = 1;
+      for (int gi = 0; gi < groups_per_tile && !stop; ++gi) {
+        const int sa = ia % SA;
+        if (!mbar_wait_bounded(&a_full[sa], static_cast<uint32_t>(ia / SA) & 1u, kErrWaitFull)) {
+          stop = true;
           break;
         }
-        tc_fence_after();
-        const uint32_t a_base = smem_u32(smem + static_cast<size_t>(s) * L.stage_bytes);
-        const uint32_t b_base = a_base + L.a_bytes;
-        bool stop = false;
+        ++ia;
+        const uint32_t a_base = smem_u32(smem + static_cast<size_t>(sa) * L.a_bytes);
+        for (int kw = 0; kw < 3 && !stop; ++kw) {
+          const int s = ib % S;
+          if (!mbar_wait_bounded(&full[s], static_cast<uint32_t>(ib / S) & 1u, kErrWaitFull)) {
+            stop = true;
+            break;
+          }
+          ++ib;
+          tc_fence_after();
+          const uint32_t b_base = smem_u32(b_ring + static_cast<size_t>(s) * L.b_bytes);
+          const bool first = gi == 0 && kw == 0;
 #pragma unroll
-        for (int m = 0; m < MT; ++m) {
-          // The columns about to be overwritten must have been read out: with two buffers the
-          // tile before last's buffer, with one the previous tile's depth m.
-          const bool wait_rel = st == 0 && (nbuf == 2 ? (m == 0 && lt >= 2) : lt >= 1);
-          if (wait_rel) {
-            const int rel = nbuf == 2 ? buf : m;
-            const uint32_t par = static_cast<uint32_t>(nbuf == 2 ? (lt >> 1) - 1 : lt - 1) & 1u;
-            if (!mbar_wait_bounded(&tmem_empty[rel], par, kErrWaitAcc)) {
-              stop = true;
-              break;
+          for (int m = 0; m < MT; ++m) {
+            // The columns about to be overwritten must have been read out: with two buffers the
+            // tile before last's buffer, with one the previous tile's depth m.
+            const bool wait_rel = first && (nbuf == 2 ? (m == 0 && lt >= 2) : lt >= 1);
+            if (wait_rel) {
+              const int rel = nbuf == 2 ? buf : m;
+              const uint32_t par = static_cast<uint32_t>(nbuf == 2 ? (lt >> 1) - 1 : lt - 1) & 1u;
+              if (!mbar_wait_bounded(&tmem_empty[rel], par, kErrWaitAcc)) {
+                stop = true;
+                break;
+              }
+              tc_fence_after();
             }
-            tc_fence_after();
-          }
+            const uint32_t a_win = a_base + static_cast<uint32_t>(m) * L.a_m_bytes + static_cast<uint32_t>(kw) * L.kw_bytes;
 #pragma unroll
-          for (int k = 0; k < kSteps; ++k) {
-            umma_f16(acc0 + static_cast<uint32_t>(m) * n3,
-                     smem_desc_kmajor(a_base + static_cast<uint32_t>(m) * L.a_m_bytes + k * 32u, kRowBytes),
-                     smem_desc_kmajor(b_base + k * 32u, kRowBytes), idesc, (st == 0 && k == 0) ? 0u : 1u);
+            for (int k = 0; k < kSteps; ++k) {
+              umma_f16(acc0 + static_cast<uint32_t>(m) * n3, smem_desc_kmajor(a_win + k * 32u, kRowBytes),
+                       smem_desc_kmajor(b_base + k * 32u, kRowBytes), idesc, (first && k == 0) ? 0u : 1u);
+            }
           }
+          umma_commit(&empty[s]);
         }
-        umma_commit(&empty[s]);
-        if (stop) {
-          *abort_flag = 1;
-          break;
-        }
+        umma_commit(&a_empty[sa]);
       }
+      if (stop) break;
       umma_commit(&tmem_full[buf]);
     }
+    if (stop) *abort_flag = 1;
   } else if (warp >= 2) {
     // ------------------------------------------------------------ epilogue
     const int ew = warp - 2;
     const int quarter = warp & 3;  // TMEM lanes a warp may read: 32 x (warp id mod 4)
-    const int half = ew >> 2;      // 16-column chunks j with j % 2 == half
-    const int row = quarter * 32 + lane;
-    const int atom = row >> 3, iw = row & 7;
+    const int half = ew >> 2;      // which of the two 16-column chunk pairs this warp reads
+    // Lane l of quarter q holds tile row h = l % 16 (0 and 15 are halo) of w = 2 q + l / 16.
     const uint32_t lane_addr = tmem + (static_cast<uint32_t>(quarter * 32) << 16);
     const int nchunks = bn >> 4;
-    const uint32_t edge_base = smem_u32(edges);
+    // 64 output channels: half h reads chunks 2h, 2h + 1 (32 contiguous channels per lane), stored
+    // through an 8-lane transpose. Fewer: chunks h, h + 2 (both halves busy), stored per voxel.
+    const bool wide = nchunks == 4;
     int lt = 0;
-    int eit = 0;  // edge exchanges so far (uniform over the four warps of a half): picks the buffer
-    // The eight epilogue warps take every decision together (the wait outcome is
-    // voted on), so no warp leaves while another waits at a named barrier.
+    // The eight epilogue warps take every decision together (the wait outcome is voted on).
     for (int t = blockIdx.x; t < g.total_tiles; t += gridDim.x, ++lt) {
       int w0, h0, d0, b;
       decode(t, w0, h0, d0, b);
@@ -273,8 +376,12 @@ __global__ void __launch_bounds__(kKhThreads, 1)
       for (int m = 0; m < MT; ++m) {
 #pragma unroll
         for (int jj = 0; jj < 2; ++jj) {
-          const int j = 2 * jj + half;
-          if (j >= nchunks) continue;  // uniform over the four warps of this half
+          const int j = wide ? 2 * half + jj : 2 * jj + half;
+          if (j >= nchunks) {  // uniform over the four warps of this half
+#pragma unroll
+            for (int i = 0; i < 16; ++i) out[m][jj][i] = 0.f;
+            continue;
+          }
           const uint32_t col = static_cast<uint32_t>(buf * MT + m) * n3 + static_cast<uint32_t>(j * 16);
           uint32_t r0[16], r1[16], r2[16];
           tmem_ld16_issue(lane_addr + col, r0);
@@ -284,42 +391,13 @@ __global__ void __launch_bounds__(kKhThreads, 1)
           reg_fence16(r0);
           reg_fence16(r1);
           reg_fence16(r2);
-          // Quarter edges: P0 of lanes 24..31 feeds the next quarter's lanes 0..7,
-          // P2 of lanes 0..7 the previous quarter's lanes 24..31.
-          const int ebuf = eit++ & 1;
-          const uint32_t eb = edge_base + static_cast<uint32_t>((half * 2 + ebuf) * 4) * kKhEdgeQuarter * 4u;
-          const uint32_t own = eb + static_cast<uint32_t>(quarter) * kKhEdgeQuarter * 4u +
-                               static_cast<uint32_t>(lane & 7) * kKhLanePitch * 4u;
-          if (lane >= 24) {
+          // y[h] = P0[h - 1] + P1[h] + P2[h + 1]: neighbouring h are neighbouring lanes of the
+          // same 16-lane group (the group's end lanes are halo rows, whose sums are not stored).
 #pragma unroll
-            for (int i = 0; i < 16; i += 4) sts128(own + i * 4u, r0[i], r0[i + 1], r0[i + 2], r0[i + 3]);
-          }
-          if (lane < 8) {
-#pragma unroll
-            for (int i = 0; i < 16; i += 4)
-              sts128(own + 8u * kKhLanePitch * 4u + i * 4u, r2[i], r2[i + 1], r2[i + 2], r2[i + 3]);
-          }
-          named_barrier(1 + half, 128);
-          // Every lane reads both neighbours' edge rows (the same eight addresses per
-          // quarter: broadcasts) and keeps what its own row needs.
-          const uint32_t prev = eb + static_cast<uint32_t>(quarter > 0 ? quarter - 1 : 0) * kKhEdgeQuarter * 4u +
-                                static_cast<uint32_t>(lane & 7) * kKhLanePitch * 4u;
-          const uint32_t next = eb + static_cast<uint32_t>(quarter < 3 ? quarter + 1 : 3) * kKhEdgeQuarter * 4u +
-                                8u * kKhLanePitch * 4u + static_cast<uint32_t>(lane & 7) * kKhLanePitch * 4u;
-#pragma unroll
-          for (int i = 0; i < 16; i += 4) {
-            const float4 pv = lds128(prev + i * 4u);
-            const float4 nv = lds128(next + i * 4u);
-            const float pe[4] = {pv.x, pv.y, pv.z, pv.w};
-            const float ne[4] = {nv.x, nv.y, nv.z, nv.w};
-#pragma unroll
-            for (int e = 0; e < 4; ++e) {
-              float p0 = __shfl_up_sync(0xffffffffu, __uint_as_float(r0[i + e]), 8);
-              float p2 = __shfl_down_sync(0xffffffffu, __uint_as_float(r2[i + e]), 8);
-              if (lane < 8) p0 = pe[e];
-              if (lane >= 24) p2 = ne[e];
-              out[m][jj][i + e] = (p0 + __uint_as_float(r1[i + e])) + p2;
-            }
+          for (int i = 0; i < 16; ++i) {
+            const float p0 = __shfl_up_sync(0xffffffffu, __uint_as_float(r0[i]), 1, 16);
+            const float p2 = __shfl_down_sync(0xffffffffu, __uint_as_float(r2[i]), 1, 16);
+            out[m][jj][i] = (p0 + __uint_as_float(r1[i])) + p2;
           }
         }
         // Depth m's columns are in registers (with one buffer the next tile may overwrite them now).
@@ -329,46 +407,110 @@ __global__ void __launch_bounds__(kKhThreads, 1)
         }
       }
 
-      const int oh = h0 + atom - 1, ow = w0 + iw;
-      const float* bias = g.bias != nullptr ? g.bias + static_cast<long long>(b) * g.bias_bstride : nullptr;
+      const float* bias_b = g.bias != nullptr ? g.bias + static_cast<long long>(b) * g.bias_bstride : nullptr;
+      if (wide) {
+        // Each 8-lane group transposes its 32 channels (8 float4 per lane), so that store
+        // instruction k writes lane k's voxel with the whole group: four voxels' 128-byte runs of
+        // 32 channels per warp instruction instead of 32 scattered 16-byte pieces.
+        const int gi = lane & 7, gbase = lane & ~7;
+        const int n = 32 * half + 4 * gi;  // the four channels this lane stores
+        float4 bq = make_float4(0.f, 0.f, 0.f, 0.f);
+        if (bias_b != nullptr) {
+          if (n + 4 <= g.cout && (reinterpret_cast<uintptr_t>(bias_b + n) & 15) == 0) {
+            bq = __ldg(reinterpret_cast<const float4*>(bias_b + n));
+          } else {
+            float t4[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
-      for (int m = 0; m < MT; ++m) {
-        const int od = d0 + m;
-        const bool valid = atom >= 1 && atom <= kKhRows && oh < g.out_h && ow < g.out_w && od < g.out_d;
-        if (!valid) continue;
-        const long long vox = ((static_cast<long long>(b) * g.out_d + od) * g.out_h + oh) * g.out_w + ow;
-        const long long out_base = vox * g.out_cstride + g.out_coff;
-        long long res_base = 0;
-        if (g.res != nullptr) {
-          const int qd = g.res_up ? od >> 1 : od, qh = g.res_up ? oh >> 1 : oh, qw = g.res_up ? ow >> 1 : ow;
-          res_base = (((static_cast<long long>(b) * g.res_d + qd) * g.res_h + qh) * g.res_w + qw) * g.res_cstride;
+            for (int e = 0; e < 4; ++e)
+              if (n + e < g.cout) t4[e] = __ldg(bias_b + n + e);
+            bq = make_float4(t4[0], t4[1], t4[2], t4[3]);
+          }
         }
 #pragma unroll
-        for (int jj = 0; jj < 2; ++jj) {
-          const int j = 2 * jj + half;
-          const int n = j * 16;
-          if (j >= nchunks || n >= g.cout) continue;
-          float v[16];
+        for (int m = 0; m < MT; ++m) {
+          // Before the transpose q[k] is channel group k of this lane's voxel; after it, channels
+          // n .. n + 3 of voxel k of the group, so the bias goes in afterwards.
+          float4 q[8];
 #pragma unroll
-          for (int i = 0; i < 16; ++i) v[i] = out[m][jj][i];
-          const int cnt = min(16, g.cout - n);
-          if (bias != nullptr) {
-            if (cnt == 16 && (reinterpret_cast<uintptr_t>(bias + n) & 15) == 0) {
+          for (int k = 0; k < 8; ++k) {
+            const float* s4 = &out[m][k >> 2][4 * (k & 3)];
+            q[k] = make_float4(s4[0], s4[1], s4[2], s4[3]);
+          }
+          transpose_f4<8>(q, gi);
+          const int od = d0 + m;
+          if (od >= g.out_d) continue;
+          long long vox[8];
+          bool ok[8];
 #pragma unroll
-              for (int i = 0; i < 4; ++i) {
-                const float4 q = __ldg(reinterpret_cast<const float4*>(bias + n) + i);
-                v[4 * i] += q.x;
-                v[4 * i + 1] += q.y;
-                v[4 * i + 2] += q.z;
-                v[4 * i + 3] += q.w;
+          for (int k = 0; k < 8; ++k) {
+            const int src = gbase + k;  // the lane whose voxel instruction k stores
+            const int sh = src & 15;
+            const int oh = h0 + sh - 1, ow = w0 + 2 * quarter + (src >> 4);
+            ok[k] = sh >= 1 && sh <= kKhRows && oh < g.out_h && ow < g.out_w;
+            vox[k] = ((static_cast<long long>(b) * g.out_d + od) * g.out_h + oh) * g.out_w + ow;
+            q[k].x += bq.x;
+            q[k].y += bq.y;
+            q[k].z += bq.z;
+            q[k].w += bq.w;
+          }
+          if (g.res != nullptr) {
+            // All eight residual reads go out before the first store (a store may alias them).
+            float4 rv[8];
+#pragma unroll
+            for (int k = 0; k < 8; ++k) {
+              rv[k] = make_float4(0.f, 0.f, 0.f, 0.f);
+              if (ok[k]) {
+                const int src = gbase + k;
+                const int oh = h0 + (src & 15) - 1, ow = w0 + 2 * quarter + (src >> 4);
+                const int qd = g.res_up ? od >> 1 : od, qh = g.res_up ? oh >> 1 : oh, qw = g.res_up ? ow >> 1 : ow;
+                const long long ro =
+                    (((static_cast<long long>(b) * g.res_d + qd) * g.res_h + qh) * g.res_w + qw) * g.res_cstride + n;
+                rv[k] = kh_load4(g, ro, n);
               }
-            } else {
+            }
 #pragma unroll
-              for (int i = 0; i < 16; ++i)
-                if (i < cnt) v[i] += __ldg(bias + n + i);
+            for (int k = 0; k < 8; ++k) {
+              q[k].x += rv[k].x;
+              q[k].y += rv[k].y;
+              q[k].z += rv[k].z;
+              q[k].w += rv[k].w;
             }
           }
-          store_row16(g, v, n, out_base + n, res_base + n);
+#pragma unroll
+          for (int k = 0; k < 8; ++k)
+            if (ok[k]) kh_store4(g, q[k], n, vox[k] * g.out_cstride + g.out_coff + n);
+        }
+      } else {
+        const int row = quarter * 32 + lane;
+        const int oh = h0 + (row & 15) - 1, ow = w0 + (row >> 4);
+#pragma unroll
+        for (int m = 0; m < MT; ++m) {
+          const int od = d0 + m;
+          const bool valid = (row & 15) >= 1 && (row & 15) <= kKhRows && oh < g.out_h && ow < g.out_w && od < g.out_d;
+          if (!valid) continue;
+          const long long vox = ((static_cast<long long>(b) * g.out_d + od) * g.out_h + oh) * g.out_w + ow;
+          const long long out_base = vox * g.out_cstride + g.out_coff;
+          long long res_base = 0;
+          if (g.res != nullptr) {
+            const int qd = g.res_up ? od >> 1 : od, qh = g.res_up ? oh >> 1 : oh, qw = g.res_up ? ow >> 1 : ow;
+            res_base = (((static_cast<long long>(b) * g.res_d + qd) * g.res_h + qh) * g.res_w + qw) * g.res_cstride;
+          }
+#pragma unroll
+          for (int jj = 0; jj < 2; ++jj) {
+            const int j = 2 * jj + half;
+            const int n = j * 16;
+            if (j >= nchunks || n >= g.cout) continue;
+            float v[16];
+#pragma unroll
+            for (int i = 0; i < 16; ++i) v[i] = out[m][jj][i];
+            const int cnt = min(16, g.cout - n);
+            if (bias_b != nullptr) {
+#pragma unroll
+              for (int i = 0; i < 16; ++i)
+                if (i < cnt) v[i] += __ldg(bias_b + n + i);
+            }
+            store_row16(g, v, n, out_base + n, res_base + n);
+          }
         }
       }
     }
@@ -394,11 +536,13 @@ cudaError_t launch_khcat_typed(const ConvMaps& maps, const ConvGeom& g, int grid
 
 int conv_khcat_stage_plan(int kc, int bn, int mt, size_t* smem_bytes) {
   const KhLayout L(kc, bn, mt);
-  const size_t extra = 1024 + kKhEdgeFloats * sizeof(float) + 256;
-  int stages = static_cast<int>((227 * 1024 - extra) / L.stage_bytes);
-  if (stages > 8) stages = 8;
+  const size_t extra = 1024 + 512;  // alignment slack, barriers
+  const size_t fixed = extra + static_cast<size_t>(L.a_slots) * L.a_bytes;
+  if (fixed >= 227 * 1024) return 0;
+  int stages = static_cast<int>((227 * 1024 - fixed) / L.b_bytes);
+  if (stages > kKhMaxBSlots) stages = kKhMaxBSlots;
   if (stages < 2) return 0;
-  *smem_bytes = static_cast<size_t>(stages) * L.stage_bytes + extra;
+  *smem_bytes = fixed + static_cast<size_t>(stages) * L.b_bytes;
   return stages;
 }
 

@@ -177,6 +177,7 @@ KHCAT_SHAPES = [
     ((1, 128, 4, 16, 16), 48),   # two channel blocks, N = 3 x 48
     ((1, 32, 2, 8, 8), 16),      # 32-channel blocks, N = 3 x 16, smallest grid
     ((2, 192, 2, 14, 24), 64),   # three channel blocks, H = one tile
+    ((2, 32, 4, 20, 24), 32),    # 32 outputs (4-lane transposed stores), partial h tile
 ]
 
 
