@@ -184,9 +184,9 @@ def run_reference(args, rank: int) -> None:
 
 # ---------------------------------------------------------------- kernel-level cases
 # The bench roofline's launch: the VAE decoder's full-resolution 64 -> 64 conv (B, C, D, H, W, O),
-# and the DRAM bytes per output voxel ncu measured for that kernel (248.9 MB over 786,432 voxels).
+# and the DRAM bytes per output voxel ncu measured for that kernel (246.6 MB over 786,432 voxels).
 DOMINANT_CONV = (1, 64, 96, 256, 128, 64)
-DOMINANT_TRAFFIC_PER_VOXEL = (101.027584e6 + 147.916032e6) / 786432
+DOMINANT_TRAFFIC_PER_VOXEL = (100.98944e6 + 145.607168e6) / 786432
 
 SWEEP_SHAPES = [(b, c, n, n, n, o) for n in (16, 32, 64) for c, o in ((32, 32), (64, 64), (128, 128), (256, 256))
                 for b in (1, 2)] + [(2, 512, 8, 8, 4, 512), (2, 512, 16, 16, 8, 512), (1, 128, 128, 128, 64, 128),
