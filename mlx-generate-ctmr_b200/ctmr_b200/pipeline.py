@@ -367,23 +367,26 @@ def sample_image_ncdhw(output_size: Sequence[int], spacing_mm: Sequence[float], 
     spacing = image_spacing_tensor(spacing_mm, device)
     timesteps, _ = set_timesteps_rflow(num_inference_steps=num_inference_steps,
                                        input_img_size_numel=math.prod(shape[2:]))
-    started = time.perf_counter()
     if sampler is None:
         sampler = GuidedUNetStep(unet_weights, unet_constructor, shape, class_label=mod, spacing=spacing,
                                  guidance_scale=guidance, device=device, use_cuda_graph=use_cuda_graph)
+    # Stage times come from CUDA events: no host wait between the stages, so the decode's launches
+    # are queued while the rflow steps still run on the device.
+    marks = [torch.cuda.Event(enable_timing=True) for _ in range(3)]
+    marks[0].record()
     final = sampler.sample(latent.to(device=device, dtype=torch.float32).contiguous(
         memory_format=torch.channels_last_3d), timesteps)
-    torch.cuda.synchronize(device)
-    rflow_s = time.perf_counter() - started
-    started = time.perf_counter()
+    marks[1].record()
     decoded = sliding_window_decode_ncdhw(final, vae_weights, constructor=vae_constructor, roi=roi, overlap=overlap,
                                           scale_factor=scale_factor)
     image = None
     if to_host:
         image = to_host_array(output_intensities_device(decoded, configuration=configuration))
+    marks[2].record()
     torch.cuda.synchronize(device)
     return ImageResult(final, decoded, image, np.diag((*map(float, spacing_mm), 1.0)),
-                       {"rflow_unet": rflow_s, "vae_decode": time.perf_counter() - started})
+                       {"rflow_unet": marks[0].elapsed_time(marks[1]) * 1e-3,
+                        "vae_decode": marks[1].elapsed_time(marks[2]) * 1e-3})
 
 
 def run(*, model: str = "mlx-generate-ctmr-mr-brain", output_dir=None, modality: int | None = None, seed: int = 0,
