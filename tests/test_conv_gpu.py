@@ -223,6 +223,44 @@ def test_kh_concatenated_kernel(cuda, shape, out_channels, precision, depths, mo
     assert not wide[:, :16].any() and not wide[:, 16 + out_channels:].any()
 
 
+@pytest.mark.parametrize("out_channels", [64, 48])
+def test_kh_concatenated_residual_forms(cuda, out_channels, monkeypatch):
+    """The kh-concatenated kernel's two store paths (64 outputs: 8-lane transposed; fewer: per
+    voxel) with a bf16 residual and with a residual on the half-resolution grid (nearest-upsampled
+    in the epilogue): each against the float64 oracle and against the atom-shifted kernel."""
+    from ctmr_b200 import ops
+
+    rng = np.random.default_rng(91)
+    shape = (2, 64, 4, 18, 16)
+    b, c = shape[:2]
+    x = torch.from_numpy(rng.standard_normal(shape).astype(np.float32))
+    w = torch.from_numpy((rng.standard_normal((out_channels, c, 3, 3, 3)) / np.sqrt(27 * c)).astype(np.float32))
+    bias = torch.from_numpy(rng.standard_normal(out_channels).astype(np.float32))
+    res_full = torch.from_numpy(rng.standard_normal((b, out_channels, *shape[2:])).astype(np.float32))
+    res_half = torch.from_numpy(rng.standard_normal((b, out_channels, 2, 9, 8)).astype(np.float32))
+    xc = ops.to_ndhwc(x.to(cuda))
+    packed = ops.pack_weight(w.to(cuda), "fp16")
+    res_bf16 = ops.to_ndhwc(res_full.to(cuda)).to(torch.bfloat16)
+    res_half_dev = ops.to_ndhwc(res_half.to(cuda))
+    conv = ops_ref.conv3d_ref(x.double(), w.double(), bias.double())
+    cases = [
+        (dict(residual=res_bf16), conv + res_bf16.double().cpu()),
+        (dict(residual=res_half_dev, residual_upsampled=True), conv + ops_ref.upsample_nearest_ref(res_half.double())),
+    ]
+    for kw, expected in cases:
+        monkeypatch.delenv("CTMR_DISABLE_KHCAT", raising=False)
+        y = ops.conv3d(xc, packed, bias.to(cuda), **kw)
+        monkeypatch.setenv("CTMR_DISABLE_KHCAT", "1")
+        y_v2 = ops.conv3d(xc, packed, bias.to(cuda), **kw)
+        monkeypatch.delenv("CTMR_DISABLE_KHCAT")
+        torch.cuda.synchronize()
+        err = ops_ref.rel_l2(y.cpu(), expected)
+        assert err <= FP16_CONV_REL_L2, f"{sorted(kw)} rel-L2 {err:.3e}"
+        diff = ops_ref.rel_l2(y.cpu(), y_v2.cpu().double())
+        assert diff <= 1e-5, f"{sorted(kw)} kh-concatenated vs atom-shifted rel-L2 {diff:.3e}"
+        assert not torch.equal(y, y_v2)
+
+
 @pytest.mark.parametrize("precision", ["fp16", "bf16"])
 @pytest.mark.parametrize(("shape", "x2_channels", "out_channels"), [
     ((2, 64, 3, 12, 24), 128, 64),   # skip 1x1 over cat(hidden, skip): partial tiles, two sources
