@@ -347,7 +347,11 @@ def sample_image_ncdhw(output_size: Sequence[int], spacing_mm: Sequence[float], 
                        num_inference_steps: int = 30, roi=IMAGE_ROI, overlap=IMAGE_OVERLAP, device=None,
                        use_cuda_graph: bool = True, to_host: bool = True, sampler: GuidedUNetStep | None = None
                        ) -> ImageResult:
-    """``image.sample_image_ncdhw`` (``image.py:204-346``) on the B200 path."""
+    """``image.sample_image_ncdhw`` (``image.py:204-346``) on the B200 path.
+
+    ``stage_timings_s`` holds device times (CUDA events, seconds) of the rflow loop and of the
+    decode plus intensity readback; the host waits for the device only once, at the end.
+    """
     config = CONFIGURATIONS[configuration]
     device = torch.device(device or "cuda")
     divisor = Z_SCALE * 2 ** (len(unet_constructor["num_channels"]) - 1)
