@@ -43,10 +43,11 @@ constexpr int kKhMaxBSlots = 12;  // weight ring slots at most
 __host__ __device__ constexpr uint32_t ru_kh(uint32_t v, uint32_t a) { return (v + a - 1) / a * a; }
 
 // Shared-memory ring slots: activations (MT depth slabs of 16 h x 10 w rows of kc channels) and
-// weights (3 x C_out rows of kc channels). All sizes are multiples of 1024 bytes, the 128-byte
-// swizzle period, so every MMA operand window starts on a swizzle-atom boundary.
-// Small activation boxes (<= 24 KB: 32 or 16 channels per block) serve only a few short MMA
-// stages each, so their ring is deeper (4 slots) to keep enough loads in flight.
+// weights (3 x C_out rows of kc channels). Slots and depth slabs are multiples of 1024 bytes and
+// the kw window offset (16 rows) is two swizzle atoms (8 rows x kc x 2 bytes each), so every MMA
+// operand window starts on a swizzle-atom boundary.
+// Small activation boxes (<= 24 KB: channel blocks of 32 or 16, or one depth per tile) serve
+// only a few short MMA stages each, so their ring is deeper (4 slots) to keep loads in flight.
 struct KhLayout {
   uint32_t a_m_bytes, a_bytes, kw_bytes, b_bytes;
   int a_slots;
