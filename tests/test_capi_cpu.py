@@ -69,6 +69,17 @@ def test_workspace_size_reports_prepared_operand():
     ({"precision": 7}, _lib.CTMR_ERR_INVALID),
     ({"trilinear": 1, "silu": 1}, _lib.CTMR_ERR_UNSUPPORTED),
     ({"stride": 2, "width": 1}, _lib.CTMR_ERR_UNSUPPORTED),
+    # label volumes (int16 ids read as 8 bit planes): 8 channels, only as the plain conv input
+    ({"x": _lib.Tensor(0x10000, _lib.DTYPE_LABEL8, 4, 1)}, _lib.CTMR_ERR_INVALID),
+    ({"residual": _lib.Tensor(0x50000, _lib.DTYPE_LABEL8, 8, 1)}, _lib.CTMR_ERR_INVALID),
+    ({"x": _lib.Tensor(0x10000, _lib.DTYPE_LABEL8, 8, 1), "stride": 2}, _lib.CTMR_ERR_UNSUPPORTED),
+    ({"x": _lib.Tensor(0x10000, _lib.DTYPE_LABEL8, 8, 1), "trilinear": 1}, _lib.CTMR_ERR_UNSUPPORTED),
+    ({"x": _lib.Tensor(0x10000, _lib.DTYPE_LABEL8, 8, 1), "x2": _lib.Tensor(0x50000, _lib.DTYPE_F32, 8, 8)},
+     _lib.CTMR_ERR_UNSUPPORTED),
+    ({"x": _lib.Tensor(0x10000, _lib.DTYPE_LABEL8, 8, 1), "gn_groups": 8}, _lib.CTMR_ERR_UNSUPPORTED),
+    # per-batch bias rows: 0 (rows of out_channels) or a stride of at least out_channels
+    ({"bias_row_stride": 16}, _lib.CTMR_ERR_INVALID),
+    ({"bias_row_stride": 1 << 31}, _lib.CTMR_ERR_INVALID),
 ])
 def test_conv_argument_validation(overrides, status):
     assert _status(_desc(**overrides)) == status
