@@ -103,3 +103,16 @@ def test_group_norm_validation():
     none = _lib.Tensor(None, 0, 0, 0)
     st = _lib.LIB.ctmr_group_norm_affine(t, none, 1, 64, None, None, 32, 1e-6, 0x2000, 0x3000, 1 << 20, None)
     assert st == _lib.CTMR_ERR_INVALID  # 30 channels are not divisible by 32 groups
+
+
+@pytest.mark.parametrize(("args", "status"), [
+    ((None, _lib.DTYPE_F16, 1, 128, 1, 0x2000), _lib.CTMR_ERR_INVALID),        # no Q/K/V
+    ((0x1000, _lib.DTYPE_F32, 1, 128, 1, 0x2000), _lib.CTMR_ERR_INVALID),      # fp32 operands
+    ((0x1000, _lib.DTYPE_BF16, 0, 128, 1, 0x2000), _lib.CTMR_ERR_INVALID),     # empty batch
+    ((0x1000, _lib.DTYPE_F16, 1, 200, 1, 0x2000), _lib.CTMR_ERR_UNSUPPORTED),  # tokens not a multiple of 128
+    ((0x1008, _lib.DTYPE_F16, 1, 128, 1, 0x2000), _lib.CTMR_ERR_INVALID),      # Q/K/V not 16-byte aligned
+])
+def test_attention_validation(args, status):
+    qkv, dtype, batch, tokens, heads, out = args
+    assert _lib.LIB.ctmr_attention_d32(qkv, dtype, batch, tokens, heads, 1.0, out, None) == status
+    assert _lib.LIB.ctmr_last_error()
