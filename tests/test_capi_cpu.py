@@ -116,3 +116,27 @@ def test_attention_validation(args, status):
     qkv, dtype, batch, tokens, heads, out = args
     assert _lib.LIB.ctmr_attention_d32(qkv, dtype, batch, tokens, heads, 1.0, out, None) == status
     assert _lib.LIB.ctmr_last_error()
+
+
+def _tdesc(**kw) -> _lib.TransformDesc:
+    d = _lib.TransformDesc()
+    d.batch, d.depth, d.height, d.width = 1, 4, 4, 4
+    d.x = _lib.Tensor(0x10000, _lib.DTYPE_F32, 32, 32)
+    d.y, d.y_dtype, d.y_channels, d.y_cstride = 0x40000, _lib.DTYPE_F32, 32, 32
+    for k, v in kw.items():
+        setattr(d, k, v)
+    return d
+
+
+@pytest.mark.parametrize(("overrides", "status"), [
+    ({"x": _lib.Tensor(0x10000, _lib.DTYPE_LABEL8, 8, 1)}, _lib.CTMR_ERR_INVALID),  # labels only feed a conv
+    ({"y": None}, _lib.CTMR_ERR_INVALID),
+    ({"y_dtype": _lib.DTYPE_LABEL8}, _lib.CTMR_ERR_INVALID),
+    ({"y_channels": 16, "y_cstride": 16}, _lib.CTMR_ERR_INVALID),                    # narrower than the input
+    ({"depth": 0}, _lib.CTMR_ERR_INVALID),
+    ({"mode": _lib.TRANSFORM_TRILINEAR, "silu": 1}, _lib.CTMR_ERR_UNSUPPORTED),
+    ({"mode": _lib.TRANSFORM_AVGPOOL, "width": 3}, _lib.CTMR_ERR_INVALID),
+])
+def test_transform_validation(overrides, status):
+    assert _lib.LIB.ctmr_transform(ctypes.byref(_tdesc(**overrides)), None) == status
+    assert _lib.LIB.ctmr_last_error()
