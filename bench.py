@@ -60,8 +60,11 @@ def _args():
     p.add_argument("--warmup", type=int, default=3)
     p.add_argument("--impl", choices=("ours", "reference"), default="ours")
     p.add_argument("--precision", choices=("fp16", "bf16", "fp32"), default="fp16")
-    p.add_argument("--mode", choices=("replicas", "split"), default="replicas",
-                   help="N > 1: independent volumes per GPU, or pairs splitting CFG branches and decode windows")
+    p.add_argument("--mode", choices=("replicas", "partition"), default="replicas",
+                   help="N > 1: independent volumes per GPU (the partition is timed beside them), or all N GPUs "
+                        "on one volume as the headline")
+    p.add_argument("--no-fp32-line", action="store_true",
+                   help="N = 1: skip the fp32-mode volume rate printed beside a 16-bit headline")
     p.add_argument("--no-graph", action="store_true")
     p.add_argument("--no-cpu-baseline", action="store_true")
     p.add_argument("--case", choices=("volume", "sweep", "conv", "gn", "unet-step", "vae-window", "breakdown"),
@@ -121,62 +124,99 @@ class ClockSampler:
 
 
 # ---------------------------------------------------------------- CPU baseline (oracle)
-def cpu_baseline(reps: int = 1) -> dict:
-    """The reference's arithmetic restated in torch on the host CPU (``oracle/``), a bounded sample.
+WORKLOAD = ("MR-Brain 256x256x128: 30 rflow steps (CFG batch 2, latent 1x4x64x64x32) + VAE decode as 4 depth "
+            "windows ROI (24,64,32) overlap 0.25")
 
-    Sample: one guided UNet step (CFG batch 2, 64x64x32) and the VAE decoder on one
-    (8, 64, 32) latent slab; per-volume time = 30 x UNet step + decode scaled by the
-    4-window decode's FLOPs over the slab's.
-    """
-    from ctmr_b200 import pipeline as P
-    from ctmr_b200 import weights as W
-    from oracle import networks_ref as N
 
-    threads = len(os.sched_getaffinity(0))
-    torch.set_num_threads(threads)
-    unet_w = W.random_weights(W.unet_shapes(P.PRODUCTION_UNET), seed=0, device="cpu")
-    vae_w = W.random_weights(W.vae_decoder_shapes(P.PRODUCTION_VAE), seed=1, device="cpu")
-    gen = torch.Generator().manual_seed(0)
-    z = torch.randn(LATENT, generator=gen)
-    spacing = N.image_spacing_tensor(SPACING)
-    slab = torch.randn((1, 4, 8, 64, 32), generator=gen)
-    with torch.inference_mode():
-        t0 = time.perf_counter()
-        for _ in range(reps):
-            N.guided_velocity(z, 1000.0, torch.tensor([MODALITY]), spacing, unet_w, P.PRODUCTION_UNET, GUIDANCE)
-        unet_s = (time.perf_counter() - t0) / reps
-        t0 = time.perf_counter()
-        N.decode_vae(slab, vae_w, P.PRODUCTION_VAE)
-        slab_s = time.perf_counter() - t0
-    windows = len(P.plan_windows(LATENT[2:], DECODE_ROI, DECODE_OVERLAP).starts)
-    decode_s = slab_s * windows * math.prod(DECODE_ROI) / (8 * 64 * 32)
-    per_volume = STEPS_RFLOW * unet_s + decode_s
-    cpu = "unknown"
+def workload_config() -> dict:
+    """The ``config`` object of every volume line, identical in both arms."""
+    return {"workload": WORKLOAD,
+            "networks": "MAISI rflow UNet [64,128,256,512] + VAE decoder [64,128,256], random init",
+            "inputs": "synthetic N(0,1) latent; MR-Brain spacing (0.94,0.94,1.36), modality 9, guidance 2",
+            "l2": "working set far above L2 (VAE activations 2.1 GB per tensor): no flush needed"}
+
+
+def _cpu_model() -> str:
     try:
-        cpu = next(line.split(":", 1)[1].strip() for line in Path("/proc/cpuinfo").read_text().splitlines()
-                   if line.startswith("model name"))
+        return next(line.split(":", 1)[1].strip() for line in Path("/proc/cpuinfo").read_text().splitlines()
+                    if line.startswith("model name"))
     except (OSError, StopIteration):
-        pass
-    return {"value": 60.0 / per_volume, "unit": UNIT, "cores": threads, "kind": "port",
-            "sample": (f"torch-CPU fp32 oracle: 1 guided UNet step (CFG batch 2, 64x64x32) x30 = {30 * unet_s:.1f} s "
-                       f"+ VAE decoder on a (8,64,32) latent slab scaled to {windows} windows of {DECODE_ROI} "
-                       f"= {decode_s:.1f} s per volume; {cpu}")}
+        return "unknown"
+
+
+class CpuSample:
+    """The reference's arithmetic restated in torch on the host CPU (``oracle/``), one bounded sample
+    of the volume workload: one guided UNet step (CFG batch 2, 64x64x32) and the VAE decoder on one
+    (8, 64, 32) latent slab. A volume is 30 UNet steps plus the 4 decode windows, whose work is 12
+    such slabs (4 x 24 / 8 depth planes), so the volume time is ``30 x unet_s + 12 x slab_s``.
+    Imports only the oracle: no product code is loaded on this path."""
+
+    def __init__(self) -> None:
+        from oracle import networks_ref as N
+        from oracle import production as OP
+
+        self.N = N
+        self.threads = len(os.sched_getaffinity(0))
+        torch.set_num_threads(self.threads)
+        self.unet_w = OP.parameters("unet", seed=0)
+        self.vae_w = OP.parameters("vae", seed=1)
+        self.unet_ctor, self.vae_ctor = OP.UNET, OP.VAE
+        gen = torch.Generator().manual_seed(0)
+        self.z = torch.randn(LATENT, generator=gen)
+        self.slab = torch.randn((1, 4, 8, 64, 32), generator=gen)
+        self.spacing = N.image_spacing_tensor(SPACING)
+        starts = N.window_starts(LATENT[2:], DECODE_ROI, N.scan_interval(LATENT[2:], DECODE_ROI, DECODE_OVERLAP))
+        self.windows = math.prod(len(s) for s in starts)
+        self.slabs_per_volume = self.windows * math.prod(DECODE_ROI) / (8 * 64 * 32)
+
+    def run(self) -> dict:
+        N = self.N
+        with torch.inference_mode():
+            t0 = time.perf_counter()
+            N.guided_velocity(self.z, 1000.0, torch.tensor([MODALITY]), self.spacing, self.unet_w, self.unet_ctor,
+                              GUIDANCE)
+            t1 = time.perf_counter()
+            N.decode_vae(self.slab, self.vae_w, self.vae_ctor)
+            t2 = time.perf_counter()
+        unet_s, slab_s = t1 - t0, t2 - t1
+        per_volume = STEPS_RFLOW * unet_s + self.slabs_per_volume * slab_s
+        return {"value": 60.0 / per_volume, "unit": UNIT, "cores": self.threads, "kind": "port",
+                "sample_s": t2 - t0, "per_volume_s": per_volume,
+                "sample": (f"torch-CPU fp32 oracle on {self.threads} threads ({_cpu_model()}): one guided UNet step "
+                           f"(CFG batch 2, 64x64x32) {unet_s:.2f} s x {STEPS_RFLOW} + the VAE decoder on one "
+                           f"(8,64,32) latent slab {slab_s:.2f} s x {self.slabs_per_volume:g} (the {self.windows} "
+                           f"windows of {DECODE_ROI}) = {per_volume:.1f} s per volume")}
+
+
+def cpu_baseline() -> dict:
+    sample = CpuSample()
+    sample.run()  # warm-up (first-touch of the weights, oneDNN primitive creation)
+    return sample.run()
 
 
 def run_reference(args, rank: int) -> None:
-    """``--impl reference``: the oracle port on all host cores; each step is one bounded sample."""
+    """``--impl reference``: the oracle port on all host cores. Each step is one bounded sample
+    (``CpuSample``) timed on the host; ``ms_per_step`` is that sample's wall time, ``value`` the
+    volumes/min the sample extrapolates to (``extrapolation``)."""
     if rank != 0:
         return
+    sample = CpuSample()
     for _ in range(args.warmup):
-        cpu_baseline()
-    samples = [cpu_baseline() for _ in range(args.steps)]
+        sample.run()
+    samples = [sample.run() for _ in range(args.steps)]
     value = statistics.median(s["value"] for s in samples)
-    base = dict(samples[-1], value=value)
+    sample_ms = statistics.median(s["sample_s"] for s in samples) * 1e3
+    base = {k: v for k, v in samples[-1].items() if k not in ("sample_s", "per_volume_s")}
+    base["value"] = value
     line = {"impl": "reference", "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": args.gpus,
-            "steps": args.steps, "warmup": args.warmup, "ms_per_step": 60000.0 / value, "higher_is_better": True,
-            "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
-            "config": {"workload": "MR-Brain 256x256x128: 30 rflow steps (CFG batch 2) + 4-window VAE decode",
-                       "model": "MAISI rflow UNet + VAE decoder (random init)", "parallelism": "host CPU"},
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(sample_ms, 1),
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+            "data": "synthetic (random-init weights, N(0,1) latent)", "config": workload_config(),
+            "device": "host CPU",
+            "extrapolation": {"step": "one sample: 1 guided UNet step + the VAE decoder on one (8,64,32) slab",
+                              "ms_per_step": "wall time of one sample (median over the timed steps)",
+                              "value": "60 / (30 x UNet-step s + 12 x slab s): volumes/min of whole volumes",
+                              "per_volume_s": round(60.0 / value, 2)},
             "cpu_baseline": base,
             "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
     print(json.dumps(line), flush=True)
@@ -431,241 +471,243 @@ def run_case(args) -> None:
 
 
 # ---------------------------------------------------------------- GPU arm
-def main() -> None:
-    args = _args()
-    if args.case != "volume":
-        run_case(args)
-        return
-    from ctmr_b200 import distributed as D
+class VolumeRun:
+    """One precision's volume workload on this rank: the sampler (CUDA-graph UNet step) and the decode,
+    with the device-resident timing (``value``) and the end-to-end timing through the public API
+    (``e2e``: the latent copied in from pinned host memory, the int16 image read back, every step)."""
 
-    rank, world, local = D.init_from_env() if int(os.environ.get("WORLD_SIZE", "1")) > 1 else (0, 1, 0)
-    if args.impl == "reference":
-        run_reference(args, rank)
-        if world > 1:
-            torch.distributed.destroy_process_group()
-        return
-    if world > 1 and world % 2 and args.mode == "split":
-        raise SystemExit("--mode split needs an even N (ranks pair up per volume)")
-    dev = torch.device("cuda", local)
-    torch.cuda.set_device(dev)
+    def __init__(self, precision: str, *, unet_w, vae_w, dev, world: int, rank: int, local: int, group,
+                 no_graph: bool) -> None:
+        from ctmr_b200 import distributed as D
+        from ctmr_b200 import fast_b200 as A
+        from ctmr_b200 import pipeline as P
 
+        self.D, self.A, self.P = D, A, P
+        self.precision, self.dev, self.world, self.local, self.group = precision, dev, world, local, group
+        self.unet_w, self.vae_w = unet_w, vae_w
+        self.spacing = P.image_spacing_tensor(SPACING, dev)
+        self.timesteps, _ = P.set_timesteps_rflow(num_inference_steps=STEPS_RFLOW,
+                                                  input_img_size_numel=math.prod(LATENT[2:]))
+        seed = rank if group is None else group.index
+        self.latent_host = torch.randn(LATENT, generator=torch.Generator().manual_seed(seed)).pin_memory()
+        self.latent_dev = self.latent_host.to(dev).contiguous(memory_format=torch.channels_last_3d)
+        with A.arithmetic_precision(precision):
+            if group is None:
+                self.sampler = P.GuidedUNetStep(unet_w, P.PRODUCTION_UNET, LATENT, class_label=MODALITY,
+                                                spacing=self.spacing, guidance_scale=GUIDANCE, device=dev,
+                                                use_cuda_graph=not no_graph)
+            else:
+                self.sampler = D.GroupGuidedStep(unet_w, P.PRODUCTION_UNET, LATENT, class_label=MODALITY,
+                                                 spacing=self.spacing, guidance_scale=GUIDANCE, device=dev,
+                                                 group=group, use_cuda_graph=not no_graph)
+            self.sampler.prepare()
+        self.volumes_per_step = world if group is None else group.count
+
+    def decode(self, latent: torch.Tensor) -> torch.Tensor | None:
+        if self.group is None:
+            return self.P.sliding_window_decode_ncdhw(latent, self.vae_w, constructor=self.P.PRODUCTION_VAE,
+                                                      roi=DECODE_ROI, overlap=DECODE_OVERLAP, scale_factor=1.0)
+        return self.D.group_window_decode(latent, self.vae_w, constructor=self.P.PRODUCTION_VAE, roi=DECODE_ROI,
+                                          overlap=DECODE_OVERLAP, scale_factor=1.0, group=self.group)
+
+    def volume(self) -> torch.Tensor | None:
+        with self.A.arithmetic_precision(self.precision):
+            return self.decode(self.sampler.sample(self.latent_dev, self.timesteps))
+
+    def e2e_step(self):
+        P = self.P
+        with self.A.arithmetic_precision(self.precision):
+            latent = self.latent_host.to(self.dev, non_blocking=True)
+            if self.group is None:
+                res = P.sample_image_ncdhw(OUTPUT, SPACING, unet_weights=self.unet_w, vae_weights=self.vae_w,
+                                           configuration="mr-brain", modality=MODALITY, guidance_scale=GUIDANCE,
+                                           latent=latent, roi=DECODE_ROI, overlap=DECODE_OVERLAP, device=self.dev,
+                                           sampler=self.sampler)
+                return res.image
+            final = self.sampler.sample(latent.contiguous(memory_format=torch.channels_last_3d), self.timesteps)
+            dec = self.decode(final)
+            return None if dec is None else P.to_host_array(P.output_intensities_device(dec, configuration="mr-brain"))
+
+    def barrier(self) -> None:
+        if self.world > 1:
+            torch.distributed.barrier(device_ids=[self.local])
+        torch.cuda.synchronize(self.dev)
+
+    def max_over_ranks(self, value: float) -> float:
+        if self.world == 1:
+            return value
+        t = torch.tensor([value], device=self.dev)
+        torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
+        return float(t.item())
+
+    def measure(self, steps: int, warmup: int, *, clocks: bool = False) -> dict:
+        from ctmr_b200 import ops
+
+        out = None
+        for _ in range(warmup):
+            out = self.volume()
+        self.barrier()
+        sampler_clocks = ClockSampler(self.local) if clocks and self.local == 0 else None
+        launches0 = ops.LAUNCHES[0]
+        start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        self.barrier()
+        start.record()
+        for _ in range(steps):
+            out = self.volume()
+        end.record()
+        self.barrier()
+        clock_info = sampler_clocks.stop() if sampler_clocks is not None else None
+        ms = self.max_over_ranks(start.elapsed_time(end) / steps)
+        launches = (ops.LAUNCHES[0] - launches0) / steps
+        if out is not None:
+            assert torch.isfinite(out).all(), f"non-finite decoded volume ({self.precision})"
+        # End to end through the public API with host buffers. The same W untimed warm-up calls: a
+        # repeated caller holds the previous image while the next call reads its result back, so the
+        # first two calls fill the pinned host cache that every later call reuses.
+        image = None
+        for _ in range(warmup):
+            image = self.e2e_step()
+        self.barrier()
+        t0 = time.perf_counter()
+        for _ in range(steps):
+            image = self.e2e_step()
+        self.barrier()
+        e2e_s = self.max_over_ranks((time.perf_counter() - t0) / steps)
+        if image is not None:
+            assert image.dtype == np.int16 and image.shape == (1, 1, *OUTPUT)
+        return {"ms": ms, "value": self.volumes_per_step * 60000.0 / ms, "launches": launches, "clocks": clock_info,
+                "e2e": {"value": round(self.volumes_per_step * 60.0 / e2e_s, 3), "unit": UNIT,
+                        "h2d_bytes_per_step": self.latent_host.numel() * self.latent_host.element_size(),
+                        "d2h_bytes_per_step": math.prod(OUTPUT) * 2}}
+
+    def release(self) -> None:
+        self.sampler.release()
+
+
+def conv_roofline(precision: str, unet_w, vae_w, dev, ms_per_volume: float) -> dict:
+    """The dominant launch against the burst peak, and every conv GEMM of one volume against the
+    sustained peak (CUDA events around each GEMM stage of one eager pass)."""
     from ctmr_b200 import fast_b200 as A
     from ctmr_b200 import ops
     from ctmr_b200 import pipeline as P
-    from ctmr_b200 import weights as W
 
-    unet_w = W.random_weights(W.unet_shapes(P.PRODUCTION_UNET), seed=0, device=dev)
-    vae_w = W.random_weights(W.vae_decoder_shapes(P.PRODUCTION_VAE), seed=1, device=dev)
-    spacing = P.image_spacing_tensor(SPACING, dev)
-    timesteps, _ = P.set_timesteps_rflow(num_inference_steps=STEPS_RFLOW, input_img_size_numel=math.prod(LATENT[2:]))
-    pairs = D.Pairs(rank, world) if world > 1 and args.mode == "split" else None
-    seed_volume = rank // 2 if pairs is not None else rank
-    latent_host = torch.randn(LATENT, generator=torch.Generator().manual_seed(seed_volume)).pin_memory()
-    ctx = A.arithmetic_precision(args.precision)
-    ctx.__enter__()
-    if pairs is None:
-        sampler = P.GuidedUNetStep(unet_w, P.PRODUCTION_UNET, LATENT, class_label=MODALITY, spacing=spacing,
-                                   guidance_scale=GUIDANCE, device=dev, use_cuda_graph=not args.no_graph)
-    else:
-        sampler = D.CfgSplitStep(unet_w, P.PRODUCTION_UNET, LATENT, class_label=MODALITY, spacing=spacing,
-                                 guidance_scale=GUIDANCE, device=dev, pairs=pairs, use_cuda_graph=not args.no_graph)
-    sampler.prepare()
-
-    def decode(latent: torch.Tensor) -> torch.Tensor:
-        if pairs is None:
-            return P.sliding_window_decode_ncdhw(latent, vae_w, constructor=P.PRODUCTION_VAE, roi=DECODE_ROI,
-                                                 overlap=DECODE_OVERLAP, scale_factor=1.0)
-        return D.pair_window_decode(latent, vae_w, constructor=P.PRODUCTION_VAE, roi=DECODE_ROI,
-                                    overlap=DECODE_OVERLAP, scale_factor=1.0, pairs=pairs)
-
-    latent_dev = latent_host.to(dev).contiguous(memory_format=torch.channels_last_3d)
-
-    def volume() -> torch.Tensor:
-        final = sampler.sample(latent_dev, timesteps)
-        return decode(final)
-
-    def barrier() -> None:
-        if world > 1:
-            torch.distributed.barrier(device_ids=[local])
-        torch.cuda.synchronize(dev)
-
-    for _ in range(args.warmup):
-        out = volume()
-    barrier()
-    # ------------------------------------------------ timed region (device-resident inputs)
-    clocks = ClockSampler(local) if local == 0 else None
-    launches0 = ops.LAUNCHES[0]
-    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    barrier()
-    start.record()
-    for _ in range(args.steps):
-        out = volume()
-    end.record()
-    barrier()
-    clock_info = clocks.stop() if clocks is not None else None
-    ms = start.elapsed_time(end) / args.steps
-    launches = (ops.LAUNCHES[0] - launches0) / args.steps
-    if world > 1:
-        t = torch.tensor([ms], device=dev)
-        torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
-        ms = float(t.item())
-    volumes_per_step = world // 2 if pairs is not None else world
-    value = volumes_per_step * 60000.0 / ms
-    assert torch.isfinite(out).all(), "non-finite decoded volume"
-
-    # ------------------------------------------------ end to end through the public API, host buffers
-    h2d = latent_host.numel() * latent_host.element_size()
-    d2h = math.prod(OUTPUT) * 2  # int16 image
-
-    def e2e_step():
-        if pairs is None:
-            res = P.sample_image_ncdhw(OUTPUT, SPACING, unet_weights=unet_w, vae_weights=vae_w,
-                                       configuration="mr-brain", modality=MODALITY, guidance_scale=GUIDANCE,
-                                       latent=latent_host.to(dev, non_blocking=True), roi=DECODE_ROI,
-                                       overlap=DECODE_OVERLAP, device=dev, sampler=sampler)
-            return res.image
-        final = sampler.sample(latent_host.to(dev, non_blocking=True).contiguous(
-            memory_format=torch.channels_last_3d), timesteps)
-        dec = decode(final)
-        return (P.to_host_array(P.output_intensities_device(dec, configuration="mr-brain"))
-                if pairs.member == 0 else None)
-
-    # The same W untimed warm-up calls as the device-resident timing: a repeated caller holds the
-    # previous image while the next call reads its result back, so the first two calls fill the
-    # pinned host cache that every later call reuses.
-    image = None
-    for _ in range(args.warmup):
-        image = e2e_step()
-    barrier()
-    t0 = time.perf_counter()
-    for _ in range(args.steps):
-        image = e2e_step()
-    barrier()
-    e2e_s = (time.perf_counter() - t0) / args.steps
-    if world > 1:
-        t = torch.tensor([e2e_s], device=dev)
-        torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
-        e2e_s = float(t.item())
-    if image is not None:
-        assert image.dtype == np.int16 and image.shape == (1, 1, *OUTPUT)
-
-    # ------------------------------------------------ conv roofline: GEMM launches timed with events
+    peaks, peak_kind = _peaks()
     prof: list = []
-    ops.PROFILE = prof
-    if pairs is None:
-        eager = P.GuidedUNetStep(unet_w, P.PRODUCTION_UNET, LATENT, class_label=MODALITY, spacing=spacing,
-                                 guidance_scale=GUIDANCE, device=dev, use_cuda_graph=False)
-        eager.z.copy_(latent_dev)
+    with A.arithmetic_precision(precision):
+        timesteps, _ = P.set_timesteps_rflow(num_inference_steps=STEPS_RFLOW,
+                                             input_img_size_numel=math.prod(LATENT[2:]))
+        eager = P.GuidedUNetStep(unet_w, P.PRODUCTION_UNET, LATENT, class_label=MODALITY,
+                                 spacing=P.image_spacing_tensor(SPACING, dev), guidance_scale=GUIDANCE, device=dev,
+                                 use_cuda_graph=False)
+        eager.z.copy_(torch.randn(LATENT, generator=torch.Generator().manual_seed(0)).to(dev))
         eager.t.fill_(float(timesteps[0]))
         eager.dt.fill_(P.euler_dt(timesteps[0], timesteps[1]))
-        n0 = len(prof)
+        ops.PROFILE = prof
         eager._step()
-        unet_part = prof[n0:]
-        n1 = len(prof)
-        decode(latent_dev)
-        vae_part = prof[n1:]
-    else:
-        unet_part, vae_part = [], []
-    ops.PROFILE = None
-    torch.cuda.synchronize(dev)
-    peaks, peak_kind = _peaks()
-    roofline = None
-    if unet_part:
+        unet_part = list(prof)
+        del prof[:]
+        P.sliding_window_decode_ncdhw(eager.z, vae_w, constructor=P.PRODUCTION_VAE, roi=DECODE_ROI,
+                                      overlap=DECODE_OVERLAP, scale_factor=1.0)
+        vae_part = list(prof)
+        ops.PROFILE = None
+        torch.cuda.synchronize(dev)
         unet_gemm = [r for r in unet_part if r["kind"] == "gemm"]
         vae_gemm = [r for r in vae_part if r["kind"] == "gemm"]
         conv_ms = STEPS_RFLOW * _total_ms(unet_gemm) + _total_ms(vae_gemm)
         conv_flop = STEPS_RFLOW * sum(r["flops"] for r in unet_gemm) + sum(r["flops"] for r in vae_gemm)
-        n_launch = STEPS_RFLOW * len(unet_gemm) + len(vae_gemm)
         agg = conv_flop / (conv_ms * 1e-3) / 1e12
         sustained = float(peaks.get("bf16_tflops_sustained", FALLBACK_PEAKS["bf16_tflops_sustained"]))
         burst = float(peaks.get("bf16_tflops", FALLBACK_PEAKS["bf16_tflops"]))
         # The largest launch class: the decoder's full-resolution 64 -> 64 conv (GN + SiLU input),
         # one launch timed by CUDA-graph replay on the device (no host gaps), against the burst peak.
-        dom_ms, dom_tflops, dom_prep_ms = _time_conv(DOMINANT_CONV, args.precision, 5, dev, "norm")
-        b_, c_, d_, h_, w_, o_ = DOMINANT_CONV
-        vox = b_ * d_ * h_ * w_
-        roofline = {"bound": "tensor", "achieved": round(dom_tflops, 1), "peak": burst, "unit": "TFLOP/s",
-                    "frac": round(dom_tflops / burst, 4),
-                    "traffic": round(DOMINANT_TRAFFIC_PER_VOXEL * vox),
-                    "kernel": "conv3d_khcat_kernel<64,2>: VAE decoder full-resolution 64->64 conv "
-                              f"{b_}x{c_}x{d_}x{h_}x{w_} (GN affine + SiLU input), the largest launch class",
-                    "launch_ms": round(dom_ms, 4), "prepare_ms": round(dom_prep_ms, 4),
-                    "algorithmic_bytes": vox * (c_ * 2 + o_ * 4),
-                    "traffic_source": "ncu dram__bytes_read+write of the same kernel on 1x64x48x128x128 "
-                                      "(profiles/conv3d_khcat_fp16_64to64_48x128x128.md), scaled by voxels",
-                    "peak_source": f"{peak_kind} bf16_tflops (burst: one launch timed alone)",
-                    "all_conv_launches": {"achieved": round(agg, 1), "peak": sustained,
-                                          "frac": round(agg / sustained, 4),
-                                          "peak_source": f"{peak_kind} bf16_tflops_sustained",
-                                          "launches_per_volume": n_launch,
-                                          "algorithmic_tflop_per_volume": round(conv_flop / 1e12, 2),
-                                          "conv_ms_per_volume": round(conv_ms, 2),
-                                          "share_of_step": round(conv_ms / ms, 3),
-                                          "timing": "CUDA events around each GEMM stage in an eager pass"}}
+        dom_ms, dom_tflops, dom_prep_ms = _time_conv(DOMINANT_CONV, precision, 5, dev, "norm")
+    b_, c_, d_, h_, w_, o_ = DOMINANT_CONV
+    vox = b_ * d_ * h_ * w_
+    return {"bound": "tensor", "achieved": round(dom_tflops, 1), "peak": burst, "unit": "TFLOP/s",
+            "frac": round(dom_tflops / burst, 4), "traffic": round(DOMINANT_TRAFFIC_PER_VOXEL * vox),
+            "kernel": "conv3d_khcat_kernel<64,2>: VAE decoder full-resolution 64->64 conv "
+                      f"{b_}x{c_}x{d_}x{h_}x{w_} (GN affine + SiLU input), the largest launch class",
+            "launch_ms": round(dom_ms, 4), "prepare_ms": round(dom_prep_ms, 4),
+            "algorithmic_flop": round(2 * vox * o_ * c_ * 27),
+            "algorithmic_bytes": vox * (c_ * 2 + o_ * 4),
+            "traffic_source": "ncu dram__bytes_read+write of the same kernel on a 1x64x48x128x128 case, "
+                              "scaled by voxels",
+            "peak_source": f"{peak_kind} bf16_tflops (burst: one launch timed alone)",
+            "all_conv_launches": {"achieved": round(agg, 1), "peak": sustained, "frac": round(agg / sustained, 4),
+                                  "peak_source": f"{peak_kind} bf16_tflops_sustained",
+                                  "launches_per_volume": STEPS_RFLOW * len(unet_gemm) + len(vae_gemm),
+                                  "algorithmic_tflop_per_volume": round(conv_flop / 1e12, 2),
+                                  "conv_ms_per_volume": round(conv_ms, 2),
+                                  "timing": "CUDA events around each GEMM launch of one eager (not graph-captured) "
+                                            "pass; host launch gaps can land inside the events, so this is an "
+                                            "upper bound on conv time"}}
 
-    # ------------------------------------------------ the north-star partition beside the replicas
-    split = None
-    if pairs is None and world > 1 and world % 2 == 0:
-        split_pairs = D.Pairs(rank, world)
-        split_sampler = D.CfgSplitStep(unet_w, P.PRODUCTION_UNET, LATENT, class_label=MODALITY, spacing=spacing,
-                                       guidance_scale=GUIDANCE, device=dev, pairs=split_pairs,
-                                       use_cuda_graph=not args.no_graph)
-        split_sampler.prepare()
-        split_latent = torch.randn(LATENT, generator=torch.Generator().manual_seed(rank // 2)).to(dev).contiguous(
-            memory_format=torch.channels_last_3d)
 
-        def split_volume() -> torch.Tensor:
-            final = split_sampler.sample(split_latent, timesteps)
-            return D.pair_window_decode(final, vae_w, constructor=P.PRODUCTION_VAE, roi=DECODE_ROI,
-                                        overlap=DECODE_OVERLAP, scale_factor=1.0, pairs=split_pairs)
+def main() -> None:
+    args = _args()
+    if args.case != "volume":
+        run_case(args)
+        return
+    if args.impl == "reference":
+        # The reference's CPU arithmetic only (the oracle); rank 0 alone under torchrun.
+        run_reference(args, int(os.environ.get("RANK", "0")))
+        return
+    from ctmr_b200 import distributed as D
+    from ctmr_b200 import pipeline as P
+    from ctmr_b200 import weights as W
 
-        for _ in range(args.warmup):
-            split_volume()
-        barrier()
-        s0, s1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        s0.record()
-        for _ in range(args.steps):
-            split_out = split_volume()
-        s1.record()
-        barrier()
-        split_ms = torch.tensor([s0.elapsed_time(s1) / args.steps], device=dev)
-        torch.distributed.all_reduce(split_ms, op=torch.distributed.ReduceOp.MAX)
-        assert torch.isfinite(split_out).all(), "non-finite decoded volume (split mode)"
-        split = {"value": round((world // 2) * 60000.0 / float(split_ms.item()), 3), "unit": UNIT,
-                 "ms_per_step": round(float(split_ms.item()), 2), "volumes_per_step": world // 2,
-                 "parallelism": f"{world // 2} pairs x (CFG branches split, one velocity all_gather per rflow "
-                                "step; decode windows split, one all_reduce of the blend)"}
-        split_sampler.release()
+    world_env = int(os.environ.get("WORLD_SIZE", "1"))
+    rank, world, local = D.init_from_env() if world_env > 1 else (0, 1, 0)
+    if world > 1 and args.mode == "partition" and world not in D.GROUP_SIZES:
+        raise SystemExit(f"--mode partition needs N in {D.GROUP_SIZES}")
+    dev = torch.device("cuda", local)
+    torch.cuda.set_device(dev)
+    unet_w = W.random_weights(W.unet_shapes(P.PRODUCTION_UNET), seed=0, device=dev)
+    vae_w = W.random_weights(W.vae_decoder_shapes(P.PRODUCTION_VAE), seed=1, device=dev)
+    common = dict(unet_w=unet_w, vae_w=vae_w, dev=dev, world=world, rank=rank, local=local, no_graph=args.no_graph)
 
+    headline_group = D.VolumeGroup(rank, world, world) if world > 1 and args.mode == "partition" else None
+    run = VolumeRun(args.precision, group=headline_group, **common)
+    head = run.measure(args.steps, args.warmup, clocks=True)
+    run.release()
+
+    # The precision-matched line: the reference's own arithmetic is FP32 (split-fp16 "exact" products).
+    fp32 = None
+    if world == 1 and args.precision != "fp32" and not args.no_fp32_line:
+        run32 = VolumeRun("fp32", group=None, **common)
+        m = run32.measure(args.steps, args.warmup)
+        run32.release()
+        fp32 = {"value": round(m["value"], 3), "unit": UNIT, "ms_per_step": round(m["ms"], 2), "e2e": m["e2e"],
+                "gpu_launches": int(m["launches"]), "dtype": "fp32 (split-fp16 operands, 3 products)"}
+
+    # The north-star partition beside the replicas: all N GPUs on one volume.
+    partition = None
+    if world > 1 and headline_group is None and world in D.GROUP_SIZES:
+        prun = VolumeRun(args.precision, group=D.VolumeGroup(rank, world, world), **common)
+        m = prun.measure(args.steps, args.warmup)
+        prun.release()
+        partition = {"value": round(m["value"], 3), "unit": UNIT, "ms_per_volume": round(m["ms"], 2),
+                     "ranks_per_volume": world, "e2e": m["e2e"], "parallelism": D.describe_partition(world)}
+
+    roofline = conv_roofline(args.precision, unet_w, vae_w, dev, head["ms"]) if world == 1 else None
     if rank == 0:
-        base = None
-        if world == 1 and not args.no_cpu_baseline:
-            base = cpu_baseline()
+        base = None if (world > 1 or args.no_cpu_baseline) else cpu_baseline()
         line = {
-            "metric": METRIC, "value": round(value, 3), "unit": UNIT, "n_gpus": world, "steps": args.steps,
-            "warmup": args.warmup, "ms_per_step": round(ms, 2), "higher_is_better": True, "scaling": "weak",
+            "metric": METRIC, "value": round(head["value"], 3), "unit": UNIT, "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": round(head["ms"], 2), "higher_is_better": True, "scaling": "weak",
             "vs_baseline": None, "dtype": args.precision, "data": "synthetic (random-init weights, N(0,1) latent)",
-            "config": {"workload": "MR-Brain 256x256x128: 30 rflow steps (CFG batch 2, latent 1x4x64x64x32) + "
-                                   "VAE decode as 4 depth windows ROI (24,64,32) overlap 0.25",
-                       "model": "MAISI rflow UNet [64,128,256,512] + VAE decoder [64,128,256] (random init)",
-                       "global_batch": volumes_per_step, "seq_len": None,
-                       "parallelism": ("single GPU" if world == 1 else
-                                       f"{world // 2} pairs x (CFG split + window split)" if pairs is not None else
-                                       f"{world} replicas (one volume per GPU per step, no data-path collective)"),
-                       "l2": "working set far above L2 (VAE activations 2.1 GB per tensor)",
-                       "precision": args.precision, "cuda_graph": not args.no_graph},
-            "e2e": {"value": round(volumes_per_step * 60.0 / e2e_s, 3), "unit": UNIT, "h2d_bytes_per_step": h2d,
-                    "d2h_bytes_per_step": d2h},
-            "gpu_launches": int(launches),
-            "clocks": clock_info,
-            "roofline": roofline,
-            "cpu_baseline": base,
+            "config": workload_config(),
+            "parallelism": ("single GPU" if world == 1 else D.describe_partition(world) if headline_group else
+                            f"{world} replicas (one volume per GPU per step, no data-path collective)"),
+            "cuda_graph": not args.no_graph,
+            "e2e": head["e2e"], "gpu_launches": int(head["launches"]), "clocks": head["clocks"],
+            "roofline": roofline, "cpu_baseline": base,
         }
-        if split is not None:
-            line["split"] = split
+        if fp32 is not None:
+            line["fp32"] = fp32
+        if partition is not None:
+            line["partition"] = partition
         print(json.dumps(line), flush=True)
-    sampler.release()
-    ctx.__exit__(None, None, None)
     if world > 1:
         torch.distributed.barrier(device_ids=[local])
         torch.distributed.destroy_process_group()

@@ -199,6 +199,23 @@ CTMR_API int ctmr_group_norm_affine(ctmr_tensor x, ctmr_tensor x2, int batch, lo
                            const float* beta, int groups, float eps, float* affine, void* workspace,
                            size_t workspace_bytes, void* stream);
 
+/* The GroupNorm statistics of ctmr_group_norm_affine stopped before the affine: the merged
+ * (count, mean, M2) of each (batch item, group) of (x ++ x2), float moments[batch][groups][3].
+ * Same workspace as ctmr_group_norm_affine. For a tensor split across devices (depth shards
+ * of one volume, each holding `voxels` of it): each part computes its moments, the parts
+ * exchange them, and ctmr_group_norm_affine_from_moments forms the affine of the whole
+ * tensor. The reference normalises whole tensors only (`fast_fp32.py:183-189`); this is the
+ * same statistic, split at the boundary between the two kernels of its computation. */
+CTMR_API int ctmr_group_norm_moments(ctmr_tensor x, ctmr_tensor x2, int batch, long long voxels, int groups,
+                                     float* moments, void* workspace, size_t workspace_bytes, void* stream);
+
+/* The affine of group_norm_affine (`fast_fp32.py:183-189`) from the moments of `parts` parts
+ * of one tensor, float moments[parts][batch][groups][3] (1 <= parts <= 64), merged in part
+ * order in double precision, so every caller holding the same moments gets the same affine. */
+CTMR_API int ctmr_group_norm_affine_from_moments(const float* moments, int parts, int batch, int channels,
+                                                 const float* gamma, const float* beta, int groups, float eps,
+                                                 float* affine, void* stream);
+
 /* Kernel launches one ctmr_conv3d call with this descriptor issues (instrumentation;
  * no reference counterpart), or 0 for an invalid descriptor. */
 CTMR_API int ctmr_conv3d_launch_count(const ctmr_conv3d_desc* desc);

@@ -923,6 +923,51 @@ int ctmr_group_norm_affine(ctmr_tensor x, ctmr_tensor x2, int batch, long long v
   return e == cudaSuccess ? CTMR_OK : cuda_fail(e, "group_norm launch");
 }
 
+int ctmr_group_norm_moments(ctmr_tensor x, ctmr_tensor x2, int batch, long long voxels, int groups, float* moments,
+                            void* workspace, size_t workspace_bytes, void* stream) {
+  int st = check_view(x, "x", true);
+  if (st) return st;
+  if ((st = check_view(x2, "x2", false))) return st;
+  const int ctot = x.channels + (x2.data ? x2.channels : 0);
+  if (batch <= 0 || voxels <= 0) return fail(CTMR_ERR_INVALID, "group_norm extents");
+  if (groups <= 0 || ctot % groups != 0) return fail(CTMR_ERR_INVALID, "group_norm channels must be divisible by num_groups");
+  if (ctot > 2048) return fail(CTMR_ERR_UNSUPPORTED, "group_norm supports at most 2048 channels");
+  if (moments == nullptr) return fail(CTMR_ERR_INVALID, "moments output missing");
+  const size_t need = ctmr_group_norm_workspace_size(batch, voxels, groups);
+  if (workspace == nullptr || workspace_bytes < need)
+    return fail(CTMR_ERR_WORKSPACE, "group_norm needs %zu workspace bytes, got %zu", need, workspace_bytes);
+  ctmr::GnParams p{};
+  p.src[0] = as_source(x);
+  p.src[1] = as_source(x2);
+  p.batch = batch;
+  p.voxels = voxels;
+  p.groups = groups;
+  p.partials = static_cast<float*>(workspace);
+  p.chunks = ctmr::gn_chunks_for(batch, voxels, ctot);
+  cudaError_t e = ctmr::launch_group_norm_moments(p, moments, static_cast<cudaStream_t>(stream));
+  return e == cudaSuccess ? CTMR_OK : cuda_fail(e, "group_norm moments launch");
+}
+
+int ctmr_group_norm_affine_from_moments(const float* moments, int parts, int batch, int channels, const float* gamma,
+                                        const float* beta, int groups, float eps, float* affine, void* stream) {
+  if (moments == nullptr || affine == nullptr) return fail(CTMR_ERR_INVALID, "moments or affine missing");
+  if (parts <= 0 || parts > 64 || batch <= 0) return fail(CTMR_ERR_INVALID, "moments parts / batch out of range");
+  if (groups <= 0 || channels <= 0 || channels % groups != 0)
+    return fail(CTMR_ERR_INVALID, "group_norm channels must be divisible by num_groups");
+  ctmr::GnMomentsParams p{};
+  p.moments = moments;
+  p.parts = parts;
+  p.batch = batch;
+  p.channels = channels;
+  p.groups = groups;
+  p.eps = eps;
+  p.gamma = gamma;
+  p.beta = beta;
+  p.affine = affine;
+  cudaError_t e = ctmr::launch_group_norm_from_moments(p, static_cast<cudaStream_t>(stream));
+  return e == cudaSuccess ? CTMR_OK : cuda_fail(e, "group_norm from moments launch");
+}
+
 int ctmr_conv3d_stats_slots(const ctmr_conv3d_desc* d) {
   ConvPlan p{};
   if (d == nullptr || plan_conv(d, &p) != CTMR_OK) return 0;

@@ -247,14 +247,10 @@ __device__ __forceinline__ MomentsD shfl_down_moments(const MomentsD& m, int off
 constexpr int kFinThreads = 128;
 constexpr int kFinPerThread = 5;  // ceil(gn_max_chunks(1) / kFinThreads)
 
-__global__ void __launch_bounds__(kFinThreads) gn_finalize_kernel(const GnParams p) {
-  griddep_wait();  // the preceding kernel's writes are visible from here on
-  griddep_launch_dependents();
-  __shared__ double s_m[kFinThreads / 32][3];
-  __shared__ double s_stat[2];
-  const int g = blockIdx.x, b = blockIdx.y;
-  const int ctot = p.src[0].channels + p.src[1].channels;
-  const int cpg = ctot / p.groups;
+// The (count, mean, M2) of group g of batch item b over all chunk partials, merged in a
+// fixed order (per thread its strided chunks, a shuffle tree per warp, then the warps in
+// order) in double precision; the result is valid in thread 0.
+__device__ __forceinline__ MomentsD merge_chunks(const GnParams& p, int g, int b, double (*s_m)[3]) {
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   float q[kFinPerThread][3];
 #pragma unroll
@@ -285,29 +281,81 @@ __global__ void __launch_bounds__(kFinThreads) gn_finalize_kernel(const GnParams
     s_m[warp][2] = m.m2;
   }
   __syncthreads();
-  if (tid == 0) {
-    MomentsD t{0.0, 0.0, 0.0};
+  MomentsD t{0.0, 0.0, 0.0};
+  if (tid == 0)
     for (int w = 0; w < kFinThreads / 32; ++w) t = merge_d(t, MomentsD{s_m[w][0], s_m[w][1], s_m[w][2]});
-    const double var = t.n > 0.0 ? t.m2 / t.n : 0.0;
-    s_stat[0] = t.mean;
-    s_stat[1] = 1.0 / sqrt(var + static_cast<double>(p.eps));
-  }
-  __syncthreads();
-  const double mean = s_stat[0], rstd = s_stat[1];
-  for (int c = g * cpg + tid; c < (g + 1) * cpg; c += kFinThreads) {
-    const double gam = p.gamma != nullptr ? static_cast<double>(p.gamma[c]) : 1.0;
-    const double bet = p.beta != nullptr ? static_cast<double>(p.beta[c]) : 0.0;
+  return t;
+}
+
+// scale = gamma * rstd, offset = beta - mean * scale for the channels of group g.
+__device__ __forceinline__ void write_group_affine(double mean, double rstd, int g, int b, int ctot, int cpg,
+                                                   const float* gamma, const float* beta, float* affine) {
+  for (int c = g * cpg + static_cast<int>(threadIdx.x); c < (g + 1) * cpg; c += kFinThreads) {
+    const double gam = gamma != nullptr ? static_cast<double>(gamma[c]) : 1.0;
+    const double bet = beta != nullptr ? static_cast<double>(beta[c]) : 0.0;
     const double scale = gam * rstd;
-    float* a = p.affine + (static_cast<long long>(b) * ctot + c) * 2;
+    float* a = affine + (static_cast<long long>(b) * ctot + c) * 2;
     a[0] = static_cast<float>(scale);
     a[1] = static_cast<float>(bet - mean * scale);
   }
 }
 
-// From convolution output statistics: one block per (group, batch item); thread
-// i merges the (slot, channel) entries i, i + 128, ... of the group in order
-// (slot-major within each source, then the second source), then the fixed
-// shuffle tree and the warps in order, in double precision.
+__global__ void __launch_bounds__(kFinThreads) gn_finalize_kernel(const GnParams p) {
+  griddep_wait();  // the preceding kernel's writes are visible from here on
+  griddep_launch_dependents();
+  __shared__ double s_m[kFinThreads / 32][3];
+  __shared__ double s_stat[2];
+  const int g = blockIdx.x, b = blockIdx.y;
+  const int ctot = p.src[0].channels + p.src[1].channels;
+  const int cpg = ctot / p.groups;
+  const MomentsD t = merge_chunks(p, g, b, s_m);
+  if (threadIdx.x == 0) {
+    const double var = t.n > 0.0 ? t.m2 / t.n : 0.0;
+    s_stat[0] = t.mean;
+    s_stat[1] = 1.0 / sqrt(var + static_cast<double>(p.eps));
+  }
+  __syncthreads();
+  write_group_affine(s_stat[0], s_stat[1], g, b, ctot, cpg, p.gamma, p.beta, p.affine);
+}
+
+// The merged moments themselves, float (count, mean, M2) per (batch item, group), for a
+// caller that combines the moments of several parts of one tensor (depth shards).
+__global__ void __launch_bounds__(kFinThreads) gn_moments_kernel(const GnParams p, float* moments) {
+  griddep_wait();
+  griddep_launch_dependents();
+  __shared__ double s_m[kFinThreads / 32][3];
+  const int g = blockIdx.x, b = blockIdx.y;
+  const MomentsD t = merge_chunks(p, g, b, s_m);
+  if (threadIdx.x == 0) {
+    float* out = moments + (static_cast<long long>(b) * p.groups + g) * 3;
+    out[0] = static_cast<float>(t.n);
+    out[1] = static_cast<float>(t.mean);
+    out[2] = static_cast<float>(t.m2);
+  }
+}
+
+// Affine from the moments of `parts` parts, float[parts][batch][groups][3], merged in part
+// order in double precision: every holder of the same moments gets the same affine, bit for bit.
+__global__ void __launch_bounds__(kFinThreads) gn_affine_from_moments_kernel(const GnMomentsParams p) {
+  griddep_wait();
+  griddep_launch_dependents();
+  __shared__ double s_stat[2];
+  const int g = blockIdx.x, b = blockIdx.y;
+  const int cpg = p.channels / p.groups;
+  if (threadIdx.x == 0) {
+    MomentsD t{0.0, 0.0, 0.0};
+    for (int k = 0; k < p.parts; ++k) {
+      const float* q = p.moments + ((static_cast<long long>(k) * p.batch + b) * p.groups + g) * 3;
+      t = merge_d(t, MomentsD{q[0], q[1], q[2]});
+    }
+    const double var = t.n > 0.0 ? t.m2 / t.n : 0.0;
+    s_stat[0] = t.mean;
+    s_stat[1] = 1.0 / sqrt(var + static_cast<double>(p.eps));
+  }
+  __syncthreads();
+  write_group_affine(s_stat[0], s_stat[1], g, b, p.channels, cpg, p.gamma, p.beta, p.affine);
+}
+
 __global__ void __launch_bounds__(kFinThreads) gn_from_stats_kernel(const GnStatsParams p) {
   griddep_wait();
   griddep_launch_dependents();
@@ -408,6 +456,26 @@ namespace ctmr {
 
 cudaError_t launch_group_norm_from_stats(const GnStatsParams& p, cudaStream_t stream) {
   return launch_kernel(gn_from_stats_kernel, dim3(p.groups, p.batch), dim3(kFinThreads), 0, stream, p);
+}
+
+cudaError_t launch_group_norm_moments(const GnParams& p, float* moments, cudaStream_t stream) {
+  const int ctot = p.src[0].channels + p.src[1].channels;
+  const size_t chan_smem = static_cast<size_t>(ctot) * 3 * sizeof(float);
+  if (chan_smem > 48 * 1024) {
+    cudaError_t e = cudaFuncSetAttribute(gn_partial_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         static_cast<int>(chan_smem));
+    if (e != cudaSuccess) return e;
+  }
+  if (p.chunks > kFinThreads * kFinPerThread) return cudaErrorInvalidValue;
+  launch_kernel(gn_partial_kernel, dim3(p.chunks, p.batch), dim3(kGnThreads), chan_smem, stream, p);
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return e;
+  launch_kernel(gn_moments_kernel, dim3(p.groups, p.batch), dim3(kFinThreads), 0, stream, p, moments);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_group_norm_from_moments(const GnMomentsParams& p, cudaStream_t stream) {
+  return launch_kernel(gn_affine_from_moments_kernel, dim3(p.groups, p.batch), dim3(kFinThreads), 0, stream, p);
 }
 
 }  // namespace ctmr

@@ -32,7 +32,19 @@ struct GnStatsParams {
   float* affine;          // out: [batch][C][2]
 };
 
+// Affine from per-part moments float[parts][batch][groups][3] (count, mean, M2).
+struct GnMomentsParams {
+  const float* moments;
+  int parts, batch, channels, groups;
+  float eps;
+  const float* gamma;
+  const float* beta;
+  float* affine;          // out: [batch][channels][2]
+};
+
 int gn_max_chunks(int batch);
+cudaError_t launch_group_norm_moments(const GnParams& p, float* moments, cudaStream_t stream);
+cudaError_t launch_group_norm_from_moments(const GnMomentsParams& p, cudaStream_t stream);
 cudaError_t launch_group_norm_from_stats(const GnStatsParams& p, cudaStream_t stream);
 int gn_chunks_for(int batch, long long voxels, int channels);
 cudaError_t launch_group_norm_affine(const GnParams& p, cudaStream_t stream);

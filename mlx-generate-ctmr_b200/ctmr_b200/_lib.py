@@ -46,6 +46,8 @@ EXPORTED_SYMBOLS = (
     "ctmr_conv3d_stats_slots",
     "ctmr_conv3d_launch_count",
     "ctmr_group_norm_affine_from_stats",
+    "ctmr_group_norm_moments",
+    "ctmr_group_norm_affine_from_moments",
     "ctmr_transform",
     "ctmr_ncdhw_to_ndhwc",
     "ctmr_ndhwc_to_ncdhw",
@@ -150,6 +152,8 @@ def _load() -> ctypes.CDLL:
         "ctmr_conv3d_stats_slots": (i, [ctypes.POINTER(Conv3dDesc)]),
         "ctmr_conv3d_launch_count": (i, [ctypes.POINTER(Conv3dDesc)]),
         "ctmr_group_norm_affine_from_stats": (i, [vp, i, vp, i, i, i, vp, vp, i, f, vp, vp]),
+        "ctmr_group_norm_moments": (i, [Tensor, Tensor, i, ll, i, vp, vp, sz, vp]),
+        "ctmr_group_norm_affine_from_moments": (i, [vp, i, i, i, vp, vp, i, f, vp, vp]),
         "ctmr_transform": (i, [ctypes.POINTER(TransformDesc), vp]),
         "ctmr_ncdhw_to_ndhwc": (i, [vp, i, vp, i, i, i, ll, vp]),
         "ctmr_ndhwc_to_ncdhw": (i, [vp, i, vp, i, i, i, ll, vp]),

@@ -448,6 +448,47 @@ def group_norm_affine(
     return affine
 
 
+def group_norm_moments(x: torch.Tensor, *, groups: int, x2: torch.Tensor | None = None,
+                       out: torch.Tensor | None = None) -> torch.Tensor:
+    """Merged ``(count, mean, M2)`` per (batch item, group) of ``x ++ x2`` as ``(B, groups, 3)`` fp32
+    (``ctmr_group_norm_moments``): the statistics of ``group_norm_affine`` before the affine, for
+    tensors split across devices. ``out`` may be a view into a larger (exchange) buffer."""
+    b, c, d, h, w = (int(n) for n in x.shape)
+    ctot = c + (int(x2.shape[1]) if x2 is not None else 0)
+    if ctot % groups:
+        raise ValueError("group_norm channels must be divisible by num_groups")
+    if out is None:
+        out = torch.empty((b, groups, 3), dtype=F32, device=x.device)
+    elif out.dtype != F32 or out.numel() != b * groups * 3 or not out.is_contiguous():
+        raise ValueError(f"moments output must be {b * groups * 3} contiguous float32 values")
+    voxels = d * h * w
+    ws_bytes = int(LIB.ctmr_group_norm_workspace_size(b, voxels, groups))
+    ws = torch.empty(max(ws_bytes, 4), dtype=torch.uint8, device=x.device)
+    _count(2)
+    check(LIB.ctmr_group_norm_moments(view(x), view(x2), b, voxels, groups, out.data_ptr(), ws.data_ptr(), ws_bytes,
+                                      _stream()), "group_norm_moments")
+    return out
+
+
+def group_norm_affine_from_moments(moments: torch.Tensor, weight: torch.Tensor | None, bias: torch.Tensor | None, *,
+                                   channels: int, groups: int, eps: float) -> torch.Tensor:
+    """``(B, C, 2)`` affine from the moments ``(parts, B, groups, 3)`` of the parts of one tensor
+    (``ctmr_group_norm_affine_from_moments``; merged in part order)."""
+    if moments.dim() != 4 or int(moments.shape[2]) != groups or int(moments.shape[3]) != 3:
+        raise ValueError(f"moments must be (parts, B, {groups}, 3); got {tuple(moments.shape)}")
+    moments = moments.to(dtype=F32).contiguous()
+    parts, b = int(moments.shape[0]), int(moments.shape[1])
+    gamma = weight.to(dtype=F32).contiguous() if weight is not None else None
+    beta = bias.to(dtype=F32).contiguous() if bias is not None else None
+    affine = torch.empty((b, channels, 2), dtype=F32, device=moments.device)
+    _count(1)
+    check(LIB.ctmr_group_norm_affine_from_moments(
+        moments.data_ptr(), parts, b, int(channels), gamma.data_ptr() if gamma is not None else None,
+        beta.data_ptr() if beta is not None else None, int(groups), float(eps), affine.data_ptr(), _stream()),
+        "group_norm_affine_from_moments")
+    return affine
+
+
 def attention_d32(qkv: torch.Tensor, heads: int, scale: float) -> torch.Tensor:
     """``softmax(Q K^T * scale) V`` per head for head size 32 (``ctmr_attention_d32``).
 
@@ -518,7 +559,9 @@ def rflow_step(z: torch.Tensor, velocity: torch.Tensor, *, guidance: float | Non
     """
     if z.dtype != F32 or velocity.dtype != F32:
         raise ValueError("rflow_step takes float32 tensors")
-    if z.stride() != velocity[: z.shape[0]].stride() or not (z.is_contiguous() or z.is_contiguous(
+    # (a batch-1 tensor's batch stride is immaterial: e.g. the inner planes of a depth shard)
+    first = 1 if int(z.shape[0]) == 1 else 0
+    if z.stride()[first:] != velocity[: z.shape[0]].stride()[first:] or not (z.is_contiguous() or z.is_contiguous(
             memory_format=torch.channels_last_3d)):
         raise ValueError("z and velocity must be dense with the same memory layout")
     n = z.numel()

@@ -264,12 +264,14 @@ def plan_windows(latent_spatial, roi, overlap) -> WindowPlan:
 def sliding_window_decode_ncdhw(latent: torch.Tensor, weights, *, constructor, roi=CT_ROI, overlap=CT_OVERLAP,
                                 sigma_scale: float = SIGMA_SCALE, scale_factor: float | None = None,
                                 window_filter: Callable[[int], bool] | None = None,
-                                reduce_fn: Callable[[torch.Tensor, torch.Tensor], None] | None = None) -> torch.Tensor:
+                                reduce_fn: Callable[[torch.Tensor, torch.Tensor], bool | None] | None = None
+                                ) -> torch.Tensor | None:
     """``decode.sliding_window_decode_ncdhw`` (``decode.py:187-245``); returns NCDHW fp32 (contiguous).
 
     ``window_filter(i)`` selects the windows this caller decodes and
-    ``reduce_fn(acc, wsum)`` combines the partial blends (the multi-GPU split);
-    by default every window is decoded here.
+    ``reduce_fn(acc, wsum)`` combines the partial blends (the multi-GPU split); when it
+    returns False this caller holds no combined blend and gets None. By default every
+    window is decoded here.
     """
     if len(roi) != 3 or any(int(r) < 1 for r in roi):
         raise ValueError(f"roi must be three positive ints; got {tuple(roi)}")
@@ -310,8 +312,8 @@ def sliding_window_decode_ncdhw(latent: torch.Tensor, weights, *, constructor, r
     if acc is None:  # this caller decoded no window; contribute zeros to the reduction
         acc = torch.zeros((int(x.shape[0]), *out_sp, int(constructor["out_channels"])), dtype=torch.float32, device=dev)
         wsum = torch.zeros(out_sp, dtype=torch.float32, device=dev)
-    if reduce_fn is not None:
-        reduce_fn(acc, wsum)
+    if reduce_fn is not None and reduce_fn(acc, wsum) is False:
+        return None
     crop = [(a * Z_SCALE, n * Z_SCALE - (a + b) * Z_SCALE) for (a, b), n in zip(plan.pads, plan.spatial, strict=True)]
     return ops.window_finalize(acc, wsum, origin=tuple(c[0] for c in crop), extent=tuple(c[1] for c in crop))
 
