@@ -22,6 +22,7 @@
 #include "misc.cuh"
 #include "pack.cuh"
 #include "prepare.cuh"
+#include "launch.cuh"
 
 namespace ctmr {
 int conv_stage_plan(int kc, int bn, bool exact, bool one_cta_per_sm, size_t* smem_bytes);
@@ -149,16 +150,8 @@ int encode_weight_kh(CUtensorMap* map, const void* base, bool bf16, long long cp
 
 bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
 
-int sm_count() {
-  int dev = 0, n = 0;
-  if (cudaGetDevice(&dev) != cudaSuccess || cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess)
-    return 148;
-  return n > 0 ? n : 148;
-}
+int sm_count() { return ctmr::device_sm_count(); }
 
-// Set when the driver rejects the H-before-W tensor view of the persistent kernel; every
-// later convolution then takes the per-tap kernel.
-bool g_v2_unavailable = false;
 constexpr long long kStatsMaxEntries = 512;  // batch x output channels with output statistics
 
 int check_view(const ctmr_tensor& t, const char* name, bool required, bool labels_ok = false) {
@@ -344,8 +337,9 @@ int plan_conv(const ctmr_conv3d_desc* d, ConvPlan* p) {
   const int tcols = std::max(32, next_pow2(p->bn * (p->exact ? 3 : 1)));
   const int stages_probe = ctmr::conv_stage_plan(p->kc, p->bn, p->exact, tcols > 256, &smem_probe);
   const int per_sm = (stages_probe >= 2 && smem_probe + 1024 <= 114 * 1024) ? 2 : 1;
-  const long long wave = 148LL * per_sm;
-  if (p->mode != ctmr::kModeUp2 && ctas < 148) {
+  const long long sms = sm_count();
+  const long long wave = sms * per_sm;
+  if (p->mode != ctmr::kModeUp2 && ctas < sms) {
     long long want = wave / ctas;  // whole splits per wave: no second, nearly empty wave
     want = std::min<long long>(want, n_iter / 4);
     if (want >= 2) p->ksplit = static_cast<int>(want);
@@ -389,8 +383,6 @@ int bias_row_stride(const ctmr_conv3d_desc* d) {
   return static_cast<int>(d->bias_row_stride > 0 ? d->bias_row_stride : d->out_channels);
 }
 
-bool g_khcat_unavailable = false;  // a tensor map for the kh-concatenated kernel was refused once
-
 struct KhPlan {
   int kc, mt, stages;
   size_t smem;
@@ -399,7 +391,7 @@ struct KhPlan {
 // The kh-concatenated kernel: 16-bit stride-1 3x3x3 convolutions with at most 64
 // output channels (three taps side by side fill an N = 3 x C_out MMA).
 bool plan_khcat(const ConvPlan& p, const ctmr_conv3d_desc* d, KhPlan* k) {
-  if (p.exact || p.mode != ctmr::kModeConv3 || p.opad > 64 || d->stats != nullptr || g_khcat_unavailable ||
+  if (p.exact || p.mode != ctmr::kModeConv3 || p.opad > 64 || d->stats != nullptr ||
       p.row_w < 8 || p.row_h < 8 || getenv("CTMR_DISABLE_KHCAT") != nullptr)
     return false;
   // Two depth tiles share each weight box (measured faster than one depth with two accumulator
@@ -421,7 +413,7 @@ bool plan_khcat(const ConvPlan& p, const ctmr_conv3d_desc* d, KhPlan* k) {
 }
 
 bool plan_v2(const ConvPlan& p, const ctmr_conv3d_desc* d, bool with_stats, V2Plan* v) {
-  if (p.exact || g_v2_unavailable ||
+  if (p.exact ||
       !(p.mode == ctmr::kModeConv3 || p.mode == ctmr::kModeUp2 || p.mode == ctmr::kModeConv1) || p.row_w < 16 ||
       p.row_h < 8 || getenv("CTMR_DISABLE_V2") != nullptr)
     return false;
@@ -744,7 +736,8 @@ int ctmr_conv3d_stages(const ctmr_conv3d_desc* d, void* workspace, size_t worksp
         cudaError_t e = ctmr::launch_conv3d_khcat(maps, g, kh.kc, kh.mt, sm_count(), kh.smem, stream);
         return e == cudaSuccess ? CTMR_OK : cuda_fail(e, "conv3d kh-concatenated launch");
       }
-      g_khcat_unavailable = true;  // fall through to the other kernels
+      // A refused tensor map depends on this call's pointers and strides only: this call falls
+      // through to the other kernels, later calls try again.
     }
   }
   if (plan_v2(p, d, with_stats, &v2)) {
@@ -803,7 +796,8 @@ int ctmr_conv3d_stages(const ctmr_conv3d_desc* d, void* workspace, size_t worksp
           cudaError_t e = ctmr::launch_conv3d_umma_v2(maps, g, kc, mt, tw, sm_count(), smem2, stream);
           return e == cudaSuccess ? CTMR_OK : cuda_fail(e, "conv3d v2 launch");
         }
-        g_v2_unavailable = true;  // fall through to the per-tap kernel
+        // Refused for this call's pointers or strides: this call takes the per-tap kernel (which
+        // cannot produce output statistics); later calls try again.
         if (with_stats) return fail(CTMR_ERR_UNSUPPORTED, "persistent kernel unavailable for output statistics");
       }
     }

@@ -299,7 +299,7 @@ cudaError_t launch_typed(const NarrowParams& p, cudaStream_t stream) {
   if (e != cudaSuccess) return e;
   // Depth chunks: about two CTAs per SM over the whole grid, so one wave.
   const int cols = ((p.w + kTW - 1) / kTW) * ((p.h + kTH - 1) / kTH) * p.batch;
-  int per_col = (2 * 148) / cols;
+  int per_col = (2 * device_sm_count()) / cols;
   if (per_col < 1) per_col = 1;
   const int chunk_d = (p.d + per_col - 1) / per_col;
   const int chunks = (p.d + chunk_d - 1) / chunk_d;

@@ -17,13 +17,18 @@
 //     is rejected with CTMR_ERR_WORKSPACE before anything is launched.
 //   * The first call on a device looks up the array's device address with
 //     cudaGetSymbolAddress while that device is current (once per device, then
-//     cached). Make that first call before any stream capture.
+//     cached). Make that first call before any stream capture. The cache
+//     remembers the CUDA context the address belongs to (its process-unique
+//     id): after cudaDeviceReset the next call on that device, in the new
+//     context, looks the address up again instead of using the stale one.
 //   * Every call on a device shares the same array, which keeps the last
 //     call's contents. Nothing in it has to start at zero: the preparation pass
 //     writes every byte the GEMM then reads. Calls whose kernels overlap on the
 //     GPU (different streams without ordering between them) race on the array
 //     and must not be issued.
 //   * Nothing here calls cudaMalloc, cudaFree or any allocating routine.
+#include <cuda.h>
+#include <cudaTypedefs.h>
 #include <cuda_runtime.h>
 
 #include <mutex>
@@ -46,19 +51,46 @@ static __device__ __align__(256) unsigned char g_noalloc_scratch[kNoAllocScratch
 
 std::mutex g_scratch_mutex;
 void* g_scratch_ptr[kMaxDevices] = {};
+unsigned long long g_scratch_ctx[kMaxDevices] = {};  // id of the context each address belongs to
 
-// Device address of the scratch array on the current device (looked up once per device).
+template <typename Fn>
+Fn driver_entry(const char* name, int version) {
+  void* p = nullptr;
+  cudaDriverEntryPointQueryResult q{};
+  if (cudaGetDriverEntryPointByVersion(name, &p, version, cudaEnableDefault, &q) != cudaSuccess ||
+      q != cudaDriverEntryPointSuccess)
+    return nullptr;
+  return reinterpret_cast<Fn>(p);
+}
+
+// Process-unique id of the current device's CUDA context (cuCtxGetId), 0 if unavailable.
+unsigned long long current_context_id() {
+  static const PFN_cuCtxGetCurrent_v4000 get_current = driver_entry<PFN_cuCtxGetCurrent_v4000>("cuCtxGetCurrent", 4000);
+  static const PFN_cuCtxGetId_v12000 get_id = driver_entry<PFN_cuCtxGetId_v12000>("cuCtxGetId", 12000);
+  CUcontext ctx = nullptr;
+  unsigned long long id = 0;
+  if (get_current == nullptr || get_id == nullptr || get_current(&ctx) != CUDA_SUCCESS || ctx == nullptr ||
+      get_id(ctx, &id) != CUDA_SUCCESS)
+    return 0;
+  return id;
+}
+
+// Device address of the scratch array on the current device: looked up once per device and
+// context. Before the runtime's first call on a device there is no current context yet (id 0);
+// cudaGetSymbolAddress creates it, and its id is read afterwards.
 int scratch_for_current_device(void** out) {
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices)
     return ctmr::set_last_error(CTMR_ERR_CUDA, "conv3d_noalloc: no usable current CUDA device");
   std::lock_guard<std::mutex> lock(g_scratch_mutex);
-  if (g_scratch_ptr[dev] == nullptr) {
+  unsigned long long ctx = current_context_id();
+  if (g_scratch_ptr[dev] == nullptr || ctx == 0 || ctx != g_scratch_ctx[dev]) {
     void* ptr = nullptr;
     const cudaError_t e = cudaGetSymbolAddress(&ptr, g_noalloc_scratch);
     if (e != cudaSuccess || ptr == nullptr)
       return ctmr::set_last_error(CTMR_ERR_CUDA, "conv3d_noalloc: cudaGetSymbolAddress of the static scratch failed");
     g_scratch_ptr[dev] = ptr;
+    g_scratch_ctx[dev] = ctx != 0 ? ctx : current_context_id();
   }
   *out = g_scratch_ptr[dev];
   return CTMR_OK;

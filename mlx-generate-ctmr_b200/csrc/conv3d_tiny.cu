@@ -198,7 +198,7 @@ cudaError_t launch_tiny_conv(const TinyParams& p, cudaStream_t stream) {
   // About three blocks per SM over the whole grid (each stages the weights once).
   const long long groups = static_cast<long long>((p.cout + kOG - 1) / kOG) * p.batch;
   long long blocks = (vox + kTile - 1) / kTile;
-  const long long cap = (148LL * 3 + groups - 1) / groups;
+  const long long cap = (3LL * device_sm_count() + groups - 1) / groups;
   if (blocks > cap) blocks = cap;
   const dim3 grid(static_cast<unsigned>(blocks), static_cast<unsigned>((p.cout + kOG - 1) / kOG),
                   static_cast<unsigned>(p.batch));

@@ -403,7 +403,7 @@ cudaError_t launch_conv3d_umma(const ConvMaps& maps, const ConvGeom& g, int kc, 
   if (e != cudaSuccess || g.ksplit == 1) return e;
   const long long total = static_cast<long long>(g.batch) * g.row_d * g.row_h * g.row_w * ((g.cout + 3) / 4);
   long long blocks = (total + 255) / 256;
-  if (blocks > 148LL * 16) blocks = 148LL * 16;
+  if (blocks > 16LL * device_sm_count()) blocks = 16LL * device_sm_count();
   launch_kernel(splitk_reduce_kernel, static_cast<unsigned>(blocks), 256, 0, stream, g);
   return cudaGetLastError();
 }

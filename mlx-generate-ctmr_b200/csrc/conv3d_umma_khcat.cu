@@ -124,7 +124,7 @@ __device__ __forceinline__ float4 kh_load4(const ConvGeom& g, long long res_off,
   if (g.res_bf16) {
     const uint16_t* r = static_cast<const uint16_t*>(g.res) + res_off;
     if (cnt == 4 && (reinterpret_cast<uintptr_t>(r) & 7) == 0) {
-      const uint2 q = __ldg(reinterpret_cast<const uint2*>(r));
+      const uint2 q = __ldcg(reinterpret_cast<const uint2*>(r));
       x[0] = bf16_to_f32(static_cast<uint16_t>(q.x & 0xFFFFu));
       x[1] = bf16_to_f32(static_cast<uint16_t>(q.x >> 16));
       x[2] = bf16_to_f32(static_cast<uint16_t>(q.y & 0xFFFFu));
@@ -136,10 +136,10 @@ __device__ __forceinline__ float4 kh_load4(const ConvGeom& g, long long res_off,
     }
   } else {
     const float* r = static_cast<const float*>(g.res) + res_off;
-    if (cnt == 4 && (reinterpret_cast<uintptr_t>(r) & 15) == 0) return __ldg(reinterpret_cast<const float4*>(r));
+    if (cnt == 4 && (reinterpret_cast<uintptr_t>(r) & 15) == 0) return __ldcg(reinterpret_cast<const float4*>(r));
 #pragma unroll
     for (int e = 0; e < 4; ++e)
-      if (e < cnt) x[e] = __ldg(r + e);
+      if (e < cnt) x[e] = __ldcg(r + e);
   }
   return make_float4(x[0], x[1], x[2], x[3]);
 }
@@ -455,7 +455,9 @@ __global__ void __launch_bounds__(kKhThreads, 1)
             q[k].w += bq.w;
           }
           if (g.res != nullptr) {
-            // All eight residual reads go out before the first store (a store may alias them).
+            // All eight residual reads go out before the first store. The residual is read through
+            // L2 (ld.global.cg), not the read-only path: an in-place residual add (residual == output)
+            // stays defined, each lane reading its addresses before it writes them.
             float4 rv[8];
 #pragma unroll
             for (int k = 0; k < 8; ++k) {

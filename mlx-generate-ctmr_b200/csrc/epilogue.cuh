@@ -16,7 +16,9 @@ __device__ __forceinline__ uint32_t pack_bf16x2(float a, float b) {
   return *reinterpret_cast<uint32_t*>(&h);
 }
 
-// Add the residual and store 16 output columns [n, n+16) of one voxel row.
+// Add the residual and store 16 output columns [n, n+16) of one voxel row. Residual loads go
+// through L2 (ld.global.cg), not the read-only path, so an in-place residual add (residual ==
+// output, each element read before it is written) is defined.
 __device__ __forceinline__ void store_row16(const ConvGeom& g, float (&v)[16], int n, long long out_off,
                                             long long res_off) {
   const int cnt = min(16, g.cout - n);
@@ -25,8 +27,8 @@ __device__ __forceinline__ void store_row16(const ConvGeom& g, float (&v)[16], i
     if (g.res_bf16) {
       const uint16_t* r = static_cast<const uint16_t*>(g.res) + res_off;
       if (cnt == 16 && (reinterpret_cast<uintptr_t>(r) & 15) == 0) {
-        const uint4 q0 = __ldg(reinterpret_cast<const uint4*>(r));
-        const uint4 q1 = __ldg(reinterpret_cast<const uint4*>(r) + 1);
+        const uint4 q0 = __ldcg(reinterpret_cast<const uint4*>(r));
+        const uint4 q1 = __ldcg(reinterpret_cast<const uint4*>(r) + 1);
         const uint32_t w[8] = {q0.x, q0.y, q0.z, q0.w, q1.x, q1.y, q1.z, q1.w};
 #pragma unroll
         for (int i = 0; i < 8; ++i) {
@@ -43,7 +45,7 @@ __device__ __forceinline__ void store_row16(const ConvGeom& g, float (&v)[16], i
       if (cnt == 16 && (reinterpret_cast<uintptr_t>(r) & 15) == 0) {
 #pragma unroll
         for (int i = 0; i < 4; ++i) {
-          const float4 q = __ldg(reinterpret_cast<const float4*>(r) + i);
+          const float4 q = __ldcg(reinterpret_cast<const float4*>(r) + i);
           v[4 * i] += q.x;
           v[4 * i + 1] += q.y;
           v[4 * i + 2] += q.z;
@@ -52,7 +54,7 @@ __device__ __forceinline__ void store_row16(const ConvGeom& g, float (&v)[16], i
       } else {
 #pragma unroll
         for (int i = 0; i < 16; ++i)
-          if (i < cnt) v[i] += __ldg(r + i);
+          if (i < cnt) v[i] += __ldcg(r + i);
       }
     }
   }
@@ -144,7 +146,7 @@ __device__ __forceinline__ void res_issue64(const ConvGeom& g, int n, long long 
     if (cnt == 64 && (reinterpret_cast<uintptr_t>(r) & 15) == 0) {
 #pragma unroll
       for (int i = 0; i < 8; ++i) {
-        const uint4 q = __ldg(reinterpret_cast<const uint4*>(r) + i);
+        const uint4 q = __ldcg(reinterpret_cast<const uint4*>(r) + i);
         w[4 * i] = q.x;
         w[4 * i + 1] = q.y;
         w[4 * i + 2] = q.z;
@@ -163,7 +165,7 @@ __device__ __forceinline__ void res_issue64(const ConvGeom& g, int n, long long 
     if (cnt == 64 && (reinterpret_cast<uintptr_t>(r) & 15) == 0) {
 #pragma unroll
       for (int i = 0; i < 16; ++i) {
-        const uint4 q = __ldg(reinterpret_cast<const uint4*>(r) + i);
+        const uint4 q = __ldcg(reinterpret_cast<const uint4*>(r) + i);
         w[4 * i] = q.x;
         w[4 * i + 1] = q.y;
         w[4 * i + 2] = q.z;
@@ -171,7 +173,7 @@ __device__ __forceinline__ void res_issue64(const ConvGeom& g, int n, long long 
       }
     } else {
 #pragma unroll
-      for (int i = 0; i < 64; ++i) w[i] = i < cnt ? __float_as_uint(__ldg(r + i)) : 0u;
+      for (int i = 0; i < 64; ++i) w[i] = i < cnt ? __float_as_uint(__ldcg(r + i)) : 0u;
     }
   }
 }

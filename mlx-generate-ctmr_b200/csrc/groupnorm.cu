@@ -417,10 +417,8 @@ int gn_max_chunks(int batch) { return (2 * 296 + batch - 1) / batch; }
 // second, partial wave measured slower than fewer, longer blocks).
 int gn_chunks_for(int batch, long long voxels, int channels) {
   static const int wave = [] {
-    int dev = 0, sms = 0, per_sm = 0;
-    if (cudaGetDevice(&dev) != cudaSuccess ||
-        cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || sms < 1)
-      sms = 148;
+    const int sms = device_sm_count();
+    int per_sm = 0;
     if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, gn_partial_kernel, kGnThreads, 1024) != cudaSuccess ||
         per_sm < 1)
       per_sm = 1;

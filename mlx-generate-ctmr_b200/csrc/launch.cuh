@@ -14,6 +14,7 @@
 
 #include <cuda_runtime.h>
 
+#include <atomic>
 #include <cstdlib>
 #include <utility>
 
@@ -21,6 +22,22 @@ namespace ctmr {
 
 __device__ __forceinline__ void griddep_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
 __device__ __forceinline__ void griddep_launch_dependents() { asm volatile("griddepcontrol.launch_dependents;"); }
+
+// Streaming multiprocessors of the current device: the unit every grid-size plan of this
+// library is measured in (148 on a B200). Queried once per device.
+inline int device_sm_count() {
+  static std::atomic<int> cached[64];
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0) return 148;
+  if (dev < 64) {
+    const int hit = cached[dev].load(std::memory_order_relaxed);
+    if (hit > 0) return hit;
+  }
+  int n = 0;
+  if (cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || n < 1) return 148;
+  if (dev < 64) cached[dev].store(n, std::memory_order_relaxed);
+  return n;
+}
 
 inline bool pdl_enabled() {
   static const bool on = std::getenv("CTMR_DISABLE_PDL") == nullptr;

@@ -111,7 +111,7 @@ __global__ void rflow_step_kernel(const float* z, const float* __restrict__ vel,
 
 unsigned grid_for(long long total, int threads) {
   long long blocks = (total + threads - 1) / threads;
-  if (blocks > 148LL * 32) blocks = 148LL * 32;
+  if (blocks > 32LL * device_sm_count()) blocks = 32LL * device_sm_count();
   if (blocks < 1) blocks = 1;
   return static_cast<unsigned>(blocks);
 }

@@ -83,7 +83,7 @@ cudaError_t launch_pack_weight(const float* w, int O, int C, int k, int upsample
   const int taps = upsample ? 64 : k * k * k;
   const long long total = static_cast<long long>(taps) * opad * cpad;
   long long blocks = (total + 255) / 256;
-  if (blocks > 148LL * 32) blocks = 148LL * 32;
+  if (blocks > 32LL * device_sm_count()) blocks = 32LL * device_sm_count();
   if (blocks < 1) blocks = 1;
   launch_kernel(pack_weight_kernel, static_cast<unsigned>(blocks), 256, 0, stream, w, O, C, k, upsample, opad, cpad, kind,
                 out, out_lo, channels_last);

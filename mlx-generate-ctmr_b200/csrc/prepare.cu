@@ -532,10 +532,8 @@ bool vec_ok(const PrepParams& p, int vec) {
 // Blocks of `kern` resident on the whole GPU at once (SMs x blocks per SM).
 template <typename K>
 long long resident_blocks(K kern, int threads, size_t smem) {
-  int dev = 0, sms = 0, per_sm = 0;
-  if (cudaGetDevice(&dev) != cudaSuccess ||
-      cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || sms < 1)
-    sms = 148;
+  const int sms = device_sm_count();
+  int per_sm = 0;
   if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, threads, smem) != cudaSuccess || per_sm < 1)
     per_sm = 1;
   return static_cast<long long>(sms) * per_sm;
@@ -837,7 +835,7 @@ cudaError_t launch_prepare(const PrepParams& p, cudaStream_t stream) {
     return launch_tri_fast(p, stream);
   const int threads = 256;
   long long blocks = (total + threads - 1) / threads;
-  if (blocks > 148LL * 16) blocks = 148LL * 16;
+  if (blocks > 16LL * device_sm_count()) blocks = 16LL * device_sm_count();
   const bool fast = p.out_kind == kPrepOutBF16 || p.out_kind == kPrepOutF16;
   const dim3 grid(static_cast<unsigned>(blocks));
   const unsigned vo = static_cast<unsigned>(vox_out);
@@ -884,7 +882,7 @@ cudaError_t launch_im2col(const PrepParams& p, int cin, int kdense, cudaStream_t
   const long long items = static_cast<long long>(p.od) * p.oh * p.ow * (kdense / 8);
   if (items >= (1LL << 31)) return cudaErrorInvalidValue;
   long long blocks = (items + 255) / 256;
-  const long long cap = 148LL * 8 / p.batch + 1;
+  const long long cap = 8LL * device_sm_count() / p.batch + 1;
   if (blocks > cap) blocks = cap;
   const dim3 grid(static_cast<unsigned>(blocks), static_cast<unsigned>(p.batch));
   switch (p.out_kind) {

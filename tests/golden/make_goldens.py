@@ -86,6 +86,8 @@ def catalog(ref_root: Path) -> None:
 
 
 if __name__ == "__main__":
-    root = Path(sys.argv[1]) if len(sys.argv) > 1 else Path("/root/reference")
+    if len(sys.argv) != 2:
+        raise SystemExit("usage: python tests/golden/make_goldens.py <reference project root>")
+    root = Path(sys.argv[1])
     main(root)
     catalog(root)
