@@ -406,8 +406,10 @@ def run(*, model: str = "mlx-generate-ctmr-mr-brain", output_dir=None, modality:
 
     Without ``unet_weights``/``vae_weights`` the production architectures are
     random-initialised from ``weights_seed`` (no checkpoint download exists
-    here). ``output_dir``, when given, receives ``image.npy`` (int16) and the
-    affine; NIfTI writing is host I/O outside this build.
+    here). ``output_dir``, when given, receives the int16 image as
+    ``synthetic_<configuration>.nii.gz`` with its affine and mm units, the
+    reference's file (``image_runner.py:218, 332-336``), and ``outputs["image"]``
+    is that path.
     """
     if model not in MODELS:
         raise ValueError(f"unknown model {model!r}; supported: {sorted(MODELS)}")
@@ -436,11 +438,11 @@ def run(*, model: str = "mlx-generate-ctmr-mr-brain", output_dir=None, modality:
     if output_dir is not None:
         from pathlib import Path
 
-        path = Path(output_dir)
-        path.mkdir(parents=True, exist_ok=True)
-        np.save(path / "image.npy", result.image)
-        np.save(path / "affine.npy", result.affine)
-        outputs = {"image": str(path / "image.npy")}
+        from .nifti import write_nifti
+
+        destination = Path(output_dir) / f"synthetic_{configuration.replace('-', '_')}.nii.gz"
+        write_nifti(destination, result.image[0, 0], result.affine, xyz_units="mm")
+        outputs = {"image": destination.as_posix()}
     details = {
         "model": model, "configuration": configuration, "modality": mod, "seed": seed, "precision": precision,
         "output_size": list(out_size), "spacing_mm": list(spacing), "num_inference_steps": num_inference_steps,

@@ -1,7 +1,7 @@
 """Extract the reference's recorded golden vectors into small fixtures under tests/golden/.
 
 Run in a checkout that has the reference project (read-only) at REFERENCE_ROOT:
-    python tests/golden/make_goldens.py [REFERENCE_ROOT]
+    python tests/golden/make_goldens.py REFERENCE_ROOT
 It copies, without modification, the recorded inputs/outputs of the reference's
 own test fixtures (``tests/fixtures/darwin-arm64``) that pin this build's hot
 path, plus each fixture's weight recipe (seed, skip, shapes), from which the
