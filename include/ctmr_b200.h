@@ -63,8 +63,11 @@ enum {
  *   (`_nax_conv.py:27-35`).
  * CTMR_PRECISION_BF16: bf16 operands, fp32 accumulation.
  * CTMR_PRECISION_FP16: fp16 operands (needs |value| < 65504), fp32 accumulation;
- *   the same tensor-core rate as bf16 with 3 more mantissa bits. */
-enum { CTMR_PRECISION_FP32 = 0, CTMR_PRECISION_BF16 = 1, CTMR_PRECISION_FP16 = 2 };
+ *   the same tensor-core rate as bf16 with 3 more mantissa bits.
+ * CTMR_PRECISION_TF32: operands rounded to TF32 (fp32 range, 10 mantissa bits,
+ *   stored as fp32), fp32 accumulation, at half the 16-bit tensor-core rate: the
+ *   TF32-input mode beside the reference's exact mode. */
+enum { CTMR_PRECISION_FP32 = 0, CTMR_PRECISION_BF16 = 1, CTMR_PRECISION_FP16 = 2, CTMR_PRECISION_TF32 = 3 };
 
 /* An NDHWC activation view. data == NULL means "absent". */
 typedef struct ctmr_tensor {
@@ -129,8 +132,15 @@ typedef struct ctmr_conv3d_desc {
  * Replaces the shapes of `pack_weight` / `pack_upsample_weight` (`_nax_conv.py:391-445`). */
 CTMR_API size_t ctmr_packed_weight_elems(int out_channels, int in_channels, int kernel_size, int upsample);
 
+/* Bytes of one packed-weight plane in `precision`: 2 x ctmr_packed_weight_elems in the 16-bit
+ * and split modes; for CTMR_PRECISION_TF32, taps x round16(O) x round8(C) fp32 values. The
+ * size counterpart of `pack_weight` (`_nax_conv.py:391-404`) per precision; 0 when invalid. */
+CTMR_API size_t ctmr_packed_weight_bytes(int out_channels, int in_channels, int kernel_size, int upsample,
+                                         int precision);
+
 /* Pack an fp32 Torch-layout weight (device pointer). bf16 for CTMR_PRECISION_BF16,
- * fp16 for CTMR_PRECISION_FP16 (packed_lo unused), fp16 hi/lo planes for CTMR_PRECISION_FP32.
+ * fp16 for CTMR_PRECISION_FP16, TF32-rounded fp32 for CTMR_PRECISION_TF32 (packed_lo
+ * unused), fp16 hi/lo planes for CTMR_PRECISION_FP32.
  * Replaces `pack_weight` (`_nax_conv.py:391-404`) and, with upsample = 1,
  * `pack_upsample_weight` (`_nax_conv.py:407-445`). */
 CTMR_API int ctmr_pack_weight(const float* weight, int out_channels, int in_channels, int kernel_size, int upsample,

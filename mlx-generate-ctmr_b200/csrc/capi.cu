@@ -188,6 +188,7 @@ struct ConvPlan {
   int row_d, row_h, row_w;  // GEMM rows
   int out_d, out_h, out_w;
   bool exact, prepare, bf16, narrow;
+  bool tf32;                // TF32 operands: fp32 rows, channel counts below in 16-bit units (2 per value)
   bool tiny;                // fp32 conv of <= 4 input channels: direct FMA kernel
   bool im2col;              // tiny-input 3x3x3 conv run as a 1x1x1 conv of its im2col rows
   int cin_raw, cpad_src;    // im2col: input channels and the packed weights' channel padding
@@ -216,7 +217,7 @@ int plan_conv(const ctmr_conv3d_desc* d, ConvPlan* p) {
       (d->x2.data != nullptr || d->trilinear || d->avgpool || d->upsample || d->stride != 1 || d->gn_groups > 0))
     return fail(CTMR_ERR_UNSUPPORTED, "a label volume input takes no x2, resampling, stride or in-call GroupNorm");
   if (d->precision != CTMR_PRECISION_FP32 && d->precision != CTMR_PRECISION_BF16 &&
-      d->precision != CTMR_PRECISION_FP16)
+      d->precision != CTMR_PRECISION_FP16 && d->precision != CTMR_PRECISION_TF32)
     return fail(CTMR_ERR_INVALID, "precision");
   if (d->out_channels <= 0) return fail(CTMR_ERR_INVALID, "out_channels");
   if (d->bias_row_stride != 0 && (d->bias_row_stride < d->out_channels || d->bias_row_stride > (1LL << 30)))
@@ -245,8 +246,10 @@ int plan_conv(const ctmr_conv3d_desc* d, ConvPlan* p) {
     return fail(CTMR_ERR_INVALID, "pass either an input affine or gn_groups, not both");
   p->exact = d->precision == CTMR_PRECISION_FP32;
   p->bf16 = d->precision == CTMR_PRECISION_BF16;
+  p->tf32 = d->precision == CTMR_PRECISION_TF32;
   p->cin = d->x.channels + (d->x2.data ? d->x2.channels : 0);
-  p->cpad = static_cast<int>(round_up(p->cin, 16));
+  // Operand rows in 16-bit units: 16 values (one 32-byte MMA K step) or, for TF32, 8 fp32 values.
+  p->cpad = p->tf32 ? 2 * static_cast<int>(round_up(p->cin, 8)) : static_cast<int>(round_up(p->cin, 16));
   p->opad = static_cast<int>(round_up(d->out_channels, 16));
   p->kc = p->cpad % 64 == 0 ? 64 : (p->cpad % 32 == 0 ? 32 : 16);
   p->bn = std::min(p->opad, 128);
@@ -296,7 +299,7 @@ int plan_conv(const ctmr_conv3d_desc* d, ConvPlan* p) {
             d->x2.data == nullptr && d->x.dtype == CTMR_DTYPE_F32 &&
             (d->residual.data == nullptr || (d->residual.dtype == CTMR_DTYPE_F32 && !d->residual_upsampled)) &&
             d->y_dtype == CTMR_DTYPE_F32 && getenv("CTMR_DISABLE_TINY") == nullptr;
-  p->im2col = !p->narrow && !p->tiny && p->mode == ctmr::kModeConv3 && p->cin <= 4 && !d->trilinear &&
+  p->im2col = !p->narrow && !p->tiny && !p->tf32 && p->mode == ctmr::kModeConv3 && p->cin <= 4 && !d->trilinear &&
               !d->avgpool && d->x2.data == nullptr && getenv("CTMR_DISABLE_IM2COL") == nullptr;
   p->cin_raw = p->cin;
   p->cpad_src = p->cpad;
@@ -358,7 +361,7 @@ int plan_conv(const ctmr_conv3d_desc* d, ConvPlan* p) {
     const long long voxels = static_cast<long long>(d->depth) * d->height * d->width;
     if (p->cin % d->gn_groups != 0) return fail(CTMR_ERR_INVALID, "gn_groups must divide the input channels");
     if (p->cin > 2048) return fail(CTMR_ERR_UNSUPPORTED, "group_norm supports at most 2048 channels");
-    p->gn_small = p->prepare && !p->im2col && !d->trilinear && !d->avgpool &&
+    p->gn_small = p->prepare && !p->im2col && !p->tf32 && !d->trilinear && !d->avgpool &&
                   ctmr::gn_prepare_small_fits(voxels, p->cin, d->gn_groups) &&
                   getenv("CTMR_GN_FUSED") != nullptr;  // opt-in: slower in the MAISI UNet step (6.39 vs 6.26 ms)
     if (!p->gn_small) {
@@ -473,6 +476,17 @@ size_t ctmr_packed_weight_elems(int out_channels, int in_channels, int kernel_si
   return static_cast<size_t>(taps * round_up(out_channels, 16) * round_up(in_channels, 16));
 }
 
+size_t ctmr_packed_weight_bytes(int out_channels, int in_channels, int kernel_size, int upsample, int precision) {
+  if (precision == CTMR_PRECISION_TF32) {
+    if (out_channels <= 0 || in_channels <= 0 || (kernel_size != 1 && kernel_size != 3)) return 0;
+    const long long taps = upsample ? 64 : static_cast<long long>(kernel_size) * kernel_size * kernel_size;
+    return static_cast<size_t>(taps * round_up(out_channels, 16) * round_up(in_channels, 8) * 4);
+  }
+  if (precision != CTMR_PRECISION_FP32 && precision != CTMR_PRECISION_BF16 && precision != CTMR_PRECISION_FP16)
+    return 0;
+  return 2 * ctmr_packed_weight_elems(out_channels, in_channels, kernel_size, upsample);
+}
+
 namespace {
 int pack_weight_any(const float* weight, int out_channels, int in_channels, int kernel_size, int upsample,
                     int precision, void* packed, void* packed_lo, void* stream, int channels_last) {
@@ -480,15 +494,18 @@ int pack_weight_any(const float* weight, int out_channels, int in_channels, int 
   if (out_channels <= 0 || in_channels <= 0) return fail(CTMR_ERR_INVALID, "channel counts");
   if (kernel_size != 1 && kernel_size != 3) return fail(CTMR_ERR_UNSUPPORTED, "kernel_size must be 1 or 3");
   if (upsample && kernel_size != 3) return fail(CTMR_ERR_UNSUPPORTED, "upsample fold needs a 3x3x3 kernel");
-  if (precision != CTMR_PRECISION_FP32 && precision != CTMR_PRECISION_BF16 && precision != CTMR_PRECISION_FP16)
+  if (precision != CTMR_PRECISION_FP32 && precision != CTMR_PRECISION_BF16 && precision != CTMR_PRECISION_FP16 &&
+      precision != CTMR_PRECISION_TF32)
     return fail(CTMR_ERR_INVALID, "precision");
   const bool split = precision == CTMR_PRECISION_FP32;
   if (split && packed_lo == nullptr) return fail(CTMR_ERR_INVALID, "lo plane missing");
-  const int kind = split ? ctmr::kPackSplitF16 : (precision == CTMR_PRECISION_BF16 ? ctmr::kPackBF16 : ctmr::kPackF16);
+  const bool tf32 = precision == CTMR_PRECISION_TF32;
+  const int kind = split ? ctmr::kPackSplitF16
+                         : (tf32 ? ctmr::kPackTF32 : (precision == CTMR_PRECISION_BF16 ? ctmr::kPackBF16 : ctmr::kPackF16));
   cudaError_t e = ctmr::launch_pack_weight(weight, out_channels, in_channels, kernel_size, upsample,
                                            static_cast<int>(round_up(out_channels, 16)),
-                                           static_cast<int>(round_up(in_channels, 16)), kind, packed, packed_lo,
-                                           static_cast<cudaStream_t>(stream), channels_last);
+                                           static_cast<int>(round_up(in_channels, tf32 ? 8 : 16)), kind, packed,
+                                           packed_lo, static_cast<cudaStream_t>(stream), channels_last);
   return e == cudaSuccess ? CTMR_OK : cuda_fail(e, "pack_weight launch");
 }
 }  // namespace
@@ -667,9 +684,10 @@ int ctmr_conv3d_stages(const ctmr_conv3d_desc* d, void* workspace, size_t worksp
     pp.mode = d->trilinear ? ctmr::kPrepTrilinear : (d->avgpool ? ctmr::kPrepAvgPool : ctmr::kPrepCopy);
     pp.affine = affine;
     pp.silu = d->silu;
-    pp.cpad = p.cpad;
-    pp.out_cstride = p.cpad;
-    pp.out_kind = p.exact ? ctmr::kPrepOutSplitF16 : (p.bf16 ? ctmr::kPrepOutBF16 : ctmr::kPrepOutF16);
+    pp.cpad = p.tf32 ? p.cpad / 2 : p.cpad;  // in output elements (fp32 values for TF32)
+    pp.out_cstride = pp.cpad;
+    pp.out_kind = p.exact ? ctmr::kPrepOutSplitF16
+                          : (p.tf32 ? ctmr::kPrepOutTF32 : (p.bf16 ? ctmr::kPrepOutBF16 : ctmr::kPrepOutF16));
     pp.out = workspace;
     pp.out_lo = p.exact ? static_cast<uint8_t*>(workspace) + p.prep_bytes : nullptr;
     cudaError_t e = p.gn_small ? ctmr::launch_gn_prepare_small(pp, d->gn_gamma, d->gn_beta, d->gn_groups, d->gn_eps,
@@ -703,6 +721,7 @@ int ctmr_conv3d_stages(const ctmr_conv3d_desc* d, void* workspace, size_t worksp
     g.stages = kh.stages;
     g.tmem_cols = 512;
     g.operand_bf16 = p.bf16 ? 1 : 0;
+    g.operand_tf32 = p.tf32 ? 1 : 0;
     g.ksplit = 1;
     g.n_tiles = 1;
     const long long total = static_cast<long long>(g.tiles_w) * g.tiles_h * g.tiles_d * d->batch;
@@ -760,6 +779,7 @@ int ctmr_conv3d_stages(const ctmr_conv3d_desc* d, void* workspace, size_t worksp
       g.stages = stages2;
       g.tmem_cols = static_cast<uint32_t>(std::max(32, next_pow2(2 * mt * bn)));
       g.operand_bf16 = p.bf16 ? 1 : 0;
+    g.operand_tf32 = p.tf32 ? 1 : 0;
       g.ksplit = 1;
       g.n_tiles = (p.opad + bn - 1) / bn;
       const long long total = static_cast<long long>(g.n_tiles) * g.tiles_w * g.tiles_h * g.tiles_d * d->batch *
@@ -843,6 +863,7 @@ int ctmr_conv3d_stages(const ctmr_conv3d_desc* d, void* workspace, size_t worksp
   g.out_d = p.out_d, g.out_h = p.out_h, g.out_w = p.out_w;
   g.lo_scale = 1.0f / 2048.0f;
   g.operand_bf16 = p.bf16 ? 1 : 0;
+    g.operand_tf32 = p.tf32 ? 1 : 0;
 
   // 3. TMA descriptors.
   ctmr::ConvMaps maps;

@@ -174,7 +174,9 @@ __global__ void __launch_bounds__(kThreads, 1)
     // chunk into fp32 registers with round-to-nearest adds while the next chunk
     // accumulates. This bounds how long the tensor core's own fp32 accumulation
     // runs, whose rounding error otherwise grows with K (27 * C_in products).
-    const uint32_t idesc = idesc_f16(!EXACT && g.operand_bf16 != 0, kRows, static_cast<uint32_t>(g.bn));
+    const uint32_t idesc = idesc_f16(!EXACT && g.operand_bf16 != 0, kRows, static_cast<uint32_t>(g.bn),
+                                           !EXACT && g.operand_tf32 != 0);
+    const bool tf32 = !EXACT && g.operand_tf32 != 0;
     const uint32_t bn = static_cast<uint32_t>(g.bn);
     const uint32_t acc_lo = tmem + 2u * bn;
     const int T = EXACT ? g.chunk_iters : n_iter;
@@ -200,8 +202,8 @@ __global__ void __launch_bounds__(kThreads, 1)
       const uint32_t acc_hi = tmem + static_cast<uint32_t>(buf) * bn;
 #pragma unroll
       for (int k = 0; k < kSteps; ++k) {
-        const uint32_t koff = static_cast<uint32_t>(k) * 32u;  // 16 fp16/bf16 = 32 B along K
-        umma_f16(acc_hi, smem_desc_kmajor(a_hi + koff, kRowBytes), smem_desc_kmajor(b_hi + koff, kRowBytes),
+        const uint32_t koff = static_cast<uint32_t>(k) * 32u;  // 16 fp16/bf16 (8 tf32) = 32 B along K
+        umma_any(tf32, acc_hi, smem_desc_kmajor(a_hi + koff, kRowBytes), smem_desc_kmajor(b_hi + koff, kRowBytes),
                  idesc, (chunk_start && k == 0) ? 0u : 1u);
         if (EXACT) {
           umma_f16(acc_lo, smem_desc_kmajor(a_hi + koff, kRowBytes), smem_desc_kmajor(b_lo + koff, kRowBytes),

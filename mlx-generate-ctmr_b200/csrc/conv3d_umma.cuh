@@ -38,6 +38,7 @@ struct ConvGeom {
   uint32_t tmem_cols;
   int chunk_iters;              // EXACT: K iterations per promoted accumulator chunk
   int operand_bf16;             // single-plane modes: 1 bf16 operands, 0 fp16 operands
+  int operand_tf32;             // single-plane mode with TF32 operands (fp32 rows; kind::tf32 MMAs)
   int n_tiles;                  // persistent kernel: N tiles per M tile
   int total_tiles;              // persistent kernel: all (M tile, N tile) pairs
   int ksplit;                   // per-tap kernel: K iterations split over grid.z (fp32 partial planes)

@@ -293,7 +293,8 @@ __global__ void __launch_bounds__(kKhThreads, 1)
     }
   } else if (warp == 1 && lane == 0) {
     // ------------------------------------------------------------ MMA issuer
-    const uint32_t idesc = idesc_f16(g.operand_bf16 != 0, 128, n3);
+    const uint32_t idesc = idesc_f16(g.operand_bf16 != 0, 128, n3, g.operand_tf32 != 0);
+    const bool tf32 = g.operand_tf32 != 0;
     int ia = 0;
     int ib = 0;
     int lt = 0;
@@ -336,7 +337,7 @@ __global__ void __launch_bounds__(kKhThreads, 1)
             const uint32_t a_win = a_base + static_cast<uint32_t>(m) * L.a_m_bytes + static_cast<uint32_t>(kw) * L.kw_bytes;
 #pragma unroll
             for (int k = 0; k < kSteps; ++k) {
-              umma_f16(acc0 + static_cast<uint32_t>(m) * n3, smem_desc_kmajor(a_win + k * 32u, kRowBytes),
+              umma_any(tf32, acc0 + static_cast<uint32_t>(m) * n3, smem_desc_kmajor(a_win + k * 32u, kRowBytes),
                        smem_desc_kmajor(b_base + k * 32u, kRowBytes), idesc, (first && k == 0) ? 0u : 1u);
             }
           }

@@ -163,7 +163,8 @@ __global__ void __launch_bounds__(kThreadsV2, 1)
     }
   } else if (warp == 1 && lane == 0) {
     // ------------------------------------------------------------ MMA issuer
-    const uint32_t idesc = idesc_f16(g.operand_bf16 != 0, 128, bn);
+    const uint32_t idesc = idesc_f16(g.operand_bf16 != 0, 128, bn, g.operand_tf32 != 0);
+    const bool tf32 = g.operand_tf32 != 0;
     int it = 0;
     int lt = 0;
     for (int t = blockIdx.x; t < g.total_tiles && !*abort_flag; t += gridDim.x, ++lt) {
@@ -193,7 +194,7 @@ __global__ void __launch_bounds__(kThreadsV2, 1)
               const uint32_t a_addr = a_base + static_cast<uint32_t>(m) * L.a_m_bytes +
                                       static_cast<uint32_t>(kw) * L.atom_bytes + static_cast<uint32_t>(k) * 32u;
               const uint32_t b_addr = b_base + static_cast<uint32_t>(kw) * L.b_tap_bytes + static_cast<uint32_t>(k) * 32u;
-              umma_f16(acc0 + static_cast<uint32_t>(m) * bn, smem_desc_kmajor(a_addr, kRowBytes),
+              umma_any(tf32, acc0 + static_cast<uint32_t>(m) * bn, smem_desc_kmajor(a_addr, kRowBytes),
                        smem_desc_kmajor(b_addr, kRowBytes), idesc, (st == 0 && kw == 0 && k == 0) ? 0u : 1u);
             }
           }

@@ -1,7 +1,7 @@
 // Weight packing for the implicit-GEMM convolution: Torch (O, C, k, k, k) fp32,
 // or the channels-last (O, k, k, k, C) of released checkpoints, -> K-major taps
-// [T][O_pad][C_pad] in bf16 or fp16, or in fp16 hi/lo planes for the split-fp32
-// mode. Counterpart of `pack_weight` / `pack_upsample_weight`
+// [T][O_pad][C_pad] in bf16 or fp16, TF32-rounded fp32, or in fp16 hi/lo planes for
+// the split-fp32 mode. Counterpart of `pack_weight` / `pack_upsample_weight`
 // (`_nax_conv.py:391-445`), with the tap-major rows transposed to the K-major
 // operand layout the tensor cores read.
 //
@@ -17,6 +17,7 @@
 
 #include "pack.cuh"
 #include "launch.cuh"
+#include "ptx.cuh"
 
 namespace ctmr {
 namespace {
@@ -70,6 +71,8 @@ __global__ void pack_weight_kernel(const float* __restrict__ w, int O, int C, in
       static_cast<__half*>(out_lo)[i] = lo;
     } else if (kind == kPackF16) {
       static_cast<__half*>(out)[i] = __float2half_rn(v);
+    } else if (kind == kPackTF32) {
+      static_cast<float*>(out)[i] = round_tf32(v);
     } else {
       static_cast<__nv_bfloat16*>(out)[i] = __float2bfloat16_rn(v);
     }

@@ -5,7 +5,8 @@
 
 namespace ctmr {
 
-enum PackKind : int { kPackBF16 = 0, kPackSplitF16 = 1, kPackF16 = 2 };
+// kPackTF32: fp32 values rounded to TF32 (cpad then counts fp32 values).
+enum PackKind : int { kPackBF16 = 0, kPackSplitF16 = 1, kPackF16 = 2, kPackTF32 = 3 };
 
 // `channels_last`: the source is (O, k, k, k, C) (the channels-last layout of
 // released checkpoints) instead of Torch's (O, C, k, k, k).

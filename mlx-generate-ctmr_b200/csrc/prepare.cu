@@ -18,6 +18,7 @@
 
 #include "prepare.cuh"
 #include "launch.cuh"
+#include "ptx.cuh"
 
 namespace ctmr {
 namespace {
@@ -153,11 +154,14 @@ __device__ __forceinline__ void store8(const PrepParams& p, long long oidx, int 
   } else {
     float* o = static_cast<float*>(p.out) + oidx;
     const int n = min(8, p.cpad - c0);
+    float r[8];
+#pragma unroll
+    for (int i = 0; i < 8; ++i) r[i] = p.out_kind == kPrepOutTF32 ? round_tf32(out[i]) : out[i];
     if (n == 8 && (reinterpret_cast<uintptr_t>(o) & 15) == 0) {
-      reinterpret_cast<float4*>(o)[0] = make_float4(out[0], out[1], out[2], out[3]);
-      reinterpret_cast<float4*>(o)[1] = make_float4(out[4], out[5], out[6], out[7]);
+      reinterpret_cast<float4*>(o)[0] = make_float4(r[0], r[1], r[2], r[3]);
+      reinterpret_cast<float4*>(o)[1] = make_float4(r[4], r[5], r[6], r[7]);
     } else {
-      for (int i = 0; i < n; ++i) o[i] = out[i];
+      for (int i = 0; i < n; ++i) o[i] = r[i];
     }
   }
 }
@@ -311,10 +315,13 @@ __device__ __forceinline__ uint32_t fdiv(const FastDiv& f, uint32_t n) {
 template <int OUTK, int N>
 __device__ __forceinline__ void store_vec(const PrepParams& p, long long oidx, const float (&v)[N]) {
   static_assert(N == 4 || N == 8, "4 or 8 channels");
-  if (OUTK == kPrepOutF32) {
+  if (OUTK == kPrepOutF32 || OUTK == kPrepOutTF32) {
     float4* o = reinterpret_cast<float4*>(static_cast<float*>(p.out) + oidx);
+    float r[N];
 #pragma unroll
-    for (int i = 0; i < N / 4; ++i) o[i] = make_float4(v[4 * i], v[4 * i + 1], v[4 * i + 2], v[4 * i + 3]);
+    for (int i = 0; i < N; ++i) r[i] = OUTK == kPrepOutTF32 ? round_tf32(v[i]) : v[i];
+#pragma unroll
+    for (int i = 0; i < N / 4; ++i) o[i] = make_float4(r[4 * i], r[4 * i + 1], r[4 * i + 2], r[4 * i + 3]);
   } else {
     uint32_t hw[N / 2], lw[N / 2];
 #pragma unroll
@@ -522,7 +529,7 @@ bool vec_ok(const PrepParams& p, int vec) {
     if (s.channels == 0) continue;
     if (s.bf16 || s.channels % vec || s.cstride % 4 || !aligned16(s.ptr)) return false;
   }
-  const int obytes = p.out_kind == kPrepOutF32 ? 4 : 2;
+  const int obytes = (p.out_kind == kPrepOutF32 || p.out_kind == kPrepOutTF32) ? 4 : 2;
   if (p.cpad % vec || (p.out_cstride * obytes) % 16 || !aligned16(p.out)) return false;
   if (p.out_kind == kPrepOutSplitF16 && !aligned16(p.out_lo)) return false;
   if (p.affine != nullptr && !aligned16(p.affine)) return false;
@@ -553,6 +560,7 @@ cudaError_t launch_copy_fast(const PrepParams& p, cudaStream_t stream) {
     case kPrepOutBF16: launch_kernel(prepare_copy_kernel<kPrepOutBF16, true>, grid, 256, 0, stream, p, q, vox); break;
     case kPrepOutF16: launch_kernel(prepare_copy_kernel<kPrepOutF16, true>, grid, 256, 0, stream, p, q, vox); break;
     case kPrepOutSplitF16: launch_kernel(prepare_copy_kernel<kPrepOutSplitF16, false>, grid, 256, 0, stream, p, q, vox); break;
+    case kPrepOutTF32: launch_kernel(prepare_copy_kernel<kPrepOutTF32, true>, grid, 256, 0, stream, p, q, vox); break;
     default: launch_kernel(prepare_copy_kernel<kPrepOutF32, false>, grid, 256, 0, stream, p, q, vox); break;
   }
   return cudaGetLastError();
@@ -573,6 +581,7 @@ cudaError_t launch_tri_fast(const PrepParams& p, cudaStream_t stream) {
     case kPrepOutBF16: launch_kernel(prepare_tri_kernel<kPrepOutBF16>, grid, 128, 0, stream, p, q, xd, yd, n); break;
     case kPrepOutF16: launch_kernel(prepare_tri_kernel<kPrepOutF16>, grid, 128, 0, stream, p, q, xd, yd, n); break;
     case kPrepOutSplitF16: launch_kernel(prepare_tri_kernel<kPrepOutSplitF16>, grid, 128, 0, stream, p, q, xd, yd, n); break;
+    case kPrepOutTF32: launch_kernel(prepare_tri_kernel<kPrepOutTF32>, grid, 128, 0, stream, p, q, xd, yd, n); break;
     default: launch_kernel(prepare_tri_kernel<kPrepOutF32>, grid, 128, 0, stream, p, q, xd, yd, n); break;
   }
   return cudaGetLastError();
@@ -836,7 +845,7 @@ cudaError_t launch_prepare(const PrepParams& p, cudaStream_t stream) {
   const int threads = 256;
   long long blocks = (total + threads - 1) / threads;
   if (blocks > 16LL * device_sm_count()) blocks = 16LL * device_sm_count();
-  const bool fast = p.out_kind == kPrepOutBF16 || p.out_kind == kPrepOutF16;
+  const bool fast = p.out_kind == kPrepOutBF16 || p.out_kind == kPrepOutF16 || p.out_kind == kPrepOutTF32;
   const dim3 grid(static_cast<unsigned>(blocks));
   const unsigned vo = static_cast<unsigned>(vox_out);
 #define CTMR_PREP(MODE)                                                         \

@@ -6,7 +6,8 @@
 namespace ctmr {
 
 enum PrepMode : int { kPrepCopy = 0, kPrepTrilinear = 1, kPrepAvgPool = 2 };
-enum PrepOut : int { kPrepOutBF16 = 0, kPrepOutSplitF16 = 1, kPrepOutF32 = 2, kPrepOutF16 = 3 };
+// kPrepOutTF32: fp32 rows of values rounded to TF32 (the kind::tf32 operand).
+enum PrepOut : int { kPrepOutBF16 = 0, kPrepOutSplitF16 = 1, kPrepOutF32 = 2, kPrepOutF16 = 3, kPrepOutTF32 = 4 };
 
 struct PrepSource {
   const void* ptr;       // NDHWC rows, `cstride` elements apart

@@ -39,6 +39,14 @@ __device__ __forceinline__ uint64_t global_timer_ns() {
 
 __device__ __forceinline__ void flag_error(unsigned bits) { atomicOr(&g_device_error, bits); }
 
+// fp32 rounded to the TF32 grid (10 mantissa bits; nearest, ties away from zero), in fp32 layout:
+// the operand the tensor cores read in kind::tf32.
+__device__ __forceinline__ float round_tf32(float v) {
+  uint32_t r;
+  asm("cvt.rna.tf32.f32 %0, %1;" : "=r"(r) : "f"(v));
+  return __uint_as_float(r);
+}
+
 // ---------------------------------------------------------------- mbarrier
 __device__ __forceinline__ void mbar_init(uint64_t* bar, uint32_t count) {
   asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count) : "memory");
@@ -143,6 +151,25 @@ __device__ __forceinline__ void umma_f16(uint32_t d_tmem, uint64_t a_desc, uint6
       : "memory");
 }
 
+// D[tmem] (+)= A[smem desc] * B[smem desc]^T, kind::tf32 (TF32 inputs stored as fp32, fp32 accumulate).
+// Each instruction consumes 32 bytes of K per row (8 TF32 values), as kind::f16 does (16 values).
+__device__ __forceinline__ void umma_tf32(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc, uint32_t idesc,
+                                          uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::tf32 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
+      "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+
+// The 16-bit or the TF32 product of the same operand bytes (`tf32` is uniform across a launch).
+__device__ __forceinline__ void umma_any(bool tf32, uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc,
+                                         uint32_t idesc, uint32_t accumulate) {
+  if (tf32) umma_tf32(d_tmem, a_desc, b_desc, idesc, accumulate);
+  else umma_f16(d_tmem, a_desc, b_desc, idesc, accumulate);
+}
+
 // Arrive on an mbarrier once every previously issued tcgen05.mma of this thread completes.
 __device__ __forceinline__ void umma_commit(uint64_t* bar) {
   asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
@@ -177,11 +204,12 @@ __device__ __forceinline__ uint64_t smem_desc_kmajor(uint32_t saddr, uint32_t ro
   return d;
 }
 
-// Instruction descriptor for kind::f16, fp32 accumulate, both operands K-major.
-__host__ __device__ constexpr uint32_t idesc_f16(bool bf16, uint32_t m, uint32_t n) {
-  return (1u << 4)                              // D = f32
-         | ((bf16 ? 1u : 0u) << 7)              // A format
-         | ((bf16 ? 1u : 0u) << 10)             // B format
+// Instruction descriptor for kind::f16 / kind::tf32, fp32 accumulate, both operands K-major.
+// Operand format: 0 fp16, 1 bf16, 2 tf32.
+__host__ __device__ constexpr uint32_t idesc_f16(bool bf16, uint32_t m, uint32_t n, bool tf32 = false) {
+  return (1u << 4)                                           // D = f32
+         | ((tf32 ? 2u : (bf16 ? 1u : 0u)) << 7)             // A format
+         | ((tf32 ? 2u : (bf16 ? 1u : 0u)) << 10)            // B format
          | ((n >> 3) << 17) | ((m >> 4) << 24);
 }
 

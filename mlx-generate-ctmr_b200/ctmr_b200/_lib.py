@@ -25,6 +25,7 @@ DTYPE_LABEL8 = 3  # conv input only: int16 label ids read as 8 bit-plane channel
 PRECISION_FP32 = 0
 PRECISION_BF16 = 1
 PRECISION_FP16 = 2
+PRECISION_TF32 = 3
 TRANSFORM_COPY = 0
 TRANSFORM_TRILINEAR = 1
 TRANSFORM_AVGPOOL = 2
@@ -34,6 +35,7 @@ CONV_GEMM = 2
 # Every symbol the header declares; tests check the library exports all of them.
 EXPORTED_SYMBOLS = (
     "ctmr_packed_weight_elems",
+    "ctmr_packed_weight_bytes",
     "ctmr_pack_weight",
     "ctmr_pack_weight_channels_last",
     "ctmr_attention_d32",
@@ -140,6 +142,7 @@ def _load() -> ctypes.CDLL:
     vp, i, ll, sz, f = ctypes.c_void_p, ctypes.c_int, ctypes.c_longlong, ctypes.c_size_t, ctypes.c_float
     protos = {
         "ctmr_packed_weight_elems": (sz, [i, i, i, i]),
+        "ctmr_packed_weight_bytes": (sz, [i, i, i, i, i]),
         "ctmr_pack_weight": (i, [vp, i, i, i, i, i, vp, vp, vp]),
         "ctmr_pack_weight_channels_last": (i, [vp, i, i, i, i, i, vp, vp, vp]),
         "ctmr_attention_d32": (i, [vp, i, i, i, i, ctypes.c_float, vp, vp]),

@@ -10,6 +10,8 @@ Precision (request-scoped, like the reference's ``arithmetic_mode``):
   ``"fp32"`` (default) — convolutions in the split-fp16 "exact" mode (fp32
       accumulation, ~2^-22 relative product error), the reference's default
       arithmetic.
+  ``"tf32"`` — TF32 tensor-core operands (fp32 range, 10 mantissa bits) with
+      fp32 accumulation and epilogue, at half the 16-bit rate; dense ops in fp32.
   ``"bf16"`` / ``"fp16"`` — bf16 or fp16 tensor-core operands with fp32
       accumulation and fp32 epilogue additions (same tensor-core rate; fp16
       carries 3 more mantissa bits and needs |value| < 65504, like the split
@@ -49,7 +51,7 @@ _precision: ContextVar[str] = ContextVar("ctmr_b200_precision", default="fp32")
 
 @contextlib.contextmanager
 def arithmetic_precision(precision: str) -> Generator[None]:
-    """Select ``"fp32"`` or ``"bf16"`` for calls made inside the block (restored on exit)."""
+    """Select ``"fp32"``, ``"tf32"``, ``"bf16"`` or ``"fp16"`` for calls made inside the block (restored on exit)."""
     if precision not in ops.PRECISIONS:
         raise ValueError(f"precision must be one of {ops.PRECISIONS}; got {precision!r}")
     token = _precision.set(precision)
@@ -166,7 +168,8 @@ def _stacked_dense(tensors: tuple[torch.Tensor, ...], dtype: torch.dtype) -> tor
 
 def dense_dtype() -> torch.dtype:
     """Operand type of the dense (non-conv) tensor-core ops: fp32, or the 16-bit mode's type."""
-    return {"fp32": torch.float32, "bf16": torch.bfloat16, "fp16": torch.float16}[_precision.get()]
+    return {"fp32": torch.float32, "tf32": torch.float32, "bf16": torch.bfloat16,
+            "fp16": torch.float16}[_precision.get()]
 
 
 # At or above this many output voxels a <= 4-output-channel conv runs faster on the
@@ -178,7 +181,7 @@ NARROW_DIRECT_VOXELS = 1 << 21
 
 def _pack(weight: torch.Tensor, *, upsample: bool = False, out_voxels: int = 0) -> ops.PackedWeight:
     precision = conv_precision(weight)
-    if precision == "fp16" and int(weight.shape[0]) <= 4 and out_voxels >= NARROW_DIRECT_VOXELS:
+    if precision in ("fp16", "tf32") and int(weight.shape[0]) <= 4 and out_voxels >= NARROW_DIRECT_VOXELS:
         precision = "fp32"
     key = (id(weight), upsample, precision)
     hit = _packed.get(key)

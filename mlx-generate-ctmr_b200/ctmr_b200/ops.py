@@ -20,7 +20,7 @@ from ._lib import LIB, check
 
 F32 = torch.float32
 BF16 = torch.bfloat16
-PRECISIONS = ("fp32", "bf16", "fp16")
+PRECISIONS = ("fp32", "bf16", "fp16", "tf32")
 
 # Instrumentation: LAUNCHES counts the library's kernel launches issued from
 # Python; when PROFILE is a list, conv3d and group_norm_affine append one record
@@ -71,6 +71,8 @@ def _precision_code(precision: str) -> int:
         return _lib.PRECISION_BF16
     if precision == "fp16":
         return _lib.PRECISION_FP16
+    if precision == "tf32":
+        return _lib.PRECISION_TF32
     raise ValueError(f"precision must be one of {PRECISIONS}; got {precision!r}")
 
 
@@ -210,6 +212,10 @@ def pack_weight(weight: torch.Tensor, precision: str, *, upsample: bool = False)
     if precision == "fp32":
         hi = torch.empty(n, dtype=torch.float16, device=w.device)
         lo = torch.empty(n, dtype=torch.float16, device=w.device)
+    elif precision == "tf32":  # TF32-rounded fp32 rows of round8(C) values
+        hi = torch.empty(int(LIB.ctmr_packed_weight_bytes(o, c, k, int(upsample), code)) // 4, dtype=F32,
+                         device=w.device)
+        lo = None
     else:
         hi = torch.empty(n, dtype=BF16 if precision == "bf16" else torch.float16, device=w.device)
         lo = None

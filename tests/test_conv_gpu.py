@@ -9,7 +9,8 @@ The bf16 mode rounds both operands to bf16 (relative rounding error RMS about
 2^-9 each), which alone puts a single convolution's rel-L2 near 2e-3; a lone
 conv is therefore held to 4e-3, while whole blocks (where the fp32 residual
 dominates) are held to the stated 2e-3 in the block tests. fp16 operands carry
-3 more mantissa bits: 6e-4 per conv.
+3 more mantissa bits: 6e-4 per conv; TF32 operands (10 mantissa bits, fp32 range) are held
+to the fp16 bar.
 """
 
 from __future__ import annotations
@@ -64,7 +65,7 @@ def test_conv_fp32_matches_float64(cuda, shape, out_channels, stride):
     _close_fp32(y, expected)
 
 
-@pytest.mark.parametrize("precision", ["bf16", "fp16"])
+@pytest.mark.parametrize("precision", ["bf16", "fp16", "tf32"])
 @pytest.mark.parametrize(("shape", "out_channels", "stride"), SHAPES)
 def test_conv_16bit_matches_float64(cuda, shape, out_channels, stride, precision):
     from ctmr_b200 import ops
@@ -147,7 +148,7 @@ V2_SHAPES = [
 ]
 
 
-@pytest.mark.parametrize("precision", ["fp16", "bf16"])
+@pytest.mark.parametrize("precision", ["fp16", "bf16", "tf32"])
 @pytest.mark.parametrize(("shape", "out_channels", "upsample"), V2_SHAPES)
 def test_persistent_kernel_shapes(cuda, shape, out_channels, upsample, precision):
     """16-bit stride-1 convs on grids with W >= 16 and H >= 8 run a persistent kernel (the
@@ -169,7 +170,7 @@ def test_persistent_kernel_shapes(cuda, shape, out_channels, upsample, precision
     xin = ops_ref.upsample_nearest_ref(x.double()) if upsample else x.double()
     expected = ops_ref.conv3d_ref(xin, w.double(), bias.double()) + res.double()
     err = ops_ref.rel_l2(y.cpu(), expected)
-    assert err <= (FP16_CONV_REL_L2 if precision == "fp16" else BF16_CONV_REL_L2), f"{precision} rel-L2 {err:.3e}"
+    assert err <= (FP16_CONV_REL_L2 if precision in ("fp16", "tf32") else BF16_CONV_REL_L2), f"{precision} rel-L2 {err:.3e}"
 
 
 KHCAT_SHAPES = [
@@ -182,7 +183,7 @@ KHCAT_SHAPES = [
 
 
 @pytest.mark.parametrize("depths", ["1", "2"])
-@pytest.mark.parametrize("precision", ["fp16", "bf16"])
+@pytest.mark.parametrize("precision", ["fp16", "bf16", "tf32"])
 @pytest.mark.parametrize(("shape", "out_channels"), KHCAT_SHAPES)
 def test_kh_concatenated_kernel(cuda, shape, out_channels, precision, depths, monkeypatch):
     """16-bit stride-1 3x3x3 convs with <= 64 output channels run the kh-concatenated kernel (the
@@ -211,7 +212,7 @@ def test_kh_concatenated_kernel(cuda, shape, out_channels, precision, depths, mo
     torch.cuda.synchronize()
     expected = ops_ref.conv3d_ref(x.double(), w.double(), bias.double()) + res.double()
     err = ops_ref.rel_l2(y.cpu(), expected)
-    assert err <= (FP16_CONV_REL_L2 if precision == "fp16" else BF16_CONV_REL_L2), f"{precision} rel-L2 {err:.3e}"
+    assert err <= (FP16_CONV_REL_L2 if precision in ("fp16", "tf32") else BF16_CONV_REL_L2), f"{precision} rel-L2 {err:.3e}"
     # Same rounded operands, fp32 sums in another order: the two kernels agree to fp32 rounding,
     # and do not agree bitwise (which would mean the route switch changed nothing).
     diff = ops_ref.rel_l2(y.cpu(), y_v2.cpu().double())
@@ -261,7 +262,7 @@ def test_kh_concatenated_residual_forms(cuda, out_channels, monkeypatch):
         assert not torch.equal(y, y_v2)
 
 
-@pytest.mark.parametrize("precision", ["fp16", "bf16"])
+@pytest.mark.parametrize("precision", ["fp16", "bf16", "tf32"])
 @pytest.mark.parametrize(("shape", "x2_channels", "out_channels"), [
     ((2, 64, 3, 12, 24), 128, 64),   # skip 1x1 over cat(hidden, skip): partial tiles, two sources
     ((1, 128, 4, 16, 32), 0, 64),    # VAE shortcut class
@@ -286,7 +287,7 @@ def test_persistent_pointwise_conv(cuda, shape, x2_channels, out_channels, preci
     xin = torch.cat([x, x2], dim=1) if x2 is not None else x
     expected = ops_ref.conv3d_ref(xin.double(), w.double(), bias.double(), padding=0) + res.double()
     err = ops_ref.rel_l2(y.cpu(), expected)
-    assert err <= (FP16_CONV_REL_L2 if precision == "fp16" else BF16_CONV_REL_L2), f"{precision} rel-L2 {err:.3e}"
+    assert err <= (FP16_CONV_REL_L2 if precision in ("fp16", "tf32") else BF16_CONV_REL_L2), f"{precision} rel-L2 {err:.3e}"
 
 
 @pytest.mark.parametrize("precision", ["fp32", "fp16"])
@@ -325,7 +326,7 @@ def test_tiny_input_im2col(cuda, shape, out_channels, norm, precision):
         assert ops_ref.rel_l2(y.cpu(), expected) <= FP16_CONV_REL_L2
 
 
-@pytest.mark.parametrize("precision", ["fp32", "fp16"])
+@pytest.mark.parametrize("precision", ["fp32", "fp16", "tf32"])
 def test_splitk_reduction_epilogue(cuda, precision):
     """A deep, small grid (2 x 256 x 4^3) splits K across CTAs; the reduction adds the
     per-batch bias and the residual before the single rounding."""
@@ -538,7 +539,7 @@ def test_transform_fp16_output(cuda):
     assert torch.equal(y16, y32.to(torch.float16))
 
 
-@pytest.mark.parametrize("precision", ["fp32", "bf16", "fp16"])
+@pytest.mark.parametrize("precision", ["fp32", "bf16", "fp16", "tf32"])
 @pytest.mark.parametrize(("o", "c", "k", "upsample"), [(48, 64, 3, False), (32, 16, 3, True), (20, 24, 3, False)])
 def test_channels_last_weight_packs_identically(cuda, o, c, k, upsample, precision):
     """A weight stored channels-last (O, k, k, k, C) — a released checkpoint's layout, seen through
@@ -554,6 +555,37 @@ def test_channels_last_weight_packs_identically(cuda, o, c, k, upsample, precisi
     torch.cuda.synchronize()
     assert torch.equal(a.hi, b.hi)
     assert (a.lo is None and b.lo is None) or torch.equal(a.lo, b.lo)
+
+
+def _round_tf32_host(a: np.ndarray) -> np.ndarray:
+    """fp32 -> TF32 (10 mantissa bits), nearest with ties away from zero, as fp32 bits."""
+    u = a.astype(np.float32).view(np.uint32).astype(np.uint64)
+    return ((u + 0x1000) & 0xFFFFE000).astype(np.uint32).view(np.float32)
+
+
+def test_tf32_weights_and_operands(cuda):
+    """TF32 mode: the packed weights are the fp32 weights rounded to TF32 at the K-major
+    [tap][O16][C8] positions, and a conv whose 20 input channels fill no whole 16-value row
+    (8-value TF32 rows, zero padded) meets the fp16 bar against float64."""
+    from ctmr_b200 import ops
+
+    rng = np.random.default_rng(23)
+    w = (rng.standard_normal((24, 20, 3, 3, 3)) / np.sqrt(27 * 20)).astype(np.float32)
+    packed = ops.pack_weight(torch.from_numpy(w).to(cuda), "tf32")
+    torch.cuda.synchronize()
+    assert packed.hi.dtype == torch.float32 and packed.hi.numel() == 27 * 32 * 24
+    got = packed.hi.cpu().numpy().reshape(27, 32, 24)
+    want = np.zeros((27, 32, 24), dtype=np.float32)
+    want[:, :24, :20] = _round_tf32_host(w.reshape(24, 20, 27).transpose(2, 0, 1))
+    np.testing.assert_array_equal(got, want)
+    x = rng.standard_normal((2, 20, 6, 12, 16)).astype(np.float32)
+    b = rng.standard_normal(24).astype(np.float32)
+    y = ops.conv3d(ops.to_ndhwc(torch.from_numpy(x).to(cuda)), packed, torch.from_numpy(b).to(cuda))
+    torch.cuda.synchronize()
+    expected = ops_ref.conv3d_ref(torch.from_numpy(x).double(), torch.from_numpy(w).double(),
+                                  torch.from_numpy(b).double())
+    err = ops_ref.rel_l2(y.cpu(), expected)
+    assert err <= FP16_CONV_REL_L2, f"tf32 rel-L2 {err:.3e}"
 
 
 def test_decoder_from_a_native_checkpoint(cuda, tmp_path):
