@@ -59,12 +59,12 @@ def _args():
     p.add_argument("--steps", type=int, default=2)
     p.add_argument("--warmup", type=int, default=3)
     p.add_argument("--impl", choices=("ours", "reference"), default="ours")
-    p.add_argument("--precision", choices=("fp16", "bf16", "fp32"), default="fp16")
+    p.add_argument("--precision", choices=("fp16", "bf16", "tf32", "fp32"), default="fp16")
     p.add_argument("--mode", choices=("replicas", "partition"), default="replicas",
                    help="N > 1: independent volumes per GPU (the partition is timed beside them), or all N GPUs "
                         "on one volume as the headline")
     p.add_argument("--no-fp32-line", action="store_true",
-                   help="N = 1: skip the fp32-mode volume rate printed beside a 16-bit headline")
+                   help="N = 1: skip the fp32- and tf32-mode volume rates printed beside the headline")
     p.add_argument("--no-graph", action="store_true")
     p.add_argument("--no-cpu-baseline", action="store_true")
     p.add_argument("--case", choices=("volume", "sweep", "conv", "gn", "unet-step", "vae-window", "breakdown"),
@@ -671,14 +671,19 @@ def main() -> None:
     head = run.measure(args.steps, args.warmup, clocks=True)
     run.release()
 
-    # The precision-matched line: the reference's own arithmetic is FP32 (split-fp16 "exact" products).
-    fp32 = None
-    if world == 1 and args.precision != "fp32" and not args.no_fp32_line:
-        run32 = VolumeRun("fp32", group=None, **common)
-        m = run32.measure(args.steps, args.warmup)
-        run32.release()
-        fp32 = {"value": round(m["value"], 3), "unit": UNIT, "ms_per_step": round(m["ms"], 2), "e2e": m["e2e"],
-                "gpu_launches": int(m["launches"]), "dtype": "fp32 (split-fp16 operands, 3 products)"}
+    # The precision-matched line (the reference's own arithmetic is FP32: split-fp16 "exact" products)
+    # and the TF32-input mode's line, beside a 16-bit headline.
+    other_modes = {}
+    if world == 1 and not args.no_fp32_line:
+        for mode, dtype in (("fp32", "fp32 (split-fp16 operands, 3 products)"),
+                            ("tf32", "tf32 (TF32-rounded operands, fp32 accumulation)")):
+            if mode == args.precision:
+                continue
+            run_m = VolumeRun(mode, group=None, **common)
+            m = run_m.measure(args.steps, args.warmup)
+            run_m.release()
+            other_modes[mode] = {"value": round(m["value"], 3), "unit": UNIT, "ms_per_step": round(m["ms"], 2),
+                                 "e2e": m["e2e"], "gpu_launches": int(m["launches"]), "dtype": dtype}
 
     # The north-star partition beside the replicas: all N GPUs on one volume.
     partition = None
@@ -703,8 +708,7 @@ def main() -> None:
             "e2e": head["e2e"], "gpu_launches": int(head["launches"]), "clocks": head["clocks"],
             "roofline": roofline, "cpu_baseline": base,
         }
-        if fp32 is not None:
-            line["fp32"] = fp32
+        line.update(other_modes)
         if partition is not None:
             line["partition"] = partition
         print(json.dumps(line), flush=True)
