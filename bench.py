@@ -67,7 +67,8 @@ def _args():
                    help="N = 1: skip the fp32- and tf32-mode volume rates printed beside the headline")
     p.add_argument("--no-graph", action="store_true")
     p.add_argument("--no-cpu-baseline", action="store_true")
-    p.add_argument("--case", choices=("volume", "sweep", "conv", "gn", "unet-step", "vae-window", "breakdown"),
+    p.add_argument("--case", choices=("volume", "sweep", "conv", "gn", "unet-step", "vae-window", "breakdown",
+                                      "attention"),
                    default="volume",
                    help="volume: the benchmark; sweep: the reference's conv-kernel sweep (TFLOP/s per shape); "
                         "conv / unet-step / vae-window: one kernel shape, one UNet step or one decode window "
@@ -406,6 +407,52 @@ def _time_groupnorm(shape: tuple[int, ...], iters: int, dev: torch.device) -> No
         del g
 
 
+def _time_attention(iters: int, dev: torch.device) -> None:
+    """Head-size-32 attention of the UNet's attention levels (batch 2: 2048 tokens x 8 heads, 256 x 16)
+    on this library's kernel and on torch's SDPA backends, each captured in a CUDA graph and replayed
+    ``iters`` times between CUDA events (inputs stay L2-resident: a kernel comparison)."""
+    import torch.nn.functional as F
+    from torch.nn.attention import SDPBackend, sdpa_kernel
+
+    from ctmr_b200 import ops
+
+    for length, heads in ((2048, 8), (256, 16)):
+        gen = torch.Generator(device=dev).manual_seed(0)
+        qkv = torch.randn((2, length, 3 * heads * 32), device=dev, generator=gen).to(torch.float16)
+        q, k, v = (t.reshape(2, length, heads, 32).transpose(1, 2) for t in qkv.chunk(3, dim=-1))
+        scale = 32 ** -0.5
+        runs = {"ctmr_attention_d32": lambda: ops.attention_d32(qkv, heads, scale)}
+        for name, backend in (("cudnn", SDPBackend.CUDNN_ATTENTION), ("flash", SDPBackend.FLASH_ATTENTION)):
+            def call(backend=backend):
+                with sdpa_kernel([backend]):
+                    return F.scaled_dot_product_attention(q, k, v, scale=scale)
+            runs[name] = call
+        for name, fn in runs.items():
+            try:
+                for _ in range(3):
+                    fn()
+                torch.cuda.synchronize(dev)
+                g = torch.cuda.CUDAGraph()
+                with torch.cuda.graph(g):
+                    for _ in range(iters):
+                        fn()
+                g.replay()
+                torch.cuda.synchronize(dev)
+                e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                e0.record()
+                g.replay()
+                e1.record()
+                torch.cuda.synchronize(dev)
+                us = e0.elapsed_time(e1) * 1e3 / iters
+                print(json.dumps({"case": "attention", "impl": name, "batch": 2, "tokens": length, "heads": heads,
+                                  "us": round(us, 2),
+                                  "exp2_per_s": round(2 * heads * length * length / (us * 1e-6) / 1e12, 3)}),
+                      flush=True)
+                del g
+            except RuntimeError as e:
+                print(json.dumps({"case": "attention", "impl": name, "tokens": length, "error": str(e)[:120]}))
+
+
 def run_case(args) -> None:
     from ctmr_b200 import fast_b200 as A
     from ctmr_b200 import pipeline as P
@@ -425,6 +472,9 @@ def run_case(args) -> None:
                                   "gemm_ms": round(ms, 4), "tflops": round(tflops, 1),
                                   "frac_of_peak": round(tflops / peak, 3), "peak": f"{kind} bf16_tflops {peak}"}),
                       flush=True)
+            return
+        if args.case == "attention":
+            _time_attention(args.iters, dev)
             return
         if args.case == "gn":
             _time_groupnorm(tuple(int(v) for v in args.shape.split(","))[:5], args.iters, dev)

@@ -20,6 +20,14 @@
 // softmax threads' registers: while P_{j+1} is produced, PV_j is folded in as
 // O = O * exp2(m_{j-1} - m_j) + PV_j, so the tensor core and the exponentials
 // overlap. The last step divides by l and stores the row.
+//
+// At head size 32 the pass is bound by the exponentials (B x H x L^2 of them, 16 per clock
+// per SM on the exponential unit), so a quarter of them (keys 24..31 of every 32) are
+// computed on the FMA pipe instead: 2^x = 2^n * p(f) with x = n + f, n the nearest integer
+// (Cody-Waite range reduction with the 1.5 * 2^23 rounding constant, f in [-1/2, 1/2]) and
+// p a degree-3 polynomial fitted to 2^f on [-1/2, 1/2] for least maximum relative error
+// (linear-programming minimax fit; max relative error 7.5e-5, below the fp16 P operand's
+// half-ulp of 4.9e-4), 2^n added into the exponent field.
 #include <cuda_bf16.h>
 #include <cuda_fp16.h>
 #include <cstdint>
@@ -82,6 +90,29 @@ __device__ __forceinline__ uint64_t smem_desc_mn_sw64(uint32_t saddr) {
   return d;
 }
 
+// 2^x on the exponential unit (flushes results below 2^-126 to zero).
+__device__ __forceinline__ float fast_exp2(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+
+// 2^x for x <= 0 on the FMA pipe: x = n + f (n nearest integer, |f| <= 1/2), 2^f by the degree-3
+// minimax polynomial, n added to the exponent. x is clamped at -125 (2^-125 is zero in the P operand).
+constexpr float kExp2C0 = 0.9999280571937561f;
+constexpr float kExp2C1 = 0.6932609677314758f;
+constexpr float kExp2C2 = 0.2426111251115799f;
+constexpr float kExp2C3 = 0.0551716685295105f;
+__device__ __forceinline__ float poly_exp2(float x) {
+  x = fmaxf(x, -125.f);
+  const float j = x + 12582912.f;  // 1.5 * 2^23: the low mantissa bits of j hold round(x)
+  const float f = x - (j - 12582912.f);
+  float p = fmaf(kExp2C3, f, kExp2C2);
+  p = fmaf(p, f, kExp2C1);
+  p = fmaf(p, f, kExp2C0);
+  return __int_as_float(__float_as_int(p) + (__float_as_int(j) << 23));
+}
+
 __device__ __forceinline__ uint32_t pack2(float a, float b, bool bf16) {
   if (bf16) {
     __nv_bfloat162 h = __floats2bfloat162_rn(a, b);
@@ -91,8 +122,10 @@ __device__ __forceinline__ uint32_t pack2(float a, float b, bool bf16) {
   return *reinterpret_cast<uint32_t*>(&h);
 }
 
+// Two CTAs per SM (at most 170 registers per thread): while one waits on its tensor-core
+// products the other's softmax warps keep the exponential unit busy.
 template <bool BF16>
-__global__ void __launch_bounds__(kAttnThreads, 1)
+__global__ void __launch_bounds__(kAttnThreads, 2)
     attention_d32_kernel(const __grid_constant__ CUtensorMap map, AttnParams p) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -215,7 +248,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
       uint32_t r[32];
       tmem_ld32_issue(tmem + lane_addr + (t_o - tmem) + static_cast<uint32_t>(s) * kHead, r);
       tmem_ld32_wait(r);
-      const float f = m_old == -INFINITY ? 0.f : exp2f(m_old - m_new);
+      const float f = m_old == -INFINITY ? 0.f : fast_exp2(m_old - m_new);
 #pragma unroll
       for (int c = 0; c < kHead; ++c) acc[c] = fmaf(acc[c], f, __uint_as_float(r[c]));
       tc_fence_before();
@@ -226,15 +259,17 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
       ok = mbar_wait_bounded(s_full, static_cast<uint32_t>(j) & 1u, kErrWaitAcc) && !*abort_flag;
       if (!ok) break;
       tc_fence_after();
-      // Pass 1: the row maximum over the tile.
+      // Pass 1: the row maximum over the tile (two 32-column loads in flight per wait).
       float mx = -INFINITY;
 #pragma unroll
-      for (int c = 0; c < kRows; c += 32) {
-        uint32_t r[32];
+      for (int c = 0; c < kRows; c += 64) {
+        uint32_t r[32], r2[32];
         tmem_ld32_issue(t_s + lane_addr + static_cast<uint32_t>(c), r);
+        tmem_ld32_issue(t_s + lane_addr + static_cast<uint32_t>(c + 32), r2);
         tmem_ld32_wait(r);
+        tmem_ld32_wait(r2);
 #pragma unroll
-        for (int i = 0; i < 32; ++i) mx = fmaxf(mx, __uint_as_float(r[i]));
+        for (int i = 0; i < 32; ++i) mx = fmaxf(mx, fmaxf(__uint_as_float(r[i]), __uint_as_float(r2[i])));
       }
       const float m_new = fmaxf(m_cur, mx * scale);
       // Pass 2: P = 2^(s * scale - m_new) in the operand type, written swizzled.
@@ -249,8 +284,11 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
         uint32_t w[16];
 #pragma unroll
         for (int i = 0; i < 16; ++i) {
-          const float e0 = exp2f(fmaf(__uint_as_float(r[2 * i]), scale, -m_new));
-          const float e1 = exp2f(fmaf(__uint_as_float(r[2 * i + 1]), scale, -m_new));
+          const float x0 = fmaf(__uint_as_float(r[2 * i]), scale, -m_new);
+          const float x1 = fmaf(__uint_as_float(r[2 * i + 1]), scale, -m_new);
+          // Keys 24..31 of the 32 on the FMA pipe, the rest on the exponential unit.
+          const float e0 = i >= 12 ? poly_exp2(x0) : fast_exp2(x0);
+          const float e1 = i >= 12 ? poly_exp2(x1) : fast_exp2(x1);
           sum += e0 + e1;
           w[i] = pack2(e0, e1, BF16);
         }
@@ -268,7 +306,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
       // P_j is in shared memory: visible to the tensor core's async proxy, then published.
       fence_proxy_async_shared();
       mbar_arrive(&p_full[s]);
-      l = (m_cur == -INFINITY ? 0.f : l * exp2f(m_cur - m_new)) + sum;
+      l = (m_cur == -INFINITY ? 0.f : l * fast_exp2(m_cur - m_new)) + sum;
       // Fold PV_{j-1} (scale m_cur) while PV_j runs.
       if (j >= 1 && !fold(j - 1, m_prev, m_cur)) { ok = false; break; }
       m_prev = m_cur;
