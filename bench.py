@@ -68,7 +68,7 @@ def _args():
     p.add_argument("--no-graph", action="store_true")
     p.add_argument("--no-cpu-baseline", action="store_true")
     p.add_argument("--case", choices=("volume", "sweep", "conv", "gn", "unet-step", "vae-window", "breakdown",
-                                      "attention"),
+                                      "attention", "ct"),
                    default="volume",
                    help="volume: the benchmark; sweep: the reference's conv-kernel sweep (TFLOP/s per shape); "
                         "conv / unet-step / vae-window: one kernel shape, one UNet step or one decode window "
@@ -453,6 +453,61 @@ def _time_attention(iters: int, dev: torch.device) -> None:
                 print(json.dumps({"case": "attention", "impl": name, "tokens": length, "error": str(e)[:120]}))
 
 
+def _time_ct_from_mask(iters: int, dev: torch.device, precision: str) -> None:
+    """The CT-from-mask configuration (C4): a 256^3 int16 label mask, its ControlNet condition embedding
+    (bit planes formed in the first conv), 30 ControlNet-conditioned rflow steps of the production UNet
+    on the 1x4x64^3 latent (one captured CUDA graph per step) and the default-ROI (48,48,64)
+    sliding-window decode to 256^3 with HU mapping: the stages of ``pipeline.sample_ct_from_mask_ncdhw``
+    with the step graph captured once, timed with CUDA events over ``iters`` volumes."""
+    from ctmr_b200 import networks, ops
+    from ctmr_b200 import pipeline as P
+    from ctmr_b200 import weights as W
+
+    unet = W.random_weights(W.unet_shapes(P.PRODUCTION_UNET), seed=0, device=dev)
+    cn = W.random_weights(W.controlnet_shapes(P.PRODUCTION_CONTROLNET), seed=4, device=dev)
+    vae = W.random_weights(W.vae_decoder_shapes(P.PRODUCTION_VAE), seed=1, device=dev)
+    label = torch.from_numpy(P.synthetic_ct_mask(256, 0)).to(dev)
+    shape = (1, 4, 64, 64, 64)
+    timesteps, _ = P.set_timesteps_rflow(num_inference_steps=30, input_img_size_numel=64 ** 3)
+    embedding = networks.encode_controlnet_condition_ncdhw(ops.LabelBits(label), cn,
+                                                            constructor=P.PRODUCTION_CONTROLNET)
+    step = P.ControlNetUNetStep(unet, cn, P.PRODUCTION_UNET, P.PRODUCTION_CONTROLNET, shape,
+                                conditioning_embedding=embedding, class_label=1,
+                                spacing=P.spacing_tensor_ncdhw((1.7, 1.7, 2.0), dev), device=dev)
+    step.prepare()
+    z0 = torch.randn(shape, device=dev).contiguous(memory_format=torch.channels_last_3d)
+
+    def volume():
+        emb = networks.encode_controlnet_condition_ncdhw(ops.LabelBits(label), cn, constructor=P.PRODUCTION_CONTROLNET)
+        step.embedding.copy_(emb)
+        final = step.sample(z0, timesteps)
+        mid = torch.cuda.Event(enable_timing=True)
+        mid.record()
+        dec = P.sliding_window_decode_ncdhw(final, vae, constructor=P.PRODUCTION_VAE, roi=P.CT_ROI,
+                                            overlap=P.CT_OVERLAP, scale_factor=1.0)
+        return P.to_hu_ncdhw(dec, label), mid
+
+    hu, _ = volume()
+    torch.cuda.synchronize(dev)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    mids = []
+    e0.record()
+    for _ in range(iters):
+        hu, mid = volume()
+        mids.append(mid)
+    e1.record()
+    torch.cuda.synchronize(dev)
+    assert torch.isfinite(hu).all()
+    ms = e0.elapsed_time(e1) / iters
+    print(json.dumps({"case": "ct", "precision": precision, "iters": iters,
+                      "workload": "CT from a 256^3 mask: condition embedding + ControlNet + UNet 30 rflow steps on "
+                                  "1x4x64^3 + 4-window (48,48,64) decode to 256^3 + HU",
+                      "ms_per_volume": round(ms, 2), "volumes_per_min": round(60000.0 / ms, 2),
+                      "last_volume_decode_ms": round(mids[-1].elapsed_time(e1), 2),
+                      "timing": "CUDA events around iters back-to-back volumes"}), flush=True)
+    step.release()
+
+
 def run_case(args) -> None:
     from ctmr_b200 import fast_b200 as A
     from ctmr_b200 import pipeline as P
@@ -475,6 +530,9 @@ def run_case(args) -> None:
             return
         if args.case == "attention":
             _time_attention(args.iters, dev)
+            return
+        if args.case == "ct":
+            _time_ct_from_mask(args.iters, dev, args.precision)
             return
         if args.case == "gn":
             _time_groupnorm(tuple(int(v) for v in args.shape.split(","))[:5], args.iters, dev)

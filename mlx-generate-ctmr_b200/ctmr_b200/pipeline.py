@@ -492,6 +492,25 @@ def spacing_tensor_ncdhw(spacing_mm: Sequence[float], device) -> torch.Tensor:
     return torch.tensor([values], dtype=torch.float32, device=device)
 
 
+def synthetic_ct_mask(size: int = 256, seed: int = 0, boxes: int = 48) -> np.ndarray:
+    """A synthetic CT label mask in the shape of the CT-from-mask configuration: a body (label 200)
+    ellipsoid holding ``boxes`` random axis-aligned boxes whose labels are drawn uniformly from
+    0..132; int16 ``(1, 1, size, size, size)``. (The reference's real masks are not available here.)"""
+    rng = np.random.default_rng(seed)
+    ax = (np.arange(size, dtype=np.float32) + 0.5) / size - 0.5
+    d, h, w = np.meshgrid(ax, ax, ax, indexing="ij")
+    body = (d / 0.46) ** 2 + (h / 0.40) ** 2 + (w / 0.44) ** 2 <= 1.0
+    lab = np.where(body, 200, 0).astype(np.int16)
+    for _ in range(boxes):
+        lo = rng.integers(0, size - 8, size=3)
+        ext = rng.integers(8, max(size // 5, 9), size=3)
+        hi = np.minimum(lo + ext, size)
+        box = (slice(lo[0], hi[0]), slice(lo[1], hi[1]), slice(lo[2], hi[2]))
+        inside = lab[box]
+        inside[body[box]] = int(rng.integers(0, 133))
+    return lab[None, None]
+
+
 def to_hu_ncdhw(image: torch.Tensor, label: torch.Tensor) -> torch.Tensor:
     """``clip(x, 0, 1) * 2000 - 1000`` HU with background (label 0) at -1000 (``decode.py:248-259``)."""
     hu = image.clamp(0.0, 1.0) * 2000.0 - 1000.0

@@ -216,21 +216,10 @@ def test_decode_window_at_size(cuda, decode_case, precision):
 
 # ---------------------------------------------------------------- C4: ControlNet + UNet at size
 def c4_label(size: int = 256, seed: int = 0) -> np.ndarray:
-    """Synthetic CT mask: a body (label 200) ellipsoid holding random axis-aligned boxes whose labels are
-    drawn uniformly from 0..132, int16 ``(1, 1, size, size, size)``."""
-    rng = np.random.default_rng(seed)
-    ax = (np.arange(size, dtype=np.float32) + 0.5) / size - 0.5
-    d, h, w = np.meshgrid(ax, ax, ax, indexing="ij")
-    body = (d / 0.46) ** 2 + (h / 0.40) ** 2 + (w / 0.44) ** 2 <= 1.0
-    lab = np.where(body, 200, 0).astype(np.int16)
-    for _ in range(48):
-        lo = rng.integers(0, size - 8, size=3)
-        ext = rng.integers(8, size // 5, size=3)
-        hi = np.minimum(lo + ext, size)
-        box = (slice(lo[0], hi[0]), slice(lo[1], hi[1]), slice(lo[2], hi[2]))
-        inside = lab[box]
-        inside[body[box]] = int(rng.integers(0, 133))
-    return lab[None, None]
+    """The C4 mask (``pipeline.synthetic_ct_mask``): body-200 ellipsoid with 48 random label boxes."""
+    from ctmr_b200 import pipeline as P
+
+    return P.synthetic_ct_mask(size, seed)
 
 
 @pytest.fixture(scope="module")
