@@ -425,6 +425,7 @@ bool plan_v2(const ConvPlan& p, const ctmr_conv3d_desc* d, bool with_stats, V2Pl
   v->bn = std::min(p.opad, 128);
   v->stats_bytes = 0;
   if (with_stats) {
+    if (p.tf32) return false;  // no TF32 instantiation with the statistics epilogue
     // Below 128 output channels the MMA work per tile is too short to hide the
     // statistics reduction in the epilogue; a separate pass is cheaper there.
     if (d->out_channels < 128) return false;

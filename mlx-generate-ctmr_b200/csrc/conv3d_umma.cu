@@ -53,7 +53,7 @@ struct StageLayout {
   }
 };
 
-template <int KC, bool EXACT>
+template <int KC, bool EXACT, bool TF32>
 __global__ void __launch_bounds__(kThreads, 1)
     conv3d_umma_kernel(const __grid_constant__ ConvMaps maps, const __grid_constant__ ConvGeom g) {
   constexpr uint32_t kRowBytes = KC * 2;
@@ -174,9 +174,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     // chunk into fp32 registers with round-to-nearest adds while the next chunk
     // accumulates. This bounds how long the tensor core's own fp32 accumulation
     // runs, whose rounding error otherwise grows with K (27 * C_in products).
-    const uint32_t idesc = idesc_f16(!EXACT && g.operand_bf16 != 0, kRows, static_cast<uint32_t>(g.bn),
-                                           !EXACT && g.operand_tf32 != 0);
-    const bool tf32 = !EXACT && g.operand_tf32 != 0;
+    static_assert(!(EXACT && TF32), "the split mode has fp16 operands");
+    const uint32_t idesc = idesc_f16(!EXACT && g.operand_bf16 != 0, kRows, static_cast<uint32_t>(g.bn), TF32);
     const uint32_t bn = static_cast<uint32_t>(g.bn);
     const uint32_t acc_lo = tmem + 2u * bn;
     const int T = EXACT ? g.chunk_iters : n_iter;
@@ -197,19 +196,16 @@ __global__ void __launch_bounds__(kThreads, 1)
       if (*abort_flag) break;
       tc_fence_after();
       const uint32_t st = smem_u32(smem + static_cast<size_t>(s) * L.stage_bytes);
-      const uint32_t a_hi = st, a_lo = st + L.a_bytes;
-      const uint32_t b_hi = st + L.a_bytes * (EXACT ? 2 : 1), b_lo = b_hi + L.b_bytes;
+      const uint64_t a_hi = smem_desc_kmajor(st, kRowBytes), a_lo = desc_advance(a_hi, L.a_bytes);
+      const uint64_t b_hi = desc_advance(a_hi, L.a_bytes * (EXACT ? 2 : 1)), b_lo = desc_advance(b_hi, L.b_bytes);
       const uint32_t acc_hi = tmem + static_cast<uint32_t>(buf) * bn;
 #pragma unroll
-      for (int k = 0; k < kSteps; ++k) {
-        const uint32_t koff = static_cast<uint32_t>(k) * 32u;  // 16 fp16/bf16 (8 tf32) = 32 B along K
-        umma_any(tf32, acc_hi, smem_desc_kmajor(a_hi + koff, kRowBytes), smem_desc_kmajor(b_hi + koff, kRowBytes),
-                 idesc, (chunk_start && k == 0) ? 0u : 1u);
+      for (int k = 0; k < kSteps; ++k) {  // 32 bytes of K per MMA (16 fp16/bf16, 8 tf32): +2 in the address field
+        const uint32_t kd = 2u * static_cast<uint32_t>(k);
+        umma<TF32>(acc_hi, a_hi + kd, b_hi + kd, idesc, (chunk_start && k == 0) ? 0u : 1u);
         if (EXACT) {
-          umma_f16(acc_lo, smem_desc_kmajor(a_hi + koff, kRowBytes), smem_desc_kmajor(b_lo + koff, kRowBytes),
-                   idesc, (it == 0 && k == 0) ? 0u : 1u);
-          umma_f16(acc_lo, smem_desc_kmajor(a_lo + koff, kRowBytes), smem_desc_kmajor(b_hi + koff, kRowBytes),
-                   idesc, 1u);
+          umma_f16(acc_lo, a_hi + kd, b_lo + kd, idesc, (it == 0 && k == 0) ? 0u : 1u);
+          umma_f16(acc_lo, a_lo + kd, b_hi + kd, idesc, 1u);
         }
       }
       umma_commit(&empty[s]);
@@ -365,7 +361,8 @@ __global__ void splitk_reduce_kernel(const ConvGeom g) {
 template <int KC, bool EXACT>
 static cudaError_t launch_typed(const ConvMaps& maps, const ConvGeom& g, dim3 grid, size_t smem,
                                 cudaStream_t stream) {
-  auto kern = conv3d_umma_kernel<KC, EXACT>;
+  auto kern = EXACT ? conv3d_umma_kernel<KC, EXACT, false>
+                    : (g.operand_tf32 ? conv3d_umma_kernel<KC, EXACT, !EXACT> : conv3d_umma_kernel<KC, EXACT, false>);
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
   if (e != cudaSuccess) return e;
   launch_kernel(kern, grid, kThreads, smem, stream, maps, g);

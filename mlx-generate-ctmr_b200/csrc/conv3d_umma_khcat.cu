@@ -178,7 +178,7 @@ __device__ __forceinline__ void kh_store4(const ConvGeom& g, float4 v, int n, lo
 // tile i + 1) when 2 x MT x 3 x C_out columns fit, else one, released depth by depth.
 __host__ __device__ constexpr int kh_buffers(int mt, int bn) { return 2 * mt * 3 * bn <= 512 ? 2 : 1; }
 
-template <int KC, int MT>
+template <int KC, int MT, bool TF32>
 __global__ void __launch_bounds__(kKhThreads, 1)
     conv3d_khcat_kernel(const __grid_constant__ ConvMaps maps, const __grid_constant__ ConvGeom g) {
   constexpr uint32_t kRowBytes = KC * 2;
@@ -293,8 +293,7 @@ __global__ void __launch_bounds__(kKhThreads, 1)
     }
   } else if (warp == 1 && lane == 0) {
     // ------------------------------------------------------------ MMA issuer
-    const uint32_t idesc = idesc_f16(g.operand_bf16 != 0, 128, n3, g.operand_tf32 != 0);
-    const bool tf32 = g.operand_tf32 != 0;
+    const uint32_t idesc = idesc_f16(g.operand_bf16 != 0, 128, n3, TF32);
     int ia = 0;
     int ib = 0;
     int lt = 0;
@@ -309,7 +308,7 @@ __global__ void __launch_bounds__(kKhThreads, 1)
           break;
         }
         ++ia;
-        const uint32_t a_base = smem_u32(smem + static_cast<size_t>(sa) * L.a_bytes);
+        const uint64_t a_desc0 = smem_desc_kmajor(smem_u32(smem + static_cast<size_t>(sa) * L.a_bytes), kRowBytes);
         for (int kw = 0; kw < 3 && !stop; ++kw) {
           const int s = ib % S;
           if (!mbar_wait_bounded(&full[s], static_cast<uint32_t>(ib / S) & 1u, kErrWaitFull)) {
@@ -318,7 +317,7 @@ __global__ void __launch_bounds__(kKhThreads, 1)
           }
           ++ib;
           tc_fence_after();
-          const uint32_t b_base = smem_u32(b_ring + static_cast<size_t>(s) * L.b_bytes);
+          const uint64_t b_desc = smem_desc_kmajor(smem_u32(b_ring + static_cast<size_t>(s) * L.b_bytes), kRowBytes);
           const bool first = gi == 0 && kw == 0;
 #pragma unroll
           for (int m = 0; m < MT; ++m) {
@@ -334,11 +333,12 @@ __global__ void __launch_bounds__(kKhThreads, 1)
               }
               tc_fence_after();
             }
-            const uint32_t a_win = a_base + static_cast<uint32_t>(m) * L.a_m_bytes + static_cast<uint32_t>(kw) * L.kw_bytes;
+            const uint64_t a_desc = desc_advance(a_desc0, static_cast<uint32_t>(m) * L.a_m_bytes +
+                                                              static_cast<uint32_t>(kw) * L.kw_bytes);
+            const uint32_t d_acc = acc0 + static_cast<uint32_t>(m) * n3;
 #pragma unroll
-            for (int k = 0; k < kSteps; ++k) {
-              umma_any(tf32, acc0 + static_cast<uint32_t>(m) * n3, smem_desc_kmajor(a_win + k * 32u, kRowBytes),
-                       smem_desc_kmajor(b_base + k * 32u, kRowBytes), idesc, (first && k == 0) ? 0u : 1u);
+            for (int k = 0; k < kSteps; ++k) {  // 32 bytes of K per MMA: +2 in the descriptors' address field
+              umma<TF32>(d_acc, a_desc + 2u * k, b_desc + 2u * k, idesc, (first && k == 0) ? 0u : 1u);
             }
           }
           umma_commit(&empty[s]);
@@ -530,7 +530,7 @@ __global__ void __launch_bounds__(kKhThreads, 1)
 
 template <int KC, int MT>
 cudaError_t launch_khcat_typed(const ConvMaps& maps, const ConvGeom& g, int grid, size_t smem, cudaStream_t stream) {
-  auto kern = conv3d_khcat_kernel<KC, MT>;
+  auto kern = g.operand_tf32 ? conv3d_khcat_kernel<KC, MT, true> : conv3d_khcat_kernel<KC, MT, false>;
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
   if (e != cudaSuccess) return e;
   return launch_kernel(kern, grid, kKhThreads, smem, stream, maps, g);

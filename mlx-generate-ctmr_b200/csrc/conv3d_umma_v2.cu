@@ -47,7 +47,7 @@ struct V2Layout {
   }
 };
 
-template <int KC, int MT, int TW, bool STATS>
+template <int KC, int MT, int TW, bool STATS, bool TF32>
 __global__ void __launch_bounds__(kThreadsV2, 1)
     conv3d_umma_v2_kernel(const __grid_constant__ ConvMaps maps, const __grid_constant__ ConvGeom g) {
   constexpr uint32_t kRowBytes = KC * 2;
@@ -163,8 +163,7 @@ __global__ void __launch_bounds__(kThreadsV2, 1)
     }
   } else if (warp == 1 && lane == 0) {
     // ------------------------------------------------------------ MMA issuer
-    const uint32_t idesc = idesc_f16(g.operand_bf16 != 0, 128, bn, g.operand_tf32 != 0);
-    const bool tf32 = g.operand_tf32 != 0;
+    const uint32_t idesc = idesc_f16(g.operand_bf16 != 0, 128, bn, TF32);
     int it = 0;
     int lt = 0;
     for (int t = blockIdx.x; t < g.total_tiles && !*abort_flag; t += gridDim.x, ++lt) {
@@ -184,18 +183,19 @@ __global__ void __launch_bounds__(kThreadsV2, 1)
         }
         tc_fence_after();
         const uint32_t a_base = smem_u32(smem + static_cast<size_t>(s) * L.stage_bytes);
-        const uint32_t b_base = a_base + L.a_bytes;
+        const uint64_t a_desc0 = smem_desc_kmajor(a_base, kRowBytes);
+        const uint64_t b_desc0 = smem_desc_kmajor(a_base + L.a_bytes, kRowBytes);
 #pragma unroll
         for (int m = 0; m < MT; ++m) {
 #pragma unroll
           for (int kw = 0; kw < TW; ++kw) {
+            const uint64_t a_desc = desc_advance(a_desc0, static_cast<uint32_t>(m) * L.a_m_bytes +
+                                                              static_cast<uint32_t>(kw) * L.atom_bytes);
+            const uint64_t b_desc = desc_advance(b_desc0, static_cast<uint32_t>(kw) * L.b_tap_bytes);
 #pragma unroll
-            for (int k = 0; k < kSteps; ++k) {
-              const uint32_t a_addr = a_base + static_cast<uint32_t>(m) * L.a_m_bytes +
-                                      static_cast<uint32_t>(kw) * L.atom_bytes + static_cast<uint32_t>(k) * 32u;
-              const uint32_t b_addr = b_base + static_cast<uint32_t>(kw) * L.b_tap_bytes + static_cast<uint32_t>(k) * 32u;
-              umma_any(tf32, acc0 + static_cast<uint32_t>(m) * bn, smem_desc_kmajor(a_addr, kRowBytes),
-                       smem_desc_kmajor(b_addr, kRowBytes), idesc, (st == 0 && kw == 0 && k == 0) ? 0u : 1u);
+            for (int k = 0; k < kSteps; ++k) {  // 32 bytes of K per MMA: +2 in the descriptors' address field
+              umma<TF32>(acc0 + static_cast<uint32_t>(m) * bn, a_desc + 2u * k, b_desc + 2u * k, idesc,
+                         (st == 0 && kw == 0 && k == 0) ? 0u : 1u);
             }
           }
         }
@@ -353,8 +353,12 @@ __global__ void __launch_bounds__(kThreadsV2, 1)
 
 template <int KC, int MT, int TW>
 cudaError_t launch_v2_typed(const ConvMaps& maps, const ConvGeom& g, int grid, size_t smem, cudaStream_t stream) {
-  // The statistics epilogue is a separate instantiation so the plain kernel keeps its registers.
-  auto kern = g.stats != nullptr ? conv3d_umma_v2_kernel<KC, MT, TW, true> : conv3d_umma_v2_kernel<KC, MT, TW, false>;
+  // The statistics epilogue is a separate instantiation so the plain kernel keeps its registers;
+  // TF32 operands are a third (the planner gives them no statistics).
+  if (g.operand_tf32 && g.stats != nullptr) return cudaErrorInvalidValue;
+  auto kern = g.operand_tf32 ? conv3d_umma_v2_kernel<KC, MT, TW, false, true>
+                             : (g.stats != nullptr ? conv3d_umma_v2_kernel<KC, MT, TW, true, false>
+                                                   : conv3d_umma_v2_kernel<KC, MT, TW, false, false>);
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
   if (e != cudaSuccess) return e;
   return launch_kernel(kern, grid, kThreadsV2, smem, stream, maps, g);

@@ -163,10 +163,12 @@ __device__ __forceinline__ void umma_tf32(uint32_t d_tmem, uint64_t a_desc, uint
       : "memory");
 }
 
-// The 16-bit or the TF32 product of the same operand bytes (`tf32` is uniform across a launch).
-__device__ __forceinline__ void umma_any(bool tf32, uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc,
-                                         uint32_t idesc, uint32_t accumulate) {
-  if (tf32) umma_tf32(d_tmem, a_desc, b_desc, idesc, accumulate);
+// The 16-bit or the TF32 product of the same operand bytes, chosen at compile time: the single
+// issuing thread's instruction stream is on the MMA critical path, so it carries no branch.
+template <bool TF32>
+__device__ __forceinline__ void umma(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc, uint32_t idesc,
+                                     uint32_t accumulate) {
+  if constexpr (TF32) umma_tf32(d_tmem, a_desc, b_desc, idesc, accumulate);
   else umma_f16(d_tmem, a_desc, b_desc, idesc, accumulate);
 }
 
@@ -202,6 +204,13 @@ __device__ __forceinline__ uint64_t smem_desc_kmajor(uint32_t saddr, uint32_t ro
   d |= 1ull << 46;                                                      // descriptor version (sm_100)
   d |= layout << 61;
   return d;
+}
+
+// A descriptor moved `bytes` further into the same swizzled tile: the start address field holds
+// address / 16 in its low 14 bits, and shared-memory addresses stay below 2^18 bytes, so the sum
+// never carries out of the field. Cheaper than rebuilding the descriptor for every MMA.
+__device__ __forceinline__ uint64_t desc_advance(uint64_t desc, uint32_t bytes) {
+  return desc + static_cast<uint64_t>(bytes >> 4);
 }
 
 // Instruction descriptor for kind::f16 / kind::tf32, fp32 accumulate, both operands K-major.
