@@ -8,17 +8,13 @@
 // columns h*32 (q), C + h*32 (k), 2C + h*32 (v); output (B, L, C) in the same
 // type. One CTA per (128-query tile, head, batch item). Warp roles: a TMA
 // producer (Q once, K/V tiles of 128 keys double-buffered), a single-thread
-// tcgen05.mma issuer, and eight softmax warps: two per TMEM lane quarter, so each
-// query row is shared by two threads, one per 64-key half of a tile (and per
-// 16-column half of the output); they meet through shared memory for the row
-// maximum of every tile and, at the end, for the row sum.
+// tcgen05.mma issuer, and four softmax warps owning one query row per thread.
 //
 // Per key tile j: S = Q K_j^T (M = 128 queries, N = 128 keys, K = 32) lands in
-// TMEM; the softmax threads read their half row, agree on the row maximum,
-// track the running maximum m and their half of the sum l (base-2 exponentials
-// of the scaled logits), write P_j = exp2(s - m_j) in the operand type to shared
-// memory in the 128-byte-swizzled K-major layout (two 64-key chunks, one per
-// half), and the issuer computes PV_j = P_j V_j (M = 128,
+// TMEM; the softmax threads read their row, track the running maximum m and
+// sum l (base-2 exponentials of the scaled logits), write P_j = exp2(s - m_j)
+// in the operand type to shared memory in the 128-byte-swizzled K-major layout
+// (two 64-key chunks), and the issuer computes PV_j = P_j V_j (M = 128,
 // N = 32, K = 128; V read MN-major: its 32 head channels are the contiguous N
 // dimension) into one of two TMEM tiles. The output accumulator stays in the
 // softmax threads' registers: while P_{j+1} is produced, PV_j is folded in as
@@ -43,8 +39,7 @@
 namespace ctmr {
 namespace {
 
-constexpr int kAttnThreads = 320;      // warp 0 TMA, warp 1 MMA + TMEM, warps 2..9 softmax
-constexpr int kSoftmaxThreads = 256;
+constexpr int kAttnThreads = 192;      // warp 0 TMA, warp 1 MMA + TMEM, warps 2..5 softmax
 constexpr int kRows = 128;             // queries per CTA, keys per tile
 constexpr int kHead = 32;              // head size
 constexpr uint32_t kTileBytes = kRows * kHead * 2;   // 8 KB: one Q, K or V tile (64-byte rows)
@@ -56,8 +51,7 @@ constexpr uint32_t kOffQ = 0;
 constexpr uint32_t kOffK = kOffQ + kTileBytes;
 constexpr uint32_t kOffV = kOffK + 2 * kTileBytes;
 constexpr uint32_t kOffP = kOffV + 2 * kTileBytes;
-constexpr uint32_t kOffRed = kOffP + 2 * kPBytes;      // [2 tiles + row sums][2 halves][128 rows]
-constexpr uint32_t kOffBar = kOffRed + 3 * 2 * kRows * 4;
+constexpr uint32_t kOffBar = kOffP + 2 * kPBytes;
 constexpr uint32_t kSmemBytes = kOffBar + 256 + 1024;  // + barriers + alignment slack
 
 __device__ __forceinline__ void tmem_ld32_issue(uint32_t taddr, uint32_t (&r)[32]) {
@@ -119,20 +113,6 @@ __device__ __forceinline__ float poly_exp2(float x) {
   return __int_as_float(__float_as_int(p) + (__float_as_int(j) << 23));
 }
 
-// Barrier over `threads` threads that also returns whether `v` held on all of them.
-__device__ __forceinline__ bool barrier_all(int id, int threads, bool v) {
-  uint32_t r;
-  asm volatile(
-      "{\n\t.reg .pred p, q;\n\t"
-      "setp.ne.u32 q, %2, 0;\n\t"
-      "bar.red.and.pred p, %1, %3, q;\n\t"
-      "selp.u32 %0, 1, 0, p;\n\t}"
-      : "=r"(r)
-      : "r"(id), "r"(static_cast<uint32_t>(v)), "r"(threads)
-      : "memory");
-  return r != 0;
-}
-
 __device__ __forceinline__ uint32_t pack2(float a, float b, bool bf16) {
   if (bf16) {
     __nv_bfloat162 h = __floats2bfloat162_rn(a, b);
@@ -142,7 +122,7 @@ __device__ __forceinline__ uint32_t pack2(float a, float b, bool bf16) {
   return *reinterpret_cast<uint32_t*>(&h);
 }
 
-// Two CTAs per SM (at most 102 registers per thread): while one waits on its tensor-core
+// Two CTAs per SM (at most 170 registers per thread): while one waits on its tensor-core
 // products the other's softmax warps keep the exponential unit busy.
 template <bool BF16>
 __global__ void __launch_bounds__(kAttnThreads, 2)
@@ -171,12 +151,12 @@ __global__ void __launch_bounds__(kAttnThreads, 2)
     for (int i = 0; i < 2; ++i) {
       mbar_init(&kv_full[i], 1);
       mbar_init(&kv_empty[i], 1);
-      mbar_init(&p_full[i], kSoftmaxThreads);
+      mbar_init(&p_full[i], 128);
       mbar_init(&o_full[i], 1);
-      mbar_init(&o_free[i], kSoftmaxThreads);
+      mbar_init(&o_free[i], 128);
     }
     mbar_init(s_full, 1);
-    mbar_init(s_free, kSoftmaxThreads);
+    mbar_init(s_free, 128);
     *abort_flag = 0;
     fence_barrier_init();
   }
@@ -251,76 +231,55 @@ __global__ void __launch_bounds__(kAttnThreads, 2)
     if (ok && n_tiles > 0 && !pv(n_tiles - 1)) ok = false;
     if (!ok) *abort_flag = 1;
   } else if (warp >= 2) {
-    // ------------------------------------------------------------ softmax, two threads per query row
+    // ------------------------------------------------------------ softmax, one query row per thread
     const int quarter = warp & 3;
-    const int half = (warp - 2) >> 2;  // keys [64 half, 64 half + 64) of a tile, output columns [16 half, + 16)
     const int row = quarter * 32 + lane;
     const uint32_t lane_addr = static_cast<uint32_t>(quarter * 32) << 16;
-    const uint32_t col0 = static_cast<uint32_t>(half * 64);
-    float* red = reinterpret_cast<float*>(smem + kOffRed);  // [tile & 1, or 2 for the row sums][half][row]
     const float scale = p.scale * 1.4426950408889634f;  // logits in base 2
     float m_prev = -INFINITY, m_cur = -INFINITY, l = 0.f;
-    float acc[kHead / 2];
+    float acc[kHead];
 #pragma unroll
-    for (int i = 0; i < kHead / 2; ++i) acc[i] = 0.f;
+    for (int i = 0; i < kHead; ++i) acc[i] = 0.f;
     bool ok = true;
-    auto fold = [&](int i, float m_old, float m_new) -> bool {  // acc = acc * 2^(m_old - m_new) + PV_i (this half)
+    auto fold = [&](int i, float m_old, float m_new) -> bool {  // acc = acc * 2^(m_old - m_new) + PV_i
       const int s = i & 1;
-      if (!__all_sync(0xffffffffu, mbar_wait_bounded(&o_full[s], static_cast<uint32_t>(i >> 1) & 1u, kErrWaitAcc)))
-        return false;
+      if (!mbar_wait_bounded(&o_full[s], static_cast<uint32_t>(i >> 1) & 1u, kErrWaitAcc)) return false;
       tc_fence_after();
-      uint32_t r[16];
-      asm volatile(
-          "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];"
-          : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
-            "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
-          : "r"(t_o + lane_addr + static_cast<uint32_t>(s) * kHead + static_cast<uint32_t>(16 * half)));
-      asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+      uint32_t r[32];
+      tmem_ld32_issue(tmem + lane_addr + (t_o - tmem) + static_cast<uint32_t>(s) * kHead, r);
+      tmem_ld32_wait(r);
       const float f = m_old == -INFINITY ? 0.f : fast_exp2(m_old - m_new);
 #pragma unroll
-      for (int c = 0; c < kHead / 2; ++c) acc[c] = fmaf(acc[c], f, __uint_as_float(r[c]));
+      for (int c = 0; c < kHead; ++c) acc[c] = fmaf(acc[c], f, __uint_as_float(r[c]));
       tc_fence_before();
       mbar_arrive(&o_free[s]);
       return true;
     };
     for (int j = 0; j < n_tiles; ++j) {
-      // Warp-uniform (the TMEM loads below are warp-wide instructions).
-      const bool mine = __all_sync(0xffffffffu, ok && mbar_wait_bounded(s_full, static_cast<uint32_t>(j) & 1u,
-                                                                          kErrWaitAcc) && !*abort_flag);
-      // Pass 1: this half's maximum, then the row's (the other half's through shared memory).
+      ok = mbar_wait_bounded(s_full, static_cast<uint32_t>(j) & 1u, kErrWaitAcc) && !*abort_flag;
+      if (!ok) break;
+      tc_fence_after();
+      // Pass 1: the row maximum over the tile (two 32-column loads in flight per wait).
       float mx = -INFINITY;
-      if (mine) {
-        tc_fence_after();
+#pragma unroll
+      for (int c = 0; c < kRows; c += 64) {
         uint32_t r[32], r2[32];
-        tmem_ld32_issue(t_s + lane_addr + col0, r);
-        tmem_ld32_issue(t_s + lane_addr + col0 + 32u, r2);
+        tmem_ld32_issue(t_s + lane_addr + static_cast<uint32_t>(c), r);
+        tmem_ld32_issue(t_s + lane_addr + static_cast<uint32_t>(c + 32), r2);
         tmem_ld32_wait(r);
         tmem_ld32_wait(r2);
 #pragma unroll
         for (int i = 0; i < 32; ++i) mx = fmaxf(mx, fmaxf(__uint_as_float(r[i]), __uint_as_float(r2[i])));
       }
-      // Maxima of tile j and j + 1 use separate slots, so a slot is rewritten only after both
-      // threads of the row passed the barrier of the tile in between.
-      float* red_j = red + (j & 1) * 2 * kRows;
-      red_j[half * kRows + row] = mx;
-      // The two warps of this lane quarter (64 threads) meet on named barrier 1 + quarter, which
-      // also votes: both threads of every row continue, or both leave the loop (a wait that gave up,
-      // a failed fold, or the CTA's abort flag on either side), so neither is left at a barrier.
-      if (!barrier_all(1 + quarter, 64, mine)) {
-        ok = false;
-        break;
-      }
-      mx = fmaxf(mx, red_j[(1 - half) * kRows + row]);
       const float m_new = fmaxf(m_cur, mx * scale);
-      // Pass 2: P = 2^(s * scale - m_new) for this half's 64 keys (P chunk `half`), written swizzled.
+      // Pass 2: P = 2^(s * scale - m_new) in the operand type, written swizzled.
       const int s = j & 1;
-      uint8_t* chunk = smem + kOffP + s * kPBytes + static_cast<size_t>(half) * (kRows * 128) +
-                       static_cast<size_t>(row) * 128;
+      uint8_t* prow = smem + kOffP + s * kPBytes + static_cast<size_t>(row) * 128;
       float sum = 0.f;
 #pragma unroll
-      for (int c = 0; c < 64; c += 32) {
+      for (int c = 0; c < kRows; c += 32) {
         uint32_t r[32];
-        tmem_ld32_issue(t_s + lane_addr + col0 + static_cast<uint32_t>(c), r);
+        tmem_ld32_issue(t_s + lane_addr + static_cast<uint32_t>(c), r);
         tmem_ld32_wait(r);
         uint32_t w[16];
 #pragma unroll
@@ -333,10 +292,11 @@ __global__ void __launch_bounds__(kAttnThreads, 2)
           sum += e0 + e1;
           w[i] = pack2(e0, e1, BF16);
         }
-        // Keys c .. c + 31 of the chunk: 16-byte units c / 8 .. + 3, swizzled by row % 8.
+        // Keys c .. c + 31: chunk c / 64, 16-byte units (c % 64) / 8 .. + 3, swizzled by row % 8.
+        uint8_t* chunk = prow + static_cast<size_t>(c >> 6) * (kRows * 128);
 #pragma unroll
         for (int u = 0; u < 4; ++u) {
-          const int unit = ((c >> 3) + u) ^ (row & 7);
+          const int unit = (((c & 63) >> 3) + u) ^ (row & 7);
           *reinterpret_cast<uint4*>(chunk + unit * 16) = make_uint4(w[4 * u], w[4 * u + 1], w[4 * u + 2], w[4 * u + 3]);
         }
       }
@@ -346,30 +306,23 @@ __global__ void __launch_bounds__(kAttnThreads, 2)
       // P_j is in shared memory: visible to the tensor core's async proxy, then published.
       fence_proxy_async_shared();
       mbar_arrive(&p_full[s]);
-      l = (m_cur == -INFINITY ? 0.f : l * fast_exp2(m_cur - m_new)) + sum;  // this half's share of the row sum
-      // Fold PV_{j-1} (scale m_cur) while PV_j runs; a failure is voted on at the next tile.
-      if (j >= 1 && !fold(j - 1, m_prev, m_cur)) ok = false;
+      l = (m_cur == -INFINITY ? 0.f : l * fast_exp2(m_cur - m_new)) + sum;
+      // Fold PV_{j-1} (scale m_cur) while PV_j runs.
+      if (j >= 1 && !fold(j - 1, m_prev, m_cur)) { ok = false; break; }
       m_prev = m_cur;
       m_cur = m_new;
     }
     if (ok && n_tiles > 0) ok = fold(n_tiles - 1, m_prev, m_cur);
     if (!ok) *abort_flag = 1;
-    // Row sum = both halves' shares (the same running maximum scales both), in a slot of its own.
-    // Both threads of every row reach this barrier: the loop ends for both at the same vote, or for
-    // both after its last tile.
-    float* red_l = red + 4 * kRows;
-    red_l[half * kRows + row] = l;
-    asm volatile("bar.sync %0, 64;" ::"r"(1 + quarter) : "memory");
-    const float l_row = l + red_l[(1 - half) * kRows + row];
-    const float inv = l_row > 0.f ? 1.f / l_row : 0.f;
-    uint32_t o[kHead / 4];
+    // Output row: acc / l.
+    const float inv = l > 0.f ? 1.f / l : 0.f;
+    uint32_t o[kHead / 2];
 #pragma unroll
-    for (int i = 0; i < kHead / 4; ++i) o[i] = pack2(acc[2 * i] * inv, acc[2 * i + 1] * inv, BF16);
+    for (int i = 0; i < kHead / 2; ++i) o[i] = pack2(acc[2 * i] * inv, acc[2 * i + 1] * inv, BF16);
     uint4* dst = reinterpret_cast<uint4*>(static_cast<uint16_t*>(p.out) +
-                                          (static_cast<long long>(b) * p.tokens + q0 + row) * C + h * kHead +
-                                          16 * half);
+                                          (static_cast<long long>(b) * p.tokens + q0 + row) * C + h * kHead);
 #pragma unroll
-    for (int i = 0; i < 2; ++i) dst[i] = make_uint4(o[4 * i], o[4 * i + 1], o[4 * i + 2], o[4 * i + 3]);
+    for (int i = 0; i < 4; ++i) dst[i] = make_uint4(o[4 * i], o[4 * i + 1], o[4 * i + 2], o[4 * i + 3]);
   }
 
   tc_fence_before();
