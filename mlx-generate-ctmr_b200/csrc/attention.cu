@@ -259,8 +259,11 @@ __global__ void __launch_bounds__(kAttnThreads, 2)
       ok = mbar_wait_bounded(s_full, static_cast<uint32_t>(j) & 1u, kErrWaitAcc) && !*abort_flag;
       if (!ok) break;
       tc_fence_after();
-      // Pass 1: the row maximum over the tile (two 32-column loads in flight per wait).
-      float mx = -INFINITY;
+      // Pass 1: the row maximum over the tile (two 32-column loads in flight per wait), in eight
+      // independent running maxima so the comparisons do not form one serial chain.
+      float mq[8];
+#pragma unroll
+      for (int q = 0; q < 8; ++q) mq[q] = -INFINITY;
 #pragma unroll
       for (int c = 0; c < kRows; c += 64) {
         uint32_t r[32], r2[32];
@@ -269,13 +272,19 @@ __global__ void __launch_bounds__(kAttnThreads, 2)
         tmem_ld32_wait(r);
         tmem_ld32_wait(r2);
 #pragma unroll
-        for (int i = 0; i < 32; ++i) mx = fmaxf(mx, fmaxf(__uint_as_float(r[i]), __uint_as_float(r2[i])));
+        for (int i = 0; i < 32; ++i)
+          mq[i & 7] = fmaxf(mq[i & 7], fmaxf(__uint_as_float(r[i]), __uint_as_float(r2[i])));
       }
+      const float mx = fmaxf(fmaxf(fmaxf(mq[0], mq[1]), fmaxf(mq[2], mq[3])),
+                             fmaxf(fmaxf(mq[4], mq[5]), fmaxf(mq[6], mq[7])));
       const float m_new = fmaxf(m_cur, mx * scale);
       // Pass 2: P = 2^(s * scale - m_new) in the operand type, written swizzled.
       const int s = j & 1;
       uint8_t* prow = smem + kOffP + s * kPBytes + static_cast<size_t>(row) * 128;
-      float sum = 0.f;
+      // The row sum in eight independent partial sums (no serial chain of 64 additions per chunk).
+      float sq[8];
+#pragma unroll
+      for (int q = 0; q < 8; ++q) sq[q] = 0.f;
 #pragma unroll
       for (int c = 0; c < kRows; c += 32) {
         uint32_t r[32];
@@ -289,7 +298,7 @@ __global__ void __launch_bounds__(kAttnThreads, 2)
           // Keys 24..31 of the 32 on the FMA pipe, the rest on the exponential unit.
           const float e0 = i >= 12 ? poly_exp2(x0) : fast_exp2(x0);
           const float e1 = i >= 12 ? poly_exp2(x1) : fast_exp2(x1);
-          sum += e0 + e1;
+          sq[i & 7] += e0 + e1;
           w[i] = pack2(e0, e1, BF16);
         }
         // Keys c .. c + 31: chunk c / 64, 16-byte units (c % 64) / 8 .. + 3, swizzled by row % 8.
@@ -306,6 +315,7 @@ __global__ void __launch_bounds__(kAttnThreads, 2)
       // P_j is in shared memory: visible to the tensor core's async proxy, then published.
       fence_proxy_async_shared();
       mbar_arrive(&p_full[s]);
+      const float sum = ((sq[0] + sq[1]) + (sq[2] + sq[3])) + ((sq[4] + sq[5]) + (sq[6] + sq[7]));
       l = (m_cur == -INFINITY ? 0.f : l * fast_exp2(m_cur - m_new)) + sum;
       // Fold PV_{j-1} (scale m_cur) while PV_j runs.
       if (j >= 1 && !fold(j - 1, m_prev, m_cur)) { ok = false; break; }
