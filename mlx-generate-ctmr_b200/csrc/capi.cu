@@ -518,6 +518,7 @@ int ctmr_attention_d32(const void* qkv, int dtype, int batch, int tokens, int he
   if (batch <= 0 || heads <= 0 || tokens <= 0) return fail(CTMR_ERR_INVALID, "attention extents");
   if (tokens % 128 != 0) return fail(CTMR_ERR_UNSUPPORTED, "attention tokens must be a multiple of 128");
   if (!aligned16(qkv) || !aligned16(out)) return fail(CTMR_ERR_INVALID, "attention pointers must be 16-byte aligned");
+  if (!(scale > 0.f)) return fail(CTMR_ERR_INVALID, "attention scale must be positive");
   auto enc = tensor_map_encoder();
   if (enc == nullptr) return fail(CTMR_ERR_CUDA, "cuTensorMapEncodeTiled is unavailable");
   const long long c3 = 3LL * heads * 32;

@@ -118,6 +118,15 @@ def test_attention_validation(args, status):
     assert _lib.LIB.ctmr_last_error()
 
 
+@pytest.mark.parametrize("scale", [0.0, -0.5, float("nan")])
+def test_attention_scale_must_be_positive(scale):
+    """The kernel takes each row's maximum of the raw logits and scales it afterwards, which is the
+    maximum of the scaled logits only for a positive scale: anything else is refused, nothing launched."""
+    st = _lib.LIB.ctmr_attention_d32(0x1000, _lib.DTYPE_F16, 1, 128, 1, scale, 0x2000, None)
+    assert st == _lib.CTMR_ERR_INVALID
+    assert b"scale" in _lib.LIB.ctmr_last_error()
+
+
 def _tdesc(**kw) -> _lib.TransformDesc:
     d = _lib.TransformDesc()
     d.batch, d.depth, d.height, d.width = 1, 4, 4, 4

@@ -632,3 +632,32 @@ def test_attention_d32_matches_sdpa(cuda, b, length, heads, dtype):
     assert out.shape == ref.shape and out.dtype == dtype
     err = ((out.float() - ref).norm() / ref.norm()).item()
     assert err <= (2e-3 if dtype == torch.float16 else 1e-2), f"rel-L2 {err:.3e}"
+
+
+@pytest.mark.parametrize("dtype", [torch.float16, torch.bfloat16])
+@pytest.mark.parametrize("ramp", [(0.25, 4.0), (4.0, 0.25)])
+def test_attention_d32_row_maximum_growing_and_shrinking(cuda, ramp, dtype):
+    """Keys scaled by a ramp along the sequence: rising, each row's maximum grows by many powers
+    of two from key tile to key tile, so the online softmax rescales its running output and sum on
+    every tile; falling, the first tile holds the maximum and every later tile's exponentials are
+    far below one."""
+    from ctmr_b200 import ops
+
+    b, length, heads = 1, 1024, 4
+    g = torch.Generator().manual_seed(5)
+    c = heads * 32
+    qkv = torch.randn(b, length, 3 * c, generator=g) * 1.5
+    qkv[:, :, c:2 * c] *= torch.linspace(*ramp, length)[None, :, None]
+    qkv = qkv.to(cuda, dtype)
+    scale = 32 ** -0.5
+    out = ops.attention_d32(qkv, heads, scale)
+    q, k, v = qkv.float().chunk(3, dim=-1)
+
+    def split(a):
+        return a.reshape(b, length, heads, 32).transpose(1, 2)
+
+    ref = torch.nn.functional.scaled_dot_product_attention(split(q), split(k), split(v), scale=scale)
+    ref = ref.transpose(1, 2).reshape(b, length, c)
+    torch.cuda.synchronize()
+    err = ((out.float() - ref).norm() / ref.norm()).item()
+    assert err <= (2e-3 if dtype == torch.float16 else 1e-2), f"rel-L2 {err:.3e}"
