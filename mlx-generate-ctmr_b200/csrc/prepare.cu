@@ -427,14 +427,17 @@ __global__ void __launch_bounds__(256, 5) prepare_copy_kernel(const PrepParams p
   }
 }
 
-// Trilinear 2x (half-pixel, clamped; no transform), 4 channels per item and a
-// 2 (h) x 2 (w) output block per thread at one output depth: the block reads a
-// 2 x 3 x 3 source neighbourhood (4.5 loads per output instead of 8). Each
-// output uses exactly the source pair and weight of tri_axis and the same lerp
-// order (w, then h, then d) as the general path, so results are bitwise equal.
+// Trilinear 2x (half-pixel, clamped; no transform), 4 channels per item. An item is one
+// column: a source (h, w) position and channel chunk, whose 2 (h) x 2 (w) output block the
+// thread produces at every output depth. Walking the source depths once, it reads the 3 x 3
+// source neighbourhood of each depth (9 loads for 8 outputs), lerps it along w then h into
+// that depth's 2 x 2 block, and emits every output depth whose two source depths it now
+// holds (2 zs - 1 and 2 zs, output 0 at zs = 1, the last output at the last depth). Each
+// output uses exactly the source pair and weight of tri_axis and the same lerp order (w,
+// then h, then d) as the general path, so results are bitwise equal.
 template <int OUTK>
 __global__ void __launch_bounds__(128) prepare_tri_kernel(const PrepParams p, const FastDiv qdiv, const FastDiv xdiv,
-                                                          const FastDiv ydiv, const unsigned items) {
+                                                          const unsigned items) {
   griddep_wait();  // the preceding kernel's writes are visible from here on
   griddep_launch_dependents();
   const int b = blockIdx.y;
@@ -444,13 +447,9 @@ __global__ void __launch_bounds__(128) prepare_tri_kernel(const PrepParams p, co
   for (unsigned item = blockIdx.x * blockDim.x + threadIdx.x; item < items; item += gridDim.x * blockDim.x) {
     const unsigned r1 = fdiv(qdiv, item);
     const int c0 = static_cast<int>(item - r1 * qdiv.d) * 4;
-    const unsigned r2 = fdiv(xdiv, r1);
-    const int xi = static_cast<int>(r1 - r2 * xdiv.d);  // source w index = output w pair
-    const unsigned z = fdiv(ydiv, r2);
-    const int yj = static_cast<int>(r2 - z * ydiv.d);   // source h index = output h pair
-    int z0, z1;
-    float az;
-    tri_axis(static_cast<int>(z), p.sd, z0, z1, az);
+    const unsigned yj_u = fdiv(xdiv, r1);
+    const int xi = static_cast<int>(r1 - yj_u * xdiv.d);  // source w index = output w pair
+    const int yj = static_cast<int>(yj_u);               // source h index = output h pair
     const int xs[3] = {max(xi - 1, 0), xi, min(xi + 1, p.sw - 1)};
     const int ys[3] = {max(yj - 1, 0), yj, min(yj + 1, p.sh - 1)};
     // Output pair element e (0: 2i, 1: 2i + 1) uses slots (lo, hi) and weight a:
@@ -468,18 +467,28 @@ __global__ void __launch_bounds__(128) prepare_tri_kernel(const PrepParams p, co
       yo[0] = yj >= 1 ? 0 : 1;
       yo[1] = 1;
     }
-    float o[2][2][4];  // [h pair][w pair][channel]
-    float zr[2][2][2][4];  // [z][h pair][w pair] after the w and h lerps
+    // The 2 x 2 output block of output depth o from the w-then-h lerped blocks of its source depths.
+    auto emit = [&](int o, const float (&lo)[2][2][4], const float (&hi)[2][2][4], float az) {
+      float v[4];
 #pragma unroll
-    for (int zi = 0; zi < 2; ++zi) {
-      const int zz = zi == 0 ? z0 : z1;
-      float s[3][3][4];
+      for (int f = 0; f < 2; ++f)
+#pragma unroll
+        for (int e = 0; e < 2; ++e) {
+#pragma unroll
+          for (int ch = 0; ch < 4; ++ch) v[ch] = lerp_ref(lo[f][e][ch], hi[f][e][ch], az);
+          const long long ov = bout + (static_cast<long long>(o) * p.oh + 2 * yj + f) * p.ow + 2 * xi + e;
+          store_vec<OUTK, 4>(p, ov * p.out_cstride + c0, v);
+        }
+    };
+    float prev[2][2][4], cur[2][2][4];  // [h pair][w pair][channel] of source depths zs - 1 and zs
+    for (int zs = 0; zs < p.sd; ++zs) {
+      float sv[3][3][4];
 #pragma unroll
       for (int a = 0; a < 3; ++a)
 #pragma unroll
         for (int c = 0; c < 3; ++c)
-          load_vec<4>(p, ctot, bsrc + (static_cast<long long>(zz) * p.sh + ys[a]) * p.sw + xs[c], c0, s[a][c]);
-      // w lerps for every source row, both output w elements.
+          load_vec<4>(p, ctot, bsrc + (static_cast<long long>(zs) * p.sh + ys[a]) * p.sw + xs[c], c0, sv[a][c]);
+      // w lerps for every source row, both output w elements; then the h lerps.
       float wl[3][2][4];
 #pragma unroll
       for (int a = 0; a < 3; ++a)
@@ -487,8 +496,8 @@ __global__ void __launch_bounds__(128) prepare_tri_kernel(const PrepParams p, co
         for (int e = 0; e < 2; ++e)
 #pragma unroll
           for (int ch = 0; ch < 4; ++ch) {
-            const float lo = xo[e] == 0 ? s[a][0][ch] : s[a][1][ch];
-            const float hi = xo[e] == 0 ? s[a][1][ch] : s[a][2][ch];
+            const float lo = xo[e] == 0 ? sv[a][0][ch] : sv[a][1][ch];
+            const float hi = xo[e] == 0 ? sv[a][1][ch] : sv[a][2][ch];
             wl[a][e][ch] = lerp_ref(lo, hi, ax[e]);
           }
 #pragma unroll
@@ -499,22 +508,35 @@ __global__ void __launch_bounds__(128) prepare_tri_kernel(const PrepParams p, co
           for (int ch = 0; ch < 4; ++ch) {
             const float lo = yo[f] == 0 ? wl[0][e][ch] : wl[1][e][ch];
             const float hi = yo[f] == 0 ? wl[1][e][ch] : wl[2][e][ch];
-            zr[zi][f][e][ch] = lerp_ref(lo, hi, ay[f]);
+            cur[f][e][ch] = lerp_ref(lo, hi, ay[f]);
           }
-    }
-#pragma unroll
-    for (int f = 0; f < 2; ++f)
-#pragma unroll
-      for (int e = 0; e < 2; ++e)
-#pragma unroll
-        for (int ch = 0; ch < 4; ++ch) o[f][e][ch] = lerp_ref(zr[0][f][e][ch], zr[1][f][e][ch], az);
-#pragma unroll
-    for (int f = 0; f < 2; ++f)
-#pragma unroll
-      for (int e = 0; e < 2; ++e) {
-        const long long ov = bout + (static_cast<long long>(z) * p.oh + 2 * yj + f) * p.ow + 2 * xi + e;
-        store_vec<OUTK, 4>(p, ov * p.out_cstride + c0, o[f][e]);
+      int z0, z1;
+      float az;
+      if (zs >= 1) {
+        if (zs == 1) {  // output 0: source depths (0, 1), weight 0
+          tri_axis(0, p.sd, z0, z1, az);
+          emit(0, prev, cur, az);
+        }
+        tri_axis(2 * zs - 1, p.sd, z0, z1, az);  // (zs - 1, zs)
+        emit(2 * zs - 1, prev, cur, az);
+        tri_axis(2 * zs, p.sd, z0, z1, az);      // (zs - 1, zs)
+        emit(2 * zs, prev, cur, az);
       }
+      if (zs == p.sd - 1) {
+        if (zs == 0) {  // a single source depth: outputs 0 and 1 both read it twice
+          tri_axis(0, p.sd, z0, z1, az);
+          emit(0, cur, cur, az);
+        }
+        tri_axis(2 * zs + 1, p.sd, z0, z1, az);  // (zs, zs): the far edge clamps
+        emit(2 * zs + 1, cur, cur, az);
+      }
+#pragma unroll
+      for (int f = 0; f < 2; ++f)
+#pragma unroll
+        for (int e = 0; e < 2; ++e)
+#pragma unroll
+          for (int ch = 0; ch < 4; ++ch) prev[f][e][ch] = cur[f][e][ch];
+    }
   }
 }
 
@@ -569,8 +591,7 @@ cudaError_t launch_copy_fast(const PrepParams& p, cudaStream_t stream) {
 cudaError_t launch_tri_fast(const PrepParams& p, cudaStream_t stream) {
   const FastDiv q = make_fastdiv(static_cast<uint32_t>(p.cpad / 4));
   const FastDiv xd = make_fastdiv(static_cast<uint32_t>(p.sw));
-  const FastDiv yd = make_fastdiv(static_cast<uint32_t>(p.sh));
-  const long long items = static_cast<long long>(p.od) * p.sh * p.sw * q.d;
+  const long long items = static_cast<long long>(p.sh) * p.sw * q.d;  // columns: every output depth per item
   long long blocks = (items + 127) / 128;
   static const long long resident = resident_blocks(prepare_tri_kernel<kPrepOutF16>, 128, 0);
   const long long cap = resident / p.batch > 0 ? resident / p.batch : 1;
@@ -578,11 +599,11 @@ cudaError_t launch_tri_fast(const PrepParams& p, cudaStream_t stream) {
   const dim3 grid(static_cast<unsigned>(blocks), static_cast<unsigned>(p.batch));
   const unsigned n = static_cast<unsigned>(items);
   switch (p.out_kind) {
-    case kPrepOutBF16: launch_kernel(prepare_tri_kernel<kPrepOutBF16>, grid, 128, 0, stream, p, q, xd, yd, n); break;
-    case kPrepOutF16: launch_kernel(prepare_tri_kernel<kPrepOutF16>, grid, 128, 0, stream, p, q, xd, yd, n); break;
-    case kPrepOutSplitF16: launch_kernel(prepare_tri_kernel<kPrepOutSplitF16>, grid, 128, 0, stream, p, q, xd, yd, n); break;
-    case kPrepOutTF32: launch_kernel(prepare_tri_kernel<kPrepOutTF32>, grid, 128, 0, stream, p, q, xd, yd, n); break;
-    default: launch_kernel(prepare_tri_kernel<kPrepOutF32>, grid, 128, 0, stream, p, q, xd, yd, n); break;
+    case kPrepOutBF16: launch_kernel(prepare_tri_kernel<kPrepOutBF16>, grid, 128, 0, stream, p, q, xd, n); break;
+    case kPrepOutF16: launch_kernel(prepare_tri_kernel<kPrepOutF16>, grid, 128, 0, stream, p, q, xd, n); break;
+    case kPrepOutSplitF16: launch_kernel(prepare_tri_kernel<kPrepOutSplitF16>, grid, 128, 0, stream, p, q, xd, n); break;
+    case kPrepOutTF32: launch_kernel(prepare_tri_kernel<kPrepOutTF32>, grid, 128, 0, stream, p, q, xd, n); break;
+    default: launch_kernel(prepare_tri_kernel<kPrepOutF32>, grid, 128, 0, stream, p, q, xd, n); break;
   }
   return cudaGetLastError();
 }

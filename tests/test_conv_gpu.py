@@ -110,13 +110,16 @@ def test_fused_norm_conv_matches_float64(cuda, upsample):
     _close_fp32(y, expected)
 
 
-def test_trilinear_conv_matches_materialized_upsampling(cuda):
-    """``tests/test_fast_fp32.py:130-150``: fused trilinear conv equals materialised trilinear + conv bitwise."""
+@pytest.mark.parametrize("shape", [(2, 24, 3, 5, 6), (1, 24, 1, 4, 4), (1, 24, 2, 3, 5), (1, 64, 5, 6, 8)])
+def test_trilinear_conv_matches_materialized_upsampling(cuda, shape):
+    """``tests/test_fast_fp32.py:130-150``: fused trilinear conv equals materialised trilinear + conv bitwise;
+    one and two source depths exercise the depth walk's first and last outputs."""
     from ctmr_b200 import ops, _lib
 
     rng = np.random.default_rng(7)
-    x = torch.from_numpy(rng.standard_normal((2, 24, 3, 5, 6)).astype(np.float32))
-    w = torch.from_numpy((rng.standard_normal((32, 24, 3, 3, 3)) / np.sqrt(27 * 24)).astype(np.float32))
+    x = torch.from_numpy(rng.standard_normal(shape).astype(np.float32))
+    c = shape[1]
+    w = torch.from_numpy((rng.standard_normal((32, c, 3, 3, 3)) / np.sqrt(27 * c)).astype(np.float32))
     b = torch.from_numpy(rng.standard_normal(32).astype(np.float32))
     xg = ops.to_ndhwc(x.to(cuda))
     packed = ops.pack_weight(w.to(cuda), "fp32")
@@ -124,7 +127,7 @@ def test_trilinear_conv_matches_materialized_upsampling(cuda):
     up = ops.transform(xg, mode=_lib.TRANSFORM_TRILINEAR)
     materialized = ops.conv3d(up, packed, b.to(cuda))
     torch.cuda.synchronize()
-    assert tuple(fused.shape) == (2, 32, 6, 10, 12)
+    assert tuple(fused.shape) == (shape[0], 32, 2 * shape[2], 2 * shape[3], 2 * shape[4])
     assert torch.equal(fused.cpu(), materialized.cpu())
     # and the upsampling itself matches the oracle's half-pixel trilinear
     ref_up = ops_ref.upsample_trilinear_ref(x.double())
