@@ -381,48 +381,53 @@ __device__ __forceinline__ void load_vec(const PrepParams& p, int ctot, long lon
 
 // Copy mode, 8 channels per item, two items in flight per thread; batch item
 // on grid y. Preconditions (checked by the launcher): fp32 sources, channel
-// counts, strides and cpad multiples of 8, 16-byte aligned rows. At most 48
-// registers, so five blocks share an SM (more loads in flight; no spills).
+// counts, strides and cpad multiples of 8, 16-byte aligned rows; the grid's
+// thread count a multiple of the chunks per voxel, so every item of a thread
+// has the same 8-channel chunk and its GroupNorm scale / offset pairs are loaded
+// once (16 registers held; four blocks of 256 threads per SM at 64 registers).
 template <int OUTK, bool FAST>
-__global__ void __launch_bounds__(256, 5) prepare_copy_kernel(const PrepParams p, const FastDiv qdiv,
+__global__ void __launch_bounds__(256, 4) prepare_copy_kernel(const PrepParams p, const FastDiv qdiv,
                                                            const unsigned vox) {
   griddep_wait();  // the preceding kernel's writes are visible from here on
   griddep_launch_dependents();
   const int b = blockIdx.y;
   const int ctot = p.src[0].channels + p.src[1].channels;
-  const unsigned items = vox * qdiv.d;
   const long long bvox = static_cast<long long>(b) * vox;
-  const unsigned step = gridDim.x * blockDim.x;
-  for (unsigned base = blockIdx.x * blockDim.x + threadIdx.x; base < items; base += 2 * step) {
-    float r[2][8];
-    int c0[2];
-    unsigned v[2];
+  const unsigned first = blockIdx.x * blockDim.x + threadIdx.x;
+  const unsigned v0 = fdiv(qdiv, first);
+  const int c0 = static_cast<int>(first - v0 * qdiv.d) * 8;  // this thread's chunk, for all its items
+  const unsigned vstep = fdiv(qdiv, gridDim.x * blockDim.x);  // voxels between a thread's items
+  const bool live = c0 < ctot;
+  float sc[8], of[8];
+  const bool aff = live && p.affine != nullptr;
+  if (aff) {
+    const float4* a = reinterpret_cast<const float4*>(p.affine + (static_cast<long long>(b) * ctot + c0) * 2);
 #pragma unroll
-    for (int k = 0; k < 2; ++k) {
-      const unsigned item = base + k * step;
-      v[k] = fdiv(qdiv, item);
-      c0[k] = static_cast<int>(item - v[k] * qdiv.d) * 8;
-      if (item < items) load_vec<8>(p, ctot, bvox + v[k], c0[k], r[k]);
+    for (int i = 0; i < 4; ++i) {
+      const float4 q = __ldg(a + i);
+      sc[2 * i] = q.x, of[2 * i] = q.y, sc[2 * i + 1] = q.z, of[2 * i + 1] = q.w;
     }
+  }
+  for (unsigned v = v0; v < vox; v += 2 * vstep) {
+    float r[2][8];
+#pragma unroll
+    for (int k = 0; k < 2; ++k)
+      if (v + k * vstep < vox) load_vec<8>(p, ctot, bvox + v + k * vstep, c0, r[k]);
 #pragma unroll
     for (int k = 0; k < 2; ++k) {
-      if (base + k * step >= items) break;
-      if (c0[k] < ctot) {
-        if (p.affine != nullptr) {
-          const float4* a = reinterpret_cast<const float4*>(p.affine + (static_cast<long long>(b) * ctot + c0[k]) * 2);
+      const unsigned vk = v + k * vstep;
+      if (vk >= vox) break;
+      if (live) {
+        if (aff) {
 #pragma unroll
-          for (int i = 0; i < 4; ++i) {
-            const float4 q = __ldg(a + i);
-            r[k][2 * i] = fmaf(r[k][2 * i], q.x, q.y);
-            r[k][2 * i + 1] = fmaf(r[k][2 * i + 1], q.z, q.w);
-          }
+          for (int i = 0; i < 8; ++i) r[k][i] = fmaf(r[k][i], sc[i], of[i]);
         }
         if (p.silu) {
 #pragma unroll
           for (int i = 0; i < 8; ++i) r[k][i] = silu_f<FAST>(r[k][i]);
         }
       }
-      store_vec<OUTK, 8>(p, (bvox + v[k]) * p.out_cstride + c0[k], r[k]);
+      store_vec<OUTK, 8>(p, (bvox + vk) * p.out_cstride + c0, r[k]);
     }
   }
 }
@@ -577,6 +582,15 @@ cudaError_t launch_copy_fast(const PrepParams& p, cudaStream_t stream) {
   static const long long resident = resident_blocks(prepare_copy_kernel<kPrepOutF16, true>, 256, 0);
   const long long cap = resident / p.batch > 0 ? resident / p.batch : 1;
   if (blocks > cap) blocks = cap;
+  // The grid's thread count a multiple of the chunks per voxel: blocks a multiple of q / gcd(q, 256).
+  long long g = q.d, r = 256;
+  while (r != 0) {
+    const long long t = g % r;
+    g = r;
+    r = t;
+  }
+  const long long unit = q.d / g;
+  blocks = blocks < unit ? unit : blocks / unit * unit;
   const dim3 grid(static_cast<unsigned>(blocks), static_cast<unsigned>(p.batch));
   switch (p.out_kind) {
     case kPrepOutBF16: launch_kernel(prepare_copy_kernel<kPrepOutBF16, true>, grid, 256, 0, stream, p, q, vox); break;
