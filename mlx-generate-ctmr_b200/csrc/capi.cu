@@ -421,7 +421,11 @@ bool plan_v2(const ConvPlan& p, const ctmr_conv3d_desc* d, bool with_stats, V2Pl
       p.row_h < 8 || getenv("CTMR_DISABLE_V2") != nullptr)
     return false;
   v->tw = p.mode == ctmr::kModeConv3 ? 3 : (p.mode == ctmr::kModeUp2 ? 2 : 1);
-  v->mt = p.row_d >= 2 ? 2 : 1;
+  // Two depth tiles share each weight box of a 3x3x3 or folded conv. A 1x1x1 conv into <= 64
+  // channels has one short K walk and a short epilogue per tile, where one depth per tile drains
+  // and refills faster (measured: 2 x 128 -> 64 at 64 x 64 x 32 54 -> 41 us, 1 x 128 -> 64 at
+  // 96 x 256 x 128 549 -> 389 us; 1 x 256 -> 128 at 48 x 128 x 64 130 -> 135 us, so not above 64).
+  v->mt = p.row_d >= 2 && !(p.mode == ctmr::kModeConv1 && p.opad <= 64) ? 2 : 1;
   v->bn = std::min(p.opad, 128);
   v->stats_bytes = 0;
   if (with_stats) {
