@@ -44,18 +44,37 @@ constexpr int kRows = 128;
 
 __host__ __device__ constexpr uint32_t round_up_u32(uint32_t v, uint32_t a) { return (v + a - 1) / a * a; }
 
+// EXACT with at most 64 output columns per tile ("paired"): hi*hi and hi*lo come from one N = 2 bn
+// MMA whose B is the weight blocks [hi; lo] (or [lo; hi]) stacked along N, with its D the hi chunk
+// buffer and the lo accumulator side by side in TMEM; lo*hi is a second MMA. Two MMAs per K step
+// instead of three, where an N <= 64 MMA costs about as much as an N = 128 one. The stacked blocks
+// must be contiguous whole swizzle atoms: bn * kc * 2 bytes a multiple of 1024.
+__host__ __device__ constexpr bool exact_pair(int kc, int bn, bool exact) {
+  return exact && bn <= 64 && (bn * kc * 2) % 1024 == 0;
+}
+
 struct StageLayout {
   uint32_t a_bytes, b_bytes, stage_bytes;
   __host__ __device__ StageLayout(int kc, int bn, bool exact) {
     a_bytes = round_up_u32(kRows * kc * 2, 1024);
     b_bytes = round_up_u32(static_cast<uint32_t>(bn) * kc * 2, 1024);
-    stage_bytes = (a_bytes + b_bytes) * (exact ? 2u : 1u);
+    // Paired: the weight blocks [hi; lo; hi], so that both [hi; lo] and [lo; hi] are contiguous.
+    stage_bytes = exact ? 2u * a_bytes + (exact_pair(kc, bn, exact) ? 3u : 2u) * b_bytes : a_bytes + b_bytes;
   }
 };
 
-template <int KC, bool EXACT, bool TF32>
+// 16 zero columns into this warp's 32 TMEM lanes (completed by tcgen05.wait::st).
+__device__ __forceinline__ void tmem_zero16(uint32_t taddr) {
+  asm volatile(
+      "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], {%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1};" ::"r"(taddr),
+      "r"(0u)
+      : "memory");
+}
+
+template <int KC, bool EXACT, bool TF32, bool PAIR>
 __global__ void __launch_bounds__(kThreads, 1)
     conv3d_umma_kernel(const __grid_constant__ ConvMaps maps, const __grid_constant__ ConvGeom g) {
+  static_assert(!PAIR || EXACT, "the paired products are the split mode's");
   constexpr uint32_t kRowBytes = KC * 2;
   constexpr int kSteps = KC / 16;  // K=16 MMAs per channel block
   extern __shared__ uint8_t smem_raw[];
@@ -155,12 +174,14 @@ __global__ void __launch_bounds__(kThreads, 1)
         x -= (kw == 0);
       }
       uint8_t* st = smem + static_cast<size_t>(s) * L.stage_bytes;
-      mbar_arrive_expect_tx(&full[s], (kRows + static_cast<uint32_t>(g.bn)) * kRowBytes * (EXACT ? 2u : 1u));
+      mbar_arrive_expect_tx(&full[s], (kRows * (EXACT ? 2u : 1u) + static_cast<uint32_t>(g.bn) * (PAIR ? 3u : (EXACT ? 2u : 1u))) *
+                                          kRowBytes);
       tma_load_5d(st, &maps.a[map], &full[s], c, x, y, z, b);
       if (EXACT) tma_load_5d(st + L.a_bytes, &maps.a_lo[map], &full[s], c, x, y, z, b);
       uint8_t* bs = st + L.a_bytes * (EXACT ? 2 : 1);
       tma_load_3d(bs, &maps.b, &full[s], c, n0, btap);
       if (EXACT) tma_load_3d(bs + L.b_bytes, &maps.b_lo, &full[s], c, n0, btap);
+      if (PAIR) tma_load_3d(bs + 2 * L.b_bytes, &maps.b, &full[s], c, n0, btap);
       ++issued;
     }
     // Drain: the newest load of every stage must land before the CTA can exit.
@@ -176,16 +197,22 @@ __global__ void __launch_bounds__(kThreads, 1)
     // runs, whose rounding error otherwise grows with K (27 * C_in products).
     static_assert(!(EXACT && TF32), "the split mode has fp16 operands");
     const uint32_t idesc = idesc_f16(!EXACT && g.operand_bf16 != 0, kRows, static_cast<uint32_t>(g.bn), TF32);
+    const uint32_t idesc_pair = idesc_f16(false, kRows, 2u * static_cast<uint32_t>(g.bn));
     const uint32_t bn = static_cast<uint32_t>(g.bn);
-    const uint32_t acc_lo = tmem + 2u * bn;
+    // TMEM: [hi0 | hi1 | lo], or paired [hi0 | lo | hi1] (each hi buffer adjacent to lo).
+    const uint32_t acc_lo = tmem + (PAIR ? 1u : 2u) * bn;
     const int T = EXACT ? g.chunk_iters : n_iter;
     for (int it = 0; it < n_iter; ++it) {
       const int s = it % S;
       const int chunk = it / T;
       const int buf = chunk & 1;
       const bool chunk_start = it - chunk * T == 0;
-      if (EXACT && chunk_start && chunk >= 2 &&
-          !mbar_wait_bounded(&chunk_empty[buf], static_cast<uint32_t>((chunk >> 1) - 1) & 1u, kErrWaitAcc)) {
+      // The hi buffer about to be reused must be drained (paired: and zeroed; the epilogue also zeroes
+      // buffer 1 once before its first use, which is that buffer's first completion).
+      if (EXACT && chunk_start && (PAIR ? chunk >= 1 : chunk >= 2) &&
+          !mbar_wait_bounded(&chunk_empty[buf],
+                             static_cast<uint32_t>(PAIR && buf == 1 ? (chunk - 1) >> 1 : (chunk >> 1) - 1) & 1u,
+                             kErrWaitAcc)) {
         *abort_flag = 1;
         break;
       }
@@ -198,14 +225,28 @@ __global__ void __launch_bounds__(kThreads, 1)
       const uint32_t st = smem_u32(smem + static_cast<size_t>(s) * L.stage_bytes);
       const uint64_t a_hi = smem_desc_kmajor(st, kRowBytes), a_lo = desc_advance(a_hi, L.a_bytes);
       const uint64_t b_hi = desc_advance(a_hi, L.a_bytes * (EXACT ? 2 : 1)), b_lo = desc_advance(b_hi, L.b_bytes);
-      const uint32_t acc_hi = tmem + static_cast<uint32_t>(buf) * bn;
+      if (PAIR) {
+        // Buffer 0: D = [hi0 | lo], B = [hi; lo]; buffer 1: D = [lo | hi1], B = [lo; hi] (the stage's
+        // weight blocks are [hi; lo; hi]). The hi buffers restart from the epilogue's zeros, so only
+        // the first product overwrites.
+        const uint32_t d_pair = tmem + static_cast<uint32_t>(buf) * bn;
+        const uint64_t b_pair = buf == 0 ? b_hi : b_lo;
 #pragma unroll
-      for (int k = 0; k < kSteps; ++k) {  // 32 bytes of K per MMA (16 fp16/bf16, 8 tf32): +2 in the address field
-        const uint32_t kd = 2u * static_cast<uint32_t>(k);
-        umma<TF32>(acc_hi, a_hi + kd, b_hi + kd, idesc, (chunk_start && k == 0) ? 0u : 1u);
-        if (EXACT) {
-          umma_f16(acc_lo, a_hi + kd, b_lo + kd, idesc, (it == 0 && k == 0) ? 0u : 1u);
+        for (int k = 0; k < kSteps; ++k) {
+          const uint32_t kd = 2u * static_cast<uint32_t>(k);
+          umma_f16(d_pair, a_hi + kd, b_pair + kd, idesc_pair, (it == 0 && k == 0) ? 0u : 1u);
           umma_f16(acc_lo, a_lo + kd, b_hi + kd, idesc, 1u);
+        }
+      } else {
+        const uint32_t acc_hi = tmem + static_cast<uint32_t>(buf) * bn;
+#pragma unroll
+        for (int k = 0; k < kSteps; ++k) {  // 32 bytes of K per MMA (16 fp16/bf16, 8 tf32): +2 in the address field
+          const uint32_t kd = 2u * static_cast<uint32_t>(k);
+          umma<TF32>(acc_hi, a_hi + kd, b_hi + kd, idesc, (chunk_start && k == 0) ? 0u : 1u);
+          if (EXACT) {
+            umma_f16(acc_lo, a_hi + kd, b_lo + kd, idesc, (it == 0 && k == 0) ? 0u : 1u);
+            umma_f16(acc_lo, a_lo + kd, b_hi + kd, idesc, 1u);
+          }
         }
       }
       umma_commit(&empty[s]);
@@ -226,6 +267,17 @@ __global__ void __launch_bounds__(kThreads, 1)
     if (EXACT) {
       const int T = g.chunk_iters;
       const int nchunks = (n_iter + T - 1) / T;
+      // Paired: hi buffer 0 sits at column 0, buffer 1 at 2 bn (lo between them).
+      auto hi_col = [&](int buf) { return PAIR ? buf * 2 * g.bn : buf * g.bn; };
+      if (PAIR) {
+        // Buffer 1's first chunk accumulates onto zeros: clear it, then hand it to the issuer.
+#pragma unroll
+        for (int cb = 0; cb < 4; ++cb)
+          if (cb * 16 < g.bn) tmem_zero16(lane_addr + static_cast<uint32_t>(hi_col(1) + cb * 16));
+        asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
+        tc_fence_before();
+        mbar_arrive(&chunk_empty[1]);
+      }
       for (int chunk = 0; chunk < nchunks && ok; ++chunk) {
         const int buf = chunk & 1;
         ok = mbar_wait_bounded(&chunk_full[buf], static_cast<uint32_t>(chunk >> 1) & 1u, kErrWaitAcc);
@@ -234,11 +286,13 @@ __global__ void __launch_bounds__(kThreads, 1)
         for (int cb = 0; cb < 8; ++cb) {
           if (cb * 16 < g.bn) {
             float v[16];
-            tmem_ld16(lane_addr + static_cast<uint32_t>(buf * g.bn + cb * 16), v);
+            tmem_ld16(lane_addr + static_cast<uint32_t>(hi_col(buf) + cb * 16), v);
 #pragma unroll
             for (int i = 0; i < 16; ++i) sum[(cb * 16 + i) & (EXACT ? 127 : 0)] += v[i];
+            if (PAIR) tmem_zero16(lane_addr + static_cast<uint32_t>(hi_col(buf) + cb * 16));
           }
         }
+        if (PAIR) asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
         tc_fence_before();
         mbar_arrive(&chunk_empty[buf]);
       }
@@ -271,7 +325,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         float v[16];
         if (EXACT) {
           float l[16];
-          tmem_ld16(lane_addr + static_cast<uint32_t>(2 * g.bn + c), l);
+          tmem_ld16(lane_addr + static_cast<uint32_t>((PAIR ? 1 : 2) * g.bn + c), l);
 #pragma unroll
           for (int i = 0; i < 16; ++i) v[i] = fmaf(l[i], g.lo_scale, sum[(c + i) & (EXACT ? 127 : 0)]);
         } else {
@@ -361,8 +415,10 @@ __global__ void splitk_reduce_kernel(const ConvGeom g) {
 template <int KC, bool EXACT>
 static cudaError_t launch_typed(const ConvMaps& maps, const ConvGeom& g, dim3 grid, size_t smem,
                                 cudaStream_t stream) {
-  auto kern = EXACT ? conv3d_umma_kernel<KC, EXACT, false>
-                    : (g.operand_tf32 ? conv3d_umma_kernel<KC, EXACT, !EXACT> : conv3d_umma_kernel<KC, EXACT, false>);
+  auto kern = EXACT ? (exact_pair(KC, g.bn, true) ? conv3d_umma_kernel<KC, EXACT, false, EXACT>
+                                                   : conv3d_umma_kernel<KC, EXACT, false, false>)
+                    : (g.operand_tf32 ? conv3d_umma_kernel<KC, EXACT, !EXACT, false>
+                                      : conv3d_umma_kernel<KC, EXACT, false, false>);
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
   if (e != cudaSuccess) return e;
   launch_kernel(kern, grid, kThreads, smem, stream, maps, g);
