@@ -28,9 +28,9 @@ namespace ctmr {
 int conv_stage_plan(int kc, int bn, bool exact, bool one_cta_per_sm, size_t* smem_bytes);
 cudaError_t launch_conv3d_umma(const ConvMaps& maps, const ConvGeom& g, int kc, bool exact, size_t smem,
                                cudaStream_t stream);
-int conv_v2_stage_plan(int kc, int mt, int tw, int bn, size_t* smem_bytes, size_t stats_bytes);
+int conv_v2_stage_plan(int kc, int mt, int tw, int bn, size_t* smem_bytes, size_t stats_bytes, bool exact);
 cudaError_t launch_conv3d_umma_v2(const ConvMaps& maps, const ConvGeom& g, int kc, int mt, int tw, int sms,
-                                  size_t smem, cudaStream_t stream);
+                                  size_t smem, bool exact, cudaStream_t stream);
 int conv_khcat_stage_plan(int kc, int bn, int mt, size_t* smem_bytes);
 int conv_khcat_rows();
 cudaError_t launch_conv3d_khcat(const ConvMaps& maps, const ConvGeom& g, int kc, int mt, int sms, size_t smem,
@@ -416,7 +416,7 @@ bool plan_khcat(const ConvPlan& p, const ctmr_conv3d_desc* d, KhPlan* k) {
 }
 
 bool plan_v2(const ConvPlan& p, const ctmr_conv3d_desc* d, bool with_stats, V2Plan* v) {
-  if (p.exact ||
+  if ((p.exact && with_stats) ||
       !(p.mode == ctmr::kModeConv3 || p.mode == ctmr::kModeUp2 || p.mode == ctmr::kModeConv1) || p.row_w < 16 ||
       p.row_h < 8 || getenv("CTMR_DISABLE_V2") != nullptr)
     return false;
@@ -426,6 +426,15 @@ bool plan_v2(const ConvPlan& p, const ctmr_conv3d_desc* d, bool with_stats, V2Pl
   // and refills faster (measured: 2 x 128 -> 64 at 64 x 64 x 32 54 -> 41 us, 1 x 128 -> 64 at
   // 96 x 256 x 128 549 -> 389 us; 1 x 256 -> 128 at 48 x 128 x 64 130 -> 135 us, so not above 64).
   v->mt = p.row_d >= 2 && !(p.mode == ctmr::kModeConv1 && p.opad <= 64) ? 2 : 1;
+  // The fp32 split mode: one depth per tile, so that two hi chunk buffers and a double-buffered lo
+  // accumulator (4 x bn columns) fit TMEM. On grids of fewer tiles than half the SMs the per-tap
+  // kernel's split-K fills the GPU better (measured: 64 tiles 1.2-1.8x slower here, 128 tiles 1.3x faster).
+  if (p.exact) {
+    v->mt = 1;
+    const long long tiles = static_cast<long long>((p.opad + std::min(p.opad, 128) - 1) / std::min(p.opad, 128)) *
+                            ((p.row_w + 15) / 16) * ((p.row_h + 7) / 8) * p.row_d * d->batch * p.phases;
+    if (2 * tiles < sm_count()) return false;
+  }
   v->bn = std::min(p.opad, 128);
   v->stats_bytes = 0;
   if (with_stats) {
@@ -444,7 +453,8 @@ bool plan_v2(const ConvPlan& p, const ctmr_conv3d_desc* d, bool with_stats, V2Pl
   for (int min_stages : {2}) {
     for (int cand : {64, 32, 16}) {
       size_t sm_b = 0;
-      const int st = p.cpad % cand ? 0 : ctmr::conv_v2_stage_plan(cand, v->mt, v->tw, v->bn, &sm_b, v->stats_bytes);
+      const int st =
+          p.cpad % cand ? 0 : ctmr::conv_v2_stage_plan(cand, v->mt, v->tw, v->bn, &sm_b, v->stats_bytes, p.exact);
       if (st >= min_stages) {
         v->kc = cand, v->smem = sm_b, v->stages = st;
         return true;
@@ -783,9 +793,10 @@ int ctmr_conv3d_stages(const ctmr_conv3d_desc* d, void* workspace, size_t worksp
       g.bn = bn;
       g.cout = d->out_channels;
       g.stages = stages2;
-      g.tmem_cols = static_cast<uint32_t>(std::max(32, next_pow2(2 * mt * bn)));
+      g.tmem_cols = static_cast<uint32_t>(std::max(32, next_pow2(p.exact ? 4 * bn : 2 * mt * bn)));
       g.operand_bf16 = p.bf16 ? 1 : 0;
-    g.operand_tf32 = p.tf32 ? 1 : 0;
+      g.operand_tf32 = p.tf32 ? 1 : 0;
+      g.lo_scale = 1.0f / 2048.0f;
       g.ksplit = 1;
       g.n_tiles = (p.opad + bn - 1) / bn;
       const long long total = static_cast<long long>(g.n_tiles) * g.tiles_w * g.tiles_h * g.tiles_d * d->batch *
@@ -813,13 +824,16 @@ int ctmr_conv3d_stages(const ctmr_conv3d_desc* d, void* workspace, size_t worksp
         const long long rs = a_cstride * 2;
         const long long W = p.in_w, H = p.in_h, D = p.in_d;
         // H before W: an 8-row swizzle atom holds 8 consecutive h of one w.
+        const long long wtaps = p.mode == ctmr::kModeUp2 ? 64 : (p.mode == ctmr::kModeConv1 ? 1 : 27);
         if (rs % 16 == 0 &&
             encode_act(&maps.a[0], a_hi, p.bf16, p.cpad, H, W, D, d->batch, W * rs, rs, H * W * rs, D * H * W * rs,
                        kc, 8, 16 + tw - 1, mt) == CTMR_OK &&
-            encode_weight3(&maps.b, w_hi, p.bf16, p.cpad, p.opad,
-                           p.mode == ctmr::kModeUp2 ? 64 : (p.mode == ctmr::kModeConv1 ? 1 : 27), kc, bn,
-                           tw) == CTMR_OK) {
-          cudaError_t e = ctmr::launch_conv3d_umma_v2(maps, g, kc, mt, tw, sm_count(), smem2, stream);
+            encode_weight3(&maps.b, w_hi, p.bf16, p.cpad, p.opad, wtaps, kc, bn, tw) == CTMR_OK &&
+            (!p.exact ||
+             (encode_act(&maps.a_lo[0], a_lo, false, p.cpad, H, W, D, d->batch, W * rs, rs, H * W * rs,
+                         D * H * W * rs, kc, 8, 16 + tw - 1, mt) == CTMR_OK &&
+              encode_weight3(&maps.b_lo, w_lo, false, p.cpad, p.opad, wtaps, kc, bn, tw) == CTMR_OK))) {
+          cudaError_t e = ctmr::launch_conv3d_umma_v2(maps, g, kc, mt, tw, sm_count(), smem2, p.exact, stream);
           return e == cudaSuccess ? CTMR_OK : cuda_fail(e, "conv3d v2 launch");
         }
         // Refused for this call's pointers or strides: this call takes the per-tap kernel (which

@@ -15,6 +15,14 @@
 // double-buffered in TMEM so the epilogue warps drain tile i while the MMA
 // issuer accumulates tile i + 1.
 //
+// EXACT (the fp32 mode, one depth per tile): every operand is carried as fp16 hi + lo planes
+// (hi = half(v), lo = half((v - hi) * 2^11)) and each K step issues hi*hi into a chunk buffer and
+// hi*lo + lo*hi into the tile's lo accumulator. The hi*hi products accumulate in chunks of at most
+// 512 K terms (whole stages), alternating between two TMEM buffers that the epilogue promotes into
+// fp32 registers as they complete; the lo accumulator is double-buffered across tiles. TMEM:
+// [hi0 | hi1 | lo0 | lo1], bn columns each. The same split-precision scheme as the per-tap kernel
+// (Ootomo & Yokota 2022), with the kw reuse of the input box.
+//
 // Modes: kModeConv3 (TW = 3; stages over (kd, kh)), kModeUp2 (TW = 2; stages
 // over the (td, th) of each nearest-2x parity, whose taps are the folded
 // weights of pack_weight(upsample=1)) and kModeConv1 (TW = 1: the 1x1x1
@@ -35,34 +43,43 @@ constexpr int kThreadsV2 = 192;
 
 __host__ __device__ constexpr uint32_t ru(uint32_t v, uint32_t a) { return (v + a - 1) / a * a; }
 
+// Stage: A (hi) | A lo | B (hi) | B lo; the lo planes only in EXACT.
 struct V2Layout {
-  uint32_t atom_bytes, a_m_bytes, a_bytes, b_tap_bytes, b_bytes, stage_bytes;
-  __host__ __device__ V2Layout(int kc, int mt, int tw, int bn) {
+  uint32_t atom_bytes, a_m_bytes, a_bytes, b_tap_bytes, b_bytes, b_off, stage_bytes;
+  __host__ __device__ V2Layout(int kc, int mt, int tw, int bn, bool exact = false) {
     atom_bytes = 8u * static_cast<uint32_t>(kc) * 2u;
     a_m_bytes = static_cast<uint32_t>(16 + tw - 1) * atom_bytes;
     a_bytes = ru(static_cast<uint32_t>(mt) * a_m_bytes, 1024);
     b_tap_bytes = static_cast<uint32_t>(bn) * kc * 2u;
     b_bytes = ru(static_cast<uint32_t>(tw) * b_tap_bytes, 1024);
-    stage_bytes = a_bytes + b_bytes;
+    b_off = a_bytes * (exact ? 2u : 1u);
+    stage_bytes = (a_bytes + b_bytes) * (exact ? 2u : 1u);
   }
 };
 
-template <int KC, int MT, int TW, bool STATS, bool TF32>
+// EXACT: whole stages per hi*hi promotion chunk (at most 512 K terms, at least one stage).
+__host__ __device__ constexpr int v2_chunk_stages(int kc, int tw) { return 512 / (tw * kc) > 0 ? 512 / (tw * kc) : 1; }
+
+template <int KC, int MT, int TW, bool STATS, bool TF32, bool EXACT>
 __global__ void __launch_bounds__(kThreadsV2, 1)
     conv3d_umma_v2_kernel(const __grid_constant__ ConvMaps maps, const __grid_constant__ ConvGeom g) {
+  static_assert(!EXACT || (MT == 1 && !STATS && !TF32), "the split mode: one depth per tile, fp16 planes");
+  constexpr int CH = v2_chunk_stages(KC, TW);
   constexpr uint32_t kRowBytes = KC * 2;
   constexpr int kSteps = KC / 16;
   constexpr int KDH = TW == 3 ? 9 : (TW == 2 ? 4 : 1);  // (kd, kh) or (td, th) pairs per tile (1x1: one)
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>(ru(smem_u32(smem_raw), 1024) - smem_u32(smem_raw) +
                                              reinterpret_cast<uintptr_t>(smem_raw));
-  const V2Layout L(KC, MT, TW, g.bn);
+  const V2Layout L(KC, MT, TW, g.bn, EXACT);
   const int S = g.stages;
   uint64_t* full = reinterpret_cast<uint64_t*>(smem + static_cast<size_t>(S) * L.stage_bytes);
   uint64_t* empty = full + S;
-  uint64_t* tmem_full = empty + S;      // [2]
+  uint64_t* tmem_full = empty + S;      // [2] (EXACT: the tile's lo accumulator)
   uint64_t* tmem_empty = tmem_full + 2;  // [2]
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(tmem_empty + 2);
+  uint64_t* chunk_full = tmem_empty + 2;   // [2] EXACT: a hi*hi chunk is complete
+  uint64_t* chunk_empty = chunk_full + 2;  // [2] EXACT: the epilogue has promoted that chunk buffer
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(chunk_empty + 2);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
   // Output statistics: one accumulator per epilogue warp, [4][batch][cout][3].
   float* s_stats = reinterpret_cast<float*>(smem + static_cast<size_t>(S) * L.stage_bytes + 256);
@@ -80,6 +97,8 @@ __global__ void __launch_bounds__(kThreadsV2, 1)
     for (int i = 0; i < 2; ++i) {
       mbar_init(&tmem_full[i], 1);
       mbar_init(&tmem_empty[i], 128);
+      mbar_init(&chunk_full[i], 1);
+      mbar_init(&chunk_empty[i], 128);
     }
     *abort_flag = 0;
     fence_barrier_init();
@@ -116,6 +135,10 @@ __global__ void __launch_bounds__(kThreadsV2, 1)
     // ------------------------------------------------------------ TMA producer
     tma_prefetch_desc(&maps.a[0]);
     tma_prefetch_desc(&maps.b);
+    if (EXACT) {
+      tma_prefetch_desc(&maps.a_lo[0]);
+      tma_prefetch_desc(&maps.b_lo);
+    }
     int it = 0;
     int issued = 0;
     for (int t = blockIdx.x; t < g.total_tiles && !*abort_flag; t += gridDim.x) {
@@ -151,10 +174,13 @@ __global__ void __launch_bounds__(kThreadsV2, 1)
           btap = phase * 8 + td * 4 + th * 2;
         }
         uint8_t* st_base = smem + static_cast<size_t>(s) * L.stage_bytes;
-        mbar_arrive_expect_tx(&full[s], static_cast<uint32_t>(MT) * L.a_m_bytes + static_cast<uint32_t>(TW) *
-                                                                                    L.b_tap_bytes);
+        mbar_arrive_expect_tx(&full[s], (static_cast<uint32_t>(MT) * L.a_m_bytes + static_cast<uint32_t>(TW) *
+                                                                                     L.b_tap_bytes) *
+                                            (EXACT ? 2u : 1u));
         tma_load_5d(st_base, &maps.a[0], &full[s], c, y, x, z, b);
-        tma_load_3d(st_base + L.a_bytes, &maps.b, &full[s], c, n0, btap);
+        if (EXACT) tma_load_5d(st_base + L.a_bytes, &maps.a_lo[0], &full[s], c, y, x, z, b);
+        tma_load_3d(st_base + L.b_off, &maps.b, &full[s], c, n0, btap);
+        if (EXACT) tma_load_3d(st_base + L.b_off + L.b_bytes, &maps.b_lo, &full[s], c, n0, btap);
         ++issued;
       }
     }
@@ -163,9 +189,66 @@ __global__ void __launch_bounds__(kThreadsV2, 1)
     }
   } else if (warp == 1 && lane == 0) {
     // ------------------------------------------------------------ MMA issuer
-    const uint32_t idesc = idesc_f16(g.operand_bf16 != 0, 128, bn, TF32);
+    const uint32_t idesc = idesc_f16(!EXACT && g.operand_bf16 != 0, 128, bn, TF32);
     int it = 0;
     int lt = 0;
+    if (EXACT) {
+      int chunk = 0;  // hi*hi chunks over all of this CTA's tiles
+      for (int t = blockIdx.x; t < g.total_tiles && !*abort_flag; t += gridDim.x, ++lt) {
+        const int lbuf = lt & 1;
+        if (lt >= 2 &&
+            !mbar_wait_bounded(&tmem_empty[lbuf], static_cast<uint32_t>((lt >> 1) - 1) & 1u, kErrWaitAcc)) {
+          *abort_flag = 1;
+          break;
+        }
+        const uint32_t acc_lo = tmem + static_cast<uint32_t>(2 + lbuf) * bn;
+        bool stop = false;
+        for (int st = 0; st < stages_per_tile; ++st, ++it) {
+          const int cs = st % CH;  // stage within the chunk
+          const int cbuf = chunk & 1;
+          if (cs == 0 && chunk >= 2 &&
+              !mbar_wait_bounded(&chunk_empty[cbuf], static_cast<uint32_t>((chunk >> 1) - 1) & 1u, kErrWaitAcc)) {
+            stop = true;
+            break;
+          }
+          const int s = it % S;
+          if (!mbar_wait_bounded(&full[s], static_cast<uint32_t>(it / S) & 1u, kErrWaitFull)) {
+            stop = true;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t a_base = smem_u32(smem + static_cast<size_t>(s) * L.stage_bytes);
+          const uint64_t a_hi0 = smem_desc_kmajor(a_base, kRowBytes);
+          const uint64_t a_lo0 = desc_advance(a_hi0, L.a_bytes);
+          const uint64_t b_hi0 = desc_advance(a_hi0, L.b_off);
+          const uint64_t b_lo0 = desc_advance(b_hi0, L.b_bytes);
+          const uint32_t acc_hi = tmem + static_cast<uint32_t>(cbuf) * bn;
+#pragma unroll
+          for (int kw = 0; kw < TW; ++kw) {
+            const uint32_t ao = static_cast<uint32_t>(kw) * L.atom_bytes, bo = static_cast<uint32_t>(kw) * L.b_tap_bytes;
+            const uint64_t a_hi = desc_advance(a_hi0, ao), a_lo = desc_advance(a_lo0, ao);
+            const uint64_t b_hi = desc_advance(b_hi0, bo), b_lo = desc_advance(b_lo0, bo);
+#pragma unroll
+            for (int k = 0; k < kSteps; ++k) {
+              const uint32_t kd = 2u * static_cast<uint32_t>(k);
+              umma_f16(acc_hi, a_hi + kd, b_hi + kd, idesc, (cs == 0 && kw == 0 && k == 0) ? 0u : 1u);
+              umma_f16(acc_lo, a_hi + kd, b_lo + kd, idesc, (st == 0 && kw == 0 && k == 0) ? 0u : 1u);
+              umma_f16(acc_lo, a_lo + kd, b_hi + kd, idesc, 1u);
+            }
+          }
+          umma_commit(&empty[s]);
+          if (cs == CH - 1 || st == stages_per_tile - 1) {  // a chunk ends with the tile at the latest
+            umma_commit(&chunk_full[cbuf]);
+            ++chunk;
+          }
+        }
+        if (stop) {
+          *abort_flag = 1;
+          break;
+        }
+        umma_commit(&tmem_full[lbuf]);
+      }
+    } else {
     for (int t = blockIdx.x; t < g.total_tiles && !*abort_flag; t += gridDim.x, ++lt) {
       const int buf = lt & 1;
       if (lt >= 2 &&
@@ -203,6 +286,7 @@ __global__ void __launch_bounds__(kThreadsV2, 1)
       }
       umma_commit(&tmem_full[buf]);
     }
+    }
   } else if (warp >= 2) {
     // ------------------------------------------------------------ epilogue
     const int quarter = warp & 3;
@@ -232,6 +316,72 @@ __global__ void __launch_bounds__(kThreadsV2, 1)
         res_base = (((static_cast<long long>(b) * g.res_d + qd) * g.res_h + qh) * g.res_w + qw) * g.res_cstride;
       }
     };
+    if (EXACT) {
+      // Promote each hi*hi chunk into fp32 registers as it completes, then fold in the tile's lo
+      // accumulator at 2^-11, add bias and residual, and store (the per-tap kernel's epilogue order).
+      const int nch = (stages_per_tile + CH - 1) / CH;
+      int chunk = 0;
+      int et = 0;
+      for (int t = blockIdx.x; t < g.total_tiles && !*abort_flag; t += gridDim.x, ++et) {
+        const int lbuf = et & 1;
+        decode(t, n0, w0, h0, d0, b, phase);
+        bool ok = true;
+        float sum[128];
+#pragma unroll
+        for (int i = 0; i < 128; ++i) sum[i] = 0.f;
+        for (int c = 0; c < nch && ok; ++c, ++chunk) {
+          const int cbuf = chunk & 1;
+          ok = __all_sync(0xffffffffu,
+                          mbar_wait_bounded(&chunk_full[cbuf], static_cast<uint32_t>(chunk >> 1) & 1u, kErrWaitAcc));
+          tc_fence_after();
+#pragma unroll
+          for (int cb = 0; cb < 8; ++cb) {
+            if (cb * 16 < g.bn) {
+              float v[16];
+              tmem_ld16(lane_addr + static_cast<uint32_t>(cbuf * g.bn + cb * 16), v);
+#pragma unroll
+              for (int i = 0; i < 16; ++i) sum[cb * 16 + i] += v[i];
+            }
+          }
+          tc_fence_before();
+          mbar_arrive(&chunk_empty[cbuf]);
+        }
+        ok = ok && __all_sync(0xffffffffu, mbar_wait_bounded(&tmem_full[lbuf], static_cast<uint32_t>(et >> 1) & 1u,
+                                                             kErrWaitAcc));
+        tc_fence_after();
+        bool valid;
+        long long out_base, res_base;
+        row_of(0, valid, out_base, res_base);
+        valid = valid && ok;
+        const float* bias = g.bias != nullptr ? g.bias + static_cast<long long>(b) * g.bias_bstride : nullptr;
+#pragma unroll
+        for (int cb = 0; cb < 8; ++cb) {
+          const int c = cb * 16;
+          if (c < g.bn) {
+            float l[16], v[16];
+            tmem_ld16(lane_addr + static_cast<uint32_t>((2 + lbuf) * g.bn + c), l);
+#pragma unroll
+            for (int i = 0; i < 16; ++i) v[i] = fmaf(l[i], g.lo_scale, sum[c + i]);
+            const int n = n0 + c;
+            if (valid && n < g.cout) {
+              if (bias != nullptr) {
+                const int cnt = min(16, g.cout - n);
+#pragma unroll
+                for (int i = 0; i < 16; ++i)
+                  if (i < cnt) v[i] += __ldg(bias + n + i);
+              }
+              store_row16(g, v, n, out_base + n, res_base + n);
+            }
+          }
+        }
+        tc_fence_before();
+        mbar_arrive(&tmem_empty[lbuf]);
+        if (!ok) {
+          *abort_flag = 1;
+          break;
+        }
+      }
+    }
     auto issue = [&](int k, uint32_t(&w)[64]) {
       if (g.res == nullptr) return;
       const int m = k / halves, c0 = (k - m * halves) * 64;
@@ -289,7 +439,7 @@ __global__ void __launch_bounds__(kThreadsV2, 1)
       for (int e = lane; e < g.batch * g.cout * 3; e += 32) mine[e] = 0.f;
       __syncwarp();
     }
-    for (int t = blockIdx.x; t < g.total_tiles && !*abort_flag; t += gridDim.x, ++lt) {
+    for (int t = blockIdx.x; !EXACT && t < g.total_tiles && !*abort_flag; t += gridDim.x, ++lt) {
       const int buf = lt & 1;
       decode(t, n0, w0, h0, d0, b, phase);
       uint32_t ra[64], rb[64];
@@ -352,13 +502,16 @@ __global__ void __launch_bounds__(kThreadsV2, 1)
 }
 
 template <int KC, int MT, int TW>
-cudaError_t launch_v2_typed(const ConvMaps& maps, const ConvGeom& g, int grid, size_t smem, cudaStream_t stream) {
+cudaError_t launch_v2_typed(const ConvMaps& maps, const ConvGeom& g, int grid, size_t smem, bool exact,
+                            cudaStream_t stream) {
   // The statistics epilogue is a separate instantiation so the plain kernel keeps its registers;
-  // TF32 operands are a third (the planner gives them no statistics).
+  // TF32 operands are a third (the planner gives them no statistics), the fp32 split mode a fourth.
   if (g.operand_tf32 && g.stats != nullptr) return cudaErrorInvalidValue;
-  auto kern = g.operand_tf32 ? conv3d_umma_v2_kernel<KC, MT, TW, false, true>
-                             : (g.stats != nullptr ? conv3d_umma_v2_kernel<KC, MT, TW, true, false>
-                                                   : conv3d_umma_v2_kernel<KC, MT, TW, false, false>);
+  if (exact && (MT != 1 || g.stats != nullptr || g.operand_tf32)) return cudaErrorInvalidValue;
+  auto kern = exact ? conv3d_umma_v2_kernel<KC, MT, TW, false, false, MT == 1>
+                    : g.operand_tf32 ? conv3d_umma_v2_kernel<KC, MT, TW, false, true, false>
+                                     : (g.stats != nullptr ? conv3d_umma_v2_kernel<KC, MT, TW, true, false, false>
+                                                           : conv3d_umma_v2_kernel<KC, MT, TW, false, false, false>);
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
   if (e != cudaSuccess) return e;
   return launch_kernel(kern, grid, kThreadsV2, smem, stream, maps, g);
@@ -368,8 +521,8 @@ cudaError_t launch_v2_typed(const ConvMaps& maps, const ConvGeom& g, int grid, s
 
 // Shared-memory plan of the v2 kernel: the deepest pipeline (<= 6 stages) that
 // fits one CTA per SM; 0 when fewer than 2 stages fit.
-int conv_v2_stage_plan(int kc, int mt, int tw, int bn, size_t* smem_bytes, size_t stats_bytes) {
-  const V2Layout L(kc, mt, tw, bn);
+int conv_v2_stage_plan(int kc, int mt, int tw, int bn, size_t* smem_bytes, size_t stats_bytes, bool exact) {
+  const V2Layout L(kc, mt, tw, bn, exact);
   const size_t extra = 1024 + 256 + stats_bytes;
   int stages = static_cast<int>((227 * 1024 - extra) / L.stage_bytes);
   if (stages > 6) stages = 6;
@@ -379,11 +532,11 @@ int conv_v2_stage_plan(int kc, int mt, int tw, int bn, size_t* smem_bytes, size_
 }
 
 cudaError_t launch_conv3d_umma_v2(const ConvMaps& maps, const ConvGeom& g, int kc, int mt, int tw, int sms,
-                                  size_t smem, cudaStream_t stream) {
+                                  size_t smem, bool exact, cudaStream_t stream) {
   if (g.total_tiles <= 0) return cudaErrorInvalidValue;
   const int grid = g.total_tiles < sms ? g.total_tiles : sms;
 #define CTMR_V2(KC_, MT_, TW_) \
-  if (kc == KC_ && mt == MT_ && tw == TW_) return launch_v2_typed<KC_, MT_, TW_>(maps, g, grid, smem, stream);
+  if (kc == KC_ && mt == MT_ && tw == TW_) return launch_v2_typed<KC_, MT_, TW_>(maps, g, grid, smem, exact, stream);
   CTMR_V2(64, 2, 3) CTMR_V2(32, 2, 3) CTMR_V2(16, 2, 3)
   CTMR_V2(64, 1, 3) CTMR_V2(32, 1, 3) CTMR_V2(16, 1, 3)
   CTMR_V2(64, 2, 2) CTMR_V2(32, 2, 2) CTMR_V2(16, 2, 2)
