@@ -21,11 +21,16 @@
 
 #include "groupnorm.cuh"
 #include "launch.cuh"
+#include "ptx.cuh"
 
 namespace ctmr {
 namespace {
 
 constexpr int kGnThreads = 256;
+// Bulk-staged pass 1 (dense fp32 rows): the block's voxel range streams through a ring of
+// kGnStages shared-memory segments of at most kGnSegBytes, filled by cp.async.bulk copies.
+constexpr int kGnStages = 4;
+constexpr int kGnSegBytes = 16 << 10;
 
 __device__ __forceinline__ float gn_load(const PrepSource& s, long long vox, int c) {
   const long long i = vox * s.cstride + c;
@@ -85,13 +90,18 @@ __device__ __forceinline__ Moments merge(Moments a, Moments b) {
   return r;
 }
 
+// BULK: the sources are dense fp32 rows (cstride == channels, channel counts multiples of 8,
+// 16-byte aligned): the voxels come through the shared-memory ring instead of per-thread loads,
+// so the bytes in flight do not depend on registers. Same per-thread arithmetic either way.
+template <bool BULK>
 __global__ void __launch_bounds__(kGnThreads) gn_partial_kernel(const GnParams p) {
   griddep_wait();  // the preceding kernel's writes are visible from here on
   griddep_launch_dependents();
   __shared__ float s_sum[kGnThreads][8];   // per thread, then per warp: sums of (x - pivot)
   __shared__ float s_sq[kGnThreads][8];    // ... of (x - pivot)^2
   __shared__ float s_n[kGnThreads];
-  extern __shared__ float s_chan[];        // [ctot][3]: (count, mean, M2) per channel
+  __shared__ uint64_t s_full[kGnStages];   // BULK: a ring segment has landed
+  extern __shared__ float s_chan[];        // [ctot][3]: (count, mean, M2) per channel; BULK: then the ring
   const int ctot = p.src[0].channels + p.src[1].channels;
   const int nslices = (ctot + 7) / 8;
   const int lanes = kGnThreads / nslices;
@@ -119,7 +129,67 @@ __global__ void __launch_bounds__(kGnThreads) gn_partial_kernel(const GnParams p
     int cnt;
     gn_load8(p, base + v_begin, slice * 8, pivot, cnt);
   }
-  if (lane < lanes) {
+  if (BULK) {
+    const int c0n = p.src[0].channels, c1n = p.src[1].channels;
+    const int seg = max(1, kGnSegBytes / (ctot * 4));  // voxels per segment
+    const long long nvox = v_end - v_begin;
+    const int nseg = static_cast<int>((nvox + seg - 1) / seg);
+    float* ring = s_chan + ((ctot * 3 + 3) & ~3);     // 16-byte aligned after the channel moments
+    const int stage_floats = seg * ctot;
+    if (tid == 0) {
+      for (int i = 0; i < kGnStages; ++i) mbar_init(&s_full[i], 1);
+      fence_barrier_init();
+    }
+    __syncthreads();
+    int issued = 0;
+    auto issue = [&](int k) {  // segment k into ring slot k % kGnStages (thread 0)
+      const int st = k % kGnStages;
+      const long long v0 = v_begin + static_cast<long long>(k) * seg;
+      const int nv = static_cast<int>(min(static_cast<long long>(seg), v_end - v0));
+      const uint32_t b0 = static_cast<uint32_t>(nv * c0n * 4), b1 = static_cast<uint32_t>(nv * c1n * 4);
+      float* dst = ring + static_cast<size_t>(st) * stage_floats;
+      mbar_arrive_expect_tx(&s_full[st], b0 + b1);
+      bulk_load(dst, static_cast<const float*>(p.src[0].ptr) + (base + v0) * c0n, b0, &s_full[st]);
+      if (c1n > 0)
+        bulk_load(dst + seg * c0n, static_cast<const float*>(p.src[1].ptr) + (base + v0) * c1n, b1, &s_full[st]);
+      ++issued;
+    };
+    if (tid == 0)
+      for (int k = 0; k < nseg && k < kGnStages; ++k) issue(k);
+    bool ok = true;
+    int consumed = 0;
+    for (int k = 0; k < nseg; ++k) {
+      const int st = k % kGnStages;
+      ok = ok && mbar_wait_bounded(&s_full[st], static_cast<uint32_t>(k / kGnStages) & 1u, kErrWaitFull);
+      if (ok && lane < lanes) {
+        const long long v0 = v_begin + static_cast<long long>(k) * seg;
+        const int nv = static_cast<int>(min(static_cast<long long>(seg), v_end - v0));
+        const int c = slice * 8;
+        const float* row0 = ring + static_cast<size_t>(st) * stage_floats +
+                            (c < c0n ? c : seg * c0n + (c - c0n));
+        const int pitch = c < c0n ? c0n : c1n;
+        for (int j = lane; j < nv; j += lanes) {
+          const float4 a = reinterpret_cast<const float4*>(row0 + j * pitch)[0];
+          const float4 bq = reinterpret_cast<const float4*>(row0 + j * pitch)[1];
+          const float x[8] = {a.x, a.y, a.z, a.w, bq.x, bq.y, bq.z, bq.w};
+#pragma unroll
+          for (int i = 0; i < 8; ++i) {
+            const float d = x[i] - pivot[i];
+            s[i] += d;
+            q[i] = fmaf(d, d, q[i]);
+          }
+          n += 1.f;
+        }
+      }
+      ++consumed;
+      __syncthreads();  // every thread is done with slot st
+      if (tid == 0 && ok && k + kGnStages < nseg) issue(k + kGnStages);
+    }
+    // A copy still in flight (only after a timed-out wait) lands before the block can exit.
+    if (tid == 0)
+      for (int k = consumed; k < issued; ++k)
+        mbar_wait_bounded(&s_full[k % kGnStages], static_cast<uint32_t>(k / kGnStages) & 1u, kErrWaitDrain);
+  } else if (lane < lanes) {
     long long v = v_begin + lane;
     // Four voxels per step, all loads issued before any accumulation.
     for (; v + 3 * lanes < v_end; v += 4 * lanes) {
@@ -419,7 +489,8 @@ int gn_chunks_for(int batch, long long voxels, int channels) {
   static const int wave = [] {
     const int sms = device_sm_count();
     int per_sm = 0;
-    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, gn_partial_kernel, kGnThreads, 1024) != cudaSuccess ||
+    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, gn_partial_kernel<false>, kGnThreads, 1024) !=
+            cudaSuccess ||
         per_sm < 1)
       per_sm = 1;
     return sms * per_sm;
@@ -432,16 +503,45 @@ int gn_chunks_for(int batch, long long voxels, int channels) {
   return static_cast<int>(chunks);
 }
 
-cudaError_t launch_group_norm_affine(const GnParams& p, cudaStream_t stream) {
+namespace {
+// Whether pass 1 can stream the sources through the shared-memory ring: dense fp32 rows whose
+// channel counts (and the concat boundary) are multiples of 8, 16-byte aligned.
+bool gn_bulk_ok(const GnParams& p) {
+  for (int i = 0; i < 2; ++i) {
+    const PrepSource& q = p.src[i];
+    if (q.channels == 0) continue;
+    if (q.bf16 || q.cstride != q.channels || q.channels % 8 || (reinterpret_cast<uintptr_t>(q.ptr) & 15)) return false;
+  }
+  return p.src[0].channels > 0;
+}
+
+// Pass 1 over all chunks: the bulk-staged kernel where it applies (its dynamic shared memory is the
+// channel moments, then the ring), the per-thread-load kernel otherwise.
+cudaError_t launch_gn_partial(const GnParams& p, cudaStream_t stream) {
   const int ctot = p.src[0].channels + p.src[1].channels;
   const size_t chan_smem = static_cast<size_t>(ctot) * 3 * sizeof(float);
-  if (chan_smem > 48 * 1024) {
-    cudaError_t e = cudaFuncSetAttribute(gn_partial_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                         static_cast<int>(chan_smem));
+  const bool bulk = gn_bulk_ok(p);
+  const int seg = bulk ? std::max(1, kGnSegBytes / (ctot * 4)) : 0;
+  const size_t smem = bulk ? ((chan_smem + 15) & ~static_cast<size_t>(15)) +
+                                 static_cast<size_t>(kGnStages) * seg * ctot * sizeof(float)
+                           : chan_smem;
+  auto kern = bulk ? gn_partial_kernel<true> : gn_partial_kernel<false>;
+  if (smem > 48 * 1024) {
+    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
     if (e != cudaSuccess) return e;
   }
-  launch_kernel(gn_partial_kernel, dim3(p.chunks, p.batch), dim3(kGnThreads), chan_smem, stream, p);
-  cudaError_t e = cudaGetLastError();
+  if (bulk) {  // two ring-holding blocks per SM need the whole unified L1 as shared memory
+    cudaError_t e =
+        cudaFuncSetAttribute(kern, cudaFuncAttributePreferredSharedMemoryCarveout, cudaSharedmemCarveoutMaxShared);
+    if (e != cudaSuccess) return e;
+  }
+  launch_kernel(kern, dim3(p.chunks, p.batch), dim3(kGnThreads), smem, stream, p);
+  return cudaGetLastError();
+}
+}  // namespace
+
+cudaError_t launch_group_norm_affine(const GnParams& p, cudaStream_t stream) {
+  cudaError_t e = launch_gn_partial(p, stream);
   if (e != cudaSuccess) return e;
   if (p.chunks > kFinThreads * kFinPerThread) return cudaErrorInvalidValue;
   launch_kernel(gn_finalize_kernel, dim3(p.groups, p.batch), dim3(kFinThreads), 0, stream, p);
@@ -457,16 +557,8 @@ cudaError_t launch_group_norm_from_stats(const GnStatsParams& p, cudaStream_t st
 }
 
 cudaError_t launch_group_norm_moments(const GnParams& p, float* moments, cudaStream_t stream) {
-  const int ctot = p.src[0].channels + p.src[1].channels;
-  const size_t chan_smem = static_cast<size_t>(ctot) * 3 * sizeof(float);
-  if (chan_smem > 48 * 1024) {
-    cudaError_t e = cudaFuncSetAttribute(gn_partial_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                         static_cast<int>(chan_smem));
-    if (e != cudaSuccess) return e;
-  }
   if (p.chunks > kFinThreads * kFinPerThread) return cudaErrorInvalidValue;
-  launch_kernel(gn_partial_kernel, dim3(p.chunks, p.batch), dim3(kGnThreads), chan_smem, stream, p);
-  cudaError_t e = cudaGetLastError();
+  cudaError_t e = launch_gn_partial(p, stream);
   if (e != cudaSuccess) return e;
   launch_kernel(gn_moments_kernel, dim3(p.groups, p.batch), dim3(kFinThreads), 0, stream, p, moments);
   return cudaGetLastError();
