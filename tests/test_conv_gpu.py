@@ -65,6 +65,34 @@ def test_conv_fp32_matches_float64(cuda, shape, out_channels, stride):
     _close_fp32(y, expected)
 
 
+# Grids with at least half as many persistent tiles (8 h x 16 w of one depth, per N tile) as SMs: the
+# fp32 mode runs on the atom-shifted kernel's split-precision variant there (3x3x3 with one and two N
+# tiles, 1x1x1, the nearest-2x fold), held to the reference's bar like the per-tap kernel.
+PERSISTENT_EXACT = [
+    ((2, 64, 16, 32, 32), 64, 3, False),
+    ((1, 96, 12, 32, 32), 128, 3, False),
+    ((1, 32, 8, 32, 32), 256, 3, False),
+    ((2, 64, 16, 32, 32), 48, 1, False),
+    ((1, 64, 8, 16, 16), 64, 3, True),
+]
+
+
+@pytest.mark.parametrize(("shape", "out_channels", "k", "upsample"), PERSISTENT_EXACT)
+def test_conv_fp32_persistent_kernel_matches_float64(cuda, shape, out_channels, k, upsample):
+    from ctmr_b200 import ops
+
+    rng = np.random.default_rng(11)
+    x = torch.from_numpy(rng.standard_normal(shape).astype(np.float32))
+    c = shape[1]
+    w = torch.from_numpy((rng.standard_normal((out_channels, c, k, k, k)) / np.sqrt(k ** 3 * c)).astype(np.float32))
+    b = torch.from_numpy(rng.standard_normal(out_channels).astype(np.float32))
+    packed = ops.pack_weight(w.to(cuda), "fp32", upsample=upsample)
+    y = ops.conv3d(ops.to_ndhwc(x.to(cuda)), packed, b.to(cuda))
+    torch.cuda.synchronize()
+    xin = ops_ref.upsample_nearest_ref(x.double()) if upsample else x.double()
+    _close_fp32(y, ops_ref.conv3d_ref(xin, w.double(), b.double()))
+
+
 @pytest.mark.parametrize("precision", ["bf16", "fp16", "tf32"])
 @pytest.mark.parametrize(("shape", "out_channels", "stride"), SHAPES)
 def test_conv_16bit_matches_float64(cuda, shape, out_channels, stride, precision):
