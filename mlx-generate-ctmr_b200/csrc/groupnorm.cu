@@ -320,6 +320,11 @@ constexpr int kFinPerThread = 5;  // ceil(gn_max_chunks(1) / kFinThreads)
 // The (count, mean, M2) of group g of batch item b over all chunk partials, merged in a
 // fixed order (per thread its strided chunks, a shuffle tree per warp, then the warps in
 // order) in double precision; the result is valid in thread 0.
+// The chunk partials of group g, batch item b, merged in a fixed order: each (n, mean, M2) becomes
+// (n, S = n mean, Q = M2 + n mean^2) in double, which add without a division (each thread its
+// strided chunks in order, a shuffle-xor tree per warp, then the warps in order); the whole group's
+// (n, mean, M2) follows from one division at the end. In double the final Q - S mean loses
+// log2(mean^2 / var) of 53 bits, harmless for activations. Valid in thread 0.
 __device__ __forceinline__ MomentsD merge_chunks(const GnParams& p, int g, int b, double (*s_m)[3]) {
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   float q[kFinPerThread][3];
@@ -337,27 +342,42 @@ __device__ __forceinline__ MomentsD merge_chunks(const GnParams& p, int g, int b
       q[j][2] = 0.f;
     }
   }
-  MomentsD m{0.0, 0.0, 0.0};
+  double n = 0.0, sum = 0.0, sq = 0.0;
 #pragma unroll
-  for (int j = 0; j < kFinPerThread; ++j) m = merge_d(m, MomentsD{q[j][0], q[j][1], q[j][2]});
+  for (int j = 0; j < kFinPerThread; ++j) {
+    const double nn = q[j][0], mm = q[j][1];
+    n += nn;
+    sum += nn * mm;
+    sq += static_cast<double>(q[j][2]) + nn * mm * mm;
+  }
 #pragma unroll
-  for (int off = 1; off < 32; off <<= 1) {
-    const MomentsD o = shfl_down_moments(m, off);
-    if ((lane & (2 * off - 1)) == 0) m = merge_d(m, o);
+  for (int off = 16; off > 0; off >>= 1) {
+    n += __shfl_xor_sync(0xffffffffu, n, off);
+    sum += __shfl_xor_sync(0xffffffffu, sum, off);
+    sq += __shfl_xor_sync(0xffffffffu, sq, off);
   }
   if (lane == 0) {
-    s_m[warp][0] = m.n;
-    s_m[warp][1] = m.mean;
-    s_m[warp][2] = m.m2;
+    s_m[warp][0] = n;
+    s_m[warp][1] = sum;
+    s_m[warp][2] = sq;
   }
   __syncthreads();
   MomentsD t{0.0, 0.0, 0.0};
-  if (tid == 0)
-    for (int w = 0; w < kFinThreads / 32; ++w) t = merge_d(t, MomentsD{s_m[w][0], s_m[w][1], s_m[w][2]});
+  if (tid == 0) {
+    double tn = 0.0, ts = 0.0, tq = 0.0;
+    for (int w = 0; w < kFinThreads / 32; ++w) {
+      tn += s_m[w][0];
+      ts += s_m[w][1];
+      tq += s_m[w][2];
+    }
+    if (tn > 0.0) {
+      const double mean = ts / tn;
+      t = MomentsD{tn, mean, fmax(0.0, tq - ts * mean)};
+    }
+  }
   return t;
 }
 
-// scale = gamma * rstd, offset = beta - mean * scale for the channels of group g.
 __device__ __forceinline__ void write_group_affine(double mean, double rstd, int g, int b, int ctot, int cpg,
                                                    const float* gamma, const float* beta, float* affine) {
   for (int c = g * cpg + static_cast<int>(threadIdx.x); c < (g + 1) * cpg; c += kFinThreads) {
