@@ -11,11 +11,12 @@
 // each warp, then the warps in order through shared memory. Channels then merge
 // into groups in a fixed order (Chan et al.'s pairwise update), one (n, mean,
 // M2) partial per group.
-// Pass 2 (grid groups x batch): one block per group merges the chunk partials
-// (each thread its strided chunks in order, a fixed shuffle tree per warp, then
-// the warps in order) in double precision, then writes
-// scale = gamma * rstd and offset = beta - mean * scale for each channel. The
-// fixed merge order makes the result bitwise reproducible run to run.
+// Pass 2 (grid groups x batch): one block per group merges the chunk partials as
+// double-precision sums (n, n mean, M2 + n mean^2: each thread its strided chunks
+// in order, a fixed shuffle-xor tree per warp, then the warps in order; one
+// division at the end), then writes scale = gamma * rstd and offset =
+// beta - mean * scale for each channel. The fixed merge order makes the result
+// bitwise reproducible run to run.
 #include <cuda_runtime.h>
 #include <cstdint>
 
