@@ -35,6 +35,8 @@ int conv_khcat_stage_plan(int kc, int bn, int mt, size_t* smem_bytes);
 int conv_khcat_rows();
 cudaError_t launch_conv3d_khcat(const ConvMaps& maps, const ConvGeom& g, int kc, int mt, int sms, size_t smem,
                                 cudaStream_t stream);
+int conv_khcat_pair_stage_plan(size_t* smem_bytes);
+cudaError_t launch_conv3d_khcat_pair(const ConvMaps& maps, const ConvGeom& g, size_t smem, cudaStream_t stream);
 extern __device__ unsigned int g_device_error;
 }  // namespace ctmr
 
@@ -131,15 +133,17 @@ int encode_weight3(CUtensorMap* map, const void* base, bool bf16, long long cpad
 }
 
 // 5-D view (c, o, kw, kh, kd) of 3x3x3 packed weights [kd][kh][kw][O][C]: a box of
-// (kc, opad, 1, 3, 1) holds the three kh taps of one (kd, kw) as 3 x opad rows.
-int encode_weight_kh(CUtensorMap* map, const void* base, bool bf16, long long cpad, long long opad, int kc) {
+// (kc, box_o, 1, 3, 1) holds the three kh taps of one (kd, kw) as 3 x box_o rows (box_o = opad,
+// or half of it for one CTA of a pair).
+int encode_weight_kh(CUtensorMap* map, const void* base, bool bf16, long long cpad, long long opad, int kc,
+                     long long box_o) {
   auto enc = tensor_map_encoder();
   if (enc == nullptr) return fail(CTMR_ERR_CUDA, "cuTensorMapEncodeTiled is unavailable");
   const long long tap = cpad * 2 * opad;
   cuuint64_t dims[5] = {static_cast<cuuint64_t>(cpad), static_cast<cuuint64_t>(opad), 3, 3, 3};
   cuuint64_t strides[4] = {static_cast<cuuint64_t>(cpad * 2), static_cast<cuuint64_t>(tap),
                            static_cast<cuuint64_t>(3 * tap), static_cast<cuuint64_t>(9 * tap)};
-  cuuint32_t box[5] = {static_cast<cuuint32_t>(kc), static_cast<cuuint32_t>(opad), 1, 3, 1};
+  cuuint32_t box[5] = {static_cast<cuuint32_t>(kc), static_cast<cuuint32_t>(box_o), 1, 3, 1};
   cuuint32_t estr[5] = {1, 1, 1, 1, 1};
   CUresult r = enc(map, bf16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 5,
                    const_cast<void*>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
@@ -766,10 +770,28 @@ int ctmr_conv3d_stages(const ctmr_conv3d_desc* d, void* workspace, size_t worksp
       // the windows of all three kw taps.
       if (rs % 16 == 0 &&
           encode_act(&maps.a[0], a_hi, p.bf16, p.cpad, H, W, D, d->batch, W * rs, rs, H * W * rs, D * H * W * rs,
-                     kh.kc, 16, 10, md) == CTMR_OK &&
-          encode_weight_kh(&maps.b, w_hi, p.bf16, p.cpad, p.opad, kh.kc) == CTMR_OK) {
-        cudaError_t e = ctmr::launch_conv3d_khcat(maps, g, kh.kc, kh.mt, sm_count(), kh.smem, stream);
-        return e == cudaSuccess ? CTMR_OK : cuda_fail(e, "conv3d kh-concatenated launch");
+                     kh.kc, 16, 10, md) == CTMR_OK) {
+        // CTMR_KHCAT_PAIR=1: 64 -> 64 channels in 64-channel blocks, two depths per tile, on the
+        // CTA-pair kernel (each SM streams half of every weight box). Off by default: it measured
+        // slower than the one-SM kernel (0.821 vs 0.763 ms on 1 x 64 x 96 x 256 x 128 -> 64).
+        size_t smem_pair = 0;
+        const char* pair_env = getenv("CTMR_KHCAT_PAIR");
+        if (kh.kc == 64 && kh.mt == 2 && p.opad == 64 && !p.tf32 && g.total_tiles >= 2 && pair_env != nullptr &&
+            pair_env[0] == '1') {
+          const int st = ctmr::conv_khcat_pair_stage_plan(&smem_pair);
+          ctmr::ConvMaps maps_pair = maps;
+          if (st >= 2 && encode_weight_kh(&maps_pair.b, w_hi, p.bf16, p.cpad, p.opad, kh.kc, p.opad / 2) == CTMR_OK) {
+            ctmr::ConvGeom gp = g;
+            gp.stages = st;
+            cudaError_t e = ctmr::launch_conv3d_khcat_pair(maps_pair, gp, smem_pair, stream);
+            if (e == cudaSuccess) return CTMR_OK;
+            if (e != cudaErrorNotSupported) return cuda_fail(e, "conv3d kh-concatenated pair launch");
+          }
+        }
+        if (encode_weight_kh(&maps.b, w_hi, p.bf16, p.cpad, p.opad, kh.kc, p.opad) == CTMR_OK) {
+          cudaError_t e = ctmr::launch_conv3d_khcat(maps, g, kh.kc, kh.mt, sm_count(), kh.smem, stream);
+          return e == cudaSuccess ? CTMR_OK : cuda_fail(e, "conv3d kh-concatenated launch");
+        }
       }
       // A refused tensor map depends on this call's pointers and strides only: this call falls
       // through to the other kernels, later calls try again.

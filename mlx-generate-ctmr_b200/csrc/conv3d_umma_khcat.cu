@@ -24,6 +24,8 @@
 // with 16-wide lane shuffles and release it, then add bias and residual and
 // store while the next tile's MMAs run (with 64 output channels through an
 // 8-lane transpose, so that each warp store writes whole 128-byte lines).
+// A CTA-pair variant (clusters of two, tcgen05.mma.cta_group::2 with M = 256) is at
+// the end of the file; it runs only when CTMR_KHCAT_PAIR=1 selects it.
 #include <cuda_bf16.h>
 #include <cuda_fp16.h>
 
@@ -528,6 +530,324 @@ __global__ void __launch_bounds__(kKhThreads, 1)
   }
 }
 
+// ---------------------------------------------------------------- CTA-pair variant
+// 64 -> 64 channels, 64-channel blocks, two depths per tile: the same tiling, but two CTAs of a
+// cluster (one per SM) share every product. tcgen05.mma.cta_group::2 with M = 256 takes rows
+// 0..127 from the first CTA's activation box (its tile) and rows 128..255 from the second's (the
+// pair's other tile), and B's N = 192 rows half from each CTA: CTA r loads the three kh taps of
+// output channels 32 r .. 32 r + 31, a (64 c, 32 o, 1, 3, 1) box of the weight view. So each SM
+// streams half of every weight box (12 KB instead of 24 KB per (kd, kw)), reads half of B from
+// shared memory per product, and one thread issues the products of both tiles. Each CTA's TMEM
+// receives its own tile's 128 rows x 192 columns; column 96 h + 32 kh + (o - 32 h) holds P_kh
+// of output channel o, h = o / 32. Both CTAs' copies of a stage count on the first CTA's
+// barriers; the products' commits arrive on both CTAs' ring and accumulator barriers; each CTA's
+// epilogue warps release a depth on the first CTA's barrier (16 warp arrivals).
+constexpr int kPairKC = 64;
+constexpr int kPairMT = 2;
+constexpr int kPairBN = 64;
+constexpr uint32_t kPairN = 3u * kPairBN;                         // accumulator columns per depth
+constexpr uint32_t kPairKwBytes = 16u * kPairKC * 2u;             // 16 rows: one kw step
+constexpr uint32_t kPairAmBytes = kKhBoxW * kPairKwBytes;         // one depth of the activation box
+constexpr uint32_t kPairABytes = kPairMT * kPairAmBytes;          // 40 KB
+constexpr uint32_t kPairBBytes = 3u * (kPairBN / 2) * kPairKC * 2u;  // 12 KB: this CTA's half of N
+constexpr int kPairASlots = 2;
+static_assert(kPairBBytes % 1024 == 0 && kPairABytes % 1024 == 0, "ring slots stay swizzle-atom aligned");
+static_assert(kPairMT * kPairN <= 512, "both depths' accumulators fit one TMEM allocation");
+
+__global__ void __launch_bounds__(kKhThreads, 1)
+    conv3d_khcat_pair_kernel(const __grid_constant__ ConvMaps maps, const __grid_constant__ ConvGeom g) {
+  constexpr uint32_t kRowBytes = kPairKC * 2;
+  constexpr int kSteps = kPairKC / 16;
+  constexpr int SA = kPairASlots;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>(ru_kh(smem_u32(smem_raw), 1024) - smem_u32(smem_raw) +
+                                             reinterpret_cast<uintptr_t>(smem_raw));
+  const int S = g.stages;  // weight ring slots
+  uint8_t* b_ring = smem + static_cast<size_t>(SA) * kPairABytes;
+  uint64_t* a_full = reinterpret_cast<uint64_t*>(b_ring + static_cast<size_t>(S) * kPairBBytes);
+  uint64_t* a_empty = a_full + SA;
+  uint64_t* full = a_empty + SA;  // weight ring
+  uint64_t* empty = full + S;
+  uint64_t* tmem_full = empty + S;       // [1]: the pair's accumulators complete
+  uint64_t* tmem_empty = tmem_full + 2;  // [2]: depth m read out by both CTAs (first CTA's barrier)
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(tmem_empty + 2);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const uint32_t rank = cluster_ctarank();  // 0: the CTA whose thread issues the products
+  const int pair = static_cast<int>(blockIdx.x >> 1);
+  const int pairs = static_cast<int>(gridDim.x >> 1);
+  const int pair_tiles = (g.total_tiles + 1) >> 1;
+  const int groups_per_tile = 3 * g.kblocks;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < SA; ++s) {
+      mbar_init(&a_full[s], 1);
+      mbar_init(&a_empty[s], 1);
+    }
+    for (int s = 0; s < S; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&tmem_full[i], 1);
+      mbar_init(&tmem_empty[i], 16);
+    }
+    *abort_flag = 0;
+    fence_barrier_init();
+  }
+  if (warp == 1) {
+    tmem_alloc_pair(tmem_slot, 512);
+    tmem_relinquish_pair();
+  }
+  tc_fence_before();
+  __syncthreads();
+  cluster_sync();  // both CTAs' barriers exist before a copy, commit or arrive crosses the pair
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+  griddep_wait();
+  griddep_launch_dependents();
+
+  // Pair tile pt holds tiles 2 pt (first CTA) and 2 pt + 1 (second); tile t -> (w tile fastest,
+  // then h, d, batch item). With an odd tile count the last pair's second CTA computes a copy of
+  // the last tile and stores nothing.
+  auto decode = [&](int t, int& w0, int& h0, int& d0, int& b) {
+    const int tw_i = t % g.tiles_w; t /= g.tiles_w;
+    const int th_i = t % g.tiles_h; t /= g.tiles_h;
+    const int td_i = t % g.tiles_d;
+    b = t / g.tiles_d;
+    w0 = tw_i * 8;
+    h0 = th_i * kKhRows;
+    d0 = td_i * kPairMT;
+  };
+
+  if (warp == 0 && lane == 0) {
+    // ------------------------------------------------------------ TMA producer (both CTAs)
+    tma_prefetch_desc(&maps.a[0]);
+    tma_prefetch_desc(&maps.b);
+    const uint32_t a_full0 = cluster_addr(a_full, 0);
+    const uint32_t full0 = cluster_addr(full, 0);
+    int ia = 0;
+    int ib = 0;
+    bool stop = false;
+    for (int pt = pair; pt < pair_tiles && !stop && !*abort_flag; pt += pairs) {
+      int w0, h0, d0, b;
+      decode(min(2 * pt + static_cast<int>(rank), g.total_tiles - 1), w0, h0, d0, b);
+      for (int gi = 0; gi < groups_per_tile && !stop; ++gi) {
+        const int kd = gi / g.kblocks;
+        const int c = (gi - kd * g.kblocks) * kPairKC;
+        const int sa = ia % SA;
+        if (ia >= SA &&
+            !mbar_wait_bounded(&a_empty[sa], static_cast<uint32_t>(ia / SA - 1) & 1u, kErrWaitEmpty)) {
+          stop = true;
+          break;
+        }
+        if (rank == 0) mbar_arrive_expect_tx(&a_full[sa], 2u * kPairABytes);
+        tma_load_5d_pair(smem + static_cast<size_t>(sa) * kPairABytes, &maps.a[0], a_full0 + 8u * sa, c, h0 - 1,
+                         w0 - 1, d0 + kd - 1, b);
+        ++ia;
+        for (int kw = 0; kw < 3; ++kw) {
+          const int s = ib % S;
+          if (ib >= S && !mbar_wait_bounded(&empty[s], static_cast<uint32_t>(ib / S - 1) & 1u, kErrWaitEmpty)) {
+            stop = true;
+            break;
+          }
+          if (rank == 0) mbar_arrive_expect_tx(&full[s], 2u * kPairBBytes);
+          // Weights (c, o, kw, kh, kd): this CTA's 32 output channels, three kh taps.
+          tma_load_5d_pair(b_ring + static_cast<size_t>(s) * kPairBBytes, &maps.b, full0 + 8u * s, c,
+                           static_cast<int>(rank) * (kPairBN / 2), kw, 0, kd);
+          ++ib;
+        }
+      }
+    }
+    if (stop) *abort_flag = 1;
+    // The first CTA's barriers count both CTAs' bytes: every copy in flight lands before the
+    // closing cluster barrier lets either CTA exit.
+    if (rank == 0) {
+      for (int k = max(0, ia - SA); k < ia; ++k) {
+        if (!mbar_wait_bounded(&a_full[k % SA], static_cast<uint32_t>(k / SA) & 1u, kErrWaitDrain)) break;
+      }
+      for (int k = max(0, ib - S); k < ib; ++k) {
+        if (!mbar_wait_bounded(&full[k % S], static_cast<uint32_t>(k / S) & 1u, kErrWaitDrain)) break;
+      }
+    }
+  } else if (warp == 1 && lane == 0 && rank == 0) {
+    // ------------------------------------------------------------ MMA issuer (first CTA)
+    const uint32_t idesc = idesc_f16(g.operand_bf16 != 0, 256, kPairN);
+    int ia = 0;
+    int ib = 0;
+    int lt = 0;
+    bool stop = false;
+    for (int pt = pair; pt < pair_tiles && !stop && !*abort_flag; pt += pairs, ++lt) {
+      for (int gi = 0; gi < groups_per_tile && !stop; ++gi) {
+        const int sa = ia % SA;
+        if (!mbar_wait_bounded(&a_full[sa], static_cast<uint32_t>(ia / SA) & 1u, kErrWaitFull)) {
+          stop = true;
+          break;
+        }
+        ++ia;
+        const uint64_t a_desc0 = smem_desc_kmajor(smem_u32(smem + static_cast<size_t>(sa) * kPairABytes), kRowBytes);
+        for (int kw = 0; kw < 3 && !stop; ++kw) {
+          const int s = ib % S;
+          if (!mbar_wait_bounded(&full[s], static_cast<uint32_t>(ib / S) & 1u, kErrWaitFull)) {
+            stop = true;
+            break;
+          }
+          ++ib;
+          tc_fence_after();
+          const uint64_t b_desc = smem_desc_kmajor(smem_u32(b_ring + static_cast<size_t>(s) * kPairBBytes), kRowBytes);
+          const bool first = gi == 0 && kw == 0;
+#pragma unroll
+          for (int m = 0; m < kPairMT; ++m) {
+            // Depth m's columns must have been read out of both CTAs' TMEM (previous pair tile).
+            if (first && lt >= 1) {
+              if (!mbar_wait_bounded(&tmem_empty[m], static_cast<uint32_t>(lt - 1) & 1u, kErrWaitAcc)) {
+                stop = true;
+                break;
+              }
+              tc_fence_after();
+            }
+            const uint64_t a_desc =
+                desc_advance(a_desc0, static_cast<uint32_t>(m) * kPairAmBytes + static_cast<uint32_t>(kw) * kPairKwBytes);
+            const uint32_t d_acc = tmem + static_cast<uint32_t>(m) * kPairN;
+#pragma unroll
+            for (int k = 0; k < kSteps; ++k)
+              umma_f16_pair(d_acc, a_desc + 2u * k, b_desc + 2u * k, idesc, (first && k == 0) ? 0u : 1u);
+          }
+          umma_commit_pair(&empty[s]);
+        }
+        umma_commit_pair(&a_empty[sa]);
+      }
+      if (stop) break;
+      umma_commit_pair(&tmem_full[0]);
+    }
+    if (stop) *abort_flag = 1;
+  } else if (warp >= 2) {
+    // ------------------------------------------------------------ epilogue (both CTAs)
+    const int ew = warp - 2;
+    const int quarter = warp & 3;  // TMEM lanes a warp may read: 32 x (warp id mod 4)
+    const int half = ew >> 2;      // output channels 32 half .. 32 half + 31
+    const uint32_t lane_addr = tmem + (static_cast<uint32_t>(quarter * 32) << 16);
+    const uint32_t release0 = cluster_addr(tmem_empty, 0);
+    const int gi = lane & 7, gbase = lane & ~7;
+    const int n = 32 * half + 4 * gi;  // the four channels this lane stores after the transpose
+    int lt = 0;
+    for (int pt = pair; pt < pair_tiles; pt += pairs, ++lt) {
+      const int t = 2 * pt + static_cast<int>(rank);
+      const bool tile_ok = t < g.total_tiles;
+      int w0, h0, d0, b;
+      decode(min(t, g.total_tiles - 1), w0, h0, d0, b);
+      const bool ok = mbar_wait_bounded(&tmem_full[0], static_cast<uint32_t>(lt) & 1u, kErrWaitAcc);
+      if (!barrier_all(3, 256, ok && !*abort_flag)) {
+        *abort_flag = 1;
+        break;
+      }
+      tc_fence_after();
+      float out[kPairMT][2][16];
+#pragma unroll
+      for (int m = 0; m < kPairMT; ++m) {
+#pragma unroll
+        for (int jj = 0; jj < 2; ++jj) {
+          const uint32_t col = static_cast<uint32_t>(m) * kPairN + static_cast<uint32_t>(96 * half + 16 * jj);
+          uint32_t r0[16], r1[16], r2[16];
+          tmem_ld16_issue(lane_addr + col, r0);
+          tmem_ld16_issue(lane_addr + col + 32u, r1);
+          tmem_ld16_issue(lane_addr + col + 64u, r2);
+          tmem_wait_ld();
+          reg_fence16(r0);
+          reg_fence16(r1);
+          reg_fence16(r2);
+#pragma unroll
+          for (int i = 0; i < 16; ++i) {
+            const float p0 = __shfl_up_sync(0xffffffffu, __uint_as_float(r0[i]), 1, 16);
+            const float p2 = __shfl_down_sync(0xffffffffu, __uint_as_float(r2[i]), 1, 16);
+            out[m][jj][i] = (p0 + __uint_as_float(r1[i])) + p2;
+          }
+        }
+        // Depth m of this CTA's accumulator is in registers: one arrival per warp on the first
+        // CTA's barrier, after every lane's TMEM loads.
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive_cluster(release0 + 8u * static_cast<uint32_t>(m));
+      }
+
+      const float* bias_b = g.bias != nullptr ? g.bias + static_cast<long long>(b) * g.bias_bstride : nullptr;
+      float4 bq = make_float4(0.f, 0.f, 0.f, 0.f);
+      if (bias_b != nullptr) {
+        if (n + 4 <= g.cout && (reinterpret_cast<uintptr_t>(bias_b + n) & 15) == 0) {
+          bq = __ldg(reinterpret_cast<const float4*>(bias_b + n));
+        } else {
+          float t4[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+          for (int e = 0; e < 4; ++e)
+            if (n + e < g.cout) t4[e] = __ldg(bias_b + n + e);
+          bq = make_float4(t4[0], t4[1], t4[2], t4[3]);
+        }
+      }
+#pragma unroll
+      for (int m = 0; m < kPairMT; ++m) {
+        float4 q[8];
+#pragma unroll
+        for (int k = 0; k < 8; ++k) {
+          const float* s4 = &out[m][k >> 2][4 * (k & 3)];
+          q[k] = make_float4(s4[0], s4[1], s4[2], s4[3]);
+        }
+        transpose_f4<8>(q, gi);
+        const int od = d0 + m;
+        if (!tile_ok || od >= g.out_d) continue;
+        long long vox[8];
+        bool okk[8];
+#pragma unroll
+        for (int k = 0; k < 8; ++k) {
+          const int src = gbase + k;
+          const int sh = src & 15;
+          const int oh = h0 + sh - 1, ow = w0 + 2 * quarter + (src >> 4);
+          okk[k] = sh >= 1 && sh <= kKhRows && oh < g.out_h && ow < g.out_w;
+          vox[k] = ((static_cast<long long>(b) * g.out_d + od) * g.out_h + oh) * g.out_w + ow;
+          q[k].x += bq.x;
+          q[k].y += bq.y;
+          q[k].z += bq.z;
+          q[k].w += bq.w;
+        }
+        if (g.res != nullptr) {
+          float4 rv[8];
+#pragma unroll
+          for (int k = 0; k < 8; ++k) {
+            rv[k] = make_float4(0.f, 0.f, 0.f, 0.f);
+            if (okk[k]) {
+              const int src = gbase + k;
+              const int oh = h0 + (src & 15) - 1, ow = w0 + 2 * quarter + (src >> 4);
+              const int qd = g.res_up ? od >> 1 : od, qh = g.res_up ? oh >> 1 : oh, qw = g.res_up ? ow >> 1 : ow;
+              const long long ro =
+                  (((static_cast<long long>(b) * g.res_d + qd) * g.res_h + qh) * g.res_w + qw) * g.res_cstride + n;
+              rv[k] = kh_load4(g, ro, n);
+            }
+          }
+#pragma unroll
+          for (int k = 0; k < 8; ++k) {
+            q[k].x += rv[k].x;
+            q[k].y += rv[k].y;
+            q[k].z += rv[k].z;
+            q[k].w += rv[k].w;
+          }
+        }
+#pragma unroll
+        for (int k = 0; k < 8; ++k)
+          if (okk[k]) kh_store4(g, q[k], n, vox[k] * g.out_cstride + g.out_coff + n);
+      }
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  cluster_sync();  // neither CTA exits while the other's products, copies or arrivals may reach it
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc_pair(tmem, 512);
+  }
+}
+
 template <int KC, int MT>
 cudaError_t launch_khcat_typed(const ConvMaps& maps, const ConvGeom& g, int grid, size_t smem, cudaStream_t stream) {
   auto kern = g.operand_tf32 ? conv3d_khcat_kernel<KC, MT, true> : conv3d_khcat_kernel<KC, MT, false>;
@@ -551,6 +871,55 @@ int conv_khcat_stage_plan(int kc, int bn, int mt, size_t* smem_bytes) {
 }
 
 int conv_khcat_rows() { return kKhRows; }
+
+int conv_khcat_pair_stage_plan(size_t* smem_bytes) {
+  const size_t fixed = 1024 + 512 + static_cast<size_t>(kPairASlots) * kPairABytes;
+  int stages = static_cast<int>((227 * 1024 - fixed) / kPairBBytes);
+  if (stages > kKhMaxBSlots) stages = kKhMaxBSlots;
+  if (stages < 2) return 0;
+  *smem_bytes = fixed + static_cast<size_t>(stages) * kPairBBytes;
+  return stages;
+}
+
+// One cluster of two CTAs per SM pair, as many pairs as can be resident at once (queried once
+// per device) or as there are pair tiles. cudaErrorNotSupported: no pair fits, use the one-SM kernel.
+cudaError_t launch_conv3d_khcat_pair(const ConvMaps& maps, const ConvGeom& g, size_t smem, cudaStream_t stream) {
+  if (g.total_tiles <= 0 || g.bn != kPairBN || g.kblocks < 1 || g.tmem_cols != 512 || g.operand_tf32)
+    return cudaErrorInvalidValue;
+  auto kern = conv3d_khcat_pair_kernel;
+  cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
+  if (e != cudaSuccess) return e;
+  cudaLaunchConfig_t cfg = {};
+  cfg.blockDim = dim3(kKhThreads);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[2];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = 2;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[1].val.programmaticStreamSerializationAllowed = pdl_enabled() ? 1 : 0;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  static std::atomic<int> cached[64];
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) dev = 0;
+  int clusters = dev >= 0 && dev < 64 ? cached[dev].load(std::memory_order_relaxed) : 0;
+  if (clusters == 0) {
+    cfg.gridDim = dim3(2 * (device_sm_count() / 2));
+    if (cudaOccupancyMaxActiveClusters(&clusters, kern, &cfg) != cudaSuccess || clusters < 1) {
+      (void)cudaGetLastError();
+      clusters = -1;
+    }
+    if (dev >= 0 && dev < 64) cached[dev].store(clusters, std::memory_order_relaxed);
+  }
+  if (clusters < 1) return cudaErrorNotSupported;
+  const int pair_tiles = (g.total_tiles + 1) / 2;
+  cfg.gridDim = dim3(2 * (pair_tiles < clusters ? pair_tiles : clusters));
+  cfg.numAttrs = 2;
+  return cudaLaunchKernelEx(&cfg, kern, maps, g);
+}
 
 cudaError_t launch_conv3d_khcat(const ConvMaps& maps, const ConvGeom& g, int kc, int mt, int sms, size_t smem,
                                 cudaStream_t stream) {

@@ -255,6 +255,67 @@ def test_kh_concatenated_kernel(cuda, shape, out_channels, precision, depths, mo
     assert not wide[:, :16].any() and not wide[:, 16 + out_channels:].any()
 
 
+KHCAT_PAIR_SHAPES = [
+    (2, 64, 3, 30, 20),    # 36 tiles: partial h, w and depth-pair tiles
+    (1, 64, 2, 14, 24),    # 3 tiles: the last pair's second CTA repeats a tile and stores nothing
+    (2, 192, 2, 14, 24),   # three channel blocks
+    (1, 128, 6, 44, 40),   # 60 tiles, two channel blocks
+    (1, 64, 8, 128, 64),   # 320 tiles: each CTA pair walks several pair tiles
+]
+
+
+def _kernel_names(fn) -> list[str]:
+    """Names of the CUDA kernels `fn` launches (torch's profiler, CUDA activity)."""
+    from torch.profiler import ProfilerActivity, profile
+
+    with profile(activities=[ProfilerActivity.CUDA]) as prof:
+        fn()
+        torch.cuda.synchronize()
+    return [e.name for e in prof.events() if e.device_type == torch.autograd.DeviceType.CUDA]
+
+
+@pytest.mark.parametrize("precision", ["fp16", "bf16"])
+@pytest.mark.parametrize("shape", KHCAT_PAIR_SHAPES)
+def test_kh_concatenated_pair_kernel(cuda, shape, precision, monkeypatch):
+    """With CTMR_KHCAT_PAIR=1, 64 -> 64 convs in 64-channel blocks run the CTA-pair kernel
+    (tcgen05.mma.cta_group::2, M = 256: two tiles per product, each SM holding half of every weight
+    box): it is the kernel launched, it meets the float64 oracle at the 16-bit bar, and it agrees with
+    the one-SM kernel (the default) on the same rounded operands, with a bias, a residual and a bf16
+    output into a channel slice."""
+    from ctmr_b200 import ops
+
+    rng = np.random.default_rng(64)
+    b, c = shape[:2]
+    x = torch.from_numpy(rng.standard_normal(shape).astype(np.float32))
+    w = torch.from_numpy((rng.standard_normal((64, c, 3, 3, 3)) / np.sqrt(27 * c)).astype(np.float32))
+    bias = torch.from_numpy(rng.standard_normal(64).astype(np.float32))
+    res = torch.from_numpy(rng.standard_normal((b, 64, *shape[2:])).astype(np.float32))
+    xc, bc, rc = ops.to_ndhwc(x.to(cuda)), bias.to(cuda), ops.to_ndhwc(res.to(cuda))
+    packed = ops.pack_weight(w.to(cuda), precision)
+    monkeypatch.delenv("CTMR_DISABLE_KHCAT", raising=False)
+    monkeypatch.delenv("CTMR_KHCAT_MT", raising=False)
+    monkeypatch.setenv("CTMR_KHCAT_PAIR", "1")
+    out = {}
+    names = _kernel_names(lambda: out.setdefault("y", ops.conv3d(xc, packed, bc, residual=rc)))
+    assert any("khcat_pair" in n for n in names), names
+    y = out["y"]
+    wide = ops.empty_ndhwc(b, 96, *shape[2:], torch.bfloat16, xc.device).zero_()
+    ops.conv3d(xc, packed, bc, out=wide[:, 16:80])
+    monkeypatch.delenv("CTMR_KHCAT_PAIR")
+    names_one = _kernel_names(lambda: out.setdefault("y_one", ops.conv3d(xc, packed, bc, residual=rc)))
+    assert not any("khcat_pair" in n for n in names_one) and any("khcat_kernel" in n for n in names_one), names_one
+    y_one = out["y_one"]
+    plain_one = ops.conv3d(xc, packed, bc)
+    torch.cuda.synchronize()
+    expected = ops_ref.conv3d_ref(x.double(), w.double(), bias.double()) + res.double()
+    err = ops_ref.rel_l2(y.cpu(), expected)
+    assert err <= (FP16_CONV_REL_L2 if precision == "fp16" else BF16_CONV_REL_L2), f"{precision} rel-L2 {err:.3e}"
+    diff = ops_ref.rel_l2(y.cpu(), y_one.cpu().double())
+    assert diff <= 1e-6, f"pair vs one-SM kernel rel-L2 {diff:.3e}"
+    torch.testing.assert_close(wide[:, 16:80].float(), plain_one.to(torch.bfloat16).float(), rtol=8e-3, atol=1e-3)
+    assert not wide[:, :16].any() and not wide[:, 80:].any()
+
+
 @pytest.mark.parametrize("out_channels", [64, 48])
 def test_kh_concatenated_residual_forms(cuda, out_channels, monkeypatch):
     """The kh-concatenated kernel's two store paths (64 outputs: 8-lane transposed; fewer: per
