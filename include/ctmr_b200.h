@@ -230,10 +230,17 @@ CTMR_API int ctmr_group_norm_affine_from_moments(const float* moments, int parts
  * no reference counterpart), or 0 for an invalid descriptor. */
 CTMR_API int ctmr_conv3d_launch_count(const ctmr_conv3d_desc* desc);
 
-/* Statistics slots a convolution writes when desc->stats is set (its persistent
- * kernel's CTA count bound), or 0 when this convolution does not produce them (it
- * does not run the persistent kernel, has fewer than 128 output channels, or
- * batch x out_channels > 512). Has no
+/* Kernel launches one ctmr_group_norm_affine call over `voxels` voxels per batch item and
+ * `channels` channels in `groups` groups issues for dense, 16-byte aligned fp32 sources: 1 for
+ * small groups (one block per group and batch item computes the affine directly), 2 otherwise
+ * (partials, then the merge); 0 for invalid extents. Instrumentation; no reference counterpart. */
+CTMR_API int ctmr_group_norm_launch_count(long long voxels, int channels, int groups);
+
+/* Statistics slots a convolution writes when desc->stats is set, or 0 when this
+ * convolution does not produce them. The kh-concatenated persistent kernel (16-bit
+ * operands, stride-1 3x3x3, 64 padded output channels) writes four per SM, one per
+ * epilogue lane quarter of each CTA; the atom-shifted persistent kernel (at least 128
+ * output channels, batch x out_channels <= 512) one per SM; other routes none. Has no
  * reference counterpart: the reference recomputes the statistics from the tensor. */
 CTMR_API int ctmr_conv3d_stats_slots(const ctmr_conv3d_desc* desc);
 

@@ -396,9 +396,10 @@ struct KhPlan {
 };
 
 // The kh-concatenated kernel: 16-bit stride-1 3x3x3 convolutions with at most 64
-// output channels (three taps side by side fill an N = 3 x C_out MMA).
-bool plan_khcat(const ConvPlan& p, const ctmr_conv3d_desc* d, KhPlan* k) {
-  if (p.exact || p.mode != ctmr::kModeConv3 || p.opad > 64 || d->stats != nullptr ||
+// output channels (three taps side by side fill an N = 3 x C_out MMA). With output
+// statistics (four slots per CTA): 64 output columns and 16-bit operands only.
+bool plan_khcat(const ConvPlan& p, const ctmr_conv3d_desc* d, bool with_stats, KhPlan* k) {
+  if (p.exact || p.mode != ctmr::kModeConv3 || p.opad > 64 || (with_stats && (p.opad != 64 || p.tf32)) ||
       p.row_w < 8 || p.row_h < 8 || getenv("CTMR_DISABLE_KHCAT") != nullptr)
     return false;
   // Two depth tiles share each weight box (measured faster than one depth with two accumulator
@@ -720,10 +721,12 @@ int ctmr_conv3d_stages(const ctmr_conv3d_desc* d, void* workspace, size_t worksp
   // 2a. The persistent atom-shifted kernel for 16-bit stride-1 3x3x3, nearest-2x and 1x1x1 convolutions.
   const bool with_stats = d->stats != nullptr;
   V2Plan v2{};
-  if (with_stats && (d->stats_slots < sm_count() || !plan_v2(p, d, true, &v2)))
-    return fail(CTMR_ERR_UNSUPPORTED, "output statistics need the persistent kernel (ctmr_conv3d_stats_slots)");
   KhPlan kh{};
-  if (plan_khcat(p, d, &kh)) {
+  const bool kh_ok = plan_khcat(p, d, with_stats, &kh);
+  if (with_stats && !(kh_ok ? d->stats_slots >= 4 * sm_count()
+                            : d->stats_slots >= sm_count() && plan_v2(p, d, true, &v2)))
+    return fail(CTMR_ERR_UNSUPPORTED, "output statistics need the persistent kernel (ctmr_conv3d_stats_slots)");
+  if (kh_ok) {
     const int rows = ctmr::conv_khcat_rows(), md = kh.mt;
     ctmr::ConvGeom g{};
     g.batch = d->batch;
@@ -744,6 +747,8 @@ int ctmr_conv3d_stages(const ctmr_conv3d_desc* d, void* workspace, size_t worksp
     g.operand_tf32 = p.tf32 ? 1 : 0;
     g.ksplit = 1;
     g.n_tiles = 1;
+    g.stats = d->stats;
+    g.stats_slots = d->stats_slots;
     const long long total = static_cast<long long>(g.tiles_w) * g.tiles_h * g.tiles_d * d->batch;
     if (total > 0 && total < (1LL << 31)) {
       g.total_tiles = static_cast<int>(total);
@@ -776,8 +781,8 @@ int ctmr_conv3d_stages(const ctmr_conv3d_desc* d, void* workspace, size_t worksp
         // slower than the one-SM kernel (0.821 vs 0.763 ms on 1 x 64 x 96 x 256 x 128 -> 64).
         size_t smem_pair = 0;
         const char* pair_env = getenv("CTMR_KHCAT_PAIR");
-        if (kh.kc == 64 && kh.mt == 2 && p.opad == 64 && !p.tf32 && g.total_tiles >= 2 && pair_env != nullptr &&
-            pair_env[0] == '1') {
+        if (kh.kc == 64 && kh.mt == 2 && p.opad == 64 && !p.tf32 && !with_stats && g.total_tiles >= 2 &&
+            pair_env != nullptr && pair_env[0] == '1') {
           const int st = ctmr::conv_khcat_pair_stage_plan(&smem_pair);
           ctmr::ConvMaps maps_pair = maps;
           if (st >= 2 && encode_weight_kh(&maps_pair.b, w_hi, p.bf16, p.cpad, p.opad, kh.kc, p.opad / 2) == CTMR_OK) {
@@ -794,7 +799,10 @@ int ctmr_conv3d_stages(const ctmr_conv3d_desc* d, void* workspace, size_t worksp
         }
       }
       // A refused tensor map depends on this call's pointers and strides only: this call falls
-      // through to the other kernels, later calls try again.
+      // through to the other kernels (none of which then keeps statistics for fewer than 128
+      // output channels), later calls try again.
+      if (with_stats && !plan_v2(p, d, true, &v2))
+        return fail(CTMR_ERR_UNSUPPORTED, "output statistics: the kh-concatenated kernel's tensor maps were refused");
     }
   }
   if (plan_v2(p, d, with_stats, &v2)) {
@@ -1028,21 +1036,30 @@ int ctmr_group_norm_affine_from_moments(const float* moments, int parts, int bat
 int ctmr_conv3d_stats_slots(const ctmr_conv3d_desc* d) {
   ConvPlan p{};
   if (d == nullptr || plan_conv(d, &p) != CTMR_OK) return 0;
+  if (p.narrow || p.tiny) return 0;
+  KhPlan kh{};
+  if (plan_khcat(p, d, true, &kh)) return 4 * sm_count();  // one slot per epilogue lane quarter
   V2Plan v2{};
-  if (p.narrow || p.tiny || !plan_v2(p, d, true, &v2)) return 0;
+  if (!plan_v2(p, d, true, &v2)) return 0;
   return sm_count();
 }
 
 int ctmr_conv3d_launch_count(const ctmr_conv3d_desc* d) {
   ConvPlan p{};
   if (d == nullptr || plan_conv(d, &p) != CTMR_OK) return 0;
-  int n = (p.gn_in && !p.gn_small) ? 2 : 0;
+  const long long voxels = static_cast<long long>(d->depth) * d->height * d->width;
+  int n = (p.gn_in && !p.gn_small) ? (ctmr::gn_direct_fits(voxels, p.cin, d->gn_groups) ? 1 : 2) : 0;
   if (p.narrow || p.tiny) return n + 1;
   if (p.prepare) n += p.im2col ? 2 : 1;
   V2Plan v2{};
   KhPlan kh{};
-  if (plan_khcat(p, d, &kh) || plan_v2(p, d, d->stats != nullptr, &v2)) return n + 1;
+  if (plan_khcat(p, d, d->stats != nullptr, &kh) || plan_v2(p, d, d->stats != nullptr, &v2)) return n + 1;
   return n + 1 + (p.ksplit > 1 ? 1 : 0);
+}
+
+int ctmr_group_norm_launch_count(long long voxels, int channels, int groups) {
+  if (voxels < 0 || channels <= 0 || groups <= 0 || channels % groups != 0) return 0;
+  return ctmr::gn_direct_fits(voxels, channels, groups) ? 1 : 2;
 }
 
 int ctmr_group_norm_affine_from_stats(const float* stats_a, int channels_a, const float* stats_b, int channels_b,

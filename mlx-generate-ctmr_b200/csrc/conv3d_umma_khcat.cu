@@ -180,7 +180,7 @@ __device__ __forceinline__ void kh_store4(const ConvGeom& g, float4 v, int n, lo
 // tile i + 1) when 2 x MT x 3 x C_out columns fit, else one, released depth by depth.
 __host__ __device__ constexpr int kh_buffers(int mt, int bn) { return 2 * mt * 3 * bn <= 512 ? 2 : 1; }
 
-template <int KC, int MT, bool TF32>
+template <int KC, int MT, bool TF32, bool STATS>
 __global__ void __launch_bounds__(kKhThreads, 1)
     conv3d_khcat_kernel(const __grid_constant__ ConvMaps maps, const __grid_constant__ ConvGeom g) {
   constexpr uint32_t kRowBytes = KC * 2;
@@ -362,11 +362,67 @@ __global__ void __launch_bounds__(kKhThreads, 1)
     // 64 output channels: half h reads chunks 2h, 2h + 1 (32 contiguous channels per lane), stored
     // through an 8-lane transpose. Fewer: chunks h, h + 2 (both halves busy), stored per voxel.
     const bool wide = nchunks == 4;
+    // STATS (64 output columns only): each lane keeps the (count, mean, M2) moments of its four
+    // output channels over the voxels it stores, for one batch item at a time (tiles come in
+    // batch order); at a batch change and at the end the warp merges its four 8-lane groups and
+    // lanes 0..7 write the warp's slot 4 x CTA + quarter. Batch items a warp never saw get zeros.
+    float st[4][3];
+    int st_b = -1, st_next = 0;
+    auto stats_reset = [&]() {
+#pragma unroll
+      for (int e = 0; e < 4; ++e) st[e][0] = st[e][1] = st[e][2] = 0.f;
+    };
+    auto stats_zero = [&](int bb) {  // this warp's slot for batch item bb holds nothing
+      if (lane < 8) {
+        const int nc = 32 * half + 4 * lane;
+        float* dst = g.stats + ((static_cast<size_t>(bb) * g.stats_slots + 4 * blockIdx.x + quarter) * g.cout) * 3;
+#pragma unroll
+        for (int e = 0; e < 4; ++e)
+          if (nc + e < g.cout) dst[(nc + e) * 3] = dst[(nc + e) * 3 + 1] = dst[(nc + e) * 3 + 2] = 0.f;
+      }
+    };
+    auto stats_flush = [&]() {  // warp-collective: merge the 8-lane groups, write slot of st_b
+#pragma unroll
+      for (int off = 8; off < 32; off <<= 1) {
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          const float on = __shfl_xor_sync(0xffffffffu, st[e][0], off);
+          const float om = __shfl_xor_sync(0xffffffffu, st[e][1], off);
+          const float o2 = __shfl_xor_sync(0xffffffffu, st[e][2], off);
+          if (lane & off) {  // both partners merge (lower group, upper group): the same result
+            float m[3] = {on, om, o2};
+            chan_merge(m, st[e][0], st[e][1], st[e][2]);
+            st[e][0] = m[0], st[e][1] = m[1], st[e][2] = m[2];
+          } else {
+            chan_merge(st[e], on, om, o2);
+          }
+        }
+      }
+      if (lane < 8) {
+        const int nc = 32 * half + 4 * lane;
+        float* dst = g.stats + ((static_cast<size_t>(st_b) * g.stats_slots + 4 * blockIdx.x + quarter) * g.cout) * 3;
+#pragma unroll
+        for (int e = 0; e < 4; ++e)
+          if (nc + e < g.cout) {
+            dst[(nc + e) * 3] = st[e][0];
+            dst[(nc + e) * 3 + 1] = st[e][1];
+            dst[(nc + e) * 3 + 2] = st[e][2];
+          }
+      }
+    };
+    if (STATS) stats_reset();
     int lt = 0;
     // The eight epilogue warps take every decision together (the wait outcome is voted on).
     for (int t = blockIdx.x; t < g.total_tiles; t += gridDim.x, ++lt) {
       int w0, h0, d0, b;
       decode(t, w0, h0, d0, b);
+      if (STATS && b != st_b) {
+        if (st_b >= 0) stats_flush();
+        for (; st_next < b; ++st_next) stats_zero(st_next);
+        st_b = b;
+        st_next = b + 1;
+        stats_reset();
+      }
       const int buf = nbuf == 2 ? (lt & 1) : 0;
       const bool ok = mbar_wait_bounded(&tmem_full[buf], static_cast<uint32_t>(nbuf == 2 ? lt >> 1 : lt) & 1u,
                                         kErrWaitAcc);
@@ -482,6 +538,28 @@ __global__ void __launch_bounds__(kKhThreads, 1)
               q[k].w += rv[k].w;
             }
           }
+          if (STATS) {  // moments of this depth's (up to) eight voxels, merged into the lane's
+#pragma unroll
+            for (int e = 0; e < 4; ++e) {
+              float cnt = 0.f, sum = 0.f;
+#pragma unroll
+              for (int k = 0; k < 8; ++k) {
+                const float x = e == 0 ? q[k].x : e == 1 ? q[k].y : e == 2 ? q[k].z : q[k].w;
+                if (ok[k]) cnt += 1.f, sum += x;
+              }
+              if (cnt > 0.f && n + e < g.cout) {
+                const float mean = sum / cnt;
+                float m2 = 0.f;
+#pragma unroll
+                for (int k = 0; k < 8; ++k) {
+                  const float x = e == 0 ? q[k].x : e == 1 ? q[k].y : e == 2 ? q[k].z : q[k].w;
+                  const float dv = x - mean;
+                  if (ok[k]) m2 = fmaf(dv, dv, m2);
+                }
+                chan_merge(st[e], cnt, mean, m2);
+              }
+            }
+          }
 #pragma unroll
           for (int k = 0; k < 8; ++k)
             if (ok[k]) kh_store4(g, q[k], n, vox[k] * g.out_cstride + g.out_coff + n);
@@ -517,6 +595,18 @@ __global__ void __launch_bounds__(kKhThreads, 1)
             }
             store_row16(g, v, n, out_base + n, res_base + n);
           }
+        }
+      }
+    }
+    if (STATS) {
+      if (st_b >= 0) stats_flush();
+      for (; st_next < g.batch; ++st_next) stats_zero(st_next);
+      if (blockIdx.x == 0) {  // the slots of CTAs past the grid hold nothing
+        const int first = 4 * static_cast<int>(gridDim.x), extra = g.stats_slots - first;
+        for (int e = static_cast<int>(threadIdx.x) - 64; e < g.batch * extra * g.cout; e += 256) {
+          const int bb = e / (extra * g.cout), r = e - bb * extra * g.cout;
+          float* dst = g.stats + (static_cast<size_t>(bb) * g.stats_slots * g.cout + static_cast<size_t>(first) * g.cout + r) * 3;
+          dst[0] = dst[1] = dst[2] = 0.f;
         }
       }
     }
@@ -850,7 +940,10 @@ __global__ void __launch_bounds__(kKhThreads, 1)
 
 template <int KC, int MT>
 cudaError_t launch_khcat_typed(const ConvMaps& maps, const ConvGeom& g, int grid, size_t smem, cudaStream_t stream) {
-  auto kern = g.operand_tf32 ? conv3d_khcat_kernel<KC, MT, true> : conv3d_khcat_kernel<KC, MT, false>;
+  // Epilogue statistics: 16-bit operands and 64 output columns only (the planner's condition).
+  auto kern = g.stats != nullptr ? conv3d_khcat_kernel<KC, MT, false, true>
+              : g.operand_tf32  ? conv3d_khcat_kernel<KC, MT, true, false>
+                                : conv3d_khcat_kernel<KC, MT, false, false>;
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
   if (e != cudaSuccess) return e;
   return launch_kernel(kern, grid, kKhThreads, smem, stream, maps, g);
@@ -925,6 +1018,7 @@ cudaError_t launch_conv3d_khcat(const ConvMaps& maps, const ConvGeom& g, int kc,
                                 cudaStream_t stream) {
   if (g.total_tiles <= 0 || g.bn > 64 || g.bn % 16 != 0 || g.tmem_cols != 512) return cudaErrorInvalidValue;
   const int grid = g.total_tiles < sms ? g.total_tiles : sms;
+  if (g.stats != nullptr && (g.bn != 64 || g.operand_tf32 || g.stats_slots < 4 * grid)) return cudaErrorInvalidValue;
 #define CTMR_KH(KC_, MT_) \
   if (kc == KC_ && mt == MT_) return launch_khcat_typed<KC_, MT_>(maps, g, grid, smem, stream);
   CTMR_KH(64, 2) CTMR_KH(32, 2) CTMR_KH(16, 2) CTMR_KH(64, 1) CTMR_KH(32, 1) CTMR_KH(16, 1)

@@ -48,5 +48,7 @@ cudaError_t launch_group_norm_from_moments(const GnMomentsParams& p, cudaStream_
 cudaError_t launch_group_norm_from_stats(const GnStatsParams& p, cudaStream_t stream);
 int gn_chunks_for(int batch, long long voxels, int channels);
 cudaError_t launch_group_norm_affine(const GnParams& p, cudaStream_t stream);
+// launch_group_norm_affine makes one launch (the small-tensor kernel) instead of two.
+bool gn_direct_fits(long long voxels, int channels, int groups);
 
 }  // namespace ctmr

@@ -47,6 +47,7 @@ EXPORTED_SYMBOLS = (
     "ctmr_group_norm_affine",
     "ctmr_conv3d_stats_slots",
     "ctmr_conv3d_launch_count",
+    "ctmr_group_norm_launch_count",
     "ctmr_group_norm_affine_from_stats",
     "ctmr_group_norm_moments",
     "ctmr_group_norm_affine_from_moments",
@@ -154,6 +155,7 @@ def _load() -> ctypes.CDLL:
         "ctmr_group_norm_affine": (i, [Tensor, Tensor, i, ll, vp, vp, i, f, vp, vp, sz, vp]),
         "ctmr_conv3d_stats_slots": (i, [ctypes.POINTER(Conv3dDesc)]),
         "ctmr_conv3d_launch_count": (i, [ctypes.POINTER(Conv3dDesc)]),
+        "ctmr_group_norm_launch_count": (i, [ll, i, i]),
         "ctmr_group_norm_affine_from_stats": (i, [vp, i, vp, i, i, i, vp, vp, i, f, vp, vp]),
         "ctmr_group_norm_moments": (i, [Tensor, Tensor, i, ll, i, vp, vp, sz, vp]),
         "ctmr_group_norm_affine_from_moments": (i, [vp, i, i, i, vp, vp, i, f, vp, vp]),

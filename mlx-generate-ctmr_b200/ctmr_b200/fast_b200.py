@@ -146,11 +146,22 @@ def _dense_weight(weight: torch.Tensor, dtype: torch.dtype) -> torch.Tensor:
     return cast
 
 
-# Whether GroupNorm-feeding convolutions reduce their output statistics in the
-# epilogue (ops.conv3d(stats=True)) instead of the GroupNorm pass reading the
-# tensor. Off by default: measured on the MAISI networks, the epilogue reduction
-# costs the 64- to 128-channel convolutions more than the pass it saves.
-OUTPUT_STATS = os.environ.get("CTMR_OUTPUT_STATS", "0") == "1"
+# Whether a GroupNorm-feeding convolution reduces its output statistics in the epilogue
+# (ops.conv3d(stats=True)) instead of the GroupNorm pass re-reading the tensor. By default
+# only for outputs larger than L2 (the VAE decoder's full- and mid-resolution tensors), where
+# that pass reads HBM; an L2-resident tensor (the UNet's) is read back cheaper than the
+# epilogue reduction costs. CTMR_OUTPUT_STATS=1: every such convolution; 0: none.
+OUTPUT_STATS = os.environ.get("CTMR_OUTPUT_STATS", "auto")
+STATS_MIN_BYTES = 128 << 20
+
+
+def _want_stats(x: torch.Tensor, out_channels: int, scale: float = 1.0) -> bool:
+    """Epilogue statistics for a conv of ``x`` into ``out_channels`` on ``scale`` x its voxel count."""
+    if OUTPUT_STATS in ("0", "1"):
+        return OUTPUT_STATS == "1"
+    b, _, d, h, w = (int(n) for n in x.shape)
+    itemsize = torch.empty((), dtype=activation_dtype()).element_size()
+    return b * d * h * w * scale * out_channels * itemsize > STATS_MIN_BYTES
 
 _stacked: dict[tuple, tuple] = {}
 
@@ -293,7 +304,8 @@ def conv3d_ncdhw(array, weight: torch.Tensor, bias: torch.Tensor | None, *, padd
     if k != 3 or padding != 1 or stride not in (1, 2):
         raise ValueError(f"unsupported convolution: kernel {k}, padding {padding}, stride {stride}")
     x, x2 = _split(array)
-    return ops.conv3d(x, _pack(weight), bias, x2=x2, stride=stride, out_dtype=activation_dtype(), stats=OUTPUT_STATS)
+    return ops.conv3d(x, _pack(weight), bias, x2=x2, stride=stride, out_dtype=activation_dtype(),
+                      stats=_want_stats(x, int(weight.shape[0]), 1.0 / 8 if stride == 2 else 1.0))
 
 
 def norm_conv3d_ncdhw(array, weight: torch.Tensor, bias: torch.Tensor, *, norm, num_groups: int, eps: float,
@@ -320,7 +332,8 @@ def norm_conv3d_ncdhw(array, weight: torch.Tensor, bias: torch.Tensor, *, norm, 
     return ops.conv3d(x, _pack(weight, upsample=upsample, out_voxels=voxels), bias, x2=x2, **nargs,
                       silu=apply_silu,
                       avgpool=avgpool, residual=res, residual_upsampled=residual_upsampled,
-                      out_dtype=activation_dtype(), stats=OUTPUT_STATS)
+                      out_dtype=activation_dtype(),
+                      stats=_want_stats(x, int(weight.shape[0]), (8.0 if upsample else 1.0) / (8 if avgpool else 1)))
 
 
 def trilinear_conv3d_ncdhw(array, weight: torch.Tensor, bias: torch.Tensor, *, mx=None) -> torch.Tensor:
@@ -328,7 +341,8 @@ def trilinear_conv3d_ncdhw(array, weight: torch.Tensor, bias: torch.Tensor, *, m
     x, x2 = _split(array)
     if x2 is not None:
         x = ChannelConcat(x, x2).materialize()
-    return ops.conv3d(x, _pack(weight), bias, trilinear=True, out_dtype=activation_dtype(), stats=OUTPUT_STATS)
+    return ops.conv3d(x, _pack(weight), bias, trilinear=True, out_dtype=activation_dtype(),
+                      stats=_want_stats(x, int(weight.shape[0]), 8.0))
 
 
 _TIME_TABLES: dict[tuple, tuple[torch.Tensor, torch.Tensor, torch.Tensor, list[tuple[int, int, int]]]] = {}
@@ -399,7 +413,8 @@ def residual_block_ncdhw(x, emb: torch.Tensor, weights: Mapping[str, torch.Tenso
         else:
             skip = ops.transform(xa, x2=xb, mode=_lib.TRANSFORM_AVGPOOL, out_dtype=dtype)
         hidden = ops.conv3d(xa, _pack(weights["conv1.conv.weight"]), bias1, x2=xb, **n1, silu=True,
-                            avgpool=True, out_dtype=dtype, stats=OUTPUT_STATS)
+                            avgpool=True, out_dtype=dtype,
+                            stats=_want_stats(xa, int(weights["conv1.conv.weight"].shape[0]), 1.0 / 8))
     else:
         if project:
             skip = ops.conv3d(xa, _pack(weights["skip_connection.conv.weight"]), weights["skip_connection.conv.bias"],
@@ -407,10 +422,12 @@ def residual_block_ncdhw(x, emb: torch.Tensor, weights: Mapping[str, torch.Tenso
         else:
             skip = xa if xb is None else ChannelConcat(xa, xb).materialize()
         hidden = ops.conv3d(xa, _pack(weights["conv1.conv.weight"], upsample=up), bias1, x2=xb, **n1,
-                            silu=True, out_dtype=dtype, stats=OUTPUT_STATS)
+                            silu=True, out_dtype=dtype,
+                            stats=_want_stats(xa, int(weights["conv1.conv.weight"].shape[0]), 8.0 if up else 1.0))
     n2 = _norm_args(hidden, None, weights["norm2.weight"], weights["norm2.bias"], groups=num_groups, eps=eps)
     return ops.conv3d(hidden, _pack(weights["conv2.conv.weight"]), weights["conv2.conv.bias"], **n2,
-                      silu=True, residual=skip, residual_upsampled=up, out_dtype=dtype, stats=OUTPUT_STATS)
+                      silu=True, residual=skip, residual_upsampled=up, out_dtype=dtype,
+                      stats=_want_stats(hidden, int(weights["conv2.conv.weight"].shape[0])))
 
 
 def vae_resblock_ncdhw(state: list, conv1, conv2, norm1, norm2, shortcut, *, num_groups: int, eps: float,
@@ -421,7 +438,8 @@ def vae_resblock_ncdhw(state: list, conv1, conv2, norm1, norm2, shortcut, *, num
     del array
     dtype = activation_dtype()
     n1 = _norm_args(x, x2, norm1[0], norm1[1], groups=num_groups, eps=eps)
-    hidden = ops.conv3d(x, _pack(conv1[0]), conv1[1], x2=x2, **n1, silu=True, out_dtype=dtype, stats=OUTPUT_STATS)
+    hidden = ops.conv3d(x, _pack(conv1[0]), conv1[1], x2=x2, **n1, silu=True, out_dtype=dtype,
+                        stats=_want_stats(x, int(conv1[0].shape[0])))
     if shortcut is None:
         skip = x if x2 is None else ChannelConcat(x, x2).materialize()
     else:
@@ -429,7 +447,7 @@ def vae_resblock_ncdhw(state: list, conv1, conv2, norm1, norm2, shortcut, *, num
     del x, x2
     n2 = _norm_args(hidden, None, norm2[0], norm2[1], groups=num_groups, eps=eps)
     out = ops.conv3d(hidden, _pack(conv2[0]), conv2[1], **n2, silu=True, residual=skip, out_dtype=dtype,
-                     stats=OUTPUT_STATS)
+                     stats=_want_stats(hidden, int(conv2[0].shape[0])))
     return out
 
 

@@ -432,7 +432,7 @@ def group_norm_affine(
             with _profiled("gn", 0.0, f"{b}x{ctot} {d}x{h}x{w} g{groups} from-stats"):
                 from_stats()
         return affine
-    _count(2)
+    _count(int(LIB.ctmr_group_norm_launch_count(voxels, ctot, groups)))
     ws_bytes = int(LIB.ctmr_group_norm_workspace_size(b, voxels, groups))
     ws = torch.empty(max(ws_bytes, 4), dtype=torch.uint8, device=x.device)
     def launch() -> None:

@@ -105,6 +105,25 @@ def test_group_norm_validation():
     assert st == _lib.CTMR_ERR_INVALID  # 30 channels are not divisible by 32 groups
 
 
+def test_group_norm_launch_count(monkeypatch):
+    """One launch for groups that 1024 threads read with at most eight loads each (four channels per
+    load when the group's channel count allows, at most 64 channels), two otherwise;
+    CTMR_DISABLE_GN_DIRECT keeps the two-pass path everywhere; invalid extents count nothing."""
+    count = _lib.LIB.ctmr_group_norm_launch_count
+    monkeypatch.delenv("CTMR_DISABLE_GN_DIRECT", raising=False)
+    assert count(8 * 8 * 4, 512, 32) == 1          # the UNet's deepest level: one load per thread
+    assert count(16 * 16 * 8, 512, 32) == 1        # level 2 concat, 16 channels per group: eight loads
+    assert count(16 * 16 * 8, 768, 32) == 2        # 24 channels per group: thirteen loads
+    assert count(8192, 128, 32) == 1               # 8,192 voxels x 4 channels: eight loads
+    assert count(8193, 128, 32) == 2               # one voxel more: a ninth load
+    assert count(32 * 32 * 16, 128, 32) == 2       # level 1
+    assert count(64 * 64 * 32, 64, 32) == 2        # the UNet's level 0
+    assert count(16, 65 * 2, 2) == 2               # 65 channels per group
+    assert count(100, 30, 4) == 0                  # channels not divisible by groups
+    monkeypatch.setenv("CTMR_DISABLE_GN_DIRECT", "1")
+    assert count(8 * 8 * 4, 512, 32) == 2
+
+
 @pytest.mark.parametrize(("args", "status"), [
     ((None, _lib.DTYPE_F16, 1, 128, 1, 0x2000), _lib.CTMR_ERR_INVALID),        # no Q/K/V
     ((0x1000, _lib.DTYPE_F32, 1, 128, 1, 0x2000), _lib.CTMR_ERR_INVALID),      # fp32 operands

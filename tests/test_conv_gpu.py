@@ -509,6 +509,10 @@ def test_narrow_output_with_half_grid_residual(cuda):
     ((1, 32, 2, 8, 16), 192, False, 3),   # 192 channels: N tiles of 128 + 64
     ((2, 64, 3, 8, 16), 128, True, 3),    # nearest-2x fold: every parity writes its voxels
     ((1, 128, 4, 16, 32), 256, False, 1), # 1x1x1, two N tiles
+    ((2, 64, 3, 30, 20), 64, False, 3),   # kh-concatenated kernel (four slots per CTA), partial tiles
+    ((2, 64, 2, 14, 24), 64, False, 3),   # ... six tiles: CTAs that see one batch item zero the other's slots
+    ((2, 64, 8, 64, 64), 64, False, 3),   # ... 320 tiles: CTAs walk several tiles across the batch change
+    ((1, 128, 6, 44, 40), 64, False, 3),  # ... two input channel blocks
 ])
 def test_output_statistics_match_a_pass(cuda, shape, out_channels, upsample, k, precision):
     """GroupNorm moments reduced in the persistent kernel's epilogue give the affine of a separate
@@ -547,10 +551,40 @@ def test_output_statistics_refused_where_unsupported(cuda):
     w = torch.randn((4, 64, 3, 3, 3), device=cuda) / 40
     y = ops.conv3d(x, ops.pack_weight(w, "fp32"), None, stats=True)  # narrow fp32 kernel
     assert ops.output_stats(y) is None
-    w = torch.randn((64, 64, 3, 3, 3), device=cuda) / 40
+    w = torch.randn((48, 64, 3, 3, 3), device=cuda) / 40
     y = ops.conv3d(ops.to_ndhwc(torch.randn((1, 64, 4, 8, 16), device=cuda)), ops.pack_weight(w, "fp16"), None,
-                   stats=True)  # under 128 output channels: a separate pass is cheaper
+                   stats=True)  # 48 outputs: the kh-concatenated kernel's per-voxel stores keep none
     assert ops.output_stats(y) is None
+    w = torch.randn((64, 64, 3, 3, 3), device=cuda) / 40
+    y = ops.conv3d(ops.to_ndhwc(torch.randn((1, 64, 4, 8, 16), device=cuda)), ops.pack_weight(w, "tf32"), None,
+                   stats=True)  # TF32 operands: the kh-concatenated kernel keeps none
+    assert ops.output_stats(y) is None
+
+
+def test_output_statistics_after_residual_and_norm(cuda):
+    """The kh-concatenated kernel's statistics describe the stored output: GroupNorm affine + SiLU on
+    the input, bias and a residual added in the epilogue (the VAE residual block's conv2), against a
+    statistics pass over the output; a second conv then consumes the affine from those statistics."""
+    from ctmr_b200 import ops
+
+    rng = np.random.default_rng(43)
+    shape = (1, 64, 6, 40, 48)
+    x = ops.to_ndhwc(torch.from_numpy((rng.standard_normal(shape) * 1.5 + 0.4).astype(np.float32)).to(cuda))
+    res = ops.to_ndhwc(torch.from_numpy(rng.standard_normal(shape).astype(np.float32)).to(cuda))
+    w = torch.from_numpy((rng.standard_normal((64, 64, 3, 3, 3)) / np.sqrt(27 * 64)).astype(np.float32)).to(cuda)
+    gamma = torch.from_numpy((1 + 0.2 * rng.standard_normal(64)).astype(np.float32)).to(cuda)
+    beta = torch.from_numpy((0.3 * rng.standard_normal(64)).astype(np.float32)).to(cuda)
+    bias = torch.from_numpy(rng.standard_normal(64).astype(np.float32)).to(cuda)
+    packed = ops.pack_weight(w, "fp16")
+    y = ops.conv3d(x, packed, bias, norm=(gamma, beta, 32, 1e-6), silu=True, residual=res, stats=True)
+    assert ops.output_stats(y) is not None
+    fused = ops.group_norm_affine(y, gamma, beta, groups=32, eps=1e-6)
+    plain = ops.group_norm_affine(y.clone(), gamma, beta, groups=32, eps=1e-6)
+    z_fused = ops.conv3d(y, packed, bias, affine=fused, silu=True)
+    z_plain = ops.conv3d(y, packed, bias, affine=plain, silu=True)
+    torch.cuda.synchronize()
+    torch.testing.assert_close(fused, plain, rtol=2e-5, atol=1e-6)
+    assert ops_ref.rel_l2(z_fused.cpu(), z_plain.cpu().double()) <= 1e-5
 
 
 @pytest.mark.parametrize(("shape", "x2_channels", "out_channels", "precision", "groups"), [
@@ -592,6 +626,59 @@ def test_groupnorm_inside_the_conv_call(cuda, shape, x2_channels, out_channels, 
     torch.cuda.synchronize()
     err = ops_ref.rel_l2(got.cpu(), ref.cpu().double())
     assert err <= (1e-6 if precision == "fp32" else 1e-3), f"{precision} rel-L2 {err:.3e}"
+
+
+GN_DIRECT_CASES = [
+    ((2, 512, 4, 8, 8), 0, 32),       # 16 channels per group: shuffle-xor tree
+    ((2, 256, 8, 16, 16), 128, 32),   # virtual concat, 12 channels per group: lane-ordered sums
+    ((1, 128, 8, 32, 32), 0, 32),     # 4 channels per group over 8,192 voxels: eight 16-byte loads
+    ((2, 64, 8, 16, 32), 0, 32),      # 2 channels per group: eight 4-byte loads
+    ((2, 1024, 4, 8, 8), 512, 32),    # 48 channels per group
+    ((1, 24, 3, 5, 7), 0, 8),         # 3 channels per group, 85 lanes, odd extents
+]
+
+
+@pytest.mark.parametrize(("shape", "x2_channels", "groups"), GN_DIRECT_CASES)
+def test_group_norm_small_tensor_kernel(cuda, shape, x2_channels, groups, monkeypatch):
+    """Small GroupNorms (a group that 1024 threads read with at most eight loads each) run one kernel,
+    one block per group and batch item: it is the kernel launched, its affine matches float64 and the
+    two-pass path (CTMR_DISABLE_GN_DIRECT), and it is bitwise reproducible."""
+    from ctmr_b200 import _lib, ops
+
+    rng = np.random.default_rng(73)
+    b, c = shape[:2]
+    xh = (rng.standard_normal(shape) * 2 + 0.7).astype(np.float32)
+    x2h = rng.standard_normal((b, x2_channels, *shape[2:])).astype(np.float32) if x2_channels else None
+    x = ops.to_ndhwc(torch.from_numpy(xh).to(cuda))
+    x2 = ops.to_ndhwc(torch.from_numpy(x2h).to(cuda)) if x2_channels else None
+    ctot = c + x2_channels
+    gamma = torch.from_numpy((1 + 0.2 * rng.standard_normal(ctot)).astype(np.float32)).to(cuda)
+    beta = torch.from_numpy((0.3 * rng.standard_normal(ctot)).astype(np.float32)).to(cuda)
+    voxels = int(np.prod(shape[2:]))
+    monkeypatch.delenv("CTMR_DISABLE_GN_DIRECT", raising=False)
+    assert _lib.LIB.ctmr_group_norm_launch_count(voxels, ctot, groups) == 1
+    out = {}
+    names = _kernel_names(lambda: out.setdefault(
+        "direct", ops.group_norm_affine(x, gamma, beta, groups=groups, eps=1e-6, x2=x2)))
+    assert any("gn_direct" in n for n in names) and not any("gn_partial" in n for n in names), names
+    direct = out["direct"]
+    again = ops.group_norm_affine(x, gamma, beta, groups=groups, eps=1e-6, x2=x2)
+    monkeypatch.setenv("CTMR_DISABLE_GN_DIRECT", "1")
+    assert _lib.LIB.ctmr_group_norm_launch_count(voxels, ctot, groups) == 2
+    two_pass = ops.group_norm_affine(x, gamma, beta, groups=groups, eps=1e-6, x2=x2)
+    monkeypatch.delenv("CTMR_DISABLE_GN_DIRECT")
+    torch.cuda.synchronize()
+    assert torch.equal(direct, again)
+    full = np.concatenate([xh, x2h], axis=1) if x2_channels else xh
+    xg = full.astype(np.float64).reshape(b, groups, -1)
+    cpg = ctot // groups
+    mean = np.repeat(xg.mean(axis=2), cpg, axis=1)
+    rstd = np.repeat(1.0 / np.sqrt(xg.var(axis=2) + 1e-6), cpg, axis=1)
+    scale = gamma.double().cpu().numpy()[None, :] * rstd
+    offset = beta.double().cpu().numpy()[None, :] - mean * scale
+    expected = torch.from_numpy(np.stack([scale, offset], axis=-1))
+    torch.testing.assert_close(direct.cpu().double(), expected, rtol=1e-5, atol=1e-5)
+    torch.testing.assert_close(direct, two_pass, rtol=2e-6, atol=2e-6)
 
 
 @pytest.mark.parametrize("shape", [(2, 64, 3, 16, 16), (2, 32, 2, 8, 16)])
