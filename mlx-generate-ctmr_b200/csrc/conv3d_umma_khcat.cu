@@ -362,15 +362,20 @@ __global__ void __launch_bounds__(kKhThreads, 1)
     // 64 output channels: half h reads chunks 2h, 2h + 1 (32 contiguous channels per lane), stored
     // through an 8-lane transpose. Fewer: chunks h, h + 2 (both halves busy), stored per voxel.
     const bool wide = nchunks == 4;
-    // STATS (64 output columns only): each lane keeps the (count, mean, M2) moments of its four
-    // output channels over the voxels it stores, for one batch item at a time (tiles come in
-    // batch order); at a batch change and at the end the warp merges its four 8-lane groups and
-    // lanes 0..7 write the warp's slot 4 x CTA + quarter. Batch items a warp never saw get zeros.
-    float st[4][3];
+    // STATS (64 output columns only): each lane keeps, for its four output channels and the current
+    // batch item (tiles come in batch order), the count of the voxels it stores and the sums of
+    // (x - pivot) and (x - pivot)^2 around a pivot per channel (the first value it sees), with no
+    // division per tile. At a batch change and at the end the lane turns them into (count, mean,
+    // M2), the warp merges its four 8-lane groups by Chan's update and lanes 0..7 write the warp's
+    // slot 4 x CTA + quarter. Batch items a warp never saw get zeros.
+    float st_n = 0.f, st_p[4], st_s[4], st_q[4];
+    bool st_have = false;
     int st_b = -1, st_next = 0;
     auto stats_reset = [&]() {
+      st_n = 0.f;
+      st_have = false;
 #pragma unroll
-      for (int e = 0; e < 4; ++e) st[e][0] = st[e][1] = st[e][2] = 0.f;
+      for (int e = 0; e < 4; ++e) st_p[e] = st_s[e] = st_q[e] = 0.f;
     };
     auto stats_zero = [&](int bb) {  // this warp's slot for batch item bb holds nothing
       if (lane < 8) {
@@ -381,20 +386,28 @@ __global__ void __launch_bounds__(kKhThreads, 1)
           if (nc + e < g.cout) dst[(nc + e) * 3] = dst[(nc + e) * 3 + 1] = dst[(nc + e) * 3 + 2] = 0.f;
       }
     };
-    auto stats_flush = [&]() {  // warp-collective: merge the 8-lane groups, write slot of st_b
+    auto stats_flush = [&]() {  // warp-collective: moments, merge the 8-lane groups, write slot of st_b
+      float m[4][3];
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        const float md = st_n > 0.f ? st_s[e] / st_n : 0.f;
+        m[e][0] = st_n;
+        m[e][1] = st_p[e] + md;
+        m[e][2] = fmaxf(0.f, st_q[e] - st_s[e] * md);
+      }
 #pragma unroll
       for (int off = 8; off < 32; off <<= 1) {
 #pragma unroll
         for (int e = 0; e < 4; ++e) {
-          const float on = __shfl_xor_sync(0xffffffffu, st[e][0], off);
-          const float om = __shfl_xor_sync(0xffffffffu, st[e][1], off);
-          const float o2 = __shfl_xor_sync(0xffffffffu, st[e][2], off);
+          const float on = __shfl_xor_sync(0xffffffffu, m[e][0], off);
+          const float om = __shfl_xor_sync(0xffffffffu, m[e][1], off);
+          const float o2 = __shfl_xor_sync(0xffffffffu, m[e][2], off);
           if (lane & off) {  // both partners merge (lower group, upper group): the same result
-            float m[3] = {on, om, o2};
-            chan_merge(m, st[e][0], st[e][1], st[e][2]);
-            st[e][0] = m[0], st[e][1] = m[1], st[e][2] = m[2];
+            float r[3] = {on, om, o2};
+            chan_merge(r, m[e][0], m[e][1], m[e][2]);
+            m[e][0] = r[0], m[e][1] = r[1], m[e][2] = r[2];
           } else {
-            chan_merge(st[e], on, om, o2);
+            chan_merge(m[e], on, om, o2);
           }
         }
       }
@@ -404,9 +417,9 @@ __global__ void __launch_bounds__(kKhThreads, 1)
 #pragma unroll
         for (int e = 0; e < 4; ++e)
           if (nc + e < g.cout) {
-            dst[(nc + e) * 3] = st[e][0];
-            dst[(nc + e) * 3 + 1] = st[e][1];
-            dst[(nc + e) * 3 + 2] = st[e][2];
+            dst[(nc + e) * 3] = m[e][0];
+            dst[(nc + e) * 3 + 1] = m[e][1];
+            dst[(nc + e) * 3 + 2] = m[e][2];
           }
       }
     };
@@ -538,26 +551,20 @@ __global__ void __launch_bounds__(kKhThreads, 1)
               q[k].w += rv[k].w;
             }
           }
-          if (STATS) {  // moments of this depth's (up to) eight voxels, merged into the lane's
+          if (STATS) {  // shifted sums of this depth's (up to) eight stored voxels
+            if (!st_have) {  // the first stored voxel of this batch item sets the pivots
 #pragma unroll
-            for (int e = 0; e < 4; ++e) {
-              float cnt = 0.f, sum = 0.f;
+              for (int k = 7; k >= 0; --k)
+                if (ok[k]) st_p[0] = q[k].x, st_p[1] = q[k].y, st_p[2] = q[k].z, st_p[3] = q[k].w, st_have = true;
+            }
 #pragma unroll
-              for (int k = 0; k < 8; ++k) {
-                const float x = e == 0 ? q[k].x : e == 1 ? q[k].y : e == 2 ? q[k].z : q[k].w;
-                if (ok[k]) cnt += 1.f, sum += x;
-              }
-              if (cnt > 0.f && n + e < g.cout) {
-                const float mean = sum / cnt;
-                float m2 = 0.f;
-#pragma unroll
-                for (int k = 0; k < 8; ++k) {
-                  const float x = e == 0 ? q[k].x : e == 1 ? q[k].y : e == 2 ? q[k].z : q[k].w;
-                  const float dv = x - mean;
-                  if (ok[k]) m2 = fmaf(dv, dv, m2);
-                }
-                chan_merge(st[e], cnt, mean, m2);
-              }
+            for (int k = 0; k < 8; ++k) {
+              if (!ok[k]) continue;
+              const float dx = q[k].x - st_p[0], dy = q[k].y - st_p[1], dz = q[k].z - st_p[2], dw = q[k].w - st_p[3];
+              st_s[0] += dx, st_s[1] += dy, st_s[2] += dz, st_s[3] += dw;
+              st_q[0] = fmaf(dx, dx, st_q[0]), st_q[1] = fmaf(dy, dy, st_q[1]);
+              st_q[2] = fmaf(dz, dz, st_q[2]), st_q[3] = fmaf(dw, dw, st_q[3]);
+              st_n += 1.f;
             }
           }
 #pragma unroll
