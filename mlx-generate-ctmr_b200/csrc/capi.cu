@@ -420,6 +420,46 @@ bool plan_khcat(const ConvPlan& p, const ctmr_conv3d_desc* d, bool with_stats, K
   return false;
 }
 
+// Whether the kh-concatenated kernel converts its own operand (GroupNorm affine, SiLU and the
+// 16-bit rounding in four converter warps) instead of the separate operand pass writing a 16-bit
+// copy that the kernel then loads: CTMR_KHCAT_FUSE=1 / 0 forces it on / off.
+constexpr bool kKhcatFuseDefault = false;
+bool khcat_fuse_enabled() {
+  const char* e = getenv("CTMR_KHCAT_FUSE");
+  if (e != nullptr && e[0] != '\0') return e[0] == '1';
+  return kKhcatFuseDefault;
+}
+
+// The fused route's conditions: a stride-1 3x3x3 conv in a 16-bit mode on the kh-concatenated
+// kernel with 64-channel blocks, whose operand is a plain copy (optionally affine + SiLU) of fp32
+// sources of whole 64-channel blocks with 16-byte aligned 4-channel pieces.
+bool khcat_fusable(const ConvPlan& p, const ctmr_conv3d_desc* d, const KhPlan& kh, const float* affine) {
+  if (!khcat_fuse_enabled() || kh.kc != 64 || !p.prepare || p.im2col || p.exact || p.tf32 || p.gn_small ||
+      p.mode != ctmr::kModeConv3 || d->trilinear || d->avgpool || p.cin % 64 != 0 || p.cpad != p.cin)
+    return false;
+  if (d->x.dtype != CTMR_DTYPE_F32 || d->x.cstride % 4 != 0 || !aligned16(d->x.data)) return false;
+  if (d->x2.data != nullptr && (d->x2.dtype != CTMR_DTYPE_F32 || d->x.channels % 64 != 0 ||
+                                d->x2.cstride % 4 != 0 || !aligned16(d->x2.data)))
+    return false;
+  if (affine != nullptr && !aligned16(affine)) return false;
+  // The converter warps read the sources while the epilogue writes the output: no overlap (the
+  // operand pass would have read them in a launch of its own).
+  const long long rows = static_cast<long long>(d->batch) * d->depth * d->height * d->width;
+  const long long out_rows = static_cast<long long>(d->batch) * p.out_d * p.out_h * p.out_w;
+  const size_t y_bytes = static_cast<size_t>(((out_rows - 1) * d->y_cstride + d->y_coffset + d->out_channels) *
+                                             (d->y_dtype == CTMR_DTYPE_BF16 ? 2 : 4));
+  const auto overlaps_y = [&](const ctmr_tensor& t) {
+    const size_t t_bytes = static_cast<size_t>(((rows - 1) * t.cstride + t.channels) * 4);
+    const uintptr_t a = reinterpret_cast<uintptr_t>(t.data), y = reinterpret_cast<uintptr_t>(d->y);
+    return a < y + y_bytes && y < a + t_bytes;
+  };
+  if (overlaps_y(d->x) || (d->x2.data != nullptr && overlaps_y(d->x2))) return false;
+  const long long total = static_cast<long long>((p.row_w + 7) / 8) *
+                          ((p.row_h + ctmr::conv_khcat_rows() - 1) / ctmr::conv_khcat_rows()) *
+                          ((p.row_d + kh.mt - 1) / kh.mt) * d->batch;
+  return total > 0 && total < (1LL << 31);
+}
+
 bool plan_v2(const ConvPlan& p, const ctmr_conv3d_desc* d, bool with_stats, V2Plan* v) {
   if ((p.exact && with_stats) ||
       !(p.mode == ctmr::kModeConv3 || p.mode == ctmr::kModeUp2 || p.mode == ctmr::kModeConv1) || p.row_w < 16 ||
@@ -661,6 +701,19 @@ int ctmr_conv3d_stages(const ctmr_conv3d_desc* d, void* workspace, size_t worksp
     return e == cudaSuccess ? CTMR_OK : cuda_fail(e, "tiny-input conv launch");
   }
 
+  // The kh-concatenated kernel's plan; with converter warps it reads the fp32 input itself and the
+  // operand pass below is skipped (decided here, once its weight tensor map is known to encode).
+  const bool with_stats = d->stats != nullptr;
+  V2Plan v2{};
+  KhPlan kh{};
+  const bool kh_ok = plan_khcat(p, d, with_stats, &kh);
+  ctmr::ConvMaps fuse_maps;
+  bool fuse = false;
+  if (kh_ok && khcat_fusable(p, d, kh, affine)) {
+    std::memset(&fuse_maps, 0, sizeof(fuse_maps));
+    fuse = encode_weight_kh(&fuse_maps.b, d->weight, p.bf16, p.cpad, p.opad, kh.kc, p.opad) == CTMR_OK;
+  }
+
   // 1. Operand preparation (affine, SiLU, trilinear / avgpool, concat, cast or split).
   const void* a_hi = d->x.data;
   const void* a_lo = nullptr;
@@ -695,7 +748,7 @@ int ctmr_conv3d_stages(const ctmr_conv3d_desc* d, void* workspace, size_t worksp
     e = ctmr::launch_repack_im2col(d->weight, p.exact ? d->weight_lo : nullptr, p.opad, p.cpad_src, p.cin_raw,
                                    p.cpad, const_cast<void*>(w_hi), const_cast<void*>(w_lo), stream);
     if (e != cudaSuccess) return cuda_fail(e, "im2col weight repack launch");
-  } else if (p.prepare && (stages & CTMR_CONV_PREPARE)) {
+  } else if (p.prepare && !fuse && (stages & CTMR_CONV_PREPARE)) {
     ctmr::PrepParams pp{};
     pp.src[0] = as_source(d->x);
     pp.src[1] = as_source(d->x2);
@@ -719,10 +772,6 @@ int ctmr_conv3d_stages(const ctmr_conv3d_desc* d, void* workspace, size_t worksp
   if (!(stages & CTMR_CONV_GEMM)) return CTMR_OK;
 
   // 2a. The persistent atom-shifted kernel for 16-bit stride-1 3x3x3, nearest-2x and 1x1x1 convolutions.
-  const bool with_stats = d->stats != nullptr;
-  V2Plan v2{};
-  KhPlan kh{};
-  const bool kh_ok = plan_khcat(p, d, with_stats, &kh);
   if (with_stats && !(kh_ok ? d->stats_slots >= 4 * sm_count()
                             : d->stats_slots >= sm_count() && plan_v2(p, d, true, &v2)))
     return fail(CTMR_ERR_UNSUPPORTED, "output statistics need the persistent kernel (ctmr_conv3d_stats_slots)");
@@ -766,6 +815,18 @@ int ctmr_conv3d_stages(const ctmr_conv3d_desc* d, void* workspace, size_t worksp
       g.out_cstride = d->y_cstride;
       g.out_coff = d->y_coffset;
       g.out_d = p.out_d, g.out_h = p.out_h, g.out_w = p.out_w;
+      if (fuse) {
+        g.fuse_src0 = static_cast<const float*>(d->x.data);
+        g.fuse_cstride0 = d->x.cstride;
+        g.fuse_src1 = static_cast<const float*>(d->x2.data);
+        g.fuse_cstride1 = d->x2.data != nullptr ? d->x2.cstride : 0;
+        g.fuse_ch0 = d->x.channels;
+        g.fuse_ctot = p.cin;
+        g.fuse_affine = affine;
+        g.fuse_silu = d->silu ? 1 : 0;
+        cudaError_t e = ctmr::launch_conv3d_khcat(fuse_maps, g, kh.kc, kh.mt, sm_count(), kh.smem, stream);
+        return e == cudaSuccess ? CTMR_OK : cuda_fail(e, "conv3d kh-concatenated launch (converter warps)");
+      }
       ctmr::ConvMaps maps;
       std::memset(&maps, 0, sizeof(maps));
       const long long rs = a_cstride * 2;
@@ -1050,10 +1111,14 @@ int ctmr_conv3d_launch_count(const ctmr_conv3d_desc* d) {
   const long long voxels = static_cast<long long>(d->depth) * d->height * d->width;
   int n = (p.gn_in && !p.gn_small) ? (ctmr::gn_direct_fits(voxels, p.cin, d->gn_groups) ? 1 : 2) : 0;
   if (p.narrow || p.tiny) return n + 1;
-  if (p.prepare) n += p.im2col ? 2 : 1;
   V2Plan v2{};
   KhPlan kh{};
-  if (plan_khcat(p, d, d->stats != nullptr, &kh) || plan_v2(p, d, d->stats != nullptr, &v2)) return n + 1;
+  const bool kh_ok = plan_khcat(p, d, d->stats != nullptr, &kh);
+  // The fused route's affine is the caller's or, with the call's own GroupNorm, the workspace's
+  // (256-byte aligned within it): only the caller's pointer can disqualify it here.
+  const bool fused = kh_ok && khcat_fusable(p, d, kh, p.gn_in ? nullptr : d->affine);
+  if (p.prepare && !fused) n += p.im2col ? 2 : 1;
+  if (kh_ok || plan_v2(p, d, d->stats != nullptr, &v2)) return n + 1;
   return n + 1 + (p.ksplit > 1 ? 1 : 0);
 }
 

@@ -62,6 +62,15 @@ struct ConvGeom {
   // slot, channel) moments (count, mean, M2) as float[batch][stats_slots][cout][3].
   float* stats;                 // null: not requested
   int stats_slots;              // slots in the buffer (>= the grid; the rest are zeroed)
+  // kh-concatenated kernel with its own operand conversion (no separate operand pass): the fp32
+  // NDHWC source(s) on the row grid, channels [0, ch0) from src0 and [ch0, ctot) from src1, each
+  // value taken through silu?(v * scale[b, c] + offset[b, c]) and rounded to the operand type.
+  const float* fuse_src0;
+  const float* fuse_src1;
+  long long fuse_cstride0, fuse_cstride1;
+  int fuse_ch0, fuse_ctot;
+  const float* fuse_affine;     // [batch][ctot][2] (scale, offset) or null
+  int fuse_silu;
 };
 
 }  // namespace ctmr

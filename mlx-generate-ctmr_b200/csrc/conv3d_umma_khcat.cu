@@ -24,6 +24,12 @@
 // with 16-wide lane shuffles and release it, then add bias and residual and
 // store while the next tile's MMAs run (with 64 output channels through an
 // 8-lane transpose, so that each warp store writes whole 128-byte lines).
+// The FUSE variant (64-channel blocks) reads the fp32 input itself: four converter
+// warps load each activation box's rows from the NDHWC source (16-byte loads, eight
+// in flight per lane), apply the GroupNorm affine and SiLU, round to the operand
+// type and store the rows into the 128-byte-swizzled ring slot, so the fp16 copy of
+// the operand pass is never written or read. Rows outside the volume are the zero
+// padding of the transformed input, as the TMA fill of the prepared copy gives.
 // A CTA-pair variant (clusters of two, tcgen05.mma.cta_group::2 with M = 256) is at
 // the end of the file; it runs only when CTMR_KHCAT_PAIR=1 selects it.
 #include <cuda_bf16.h>
@@ -38,6 +44,10 @@ namespace ctmr {
 namespace {
 
 constexpr int kKhThreads = 320;  // warp 0 TMA, warp 1 MMA + TMEM, warps 2..9 epilogue
+// The variant that converts its own operand (FUSE) adds warps 10..13, which fill the activation
+// ring from the fp32 source in place of the TMA activation boxes.
+constexpr int kKhConvWarps = 4;
+constexpr int kKhThreadsFused = kKhThreads + 32 * kKhConvWarps;
 constexpr int kKhRows = 14;      // output rows along h per tile
 constexpr int kKhBoxW = 10;      // w per activation box: 8 output columns and the kw halo
 constexpr int kKhMaxBSlots = 12;  // weight ring slots at most
@@ -176,13 +186,93 @@ __device__ __forceinline__ void kh_store4(const ConvGeom& g, float4 v, int n, lo
   }
 }
 
+// SiLU of the operand, the same expression as the operand pass's 16-bit path (hardware exponential
+// and reciprocal), so that both routes give the same operand bits.
+__device__ __forceinline__ float kh_silu(float t) { return __fdividef(t, 1.f + __expf(-t)); }
+
+// One converter warp's share of an activation box: rows r = 8 i + 2 cw + (lane / 16) of the
+// MT x 10 w x 16 h box (row r at byte r x 128 of the slot, its 16-byte chunks swizzled by r mod 8),
+// each lane taking 4 channels (lane mod 16) of the 64-channel block starting at channel c0.
+// Source voxel of row r: depth d0 + kd - 1 + r / 160, w w0 - 1 + (r mod 160) / 16, h h0 - 1 + r mod 16.
+template <int MT>
+__device__ __forceinline__ void kh_convert_box(const ConvGeom& g, uint32_t slot, int cw, int lane, int b, int dd,
+                                               int h0, int w0, int c0) {
+  constexpr int kRows = MT * kKhBoxW * 16;
+  const int q = lane & 15;
+  const int c = c0 + 4 * q;
+  const bool in1 = c >= g.fuse_ch0;
+  const float* src = in1 ? g.fuse_src1 + (c - g.fuse_ch0) : g.fuse_src0 + c;
+  const long long cs = in1 ? g.fuse_cstride1 : g.fuse_cstride0;
+  float sc[4] = {1.f, 1.f, 1.f, 1.f}, of[4] = {0.f, 0.f, 0.f, 0.f};
+  const bool aff = g.fuse_affine != nullptr;
+  if (aff) {
+    const float4* a = reinterpret_cast<const float4*>(g.fuse_affine + (static_cast<long long>(b) * g.fuse_ctot + c) * 2);
+    const float4 a0 = __ldg(a), a1 = __ldg(a + 1);
+    sc[0] = a0.x, of[0] = a0.y, sc[1] = a0.z, of[1] = a0.w, sc[2] = a1.x, of[2] = a1.y, sc[3] = a1.z, of[3] = a1.w;
+  }
+  const bool silu = g.fuse_silu != 0;
+  const int D = g.row_d, H = g.row_h, W = g.row_w;
+  const uint32_t lane_byte = static_cast<uint32_t>(q & 1) << 3;
+  const uint32_t chunk = static_cast<uint32_t>(q >> 1);
+  const int r_first = 2 * cw + (lane >> 4);
+#pragma unroll 1
+  for (int r0 = 0; r0 < kRows; r0 += 64) {
+    float4 v[8];
+    uint32_t live = 0;
+#pragma unroll
+    for (int k = 0; k < 8; ++k) {
+      const int r = r0 + 8 * k + r_first;
+      const int m = r >= kKhBoxW * 16 ? 1 : 0;
+      const int rem = r - m * kKhBoxW * 16;
+      const int d = dd + m, h = h0 - 1 + (rem & 15), w = w0 - 1 + (rem >> 4);
+      v[k] = make_float4(0.f, 0.f, 0.f, 0.f);
+      if (r < kRows && static_cast<unsigned>(d) < static_cast<unsigned>(D) &&
+          static_cast<unsigned>(h) < static_cast<unsigned>(H) && static_cast<unsigned>(w) < static_cast<unsigned>(W)) {
+        v[k] = __ldg(reinterpret_cast<const float4*>(
+            src + (((static_cast<long long>(b) * D + d) * H + h) * W + w) * cs));
+        live |= 1u << k;
+      }
+    }
+#pragma unroll
+    for (int k = 0; k < 8; ++k) {
+      const int r = r0 + 8 * k + r_first;
+      if (r >= kRows) continue;
+      uint32_t lo = 0, hi = 0;  // zero padding outside the volume
+      if (live & (1u << k)) {
+        float x[4] = {v[k].x, v[k].y, v[k].z, v[k].w};
+        if (aff) {
+#pragma unroll
+          for (int e = 0; e < 4; ++e) x[e] = fmaf(x[e], sc[e], of[e]);
+        }
+        if (silu) {
+#pragma unroll
+          for (int e = 0; e < 4; ++e) x[e] = kh_silu(x[e]);
+        }
+        if (g.operand_bf16) {
+          lo = pack_bf16x2(x[0], x[1]);
+          hi = pack_bf16x2(x[2], x[3]);
+        } else {
+          const __half2 p0 = __floats2half2_rn(x[0], x[1]);
+          const __half2 p1 = __floats2half2_rn(x[2], x[3]);
+          lo = *reinterpret_cast<const uint32_t*>(&p0);
+          hi = *reinterpret_cast<const uint32_t*>(&p1);
+        }
+      }
+      const uint32_t addr = slot + static_cast<uint32_t>(r) * 128u +
+                            ((chunk ^ (static_cast<uint32_t>(r) & 7u)) << 4) + lane_byte;
+      asm volatile("st.shared.v2.b32 [%0], {%1, %2};" ::"r"(addr), "r"(lo), "r"(hi) : "memory");
+    }
+  }
+}
+
 // Accumulator buffers in the 512 TMEM columns: two (the epilogue of tile i overlaps the MMAs of
 // tile i + 1) when 2 x MT x 3 x C_out columns fit, else one, released depth by depth.
 __host__ __device__ constexpr int kh_buffers(int mt, int bn) { return 2 * mt * 3 * bn <= 512 ? 2 : 1; }
 
-template <int KC, int MT, bool TF32, bool STATS>
-__global__ void __launch_bounds__(kKhThreads, 1)
+template <int KC, int MT, bool TF32, bool STATS, bool FUSE>
+__global__ void __launch_bounds__(FUSE ? kKhThreadsFused : kKhThreads, 1)
     conv3d_khcat_kernel(const __grid_constant__ ConvMaps maps, const __grid_constant__ ConvGeom g) {
+  static_assert(!FUSE || (KC == 64 && !TF32), "the converter warps fill 64-channel 16-bit rows");
   constexpr uint32_t kRowBytes = KC * 2;
   constexpr int kSteps = KC / 16;
   extern __shared__ uint8_t smem_raw[];
@@ -210,7 +300,7 @@ __global__ void __launch_bounds__(kKhThreads, 1)
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < SA; ++s) {
-      mbar_init(&a_full[s], 1);
+      mbar_init(&a_full[s], FUSE ? kKhConvWarps : 1);  // the TMA box, or one arrival per converter warp
       mbar_init(&a_empty[s], 1);
     }
     for (int s = 0; s < S; ++s) {
@@ -248,7 +338,7 @@ __global__ void __launch_bounds__(kKhThreads, 1)
 
   if (warp == 0 && lane == 0) {
     // ------------------------------------------------------------ TMA producer
-    tma_prefetch_desc(&maps.a[0]);
+    if (!FUSE) tma_prefetch_desc(&maps.a[0]);
     tma_prefetch_desc(&maps.b);
     int ia = 0;  // activation boxes issued
     int ib = 0;  // weight boxes issued
@@ -260,18 +350,20 @@ __global__ void __launch_bounds__(kKhThreads, 1)
       for (int gi = 0; gi < groups_per_tile && !stop; ++gi) {
         const int kd = gi / g.kblocks;
         const int c = (gi - kd * g.kblocks) * KC;
-        const int sa = ia % SA;
-        if (ia >= SA &&
-            !mbar_wait_bounded(&a_empty[sa], static_cast<uint32_t>(ia / SA - 1) & 1u, kErrWaitEmpty)) {
-          stop = true;
-          break;
+        if (!FUSE) {
+          const int sa = ia % SA;
+          if (ia >= SA &&
+              !mbar_wait_bounded(&a_empty[sa], static_cast<uint32_t>(ia / SA - 1) & 1u, kErrWaitEmpty)) {
+            stop = true;
+            break;
+          }
+          mbar_arrive_expect_tx(&a_full[sa], L.a_bytes);
+          // Activations (C, H, W, D, B): 16 h from h0 - 1, 10 w from w0 - 1 (the windows of all
+          // three kw taps), MT depths at the kd offset.
+          tma_load_5d(smem + static_cast<size_t>(sa) * L.a_bytes, &maps.a[0], &a_full[sa], c, h0 - 1, w0 - 1,
+                      d0 + kd - 1, b);
+          ++ia;
         }
-        mbar_arrive_expect_tx(&a_full[sa], L.a_bytes);
-        // Activations (C, H, W, D, B): 16 h from h0 - 1, 10 w from w0 - 1 (the windows of all
-        // three kw taps), MT depths at the kd offset.
-        tma_load_5d(smem + static_cast<size_t>(sa) * L.a_bytes, &maps.a[0], &a_full[sa], c, h0 - 1, w0 - 1,
-                    d0 + kd - 1, b);
-        ++ia;
         for (int kw = 0; kw < 3; ++kw) {
           const int s = ib % S;
           if (ib >= S && !mbar_wait_bounded(&empty[s], static_cast<uint32_t>(ib / S - 1) & 1u, kErrWaitEmpty)) {
@@ -286,7 +378,7 @@ __global__ void __launch_bounds__(kKhThreads, 1)
       }
     }
     if (stop) *abort_flag = 1;
-    // Every box in flight lands before the CTA exits.
+    // Every box in flight lands before the CTA exits (FUSE: weight boxes only, ia stays 0).
     for (int k = max(0, ia - SA); k < ia; ++k) {
       if (!mbar_wait_bounded(&a_full[k % SA], static_cast<uint32_t>(k / SA) & 1u, kErrWaitDrain)) break;
     }
@@ -351,7 +443,35 @@ __global__ void __launch_bounds__(kKhThreads, 1)
       umma_commit(&tmem_full[buf]);
     }
     if (stop) *abort_flag = 1;
-  } else if (warp >= 2) {
+  } else if (FUSE && warp >= 10) {
+    // ------------------------------------------------------------ operand converters
+    // Same tile and (kd, channel block) order as the MMA issuer; each warp fills its rows of the
+    // slot, makes its shared-memory stores visible to the tensor cores' async proxy and arrives.
+    const int cw = warp - 10;
+    int ia = 0;
+    bool stop = false;
+    for (int t = blockIdx.x; t < g.total_tiles && !stop && !*abort_flag; t += gridDim.x) {
+      int w0, h0, d0, b;
+      decode(t, w0, h0, d0, b);
+      for (int gi = 0; gi < groups_per_tile; ++gi) {
+        const int kd = gi / g.kblocks;
+        const int c = (gi - kd * g.kblocks) * KC;
+        const int sa = ia % SA;
+        if (ia >= SA &&
+            !mbar_wait_bounded(&a_empty[sa], static_cast<uint32_t>(ia / SA - 1) & 1u, kErrWaitEmpty)) {
+          stop = true;
+          break;
+        }
+        kh_convert_box<MT>(g, smem_u32(smem + static_cast<size_t>(sa) * L.a_bytes), cw, lane, b, d0 + kd - 1, h0,
+                           w0, c);
+        fence_proxy_async_shared();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&a_full[sa]);
+        ++ia;
+      }
+    }
+    if (stop) *abort_flag = 1;
+  } else if (warp >= 2 && warp < 10) {
     // ------------------------------------------------------------ epilogue
     const int ew = warp - 2;
     const int quarter = warp & 3;  // TMEM lanes a warp may read: 32 x (warp id mod 4)
@@ -948,12 +1068,22 @@ __global__ void __launch_bounds__(kKhThreads, 1)
 template <int KC, int MT>
 cudaError_t launch_khcat_typed(const ConvMaps& maps, const ConvGeom& g, int grid, size_t smem, cudaStream_t stream) {
   // Epilogue statistics: 16-bit operands and 64 output columns only (the planner's condition).
-  auto kern = g.stats != nullptr ? conv3d_khcat_kernel<KC, MT, false, true>
-              : g.operand_tf32  ? conv3d_khcat_kernel<KC, MT, true, false>
-                                : conv3d_khcat_kernel<KC, MT, false, false>;
+  auto kern = g.stats != nullptr ? conv3d_khcat_kernel<KC, MT, false, true, false>
+              : g.operand_tf32  ? conv3d_khcat_kernel<KC, MT, true, false, false>
+                                : conv3d_khcat_kernel<KC, MT, false, false, false>;
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
   if (e != cudaSuccess) return e;
   return launch_kernel(kern, grid, kKhThreads, smem, stream, maps, g);
+}
+
+template <int MT>
+cudaError_t launch_khcat_fused_typed(const ConvMaps& maps, const ConvGeom& g, int grid, size_t smem,
+                                     cudaStream_t stream) {
+  auto kern = g.stats != nullptr ? conv3d_khcat_kernel<64, MT, false, true, true>
+                                 : conv3d_khcat_kernel<64, MT, false, false, true>;
+  cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
+  if (e != cudaSuccess) return e;
+  return launch_kernel(kern, grid, kKhThreadsFused, smem, stream, maps, g);
 }
 
 }  // namespace
@@ -1026,6 +1156,19 @@ cudaError_t launch_conv3d_khcat(const ConvMaps& maps, const ConvGeom& g, int kc,
   if (g.total_tiles <= 0 || g.bn > 64 || g.bn % 16 != 0 || g.tmem_cols != 512) return cudaErrorInvalidValue;
   const int grid = g.total_tiles < sms ? g.total_tiles : sms;
   if (g.stats != nullptr && (g.bn != 64 || g.operand_tf32 || g.stats_slots < 4 * grid)) return cudaErrorInvalidValue;
+  if (g.fuse_src0 != nullptr) {
+    // The converter warps: 64-channel blocks of fp32 sources, 16-byte aligned 4-channel pieces.
+    if (kc != 64 || g.operand_tf32 || g.fuse_ctot % 64 != 0 || g.fuse_ch0 % 64 != 0 || g.fuse_cstride0 % 4 != 0 ||
+        (reinterpret_cast<uintptr_t>(g.fuse_src0) & 15) != 0 ||
+        (g.fuse_ch0 < g.fuse_ctot && (g.fuse_src1 == nullptr || g.fuse_cstride1 % 4 != 0 ||
+                                      (reinterpret_cast<uintptr_t>(g.fuse_src1) & 15) != 0)) ||
+        (g.fuse_affine != nullptr && (reinterpret_cast<uintptr_t>(g.fuse_affine) & 15) != 0) ||
+        g.kblocks * 64 != g.fuse_ctot)
+      return cudaErrorInvalidValue;
+    if (mt == 2) return launch_khcat_fused_typed<2>(maps, g, grid, smem, stream);
+    if (mt == 1) return launch_khcat_fused_typed<1>(maps, g, grid, smem, stream);
+    return cudaErrorInvalidValue;
+  }
 #define CTMR_KH(KC_, MT_) \
   if (kc == KC_ && mt == MT_) return launch_khcat_typed<KC_, MT_>(maps, g, grid, smem, stream);
   CTMR_KH(64, 2) CTMR_KH(32, 2) CTMR_KH(16, 2) CTMR_KH(64, 1) CTMR_KH(32, 1) CTMR_KH(16, 1)
