@@ -382,6 +382,31 @@ class TimeBiasTable:
         return None if w is None else self._by_ptr.get(w.data_ptr())
 
 
+# The UNet ResBlock's skip projection (a 1x1x1 conv of the block input, independent of conv1)
+# runs on a second stream beside norm1 -> conv1 -> norm2, joining before conv2 reads it: on the
+# deep levels, whose launches each fill a fraction of the SMs, the two chains overlap.
+# CTMR_SKIP_SIDE_STREAM=0 keeps it on the caller's stream.
+SKIP_SIDE_STREAM = os.environ.get("CTMR_SKIP_SIDE_STREAM", "1") != "0"
+_SIDE_STREAMS: dict[int, torch.cuda.Stream] = {}
+
+
+def _side_stream(device: torch.device) -> torch.cuda.Stream:
+    index = device.index if device.index is not None else torch.cuda.current_device()
+    if index not in _SIDE_STREAMS:
+        _SIDE_STREAMS[index] = torch.cuda.Stream(device=index)
+    return _SIDE_STREAMS[index]
+
+
+@contextlib.contextmanager
+def _beside(device: torch.device) -> Generator[None, None, None]:
+    """Runs the enclosed launches on the side stream, ordered after everything queued so far on the
+    caller's stream; the caller joins with ``torch.cuda.current_stream().wait_stream(side)``."""
+    side = _side_stream(device)
+    side.wait_stream(torch.cuda.current_stream(device))
+    with torch.cuda.stream(side):
+        yield
+
+
 def residual_block_ncdhw(x, emb: torch.Tensor, weights: Mapping[str, torch.Tensor], *, num_groups: int, eps: float,
                          mx=None, up: bool = False, down: bool = False,
                          time_bias: torch.Tensor | None = None) -> torch.Tensor:
@@ -406,24 +431,30 @@ def residual_block_ncdhw(x, emb: torch.Tensor, weights: Mapping[str, torch.Tenso
     project = cin != int(weights["conv1.conv.weight"].shape[0])
     dtype = activation_dtype()
     n1 = _norm_args(xa, xb, *norm1, groups=num_groups, eps=eps)
+    side = project and SKIP_SIDE_STREAM and xa.is_cuda
+    if project:
+        # The projection's output is allocated on the caller's stream (so its lifetime follows that
+        # stream) and written on the side stream; its packed weights are made here, not there.
+        skip_w = _pack(weights["skip_connection.conv.weight"])
+        b_, o_ = int(xa.shape[0]), int(skip_w.out_channels)
+        grid = [int(n) // (2 if down else 1) for n in xa.shape[2:]]
+        skip = ops.empty_ndhwc(b_, o_, *grid, dtype, xa.device)
+        with _beside(xa.device) if side else contextlib.nullcontext():
+            ops.conv3d(xa, skip_w, weights["skip_connection.conv.bias"], x2=xb, avgpool=down, out=skip)
     if down:
-        if project:
-            skip = ops.conv3d(xa, _pack(weights["skip_connection.conv.weight"]), weights["skip_connection.conv.bias"],
-                              x2=xb, avgpool=True, out_dtype=dtype)
-        else:
+        if not project:
             skip = ops.transform(xa, x2=xb, mode=_lib.TRANSFORM_AVGPOOL, out_dtype=dtype)
         hidden = ops.conv3d(xa, _pack(weights["conv1.conv.weight"]), bias1, x2=xb, **n1, silu=True,
                             avgpool=True, out_dtype=dtype,
                             stats=_want_stats(xa, int(weights["conv1.conv.weight"].shape[0]), 1.0 / 8))
     else:
-        if project:
-            skip = ops.conv3d(xa, _pack(weights["skip_connection.conv.weight"]), weights["skip_connection.conv.bias"],
-                              x2=xb, out_dtype=dtype)
-        else:
+        if not project:
             skip = xa if xb is None else ChannelConcat(xa, xb).materialize()
         hidden = ops.conv3d(xa, _pack(weights["conv1.conv.weight"], upsample=up), bias1, x2=xb, **n1,
                             silu=True, out_dtype=dtype,
                             stats=_want_stats(xa, int(weights["conv1.conv.weight"].shape[0]), 8.0 if up else 1.0))
+    if side:
+        torch.cuda.current_stream(xa.device).wait_stream(_side_stream(xa.device))
     n2 = _norm_args(hidden, None, weights["norm2.weight"], weights["norm2.bias"], groups=num_groups, eps=eps)
     return ops.conv3d(hidden, _pack(weights["conv2.conv.weight"]), weights["conv2.conv.bias"], **n2,
                       silu=True, residual=skip, residual_upsampled=up, out_dtype=dtype,
