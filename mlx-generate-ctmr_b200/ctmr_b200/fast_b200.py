@@ -387,24 +387,31 @@ class TimeBiasTable:
 # deep levels, whose launches each fill a fraction of the SMs, the two chains overlap.
 # CTMR_SKIP_SIDE_STREAM=0 keeps it on the caller's stream.
 SKIP_SIDE_STREAM = os.environ.get("CTMR_SKIP_SIDE_STREAM", "1") != "0"
-_SIDE_STREAMS: dict[int, torch.cuda.Stream] = {}
+# One side stream per (device, parent stream): chains forked from different streams (the UNet's and
+# a concurrently running ControlNet's) do not queue behind each other.
+_SIDE_STREAMS: dict[tuple[int, int], torch.cuda.Stream] = {}
 
 
-def _side_stream(device: torch.device) -> torch.cuda.Stream:
+def side_stream(device: torch.device, parent: torch.cuda.Stream | None = None) -> torch.cuda.Stream:
+    """The side stream forked from ``parent`` (default: the current stream) on ``device``."""
     index = device.index if device.index is not None else torch.cuda.current_device()
-    if index not in _SIDE_STREAMS:
-        _SIDE_STREAMS[index] = torch.cuda.Stream(device=index)
-    return _SIDE_STREAMS[index]
+    parent = parent if parent is not None else torch.cuda.current_stream(index)
+    key = (index, int(parent.cuda_stream))
+    if key not in _SIDE_STREAMS:
+        _SIDE_STREAMS[key] = torch.cuda.Stream(device=index)
+    return _SIDE_STREAMS[key]
 
 
 @contextlib.contextmanager
-def _beside(device: torch.device) -> Generator[None, None, None]:
-    """Runs the enclosed launches on the side stream, ordered after everything queued so far on the
-    caller's stream; the caller joins with ``torch.cuda.current_stream().wait_stream(side)``."""
-    side = _side_stream(device)
-    side.wait_stream(torch.cuda.current_stream(device))
+def beside(device: torch.device) -> Generator[torch.cuda.Stream, None, None]:
+    """Runs the enclosed launches on the current stream's side stream, ordered after everything
+    queued so far on the current stream; the caller joins with
+    ``torch.cuda.current_stream().wait_stream(side)``."""
+    parent = torch.cuda.current_stream(device)
+    side = side_stream(device, parent)
+    side.wait_stream(parent)
     with torch.cuda.stream(side):
-        yield
+        yield side
 
 
 def residual_block_ncdhw(x, emb: torch.Tensor, weights: Mapping[str, torch.Tensor], *, num_groups: int, eps: float,
@@ -439,7 +446,7 @@ def residual_block_ncdhw(x, emb: torch.Tensor, weights: Mapping[str, torch.Tenso
         b_, o_ = int(xa.shape[0]), int(skip_w.out_channels)
         grid = [int(n) // (2 if down else 1) for n in xa.shape[2:]]
         skip = ops.empty_ndhwc(b_, o_, *grid, dtype, xa.device)
-        with _beside(xa.device) if side else contextlib.nullcontext():
+        with beside(xa.device) if side else contextlib.nullcontext():
             ops.conv3d(xa, skip_w, weights["skip_connection.conv.bias"], x2=xb, avgpool=down, out=skip)
     if down:
         if not project:
@@ -454,7 +461,7 @@ def residual_block_ncdhw(x, emb: torch.Tensor, weights: Mapping[str, torch.Tenso
                             silu=True, out_dtype=dtype,
                             stats=_want_stats(xa, int(weights["conv1.conv.weight"].shape[0]), 8.0 if up else 1.0))
     if side:
-        torch.cuda.current_stream(xa.device).wait_stream(_side_stream(xa.device))
+        torch.cuda.current_stream(xa.device).wait_stream(side_stream(xa.device))
     n2 = _norm_args(hidden, None, weights["norm2.weight"], weights["norm2.bias"], groups=num_groups, eps=eps)
     return ops.conv3d(hidden, _pack(weights["conv2.conv.weight"]), weights["conv2.conv.bias"], **n2,
                       silu=True, residual=skip, residual_upsampled=up, out_dtype=dtype,

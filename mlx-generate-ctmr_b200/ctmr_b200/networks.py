@@ -111,6 +111,18 @@ def _levels(constructor: Mapping):
             float(constructor["norm_eps"]), bool(constructor.get("include_fc", True)))
 
 
+class Joined(list):
+    """ControlNet residuals still being produced on ``stream``: the consumer's stream waits for
+    that stream before it first reads them."""
+
+    def __init__(self, items, stream: torch.cuda.Stream) -> None:
+        super().__init__(items)
+        self.stream = stream
+
+    def join(self) -> None:
+        torch.cuda.current_stream(self.stream.device).wait_stream(self.stream)
+
+
 def apply_down_blocks(hidden, emb, weights: Weights, constructor: Mapping, down_block_additional_residuals=None):
     """``unet.apply_down_blocks`` (``unet.py:274-356``) with ``resblock_updown``."""
     ch, res, attn, heads, g, eps, fc = _levels(constructor)
@@ -130,6 +142,8 @@ def apply_down_blocks(hidden, emb, weights: Weights, constructor: Mapping, down_
                                           num_groups=g, eps=eps, down=True)
             skips.append(hidden)
     if down_block_additional_residuals is not None:
+        if isinstance(down_block_additional_residuals, Joined):
+            down_block_additional_residuals.join()
         extras = list(down_block_additional_residuals)
         if len(extras) != len(skips):
             raise ValueError(f"ControlNet residuals length {len(extras)} != UNet skip count {len(skips)}")

@@ -542,11 +542,24 @@ class ControlNetUNetStep:
         self.launches_per_step = 0
 
     def velocity(self) -> torch.Tensor:
-        down, mid = networks.controlnet_residuals_ncdhw(self.z, self.t, self.classes, None, self.cw,
-                                                        constructor=self.cc,
-                                                        conditioning_embedding=self.embedding)
+        # The ControlNet pass runs on a side stream beside the UNet's embedding, conv_in and down
+        # path, which need its residuals only where the skips collect them (``unet.py:274-356``);
+        # the join sits there. CTMR_SKIP_SIDE_STREAM=0 runs it first on the caller's stream.
+        if not A.SKIP_SIDE_STREAM:
+            down, mid = networks.controlnet_residuals_ncdhw(self.z, self.t, self.classes, None, self.cw,
+                                                            constructor=self.cc,
+                                                            conditioning_embedding=self.embedding)
+            _, v = networks.denoise_unet_ncdhw(self.z, self.t, self.classes, self.spacing, self.uw,
+                                               constructor=self.uc, down_block_additional_residuals=down,
+                                               mid_block_additional_residual=mid)
+            return v
+        with A.beside(self.z.device) as side:
+            down, mid = networks.controlnet_residuals_ncdhw(self.z, self.t, self.classes, None, self.cw,
+                                                            constructor=self.cc,
+                                                            conditioning_embedding=self.embedding)
         _, v = networks.denoise_unet_ncdhw(self.z, self.t, self.classes, self.spacing, self.uw, constructor=self.uc,
-                                           down_block_additional_residuals=down, mid_block_additional_residual=mid)
+                                           down_block_additional_residuals=networks.Joined(down, side),
+                                           mid_block_additional_residual=mid)
         return v
 
     def _step(self) -> None:
