@@ -210,10 +210,23 @@ def denoise_unet_ncdhw(x, timesteps, class_labels, spacing, weights: Weights, *,
     if len(constructor["attention_levels"]) != len(constructor["num_channels"]):
         raise ValueError("attention_levels length must match num_channels")
     g, eps = int(constructor["norm_num_groups"]), float(constructor["norm_eps"])
+    w_in, b_in = required_weight(weights, "conv_in.conv.weight"), required_weight(weights, "conv_in.conv.bias")
+    side = None
+    if A.SKIP_SIDE_STREAM and x.is_cuda and int(w_in.shape[2]) == 3:
+        # conv_in runs on a side stream beside the condition embedding's small launches; its output
+        # is allocated (and its weight packed) on the caller's stream, which joins before the blocks.
+        xin = ops.to_ndhwc(x, A.activation_dtype())
+        hidden = ops.empty_ndhwc(int(xin.shape[0]), int(w_in.shape[0]), *(int(n) for n in xin.shape[2:]),
+                                 A.activation_dtype(), xin.device)
+        packed_in = A._pack(w_in)
+        with A.beside(xin.device) as side:
+            ops.conv3d(xin, packed_in, b_in, out=hidden, stats=A._want_stats(xin, int(w_in.shape[0])))
+    else:
+        hidden = A.conv3d_ncdhw(ops.to_ndhwc(x), w_in, b_in, padding=1)
     t_emb, emb = condition_embedding(timesteps, class_labels, spacing, weights, constructor)
-    hidden = A.conv3d_ncdhw(ops.to_ndhwc(x), required_weight(weights, "conv_in.conv.weight"),
-                            required_weight(weights, "conv_in.conv.bias"), padding=1)
     emb = A.TimeBiasTable(emb, weights)  # every block's projected embedding in one GEMM
+    if side is not None:
+        torch.cuda.current_stream(side.device).wait_stream(side)
     hidden, skips = apply_down_blocks(hidden, emb, weights, constructor, down_block_additional_residuals)
     hidden = apply_mid_block(hidden, emb, weights, constructor)
     if mid_block_additional_residual is not None:
