@@ -168,3 +168,45 @@ def _tdesc(**kw) -> _lib.TransformDesc:
 def test_transform_validation(overrides, status):
     assert _lib.LIB.ctmr_transform(ctypes.byref(_tdesc(**overrides)), None) == status
     assert _lib.LIB.ctmr_last_error()
+
+
+def _fuse_desc(**kw) -> _lib.Conv3dDesc:
+    """A 16-bit 64 -> 64 3x3x3 conv with an input affine + SiLU: a kh-concatenated-kernel call."""
+    d = _lib.Conv3dDesc()
+    d.batch, d.depth, d.height, d.width = 2, 8, 32, 32
+    d.x = _lib.Tensor(0x10000000, _lib.DTYPE_F32, 64, 64)
+    d.out_channels, d.kernel_size, d.stride = 64, 3, 1
+    d.precision = _lib.PRECISION_FP16
+    d.weight = 0x20000000
+    d.y, d.y_dtype, d.y_cstride = 0x40000000, _lib.DTYPE_F32, 64
+    d.affine, d.silu = 0x30000000, 1
+    for k, v in kw.items():
+        setattr(d, k, v)
+    return d
+
+
+def test_converter_warp_route_skips_the_operand_pass(monkeypatch):
+    """With CTMR_KHCAT_FUSE=1 the kh-concatenated kernel converts its own operand: the call makes
+    one launch (the conv) instead of two (operand pass + conv). The route is taken only where the
+    converter warps can read the sources directly; everywhere else the operand pass stays."""
+    count = lambda d: _lib.LIB.ctmr_conv3d_launch_count(ctypes.byref(d))  # noqa: E731
+    monkeypatch.setenv("CTMR_KHCAT_FUSE", "0")
+    assert count(_fuse_desc()) == 2
+    monkeypatch.setenv("CTMR_KHCAT_FUSE", "1")
+    assert count(_fuse_desc()) == 1
+    assert count(_fuse_desc(affine=None, silu=0)) == 1  # a plain cast is folded as well
+    # two sources split at a 64-channel boundary (the up path's virtual concat)
+    assert count(_fuse_desc(x2=_lib.Tensor(0x50000000, _lib.DTYPE_F32, 64, 64), out_channels=48)) == 1
+    kept = [
+        _fuse_desc(y=0x10000000 + 64 * 4),                                   # output overlaps the source
+        _fuse_desc(x=_lib.Tensor(0x10000004, _lib.DTYPE_F32, 64, 64)),        # source rows not 16-byte aligned
+        _fuse_desc(affine=0x30000008),                                       # affine not 16-byte aligned
+        _fuse_desc(x=_lib.Tensor(0x10000000, _lib.DTYPE_F32, 32, 32)),        # 32-channel blocks
+        _fuse_desc(x2=_lib.Tensor(0x50000000, _lib.DTYPE_F32, 32, 32)),       # concat split inside a block
+        _fuse_desc(x=_lib.Tensor(0x10000000, _lib.DTYPE_BF16, 64, 64)),       # bf16 source
+        _fuse_desc(precision=_lib.PRECISION_FP32, weight_lo=0x50000000),     # split-fp32 operands
+        _fuse_desc(precision=_lib.PRECISION_TF32),                           # TF32 operands
+        _fuse_desc(trilinear=1, depth=4, height=16, width=16, affine=None, silu=0),  # resampled input
+    ]
+    for d in kept:
+        assert count(d) == 2
