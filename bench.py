@@ -806,11 +806,19 @@ def main() -> None:
     # The north-star partition beside the replicas: all N GPUs on one volume.
     partition = None
     if world > 1 and headline_group is None and world in D.GROUP_SIZES:
-        prun = VolumeRun(args.precision, group=D.VolumeGroup(rank, world, world), **common)
-        m = prun.measure(args.steps, args.warmup)
-        prun.release()
-        partition = {"value": round(m["value"], 3), "unit": UNIT, "ms_per_volume": round(m["ms"], 2),
-                     "ranks_per_volume": world, "e2e": m["e2e"], "parallelism": D.describe_partition(world)}
+        # A failure that every rank meets alike (a Python error of the partition's set-up) is
+        # reported in the line instead of taking the measured replicas with it.
+        prun = None
+        try:
+            prun = VolumeRun(args.precision, group=D.VolumeGroup(rank, world, world), **common)
+            m = prun.measure(args.steps, args.warmup)
+            partition = {"value": round(m["value"], 3), "unit": UNIT, "ms_per_volume": round(m["ms"], 2),
+                         "ranks_per_volume": world, "e2e": m["e2e"], "parallelism": D.describe_partition(world)}
+        except Exception as e:  # noqa: BLE001
+            partition = {"error": f"{type(e).__name__}: {e}"[:300], "ranks_per_volume": world}
+        finally:
+            if prun is not None:
+                prun.release()
 
     roofline = conv_roofline(args.precision, unet_w, vae_w, dev, head["ms"]) if world == 1 else None
     if rank == 0:
