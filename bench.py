@@ -22,6 +22,7 @@ torch-CPU restatement in ``oracle/``; the reference itself needs MLX/Metal).
 from __future__ import annotations
 
 import argparse
+import contextlib
 import json
 import math
 import os
@@ -337,6 +338,20 @@ def _breakdown(part: str, records, total_ms: float) -> None:
         print(json.dumps(line), flush=True)
 
 
+@contextlib.contextmanager
+def _one_stream():
+    """Every launch on the caller's stream (no side-stream branches), so that the CUDA events of
+    a profiled pass bracket each launch alone instead of two overlapping chains."""
+    from ctmr_b200 import fast_b200 as A
+
+    was = A.SKIP_SIDE_STREAM
+    A.SKIP_SIDE_STREAM = False
+    try:
+        yield
+    finally:
+        A.SKIP_SIDE_STREAM = was
+
+
 def _profile_pass(part: str, fn, dev) -> None:
     from ctmr_b200 import ops
 
@@ -353,7 +368,8 @@ def _profile_pass(part: str, fn, dev) -> None:
     ops.PROFILE = prof
     torch.cuda._sleep(SPIN_CYCLES)  # the host queues the pass while the device waits: no launch gaps inside
     start.record()
-    fn()
+    with _one_stream():
+        fn()
     end.record()
     ops.PROFILE = None
     torch.cuda.synchronize(dev)
@@ -707,7 +723,7 @@ def conv_roofline(precision: str, unet_w, vae_w, dev, ms_per_volume: float) -> d
 
     peaks, peak_kind = _peaks()
     prof: list = []
-    with A.arithmetic_precision(precision):
+    with A.arithmetic_precision(precision), _one_stream():
         timesteps, _ = P.set_timesteps_rflow(num_inference_steps=STEPS_RFLOW,
                                              input_img_size_numel=math.prod(LATENT[2:]))
         eager = P.GuidedUNetStep(unet_w, P.PRODUCTION_UNET, LATENT, class_label=MODALITY,
